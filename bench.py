@@ -1,0 +1,263 @@
+"""Benchmark: decode tokens/s of the Llama-3.3-70B-shaped Q4_K_M decoder (HBM-resident), batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--prompt P] [--impl windlass|reference]
+
+One step is one decode token (batch 1) through every layer and the output head. The weights are the synthetic
+N(0, 0.02) decoder of that shape generated on the device (wl_open_synthetic; no checkpoint exists offline), 39.5 GB
+per step, which is far larger than the 126 MB L2, so no flush is needed between steps.
+
+- value: K device-resident decode steps (wl_bench_decode: no host copies) timed with CUDA events on the model's
+  stream, max over ranks; with N GPUs each rank runs its own replica (scaling "weak").
+- e2e: the same steps through the public call a host makes (wl_forward with host token ids in and host logits out).
+- roofline: the dominant kernel (the Q4_K fused dequant-matvec), its algorithmic bytes over its CUDA-event time,
+  recorded live in a second pass over the same steps with per-launch events.
+- cpu_baseline: the reference's CPU arithmetic (the C oracle) on the box's cores, one decoder layer of the same
+  shape plus a slice of the output head, scaled to a whole token.
+--impl reference prints the CPU arm alone (rank 0; other ranks exit 0).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s @70B-shape Q4_K_M b1/b8; Q4_K matvec HBM GB/s vs ~8 TB/s"
+Q4_K, Q6_K = 12, 14
+LAYER_BYTES_70B = 483.5e6   # per decoder layer (SURVEY 8d arithmetic: q, k, o, gate, up, down Q4_K + v Q6_K)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return None
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_baseline(seconds=12.0, threads=0):
+    """The oracle (the reference's CPU arithmetic) on one 70B-shape decoder layer at T=1 and a 16384-row slice of
+    the Q6_K output head, timed with all host threads; returns tok/s for a whole token (80 layers + full head)."""
+    from oracle import oracle as O
+    from windlass_b200.transformer import llama70b_spec
+    spec = llama70b_spec()
+    spec.vocab = 16384
+    m = O.Model(synth=spec, build_layers=1, max_context=64, threads=threads)
+    cores = threads or O.lib().or_default_threads()
+    x = (0.02 * __import__("numpy").random.default_rng(0).standard_normal(8192)).astype("float32")
+    m.forward([1])                                       # warm
+    side = m.new_sequence()
+    t_layer, t_fwd, reps = [], [], 0
+    t_end = time.perf_counter() + seconds
+    pos = 1
+    while time.perf_counter() < t_end and pos < 60:
+        t0 = time.perf_counter()
+        m.layer(0, x.copy(), pos0=pos - 1, seq=side)
+        t_layer.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        m.forward([5], pos0=pos)
+        t_fwd.append(time.perf_counter() - t0)
+        pos += 1
+        reps += 1
+    tl, tf = min(t_layer), min(t_fwd)
+    t_head_slice = max(tf - tl, 0.0)
+    t_token = 80 * tl + t_head_slice * (128256 / 16384)
+    m.close()
+    return {"value": 1.0 / t_token, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"C oracle (reference CPU arithmetic), {cores} threads: one 70B-shape decoder layer at T=1 "
+                      f"({tl * 1e3:.1f} ms, best of {reps}) x 80 + a 16384-row slice of the Q6_K output head scaled to "
+                      f"128256 rows ({t_head_slice * 1e3:.1f} ms x {128256 / 16384:.2f})",
+            "layer_ms": tl * 1e3, "weights_gbs": LAYER_BYTES_70B / tl / 1e9}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(seconds=2.0)
+        if i >= args.warmup:
+            per_step.append(1.0 / r["value"])
+    value = args.steps / sum(per_step)
+    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(per_step) / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/f32", "data": "synthetic",
+           "config": {"workload": "decode b1, Llama-3.3-70B-shaped Q4_K_M (configs[3]), CPU", "batch": 1},
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
+           "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=80)
+    ap.add_argument("--impl", default="windlass", choices=["windlass", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import numpy as np
+    import torch
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    from windlass_b200.transformer import CudaTransformer, llama70b_spec
+    spec = llama70b_spec(layers=args.layers)
+    steps, warm, B = args.steps, args.warmup, args.batch
+    ctx = args.prompt + 2 * (steps + warm) + 64
+    t0 = time.perf_counter()
+    m = CudaTransformer(synthetic=spec, device=local, max_context=ctx)
+    load_s = time.perf_counter() - t0
+    rng = np.random.default_rng(rank)
+    seqs = [m.new_sequence() for _ in range(B)]
+    t0 = time.perf_counter()
+    for s in seqs:
+        m.forward(rng.integers(0, spec.vocab, args.prompt).astype(np.int32), seq=s)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+
+    m.bench_decode(seqs, warm)
+    launches0 = m.stats().kernel_launches
+    barrier()
+    with ClockSampler(local) as clk:
+        ms = m.bench_decode(seqs, steps)
+        barrier()
+    launches = m.stats().kernel_launches - launches0
+    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * steps * B / (ms_max / 1e3)
+
+    # e2e: the host-facing call, host token ids in, host logits out, every step
+    toks = rng.integers(0, spec.vocab, B).astype(np.int32)
+    out = np.empty(B * spec.vocab, dtype=np.float32)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        if B == 1:
+            m.forward(toks, pos0=seqs[0].length, seq=seqs[0], out=out)
+        else:
+            m.forward_batch(seqs, toks, out=out)
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e = world * steps * B / float(e2e_t.item())
+
+    # live roofline of the dominant kernel: per-launch CUDA events over a second pass of the same steps
+    m.profile(1)
+    m.bench_decode(seqs, min(steps, 8))
+    q4 = m.profile_get(Q4_K)
+    q6 = m.profile_get(Q6_K)
+    m.profile(0)
+    hbm, _, peak_kind = measured_peaks()
+    achieved = q4.bytes / (q4.ms / 1e3) / 1e9 if q4.ms > 0 else None
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "q4k_matvec_traffic.txt")
+    if os.path.exists(tfile):
+        for line in open(tfile):
+            if line.startswith("dram_bytes_per_byte_algorithmic"):
+                traffic = float(line.split()[1]) * q4.bytes / max(q4.launches, 1)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm if achieved else None, "traffic": traffic,
+                "kernel": "k_matvec<Q4_K> (fused dequant-dot)", "peak_source": peak_kind,
+                "launches": q4.launches, "avg_launch_us": 1e3 * q4.ms / max(q4.launches, 1),
+                "bytes_per_launch": q4.bytes / max(q4.launches, 1),
+                "q6k_achieved_gbs": q6.bytes / (q6.ms / 1e3) / 1e9 if q6.ms > 0 else None}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
+                "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "q4_K/q6_K weights, f32 compute", "data": "synthetic",
+                "config": {"workload": f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
+                                       f"{args.layers} layers", "batch": B, "prompt": args.prompt,
+                           "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                           "l2": "inputs larger than L2 (39.5 GB of weights read per step)"},
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                        "d2h_bytes_per_step": 4 * B * spec.vocab},
+                "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+                "load_s": load_s, "prefill_s": prefill_s,
+                "prefill_tok_s": B * args.prompt / prefill_s}
+        print(json.dumps(line))
+    m.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

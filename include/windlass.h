@@ -1,0 +1,178 @@
+/* libwindlass_cuda: the C ABI of the B200-native Windlass quantized transformer forward.
+ *
+ * The reference engine (C#, .NET Framework 4.8) reaches its forward pass only through the Transformer object
+ * (src/Transformer.cs) inside LayeredBackend (src/Engine.cs). This library replaces that object: a C# host binds
+ * these entry points with P/Invoke (the binding is in INTEGRATION.md) and keeps its server, BatchEngine, Playbook,
+ * tokenizer and sampler unchanged. Plain pointers and sizes only; no C++ or CUDA types cross the boundary except the
+ * opaque `stream` arguments of the kernel-level test exports, which are cudaStream_t values (NULL = default stream).
+ *
+ * Error convention: every function returns WL_OK (0) or a WL_E* status and never aborts or exits. wl_last_error()
+ * returns the calling thread's message for the last failure. Statuses map to the reference's exceptions as noted.
+ * Threading: one call at a time per model (the reference serialises on LayeredBackend._run, src/Engine.cs:138 and
+ * src/BatchEngine.cs:111). Progress callbacks run on the calling thread between stages.
+ */
+#ifndef WINDLASS_H
+#define WINDLASS_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WL_OK            0
+#define WL_EINVAL        1   /* ArgumentException: bad shape, pos0 past the cache, context overflow, bad token id */
+#define WL_EUNSUPPORTED  2   /* NotSupportedException: architecture, weight type or layout the engine cannot run */
+#define WL_EIO           3   /* IOException: the file cannot be opened or read */
+#define WL_EFORMAT       4   /* InvalidDataException: the file is not valid GGUF */
+#define WL_ENOMEM        5   /* device or pinned host memory exhausted */
+#define WL_ECUDA         6   /* a CUDA call failed */
+#define WL_ENCCL         7   /* an NCCL call failed */
+#define WL_ETIMEDOUT     8   /* a bounded device-side wait gave up */
+#define WL_CANCELLED     9   /* OperationCanceledException: the cancel flag was set between stages */
+
+/* ggml_type numbers of the weight formats (src/Gguf.cs:19-25). */
+#define WL_TYPE_F32      0
+#define WL_TYPE_F16      1
+#define WL_TYPE_Q4_0     2
+#define WL_TYPE_Q4_1     3
+#define WL_TYPE_Q5_0     6
+#define WL_TYPE_Q5_1     7
+#define WL_TYPE_Q8_0     8
+#define WL_TYPE_Q2_K    10
+#define WL_TYPE_Q3_K    11
+#define WL_TYPE_Q4_K    12
+#define WL_TYPE_Q5_K    13
+#define WL_TYPE_Q6_K    14
+#define WL_TYPE_IQ2_XXS 16
+#define WL_TYPE_IQ2_XS  17
+#define WL_TYPE_IQ3_XXS 18
+#define WL_TYPE_IQ1_S   19
+#define WL_TYPE_IQ4_NL  20
+#define WL_TYPE_IQ3_S   21
+#define WL_TYPE_IQ2_S   22
+#define WL_TYPE_IQ4_XS  23
+#define WL_TYPE_IQ1_M   29
+#define WL_TYPE_BF16    30
+
+typedef struct wl_model wl_model;
+typedef struct wl_seq wl_seq;
+
+/* onStage(done, total) of Transformer.Forward (src/Transformer.cs:102,106): called after each layer and the head. */
+typedef void (*wl_progress_fn)(int32_t done, int32_t total, void* user);
+
+typedef struct wl_options {
+    int32_t size;            /* sizeof(wl_options), set by wl_options_init */
+    int32_t device;          /* CUDA device ordinal */
+    int32_t max_context;     /* positions per sequence; 0 = min(model context_length, 8192) (src/Engine.cs:26,62) */
+    int32_t max_batch;       /* most rows in one wl_forward_batch (BatchPlan.MaxBatch = 64, src/Batch.cs:40) */
+    int32_t resident;        /* 1: every weight resident in HBM; 0: layers streamed from pinned host memory through
+                                two device slots (src/LayerStream.cs); -1: resident when the weights fit */
+    int32_t prefill_path;    /* T > 8 prompts: 0 auto, 1 fp32 CUDA cores, 2 bf16 tensor cores (tcgen05) */
+    int32_t use_graphs;      /* 1: replay decode steps from captured CUDA graphs */
+    int32_t reserved[9];
+} wl_options;
+
+typedef struct wl_info {
+    int32_t layers, embd, heads, kv_heads, head_dim, vocab, context_length, max_context;
+    int32_t expert_count, expert_used, expert_ff, moe;
+    int64_t weight_bytes;    /* quantized weight bytes of all layers and the head */
+    int64_t device_bytes;    /* device memory the model holds now */
+    char arch[32];
+} wl_info;
+
+typedef struct wl_stats {
+    int64_t bytes_h2d;       /* weight bytes copied host->device (LayerStream.BytesRead, src/LayerStream.cs:83) */
+    int64_t expert_runs;     /* experts computed (Transformer.ExpertRuns, src/Transformer.cs:27,287) */
+    int64_t forward_calls, batch_calls, tokens;
+    double  last_forward_ms;
+    int64_t kernel_launches; /* kernels this process has launched from the library (all models) */
+} wl_stats;
+
+/* Per weight format: matvec/matmul launches, their summed device time (CUDA events around each launch on the
+ * model's stream) and the algorithmic bytes they moved (weights + activations in + outputs), since profiling was
+ * switched on with wl_profile(model, 1). */
+typedef struct wl_profile_entry {
+    int64_t launches;
+    double  ms;
+    double  bytes;
+} wl_profile_entry;
+
+/* Synthetic model (benchmarks and full-size tests): a decoder of the given shape whose weights are generated on the
+ * device from a counter hash (seed, tensor, element), N(0, sigma) through Irwin-Hall(12), round-to-nearest quantized.
+ * The same bytes come out of the CPU generator of the test oracle. No file is read. */
+typedef struct wl_synth_spec {
+    char arch[16];           /* "llama", "qwen3" (QK-norm) or "qwen3moe" */
+    int32_t layers, embd, heads, kv_heads, head_dim, ff, vocab, context_length;
+    int32_t experts, experts_used, expert_ff;
+    float rope_base, rms_eps, sigma;
+    int32_t type_attn, type_attn_v, type_ffn, type_ffn_down, type_embd, type_output;
+    uint64_t seed;
+} wl_synth_spec;
+
+void        wl_options_init(wl_options* opt);
+const char* wl_last_error(void);
+const char* wl_version(void);
+
+/* LayeredBackend.Load (src/Engine.cs:55-91): GgufModelFile.Open + ModelConfig.From + LayerStream + Transformer. */
+int32_t wl_open(const char* gguf_path, const wl_options* opt, wl_model** out);
+int32_t wl_open_synthetic(const wl_synth_spec* spec, const wl_options* opt, wl_model** out);
+int32_t wl_close(wl_model* model);
+int32_t wl_info_get(const wl_model* model, wl_info* info);
+int32_t wl_stats_get(const wl_model* model, wl_stats* stats);
+
+/* Transformer.NewSequence / Sequence.Truncate / Sequence.Length (src/Transformer.cs:60, src/Batch.cs:28).
+ * A sequence owns its fp16 KV cache in device memory; free every sequence before its model. */
+int32_t wl_seq_new(wl_model* model, wl_seq** out);
+int32_t wl_seq_free(wl_seq* seq);
+int32_t wl_seq_truncate(wl_seq* seq, int32_t n);
+int32_t wl_seq_length(const wl_seq* seq, int32_t* n);
+
+/* Transformer.Truncate / Transformer.Length on the model's own sequence (src/Transformer.cs:28,57). */
+int32_t wl_truncate(wl_model* model, int32_t n);
+int32_t wl_length(const wl_model* model, int32_t* n);
+
+/* Transformer.Forward (src/Transformer.cs:77-109): runs tokens[0..T) at positions pos0.. of seq (NULL = the model's
+ * own). logits_out (host memory) receives T*vocab floats when all_logits != 0, else the last token's vocab floats.
+ * cancel (may be NULL) is polled between stages; a cancelled call returns WL_CANCELLED and leaves the sequence
+ * length at pos0. */
+int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0, int32_t all_logits,
+                   float* logits_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+
+/* Transformer.ForwardBatch (src/Transformer.cs:132-170): one decode step for N sequences; token i is the next token
+ * of seqs[i] at position seqs[i]'s length. Row i of logits_out (N*vocab host floats) is bit-identical to what
+ * wl_forward(seqs[i], &tokens[i], 1, ...) returns. */
+int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N, float* logits_out,
+                         volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+
+/* ---- benchmark and profiling exports (no counterpart in the reference, which has no device) ---- */
+
+/* Runs `steps` decode steps of the N sequences seqs[0..N) with token ids already on the device (the same ids every
+ * step, taken from a seeded draw), no host copies, and returns the device time of the whole loop measured with CUDA
+ * events on the model's stream. Sequence lengths advance by `steps`. */
+int32_t wl_bench_decode(wl_model* model, wl_seq* const* seqs, int32_t N, int32_t steps, double* device_ms);
+/* on != 0 records CUDA events around every matvec/matmul launch (and clears the counters); 0 stops. */
+int32_t wl_profile(wl_model* model, int32_t on);
+/* The counters of weight format `type` (see wl_profile_entry). */
+int32_t wl_profile_get(wl_model* model, int32_t type, wl_profile_entry* out);
+
+/* ---- kernel-level exports for tests and benchmarks (device pointers, stream = cudaStream_t or NULL) ---- */
+
+/* Quants.DecodeRow (src/Quants.cs:32-52, src/IQuants.cs:27-42): n values of `type` to fp32, bit-exact. */
+int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream);
+/* Transformer.MatMulEach / Quants.DotRow (src/Transformer.cs:544-561, src/Quants.cs:67-187): y[t*rows + r] =
+ * W[r] . x[t] for t < ncols (1..8), fused dequant-dot, fp32 accumulate. Every column is computed as if alone. */
+int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t ncols,
+                  float* dev_y, void* stream);
+/* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 1 = fp32 CUDA cores, 2 = bf16 tensor
+ * cores (tcgen05, fp32 accumulate), 0 = the model's default for T. */
+int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
+                  float* dev_y, int32_t path, void* stream);
+/* Synthetic weight generator of wl_open_synthetic for one tensor (rows x cols of `type`: F32, F16, Q8_0, Q4_K or
+ * Q6_K). F32 values are offset + sigma*z; other types quantize sigma*z. */
+int32_t wl_synth_tensor(int32_t type, uint64_t seed, uint32_t tensor_id, int64_t rows, int64_t cols, float sigma,
+                        float offset, void* dev_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,124 @@
+"""GPU kernel parity against the CPU oracle, through the C ABI.
+
+- wl_dequant is bit-exact with Quants.DecodeRow for every decodable type (src/Quants.cs:32-52, IQuants.cs:27-42).
+- wl_matvec matches the reference's dot products within 1e-4 relative L2 (fp32 accumulate, different order),
+  and each activation column's result is bit-identical whatever the number of columns beside it
+  (the property ForwardBatch relies on, src/Transformer.cs:127-131).
+- wl_synth_tensor writes the same bytes as the oracle's generator.
+- Full-size (configs[1], 8192 x 8192) matvecs for the five benchmark formats against the oracle.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from gpu_util import dev, empty, host, ptr, rel_l2, weights, IQ_TYPES
+
+pytestmark = pytest.mark.gpu
+
+ALL_TYPES = ["f32", "f16", "bf16", "q4_0", "q4_1", "q5_0", "q5_1", "q8_0", "q2_K", "q3_K", "q4_K", "q5_K", "q6_K"] + \
+            list(IQ_TYPES)
+BENCH_TYPES = ["q4_K", "q6_K", "q8_0", "iq4_xs", "iq2_xxs"]
+
+
+@pytest.mark.parametrize("tname", ALL_TYPES)
+def test_dequant_bit_exact(wl, oracle, tname):
+    O = oracle
+    t = O.TYPE_OF[tname]
+    rows, cols = 5, 512
+    w = weights(O, tname, rows, cols)
+    want = O.decode(t, w, rows * cols)
+    dw = dev(w)
+    out = empty(rows * cols)
+    wl.check(wl.lib().wl_dequant(t, ptr(dw), rows * cols, ptr(out), None))
+    got = host(out)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+        f"{tname}: {int((got.view(np.uint32) != want.view(np.uint32)).sum())} values differ"
+
+
+def _matvec(wl, t, dw, rows, cols, x, ncols):
+    dx = dev(x.reshape(-1))
+    dy = empty(ncols * rows)
+    wl.check(wl.lib().wl_matvec(t, ptr(dw), rows, cols, ptr(dx), ncols, ptr(dy), None))
+    return host(dy).reshape(ncols, rows)
+
+
+@pytest.mark.parametrize("tname", ALL_TYPES)
+def test_matvec_matches_reference_and_columns_are_independent(wl, oracle, tname):
+    O = oracle
+    t = O.TYPE_OF[tname]
+    rows, cols = 67, 1024
+    w = weights(O, tname, rows, cols)
+    dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((11, cols)).astype(np.float32)
+    dw = dev(w)
+    y11 = _matvec(wl, t, dw, rows, cols, x, 11)
+    want = x.astype(np.float64) @ dec.T
+    for c in range(11):
+        assert rel_l2(y11[c], want[c]) <= 1e-4, (tname, c, rel_l2(y11[c], want[c]))
+    # each column alone gives the same bits as inside a batch of 11 (two launches of 8 and 3 columns)
+    for c in (0, 5, 8, 10):
+        y1 = _matvec(wl, t, dw, rows, cols, x[c:c + 1], 1)
+        assert np.array_equal(y1[0].view(np.uint32), y11[c].view(np.uint32)), (tname, c)
+    if O.lib().or_can_dot(t):
+        ref = O.matmul(t, w, rows, cols, x[:1])[0]      # Quants.DotRow, the reference's own single-token kernel
+        assert rel_l2(y11[0], ref) <= 1e-4
+
+
+@pytest.mark.parametrize("tname,rows,cols", [("f32", 3, 256), ("f16", 9, 512), ("q8_0", 4, 1408), ("q4_K", 2, 256),
+                                             ("q6_K", 1, 512), ("q8_0", 1, 32)])
+def test_matvec_edge_shapes(wl, oracle, tname, rows, cols):
+    """Ragged and minimal shapes: one block per row, a single row, a non-256 Q8_0 width (configs[0] ffn_down)."""
+    O = oracle
+    t = O.TYPE_OF[tname]
+    w = weights(O, tname, rows, cols)
+    dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
+    x = np.random.default_rng(1).standard_normal((3, cols)).astype(np.float32)
+    y = _matvec(wl, t, dev(w), rows, cols, x, 3)
+    assert rel_l2(y, x.astype(np.float64) @ dec.T) <= 1e-4
+
+
+@pytest.mark.parametrize("tname", ["f32", "q8_0", "q4_K", "q6_K"])
+def test_synth_bytes_match_oracle(wl, oracle, tname):
+    O = oracle
+    t = O.TYPE_OF[tname]
+    rows, cols = 33, 512
+    offset = 1.0 if t == O.F32 else 0.0
+    want = O.synth_tensor(t, 1234, 0x305, rows, cols, 0.02, offset)
+    out = empty(want.size, "uint8")
+    wl.check(wl.lib().wl_synth_tensor(t, 1234, 0x305, rows, cols, C.c_float(0.02), C.c_float(offset), ptr(out), None))
+    assert np.array_equal(host(out), want)
+
+
+@pytest.mark.parametrize("tname", BENCH_TYPES)
+def test_config1_full_size_matvec(wl, oracle, tname):
+    """8192 x 8192, batch columns 1, 4, 8 (fused matvec) and 64 (matmul), against the oracle's dot
+    products on a sample of rows; synthetic Q8_0/Q6_K/Q4_K bytes are also compared with the oracle's whole tensor."""
+    O = oracle
+    t = O.TYPE_OF[tname]
+    n = 8192
+    if tname in ("iq4_xs", "iq2_xxs"):
+        w = weights(O, tname, n, n, seed=7)
+        dw = dev(w)
+    else:
+        w = O.synth_tensor(t, 42, 0x7001, n, n, 0.02)
+        dw = empty(w.size, "uint8")
+        wl.check(wl.lib().wl_synth_tensor(t, 42, 0x7001, n, n, C.c_float(0.02), C.c_float(0.0), ptr(dw), None))
+        assert np.array_equal(host(dw), w), f"{tname}: synthetic bytes differ from the oracle's"
+    rng = np.random.default_rng(11)
+    sample = np.sort(rng.choice(n, 96, replace=False))
+    rb = O.row_bytes(t, n)
+    sub = np.concatenate([w[r * rb:(r + 1) * rb] for r in sample])
+    dec = O.decode(t, sub, sample.size * n).reshape(sample.size, n).astype(np.float64)
+    for ncols in (1, 4, 8, 64):
+        x = rng.standard_normal((ncols, n)).astype(np.float32)
+        dx = dev(x.reshape(-1))
+        dy = empty(ncols * n)
+        if ncols <= 8:
+            wl.check(wl.lib().wl_matvec(t, ptr(dw), n, n, ptr(dx), ncols, ptr(dy), None))
+        else:
+            wl.check(wl.lib().wl_matmul(t, ptr(dw), n, n, ptr(dx), ncols, ptr(dy), 0, None))
+        y = host(dy).reshape(ncols, n)[:, sample]
+        want = x.astype(np.float64) @ dec.T
+        assert rel_l2(y, want) <= 1e-4, (tname, ncols, rel_l2(y, want))

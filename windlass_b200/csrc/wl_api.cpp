@@ -1,0 +1,302 @@
+// The C ABI of libwindlass_cuda (include/windlass.h): argument checks, exception-to-status translation, and the
+// kernel-level test exports. No function aborts or exits; failures return a status and set wl_last_error().
+#include <cstring>
+#include <new>
+#include "../../include/windlass.h"
+#include "wl_common.h"
+#include "wl_kernels.h"
+#include "wl_model.h"
+
+namespace wl { const char* last_error_cstr(); }
+
+struct wl_model {
+    wl::Model* m;
+};
+struct wl_seq {
+    wl::Seq* s;
+    wl_model* owner;
+};
+
+namespace {
+template <typename F> int32_t guarded(F&& f)
+{
+    try {
+        wl::clear_error();
+        return f();
+    } catch (const wl::Error& e) {
+        return wl::fail(e.status, e.msg);
+    } catch (const std::bad_alloc&) {
+        return wl::fail(WL_ENOMEM, "out of host memory");
+    } catch (const std::exception& e) {
+        return wl::fail(WL_EINVAL, e.what());
+    } catch (...) {
+        return wl::fail(WL_EINVAL, "unknown failure");
+    }
+}
+
+wl_options defaults()
+{
+    wl_options o;
+    wl_options_init(&o);
+    return o;
+}
+}  // namespace
+
+extern "C" {
+
+void wl_options_init(wl_options* opt)
+{
+    if (!opt) return;
+    memset(opt, 0, sizeof *opt);
+    opt->size = (int32_t)sizeof(wl_options);
+    opt->device = 0;
+    opt->max_context = 0;
+    opt->max_batch = 64;
+    opt->resident = -1;
+    opt->prefill_path = 0;
+    opt->use_graphs = 0;
+}
+
+const char* wl_last_error(void) { return wl::last_error_cstr(); }
+const char* wl_version(void) { return "windlass-cuda 0.1 (sm_100a)"; }
+
+int32_t wl_open(const char* path, const wl_options* opt, wl_model** out)
+{
+    return guarded([&]() -> int32_t {
+        if (!path || !out) return wl::fail(WL_EINVAL, "wl_open: path and out are required");
+        *out = nullptr;
+        const wl_options o = opt ? *opt : defaults();
+        wl::Model* m = wl::Model::open_file(path, o);
+        *out = new wl_model{m};
+        return WL_OK;
+    });
+}
+
+int32_t wl_open_synthetic(const wl_synth_spec* spec, const wl_options* opt, wl_model** out)
+{
+    return guarded([&]() -> int32_t {
+        if (!spec || !out) return wl::fail(WL_EINVAL, "wl_open_synthetic: spec and out are required");
+        *out = nullptr;
+        const wl_options o = opt ? *opt : defaults();
+        wl::Model* m = wl::Model::open_synthetic(*spec, o);
+        *out = new wl_model{m};
+        return WL_OK;
+    });
+}
+
+int32_t wl_close(wl_model* model)
+{
+    return guarded([&]() -> int32_t {
+        if (!model) return WL_OK;
+        delete model->m;
+        delete model;
+        return WL_OK;
+    });
+}
+
+int32_t wl_info_get(const wl_model* model, wl_info* info)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !info) return wl::fail(WL_EINVAL, "wl_info_get: model and info are required");
+        const wl::Config& c = model->m->config();
+        memset(info, 0, sizeof *info);
+        info->layers = c.layers; info->embd = c.embd; info->heads = c.heads; info->kv_heads = c.kv_heads;
+        info->head_dim = c.head_dim; info->vocab = c.vocab; info->context_length = c.context_length;
+        info->max_context = model->m->max_context(); info->expert_count = c.expert_count;
+        info->expert_used = c.expert_used; info->expert_ff = c.expert_ff; info->moe = c.expert_count > 0;
+        info->weight_bytes = model->m->weight_bytes(); info->device_bytes = model->m->device_bytes();
+        strncpy(info->arch, c.arch.c_str(), sizeof info->arch - 1);
+        return WL_OK;
+    });
+}
+
+int32_t wl_stats_get(const wl_model* model, wl_stats* stats)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !stats) return wl::fail(WL_EINVAL, "wl_stats_get: model and stats are required");
+        const wl::Stats& s = model->m->stats();
+        stats->bytes_h2d = s.bytes_h2d; stats->expert_runs = s.expert_runs; stats->forward_calls = s.forward_calls;
+        stats->batch_calls = s.batch_calls; stats->tokens = s.tokens; stats->last_forward_ms = s.last_forward_ms;
+        stats->kernel_launches = wl::k::launches();
+        return WL_OK;
+    });
+}
+
+int32_t wl_bench_decode(wl_model* model, wl_seq* const* seqs, int32_t N, int32_t steps, double* device_ms)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !seqs || !device_ms) return wl::fail(WL_EINVAL, "wl_bench_decode: model, seqs and device_ms are required");
+        std::vector<wl::Seq*> ss((size_t)(N > 0 ? N : 0));
+        for (int i = 0; i < N; ++i) {
+            if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_bench_decode: a sequence belongs to another model");
+            ss[(size_t)i] = seqs[i]->s;
+        }
+        *device_ms = model->m->bench_decode(ss.data(), N, steps);
+        return WL_OK;
+    });
+}
+
+int32_t wl_profile(wl_model* model, int32_t on)
+{
+    return guarded([&]() -> int32_t {
+        if (!model) return wl::fail(WL_EINVAL, "wl_profile: model is required");
+        model->m->set_profiling(on != 0);
+        return WL_OK;
+    });
+}
+
+int32_t wl_profile_get(wl_model* model, int32_t type, wl_profile_entry* out)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !out) return wl::fail(WL_EINVAL, "wl_profile_get: model and out are required");
+        *out = model->m->profile(type);
+        return WL_OK;
+    });
+}
+
+int32_t wl_seq_new(wl_model* model, wl_seq** out)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !out) return wl::fail(WL_EINVAL, "wl_seq_new: model and out are required");
+        *out = new wl_seq{model->m->new_seq(), model};
+        return WL_OK;
+    });
+}
+
+int32_t wl_seq_free(wl_seq* seq)
+{
+    return guarded([&]() -> int32_t {
+        if (!seq) return WL_OK;
+        seq->owner->m->free_seq(seq->s);
+        delete seq;
+        return WL_OK;
+    });
+}
+
+// Sequence.Truncate (src/Batch.cs:28): drops cached positions from n onward.
+int32_t wl_seq_truncate(wl_seq* seq, int32_t n)
+{
+    return guarded([&]() -> int32_t {
+        if (!seq) return wl::fail(WL_EINVAL, "wl_seq_truncate: seq is required");
+        if (n < seq->s->length) seq->s->length = n < 0 ? 0 : n;
+        return WL_OK;
+    });
+}
+
+int32_t wl_seq_length(const wl_seq* seq, int32_t* n)
+{
+    return guarded([&]() -> int32_t {
+        if (!seq || !n) return wl::fail(WL_EINVAL, "wl_seq_length: seq and n are required");
+        *n = seq->s->length;
+        return WL_OK;
+    });
+}
+
+int32_t wl_truncate(wl_model* model, int32_t n)
+{
+    return guarded([&]() -> int32_t {
+        if (!model) return wl::fail(WL_EINVAL, "wl_truncate: model is required");
+        wl::Seq* s = model->m->own();
+        if (n < s->length) s->length = n < 0 ? 0 : n;
+        return WL_OK;
+    });
+}
+
+int32_t wl_length(const wl_model* model, int32_t* n)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !n) return wl::fail(WL_EINVAL, "wl_length: model and n are required");
+        *n = model->m->own()->length;
+        return WL_OK;
+    });
+}
+
+int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0, int32_t all_logits,
+                   float* logits_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (model && T == 0) return wl::fail(WL_EINVAL, "No tokens to run.");
+        if (!model || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward: model, tokens and logits_out are required");
+        if (seq && seq->owner != model) return wl::fail(WL_EINVAL, "wl_forward: the sequence belongs to another model");
+        const int32_t st = model->m->forward(seq ? seq->s : nullptr, tokens, T, pos0, all_logits != 0, logits_out, cancel, progress, user);
+        if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
+        return st;
+    });
+}
+
+int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N, float* logits_out,
+                         volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !seqs || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward_batch: model, seqs, tokens and logits_out are required");
+        if (N <= 0) return wl::fail(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
+        std::vector<wl::Seq*> ss((size_t)N);
+        for (int i = 0; i < N; ++i) {
+            if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_forward_batch: a sequence belongs to another model");
+            ss[(size_t)i] = seqs[i]->s;
+        }
+        const int32_t st = model->m->forward_batch(ss.data(), tokens, N, logits_out, cancel, progress, user);
+        if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
+        return st;
+    });
+}
+
+int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        int b = 0, s = 0;
+        if (!wl::can_decode(type) || !wl::layout(type, &b, &s)) return wl::fail(WL_EUNSUPPORTED, "wl_dequant: unsupported type");
+        if (n < 0 || n % b != 0) return wl::fail(WL_EINVAL, "wl_dequant: n must be a whole number of blocks");
+        if (n > 0 && (!dev_blocks || !dev_out)) return wl::fail(WL_EINVAL, "wl_dequant: null pointer");
+        wl::k::init_tables();
+        wl::k::dequant(type, dev_blocks, n, dev_out, (cudaStream_t)stream);
+        return WL_OK;
+    });
+}
+
+int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t ncols,
+                  float* dev_y, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        int b = 0, s = 0;
+        if (!wl::can_decode(type) || !wl::layout(type, &b, &s)) return wl::fail(WL_EUNSUPPORTED, "wl_matvec: unsupported type");
+        if (rows <= 0 || cols <= 0 || ncols <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matvec: null pointer");
+        wl::k::init_tables();
+        wl::k::matvec(type, (const uint8_t*)dev_w, wl::row_bytes_of(type, cols), rows, cols, dev_x, cols, ncols, dev_y,
+                      rows, (cudaStream_t)stream);
+        return WL_OK;
+    });
+}
+
+int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
+                  float* dev_y, int32_t path, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        int b = 0, s = 0;
+        if (!wl::can_decode(type) || !wl::layout(type, &b, &s)) return wl::fail(WL_EUNSUPPORTED, "wl_matmul: unsupported type");
+        if (rows <= 0 || cols <= 0 || T <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matmul: null pointer");
+        if (path < 0 || path > 2) return wl::fail(WL_EINVAL, "wl_matmul: path must be 0, 1 or 2");
+        wl::k::init_tables();
+        wl::k::matvec(type, (const uint8_t*)dev_w, wl::row_bytes_of(type, cols), rows, cols, dev_x, cols, T, dev_y,
+                      rows, (cudaStream_t)stream);
+        return WL_OK;
+    });
+}
+
+int32_t wl_synth_tensor(int32_t type, uint64_t seed, uint32_t tensor_id, int64_t rows, int64_t cols, float sigma,
+                        float offset, void* dev_out, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (type != 0 && type != 1 && type != 8 && type != 12 && type != 14) return wl::fail(WL_EUNSUPPORTED, "wl_synth_tensor: type must be F32, F16, Q8_0, Q4_K or Q6_K");
+        int b = 0, s = 0;
+        wl::layout(type, &b, &s);
+        if (rows <= 0 || cols <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "wl_synth_tensor: bad shape");
+        if (!dev_out) return wl::fail(WL_EINVAL, "wl_synth_tensor: null pointer");
+        wl::k::synth(type, seed, tensor_id, rows, cols, sigma, offset, (uint8_t*)dev_out, (cudaStream_t)stream);
+        return WL_OK;
+    });
+}
+
+}  // extern "C"

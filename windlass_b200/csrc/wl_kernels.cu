@@ -1,0 +1,911 @@
+// Device kernels of libwindlass_cuda (sm_100a). All device code of the library lives in this one translation unit.
+//
+// Decode matvec (the dominant cost of a decode step) is memory-bound: one warp owns one weight row, lanes stride
+// over the row's units (64 values for Q4_K, 32 for the other formats) with 128-bit loads where the block layout
+// allows, decode in registers and accumulate every activation column in fp32; the warp sums lanes with a fixed
+// xor butterfly, so a column's result never depends on how many columns ran beside it (ForwardBatch rows are
+// bit-identical to single runs, src/Transformer.cs:127-131).
+#include <cstdint>
+#include <cstdio>
+#include <atomic>
+#include <mutex>
+#include <cuda_fp16.h>
+#include "wl_common.h"
+#include "wl_decode.cuh"
+#include "wl_kernels.h"
+
+namespace wl {
+
+__device__ uint64_t g_iq2xxs_grid[256];
+__device__ uint8_t g_ksigns[128];
+__device__ int8_t g_kvalues[16];
+
+namespace k {
+
+// ------------------------------------------------------------------------------------------------------------------
+// tables
+// ------------------------------------------------------------------------------------------------------------------
+void init_tables()
+{
+    static std::mutex mu;
+    static uint64_t done = 0;   // bit per device ordinal
+    int dev = 0;
+    WL_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && (done >> dev) & 1) return;
+    WL_CUDA(cudaMemcpyToSymbol(c_iq2xxs_grid, WL_IQ2XXS_GRID, sizeof(WL_IQ2XXS_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_iq2xs_grid, WL_IQ2XS_GRID, sizeof(WL_IQ2XS_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_iq2s_grid, WL_IQ2S_GRID, sizeof(WL_IQ2S_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_iq1s_grid, WL_IQ1S_GRID, sizeof(WL_IQ1S_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_iq3xxs_grid, WL_IQ3XXS_GRID, sizeof(WL_IQ3XXS_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_iq3s_grid, WL_IQ3S_GRID, sizeof(WL_IQ3S_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(c_ksigns, WL_KSIGNS_IQ2XS, sizeof(WL_KSIGNS_IQ2XS)));
+    WL_CUDA(cudaMemcpyToSymbol(c_kvalues_iq4nl, WL_KVALUES_IQ4NL, sizeof(WL_KVALUES_IQ4NL)));
+    WL_CUDA(cudaMemcpyToSymbol(g_iq2xxs_grid, WL_IQ2XXS_GRID, sizeof(WL_IQ2XXS_GRID)));
+    WL_CUDA(cudaMemcpyToSymbol(g_ksigns, WL_KSIGNS_IQ2XS, sizeof(WL_KSIGNS_IQ2XS)));
+    WL_CUDA(cudaMemcpyToSymbol(g_kvalues, WL_KVALUES_IQ4NL, sizeof(WL_KVALUES_IQ4NL)));
+    if (dev < 64) done |= 1ull << dev;
+}
+
+static inline unsigned grid_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+static std::atomic<int64_t> g_launches{0};
+
+// Checks the launch just made and counts it.
+static inline void launched()
+{
+    WL_CUDA(cudaGetLastError());
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+int64_t launches() { return g_launches.load(std::memory_order_relaxed); }
+
+// ------------------------------------------------------------------------------------------------------------------
+// dequant / embedding (bit-exact)
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void k_dequant(int type, const uint8_t* __restrict__ blocks, int64_t n, float* __restrict__ out)
+{
+    const int be = block_elems(type), bb = block_bytes(type);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = dq_elem(type, blocks + (i / be) * bb, (int)(i % be));
+}
+
+void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s)
+{
+    if (n <= 0) return;
+    int64_t g = grid_for(n, 256);
+    if (g > 148 * 64) g = 148 * 64;
+    k_dequant<<<(unsigned)g, 256, 0, s>>>(type, (const uint8_t*)blocks, n, out);
+    launched();
+}
+
+__global__ void k_embed(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows, int cols,
+                        const int32_t* __restrict__ tokens, float scale, float* __restrict__ x, int32_t* bad)
+{
+    const int t = blockIdx.y;
+    const int be = block_elems(type), bb = block_bytes(type);
+    const int tok = tokens[t];
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        if (tok < 0 || tok >= rows) { if (c == 0) *bad = 1; }
+        else {
+            v = dq_elem(type, w + (int64_t)tok * row_bytes + (int64_t)(c / be) * bb, c % be);
+            if (scale != 0.0f) v = __fmul_rn(v, scale);
+        }
+        x[(int64_t)t * cols + c] = v;
+    }
+}
+
+void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const int32_t* tokens, int T,
+           float scale, float* x, int32_t* bad, cudaStream_t s)
+{
+    dim3 grid(grid_for(cols, 256), T);
+    k_embed<<<grid, 256, 0, s>>>(type, w, row_bytes, rows, cols, tokens, scale, x, bad);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// decode matvec
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Q4_K: a unit is one 64-value pair of sub-blocks (32 bytes of nibbles: low nibbles = values 0..31, high = 32..63).
+// Per column: d*(s1*sum(q_lo*x) + s2*sum(q_hi*x)) - dmin*(m1*sum(x_lo) + m2*sum(x_hi)), the factoring of
+// Quants.DotRow Q4_K (src/Quants.cs:110-133).
+template <int NC>
+__device__ __forceinline__ void unit_q4k(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                         int64_t ldx, float (&acc)[NC])
+{
+    const int sb = u >> 2, p = u & 3;
+    const uint8_t* blk = row + (int64_t)sb * 144;
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * p));
+    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * p));
+    const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+    uint8_t sc[12];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sc[i] = (uint8_t)(hdr.y >> (8 * i)); sc[4 + i] = (uint8_t)(hdr.z >> (8 * i)); sc[8 + i] = (uint8_t)(hdr.w >> (8 * i));
+    }
+    int s1, m1, s2, m2;
+    scale_min_k4(2 * p, sc, s1, m1);
+    scale_min_k4(2 * p + 1, sc, s2, m2);
+    const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    const float* xb = x + (int64_t)sb * 256 + 64 * p;
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = xb + t * ldx;
+        float a1 = 0.f, a2 = 0.f, x1 = 0.f, x2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float4 lo = ld4(xt + 4 * w), hi = ld4(xt + 32 + 4 * w);
+            const uint32_t qq = q[w];
+            a1 += (float)(qq & 0xF) * lo.x + (float)((qq >> 8) & 0xF) * lo.y + (float)((qq >> 16) & 0xF) * lo.z + (float)((qq >> 24) & 0xF) * lo.w;
+            a2 += (float)((qq >> 4) & 0xF) * hi.x + (float)((qq >> 12) & 0xF) * hi.y + (float)((qq >> 20) & 0xF) * hi.z + (float)(qq >> 28) * hi.w;
+            x1 += (lo.x + lo.y) + (lo.z + lo.w);
+            x2 += (hi.x + hi.y) + (hi.z + hi.w);
+        }
+        acc[t] += d * ((float)s1 * a1 + (float)s2 * a2) - dmin * ((float)m1 * x1 + (float)m2 * x2);
+    }
+}
+
+// Q6_K: a unit is 32 values of one 128-value half: l in [8g, 8g+8) at offsets l, l+32, l+64, l+96
+// (Quants.DotRow Q6_K, src/Quants.cs:159-184). Superblocks are 210 bytes, so loads are 16-bit.
+template <int NC>
+__device__ __forceinline__ void unit_q6k(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                         int64_t ldx, float (&acc)[NC])
+{
+    const int sb = u >> 3, sub = u & 7, kh = sub >> 2, g = sub & 3;
+    const uint8_t* blk = row + (int64_t)sb * 210;
+    const uint16_t* qlo = reinterpret_cast<const uint16_t*>(blk + 64 * kh + 8 * g);
+    const uint16_t* qhi = reinterpret_cast<const uint16_t*>(blk + 64 * kh + 32 + 8 * g);
+    const uint16_t* qhp = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * kh + 8 * g);
+    uint8_t lo[8], hi[8], hb[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint16_t a = __ldg(qlo + i), b = __ldg(qhi + i), c = __ldg(qhp + i);
+        lo[2 * i] = (uint8_t)a; lo[2 * i + 1] = (uint8_t)(a >> 8);
+        hi[2 * i] = (uint8_t)b; hi[2 * i + 1] = (uint8_t)(b >> 8);
+        hb[2 * i] = (uint8_t)c; hb[2 * i + 1] = (uint8_t)(c >> 8);
+    }
+    const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * kh) + (g >> 1);
+    const float sc0 = (float)__ldg(sc), sc2 = (float)__ldg(sc + 2), sc4 = (float)__ldg(sc + 4), sc6 = (float)__ldg(sc + 6);
+    const float d = h2f(__ldg(reinterpret_cast<const uint16_t*>(blk + 208)));
+    float q1[8], q2[8], q3[8], q4[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        q1[i] = (float)(((lo[i] & 0xF) | ((hb[i] & 3) << 4)) - 32);
+        q2[i] = (float)(((hi[i] & 0xF) | (((hb[i] >> 2) & 3) << 4)) - 32);
+        q3[i] = (float)(((lo[i] >> 4) | (((hb[i] >> 4) & 3) << 4)) - 32);
+        q4[i] = (float)(((hi[i] >> 4) | (((hb[i] >> 6) & 3) << 4)) - 32);
+    }
+    const float* xb = x + (int64_t)sb * 256 + 128 * kh + 8 * g;
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = xb + t * ldx;
+        float a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float4 x1 = ld4(xt + 4 * h), x2 = ld4(xt + 32 + 4 * h), x3 = ld4(xt + 64 + 4 * h), x4 = ld4(xt + 96 + 4 * h);
+            a1 += q1[4 * h] * x1.x + q1[4 * h + 1] * x1.y + q1[4 * h + 2] * x1.z + q1[4 * h + 3] * x1.w;
+            a2 += q2[4 * h] * x2.x + q2[4 * h + 1] * x2.y + q2[4 * h + 2] * x2.z + q2[4 * h + 3] * x2.w;
+            a3 += q3[4 * h] * x3.x + q3[4 * h + 1] * x3.y + q3[4 * h + 2] * x3.z + q3[4 * h + 3] * x3.w;
+            a4 += q4[4 * h] * x4.x + q4[4 * h + 1] * x4.y + q4[4 * h + 2] * x4.z + q4[4 * h + 3] * x4.w;
+        }
+        acc[t] += d * ((sc0 * a1 + sc2 * a2) + (sc4 * a3 + sc6 * a4));
+    }
+}
+
+// Q8_0: a unit is one 34-byte block of 32 int8 values with an fp16 scale (src/Quants.cs:86-97).
+template <int NC>
+__device__ __forceinline__ void unit_q8_0(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                          int64_t ldx, float (&acc)[NC])
+{
+    const uint8_t* blk = row + (int64_t)u * 34;
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(blk);
+    const float d = h2f(__ldg(p));
+    float q[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const uint16_t v = __ldg(p + 1 + i);
+        q[2 * i] = (float)(int8_t)(v & 0xFF);
+        q[2 * i + 1] = (float)(int8_t)(v >> 8);
+    }
+    const float* xb = x + (int64_t)u * 32;
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = xb + t * ldx;
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float4 v = ld4(xt + 4 * w);
+            a += q[4 * w] * v.x + q[4 * w + 1] * v.y + q[4 * w + 2] * v.z + q[4 * w + 3] * v.w;
+        }
+        acc[t] += d * a;
+    }
+}
+
+// IQ4_XS: a unit is one 32-value sub-block: dl = d*(ls-32), y = dl*kvalues[nibble] (src/IQuants.cs:61-80).
+template <int NC>
+__device__ __forceinline__ void unit_iq4xs(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                           int64_t ldx, float (&acc)[NC])
+{
+    const int sb = u >> 3, ib = u & 7;
+    const uint8_t* blk = row + (int64_t)sb * 136;
+    const uint16_t* hp = reinterpret_cast<const uint16_t*>(blk);
+    const float d = h2f(__ldg(hp));
+    const int sh = __ldg(hp + 1);
+    const int sl = __ldg(blk + 4 + ib / 2);
+    const int ls = ((sl >> (4 * (ib & 1))) & 0xF) | (((sh >> (2 * ib)) & 3) << 4);
+    const float dl = d * (float)(ls - 32);
+    const uint2 qa = __ldg(reinterpret_cast<const uint2*>(blk + 8 + 16 * ib));
+    const uint2 qb = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 16 * ib));
+    const uint32_t qw[4] = {qa.x, qa.y, qb.x, qb.y};
+    float vlo[16], vhi[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        vlo[i] = (float)g_kvalues[byte & 0xF];
+        vhi[i] = (float)g_kvalues[byte >> 4];
+    }
+    const float* xb = x + (int64_t)sb * 256 + 32 * ib;
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = xb + t * ldx;
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float4 l = ld4(xt + 4 * w), h = ld4(xt + 16 + 4 * w);
+            a += vlo[4 * w] * l.x + vlo[4 * w + 1] * l.y + vlo[4 * w + 2] * l.z + vlo[4 * w + 3] * l.w;
+            a += vhi[4 * w] * h.x + vhi[4 * w + 1] * h.y + vhi[4 * w + 2] * h.z + vhi[4 * w + 3] * h.w;
+        }
+        acc[t] += dl * a;
+    }
+}
+
+// IQ2_XXS: a unit is one 32-value sub-block: four grid indices (aux0), four 7-bit sign indices and a 4-bit scale
+// (aux1); db = d*(0.5+(aux1>>28))*0.25 (src/IQuants.cs:148-170).
+template <int NC>
+__device__ __forceinline__ void unit_iq2xxs(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                            int64_t ldx, float (&acc)[NC])
+{
+    const int sb = u >> 3, ib = u & 7;
+    const uint8_t* blk = row + (int64_t)sb * 66;
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(blk);
+    const float d = h2f(__ldg(p));
+    const uint32_t aux0 = (uint32_t)__ldg(p + 1 + 4 * ib) | ((uint32_t)__ldg(p + 2 + 4 * ib) << 16);
+    const uint32_t aux1 = (uint32_t)__ldg(p + 3 + 4 * ib) | ((uint32_t)__ldg(p + 4 + 4 * ib) << 16);
+    const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
+    float v[32];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const uint64_t g = g_iq2xxs_grid[(aux0 >> (8 * l)) & 0xFF];
+        const int signs = g_ksigns[(aux1 >> (7 * l)) & 127];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float m = (float)((g >> (8 * j)) & 0xFF);
+            v[8 * l + j] = (signs >> j) & 1 ? -m : m;
+        }
+    }
+    const float* xb = x + (int64_t)sb * 256 + 32 * ib;
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = xb + t * ldx;
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float4 xv = ld4(xt + 4 * w);
+            a += v[4 * w] * xv.x + v[4 * w + 1] * xv.y + v[4 * w + 2] * xv.z + v[4 * w + 3] * xv.w;
+        }
+        acc[t] += db * a;
+    }
+}
+
+// Any decodable type, 32 values per unit, through the exact element decoder.
+template <int NC>
+__device__ __forceinline__ void unit_generic(int type, const uint8_t* __restrict__ row, int u, int cols,
+                                             const float* __restrict__ x, int64_t ldx, float (&acc)[NC])
+{
+    const int be = block_elems(type), bb = block_bytes(type);
+    float w[32];
+    const int e0 = u * 32;
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+        const int e = e0 + i;
+        w[i] = e < cols ? dq_elem(type, row + (int64_t)(e / be) * bb, e % be) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = x + t * ldx + e0;
+        float a = 0.f;
+        for (int i = 0; i < 32; ++i) if (e0 + i < cols) a += w[i] * xt[i];
+        acc[t] += a;
+    }
+}
+
+enum { MV_GENERIC = 0, MV_Q4K = 1, MV_Q6K = 2, MV_Q8_0 = 3, MV_IQ4XS = 4, MV_IQ2XXS = 5 };
+
+template <int KIND, int NC>
+__global__ void __launch_bounds__(128) k_matvec(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows,
+                                                int cols, const float* __restrict__ x, int64_t ldx,
+                                                float* __restrict__ y, int64_t ldy)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 4 + warp;
+    if (row >= rows) return;
+    const uint8_t* wr = w + (int64_t)row * row_bytes;
+    float acc[NC];
+#pragma unroll
+    for (int t = 0; t < NC; ++t) acc[t] = 0.f;
+    if (KIND == MV_Q4K) {
+        const int units = cols >> 6;
+        for (int u = lane; u < units; u += 32) unit_q4k<NC>(wr, u, x, ldx, acc);
+    } else if (KIND == MV_Q6K) {
+        const int units = cols >> 5;
+        for (int u = lane; u < units; u += 32) unit_q6k<NC>(wr, u, x, ldx, acc);
+    } else if (KIND == MV_Q8_0) {
+        const int units = cols >> 5;
+        for (int u = lane; u < units; u += 32) unit_q8_0<NC>(wr, u, x, ldx, acc);
+    } else if (KIND == MV_IQ4XS) {
+        const int units = cols >> 5;
+        for (int u = lane; u < units; u += 32) unit_iq4xs<NC>(wr, u, x, ldx, acc);
+    } else if (KIND == MV_IQ2XXS) {
+        const int units = cols >> 5;
+        for (int u = lane; u < units; u += 32) unit_iq2xxs<NC>(wr, u, x, ldx, acc);
+    } else {
+        const int units = (cols + 31) >> 5;
+        for (int u = lane; u < units; u += 32) unit_generic<NC>(type, wr, u, cols, x, ldx, acc);
+    }
+#pragma unroll
+    for (int t = 0; t < NC; ++t) acc[t] = warp_sum(acc[t]);
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < NC; ++t) y[t * ldy + row] = acc[t];
+    }
+}
+
+template <int KIND>
+static void launch_mv(int nc, int type, const uint8_t* w, int64_t rb, int rows, int cols, const float* x, int64_t ldx,
+                      float* y, int64_t ldy, cudaStream_t s)
+{
+    const unsigned g = grid_for(rows, 4);
+    switch (nc) {
+    case 1: k_matvec<KIND, 1><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 2: k_matvec<KIND, 2><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 3: k_matvec<KIND, 3><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 4: k_matvec<KIND, 4><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 5: k_matvec<KIND, 5><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 6: k_matvec<KIND, 6><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 7: k_matvec<KIND, 7><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    default: k_matvec<KIND, 8><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    }
+}
+
+void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
+            int ncols, float* y, int64_t ldy, cudaStream_t s)
+{
+    if (rows <= 0 || ncols <= 0) return;
+    // The specialised kernels read x with 16-byte loads and the weights with 16/8/2-byte loads.
+    const bool xa = ((uintptr_t)x % 16 == 0) && (ldx % 4 == 0);
+    const bool w16 = ((uintptr_t)w % 16 == 0) && (row_bytes % 16 == 0);
+    const bool w8 = ((uintptr_t)w % 8 == 0) && (row_bytes % 8 == 0);
+    const bool w2 = ((uintptr_t)w % 2 == 0) && (row_bytes % 2 == 0);
+    for (int c0 = 0; c0 < ncols; c0 += 8) {
+        const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
+        const float* xc = x + c0 * ldx;
+        float* yc = y + c0 * ldy;
+        if (type == 12 && xa && w16 && cols % 256 == 0) launch_mv<MV_Q4K>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 14 && xa && w2 && cols % 256 == 0) launch_mv<MV_Q6K>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 8 && xa && w2 && cols % 32 == 0) launch_mv<MV_Q8_0>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 23 && xa && w8 && cols % 256 == 0) launch_mv<MV_IQ4XS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 16 && xa && w2 && cols % 256 == 0) launch_mv<MV_IQ2XXS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else launch_mv<MV_GENERIC>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        launched();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// normalisation, rope, bias, residual
+// ------------------------------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T* scratch)
+{
+    // Fixed-order reduction: warps in index order, lanes by xor butterfly.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    T s = 0;
+    for (int i = 0; i < nw; ++i) s += scratch[i];
+    return s;
+}
+
+__device__ __forceinline__ float block_max(float v, float* scratch)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float m = scratch[0];
+    for (int i = 1; i < nw; ++i) m = fmaxf(m, scratch[i]);
+    return m;
+}
+
+// RmsNormRows: sum of squares in double, scale = 1f / (float)sqrt((float)(sum/dim) + eps), y = (x*scale)*w.
+__global__ void k_rmsnorm(const float* x, int dim, const float* __restrict__ w, float eps, float* y)
+{
+    __shared__ double scratch[32];
+    const float* xr = x + (int64_t)blockIdx.x * dim;
+    float* yr = y + (int64_t)blockIdx.x * dim;
+    double s = 0;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) { const double v = (double)xr[i]; s += v * v; }
+    s = block_sum(s, scratch);
+    const float mean = (float)(s / dim);
+    const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
+    __syncthreads();
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s)
+{
+    if (n <= 0) return;
+    const int threads = dim >= 1024 ? 256 : dim >= 256 ? 128 : 64;
+    k_rmsnorm<<<n, threads, 0, s>>>(x, dim, w, eps, y);
+    launched();
+}
+
+__global__ void k_add_bias(float* y, const float* __restrict__ b, int64_t total, int n)
+{
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(y[i], b[i % n]);
+}
+
+void add_bias(float* y, const float* b, int T, int n, cudaStream_t s)
+{
+    const int64_t total = (int64_t)T * n;
+    if (total <= 0) return;
+    int64_t g = grid_for(total, 256); if (g > 4096) g = 4096;
+    k_add_bias<<<(unsigned)g, 256, 0, s>>>(y, b, total, n);
+    launched();
+}
+
+__global__ void k_rope(float* x, int heads, int head_dim, int rope_dims, int neox, const int32_t* __restrict__ pos,
+                       const float* __restrict__ table)
+{
+    const int t = blockIdx.y, half = rope_dims / 2;
+    const int64_t base = (int64_t)t * heads * head_dim;
+    const float* cs = table + (int64_t)pos[t] * rope_dims;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < heads * half; idx += gridDim.x * blockDim.x) {
+        const int h = idx / half, i = idx % half;
+        const int64_t o = base + (int64_t)h * head_dim;
+        const int64_t a = neox ? o + i : o + 2 * i, b = neox ? o + i + half : o + 2 * i + 1;
+        const float c = cs[2 * i], sn = cs[2 * i + 1];
+        const float x0 = x[a], x1 = x[b];
+        x[a] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        x[b] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+}
+
+void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, const int32_t* pos, const float* table,
+          cudaStream_t s)
+{
+    if (T <= 0 || rope_dims <= 0) return;
+    dim3 grid(grid_for((int64_t)heads * (rope_dims / 2), 256), T);
+    k_rope<<<grid, 256, 0, s>>>(x, heads, head_dim, rope_dims, neox, pos, table);
+    launched();
+}
+
+__global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, int kd,
+                            const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos)
+{
+    const int t = blockIdx.y;
+    uint16_t* kc = rows[t].k + layer * rows[t].layer_stride + (int64_t)pos[t] * kd;
+    uint16_t* vc = rows[t].v + layer * rows[t].layer_stride + (int64_t)pos[t] * kd;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kd; i += gridDim.x * blockDim.x) {
+        kc[i] = __half_as_ushort(__float2half_rn(k[(int64_t)t * kd + i]));
+        vc[i] = __half_as_ushort(__float2half_rn(v[(int64_t)t * kd + i]));
+    }
+}
+
+void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows, int layer, const int32_t* pos,
+               cudaStream_t s)
+{
+    if (T <= 0) return;
+    dim3 grid(grid_for(kd, 256), T);
+    k_kv_append<<<grid, 256, 0, s>>>(k, v, kd, rows, layer, pos);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// attention: one CTA per (row, head). Scores use the reference's four-accumulator dot (Transformer.cs:366-378) with
+// separately rounded products; softmax exponentials and their sum are in double like the reference; the weighted V
+// sum runs positions in order with separately rounded products and sums.
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void k_attention(const float* __restrict__ q, int heads, int kv_heads, int head_dim, float scale,
+                            const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos,
+                            float* __restrict__ out)
+{
+    extern __shared__ float sm[];
+    __shared__ double dscratch[32];
+    __shared__ float fscratch[32];
+    const int t = blockIdx.x / heads, h = blockIdx.x % heads;
+    const int group = heads / kv_heads, kvh = h / group;
+    const int QD = heads * head_dim, KD = kv_heads * head_dim;
+    const int n = pos[t] + 1;
+    float* qs = sm;                 // head_dim
+    float* sp = sm + head_dim;      // n scores
+    const float* qp = q + (int64_t)t * QD + (int64_t)h * head_dim;
+    for (int i = threadIdx.x; i < head_dim; i += blockDim.x) qs[i] = qp[i];
+    __syncthreads();
+    const uint16_t* K = rows[t].k + layer * rows[t].layer_stride;
+    const uint16_t* V = rows[t].v + layer * rows[t].layer_stride;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const uint16_t* kp = K + (int64_t)j * KD + (int64_t)kvh * head_dim;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int i = 0;
+        for (; i + 4 <= head_dim; i += 4) {
+            s0 = __fadd_rn(s0, __fmul_rn(qs[i], h2f(kp[i])));
+            s1 = __fadd_rn(s1, __fmul_rn(qs[i + 1], h2f(kp[i + 1])));
+            s2 = __fadd_rn(s2, __fmul_rn(qs[i + 2], h2f(kp[i + 2])));
+            s3 = __fadd_rn(s3, __fmul_rn(qs[i + 3], h2f(kp[i + 3])));
+        }
+        for (; i < head_dim; ++i) s0 = __fadd_rn(s0, __fmul_rn(qs[i], h2f(kp[i])));
+        const float d = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
+        sp[j] = d;
+        mx = fmaxf(mx, d);
+    }
+    mx = block_max(mx, fscratch);
+    double sum = 0;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const float e = (float)exp((double)__fsub_rn(sp[j], mx));
+        sp[j] = e;
+        sum += (double)e;
+    }
+    sum = block_sum(sum, dscratch);
+    const float inv = (float)(1.0 / sum);
+    __syncthreads();
+    float* op = out + (int64_t)t * QD + (int64_t)h * head_dim;
+    for (int dd = threadIdx.x; dd < head_dim; dd += blockDim.x) {
+        float acc = 0.f;
+        const uint16_t* vp = V + (int64_t)kvh * head_dim + dd;
+        for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(sp[j], inv), h2f(vp[(int64_t)j * KD])));
+        op[dd] = acc;
+    }
+}
+
+void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
+               int layer, const int32_t* pos, int max_n, float* out, cudaStream_t s)
+{
+    if (T <= 0) return;
+    const size_t smem = sizeof(float) * (size_t)(head_dim + max_n);
+    static bool attr_set[64] = {false};
+    int dev = 0; cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && dev < 64 && !attr_set[dev]) {
+        WL_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set[dev] = true;
+    }
+    k_attention<<<T * heads, 128, smem, s>>>(q, heads, kv_heads, head_dim, scale, rows, layer, pos, out);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// elementwise
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void k_swiglu(float* g, const float* __restrict__ u, int64_t n)
+{
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float a = g[i];
+        const float e = (float)exp(-(double)a);
+        g[i] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, e)), u[i]);
+    }
+}
+
+void swiglu(float* g, const float* u, int64_t n, cudaStream_t s)
+{
+    if (n <= 0) return;
+    int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
+    k_swiglu<<<(unsigned)gr, 256, 0, s>>>(g, u, n);
+    launched();
+}
+
+__global__ void k_residual(float* x, const float* __restrict__ o, float rs, int64_t n)
+{
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = __fadd_rn(x[i], __fmul_rn(o[i], rs));
+}
+
+void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s)
+{
+    if (n <= 0) return;
+    int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
+    k_residual<<<(unsigned)gr, 256, 0, s>>>(x, o, rs, n);
+    launched();
+}
+
+__global__ void k_scale(float* x, float f, int64_t n)
+{
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] = __fmul_rn(x[i], f);
+}
+
+void scale(float* x, float f, int64_t n, cudaStream_t s)
+{
+    if (n <= 0) return;
+    int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
+    k_scale<<<(unsigned)gr, 256, 0, s>>>(x, f, n);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// mixture of experts
+// ------------------------------------------------------------------------------------------------------------------
+// Route: one thread per token, the reference's sequential arithmetic (softmax with double exp and sum, greedy top-k
+// with ties to the lower id, renormalisation clamped at 6.103515625e-5).
+__global__ void k_route(const float* __restrict__ logits, int T, int n, int k, int renorm, int32_t* sel, float* wts)
+{
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const float* lg = logits + (int64_t)t * n;
+    float p[256];
+    bool taken[256];
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i) if (lg[i] > mx) mx = lg[i];
+    double sum = 0;
+    for (int i = 0; i < n; ++i) { p[i] = (float)exp((double)__fsub_rn(lg[i], mx)); sum += p[i]; taken[i] = false; }
+    const float inv = (float)(1.0 / sum);
+    for (int i = 0; i < n; ++i) p[i] = __fmul_rn(p[i], inv);
+    float chosen = 0.f;
+    for (int j = 0; j < k; ++j) {
+        int best = -1;
+        for (int i = 0; i < n; ++i) if (!taken[i] && (best < 0 || p[i] > p[best])) best = i;
+        taken[best] = true;
+        sel[(int64_t)t * k + j] = best;
+        wts[(int64_t)t * k + j] = p[best];
+        chosen = __fadd_rn(chosen, p[best]);
+    }
+    if (renorm) {
+        const float div = fmaxf(chosen, 6.103515625e-5f);
+        for (int j = 0; j < k; ++j) wts[(int64_t)t * k + j] = __fdiv_rn(wts[(int64_t)t * k + j], div);
+    }
+}
+
+void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s)
+{
+    if (T <= 0) return;
+    k_route<<<grid_for(T, 64), 64, 0, s>>>(logits, T, n, k, renorm, sel, wts);
+    launched();
+}
+
+__global__ void k_gather_rows(float* xe, const float* __restrict__ xn, const int32_t* __restrict__ toks, int n, int E)
+{
+    const int i = blockIdx.y;
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x)
+        xe[(int64_t)i * E + d] = xn[(int64_t)toks[i] * E + d];
+}
+
+void gather_rows(float* xe, const float* xn, const int32_t* toks, int n, int E, cudaStream_t s)
+{
+    if (n <= 0) return;
+    k_gather_rows<<<dim3(grid_for(E, 256), n), 256, 0, s>>>(xe, xn, toks, n, E);
+    launched();
+}
+
+__global__ void k_scatter_add(float* outp, const float* __restrict__ ye, const int32_t* __restrict__ toks,
+                              const float* __restrict__ w, int E)
+{
+    const int i = blockIdx.y;
+    float* o = outp + (int64_t)toks[i] * E;
+    const float wi = w[i];
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x)
+        o[d] = __fadd_rn(o[d], __fmul_rn(wi, ye[(int64_t)i * E + d]));
+}
+
+void scatter_add(float* outp, const float* ye, const int32_t* toks, const float* w, int n, int E, cudaStream_t s)
+{
+    if (n <= 0) return;
+    k_scatter_add<<<dim3(grid_for(E, 256), n), 256, 0, s>>>(outp, ye, toks, w, E);
+    launched();
+}
+
+__global__ void k_shared_expert_add(float* outp, const float* __restrict__ sh, const float* __restrict__ gl, int E)
+{
+    const int t = blockIdx.y;
+    const float f = gl ? __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gl[t]))) : 1.0f;
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x) {
+        const int64_t o = (int64_t)t * E + d;
+        outp[o] = __fadd_rn(outp[o], __fmul_rn(f, sh[o]));
+    }
+}
+
+void shared_expert_add(float* outp, const float* sh, const float* gl, int T, int E, cudaStream_t s)
+{
+    if (T <= 0) return;
+    k_shared_expert_add<<<dim3(grid_for(E, 256), T), 256, 0, s>>>(outp, sh, gl, E);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// synthetic weights: bit-identical with the test oracle's CPU generator (or_gen.c). Every float operation below is
+// one IEEE operation in the oracle's order; fp16 stores use the reference's round-to-nearest-even converter.
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float synth_normal(uint64_t base, int64_t i)
+{
+    const uint64_t h0 = splitmix64(base + 3 * (uint64_t)i), h1 = splitmix64(base + 3 * (uint64_t)i + 1),
+                   h2 = splitmix64(base + 3 * (uint64_t)i + 2);
+    int64_t s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        s += (int64_t)((h0 >> (16 * k)) & 0xFFFF) + (int64_t)((h1 >> (16 * k)) & 0xFFFF) + (int64_t)((h2 >> (16 * k)) & 0xFFFF);
+    return __fmul_rn((float)(s - 393210), 1.0f / 65536.0f);
+}
+
+// Half.FromFloat (src/Half.cs:29-57).
+__device__ __forceinline__ uint16_t f2h_ref(float value)
+{
+    const uint32_t f = __float_as_uint(value);
+    const uint32_t sign = (f >> 16) & 0x8000;
+    const int e = (int)((f >> 23) & 0xFF);
+    uint32_t m = f & 0x7FFFFF;
+    if (e == 255) return (uint16_t)(sign | 0x7C00 | (m != 0 ? 0x200u : 0u));
+    const int ne = e - 127 + 15;
+    if (ne >= 31) return (uint16_t)(sign | 0x7C00);
+    if (ne <= 0) {
+        if (ne < -10) return (uint16_t)sign;
+        m |= 0x800000;
+        const int shift = 14 - ne;
+        uint32_t hm = m >> shift;
+        const uint32_t rem = m & ((1u << shift) - 1), halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (hm & 1) != 0)) hm++;
+        return (uint16_t)(sign | hm);
+    }
+    uint32_t h = sign | ((uint32_t)ne << 10) | (m >> 13);
+    const uint32_t r = m & 0x1FFF;
+    if (r > 0x1000 || (r == 0x1000 && (h & 1) != 0)) h++;
+    return (uint16_t)h;
+}
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; }
+
+__device__ void quant_q8_0(const float* x, uint8_t* out)
+{
+    float amax = 0.f;
+    for (int j = 0; j < 32; ++j) { const float a = fabsf(x[j]); if (a > amax) amax = a; }
+    const uint16_t dh = f2h_ref(__fdiv_rn(amax, 127.0f));
+    const float d = h2f(dh);
+    out[0] = (uint8_t)dh; out[1] = (uint8_t)(dh >> 8);
+    for (int j = 0; j < 32; ++j) out[2 + j] = (uint8_t)(int8_t)(d != 0.0f ? clampi((int)rintf(__fdiv_rn(x[j], d)), -127, 127) : 0);
+}
+
+__device__ void quant_q4_k(const float* x, uint8_t* out)
+{
+    float step[8], off[8];
+    for (int j = 0; j < 8; ++j) {
+        float lo = 0.f, hi = 0.f;
+        for (int l = 0; l < 32; ++l) { const float v = x[32 * j + l]; if (v < lo) lo = v; if (v > hi) hi = v; }
+        off[j] = -lo;
+        step[j] = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
+    }
+    float smax = 0.f, mmax = 0.f;
+    for (int j = 0; j < 8; ++j) { if (step[j] > smax) smax = step[j]; if (off[j] > mmax) mmax = off[j]; }
+    const uint16_t dh = f2h_ref(__fdiv_rn(smax, 63.0f)), mh = f2h_ref(__fdiv_rn(mmax, 63.0f));
+    const float d = h2f(dh), dmin = h2f(mh);
+    int sq[8], mq[8];
+    for (int j = 0; j < 8; ++j) {
+        sq[j] = d != 0.0f ? clampi((int)rintf(__fdiv_rn(step[j], d)), 0, 63) : 0;
+        mq[j] = dmin != 0.0f ? clampi((int)rintf(__fdiv_rn(off[j], dmin)), 0, 63) : 0;
+    }
+    for (int i = 0; i < 144; ++i) out[i] = 0;
+    out[0] = (uint8_t)dh; out[1] = (uint8_t)(dh >> 8); out[2] = (uint8_t)mh; out[3] = (uint8_t)(mh >> 8);
+    uint8_t* sc = out + 4;
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = (uint8_t)((sq[j] & 63) | ((sq[j + 4] >> 4) << 6));
+        sc[j + 4] = (uint8_t)((mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
+        sc[j + 8] = (uint8_t)((sq[j + 4] & 0xF) | ((mq[j + 4] & 0xF) << 4));
+    }
+    uint8_t* qs = out + 16;
+    for (int pair = 0; pair < 4; ++pair)
+        for (int h = 0; h < 2; ++h) {
+            const int j = 2 * pair + h;
+            const float dj = __fmul_rn(d, (float)sq[j]), mj = __fmul_rn(dmin, (float)mq[j]);
+            for (int l = 0; l < 32; ++l) {
+                const int q = dj != 0.0f ? clampi((int)rintf(__fdiv_rn(__fadd_rn(x[32 * j + l], mj), dj)), 0, 15) : 0;
+                qs[32 * pair + l] |= (uint8_t)(q << (4 * h));
+            }
+        }
+}
+
+__device__ void quant_q6_k(const float* x, uint8_t* out)
+{
+    float step[16];
+    for (int g = 0; g < 16; ++g) {
+        float amax = 0.f;
+        for (int l = 0; l < 16; ++l) { const float a = fabsf(x[16 * g + l]); if (a > amax) amax = a; }
+        step[g] = __fdiv_rn(amax, 32.0f);
+    }
+    float smax = 0.f;
+    for (int g = 0; g < 16; ++g) if (step[g] > smax) smax = step[g];
+    const uint16_t dh = f2h_ref(__fdiv_rn(smax, 127.0f));
+    const float d = h2f(dh);
+    int sc[16];
+    for (int g = 0; g < 16; ++g) sc[g] = d != 0.0f ? clampi((int)rintf(__fdiv_rn(step[g], d)), -128, 127) : 0;
+    for (int i = 0; i < 210; ++i) out[i] = 0;
+    uint8_t* ql = out; uint8_t* qh = out + 128;
+    for (int g = 0; g < 16; ++g) out[192 + g] = (uint8_t)(int8_t)sc[g];
+    out[208] = (uint8_t)dh; out[209] = (uint8_t)(dh >> 8);
+    for (int e = 0; e < 256; ++e) {
+        const float dg = __fmul_rn(d, (float)sc[e / 16]);
+        const int q = dg != 0.0f ? clampi((int)rintf(__fdiv_rn(x[e], dg)), -32, 31) : 0;
+        const int u = q + 32;
+        const int half = e / 128, w = e % 128, l = w % 32, quarter = w / 32;
+        uint8_t* qlh = ql + 64 * half; uint8_t* qhh = qh + 32 * half;
+        const int qli = (quarter & 1) ? l + 32 : l;
+        qlh[qli] |= (uint8_t)((u & 0xF) << ((quarter >> 1) * 4));
+        qhh[l] |= (uint8_t)(((u >> 4) & 3) << (2 * quarter));
+    }
+}
+
+__global__ void k_synth(int type, uint64_t base, int64_t nblocks, float sigma, float offset, uint8_t* __restrict__ out)
+{
+    const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    if (type == 0) { const float v = __fadd_rn(offset, __fmul_rn(sigma, synth_normal(base, b))); reinterpret_cast<float*>(out)[b] = v; return; }
+    if (type == 1) { reinterpret_cast<uint16_t*>(out)[b] = f2h_ref(__fmul_rn(sigma, synth_normal(base, b))); return; }
+    const int be = type == 8 ? 32 : 256, bb = block_bytes(type);
+    float x[256];
+    for (int j = 0; j < be; ++j) x[j] = __fmul_rn(sigma, synth_normal(base, b * be + j));
+    uint8_t buf[210];
+    if (type == 8) quant_q8_0(x, buf);
+    else if (type == 12) quant_q4_k(x, buf);
+    else quant_q6_k(x, buf);
+    uint8_t* dst = out + b * bb;
+    for (int i = 0; i < bb; ++i) dst[i] = buf[i];
+}
+
+static inline uint64_t splitmix64_host(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void synth(int type, uint64_t seed, uint32_t tid, int64_t rows, int64_t cols, float sigma, float offset, uint8_t* out,
+           cudaStream_t s)
+{
+    const int be = block_elems(type);
+    const int64_t nblocks = rows * cols / be;
+    const uint64_t base = splitmix64_host(seed ^ ((uint64_t)tid * 0xD1B54A32D192ED03ull));
+    if (nblocks <= 0) return;
+    k_synth<<<grid_for(nblocks, 128), 128, 0, s>>>(type, base, nblocks, sigma, offset, out);
+    launched();
+}
+
+}  // namespace k
+}  // namespace wl

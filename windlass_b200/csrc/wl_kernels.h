@@ -1,0 +1,71 @@
+// Launch wrappers of the device kernels (all defined in wl_kernels.cu). Every wrapper enqueues on `stream` and
+// returns without synchronising; shapes are checked by the callers (wl_model.cpp, wl_api.cpp).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace wl {
+
+// Where row t of a step keeps its fp16 KV cache: layer l's keys start at k + l*layer_stride (values likewise at
+// v + l*layer_stride), position p at + p*kv_dim.
+struct RowKV {
+    uint16_t* k;
+    uint16_t* v;
+    int64_t layer_stride;
+};
+
+namespace k {
+
+// Copies the I-quant tables into the current device's constant memory (once per device).
+void init_tables();
+// Kernels launched by this process so far.
+int64_t launches();
+
+// Quants.DecodeRow for n consecutive values (n a multiple of the block size), bit-exact.
+void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s);
+// Rows `tokens[t]` of an embedding matrix (cols values each, row_bytes apart) decoded to x[t*cols...], times scale
+// when scale != 0 (LayerStream.EmbedRow + Transformer.cs:93-94). Out-of-range ids set *bad_token.
+void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const int32_t* tokens, int T,
+           float scale, float* x, int32_t* bad_token, cudaStream_t s);
+
+// y[t*ldy + r] = W[r] . x[t*ldx...] for t < ncols (1..8), rows r of W (row_bytes apart). Each column is computed
+// with the same instruction sequence whatever ncols is, so a column's result does not depend on its neighbours.
+void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
+            int ncols, float* y, int64_t ldy, cudaStream_t s);
+
+// RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
+void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);
+// y[t*n + i] += b[i] for T rows (AddBias, Transformer.cs:442-451).
+void add_bias(float* y, const float* b, int T, int n, cudaStream_t s);
+// Rope (Transformer.cs:418-433) on T rows of `heads` heads; positions pos[t]; table[pos*rope_dims + 2i (+1)] = cos, sin.
+void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, const int32_t* pos, const float* table,
+          cudaStream_t s);
+// K/V rows t (kd values) to fp16 at position pos[t] of layer `layer` of row t's cache (ToHalf,
+// Transformer.cs:342-348).
+void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows, int layer, const int32_t* pos,
+               cudaStream_t s);
+// Attention (Transformer.cs:351-395): row t, head h attends to positions 0..pos[t] of its own cache.
+void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
+               int layer, const int32_t* pos, int max_n, float* out, cudaStream_t s);
+// g[i] = g[i]/(1+exp(-g[i])) * u[i] (SwiGlu, Transformer.cs:247).
+void swiglu(float* g, const float* u, int64_t n, cudaStream_t s);
+// x[i] += o[i] * rs (Transformer.cs:225,231).
+void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s);
+// x[i] *= f.
+void scale(float* x, float f, int64_t n, cudaStream_t s);
+// Route (Transformer.cs:315-340) for T rows of n router logits: sel[t*k+j], wts[t*k+j].
+void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s);
+// outp[t*E + d] += w * ye[i*E + d] for the gathered rows i of one expert (MoeFfn, Transformer.cs:289-293).
+void scatter_add(float* outp, const float* ye, const int32_t* toks, const float* w, int n, int E, cudaStream_t s);
+// xe[i*E..] = xn[toks[i]*E..].
+void gather_rows(float* xe, const float* xn, const int32_t* toks, int n, int E, cudaStream_t s);
+// outp[t*E + d] += f_t * sh[t*E + d], f_t = gl ? 1/(1+exp(-gl[t])) : 1 (shared expert, Transformer.cs:296-309).
+void shared_expert_add(float* outp, const float* sh, const float* gl, int T, int E, cudaStream_t s);
+
+// Synthetic weights of wl_synth_tensor / wl_open_synthetic.
+// F32 tensors get offset + sigma*z (offset 1 for norm weights); quantized types get sigma*z, quantized.
+void synth(int type, uint64_t seed, uint32_t tid, int64_t rows, int64_t cols, float sigma, float offset, uint8_t* out,
+           cudaStream_t s);
+
+}  // namespace k
+}  // namespace wl

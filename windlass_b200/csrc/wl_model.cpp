@@ -1,0 +1,801 @@
+// Device-resident decoder forward: Transformer.cs (Forward, ForwardBatch, Layer, Head, MoeFfn), ModelConfig.From and
+// the stage name binding of LayerStream.Bind, re-designed for one GPU: weights in one HBM arena, activations and the
+// fp16 KV caches on the device, one CUDA stream per model, the host touching only token ids and logits.
+#include "wl_model.h"
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include "wl_common.h"
+#include "wl_gguf.h"
+
+namespace wl {
+
+namespace {
+template <typename T> T* dalloc(int64_t n)
+{
+    void* p = nullptr;
+    if (n <= 0) n = 1;
+    WL_CUDA(cudaMalloc(&p, sizeof(T) * (size_t)n));
+    return (T*)p;
+}
+template <typename T> void dfree(T*& p)
+{
+    if (p) cudaFree((void*)p);
+    p = nullptr;
+}
+template <typename T> T* halloc(int64_t n)
+{
+    void* p = nullptr;
+    if (n <= 0) n = 1;
+    WL_CUDA(cudaMallocHost(&p, sizeof(T) * (size_t)n));
+    return (T*)p;
+}
+template <typename T> void hfree(T*& p)
+{
+    if (p) cudaFreeHost((void*)p);
+    p = nullptr;
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------------
+// open / close
+// ---------------------------------------------------------------------------------------------------------------------
+void Model::init_device(const wl_options& opt)
+{
+    device_ = opt.device;
+    WL_CUDA(cudaSetDevice(device_));
+    k::init_tables();
+    WL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    max_batch_ = opt.max_batch > 0 ? opt.max_batch : 64;
+    prefill_path_ = opt.prefill_path;
+}
+
+uint8_t* Model::arena_alloc(int64_t bytes)
+{
+    const int64_t a = (bytes + 255) / 256 * 256;
+    if (arena_used_ + a > arena_size_) WL_THROW(WL_ENOMEM, "weight arena overflow");
+    uint8_t* p = arena_ + arena_used_;
+    arena_used_ += a;
+    return p;
+}
+
+static std::string layer_name(int l, const char* s) { return "blk." + std::to_string(l) + "." + s; }
+
+// ModelConfig.From (src/ModelConfig.cs:38-110).
+static Config read_config(const Gguf& g)
+{
+    Config c;
+    c.arch = g.get_string("general.architecture", "");
+    static const char* archs[] = {"llama", "qwen2", "qwen3", "mixtral", "qwen2moe", "qwen3moe", "granite", "olmo2"};
+    bool ok = false;
+    for (const char* a : archs) ok |= c.arch == a;
+    if (!ok)
+        WL_THROW(WL_EUNSUPPORTED, "Model architecture '" + c.arch + "' is not supported. Windlass runs llama, qwen2, qwen3, "
+                                  "mixtral, qwen2moe, qwen3moe, granite, olmo2.");
+    const std::string a = c.arch + ".";
+    c.layers = (int)g.get_int(a + "block_count", 0);
+    c.embd = (int)g.get_int(a + "embedding_length", 0);
+    c.heads = (int)g.get_int(a + "attention.head_count", 0);
+    c.kv_heads = (int)g.get_int(a + "attention.head_count_kv", c.heads);
+    c.head_dim = (int)g.get_int(a + "attention.key_length", c.heads ? c.embd / c.heads : 0);
+    c.rope_dims = (int)g.get_int(a + "rope.dimension_count", c.head_dim);
+    c.context_length = (int)g.get_int(a + "context_length", 4096);
+    c.rms_eps = g.get_float(a + "attention.layer_norm_rms_epsilon", 1e-5f);
+    c.rope_base = g.get_float(a + "rope.freq_base", 10000.f);
+    c.rope_neox = c.arch == "qwen2" || c.arch == "qwen3" || c.arch == "qwen2moe" || c.arch == "qwen3moe" || c.arch == "olmo2";
+    if (c.arch == "granite") {
+        c.embedding_scale = g.get_float(a + "embedding_scale", 0.f);
+        c.residual_scale = g.get_float(a + "residual_scale", 0.f);
+        c.attention_scale = g.get_float(a + "attention.scale", 0.f);
+        c.logit_scale = g.get_float(a + "logit_scale", 0.f);
+    }
+    c.post_norms = c.arch == "olmo2";
+    c.qk_norm_full = c.arch == "olmo2";
+    c.qk_norm = g.find("blk.0.attn_q_norm.weight") != nullptr;
+    c.tied = g.find("output.weight") == nullptr;
+    const std::string scaling = g.get_string(a + "rope.scaling.type", "none");
+    const float factor = g.get_float(a + "rope.scaling.factor", 0.f);
+    if (scaling == "linear" && factor > 0) c.rope_freq_scale = 1.f / factor;
+    c.expert_count = (int)g.get_int(a + "expert_count", 0);
+    if (c.expert_count > 0 && c.arch != "llama" && c.arch != "mixtral" && c.arch != "qwen2moe" && c.arch != "qwen3moe")
+        WL_THROW(WL_EUNSUPPORTED, "Mixture-of-experts layers are supported for llama/mixtral, qwen2moe and qwen3moe, not '" + c.arch + "'.");
+    if (c.expert_count == 0 && (c.arch == "qwen2moe" || c.arch == "qwen3moe"))
+        WL_THROW(WL_EUNSUPPORTED, c.arch + " needs " + a + "expert_count.");
+    if (c.expert_count > 0) {
+        c.expert_used = (int)g.get_int(a + "expert_used_count", 0);
+        if (c.expert_used < 1 || c.expert_used > c.expert_count)
+            WL_THROW(WL_EUNSUPPORTED, a + "expert_used_count " + std::to_string(c.expert_used) + " must be 1.." + std::to_string(c.expert_count) + ".");
+        bool norm = c.arch != "qwen2moe";
+        if (g.has(a + "expert_weights_norm")) norm = g.get_bool(a + "expert_weights_norm", norm);
+        c.expert_weights_norm = norm;
+        if (c.expert_count > 256) WL_THROW(WL_EUNSUPPORTED, "more than 256 experts");
+    }
+    if (c.layers <= 0 || c.embd <= 0 || c.heads <= 0 || c.kv_heads <= 0) WL_THROW(WL_EUNSUPPORTED, "The model shape is incomplete.");
+    if (c.heads % c.kv_heads != 0) WL_THROW(WL_EUNSUPPORTED, "head_count must be a multiple of head_count_kv.");
+    if (c.rope_dims > c.head_dim || c.rope_dims % 2 != 0) WL_THROW(WL_EUNSUPPORTED, "Unsupported rope.dimension_count " + std::to_string(c.rope_dims) + ".");
+    const GgufTensor* embd = g.find("token_embd.weight");
+    if (!embd) WL_THROW(WL_EUNSUPPORTED, "The model has no token_embd.weight.");
+    c.vocab = embd->rows();
+    return c;
+}
+
+static Weight weight_of(const GgufTensor& t)
+{
+    Weight w;
+    w.type = t.type;
+    w.cols = t.cols();
+    w.experts = t.experts();
+    const int64_t rows_all = t.elements() / t.dims[0];
+    w.rows = (int)(rows_all / w.experts);
+    w.row_bytes = t.size / rows_all;
+    w.bytes = t.size;
+    return w;
+}
+
+void Model::load_from_gguf(const Gguf& g)
+{
+    // Validate the layer tensors the forward indexes (ModelConfig.From, src/ModelConfig.cs:113-155).
+    static const char* required[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm"};
+    static const char* olmo2[] = {"attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm", "attn_k_norm", "post_attention_norm", "post_ffw_norm"};
+    for (int l = 0; l < c_.layers; ++l) {
+        if (c_.post_norms) {
+            for (const char* n : olmo2) if (!g.find(layer_name(l, n) + ".weight")) WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + " has no " + n + ".weight (unsupported layout).");
+        } else {
+            for (const char* n : required) if (!g.find(layer_name(l, n) + ".weight")) WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + " has no " + n + ".weight (unsupported layout).");
+        }
+        const bool moe = c_.expert_count > 0 && g.find(layer_name(l, "ffn_gate_inp.weight"));
+        static const char* moe_names[] = {"ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"};
+        static const char* dense_names[] = {"ffn_gate", "ffn_up", "ffn_down", "ffn_down"};
+        const char* const* names = moe ? moe_names : dense_names;
+        for (int i = 0; i < 4; ++i)
+            if (!g.find(layer_name(l, names[i]) + ".weight"))
+                WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + " has no " + names[i] + ".weight (unsupported layout" +
+                                          (moe ? "; Windlass reads the stacked expert tensors, not per-expert ffn_gate.N.weight files" : "") + ").");
+        if (moe) {
+            const GgufTensor* router = g.find(layer_name(l, "ffn_gate_inp.weight"));
+            const GgufTensor* gate = g.find(layer_name(l, "ffn_gate_exps.weight"));
+            const GgufTensor* up = g.find(layer_name(l, "ffn_up_exps.weight"));
+            const GgufTensor* down = g.find(layer_name(l, "ffn_down_exps.weight"));
+            if (router->cols() != c_.embd || router->rows() != c_.expert_count)
+                WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + ": ffn_gate_inp.weight has the wrong shape.");
+            if (gate->ndims != 3 || gate->dims[2] != c_.expert_count || gate->cols() != c_.embd || up->ndims != 3 ||
+                up->dims[2] != c_.expert_count || up->cols() != c_.embd || up->dims[1] != gate->dims[1])
+                WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + ": ffn_gate_exps/ffn_up_exps have the wrong shape.");
+            if (down->ndims != 3 || down->dims[2] != c_.expert_count || down->dims[1] != c_.embd || down->dims[0] != gate->dims[1])
+                WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + ": ffn_down_exps has the wrong shape.");
+            c_.expert_ff = (int)gate->dims[1];
+        }
+    }
+    for (const GgufTensor& t : g.tensors()) {
+        const std::string& n = t.name;
+        if (n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0 && t.ndims >= 2 && !can_decode(t.type))
+            WL_THROW(WL_EUNSUPPORTED, "Tensor " + n + " uses " + type_name(t.type) + ", which Windlass cannot decode yet.");
+    }
+
+    // One arena for every tensor plus the fp32 copies of the vectors.
+    int64_t total = 0;
+    for (const GgufTensor& t : g.tensors()) total += (t.size + 255) / 256 * 256 + (t.elements() * 4 + 255) / 256 * 256;
+    arena_ = dalloc<uint8_t>(total);
+    arena_size_ = total;
+
+    auto upload = [&](const GgufTensor* t) -> Weight {
+        if (!t) return Weight{};
+        Weight w = weight_of(*t);
+        w.d = arena_alloc(w.bytes);
+        WL_CUDA(cudaMemcpy(w.d, g.data(*t), (size_t)w.bytes, cudaMemcpyHostToDevice));
+        stats_.bytes_h2d += w.bytes;
+        return w;
+    };
+    auto vec = [&](const GgufTensor* t) -> Vec {
+        Vec v;
+        if (!t) return v;
+        const Weight w = upload(t);
+        v.n = (int)t->elements();
+        if (t->type == 0) v.d = (float*)w.d;
+        else {
+            v.d = (float*)arena_alloc((int64_t)v.n * 4);
+            k::dequant(t->type, w.d, v.n, v.d, stream_);
+        }
+        return v;
+    };
+    L_.resize(c_.layers);
+    for (int l = 0; l < c_.layers; ++l) {
+        LayerW& L = L_[l];
+        auto T = [&](const char* n) { return g.find(layer_name(l, n)); };
+        L.attn_norm = vec(T("attn_norm.weight"));
+        L.q = upload(T("attn_q.weight")); L.k = upload(T("attn_k.weight")); L.v = upload(T("attn_v.weight"));
+        L.qb = vec(T("attn_q.bias")); L.kb = vec(T("attn_k.bias")); L.vb = vec(T("attn_v.bias"));
+        L.q_norm = vec(T("attn_q_norm.weight")); L.k_norm = vec(T("attn_k_norm.weight"));
+        L.o = upload(T("attn_output.weight"));
+        L.post_attn_norm = vec(T("post_attention_norm.weight"));
+        L.ffn_norm = vec(T("ffn_norm.weight"));
+        L.post_ffw_norm = vec(T("post_ffw_norm.weight"));
+        L.moe = c_.expert_count > 0 && T("ffn_gate_inp.weight");
+        if (L.moe) {
+            L.router = upload(T("ffn_gate_inp.weight"));
+            L.gate_exps = upload(T("ffn_gate_exps.weight")); L.up_exps = upload(T("ffn_up_exps.weight")); L.down_exps = upload(T("ffn_down_exps.weight"));
+            L.sh_gate = upload(T("ffn_gate_shexp.weight")); L.sh_up = upload(T("ffn_up_shexp.weight")); L.sh_down = upload(T("ffn_down_shexp.weight"));
+            L.sh_gate_inp = upload(T("ffn_gate_inp_shexp.weight"));
+            if (L.sh_gate.present()) c_.shared_expert_ff = L.sh_gate.rows;
+        } else {
+            L.gate = upload(T("ffn_gate.weight")); L.up = upload(T("ffn_up.weight")); L.down = upload(T("ffn_down.weight"));
+        }
+    }
+    embd_ = upload(g.find("token_embd.weight"));
+    out_norm_ = vec(g.find("output_norm.weight"));
+    if (!out_norm_.present()) WL_THROW(WL_EUNSUPPORTED, "The model has no output_norm.weight.");
+    output_ = c_.tied ? embd_ : upload(g.find("output.weight"));
+    for (const GgufTensor& t : g.tensors()) weight_bytes_ += t.size;
+
+    std::vector<float> rf;
+    if (const GgufTensor* t = g.find("rope_freqs.weight")) {
+        if (t->type != 0) WL_THROW(WL_EUNSUPPORTED, "rope_freqs.weight must be F32.");
+        rf.resize((size_t)t->elements());
+        memcpy(rf.data(), g.data(*t), rf.size() * 4);
+    }
+    build_rope_table(rf.empty() ? nullptr : rf.data(), (int)rf.size());
+    WL_CUDA(cudaStreamSynchronize(stream_));
+}
+
+// RopeTable (src/Transformer.cs:399-416) for every position of the context, in double, stored as float pairs.
+void Model::build_rope_table(const float* rope_freqs, int n_rope_freqs)
+{
+    const int n = c_.rope_dims;
+    std::vector<float> t((size_t)max_context_ * n);
+    const double theta_scale = std::pow((double)c_.rope_base, -2.0 / n);
+    for (int pos = 0; pos < max_context_; ++pos) {
+        double theta = pos * (double)c_.rope_freq_scale;
+        for (int i = 0; i < n / 2; ++i) {
+            const double th = (rope_freqs && i < n_rope_freqs) ? theta / rope_freqs[i] : theta;
+            t[(size_t)pos * n + 2 * i] = (float)std::cos(th);
+            t[(size_t)pos * n + 2 * i + 1] = (float)std::sin(th);
+            theta *= theta_scale;
+        }
+    }
+    rope_table_ = dalloc<float>((int64_t)t.size());
+    WL_CUDA(cudaMemcpy(rope_table_, t.data(), t.size() * 4, cudaMemcpyHostToDevice));
+}
+
+Model* Model::open_file(const std::string& path, const wl_options& opt)
+{
+    // The file and its shape are checked before any device work, so a bad file fails the same way with or without
+    // a GPU.
+    Gguf g(path);
+    const Config c = read_config(g);
+    std::unique_ptr<Model> m(new Model());
+    m->c_ = c;
+    m->init_device(opt);
+    m->max_context_ = opt.max_context > 0 ? opt.max_context : std::min(m->c_.context_length, 8192);
+    m->load_from_gguf(g);
+    m->finish_open();
+    return m.release();
+}
+
+// Synthetic models: tensor ids are (layer+1)<<8 | slot for layer tensors and 1..3 for the embedding, final norm and
+// output head; the test oracle uses the same ids to regenerate any tensor on the CPU.
+enum Slot { S_ATTN_NORM = 1, S_Q, S_K, S_V, S_O, S_FFN_NORM, S_GATE, S_UP, S_DOWN, S_Q_NORM, S_K_NORM, S_ROUTER,
+            S_GATE_EXPS, S_UP_EXPS, S_DOWN_EXPS };
+
+Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
+{
+    std::unique_ptr<Model> m(new Model());
+    m->init_device(opt);
+    Config& c = m->c_;
+    c.arch = std::string(sp.arch, strnlen(sp.arch, sizeof sp.arch));
+    if (c.arch != "llama" && c.arch != "qwen3" && c.arch != "qwen3moe") WL_THROW(WL_EUNSUPPORTED, "synthetic arch must be llama, qwen3 or qwen3moe");
+    c.layers = sp.layers; c.embd = sp.embd; c.heads = sp.heads; c.kv_heads = sp.kv_heads;
+    c.head_dim = sp.head_dim > 0 ? sp.head_dim : sp.embd / std::max(1, sp.heads);
+    c.rope_dims = c.head_dim; c.vocab = sp.vocab; c.context_length = sp.context_length > 0 ? sp.context_length : 4096;
+    c.rms_eps = sp.rms_eps > 0 ? sp.rms_eps : 1e-5f; c.rope_base = sp.rope_base > 0 ? sp.rope_base : 10000.f;
+    c.rope_neox = c.arch != "llama";
+    c.qk_norm = c.arch != "llama";
+    if (c.arch == "qwen3moe") {
+        c.expert_count = sp.experts; c.expert_used = sp.experts_used; c.expert_ff = sp.expert_ff; c.expert_weights_norm = true;
+        if (c.expert_count < 1 || c.expert_count > 256 || c.expert_used < 1 || c.expert_used > c.expert_count)
+            WL_THROW(WL_EINVAL, "bad synthetic expert counts");
+    }
+    if (c.layers <= 0 || c.embd <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.vocab <= 0)
+        WL_THROW(WL_EINVAL, "bad synthetic shape");
+    m->max_context_ = opt.max_context > 0 ? opt.max_context : std::min(c.context_length, 8192);
+    const float sigma = sp.sigma > 0 ? sp.sigma : 0.02f;
+    const int QD = c.qdim(), KD = c.kvdim(), E = c.embd, F = sp.ff, NE = c.expert_count, X = c.expert_ff;
+
+    struct Plan { Weight* w; Vec* v; uint32_t tid; int type; int64_t rows, cols; int experts; };
+    std::vector<Plan> plan;
+    m->L_.resize(c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        LayerW& L = m->L_[l];
+        const uint32_t b = (uint32_t)(l + 1) << 8;
+        plan.push_back({nullptr, &L.attn_norm, b | S_ATTN_NORM, 0, 1, E, 1});
+        plan.push_back({&L.q, nullptr, b | S_Q, sp.type_attn, QD, E, 1});
+        plan.push_back({&L.k, nullptr, b | S_K, sp.type_attn, KD, E, 1});
+        plan.push_back({&L.v, nullptr, b | S_V, sp.type_attn_v, KD, E, 1});
+        if (c.qk_norm) {
+            plan.push_back({nullptr, &L.q_norm, b | S_Q_NORM, 0, 1, c.head_dim, 1});
+            plan.push_back({nullptr, &L.k_norm, b | S_K_NORM, 0, 1, c.head_dim, 1});
+        }
+        plan.push_back({&L.o, nullptr, b | S_O, sp.type_attn, E, QD, 1});
+        plan.push_back({nullptr, &L.ffn_norm, b | S_FFN_NORM, 0, 1, E, 1});
+        if (NE > 0) {
+            L.moe = true;
+            plan.push_back({&L.router, nullptr, b | S_ROUTER, 0, NE, E, 1});
+            plan.push_back({&L.gate_exps, nullptr, b | S_GATE_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE});
+            plan.push_back({&L.up_exps, nullptr, b | S_UP_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE});
+            plan.push_back({&L.down_exps, nullptr, b | S_DOWN_EXPS, sp.type_ffn_down, (int64_t)NE * E, X, NE});
+        } else {
+            plan.push_back({&L.gate, nullptr, b | S_GATE, sp.type_ffn, F, E, 1});
+            plan.push_back({&L.up, nullptr, b | S_UP, sp.type_ffn, F, E, 1});
+            plan.push_back({&L.down, nullptr, b | S_DOWN, sp.type_ffn_down, E, F, 1});
+        }
+    }
+    plan.push_back({&m->embd_, nullptr, 1, sp.type_embd, c.vocab, E, 1});
+    plan.push_back({nullptr, &m->out_norm_, 2, 0, 1, E, 1});
+    plan.push_back({&m->output_, nullptr, 3, sp.type_output, c.vocab, E, 1});
+
+    int64_t total = 0;
+    for (const Plan& p : plan) {
+        const int64_t rb = row_bytes_of(p.type, p.cols);
+        if (rb <= 0 || p.cols % (p.type == 0 ? 1 : p.type == 8 ? 32 : 256) != 0) WL_THROW(WL_EUNSUPPORTED, "synthetic tensor shape does not fit its type");
+        total += (rb * p.rows + 255) / 256 * 256;
+    }
+    m->arena_ = dalloc<uint8_t>(total);
+    m->arena_size_ = total;
+    for (const Plan& p : plan) {
+        Weight w;
+        w.type = p.type; w.cols = (int)p.cols; w.experts = p.experts; w.rows = (int)(p.rows / p.experts);
+        w.row_bytes = row_bytes_of(p.type, p.cols); w.bytes = w.row_bytes * p.rows;
+        w.d = m->arena_alloc(w.bytes);
+        const bool is_vec = p.v != nullptr;
+        k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, is_vec ? 1.0f : 0.0f, w.d, m->stream_);
+        m->weight_bytes_ += w.bytes;
+        if (is_vec) { p.v->d = (float*)w.d; p.v->n = (int)(p.rows * p.cols); }
+        else *p.w = w;
+    }
+    m->build_rope_table(nullptr, 0);
+    WL_CUDA(cudaStreamSynchronize(m->stream_));
+    m->finish_open();
+    return m.release();
+}
+
+void Model::finish_open()
+{
+    if (!rope_table_) build_rope_table(nullptr, 0);
+    own_ = new_seq();
+}
+
+Model::~Model()
+{
+    if (device_ >= 0) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (own_) free_seq(own_);
+    dfree(arena_); dfree(rope_table_);
+    dfree(x_); dfree(xn_); dfree(q_); dfree(k_); dfree(v_); dfree(att_); dfree(o_); dfree(g_); dfree(u_);
+    dfree(logits_); dfree(router_); dfree(wts_); dfree(xe_); dfree(ye_); dfree(ge_); dfree(ue_); dfree(moe_out_);
+    dfree(sh_gl_); dfree(tok_d_); dfree(pos_d_); dfree(sel_); dfree(bad_d_); dfree(etok_d_); dfree(ew_d_); dfree(rows_d_);
+    hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
+    for (void* p : extra_allocs_) cudaFree(p);
+    for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
+    for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+int64_t Model::device_bytes() const
+{
+    return arena_size_ + (int64_t)max_context_ * c_.rope_dims * 4;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// sequences
+// ---------------------------------------------------------------------------------------------------------------------
+Seq* Model::new_seq()
+{
+    Seq* s = new Seq();
+    s->model = this;
+    return s;
+}
+
+void Model::free_seq(Seq* s)
+{
+    if (!s) return;
+    WL_CUDA(cudaSetDevice(device_));
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    if (s->kv) cudaFree(s->kv);
+    delete s;
+}
+
+// Transformer.Reserve (src/Transformer.cs:62-73): grow to max(positions, min(context, max(256, 2*capacity))).
+void Model::reserve(Seq* s, int positions)
+{
+    if (positions <= s->capacity) return;
+    const int cap = std::max(positions, std::min(max_context_, std::max(256, s->capacity * 2)));
+    const int64_t KD = c_.kvdim(), per_layer = (int64_t)cap * KD;
+    uint16_t* nk = dalloc<uint16_t>(2 * (int64_t)c_.layers * per_layer);
+    if (s->kv && s->length > 0) {
+        const int64_t old_per_layer = (int64_t)s->capacity * KD;
+        // rows = 2*layers blocks of `length` positions
+        WL_CUDA(cudaMemcpy2DAsync(nk, per_layer * 2, s->kv, old_per_layer * 2, (size_t)s->length * KD * 2, 2 * c_.layers,
+                                  cudaMemcpyDeviceToDevice, stream_));
+    }
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    if (s->kv) cudaFree(s->kv);
+    s->kv = nk;
+    s->capacity = cap;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// workspaces
+// ---------------------------------------------------------------------------------------------------------------------
+void Model::ensure_workspace(int T, int logit_rows)
+{
+    const int E = c_.embd, QD = c_.qdim(), KD = c_.kvdim();
+    int F = 0;
+    for (const LayerW& L : L_) {
+        if (L.gate.present()) F = std::max(F, L.gate.rows);
+        if (L.sh_gate.present()) F = std::max(F, L.sh_gate.rows);
+    }
+    if (T > ws_T_) {
+        const int n = std::max(T, ws_T_ * 2 > 0 ? std::min(ws_T_ * 2, std::max(T, 8)) : T);
+        dfree(x_); dfree(xn_); dfree(q_); dfree(k_); dfree(v_); dfree(att_); dfree(o_); dfree(g_); dfree(u_);
+        dfree(router_); dfree(wts_); dfree(xe_); dfree(ye_); dfree(ge_); dfree(ue_); dfree(moe_out_); dfree(sh_gl_);
+        dfree(tok_d_); dfree(pos_d_); dfree(sel_); dfree(bad_d_); dfree(etok_d_); dfree(ew_d_); dfree(rows_d_);
+        x_ = dalloc<float>((int64_t)n * E); xn_ = dalloc<float>((int64_t)n * E); o_ = dalloc<float>((int64_t)n * E);
+        q_ = dalloc<float>((int64_t)n * QD); att_ = dalloc<float>((int64_t)n * QD);
+        k_ = dalloc<float>((int64_t)n * KD); v_ = dalloc<float>((int64_t)n * KD);
+        g_ = dalloc<float>((int64_t)n * std::max(F, 1)); u_ = dalloc<float>((int64_t)n * std::max(F, 1));
+        tok_d_ = dalloc<int32_t>(n); pos_d_ = dalloc<int32_t>(n); bad_d_ = dalloc<int32_t>(1);
+        rows_d_ = dalloc<RowKV>(n);
+        if (c_.expert_count > 0) {
+            const int NE = c_.expert_count, K = c_.expert_used, X = std::max(c_.expert_ff, 1);
+            router_ = dalloc<float>((int64_t)n * NE); wts_ = dalloc<float>((int64_t)n * K); sel_ = dalloc<int32_t>((int64_t)n * K);
+            xe_ = dalloc<float>((int64_t)n * E); ye_ = dalloc<float>((int64_t)n * E); moe_out_ = dalloc<float>((int64_t)n * E);
+            ge_ = dalloc<float>((int64_t)n * X); ue_ = dalloc<float>((int64_t)n * X); sh_gl_ = dalloc<float>(n);
+            etok_d_ = dalloc<int32_t>((int64_t)n * K); ew_d_ = dalloc<float>((int64_t)n * K);
+        }
+        hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
+        h_tok_ = halloc<int32_t>(n); h_pos_ = halloc<int32_t>(n); h_rows_ = halloc<RowKV>(n);
+        if (c_.expert_count > 0) {
+            const int K = c_.expert_used;
+            h_sel_ = halloc<int32_t>((int64_t)n * K); h_wts_ = halloc<float>((int64_t)n * K);
+            h_etok_ = halloc<int32_t>((int64_t)n * K); h_ew_ = halloc<float>((int64_t)n * K);
+        }
+        ws_T_ = n;
+    }
+    if (logit_rows > ws_logit_rows_) {
+        dfree(logits_);
+        logits_ = dalloc<float>((int64_t)logit_rows * c_.vocab);
+        ws_logit_rows_ = logit_rows;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------------------------------------------------
+void Model::matmul(const Weight& w, const float* x, int T, float* y, int path)
+{
+    (void)path;
+    ProfileMark mark{};
+    if (profiling_) {
+        for (int i = 0; i < 2; ++i) {
+            if (event_pool_.empty()) {
+                cudaEvent_t e;
+                WL_CUDA(cudaEventCreate(&e));
+                event_pool_.push_back(e);
+            }
+        }
+        mark.start = event_pool_.back(); event_pool_.pop_back();
+        mark.stop = event_pool_.back(); event_pool_.pop_back();
+        mark.type = w.type;
+        mark.bytes = (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows);
+        WL_CUDA(cudaEventRecord(mark.start, stream_));
+    }
+    k::matvec(w.type, w.d, w.row_bytes, w.rows, w.cols, x, w.cols, T, y, w.rows, stream_);
+    if (profiling_) {
+        WL_CUDA(cudaEventRecord(mark.stop, stream_));
+        marks_.push_back(mark);
+        if (marks_.size() > 4096) flush_profile();
+    }
+}
+
+static Weight slice(const Weight& w, int e)
+{
+    Weight s = w;
+    s.d = const_cast<uint8_t*>(w.expert(e));
+    s.experts = 1;
+    s.bytes = (int64_t)w.rows * w.row_bytes;
+    return s;
+}
+
+void Model::ffn_dense(const LayerW& L, int T)
+{
+    const int F = L.gate.rows;
+    matmul(L.gate, xn_, T, g_);
+    matmul(L.up, xn_, T, u_);
+    k::swiglu(g_, u_, (int64_t)T * F, stream_);
+    matmul(L.down, g_, T, o_);
+}
+
+// MoeFfn (src/Transformer.cs:259-311): router, top-k, then each chosen expert runs once on the rows routed to it, in
+// expert order; the weighted outputs are added per row in that same order, so a row's result does not depend on the
+// other rows of the step.
+void Model::ffn_moe(const LayerW& L, int T)
+{
+    const int E = c_.embd, NE = c_.expert_count, K = c_.expert_used, X = L.gate_exps.rows;
+    matmul(L.router, xn_, T, router_);
+    k::route(router_, T, NE, K, c_.expert_weights_norm ? 1 : 0, sel_, wts_, stream_);
+    WL_CUDA(cudaMemcpyAsync(h_sel_, sel_, sizeof(int32_t) * (size_t)T * K, cudaMemcpyDeviceToHost, stream_));
+    WL_CUDA(cudaMemcpyAsync(h_wts_, wts_, sizeof(float) * (size_t)T * K, cudaMemcpyDeviceToHost, stream_));
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    std::vector<int> count(NE, 0), start(NE + 1, 0);
+    for (int i = 0; i < T * K; ++i) count[h_sel_[i]]++;
+    for (int e = 0; e < NE; ++e) start[e + 1] = start[e] + count[e];
+    std::vector<int> at(start.begin(), start.end() - 1);
+    for (int t = 0; t < T; ++t)
+        for (int j = 0; j < K; ++j) {
+            const int e = h_sel_[t * K + j];
+            h_etok_[at[e]] = t;
+            h_ew_[at[e]] = h_wts_[t * K + j];
+            at[e]++;
+        }
+    WL_CUDA(cudaMemcpyAsync(etok_d_, h_etok_, sizeof(int32_t) * (size_t)T * K, cudaMemcpyHostToDevice, stream_));
+    WL_CUDA(cudaMemcpyAsync(ew_d_, h_ew_, sizeof(float) * (size_t)T * K, cudaMemcpyHostToDevice, stream_));
+    WL_CUDA(cudaMemsetAsync(moe_out_, 0, sizeof(float) * (size_t)T * E, stream_));
+    for (int e = 0; e < NE; ++e) {
+        const int n = count[e];
+        if (n == 0) continue;
+        stats_.expert_runs++;
+        const int32_t* toks = etok_d_ + start[e];
+        k::gather_rows(xe_, xn_, toks, n, E, stream_);
+        matmul(slice(L.gate_exps, e), xe_, n, ge_);
+        matmul(slice(L.up_exps, e), xe_, n, ue_);
+        k::swiglu(ge_, ue_, (int64_t)n * X, stream_);
+        matmul(slice(L.down_exps, e), ge_, n, ye_);
+        k::scatter_add(moe_out_, ye_, toks, ew_d_ + start[e], n, E, stream_);
+    }
+    if (L.sh_gate.present()) {
+        const int SF = L.sh_gate.rows;
+        matmul(L.sh_gate, xn_, T, g_);
+        matmul(L.sh_up, xn_, T, u_);
+        k::swiglu(g_, u_, (int64_t)T * SF, stream_);
+        matmul(L.sh_down, g_, T, o_);
+        if (L.sh_gate_inp.present()) matmul(L.sh_gate_inp, xn_, T, sh_gl_);
+        k::shared_expert_add(moe_out_, o_, L.sh_gate_inp.present() ? sh_gl_ : nullptr, T, E, stream_);
+    }
+    WL_CUDA(cudaMemcpyAsync(o_, moe_out_, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToDevice, stream_));
+}
+
+// Layer (src/Transformer.cs:177-232).
+void Model::layer(int l, int T, int max_n)
+{
+    const LayerW& L = L_[l];
+    const int E = c_.embd, QD = c_.qdim(), KD = c_.kvdim(), HD = c_.head_dim;
+    const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
+    const int64_t n = (int64_t)T * E;
+    if (c_.post_norms) WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
+    else k::rmsnorm(x_, T, E, L.attn_norm.d, c_.rms_eps, xn_, stream_);
+    matmul(L.q, xn_, T, q_);
+    matmul(L.k, xn_, T, k_);
+    matmul(L.v, xn_, T, v_);
+    if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
+    if (L.kb.present()) k::add_bias(k_, L.kb.d, T, KD, stream_);
+    if (L.vb.present()) k::add_bias(v_, L.vb.d, T, KD, stream_);
+    if (c_.qk_norm_full) {
+        k::rmsnorm(q_, T, QD, L.q_norm.d, c_.rms_eps, q_, stream_);
+        k::rmsnorm(k_, T, KD, L.k_norm.d, c_.rms_eps, k_, stream_);
+    } else if (c_.qk_norm) {
+        k::rmsnorm(q_, T * c_.heads, HD, L.q_norm.d, c_.rms_eps, q_, stream_);
+        k::rmsnorm(k_, T * c_.kv_heads, HD, L.k_norm.d, c_.rms_eps, k_, stream_);
+    }
+    k::rope(q_, T, c_.heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_, stream_);
+    k::rope(k_, T, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_, stream_);
+    k::kv_append(k_, v_, T, KD, rows_d_, l, pos_d_, stream_);
+    const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
+    k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, max_n, att_, stream_);
+    matmul(L.o, att_, T, o_);
+    if (c_.post_norms) k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
+    k::residual(x_, o_, rs, n, stream_);
+    if (c_.post_norms) WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
+    else k::rmsnorm(x_, T, E, L.ffn_norm.d, c_.rms_eps, xn_, stream_);
+    if (L.moe) ffn_moe(L, T);
+    else ffn_dense(L, T);
+    if (c_.post_norms) k::rmsnorm(o_, T, E, L.post_ffw_norm.d, c_.rms_eps, o_, stream_);
+    k::residual(x_, o_, rs, n, stream_);
+}
+
+// Head (src/Transformer.cs:112-125): final norm and output matrix for rows first..T-1.
+void Model::head(int T, int first)
+{
+    const int E = c_.embd, n = T - first;
+    k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
+    matmul(output_, xn_, n, logits_);
+    if (c_.logit_scale != 0.f) k::scale(logits_, 1.f / c_.logit_scale, (int64_t)n * c_.vocab, stream_);
+}
+
+// Token ids, positions and KV-cache rows of one step to the device (pinned staging, async on the model's stream).
+void Model::upload_step(int T, const RowKV* rows, const int32_t* pos, const int32_t* tokens)
+{
+    for (int t = 0; t < T; ++t) {
+        h_tok_[t] = tokens[t];
+        h_pos_[t] = pos[t];
+        h_rows_[t] = rows[t];
+    }
+    WL_CUDA(cudaMemcpyAsync(tok_d_, h_tok_, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
+    WL_CUDA(cudaMemcpyAsync(pos_d_, h_pos_, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
+    WL_CUDA(cudaMemcpyAsync(rows_d_, h_rows_, sizeof(RowKV) * T, cudaMemcpyHostToDevice, stream_));
+}
+
+// Embedding, every layer and the head, all on the device (no cancel or progress points).
+void Model::step_device(int T, int first, int max_n)
+{
+    k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
+    for (int l = 0; l < c_.layers; ++l) layer(l, T, max_n);
+    head(T, first);
+}
+
+int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
+                   int first, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int t = 0; t < T; ++t)
+        if (tokens[t] < 0 || tokens[t] >= c_.vocab)
+            WL_THROW(WL_EINVAL, "Token id " + std::to_string(tokens[t]) + " is outside the vocabulary.");
+    ensure_workspace(T, T - first);
+    upload_step(T, rows.data(), pos.data(), tokens);
+    int max_n = 0;
+    for (int t = 0; t < T; ++t) max_n = std::max(max_n, pos[t] + 1);
+    const int total = c_.layers + 1;
+    if (!cancel && !progress) step_device(T, first, max_n);
+    else {
+        k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
+        for (int l = 0; l < c_.layers; ++l) {
+            if (cancel && *cancel) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+            layer(l, T, max_n);
+            if (progress) { WL_CUDA(cudaStreamSynchronize(stream_)); progress(l + 1, total, user); }
+        }
+        if (cancel && *cancel) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+        head(T, first);
+    }
+    WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    flush_profile();
+    if (progress) progress(total, total, user);
+    stats_.tokens += T;
+    stats_.last_forward_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return WL_OK;
+}
+
+double Model::bench_decode(Seq* const* seqs, int N, int steps)
+{
+    if (N <= 0 || steps <= 0) WL_THROW(WL_EINVAL, "wl_bench_decode: N and steps must be positive");
+    WL_CUDA(cudaSetDevice(device_));
+    std::vector<int32_t> len(N);
+    int max_len = 0;
+    for (int i = 0; i < N; ++i) {
+        if (!seqs[i] || seqs[i]->model != this) WL_THROW(WL_EINVAL, "wl_bench_decode: a sequence of another model");
+        len[i] = seqs[i]->length;
+        if (len[i] + steps > max_context_) WL_THROW(WL_EINVAL, "wl_bench_decode: the steps do not fit the context");
+        reserve(seqs[i], len[i] + steps);
+        max_len = std::max(max_len, len[i]);
+    }
+    ensure_workspace(N, N);
+    // every step's positions up front, so the timed loop copies nothing from the host
+    std::vector<int32_t> pos_all((size_t)steps * N), toks(N);
+    std::vector<RowKV> rows(N);
+    for (int i = 0; i < N; ++i) {
+        const int64_t stride = (int64_t)seqs[i]->capacity * c_.kvdim();
+        rows[i] = RowKV{seqs[i]->kv, seqs[i]->kv + (int64_t)c_.layers * stride, stride};
+        toks[i] = (int32_t)((1103515245u * (uint32_t)(i + 1) + 12345u) % (uint32_t)c_.vocab);
+        for (int s = 0; s < steps; ++s) pos_all[(size_t)s * N + i] = len[i] + s;
+    }
+    int32_t* pos_all_d = dalloc<int32_t>((int64_t)steps * N);
+    WL_CUDA(cudaMemcpy(pos_all_d, pos_all.data(), pos_all.size() * 4, cudaMemcpyHostToDevice));
+    upload_step(N, rows.data(), pos_all.data(), toks.data());
+    int32_t* pos_saved = pos_d_;
+    cudaEvent_t e0, e1;
+    WL_CUDA(cudaEventCreate(&e0));
+    WL_CUDA(cudaEventCreate(&e1));
+    WL_CUDA(cudaEventRecord(e0, stream_));
+    for (int s = 0; s < steps; ++s) {
+        pos_d_ = pos_all_d + (size_t)s * N;
+        step_device(N, 0, max_len + s + 1);
+    }
+    WL_CUDA(cudaEventRecord(e1, stream_));
+    WL_CUDA(cudaEventSynchronize(e1));
+    pos_d_ = pos_saved;
+    float ms = 0.f;
+    WL_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(pos_all_d);
+    flush_profile();
+    for (int i = 0; i < N; ++i) seqs[i]->length = len[i] + steps;
+    stats_.tokens += (int64_t)N * steps;
+    return ms;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// profiling: CUDA events around every matvec/matmul launch on the model's stream
+// ---------------------------------------------------------------------------------------------------------------------
+void Model::set_profiling(bool on)
+{
+    WL_CUDA(cudaSetDevice(device_));
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    flush_profile();
+    profiling_ = on;
+    if (on) for (auto& p : prof_) p = wl_profile_entry{};
+}
+
+void Model::flush_profile()
+{
+    if (marks_.empty()) return;
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    for (const ProfileMark& m : marks_) {
+        float ms = 0.f;
+        WL_CUDA(cudaEventElapsedTime(&ms, m.start, m.stop));
+        wl_profile_entry& e = prof_[m.type & 63];
+        e.launches++;
+        e.ms += ms;
+        e.bytes += m.bytes;
+        event_pool_.push_back(m.start);
+        event_pool_.push_back(m.stop);
+    }
+    marks_.clear();
+}
+
+wl_profile_entry Model::profile(int type)
+{
+    flush_profile();
+    return prof_[type & 63];
+}
+
+// Transformer.Forward (src/Transformer.cs:83-109).
+int32_t Model::forward(Seq* sq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out,
+                       volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    if (!sq) sq = own_;
+    if (T <= 0) WL_THROW(WL_EINVAL, "No tokens to run.");
+    if (pos0 < 0 || pos0 > sq->length) WL_THROW(WL_EINVAL, "pos0 is past the cached positions.");
+    if (pos0 + T > max_context_)
+        WL_THROW(WL_EINVAL, "The prompt and reply need " + std::to_string(pos0 + T) + " positions; the context is " + std::to_string(max_context_) + ".");
+    WL_CUDA(cudaSetDevice(device_));
+    sq->length = pos0;
+    reserve(sq, pos0 + T);
+    const int64_t stride = (int64_t)sq->capacity * c_.kvdim();
+    std::vector<RowKV> rows(T, RowKV{sq->kv, sq->kv + (int64_t)c_.layers * stride, stride});
+    std::vector<int32_t> pos(T);
+    for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
+    stats_.forward_calls++;
+    const int32_t st = run(T, rows, pos, tokens, all_logits ? 0 : T - 1, out, cancel, progress, user);
+    if (st == WL_OK) sq->length = pos0 + T;
+    return st;
+}
+
+// Transformer.ForwardBatch (src/Transformer.cs:132-170).
+int32_t Model::forward_batch(Seq* const* seqs, const int32_t* tokens, int N, float* out, volatile const int32_t* cancel,
+                             wl_progress_fn progress, void* user)
+{
+    if (N <= 0 || !seqs) WL_THROW(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
+    if (N > max_batch_) WL_THROW(WL_EINVAL, "ForwardBatch takes at most " + std::to_string(max_batch_) + " sequences.");
+    WL_CUDA(cudaSetDevice(device_));
+    std::vector<int32_t> pos(N);
+    for (int i = 0; i < N; ++i) {
+        Seq* sq = seqs[i];
+        if (!sq || sq->model != this) WL_THROW(WL_EINVAL, "A sequence of another model was passed.");
+        for (int j = 0; j < i; ++j) if (seqs[j] == sq) WL_THROW(WL_EINVAL, "A sequence can take one token per batch step.");
+        if (sq->length + 1 > max_context_)
+            WL_THROW(WL_EINVAL, "The prompt and reply need " + std::to_string(sq->length + 1) + " positions; the context is " + std::to_string(max_context_) + ".");
+        pos[i] = sq->length;
+    }
+    std::vector<RowKV> rows(N);
+    for (int i = 0; i < N; ++i) {
+        reserve(seqs[i], pos[i] + 1);
+        const int64_t stride = (int64_t)seqs[i]->capacity * c_.kvdim();
+        rows[i] = RowKV{seqs[i]->kv, seqs[i]->kv + (int64_t)c_.layers * stride, stride};
+    }
+    stats_.batch_calls++;
+    const int32_t st = run(N, rows, pos, tokens, 0, out, cancel, progress, user);
+    if (st == WL_OK) for (int i = 0; i < N; ++i) seqs[i]->length = pos[i] + 1;
+    return st;
+}
+
+}  // namespace wl

@@ -1,0 +1,167 @@
+// The device-resident decoder: Transformer.cs's Forward / ForwardBatch / Truncate / NewSequence semantics on one
+// GPU. Weights live in one device arena (resident) or stream through two device slots from pinned host memory;
+// activations stay on the device for the whole pass; the host only uploads token ids and downloads logits.
+#pragma once
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+#include <cuda_runtime.h>
+#include "../../include/windlass.h"
+#include "wl_kernels.h"
+
+namespace wl {
+
+class Gguf;
+
+// One weight tensor on the device. For stacked MoE tensors [cols, rows, experts] `rows` counts one expert's rows.
+struct Weight {
+    int type = -1;
+    int rows = 0, cols = 0, experts = 1;
+    int64_t row_bytes = 0, bytes = 0;
+    uint8_t* d = nullptr;
+    bool present() const { return d != nullptr; }
+    const uint8_t* expert(int e) const { return d + (int64_t)e * rows * row_bytes; }
+};
+
+// A vector (norm weight, bias) decoded to fp32 on the device (Transformer.Vector, src/Transformer.cs:435-440).
+struct Vec {
+    float* d = nullptr;
+    int n = 0;
+    bool present() const { return d != nullptr; }
+};
+
+struct LayerW {
+    Vec attn_norm, qb, kb, vb, q_norm, k_norm, post_attn_norm, ffn_norm, post_ffw_norm;
+    Weight q, k, v, o, gate, up, down, router, gate_exps, up_exps, down_exps, sh_gate, sh_up, sh_down, sh_gate_inp;
+    bool moe = false;
+};
+
+// ModelConfig (src/ModelConfig.cs:12-36): the fields the forward pass reads.
+struct Config {
+    std::string arch;
+    int layers = 0, embd = 0, heads = 0, kv_heads = 0, head_dim = 0, vocab = 0, context_length = 0, rope_dims = 0;
+    float rms_eps = 1e-5f, rope_base = 10000.f, rope_freq_scale = 1.f;
+    bool rope_neox = false, qk_norm = false, qk_norm_full = false, post_norms = false, tied = false;
+    float embedding_scale = 0, residual_scale = 0, attention_scale = 0, logit_scale = 0;
+    int expert_count = 0, expert_used = 0, expert_ff = 0, shared_expert_ff = 0;
+    bool expert_weights_norm = false;
+    int qdim() const { return heads * head_dim; }
+    int kvdim() const { return kv_heads * head_dim; }
+};
+
+class Model;
+
+// Sequence (src/Batch.cs:13-36): one request's fp16 KV cache in device memory, [2][layers][capacity][kv_dim].
+struct Seq {
+    Model* model = nullptr;
+    uint16_t* kv = nullptr;
+    int capacity = 0;
+    int length = 0;
+};
+
+struct Stats {
+    int64_t bytes_h2d = 0, expert_runs = 0, forward_calls = 0, batch_calls = 0, tokens = 0;
+    double last_forward_ms = 0;
+};
+
+class Model {
+public:
+    static Model* open_file(const std::string& path, const wl_options& opt);
+    static Model* open_synthetic(const wl_synth_spec& spec, const wl_options& opt);
+    ~Model();
+
+    Seq* new_seq();
+    void free_seq(Seq* s);
+    Seq* own() { return own_; }
+
+    // Transformer.Forward / ForwardBatch. out is host memory. Return WL_OK or WL_CANCELLED; throw wl::Error.
+    int32_t forward(Seq* seq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out,
+                    volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    int32_t forward_batch(Seq* const* seqs, const int32_t* tokens, int N, float* out, volatile const int32_t* cancel,
+                          wl_progress_fn progress, void* user);
+
+    const Config& config() const { return c_; }
+    int max_context() const { return max_context_; }
+    const Stats& stats() const { return stats_; }
+    int64_t weight_bytes() const { return weight_bytes_; }
+    int64_t device_bytes() const;
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    // y[T][rows] = W x[T][cols] on the model's stream; path 0 chooses by T (the forward pass's own rule).
+    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0);
+
+    // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
+    double bench_decode(Seq* const* seqs, int N, int steps);
+    void set_profiling(bool on);
+    wl_profile_entry profile(int type);
+
+private:
+    struct ProfileMark {
+        cudaEvent_t start, stop;
+        int type;
+        double bytes;
+    };
+    void flush_profile();
+    void upload_step(int T, const RowKV* rows, const int32_t* pos, const int32_t* tokens);
+    void step_device(int T, int first, int max_n);
+    Model() = default;
+    void init_device(const wl_options& opt);
+    void finish_open();
+    void load_from_gguf(const Gguf& g);
+    void build_rope_table(const float* rope_freqs, int n_rope_freqs);
+    void reserve(Seq* s, int positions);
+    void ensure_workspace(int T, int logit_rows);
+    void layer(int l, int T, int max_n);
+    void ffn_dense(const LayerW& L, int T);
+    void ffn_moe(const LayerW& L, int T);
+    void head(int T, int first);
+    int32_t run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
+                int first_logit_row, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    uint8_t* arena_alloc(int64_t bytes);
+
+    Config c_;
+    int device_ = 0;
+    int max_context_ = 0;
+    int max_batch_ = 64;
+    int prefill_path_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::vector<LayerW> L_;
+    Weight embd_, output_;
+    Vec out_norm_;
+    float* rope_table_ = nullptr;         // [max_context][rope_dims] cos/sin pairs
+    Seq* own_ = nullptr;
+    Stats stats_;
+    int64_t weight_bytes_ = 0;
+
+    // device arena holding every weight
+    uint8_t* arena_ = nullptr;
+    int64_t arena_size_ = 0, arena_used_ = 0;
+    std::vector<void*> extra_allocs_;
+
+    // workspaces (grown on demand)
+    int ws_T_ = 0, ws_logit_rows_ = 0;
+    float *x_ = nullptr, *xn_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *att_ = nullptr, *o_ = nullptr;
+    float *g_ = nullptr, *u_ = nullptr, *logits_ = nullptr, *router_ = nullptr, *wts_ = nullptr;
+    float *xe_ = nullptr, *ye_ = nullptr, *ge_ = nullptr, *ue_ = nullptr, *moe_out_ = nullptr, *sh_gl_ = nullptr;
+    int32_t *tok_d_ = nullptr, *pos_d_ = nullptr, *sel_ = nullptr, *bad_d_ = nullptr, *etok_d_ = nullptr;
+    float* ew_d_ = nullptr;
+    RowKV* rows_d_ = nullptr;
+    // pinned host staging
+    int32_t* h_tok_ = nullptr;
+    int32_t* h_pos_ = nullptr;
+    RowKV* h_rows_ = nullptr;
+    int32_t* h_sel_ = nullptr;
+    float* h_wts_ = nullptr;
+    int32_t* h_etok_ = nullptr;
+    float* h_ew_ = nullptr;
+    int h_cap_ = 0;
+    // profiling
+    bool profiling_ = false;
+    std::vector<ProfileMark> marks_;
+    std::vector<cudaEvent_t> event_pool_;
+    wl_profile_entry prof_[64] = {};
+};
+
+}  // namespace wl
