@@ -141,7 +141,15 @@ def reference_arm(args):
     print(json.dumps(out))
 
 
+def trace(msg):
+    """Stage markers on stderr (the JSON line stays alone on stdout)."""
+    sys.stderr.write(f"[bench {time.strftime('%H:%M:%S')}] {msg}\n")
+    sys.stderr.flush()
+
+
 def main():
+    import faulthandler
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
@@ -176,16 +184,19 @@ def main():
     steps, warm, B = args.steps, args.warmup, args.batch
     ctx = args.prompt + 2 * (steps + warm) + 64
     t0 = time.perf_counter()
+    trace(f"opening synthetic model, {args.layers} layers, context {ctx}")
     m = CudaTransformer(synthetic=spec, device=local, max_context=ctx)
     load_s = time.perf_counter() - t0
     rng = np.random.default_rng(rank)
     seqs = [m.new_sequence() for _ in range(B)]
+    trace(f"model ready in {load_s:.1f} s; prefill {B} x {args.prompt}")
     t0 = time.perf_counter()
     for s in seqs:
         m.forward(rng.integers(0, spec.vocab, args.prompt).astype(np.int32), seq=s)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
 
+    trace(f"prefill {prefill_s:.1f} s; warmup {warm} steps")
     m.bench_decode(seqs, warm)
     launches0 = m.stats().kernel_launches
     barrier()
@@ -199,6 +210,7 @@ def main():
     ms_max = float(ms_t.item())
     value = world * steps * B / (ms_max / 1e3)
 
+    trace(f"timed {steps} steps: {ms:.1f} ms")
     # e2e: the host-facing call, host token ids in, host logits out, every step
     toks = rng.integers(0, spec.vocab, B).astype(np.int32)
     out = np.empty(B * spec.vocab, dtype=np.float32)
@@ -216,11 +228,15 @@ def main():
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e = world * steps * B / float(e2e_t.item())
 
+    trace(f"e2e {e2e_s:.2f} s")
     # live roofline of the dominant kernel: per-launch CUDA events over a second pass of the same steps
     m.profile(1)
     m.bench_decode(seqs, min(steps, 8))
     q4 = m.profile_get(Q4_K)
     q6 = m.profile_get(Q6_K)
+    att = m.profile_get(40)
+    trace(f"profile: q4_K {q4.launches} launches {q4.ms:.1f} ms {q4.bytes / 1e9:.2f} GB; q6_K {q6.launches} "
+          f"{q6.ms:.1f} ms {q6.bytes / 1e9:.2f} GB; attention {att.launches} {att.ms:.1f} ms")
     m.profile(0)
     hbm, _, peak_kind = measured_peaks()
     achieved = q4.bytes / (q4.ms / 1e3) / 1e9 if q4.ms > 0 else None
@@ -237,9 +253,11 @@ def main():
                 "bytes_per_launch": q4.bytes / max(q4.launches, 1),
                 "q6k_achieved_gbs": q6.bytes / (q6.ms / 1e3) / 1e9 if q6.ms > 0 else None}
 
+    trace("profiled pass done")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
+    trace("cpu baseline done")
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
                 "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -96,6 +96,8 @@ typedef struct wl_profile_entry {
     double  ms;
     double  bytes;
 } wl_profile_entry;
+/* wl_profile_get kinds beyond the weight formats. */
+#define WL_PROFILE_ATTENTION 40
 
 /* Synthetic model (benchmarks and full-size tests): a decoder of the given shape whose weights are generated on the
  * device from a counter hash (seed, tensor, element), N(0, sigma) through Irwin-Hall(12), round-to-nearest quantized.

@@ -1,7 +1,9 @@
 // The C ABI of libwindlass_cuda (include/windlass.h): argument checks, exception-to-status translation, and the
 // kernel-level test exports. No function aborts or exits; failures return a status and set wl_last_error().
 #include <cstring>
+#include <mutex>
 #include <new>
+#include <vector>
 #include "../../include/windlass.h"
 #include "wl_common.h"
 #include "wl_kernels.h"
@@ -39,6 +41,43 @@ wl_options defaults()
     wl_options o;
     wl_options_init(&o);
     return o;
+}
+
+// Per-device scratch of the kernel-level exports (the model keeps its own workspaces).
+void* export_scratch(size_t bytes)
+{
+    static std::mutex mu;
+    static void* ptr[64] = {};
+    static size_t size[64] = {};
+    int dev = 0;
+    WL_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64) WL_THROW(WL_EINVAL, "device ordinal out of range");
+    if (size[dev] < bytes) {
+        if (ptr[dev]) { WL_CUDA(cudaDeviceSynchronize()); cudaFree(ptr[dev]); ptr[dev] = nullptr; size[dev] = 0; }
+        WL_CUDA(cudaMalloc(&ptr[dev], bytes));
+        size[dev] = bytes;
+    }
+    return ptr[dev];
+}
+
+// The forward pass's matvec rule: the tensor-core kernel where the format and alignment allow (8 columns per
+// launch, activations prepared once per chunk), else the CUDA-core kernel. force_cuda_cores selects the latter.
+void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, int ncols, float* y, bool force_cuda_cores,
+                cudaStream_t s)
+{
+    const int64_t rb = wl::row_bytes_of(type, cols);
+    if (!force_cuda_cores && wl::k::mma_supported(type, w, rb, cols) && (uintptr_t)x % 16 == 0) {
+        void* scratch = export_scratch(wl::k::xprep_bytes(cols, 8));
+        for (int c0 = 0; c0 < ncols; c0 += 8) {
+            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
+            const wl::k::XPrep p = wl::k::xprep_view(scratch, cols, nc);
+            wl::k::xprep(x + (int64_t)c0 * cols, cols, cols, nc, p, s);
+            wl::k::matvec_mma(type, w, rb, rows, cols, p, y + (int64_t)c0 * rows, rows, s);
+        }
+        return;
+    }
+    wl::k::matvec(type, w, rb, rows, cols, x, cols, ncols, y, rows, s);
 }
 }  // namespace
 
@@ -263,8 +302,7 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
         if (rows <= 0 || cols <= 0 || ncols <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
         if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matvec: null pointer");
         wl::k::init_tables();
-        wl::k::matvec(type, (const uint8_t*)dev_w, wl::row_bytes_of(type, cols), rows, cols, dev_x, cols, ncols, dev_y,
-                      rows, (cudaStream_t)stream);
+        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, ncols, dev_y, false, (cudaStream_t)stream);
         return WL_OK;
     });
 }
@@ -279,8 +317,7 @@ int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
         if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matmul: null pointer");
         if (path < 0 || path > 2) return wl::fail(WL_EINVAL, "wl_matmul: path must be 0, 1 or 2");
         wl::k::init_tables();
-        wl::k::matvec(type, (const uint8_t*)dev_w, wl::row_bytes_of(type, cols), rows, cols, dev_x, cols, T, dev_y,
-                      rows, (cudaStream_t)stream);
+        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, T, dev_y, path == 1, (cudaStream_t)stream);
         return WL_OK;
     });
 }

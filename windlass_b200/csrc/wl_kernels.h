@@ -33,6 +33,24 @@ void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, co
 void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
             int ncols, float* y, int64_t ldy, cudaStream_t s);
 
+// Activations prepared for the tensor-core matvec: per column, f16 hi/lo pairs of 4 values (order v0 v2 v1 v3),
+// the hi/lo sums of every 32 values, and the inverse of the column's power-of-two scale.
+struct XPrep {
+    uint4* groups;      // [nc][cols/4]
+    uint2* sums;        // [nc][cols/64]
+    float* inv_scale;   // [nc]
+    int cols = 0, nc = 0;
+};
+size_t xprep_bytes(int cols, int nc);
+XPrep xprep_view(void* scratch, int cols, int nc);
+// x[t*ldx + i] for t < nc (1..8), cols a multiple of 256.
+void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s);
+// True when `type` has a tensor-core matvec and the weights' alignment allows it.
+bool mma_supported(int type, const uint8_t* w, int64_t row_bytes, int cols);
+// y[t*ldy + r] = W[r] . x[t] from prepared activations (same contract as matvec).
+void matvec_mma(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const XPrep& p, float* y,
+                int64_t ldy, cudaStream_t s);
+
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);
 // y[t*n + i] += b[i] for T rows (AddBias, Transformer.cs:442-451).

@@ -375,6 +375,7 @@ Model::~Model()
     dfree(sh_gl_); dfree(tok_d_); dfree(pos_d_); dfree(sel_); dfree(bad_d_); dfree(etok_d_); dfree(ew_d_); dfree(rows_d_);
     hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
     for (void* p : extra_allocs_) cudaFree(p);
+    if (xprep_buf_) cudaFree(xprep_buf_);
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
@@ -461,6 +462,15 @@ void Model::ensure_workspace(int T, int logit_rows)
         }
         ws_T_ = n;
     }
+    if (!xprep_buf_) {
+        int max_cols = c_.embd;
+        for (const LayerW& L : L_) {
+            for (const Weight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down, &L.gate_exps, &L.up_exps,
+                                    &L.down_exps, &L.sh_gate, &L.sh_up, &L.sh_down})
+                if (w->present()) max_cols = std::max(max_cols, w->cols);
+        }
+        WL_CUDA(cudaMalloc(&xprep_buf_, k::xprep_bytes(max_cols, 8)));
+    }
     if (logit_rows > ws_logit_rows_) {
         dfree(logits_);
         logits_ = dalloc<float>((int64_t)logit_rows * c_.vocab);
@@ -471,30 +481,58 @@ void Model::ensure_workspace(int T, int logit_rows)
 // ---------------------------------------------------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------------------------------------------------
-void Model::matmul(const Weight& w, const float* x, int T, float* y, int path)
+// y[T][rows] = W x. Formats with a tensor-core matvec take activations prepared by k::xprep (8 columns at a time);
+// reuse_x says x is the input of the previous matmul as well, so its prepared form can be reused.
+void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
 {
     (void)path;
-    ProfileMark mark{};
-    if (profiling_) {
-        for (int i = 0; i < 2; ++i) {
-            if (event_pool_.empty()) {
-                cudaEvent_t e;
-                WL_CUDA(cudaEventCreate(&e));
-                event_pool_.push_back(e);
+    if (k::mma_supported(w.type, w.d, w.row_bytes, w.cols) && xprep_buf_) {
+        for (int c0 = 0; c0 < T; c0 += 8) {
+            const int nc = std::min(8, T - c0);
+            const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
+            const bool same = reuse_x && T <= 8 && prep_x_ == x && prep_cols_ == w.cols && prep_nc_ == nc;
+            if (!same) {
+                k::xprep(x + (int64_t)c0 * w.cols, w.cols, w.cols, nc, p, stream_);
+                prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
+            const int mark = profile_begin();
+            k::matvec_mma(w.type, w.d, w.row_bytes, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, stream_);
+            profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
-        mark.start = event_pool_.back(); event_pool_.pop_back();
-        mark.stop = event_pool_.back(); event_pool_.pop_back();
-        mark.type = w.type;
-        mark.bytes = (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows);
-        WL_CUDA(cudaEventRecord(mark.start, stream_));
+        if (T > 8) prep_x_ = nullptr;
+        return;
     }
+    prep_x_ = nullptr;
+    const int mark = profile_begin();
     k::matvec(w.type, w.d, w.row_bytes, w.rows, w.cols, x, w.cols, T, y, w.rows, stream_);
-    if (profiling_) {
-        WL_CUDA(cudaEventRecord(mark.stop, stream_));
-        marks_.push_back(mark);
-        if (marks_.size() > 4096) flush_profile();
+    profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows));
+}
+
+// Starts a profiled region (an event pair around launches on the model's stream); -1 when profiling is off.
+int Model::profile_begin()
+{
+    if (!profiling_) return -1;
+    while (event_pool_.size() < 2) {
+        cudaEvent_t e;
+        WL_CUDA(cudaEventCreate(&e));
+        event_pool_.push_back(e);
     }
+    ProfileMark m{};
+    m.start = event_pool_.back(); event_pool_.pop_back();
+    m.stop = event_pool_.back(); event_pool_.pop_back();
+    WL_CUDA(cudaEventRecord(m.start, stream_));
+    marks_.push_back(m);
+    return (int)marks_.size() - 1;
+}
+
+void Model::profile_end(int mark, int kind, double bytes)
+{
+    if (mark < 0) return;
+    ProfileMark& m = marks_[(size_t)mark];
+    m.type = kind;
+    m.bytes = bytes;
+    WL_CUDA(cudaEventRecord(m.stop, stream_));
+    if (marks_.size() > 4096) flush_profile();
 }
 
 static Weight slice(const Weight& w, int e)
@@ -510,7 +548,7 @@ void Model::ffn_dense(const LayerW& L, int T)
 {
     const int F = L.gate.rows;
     matmul(L.gate, xn_, T, g_);
-    matmul(L.up, xn_, T, u_);
+    matmul(L.up, xn_, T, u_, 0, true);
     k::swiglu(g_, u_, (int64_t)T * F, stream_);
     matmul(L.down, g_, T, o_);
 }
@@ -547,7 +585,7 @@ void Model::ffn_moe(const LayerW& L, int T)
         const int32_t* toks = etok_d_ + start[e];
         k::gather_rows(xe_, xn_, toks, n, E, stream_);
         matmul(slice(L.gate_exps, e), xe_, n, ge_);
-        matmul(slice(L.up_exps, e), xe_, n, ue_);
+        matmul(slice(L.up_exps, e), xe_, n, ue_, 0, true);
         k::swiglu(ge_, ue_, (int64_t)n * X, stream_);
         matmul(slice(L.down_exps, e), ge_, n, ye_);
         k::scatter_add(moe_out_, ye_, toks, ew_d_ + start[e], n, E, stream_);
@@ -555,7 +593,7 @@ void Model::ffn_moe(const LayerW& L, int T)
     if (L.sh_gate.present()) {
         const int SF = L.sh_gate.rows;
         matmul(L.sh_gate, xn_, T, g_);
-        matmul(L.sh_up, xn_, T, u_);
+        matmul(L.sh_up, xn_, T, u_, 0, true);
         k::swiglu(g_, u_, (int64_t)T * SF, stream_);
         matmul(L.sh_down, g_, T, o_);
         if (L.sh_gate_inp.present()) matmul(L.sh_gate_inp, xn_, T, sh_gl_);
@@ -574,8 +612,8 @@ void Model::layer(int l, int T, int max_n)
     if (c_.post_norms) WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
     else k::rmsnorm(x_, T, E, L.attn_norm.d, c_.rms_eps, xn_, stream_);
     matmul(L.q, xn_, T, q_);
-    matmul(L.k, xn_, T, k_);
-    matmul(L.v, xn_, T, v_);
+    matmul(L.k, xn_, T, k_, 0, true);
+    matmul(L.v, xn_, T, v_, 0, true);
     if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
     if (L.kb.present()) k::add_bias(k_, L.kb.d, T, KD, stream_);
     if (L.vb.present()) k::add_bias(v_, L.vb.d, T, KD, stream_);
@@ -590,7 +628,9 @@ void Model::layer(int l, int T, int max_n)
     k::rope(k_, T, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_, stream_);
     k::kv_append(k_, v_, T, KD, rows_d_, l, pos_d_, stream_);
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
+    const int mark = profile_begin();
     k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, max_n, att_, stream_);
+    profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
     matmul(L.o, att_, T, o_);
     if (c_.post_norms) k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
     k::residual(x_, o_, rs, n, stream_);

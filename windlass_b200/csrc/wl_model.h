@@ -90,7 +90,7 @@ public:
     cudaStream_t stream() const { return stream_; }
 
     // y[T][rows] = W x[T][cols] on the model's stream; path 0 chooses by T (the forward pass's own rule).
-    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0);
+    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false);
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
@@ -104,6 +104,8 @@ private:
         double bytes;
     };
     void flush_profile();
+    int profile_begin();
+    void profile_end(int mark, int kind, double bytes);
     void upload_step(int T, const RowKV* rows, const int32_t* pos, const int32_t* tokens);
     void step_device(int T, int first, int max_n);
     Model() = default;
@@ -157,6 +159,10 @@ private:
     int32_t* h_etok_ = nullptr;
     float* h_ew_ = nullptr;
     int h_cap_ = 0;
+    // activations prepared for the tensor-core matvec (k::xprep), and what they were prepared from
+    void* xprep_buf_ = nullptr;
+    const float* prep_x_ = nullptr;
+    int prep_cols_ = 0, prep_nc_ = 0;
     // profiling
     bool profiling_ = false;
     std::vector<ProfileMark> marks_;
