@@ -141,6 +141,70 @@ def reference_arm(args):
     print(json.dumps(out))
 
 
+def sweep(args):
+    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the kernel time (CUDA
+    events on the launching stream, averaged over rotating weight copies whose total exceeds L2) and the weight
+    bandwidth (b <= 8) or TFLOP/s (b >= 64). One JSON line with the whole table."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from windlass_b200 import _lib
+    L = _lib.lib()
+    n = args.sweep_n
+    fmts = args.formats.split(",")
+    batches = [int(b) for b in args.batches.split(",")]
+    stream = torch.cuda.current_stream()
+    hbm, bf16, _ = measured_peaks()
+    rows = []
+    rng = np.random.default_rng(0)
+    for f in fmts:
+        t = _lib.TYPES[f]
+        bs, ts = {"q4_K": (256, 144), "q6_K": (256, 210), "q8_0": (32, 34), "iq4_xs": (256, 136),
+                  "iq2_xxs": (256, 66)}[f]
+        nbytes = n * n // bs * ts
+        copies = max(4, int(np.ceil(4 * 126e6 / nbytes)))
+        ws = []
+        for k in range(copies):
+            buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+            if f in ("q4_K", "q6_K", "q8_0"):
+                _lib.check(L.wl_synth_tensor(t, 42 + k, 0x7001, n, n, C.c_float(0.02), C.c_float(0.0),
+                                             C.c_void_p(buf.data_ptr()), C.c_void_p(stream.cuda_stream)))
+            else:   # the reference's random-payload method: random bytes with a fixed fp16 scale in each block
+                raw = rng.integers(0, 256, nbytes, dtype=np.uint8).reshape(-1, ts)
+                raw[:, 0], raw[:, 1] = 0x00, 0x1C          # fp16 0.0039
+                buf.copy_(torch.from_numpy(raw.reshape(-1)))
+            ws.append(buf)
+        for b in batches:
+            x = torch.randn(b, n, device="cuda")
+            y = torch.empty(b, n, device="cuda")
+            def run(i):
+                w = ws[i % copies]
+                if b <= 8:
+                    st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
+                                     C.c_void_p(y.data_ptr()), C.c_void_p(stream.cuda_stream))
+                else:
+                    st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
+                                     C.c_void_p(y.data_ptr()), 0, C.c_void_p(stream.cuda_stream))
+                _lib.check(st)
+            for i in range(max(args.warmup, 3)):
+                run(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(args.iters):
+                run(i)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.iters
+            alg = nbytes + 4 * b * 2 * n
+            rows.append({"format": f, "batch": b, "us": ms * 1e3, "gbs": alg / (ms / 1e3) / 1e9,
+                         "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,
+                         "tflops": 2.0 * n * n * b / (ms / 1e3) / 1e12})
+            trace(f"{f} b{b}: {ms * 1e3:.1f} us, {rows[-1]['gbs']:.0f} GB/s, {rows[-1]['tflops']:.2f} TFLOP/s")
+    print(json.dumps({"metric": "Q4_K matvec HBM GB/s (configs[1] sweep)", "unit": "GB/s", "n": n, "table": rows,
+                      "peak_hbm_gbs": hbm, "peak_bf16_tflops": bf16}))
+
+
 def trace(msg):
     """Stage markers on stderr (the JSON line stays alone on stdout)."""
     sys.stderr.write(f"[bench {time.strftime('%H:%M:%S')}] {msg}\n")
@@ -159,10 +223,17 @@ def main():
     ap.add_argument("--layers", type=int, default=80)
     ap.add_argument("--impl", default="windlass", choices=["windlass", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="configs[1] matvec sweep instead of the decode benchmark")
+    ap.add_argument("--sweep-n", type=int, default=8192)
+    ap.add_argument("--formats", default="q4_K,q6_K,q8_0,iq4_xs,iq2_xxs")
+    ap.add_argument("--batches", default="1,4,8,64")
+    ap.add_argument("--iters", type=int, default=50)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.sweep:
+        return sweep(args)
 
     import numpy as np
     import torch

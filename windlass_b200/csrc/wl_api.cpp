@@ -68,12 +68,17 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
 {
     const int64_t rb = wl::row_bytes_of(type, cols);
     if (!force_cuda_cores && wl::k::mma_supported(type, w, rb, cols) && (uintptr_t)x % 16 == 0) {
-        void* scratch = export_scratch(wl::k::xprep_bytes(cols, 8));
+        // scratch: [error word | prepared activations]
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
+        int* err = (int*)scratch;
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        wl::k::WeightMap map;
+        wl::k::make_weight_map(type, w, rows, rb, &map);
         for (int c0 = 0; c0 < ncols; c0 += 8) {
             const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
-            const wl::k::XPrep p = wl::k::xprep_view(scratch, cols, nc);
+            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
             wl::k::xprep(x + (int64_t)c0 * cols, cols, cols, nc, p, s);
-            wl::k::matvec_mma(type, w, rb, rows, cols, p, y + (int64_t)c0 * rows, rows, s);
+            wl::k::matvec_mma(type, map, 0, rows, cols, p, y + (int64_t)c0 * rows, rows, err, s);
         }
         return;
     }

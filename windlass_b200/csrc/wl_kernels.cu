@@ -60,6 +60,8 @@ static inline void launched()
 
 int64_t launches() { return g_launches.load(std::memory_order_relaxed); }
 
+void note_launch() { launched(); }
+
 // ------------------------------------------------------------------------------------------------------------------
 // dequant / embedding (bit-exact)
 // ------------------------------------------------------------------------------------------------------------------
@@ -430,241 +432,6 @@ void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, c
         else launch_mv<MV_GENERIC>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         launched();
     }
-}
-
-// ------------------------------------------------------------------------------------------------------------------
-// tensor-core decode matvec (mma.sync m16n8k16, f16 operands, fp32 accumulate)
-//
-// Weights become A fragments of exact small integers in f16 (Q4_K: q*s, the 4-bit code times its 6-bit sub-block
-// scale, at most 945, made with one HFMA2 from the 0x6400|q bit trick). Activations become B fragments of an f16
-// hi/lo pair per value (x*2^k = hi + lo, |error| <= 2^-22 relative), prepared once per input by k_xprep. Each k-step
-// sums 16 values; a thread supplies 4 of them, (v0, v2) in the first register pair and (v1, v3) in the second, so one
-// 16-byte load gives a thread its hi and lo fragments. The Q4_K min term is one more MMA per superblock over the
-// 32-value sums of x. A CTA owns 32 rows; its 8 warps split the row's superblocks and are summed in a fixed order,
-// so a column's result never depends on the other columns of the launch.
-// ------------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1)
-{
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};\n"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// 16-byte weight load that does not allocate in L1 (weights are streamed once).
-__device__ __forceinline__ uint4 ldg_stream(const void* p)
-{
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-
-// x -> f16 hi/lo groups: one CTA per activation column. The column is scaled by a power of two so its largest
-// magnitude lies in [2^9, 2^10) (exact; undone on the output), which keeps hi and the 32-value sums in f16 range
-// and lo mostly clear of subnormals.
-__global__ void __launch_bounds__(256) k_xprep(const float* __restrict__ x, int64_t ldx, int cols,
-                                               uint4* __restrict__ groups, uint2* __restrict__ sums,
-                                               float* __restrict__ inv_scale)
-{
-    __shared__ float scratch[32];
-    const int n = blockIdx.x;
-    const float* xc = x + (int64_t)n * ldx;
-    float m = 0.f;
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, fabsf(xc[i]));
-    m = block_max_f(m, scratch);
-    int e = 0;
-    if (m > 0.f) frexpf(m, &e);
-    e = e < -100 ? -100 : e > 100 ? 100 : e;
-    const float scale = m > 0.f ? ldexpf(1.0f, 10 - e) : 1.0f;   // max in [2^9, 2^10): sums of 32 stay < 2^15
-    const int ngroups = cols >> 2;
-    uint4* gc = groups + (int64_t)n * ngroups;
-    uint2* sc = sums + (int64_t)n * (cols >> 6);
-    for (int g = threadIdx.x; g < ngroups; g += blockDim.x) {
-        const float4 v4 = *reinterpret_cast<const float4*>(xc + 4 * g);
-        const float v[4] = {v4.x * scale, v4.y * scale, v4.z * scale, v4.w * scale};
-        __half hi[4], lo[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            hi[k] = __float2half_rn(v[k]);
-            lo[k] = __float2half_rn(v[k] - __half2float(hi[k]));
-        }
-        gc[g] = make_uint4(h2_bits(__halves2half2(hi[0], hi[2])), h2_bits(__halves2half2(hi[1], hi[3])),
-                           h2_bits(__halves2half2(lo[0], lo[2])), h2_bits(__halves2half2(lo[1], lo[3])));
-        // sum of the 32 values of this group's sub-block (8 consecutive groups in 8 consecutive lanes)
-        float s = (v[0] + v[1]) + (v[2] + v[3]);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        const float s_next = __shfl_down_sync(0xffffffffu, s, 8);      // the next sub-block's sum
-        if ((g & 15) == 0) {
-            const __half h0 = __float2half_rn(s), h1 = __float2half_rn(s_next);
-            const __half l0 = __float2half_rn(s - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
-            sc[g >> 4] = make_uint2(h2_bits(__halves2half2(h0, h1)), h2_bits(__halves2half2(l0, l1)));
-        }
-    }
-    if (threadIdx.x == 0) inv_scale[n] = 1.0f / scale;
-}
-
-// ScaleMinK4 (src/Quants.cs:322-330) on the 12 scale bytes held as three words (bytes 4..15 of the superblock).
-__device__ __forceinline__ void scale_min_k4_words(int j, uint32_t y, uint32_t z, uint32_t w, int& s, int& m)
-{
-    const int sh = 8 * (j & 3);
-    const int by = (y >> sh) & 0xFF, bz = (z >> sh) & 0xFF, bw = (w >> sh) & 0xFF;
-    if (j < 4) { s = by & 63; m = bz & 63; }
-    else { s = (bw & 0xF) | ((by >> 6) << 4); m = (bw >> 4) | ((bz >> 6) << 4); }
-}
-
-__device__ __forceinline__ uint32_t q4_fold(uint32_t w, int shift, __half2 s2, __half2 ns2)
-{
-    const uint32_t t = ((w >> shift) & 0x000F000Fu) | 0x64006400u;      // f16 (1024 + q) in both halves
-    return h2_bits(__hfma2(bits_h2(t), s2, ns2));                        // (1024 + q)*s - 1024*s = q*s, exact
-}
-
-template <int NC>
-__global__ void __launch_bounds__(256, 1) k_mmv_q4k(const uint8_t* __restrict__ w, int64_t row_bytes, int rows, int nsb,
-                                                    const uint4* __restrict__ xg, const uint2* __restrict__ xs,
-                                                    const float* __restrict__ xinv, float* __restrict__ y, int64_t ldy)
-{
-    __shared__ float red[8][32][9];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const int r0 = blockIdx.x * 32;
-    const uint8_t* rp[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int r = r0 + g + 8 * i;
-        r = r < rows ? r : rows - 1;
-        rp[i] = w + (int64_t)r * row_bytes;
-    }
-    const bool has_col = g < NC;
-    const uint4* xcol = xg + (int64_t)(has_col ? g : 0) * nsb * 64;
-    const uint2* scol = xs + (int64_t)(has_col ? g : 0) * nsb * 4;
-    float dt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    for (int sb = warp; sb < nsb; sb += 8) {
-        uint4 hdr[4], qa[4], qb[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint8_t* blk = rp[i] + (int64_t)sb * 144;
-            hdr[i] = ldg_stream(blk);
-            qa[i] = ldg_stream(blk + 16 + 32 * c);
-            qb[i] = ldg_stream(blk + 32 + 32 * c);
-        }
-        __half2 slo[4], nslo[4], shi[4], nshi[4];
-        uint32_t mp[4];
-        float dd[4], dm[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int s1, m1, s2, m2;
-            scale_min_k4_words(2 * c, hdr[i].y, hdr[i].z, hdr[i].w, s1, m1);
-            scale_min_k4_words(2 * c + 1, hdr[i].y, hdr[i].z, hdr[i].w, s2, m2);
-            slo[i] = __float2half2_rn((float)s1);
-            nslo[i] = __float2half2_rn(-1024.f * (float)s1);
-            shi[i] = __float2half2_rn((float)s2);
-            nshi[i] = __float2half2_rn(-1024.f * (float)s2);
-            mp[i] = h2_bits(__floats2half2_rn((float)m1, (float)m2));
-            dd[i] = h2f((uint16_t)(hdr[i].x & 0xFFFF));
-            dm[i] = h2f((uint16_t)(hdr[i].x >> 16));
-        }
-        float dq[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        float dn[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const uint4* xb = xcol + sb * 64 + 16 * c;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint4 b = has_col ? __ldg(xb + 8 * h + i) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                for (int G = 0; G < 2; ++G) {
-                    const int ra = 2 * G, rb = 2 * G + 1;
-                    const uint32_t wa = i < 4 ? (&qa[ra].x)[i] : (&qb[ra].x)[i - 4];
-                    const uint32_t wb = i < 4 ? (&qa[rb].x)[i] : (&qb[rb].x)[i - 4];
-                    const __half2 sa = h ? shi[ra] : slo[ra], nsa = h ? nshi[ra] : nslo[ra];
-                    const __half2 sbv = h ? shi[rb] : slo[rb], nsb2 = h ? nshi[rb] : nslo[rb];
-                    const uint32_t a0 = q4_fold(wa, 4 * h, sa, nsa);
-                    const uint32_t a2 = q4_fold(wa, 4 * h + 8, sa, nsa);
-                    const uint32_t a1 = q4_fold(wb, 4 * h, sbv, nsb2);
-                    const uint32_t a3 = q4_fold(wb, 4 * h + 8, sbv, nsb2);
-                    mma16816(dq[G], a0, a1, a2, a3, b.x, b.y);
-                    mma16816(dq[G], a0, a1, a2, a3, b.z, b.w);
-                }
-            }
-        }
-        const uint2 bs = has_col ? __ldg(scol + sb * 4 + c) : make_uint2(0u, 0u);
-#pragma unroll
-        for (int G = 0; G < 2; ++G) {
-            mma16816(dn[G], mp[2 * G], mp[2 * G + 1], mp[2 * G], mp[2 * G + 1], bs.x, bs.y);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int rs = 2 * G + (e >> 1);
-                dt[G][e] += dd[rs] * dq[G][e] - dm[rs] * dn[G][e];
-            }
-        }
-    }
-#pragma unroll
-    for (int G = 0; G < 2; ++G)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][16 * G + g + 8 * (e >> 1)][2 * c + (e & 1)] = dt[G][e];
-    __syncthreads();
-    const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
-    if (col < NC && r0 + rl < rows) {
-        float s = 0.f;
-#pragma unroll
-        for (int wv = 0; wv < 8; ++wv) s += red[wv][rl][col];
-        y[(int64_t)col * ldy + r0 + rl] = s * xinv[col];
-    }
-}
-
-size_t xprep_bytes(int cols, int nc)
-{
-    return (size_t)nc * ((size_t)cols * 4 + (size_t)(cols / 64) * 8 + 16) + 256;
-}
-
-XPrep xprep_view(void* scratch, int cols, int nc)
-{
-    XPrep p;
-    uint8_t* b = (uint8_t*)scratch;
-    p.groups = (uint4*)b;
-    b += (size_t)nc * cols * 4;
-    p.sums = (uint2*)b;
-    b += (size_t)nc * (cols / 64) * 8;
-    p.inv_scale = (float*)b;
-    p.cols = cols;
-    p.nc = nc;
-    return p;
-}
-
-void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s)
-{
-    k_xprep<<<nc, 256, 0, s>>>(x, ldx, cols, p.groups, p.sums, p.inv_scale);
-    launched();
-}
-
-bool mma_supported(int type, const uint8_t* w, int64_t row_bytes, int cols)
-{
-    return type == 12 && cols % 256 == 0 && (uintptr_t)w % 16 == 0 && row_bytes % 16 == 0;
-}
-
-void matvec_mma(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const XPrep& p, float* y,
-                int64_t ldy, cudaStream_t s)
-{
-    (void)type;
-    const unsigned grid = grid_for(rows, 32);
-    const int nsb = cols / 256;
-    switch (p.nc) {
-    case 1: k_mmv_q4k<1><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 2: k_mmv_q4k<2><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 3: k_mmv_q4k<3><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 4: k_mmv_q4k<4><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 5: k_mmv_q4k<5><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 6: k_mmv_q4k<6><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    case 7: k_mmv_q4k<7><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    default: k_mmv_q4k<8><<<grid, 256, 0, s>>>(w, row_bytes, rows, nsb, p.groups, p.sums, p.inv_scale, y, ldy); break;
-    }
-    launched();
 }
 
 // ------------------------------------------------------------------------------------------------------------------

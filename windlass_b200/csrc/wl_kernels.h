@@ -18,8 +18,9 @@ namespace k {
 
 // Copies the I-quant tables into the current device's constant memory (once per device).
 void init_tables();
-// Kernels launched by this process so far.
+// Kernels launched by this process so far; note_launch() checks and counts a launch made in another file.
 int64_t launches();
+void note_launch();
 
 // Quants.DecodeRow for n consecutive values (n a multiple of the block size), bit-exact.
 void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s);
@@ -33,23 +34,31 @@ void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, co
 void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
             int ncols, float* y, int64_t ldy, cudaStream_t s);
 
-// Activations prepared for the tensor-core matvec: per column, f16 hi/lo pairs of 4 values (order v0 v2 v1 v3),
-// the hi/lo sums of every 32 values, and the inverse of the column's power-of-two scale.
+// Activations prepared for the tensor-core matvec: per column and 256-value superblock, f16 hi/lo pairs of every
+// 4 values (order v0 v2 v1 v3) under a power-of-two scale, and a 48-byte record of the hi/lo sums of every 32
+// values plus the inverse scale.
 struct XPrep {
     uint4* groups;      // [nc][cols/4]
-    uint2* sums;        // [nc][cols/64]
-    float* inv_scale;   // [nc]
+    uint4* sums;        // [nc][cols/256][3]
     int cols = 0, nc = 0;
 };
 size_t xprep_bytes(int cols, int nc);
 XPrep xprep_view(void* scratch, int cols, int nc);
 // x[t*ldx + i] for t < nc (1..8), cols a multiple of 256.
 void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s);
+// A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
+struct alignas(64) WeightMap {
+    uint8_t bytes[128];
+    bool valid = false;
+};
 // True when `type` has a tensor-core matvec and the weights' alignment allows it.
 bool mma_supported(int type, const uint8_t* w, int64_t row_bytes, int cols);
-// y[t*ldy + r] = W[r] . x[t] from prepared activations (same contract as matvec).
-void matvec_mma(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const XPrep& p, float* y,
-                int64_t ldy, cudaStream_t s);
+// Map over rows_total rows (all experts of a stacked tensor); boxes of one superblock x 32 rows.
+void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row_bytes, WeightMap* out);
+// y[t*ldy + r] = W[row_base + r] . x[t] for r < rows, from prepared activations (same contract as matvec). A stuck
+// copy sets *err (device memory) instead of hanging.
+void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y,
+                int64_t ldy, int* err, cudaStream_t s);
 
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);

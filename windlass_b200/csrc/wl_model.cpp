@@ -361,6 +361,7 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
 void Model::finish_open()
 {
     if (!rope_table_) build_rope_table(nullptr, 0);
+    build_maps();
     own_ = new_seq();
 }
 
@@ -376,6 +377,7 @@ Model::~Model()
     hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
     for (void* p : extra_allocs_) cudaFree(p);
     if (xprep_buf_) cudaFree(xprep_buf_);
+    dfree(err_d_);
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
@@ -486,7 +488,7 @@ void Model::ensure_workspace(int T, int logit_rows)
 void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
 {
     (void)path;
-    if (k::mma_supported(w.type, w.d, w.row_bytes, w.cols) && xprep_buf_) {
+    if (w.map.valid && xprep_buf_) {
         for (int c0 = 0; c0 < T; c0 += 8) {
             const int nc = std::min(8, T - c0);
             const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
@@ -496,7 +498,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
-            k::matvec_mma(w.type, w.d, w.row_bytes, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, stream_);
+            k::matvec_mma(w.type, w.map, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;
@@ -541,7 +543,37 @@ static Weight slice(const Weight& w, int e)
     s.d = const_cast<uint8_t*>(w.expert(e));
     s.experts = 1;
     s.bytes = (int64_t)w.rows * w.row_bytes;
+    s.row_base = w.row_base + e * w.rows;
     return s;
+}
+
+// Tensor maps for every weight the tensor-core matvec can read.
+void Model::build_maps()
+{
+    auto mk = [&](Weight& w) {
+        if (w.present() && k::mma_supported(w.type, w.d, w.row_bytes, w.cols))
+            k::make_weight_map(w.type, w.d, (int64_t)w.rows * w.experts, w.row_bytes, &w.map);
+    };
+    for (LayerW& L : L_)
+        for (Weight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down, &L.router, &L.gate_exps, &L.up_exps,
+                          &L.down_exps, &L.sh_gate, &L.sh_up, &L.sh_down, &L.sh_gate_inp})
+            mk(*w);
+    mk(output_);
+    if (!err_d_) {
+        err_d_ = dalloc<int>(1);
+        WL_CUDA(cudaMemset(err_d_, 0, sizeof(int)));
+    }
+}
+
+// A bounded device wait that gave up leaves a code in err_d_; report it once the stream is idle.
+void Model::check_device_error()
+{
+    int e = 0;
+    WL_CUDA(cudaMemcpy(&e, err_d_, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e != 0) {
+        WL_CUDA(cudaMemset(err_d_, 0, sizeof(int)));
+        WL_THROW(WL_ETIMEDOUT, "a device-side wait gave up (code " + std::to_string(e) + ")");
+    }
 }
 
 void Model::ffn_dense(const LayerW& L, int T)
@@ -697,6 +729,7 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
     }
     WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));
     WL_CUDA(cudaStreamSynchronize(stream_));
+    check_device_error();
     flush_profile();
     if (progress) progress(total, total, user);
     stats_.tokens += T;
@@ -747,6 +780,7 @@ double Model::bench_decode(Seq* const* seqs, int N, int steps)
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     cudaFree(pos_all_d);
+    check_device_error();
     flush_profile();
     for (int i = 0; i < N; ++i) seqs[i]->length = len[i] + steps;
     stats_.tokens += (int64_t)N * steps;

@@ -20,6 +20,8 @@ struct Weight {
     int rows = 0, cols = 0, experts = 1;
     int64_t row_bytes = 0, bytes = 0;
     uint8_t* d = nullptr;
+    k::WeightMap map;            // TMA map over all rows of all experts, for formats with a tensor-core matvec
+    int row_base = 0;            // first row of this view inside the map (an expert slice)
     bool present() const { return d != nullptr; }
     const uint8_t* expert(int e) const { return d + (int64_t)e * rows * row_bytes; }
 };
@@ -104,6 +106,8 @@ private:
         double bytes;
     };
     void flush_profile();
+    void build_maps();
+    void check_device_error();
     int profile_begin();
     void profile_end(int mark, int kind, double bytes);
     void upload_step(int T, const RowKV* rows, const int32_t* pos, const int32_t* tokens);
@@ -161,6 +165,7 @@ private:
     int h_cap_ = 0;
     // activations prepared for the tensor-core matvec (k::xprep), and what they were prepared from
     void* xprep_buf_ = nullptr;
+    int* err_d_ = nullptr;              // device error word of the bounded waits
     const float* prep_x_ = nullptr;
     int prep_cols_ = 0, prep_nc_ = 0;
     // profiling
