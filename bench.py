@@ -319,7 +319,7 @@ def main():
                 traffic = float(line.split()[1]) * q4.bytes / max(q4.launches, 1)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm if achieved else None, "traffic": traffic,
-                "kernel": "k_matvec<Q4_K> (fused dequant-dot)", "peak_source": peak_kind,
+                "kernel": "k_mmv_q4k (TMA-staged tensor-core Q4_K matvec)", "peak_source": peak_kind,
                 "launches": q4.launches, "avg_launch_us": 1e3 * q4.ms / max(q4.launches, 1),
                 "bytes_per_launch": q4.bytes / max(q4.launches, 1),
                 "q6k_achieved_gbs": q6.bytes / (q6.ms / 1e3) / 1e9 if q6.ms > 0 else None}

@@ -98,7 +98,7 @@ void wl_options_init(wl_options* opt)
     opt->max_batch = 64;
     opt->resident = -1;
     opt->prefill_path = 0;
-    opt->use_graphs = 0;
+    opt->use_graphs = 1;
 }
 
 const char* wl_last_error(void) { return wl::last_error_cstr(); }
@@ -161,7 +161,7 @@ int32_t wl_stats_get(const wl_model* model, wl_stats* stats)
         const wl::Stats& s = model->m->stats();
         stats->bytes_h2d = s.bytes_h2d; stats->expert_runs = s.expert_runs; stats->forward_calls = s.forward_calls;
         stats->batch_calls = s.batch_calls; stats->tokens = s.tokens; stats->last_forward_ms = s.last_forward_ms;
-        stats->kernel_launches = wl::k::launches();
+        stats->kernel_launches = wl::k::launches() + model->m->graph_launches();
         return WL_OK;
     });
 }

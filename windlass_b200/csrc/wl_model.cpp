@@ -48,6 +48,7 @@ void Model::init_device(const wl_options& opt)
     k::init_tables();
     WL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     max_batch_ = opt.max_batch > 0 ? opt.max_batch : 64;
+    use_graphs_ = opt.use_graphs != 0;
     prefill_path_ = opt.prefill_path;
 }
 
@@ -369,6 +370,7 @@ Model::~Model()
 {
     if (device_ >= 0) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    drop_graphs();
     if (own_) free_seq(own_);
     dfree(arena_); dfree(rope_table_);
     dfree(x_); dfree(xn_); dfree(q_); dfree(k_); dfree(v_); dfree(att_); dfree(o_); dfree(g_); dfree(u_);
@@ -463,6 +465,8 @@ void Model::ensure_workspace(int T, int logit_rows)
             h_etok_ = halloc<int32_t>((int64_t)n * K); h_ew_ = halloc<float>((int64_t)n * K);
         }
         ws_T_ = n;
+        ws_gen_++;
+        drop_graphs();
     }
     if (!xprep_buf_) {
         int max_cols = c_.embd;
@@ -477,6 +481,8 @@ void Model::ensure_workspace(int T, int logit_rows)
         dfree(logits_);
         logits_ = dalloc<float>((int64_t)logit_rows * c_.vocab);
         ws_logit_rows_ = logit_rows;
+        ws_gen_++;
+        drop_graphs();
     }
 }
 
@@ -716,7 +722,9 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
     int max_n = 0;
     for (int t = 0; t < T; ++t) max_n = std::max(max_n, pos[t] + 1);
     const int total = c_.layers + 1;
-    if (!cancel && !progress) step_device(T, first, max_n);
+    if (!progress && (!cancel || !*cancel) && graph_step(T, first)) {
+        // the whole step ran as one graph; a cancel flag set meanwhile is seen by the next call
+    } else if (!cancel && !progress) step_device(T, first, max_n);
     else {
         k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
         for (int l = 0; l < c_.layers; ++l) {
@@ -735,6 +743,59 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
     stats_.tokens += T;
     stats_.last_forward_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     return WL_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// CUDA graphs: a decode step of T <= 8 rows is captured once per (T, first logit row) and replayed. The graph reads
+// token ids, positions and KV-cache rows from the fixed device buffers upload_step fills, and sizes attention for the
+// whole context, so one graph serves every step of that shape until the workspaces are reallocated. MoE layers
+// (host-side expert grouping), profiling and per-layer progress callbacks run eagerly.
+// ---------------------------------------------------------------------------------------------------------------------
+bool Model::graphable(int T) const { return use_graphs_ && !profiling_ && c_.expert_count == 0 && T <= 8; }
+
+// True when a graph for (T, first) exists or could be captured now (after one eager run of that shape).
+bool Model::graph_ready(int T, int first)
+{
+    if (!graphable(T)) return false;
+    for (const GraphEntry& g : graphs_)
+        if (g.T == T && g.first == first && g.gen == ws_gen_) return true;
+    // capture: kernels set their launch attributes during an eager run first
+    step_device(T, first, max_context_);
+    const int64_t l0 = k::launches();
+    cudaGraph_t graph = nullptr;
+    WL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+        step_device(T, first, max_context_);
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+    }
+    WL_CUDA(cudaStreamEndCapture(stream_, &graph));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    WL_CUDA(e);
+    graphs_.push_back(GraphEntry{T, first, ws_gen_, exec, k::launches() - l0});
+    return true;
+}
+
+bool Model::graph_step(int T, int first)
+{
+    if (!graph_ready(T, first)) return false;
+    for (const GraphEntry& g : graphs_)
+        if (g.T == T && g.first == first && g.gen == ws_gen_) {
+            WL_CUDA(cudaGraphLaunch(g.exec, stream_));
+            graph_launches_ += g.nodes;
+            return true;
+        }
+    return false;
+}
+
+void Model::drop_graphs()
+{
+    for (GraphEntry& g : graphs_) cudaGraphExecDestroy(g.exec);
+    graphs_.clear();
 }
 
 double Model::bench_decode(Seq* const* seqs, int N, int steps)
@@ -763,18 +824,18 @@ double Model::bench_decode(Seq* const* seqs, int N, int steps)
     int32_t* pos_all_d = dalloc<int32_t>((int64_t)steps * N);
     WL_CUDA(cudaMemcpy(pos_all_d, pos_all.data(), pos_all.size() * 4, cudaMemcpyHostToDevice));
     upload_step(N, rows.data(), pos_all.data(), toks.data());
-    int32_t* pos_saved = pos_d_;
+    // a graph is captured (or found) before the timed loop so capture costs are not timed
+    const bool graphs = graph_ready(N, 0);
     cudaEvent_t e0, e1;
     WL_CUDA(cudaEventCreate(&e0));
     WL_CUDA(cudaEventCreate(&e1));
     WL_CUDA(cudaEventRecord(e0, stream_));
     for (int s = 0; s < steps; ++s) {
-        pos_d_ = pos_all_d + (size_t)s * N;
-        step_device(N, 0, max_len + s + 1);
+        WL_CUDA(cudaMemcpyAsync(pos_d_, pos_all_d + (size_t)s * N, sizeof(int32_t) * N, cudaMemcpyDeviceToDevice, stream_));
+        if (!graphs || !graph_step(N, 0)) step_device(N, 0, max_len + s + 1);
     }
     WL_CUDA(cudaEventRecord(e1, stream_));
     WL_CUDA(cudaEventSynchronize(e1));
-    pos_d_ = pos_saved;
     float ms = 0.f;
     WL_CUDA(cudaEventElapsedTime(&ms, e0, e1));
     cudaEventDestroy(e0);

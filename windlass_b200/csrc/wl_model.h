@@ -86,6 +86,7 @@ public:
     const Config& config() const { return c_; }
     int max_context() const { return max_context_; }
     const Stats& stats() const { return stats_; }
+    int64_t graph_launches() const { return graph_launches_; }
     int64_t weight_bytes() const { return weight_bytes_; }
     int64_t device_bytes() const;
     int device() const { return device_; }
@@ -105,6 +106,15 @@ private:
         int type;
         double bytes;
     };
+    struct GraphEntry {
+        int T, first, gen;
+        cudaGraphExec_t exec;
+        int64_t nodes;
+    };
+    bool graphable(int T) const;
+    bool graph_ready(int T, int first);
+    bool graph_step(int T, int first);
+    void drop_graphs();
     void flush_profile();
     void build_maps();
     void check_device_error();
@@ -168,6 +178,11 @@ private:
     int* err_d_ = nullptr;              // device error word of the bounded waits
     const float* prep_x_ = nullptr;
     int prep_cols_ = 0, prep_nc_ = 0;
+    // CUDA graphs of decode steps
+    bool use_graphs_ = true;
+    std::vector<GraphEntry> graphs_;
+    int ws_gen_ = 0;                    // bumped whenever a workspace the graphs point into is reallocated
+    int64_t graph_launches_ = 0;        // kernels launched by graph replays
     // profiling
     bool profiling_ = false;
     std::vector<ProfileMark> marks_;
