@@ -165,6 +165,17 @@ int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_o
  * W[r] . x[t] for t < ncols (1..8), fused dequant-dot, fp32 accumulate. Every column is computed as if alone. */
 int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t ncols,
                   float* dev_y, void* stream);
+/* No counterpart in the reference. wl_matvec's tensor-core path (Q4_K only: 16-byte aligned weights and dev_x, cols
+ * a multiple of 256) with the same arguments and results, for callers that cannot let a call allocate device memory:
+ * its scratch is a static device array of this library (WL_MATVEC_STATIC_MAX_COLS columns of 8 activations, about
+ * 1.1 MB per device), so the call makes no cudaMalloc/cudaFree. cols above the limit or other formats return
+ * WL_EINVAL / WL_EUNSUPPORTED (use wl_matvec). The first call on each device looks up the array's address with
+ * cudaGetSymbolAddress and sets the kernel's shared-memory attribute: make it before any stream capture. Nothing has
+ * to start at zero (each call clears its error word on `stream`). Calls share one scratch per device, so calls that
+ * may overlap (different streams, or threads without ordering) race: order them on one stream. */
+#define WL_MATVEC_STATIC_MAX_COLS 32768
+int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x,
+                         int32_t ncols, float* dev_y, void* stream);
 /* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 1 = fp32 CUDA cores, 2 = bf16 tensor
  * cores (tcgen05, fp32 accumulate), 0 = the model's default for T. */
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,

@@ -109,6 +109,7 @@ def lib():
         "wl_forward_batch": (I32, [P, P, P, I32, P, P, PROGRESS, P]),
         "wl_dequant": (I32, [I32, P, I64, P, P]),
         "wl_matvec": (I32, [I32, P, I32, I32, P, I32, P, P]),
+        "wl_matvec_static": (I32, [I32, P, I32, I32, P, I32, P, P]),
         "wl_matmul": (I32, [I32, P, I32, I32, P, I32, P, I32, P]),
         "wl_synth_tensor": (I32, [I32, U64, C.c_uint32, I64, I64, F, F, P, P]),
         "wl_bench_decode": (I32, [P, P, I32, I32, C.POINTER(C.c_double)]),

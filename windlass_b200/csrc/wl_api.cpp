@@ -312,6 +312,43 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
     });
 }
 
+// wl_matvec's tensor-core path with its scratch in a static device array instead of the growing export scratch:
+// nothing is allocated here, so callers that own all device memory can use it. Same kernels, same results.
+int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x,
+                         int32_t ncols, float* dev_y, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        int b = 0, s = 0;
+        if (!wl::can_decode(type) || !wl::layout(type, &b, &s))
+            return wl::fail(WL_EUNSUPPORTED, "wl_matvec_static: unsupported type");
+        if (rows <= 0 || cols <= 0 || ncols <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matvec_static: null pointer");
+        if (cols > wl::k::STATIC_MAX_COLS)
+            return wl::fail(WL_EINVAL, "wl_matvec_static: cols " + std::to_string(cols) + " exceeds the static scratch limit of " +
+                                       std::to_string(wl::k::STATIC_MAX_COLS) + "; use wl_matvec");
+        const int64_t rb = wl::row_bytes_of(type, cols);
+        if (!wl::k::mma_supported(type, (const uint8_t*)dev_w, rb, cols))
+            return wl::fail(WL_EUNSUPPORTED, "wl_matvec_static: only Q4_K weights with 16-byte aligned rows and cols a "
+                                             "multiple of 256 have the tensor-core matvec; use wl_matvec");
+        if ((uintptr_t)dev_x % 16 != 0) return wl::fail(WL_EINVAL, "wl_matvec_static: dev_x must be 16-byte aligned");
+        const size_t need = 256 + wl::k::xprep_bytes(cols, 8);
+        if (need > wl::k::STATIC_SCRATCH_BYTES) return wl::fail(WL_EINVAL, "wl_matvec_static: static scratch too small");
+        const cudaStream_t st = (cudaStream_t)stream;
+        uint8_t* scratch = (uint8_t*)wl::k::static_scratch();
+        int* err = (int*)scratch;
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));
+        wl::k::WeightMap map;
+        wl::k::make_weight_map(type, (const uint8_t*)dev_w, rows, rb, &map);
+        for (int c0 = 0; c0 < ncols; c0 += 8) {
+            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
+            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
+            wl::k::xprep(dev_x + (int64_t)c0 * cols, cols, cols, nc, p, st);
+            wl::k::matvec_mma(type, map, 0, rows, cols, p, dev_y + (int64_t)c0 * rows, rows, err, st);
+        }
+        return WL_OK;
+    });
+}
+
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                   float* dev_y, int32_t path, void* stream)
 {

@@ -44,6 +44,11 @@ struct XPrep {
 };
 size_t xprep_bytes(int cols, int nc);
 XPrep xprep_view(void* scratch, int cols, int nc);
+// The static scratch of wl_matvec_static: a 256-byte error word slot, then xprep_bytes(STATIC_MAX_COLS, 8).
+constexpr int STATIC_MAX_COLS = 32768;
+constexpr size_t STATIC_SCRATCH_BYTES = 256 + 8 * ((size_t)STATIC_MAX_COLS * 4 + (size_t)(STATIC_MAX_COLS / 256) * 48) + 256;
+// Device address of this device's static scratch (looked up once per device with cudaGetSymbolAddress).
+void* static_scratch();
 // x[t*ldx + i] for t < nc (1..8), cols a multiple of 256.
 void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s);
 // A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
