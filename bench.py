@@ -270,6 +270,7 @@ def main():
     trace(f"prefill {prefill_s:.1f} s; warmup {warm} steps")
     m.bench_decode(seqs, warm)
     launches0 = m.stats().kernel_launches
+    trace(f"kernel launches before the timed region: {launches0}")
     barrier()
     with ClockSampler(local) as clk:
         ms = m.bench_decode(seqs, steps)

@@ -168,7 +168,7 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
 /* No counterpart in the reference. wl_matvec's tensor-core path (Q4_K only: 16-byte aligned weights and dev_x, cols
  * a multiple of 256) with the same arguments and results, for callers that cannot let a call allocate device memory:
  * its scratch is a static device array of this library (WL_MATVEC_STATIC_MAX_COLS columns of 8 activations, about
- * 1.1 MB per device), so the call makes no cudaMalloc/cudaFree. cols above the limit or other formats return
+ * 1 MB per device), so the call makes no cudaMalloc/cudaFree. cols above the limit or other formats return
  * WL_EINVAL / WL_EUNSUPPORTED (use wl_matvec). The first call on each device looks up the array's address with
  * cudaGetSymbolAddress and sets the kernel's shared-memory attribute: make it before any stream capture. Nothing has
  * to start at zero (each call clears its error word on `stream`). Calls share one scratch per device, so calls that

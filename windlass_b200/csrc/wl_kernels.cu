@@ -61,6 +61,7 @@ static inline void launched()
 int64_t launches() { return g_launches.load(std::memory_order_relaxed); }
 
 void note_launch() { launched(); }
+void uncount_launches(int64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
 
 // ------------------------------------------------------------------------------------------------------------------
 // dequant / embedding (bit-exact)

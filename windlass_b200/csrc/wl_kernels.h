@@ -21,6 +21,8 @@ void init_tables();
 // Kernels launched by this process so far; note_launch() checks and counts a launch made in another file.
 int64_t launches();
 void note_launch();
+// Takes back n counted launches that were captured into a graph rather than run.
+void uncount_launches(int64_t n);
 
 // Quants.DecodeRow for n consecutive values (n a multiple of the block size), bit-exact.
 void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s);
@@ -34,19 +36,20 @@ void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, co
 void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
             int ncols, float* y, int64_t ldy, cudaStream_t s);
 
-// Activations prepared for the tensor-core matvec: per column and 256-value superblock, f16 hi/lo pairs of every
-// 4 values (order v0 v2 v1 v3) under a power-of-two scale, and a 48-byte record of the hi/lo sums of every 32
-// values plus the inverse scale.
+// Activations prepared for the tensor-core matvec: per column and 256-value superblock one XP_COL-byte block of three
+// signed 8-bit digit planes (pitch XP_DIGIT) of the values under a power-of-two unit, and at XP_REC the f16 hi/lo
+// sums of every 32 values and the unit.
+constexpr int XP_DIGIT = 288, XP_REC = 864, XP_COL = 992;
+constexpr size_t xprep_bytes_c(int cols, int nc) { return (size_t)nc * (size_t)(cols / 256) * XP_COL + 256; }
 struct XPrep {
-    uint4* groups;      // [nc][cols/4]
-    uint4* sums;        // [nc][cols/256][3]
+    uint8_t* blocks;    // [nc][cols/256][XP_COL]
     int cols = 0, nc = 0;
 };
 size_t xprep_bytes(int cols, int nc);
 XPrep xprep_view(void* scratch, int cols, int nc);
 // The static scratch of wl_matvec_static: a 256-byte error word slot, then xprep_bytes(STATIC_MAX_COLS, 8).
 constexpr int STATIC_MAX_COLS = 32768;
-constexpr size_t STATIC_SCRATCH_BYTES = 256 + 8 * ((size_t)STATIC_MAX_COLS * 4 + (size_t)(STATIC_MAX_COLS / 256) * 48) + 256;
+constexpr size_t STATIC_SCRATCH_BYTES = 256 + xprep_bytes_c(STATIC_MAX_COLS, 8);
 // Device address of this device's static scratch (looked up once per device with cudaGetSymbolAddress).
 void* static_scratch();
 // x[t*ldx + i] for t < nc (1..8), cols a multiple of 256.

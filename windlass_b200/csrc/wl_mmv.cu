@@ -1,19 +1,18 @@
-// Tensor-core decode matvec for Q4_K (sm_100a): TMA-staged weights, mma.sync m16n8k16 with f16 operands and fp32
-// accumulation, for 1..8 activation columns.
+// Tensor-core decode matvec for Q4_K (sm_100a): TMA-staged weights, integer mma.sync (u8 codes x s8 activation
+// digits, int32 accumulate) for 1..8 activation columns.
 //
-// Weights. Each warp owns 32 rows and every eighth superblock of them; its lane 0 streams the [32 rows x 144 B]
-// superblock tiles into a two-stage shared-memory ring with 2-D TMA copies (cp.async.bulk.tensor, no multicast),
-// together with the activation chunks of the same superblock (1-D bulk copies), on one mbarrier per stage. The
-// lanes then read their fragments from shared memory and turn the 4-bit codes into exact f16 A fragments: q*s, the
-// code times its 6-bit sub-block scale (at most 945), made with one LOP3 and one HFMA2 per two values from the
-// 0x6400|q bit pattern (high nibbles stay in place and use s/16).
+// Weights. A CTA owns 16 rows; warp w streams superblocks w, w+8, ... of them ([16 rows x 144 B] tiles, 2-D TMA copies
+// with no multicast) into its own shared-memory ring, together with the prepared activations of the same superblock
+// (1-D bulk copies), on one mbarrier per stage. A lane's fragment of a 32-value sub-block is two words of code bytes
+// masked to the low nibbles (codes q) or the high nibbles (16q, in place).
 //
-// Activations. k_xprep writes, per column, an exact power-of-two scale and f16 hi/lo pairs of every value
-// (x*2^k = hi + lo to 2^-22 relative), grouped so that one 16-byte shared-memory read gives a lane both B fragments
-// of a k-step, plus the hi/lo sums of every 32 values for the Q4_K min term, which is one more MMA per superblock.
+// Activations. k_xprep writes each superblock of each column as three planes of balanced base-128 digits of
+// round(x * 2^(20-e)) (21 bits below the superblock's largest magnitude), so the integer MMAs are exact, plus the
+// hi/lo f16 sums of every 32 values for the Q4_K min term, which is one f16 MMA per superblock.
 //
-// Determinism. The eight warps of a CTA cover disjoint superblocks of the same 32 rows and are summed in warp order,
-// so a column's result never depends on the other columns of the launch.
+// Determinism. The eight warps of a CTA cover disjoint superblocks of the same rows and are summed in warp order,
+// and every column goes through the same fp32 operations whatever the number of columns beside it, so a column's
+// result never depends on the other columns of the launch.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -87,50 +86,19 @@ __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier
 
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
-__device__ __forceinline__ float block_max(float v, float* scratch)
-{
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    __syncthreads();
-    if (lane == 0) scratch[warp] = v;
-    __syncthreads();
-    float m = scratch[0];
-    for (int i = 1; i < nw; ++i) m = fmaxf(m, scratch[i]);
-    return m;
-}
-
-// ScaleMinK4 (src/Quants.cs:322-330) on the 12 scale bytes held as three words (bytes 4..15 of the superblock).
-__device__ __forceinline__ void scale_min_k4_words(int j, uint32_t y, uint32_t z, uint32_t w, int& s, int& m)
-{
-    const int sh = 8 * (j & 3);
-    const int by = (y >> sh) & 0xFF, bz = (z >> sh) & 0xFF, bw = (w >> sh) & 0xFF;
-    if (j < 4) { s = by & 63; m = bz & 63; }
-    else { s = (bw & 0xF) | ((by >> 6) << 4); m = (bw >> 4) | ((bz >> 6) << 4); }
-}
-
-// Two 4-bit codes at bits [b, b+4) and [b+16, b+20) of w (b = 0 or 4) as f16x2 q*s, exact:
-// (1024 + q*2^b)*(s/2^b) - 1024*(s/2^b).
-__device__ __forceinline__ uint32_t q4_pair(uint32_t w, uint32_t mask, __half2 s2, __half2 ns2)
-{
-    return h2_bits(__hfma2(bits_h2((w & mask) | 0x64006400u), s2, ns2));
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------------------------
 // activation prep
 // ------------------------------------------------------------------------------------------------------------------
-// Chunk (16 bytes) of the 4 values 4v..4v+3 of a column: superblock sb = v/64, and inside it the lane group
-// c = (v%64)/16, nibble half h = (v%16)/8, word i = v%8; stored at sb*64 + (h*8 + i)*4 + c so that, for a given
-// (h, i), the four lanes of a row group read 64 contiguous bytes.
-// One CTA of 64 threads per (superblock, column): each thread owns 4 values. The 256 values of the superblock are
-// scaled by a power of two so their largest magnitude lies in [2^9, 2^10) (exact; the matvec multiplies the
-// superblock's partial sums by the inverse), which keeps hi and the 32-value sums in f16 range and lo mostly clear of
-// subnormals. Per (column, superblock) the sums record is 48 bytes: 4 x (hi pair, lo pair) of the eight 32-value sums,
-// then the inverse scale.
-__global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64_t ldx, int nsb,
-                                              uint4* __restrict__ groups, uint4* __restrict__ sums)
+// Per (column, superblock) one XP_COL-byte block: three planes of signed 8-bit digits of the 256 values in natural
+// order (pitch XP_DIGIT; the 32 pad bytes keep the B-fragment reads of different planes on different banks), then a
+// record at XP_REC: four (hi pair, lo pair) f16x2 words holding the sums of the eight 32-value sub-blocks, then the
+// float unit of the digits. X = round(x * 2^(20-e)) (|X| <= 2^20, e the exponent of the superblock's largest
+// magnitude) is split into balanced base-128 digits X = X0*2^14 + X1*2^7 + X2, each in [-64, 64]. The sums are taken
+// at 2^(10-e), where they fit f16 with a hi/lo split good to 2^-22.
+// One CTA of 64 threads per (superblock, column); each thread owns 4 consecutive values.
+__global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64_t ldx, int nsb, uint8_t* __restrict__ out)
 {
     __shared__ float scratch[2];
     const int sb = blockIdx.x, n = blockIdx.y, t = threadIdx.x;
@@ -141,71 +109,93 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
     if ((t & 31) == 0) scratch[t >> 5] = m;
     __syncthreads();
     m = fmaxf(scratch[0], scratch[1]);
+    const bool finite = m <= 3.4e38f;          // false for inf and NaN
     int e = 0;
-    if (m > 0.f) frexpf(m, &e);
+    if (m > 0.f && finite) frexpf(m, &e);
     e = e < -100 ? -100 : e > 100 ? 100 : e;
-    const float scale = m > 0.f ? ldexpf(1.0f, 10 - e) : 1.0f;
-    uint4* gc = groups + ((int64_t)n * nsb + sb) * 64;
-    uint2* sc = reinterpret_cast<uint2*>(sums + ((int64_t)n * nsb + sb) * 3);
-    {
-        const int v = t;
-        const float f[4] = {v4.x * scale, v4.y * scale, v4.z * scale, v4.w * scale};
-        __half hi[4], lo[4];
+    const float up = ldexpf(1.0f, 20 - e);     // digit scale: |x| * up <= 2^20
+    const float sup = ldexpf(1.0f, 10 - e);    // sum scale: |x| * sup < 2^10
+    uint8_t* blk = out + ((int64_t)n * nsb + sb) * XP_COL;
+    const float f[4] = {v4.x, v4.y, v4.z, v4.w};
+    uint32_t dg0 = 0, dg1 = 0, dg2 = 0;
 #pragma unroll
-        for (int k2 = 0; k2 < 4; ++k2) {
-            hi[k2] = __float2half_rn(f[k2]);
-            lo[k2] = __float2half_rn(f[k2] - __half2float(hi[k2]));
-        }
-        const int c = (v >> 4) & 3, h = (v >> 3) & 1, i = v & 7;
-        gc[(h * 8 + i) * 4 + c] =
-            make_uint4(h2_bits(__halves2half2(hi[0], hi[2])), h2_bits(__halves2half2(hi[1], hi[3])),
-                       h2_bits(__halves2half2(lo[0], lo[2])), h2_bits(__halves2half2(lo[1], lo[3])));
-        // sum of the 32 values of this group's sub-block: 8 consecutive groups in 8 consecutive lanes
-        float s = (f[0] + f[1]) + (f[2] + f[3]);
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        const float s_next = __shfl_down_sync(0xffffffffu, s, 8);
-        if ((v & 15) == 0) {
-            const __half h0 = __float2half_rn(s), h1 = __float2half_rn(s_next);
-            const __half l0 = __float2half_rn(s - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
-            sc[v >> 4] = make_uint2(h2_bits(__halves2half2(h0, h1)), h2_bits(__halves2half2(l0, l1)));
-        }
+    for (int k2 = 0; k2 < 4; ++k2) {
+        const int X = finite ? __float2int_rn(f[k2] * up) : 0;
+        const int x2 = ((X + 64) & 127) - 64;
+        const int r = (X - x2) >> 7;
+        const int x1 = ((r + 64) & 127) - 64;
+        const int x0 = (r - x1) >> 7;
+        dg0 |= (uint32_t)(x0 & 0xFF) << (8 * k2);
+        dg1 |= (uint32_t)(x1 & 0xFF) << (8 * k2);
+        dg2 |= (uint32_t)(x2 & 0xFF) << (8 * k2);
     }
-    if (t == 0) {
-        float* tail = reinterpret_cast<float*>(sc + 4);
-        tail[0] = 1.0f / scale;
-        tail[1] = tail[2] = tail[3] = 0.f;
+    *reinterpret_cast<uint32_t*>(blk + 0 * XP_DIGIT + 4 * t) = dg0;
+    *reinterpret_cast<uint32_t*>(blk + 1 * XP_DIGIT + 4 * t) = dg1;
+    *reinterpret_cast<uint32_t*>(blk + 2 * XP_DIGIT + 4 * t) = dg2;
+    if (t < 8) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * t) = 0u;
     }
+    // sum of the 32 values of this thread's sub-block: 8 consecutive threads
+    float s = (f[0] * sup + f[1] * sup) + (f[2] * sup + f[3] * sup);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    const float s_next = __shfl_down_sync(0xffffffffu, s, 8);
+    uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
+    if ((t & 15) == 0) {
+        const __half h0 = __float2half_rn(s), h1 = __float2half_rn(s_next);
+        const __half l0 = __float2half_rn(s - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
+        rec[2 * (t >> 4)] = h2_bits(__halves2half2(h0, h1));
+        rec[2 * (t >> 4) + 1] = h2_bits(__halves2half2(l0, l1));
+    }
+    // digit unit (non-finite input makes it NaN, so the products are NaN as the fp32 dot would be), then zero padding
+    if (t == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
+    if (t >= 9 && t < 9 + (XP_COL - XP_REC) / 4 - 9) rec[t] = 0u;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
 // Q4_K matvec
 // ------------------------------------------------------------------------------------------------------------------
-constexpr int Q4_ROWS = 16;                     // rows per CTA: one m16 row group per warp
-constexpr int Q4_G = Q4_ROWS / 16, Q4_R = 2 * Q4_G;   // row groups per warp, rows per thread
-// Stages of the per-warp copy ring: two, so three CTAs (24 warps) fit an SM at one activation column.
+constexpr int Q4_ROWS = 16;                     // rows per CTA: one m16 row group, shared by the eight warps
 constexpr int Q4_TILE = Q4_ROWS * 144;          // weight bytes per stage
-constexpr int Q4_XCOL = 1024 + 64;              // activation bytes per column per stage (+64: no bank conflicts)
 
 template <int NC> struct Q4Layout {
-    static constexpr int X_OFF = Q4_TILE;
-    static constexpr int S_OFF = Q4_TILE + NC * Q4_XCOL;
-    static constexpr int STAGE = (S_OFF + NC * 48 + 127) / 128 * 128;   // TMA destinations are 128-byte aligned
-    static constexpr int TX = Q4_TILE + NC * 1024 + NC * 48;      // bytes the copies of one stage deliver
+    static constexpr int X_OFF = Q4_TILE;       // 2304, a multiple of 128
+    static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;   // TMA destinations are 128-byte aligned
+    static constexpr int TX = Q4_TILE + NC * XP_COL;                         // bytes the copies of one stage deliver
     static constexpr int STAGES = 2;
     static constexpr int SMEM = 8 * STAGES * STAGE;
 };
 
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%10,%10,%10,%10};\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
+
+// One CTA per 16 rows; warp w takes superblocks w, w+8, ... of those rows. Per superblock and 32-value sub-block
+// one integer MMA (u8 codes x s8 activation digits, exact int32) gives sum(q*X); the 6-bit sub-block scales are
+// applied in integers; the superblock's d and the digit unit are applied in fp32 per digit plane; the min term
+// dmin * sum_j m_j * sum(x_j) is one f16 MMA over the hi/lo sub-block sums.
+// Up to two columns, the 8 MMA columns hold (column, digit) pairs (one MMA per sub-block); from three columns on,
+// one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
+// result does not depend on how many columns share the launch.
 template <int NC>
 __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap, int row_base, int rows,
-                                                    int nsb, const uint4* __restrict__ xg,
-                                                    const uint4* __restrict__ xs, float* __restrict__ y, int64_t ldy,
-                                                    int* err)
+                                                    int nsb, const uint8_t* __restrict__ xq, float* __restrict__ y,
+                                                    int64_t ldy, int* err)
 {
     using LY = Q4Layout<NC>;
+    constexpr bool PACK = NC <= 2;
+    constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[8][3];
+    __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
     __shared__ float red[8][Q4_ROWS][9];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int r0 = blockIdx.x * Q4_ROWS;
@@ -224,89 +214,100 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
         mbar_expect_tx(&bars[warp][s], LY::TX);
         tma_load_2d(st, &wmap, sb * 144, row_base + r0, &bars[warp][s]);
 #pragma unroll
-        for (int n = 0; n < NC; ++n) {
-            bulk_load(st + LY::X_OFF + n * Q4_XCOL, xg + ((int64_t)n * nsb + sb) * 64, 1024, &bars[warp][s]);
-            bulk_load(st + LY::S_OFF + n * 48, xs + ((int64_t)n * nsb + sb) * 3, 48, &bars[warp][s]);
-        }
+        for (int n = 0; n < NC; ++n)
+            bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
     };
     if (lane == 0)
         for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue(j, j);
 
-    float dt[Q4_G][4] = {};
-    const bool has_col = g < NC;
+    // B operand of this lane: MMA column g is (column g/3, digit g%3) when packed, else column g
+    const bool b_ok = PACK ? g < 3 * NC : g < NC;
+    const int b_off = LY::X_OFF + (PACK ? (g / 3) * XP_COL + (g % 3) * XP_DIGIT : g * XP_COL);
+    // D columns 2c, 2c+1 of this lane: (column, digit) pairs when packed, else columns
+    int e_col[2], e_dig[2];
+    bool e_ok[2];
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+        const int nn = 2 * c + k2;
+        e_col[k2] = PACK ? nn / 3 : nn;
+        e_dig[k2] = PACK ? nn % 3 : 0;
+        e_ok[k2] = PACK ? nn < 3 * NC : nn < NC;
+    }
+    const bool m_ok0 = 2 * c < NC, m_ok1 = 2 * c + 1 < NC;   // columns of the min-term MMA's D fragment
+    // the mins of sub-blocks 2c, 2c+1 as f16 1024+m: bytes (2c)&3, (2c+1)&3 of the mins word, 0x64 above each
+    const uint32_t msel = (uint32_t)((2 * c) & 3) | (4u << 4) | ((uint32_t)((2 * c + 1) & 3) << 8) | (4u << 12);
+    const __half2 k1024 = __float2half2_rn(1024.f);
+
+    float facc[ND][4] = {};     // per digit plane: d * unit * sum_j s_j sum(q X)
+    float macc[4] = {};         // dmin * unit * sum_j m_j sum(x)
     for (int j = 0; j < njobs; ++j) {
         const int s = j % LY::STAGES;
         const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
         const uint8_t* st = ring + s * LY::STAGE;
         if (ok) {
-            uint4 hdr[Q4_R], qa[Q4_R], qb[Q4_R];
+            const uint8_t* row0 = st + g * 144;
+            const uint8_t* row1 = st + (g + 8) * 144;
+            const uint4 h0 = lds128(row0), h1 = lds128(row1);
+            // ScaleMinK4 for all eight sub-blocks at once: scales and mins as bytes
+            const uint32_t s0lo = h0.y & 0x3F3F3F3Fu, s0hi = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+            const uint32_t s1lo = h1.y & 0x3F3F3F3Fu, s1hi = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+            int acc_lo[ND][4] = {}, acc_hi[ND][4] = {};
 #pragma unroll
-            for (int i = 0; i < Q4_R; ++i) {
-                const uint8_t* row = st + (g + 8 * i) * 144;
-                hdr[i] = lds128(row);
-                qa[i] = lds128(row + 16 + 32 * c);
-                qb[i] = lds128(row + 32 + 32 * c);
-            }
-            __half2 slo[Q4_R], nslo[Q4_R], shi[Q4_R], nshi[Q4_R];
-            uint32_t mp[Q4_R];
-            float dd[Q4_R], dm[Q4_R];
+            for (int r = 0; r < 4; ++r) {
+                const uint2 w0 = lds64(row0 + 16 + 32 * r + 8 * c);
+                const uint2 w1 = lds64(row1 + 16 + 32 * r + 8 * c);
+                const uint32_t sw0 = r < 2 ? s0lo : s0hi, sw1 = r < 2 ? s1lo : s1hi;
+                const int kb = (2 * r) & 3;
+                const int sl0 = (int)((sw0 >> (8 * kb)) & 0xFFu), sh0 = (int)((sw0 >> (8 * kb + 8)) & 0xFFu);
+                const int sl1 = (int)((sw1 >> (8 * kb)) & 0xFFu), sh1 = (int)((sw1 >> (8 * kb + 8)) & 0xFFu);
 #pragma unroll
-            for (int i = 0; i < Q4_R; ++i) {
-                int s1, m1, s2, m2;
-                scale_min_k4_words(2 * c, hdr[i].y, hdr[i].z, hdr[i].w, s1, m1);
-                scale_min_k4_words(2 * c + 1, hdr[i].y, hdr[i].z, hdr[i].w, s2, m2);
-                slo[i] = __float2half2_rn((float)s1);
-                nslo[i] = __float2half2_rn(-1024.f * (float)s1);
-                shi[i] = __float2half2_rn((float)s2 * 0.0625f);        // high nibble in place: value 16q
-                nshi[i] = __float2half2_rn(-64.f * (float)s2);
-                mp[i] = h2_bits(__floats2half2_rn((float)m1, (float)m2));
-                dd[i] = h2f_((uint16_t)(hdr[i].x & 0xFFFF));
-                dm[i] = h2f_((uint16_t)(hdr[i].x >> 16));
-            }
-            // independent accumulators per (row group, nibble half, hi/lo) keep eight MMA chains in flight
-            float dq[Q4_G][2][2][4] = {};
-            float dn[Q4_G][4] = {};
-            const uint8_t* xst = st + LY::X_OFF + (has_col ? g : 0) * Q4_XCOL;
+                for (int hh = 0; hh < 2; ++hh) {
+                    const uint32_t mask = hh ? 0xF0F0F0F0u : 0x0F0F0F0Fu;   // high nibbles stay in place: 16q
+                    const uint32_t a0 = w0.x & mask, a1 = w1.x & mask, a2 = w0.y & mask, a3 = w1.y & mask;
+                    const int sa = hh ? sh0 : sl0, sb2 = hh ? sh1 : sl1;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t wa[Q4_R], ws[Q4_R];
-#pragma unroll
-                for (int r = 0; r < Q4_R; ++r) {
-                    wa[r] = i < 4 ? (&qa[r].x)[i] : (&qb[r].x)[i - 4];
-                    ws[r] = wa[r] >> 8;
-                }
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint4 b = has_col ? lds128(xst + ((h * 8 + i) * 4 + c) * 16) : make_uint4(0u, 0u, 0u, 0u);
-                    const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
-#pragma unroll
-                    for (int G = 0; G < Q4_G; ++G) {
-                        const int ra = 2 * G, rb = 2 * G + 1;
-                        const __half2 sa = h ? shi[ra] : slo[ra], nsa = h ? nshi[ra] : nslo[ra];
-                        const __half2 sv = h ? shi[rb] : slo[rb], nsv = h ? nshi[rb] : nslo[rb];
-                        const uint32_t a0 = q4_pair(wa[ra], mask, sa, nsa);   // row g: values v0, v2
-                        const uint32_t a2 = q4_pair(ws[ra], mask, sa, nsa);   // row g: values v1, v3
-                        const uint32_t a1 = q4_pair(wa[rb], mask, sv, nsv);   // row g+8
-                        const uint32_t a3 = q4_pair(ws[rb], mask, sv, nsv);
-                        mma16816(dq[G][h][0], a0, a1, a2, a3, b.x, b.y);
-                        mma16816(dq[G][h][1], a0, a1, a2, a3, b.z, b.w);
+                    for (int d = 0; d < ND; ++d) {
+                        const uint2 b = b_ok ? lds64(st + b_off + d * XP_DIGIT + 32 * (2 * r + hh) + 8 * c)
+                                             : make_uint2(0u, 0u);
+                        int D[4];
+                        imma16832(D, a0, a1, a2, a3, b.x, b.y);
+                        int (&acc)[4] = hh ? acc_hi[d] : acc_lo[d];
+                        acc[0] += sa * D[0];
+                        acc[1] += sa * D[1];
+                        acc[2] += sb2 * D[2];
+                        acc[3] += sb2 * D[3];
                     }
                 }
             }
-            const uint2 bs = has_col ? *reinterpret_cast<const uint2*>(st + LY::S_OFF + g * 48 + c * 8) : make_uint2(0u, 0u);
-            // inverse scales of this superblock for the output columns 2c and 2c+1 of the D fragment
-            const float is0 = 2 * c < NC ? *reinterpret_cast<const float*>(st + LY::S_OFF + (2 * c) * 48 + 32) : 0.f;
-            const float is1 = 2 * c + 1 < NC ? *reinterpret_cast<const float*>(st + LY::S_OFF + (2 * c + 1) * 48 + 32) : 0.f;
+            const float dd0 = h2f_((uint16_t)(h0.x & 0xFFFF)), dm0 = h2f_((uint16_t)(h0.x >> 16));
+            const float dd1 = h2f_((uint16_t)(h1.x & 0xFFFF)), dm1 = h2f_((uint16_t)(h1.x >> 16));
+            // digit planes: 16 * sum_j s_j sum(q X) = 16 acc_lo + acc_hi (exact); unit * 2^(14 - 7 digit) / 16
 #pragma unroll
-            for (int G = 0; G < Q4_G; ++G) {
-                mma16816(dn[G], mp[2 * G], mp[2 * G + 1], mp[2 * G], mp[2 * G + 1], bs.x, bs.y);
+            for (int k2 = 0; k2 < 2; ++k2) {
+                const float unit = e_ok[k2] ? *reinterpret_cast<const float*>(st + LY::X_OFF + e_col[k2] * XP_COL + XP_REC + 32) : 0.f;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int rs = 2 * G + (e >> 1);
-                    const float q = (dq[G][0][0][e] + dq[G][0][1][e]) + (dq[G][1][0][e] + dq[G][1][1][e]);
-                    dt[G][e] += (dd[rs] * q - dm[rs] * dn[G][e]) * ((e & 1) ? is1 : is0);
+                for (int d = 0; d < ND; ++d) {
+                    const int dig = PACK ? e_dig[k2] : d;
+                    const float f = unit * (dig == 0 ? 1024.f : dig == 1 ? 8.f : 0.0625f);
+                    facc[d][k2] = fmaf((float)(acc_lo[d][k2] * 16 + acc_hi[d][k2]), dd0 * f, facc[d][k2]);
+                    facc[d][k2 + 2] = fmaf((float)(acc_lo[d][k2 + 2] * 16 + acc_hi[d][k2 + 2]), dd1 * f, facc[d][k2 + 2]);
                 }
             }
+            // min term: A = the mins of sub-blocks 2c, 2c+1 (k slots 2c, 2c+1 and again 2c+8, 2c+9), B = hi sums in
+            // slots 0..7 and lo sums in 8..15 of the lane's column
+            const uint32_t m0lo = h0.z & 0x3F3F3F3Fu, m0hi = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+            const uint32_t m1lo = h1.z & 0x3F3F3F3Fu, m1hi = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+            const uint32_t mp0 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m0lo : m0hi, 0x64646464u, msel)), k1024));
+            const uint32_t mp1 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m1lo : m1hi, 0x64646464u, msel)), k1024));
+            const uint2 bs = g < NC ? lds64(st + LY::X_OFF + g * XP_COL + XP_REC + 8 * c) : make_uint2(0u, 0u);
+            float dn[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(dn, mp0, mp1, mp0, mp1, bs.x, bs.y);
+            const float mu0 = m_ok0 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c) * XP_COL + XP_REC + 32) * 1024.f : 0.f;
+            const float mu1 = m_ok1 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c + 1) * XP_COL + XP_REC + 32) * 1024.f : 0.f;
+            macc[0] = fmaf(dn[0], dm0 * mu0, macc[0]);
+            macc[1] = fmaf(dn[1], dm0 * mu1, macc[1]);
+            macc[2] = fmaf(dn[2], dm1 * mu0, macc[2]);
+            macc[3] = fmaf(dn[3], dm1 * mu1, macc[3]);
         }
         __syncwarp();
         if (lane == 0 && j + LY::STAGES < njobs) {
@@ -314,16 +315,34 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
             issue(j + LY::STAGES, s);
         }
     }
+    // per (row, column): ((plane 0 + plane 1) + plane 2) - min term, then the warps in order
+    if (PACK) {
 #pragma unroll
-    for (int G = 0; G < Q4_G; ++G)
+        for (int e = 0; e < 4; ++e) {
+            const int row = g + 8 * (e >> 1), k2 = e & 1;
+            red[warp][row][2 * c + k2] = facc[0][e];
+        }
+        if (c == 0) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][16 * G + g + 8 * (e >> 1)][2 * c + (e & 1)] = dt[G][e];
+            for (int e = 0; e < 4; ++e) red[warp][g + 8 * (e >> 1)][6 + (e & 1)] = macc[e];
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
+            if (col < NC) red[warp][row][col] = ((facc[0][e] + facc[ND > 1 ? 1 : 0][e]) + facc[ND > 2 ? 2 : 0][e]) - macc[e];
+        }
+    }
     __syncthreads();
     const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
     if (col < NC && rl < Q4_ROWS && r0 + rl < rows) {
         float sum = 0.f;
 #pragma unroll
-        for (int wv = 0; wv < 8; ++wv) sum += red[wv][rl][col];
+        for (int wv = 0; wv < 8; ++wv) {
+            const float v = PACK ? ((red[wv][rl][3 * col] + red[wv][rl][3 * col + 1]) + red[wv][rl][3 * col + 2]) - red[wv][rl][6 + col]
+                                 : red[wv][rl][col];
+            sum += v;
+        }
         y[(int64_t)col * ldy + r0 + rl] = sum;
     }
 }
@@ -331,18 +350,12 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
 // ------------------------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------------------------
-size_t xprep_bytes(int cols, int nc)
-{
-    return (size_t)nc * ((size_t)cols * 4 + (size_t)(cols / 256) * 48) + 256;
-}
+size_t xprep_bytes(int cols, int nc) { return xprep_bytes_c(cols, nc); }
 
 XPrep xprep_view(void* scratch, int cols, int nc)
 {
     XPrep p;
-    uint8_t* b = (uint8_t*)scratch;
-    p.groups = (uint4*)b;
-    b += (size_t)nc * cols * 4;
-    p.sums = (uint4*)b;
+    p.blocks = (uint8_t*)scratch;
     p.cols = cols;
     p.nc = nc;
     return p;
@@ -350,7 +363,7 @@ XPrep xprep_view(void* scratch, int cols, int nc)
 
 void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s)
 {
-    k_xprep<<<dim3(cols / 256, nc), 64, 0, s>>>(x, ldx, cols / 256, p.groups, p.sums);
+    k_xprep<<<dim3(cols / 256, nc), 64, 0, s>>>(x, ldx, cols / 256, p.blocks);
     note_launch();
 }
 
@@ -402,8 +415,8 @@ static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, co
         attr[dev] = true;
     }
     const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(map.bytes);
-    k_mmv_q4k<NC><<<(rows + Q4_ROWS - 1) / Q4_ROWS, 256, Q4Layout<NC>::SMEM, s>>>(m, row_base, rows, nsb, p.groups,
-                                                                                  p.sums, y, ldy, err);
+    k_mmv_q4k<NC><<<(rows + Q4_ROWS - 1) / Q4_ROWS, 256, Q4Layout<NC>::SMEM, s>>>(m, row_base, rows, nsb, p.blocks,
+                                                                                  y, ldy, err);
     note_launch();
 }
 

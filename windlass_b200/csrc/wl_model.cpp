@@ -776,7 +776,9 @@ bool Model::graph_ready(int T, int first)
     const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     WL_CUDA(e);
-    graphs_.push_back(GraphEntry{T, first, ws_gen_, exec, k::launches() - l0});
+    const int64_t nodes = k::launches() - l0;
+    k::uncount_launches(nodes);      // captured, not run: replays count them
+    graphs_.push_back(GraphEntry{T, first, ws_gen_, exec, nodes});
     return true;
 }
 
