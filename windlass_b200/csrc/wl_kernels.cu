@@ -12,7 +12,9 @@
 #include <cuda_fp16.h>
 #include "wl_common.h"
 #include "wl_decode.cuh"
+#include <algorithm>
 #include "wl_kernels.h"
+#include "wl_launch.cuh"
 
 namespace wl {
 
@@ -68,6 +70,8 @@ void uncount_launches(int64_t n) { g_launches.fetch_sub(n, std::memory_order_rel
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void k_dequant(int type, const uint8_t* __restrict__ blocks, int64_t n, float* __restrict__ out)
 {
+    pdl_trigger();
+    pdl_wait();
     const int be = block_elems(type), bb = block_bytes(type);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = dq_elem(type, blocks + (i / be) * bb, (int)(i % be));
@@ -78,13 +82,15 @@ void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s
     if (n <= 0) return;
     int64_t g = grid_for(n, 256);
     if (g > 148 * 64) g = 148 * 64;
-    k_dequant<<<(unsigned)g, 256, 0, s>>>(type, (const uint8_t*)blocks, n, out);
+    launch(k_dequant, dim3((unsigned)g), dim3(256), 0, s, type, (const uint8_t*)blocks, n, out);
     launched();
 }
 
 __global__ void k_embed(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows, int cols,
                         const int32_t* __restrict__ tokens, float scale, float* __restrict__ x, int32_t* bad)
 {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const int be = block_elems(type), bb = block_bytes(type);
     const int tok = tokens[t];
@@ -103,7 +109,7 @@ void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, co
            float scale, float* x, int32_t* bad, cudaStream_t s)
 {
     dim3 grid(grid_for(cols, 256), T);
-    k_embed<<<grid, 256, 0, s>>>(type, w, row_bytes, rows, cols, tokens, scale, x, bad);
+    launch(k_embed, dim3(grid), dim3(256), 0, s, type, w, row_bytes, rows, cols, tokens, scale, x, bad);
     launched();
 }
 
@@ -361,6 +367,8 @@ __global__ void __launch_bounds__(128) k_matvec(int type, const uint8_t* __restr
                                                 int cols, const float* __restrict__ x, int64_t ldx,
                                                 float* __restrict__ y, int64_t ldy)
 {
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 4 + warp;
     if (row >= rows) return;
@@ -401,14 +409,14 @@ static void launch_mv(int nc, int type, const uint8_t* w, int64_t rb, int rows, 
 {
     const unsigned g = grid_for(rows, 4);
     switch (nc) {
-    case 1: k_matvec<KIND, 1><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 2: k_matvec<KIND, 2><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 3: k_matvec<KIND, 3><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 4: k_matvec<KIND, 4><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 5: k_matvec<KIND, 5><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 6: k_matvec<KIND, 6><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    case 7: k_matvec<KIND, 7><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
-    default: k_matvec<KIND, 8><<<g, 128, 0, s>>>(type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 1: launch(k_matvec<KIND, 1>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 2: launch(k_matvec<KIND, 2>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 3: launch(k_matvec<KIND, 3>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 4: launch(k_matvec<KIND, 4>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 5: launch(k_matvec<KIND, 5>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 6: launch(k_matvec<KIND, 6>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    case 7: launch(k_matvec<KIND, 7>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
+    default: launch(k_matvec<KIND, 8>, dim3(g), dim3(128), 0, s, type, w, rb, rows, cols, x, ldx, y, ldy); break;
     }
 }
 
@@ -469,6 +477,8 @@ __device__ __forceinline__ float block_max(float v, float* scratch)
 // RmsNormRows: sum of squares in double, scale = 1f / (float)sqrt((float)(sum/dim) + eps), y = (x*scale)*w.
 __global__ void k_rmsnorm(const float* x, int dim, const float* __restrict__ w, float eps, float* y)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double scratch[32];
     const float* xr = x + (int64_t)blockIdx.x * dim;
     float* yr = y + (int64_t)blockIdx.x * dim;
@@ -481,16 +491,51 @@ __global__ void k_rmsnorm(const float* x, int dim, const float* __restrict__ w, 
     for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
+// RmsNormRows for rows of at most 8192 values: every thread loads its (up to 8) values before the sum, so a row
+// costs one memory round trip instead of one per loop iteration. Same arithmetic as k_rmsnorm.
+__global__ void __launch_bounds__(1024) k_rmsnorm8(const float* x, int dim, const float* __restrict__ w, float eps,
+                                                   float* y)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ double scratch[32];
+    const float* xr = x + (int64_t)blockIdx.x * dim;
+    float* yr = y + (int64_t)blockIdx.x * dim;
+    float v[8];
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) {
+        const int i = threadIdx.x + k2 * blockDim.x;
+        v[k2] = i < dim ? xr[i] : 0.f;
+    }
+    double s = 0;
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) s += (double)v[k2] * (double)v[k2];
+    s = block_sum(s, scratch);
+    const float mean = (float)(s / dim);
+    const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) {
+        const int i = threadIdx.x + k2 * blockDim.x;
+        if (i < dim) yr[i] = __fmul_rn(__fmul_rn(v[k2], scale), w[i]);
+    }
+}
+
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s)
 {
     if (n <= 0) return;
-    const int threads = dim >= 1024 ? 256 : dim >= 256 ? 128 : 64;
-    k_rmsnorm<<<n, threads, 0, s>>>(x, dim, w, eps, y);
+    if (dim <= 8 * 1024) {
+        const int threads = std::min(1024, std::max(32, ((dim + 7) / 8 + 31) / 32 * 32));
+        launch(k_rmsnorm8, dim3(n), dim3(threads), 0, s, x, dim, w, eps, y);
+    } else {
+        launch(k_rmsnorm, dim3(n), dim3(256), 0, s, x, dim, w, eps, y);
+    }
     launched();
 }
 
 __global__ void k_add_bias(float* y, const float* __restrict__ b, int64_t total, int n)
 {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
         y[i] = __fadd_rn(y[i], b[i % n]);
 }
@@ -500,13 +545,15 @@ void add_bias(float* y, const float* b, int T, int n, cudaStream_t s)
     const int64_t total = (int64_t)T * n;
     if (total <= 0) return;
     int64_t g = grid_for(total, 256); if (g > 4096) g = 4096;
-    k_add_bias<<<(unsigned)g, 256, 0, s>>>(y, b, total, n);
+    launch(k_add_bias, dim3((unsigned)g), dim3(256), 0, s, y, b, total, n);
     launched();
 }
 
 __global__ void k_rope(float* x, int heads, int head_dim, int rope_dims, int neox, const int32_t* __restrict__ pos,
                        const float* __restrict__ table)
 {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y, half = rope_dims / 2;
     const int64_t base = (int64_t)t * heads * head_dim;
     const float* cs = table + (int64_t)pos[t] * rope_dims;
@@ -526,13 +573,15 @@ void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, con
 {
     if (T <= 0 || rope_dims <= 0) return;
     dim3 grid(grid_for((int64_t)heads * (rope_dims / 2), 256), T);
-    k_rope<<<grid, 256, 0, s>>>(x, heads, head_dim, rope_dims, neox, pos, table);
+    launch(k_rope, dim3(grid), dim3(256), 0, s, x, heads, head_dim, rope_dims, neox, pos, table);
     launched();
 }
 
 __global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, int kd,
                             const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos)
 {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     uint16_t* kc = rows[t].k + layer * rows[t].layer_stride + (int64_t)pos[t] * kd;
     uint16_t* vc = rows[t].v + layer * rows[t].layer_stride + (int64_t)pos[t] * kd;
@@ -547,7 +596,7 @@ void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows,
 {
     if (T <= 0) return;
     dim3 grid(grid_for(kd, 256), T);
-    k_kv_append<<<grid, 256, 0, s>>>(k, v, kd, rows, layer, pos);
+    launch(k_kv_append, dim3(grid), dim3(256), 0, s, k, v, kd, rows, layer, pos);
     launched();
 }
 
@@ -560,6 +609,8 @@ __global__ void k_attention(const float* __restrict__ q, int heads, int kv_heads
                             const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos,
                             float* __restrict__ out)
 {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float sm[];
     __shared__ double dscratch[32];
     __shared__ float fscratch[32];
@@ -620,7 +671,7 @@ void attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
         WL_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         attr_set[dev] = true;
     }
-    k_attention<<<T * heads, 128, smem, s>>>(q, heads, kv_heads, head_dim, scale, rows, layer, pos, out);
+    launch(k_attention, dim3(T * heads), dim3(128), smem, s, q, heads, kv_heads, head_dim, scale, rows, layer, pos, out);
     launched();
 }
 
@@ -629,6 +680,8 @@ void attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
 // ------------------------------------------------------------------------------------------------------------------
 __global__ void k_swiglu(float* g, const float* __restrict__ u, int64_t n)
 {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float a = g[i];
         const float e = (float)exp(-(double)a);
@@ -640,12 +693,14 @@ void swiglu(float* g, const float* u, int64_t n, cudaStream_t s)
 {
     if (n <= 0) return;
     int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
-    k_swiglu<<<(unsigned)gr, 256, 0, s>>>(g, u, n);
+    launch(k_swiglu, dim3((unsigned)gr), dim3(256), 0, s, g, u, n);
     launched();
 }
 
 __global__ void k_residual(float* x, const float* __restrict__ o, float rs, int64_t n)
 {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         x[i] = __fadd_rn(x[i], __fmul_rn(o[i], rs));
 }
@@ -654,12 +709,14 @@ void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s)
 {
     if (n <= 0) return;
     int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
-    k_residual<<<(unsigned)gr, 256, 0, s>>>(x, o, rs, n);
+    launch(k_residual, dim3((unsigned)gr), dim3(256), 0, s, x, o, rs, n);
     launched();
 }
 
 __global__ void k_scale(float* x, float f, int64_t n)
 {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         x[i] = __fmul_rn(x[i], f);
 }
@@ -668,7 +725,7 @@ void scale(float* x, float f, int64_t n, cudaStream_t s)
 {
     if (n <= 0) return;
     int64_t gr = grid_for(n, 256); if (gr > 148 * 16) gr = 148 * 16;
-    k_scale<<<(unsigned)gr, 256, 0, s>>>(x, f, n);
+    launch(k_scale, dim3((unsigned)gr), dim3(256), 0, s, x, f, n);
     launched();
 }
 
@@ -679,6 +736,8 @@ void scale(float* x, float f, int64_t n, cudaStream_t s)
 // with ties to the lower id, renormalisation clamped at 6.103515625e-5).
 __global__ void k_route(const float* __restrict__ logits, int T, int n, int k, int renorm, int32_t* sel, float* wts)
 {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     const float* lg = logits + (int64_t)t * n;
@@ -708,12 +767,14 @@ __global__ void k_route(const float* __restrict__ logits, int T, int n, int k, i
 void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s)
 {
     if (T <= 0) return;
-    k_route<<<grid_for(T, 64), 64, 0, s>>>(logits, T, n, k, renorm, sel, wts);
+    launch(k_route, dim3(grid_for(T, 64)), dim3(64), 0, s, logits, T, n, k, renorm, sel, wts);
     launched();
 }
 
 __global__ void k_gather_rows(float* xe, const float* __restrict__ xn, const int32_t* __restrict__ toks, int n, int E)
 {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.y;
     for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x)
         xe[(int64_t)i * E + d] = xn[(int64_t)toks[i] * E + d];
@@ -722,13 +783,15 @@ __global__ void k_gather_rows(float* xe, const float* __restrict__ xn, const int
 void gather_rows(float* xe, const float* xn, const int32_t* toks, int n, int E, cudaStream_t s)
 {
     if (n <= 0) return;
-    k_gather_rows<<<dim3(grid_for(E, 256), n), 256, 0, s>>>(xe, xn, toks, n, E);
+    launch(k_gather_rows, dim3(dim3(grid_for(E, 256), n)), dim3(256), 0, s, xe, xn, toks, n, E);
     launched();
 }
 
 __global__ void k_scatter_add(float* outp, const float* __restrict__ ye, const int32_t* __restrict__ toks,
                               const float* __restrict__ w, int E)
 {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.y;
     float* o = outp + (int64_t)toks[i] * E;
     const float wi = w[i];
@@ -739,12 +802,14 @@ __global__ void k_scatter_add(float* outp, const float* __restrict__ ye, const i
 void scatter_add(float* outp, const float* ye, const int32_t* toks, const float* w, int n, int E, cudaStream_t s)
 {
     if (n <= 0) return;
-    k_scatter_add<<<dim3(grid_for(E, 256), n), 256, 0, s>>>(outp, ye, toks, w, E);
+    launch(k_scatter_add, dim3(dim3(grid_for(E, 256), n)), dim3(256), 0, s, outp, ye, toks, w, E);
     launched();
 }
 
 __global__ void k_shared_expert_add(float* outp, const float* __restrict__ sh, const float* __restrict__ gl, int E)
 {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.y;
     const float f = gl ? __fdiv_rn(1.0f, __fadd_rn(1.0f, (float)exp(-(double)gl[t]))) : 1.0f;
     for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x) {
@@ -756,7 +821,7 @@ __global__ void k_shared_expert_add(float* outp, const float* __restrict__ sh, c
 void shared_expert_add(float* outp, const float* sh, const float* gl, int T, int E, cudaStream_t s)
 {
     if (T <= 0) return;
-    k_shared_expert_add<<<dim3(grid_for(E, 256), T), 256, 0, s>>>(outp, sh, gl, E);
+    launch(k_shared_expert_add, dim3(dim3(grid_for(E, 256), T)), dim3(256), 0, s, outp, sh, gl, E);
     launched();
 }
 
@@ -890,6 +955,8 @@ __device__ void quant_q6_k(const float* x, uint8_t* out)
 
 __global__ void k_synth(int type, uint64_t base, int64_t nblocks, float sigma, float offset, uint8_t* __restrict__ out)
 {
+    pdl_trigger();
+    pdl_wait();
     const int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (b >= nblocks) return;
     if (type == 0) { const float v = __fadd_rn(offset, __fmul_rn(sigma, synth_normal(base, b))); reinterpret_cast<float*>(out)[b] = v; return; }
@@ -920,7 +987,7 @@ void synth(int type, uint64_t seed, uint32_t tid, int64_t rows, int64_t cols, fl
     const int64_t nblocks = rows * cols / be;
     const uint64_t base = splitmix64_host(seed ^ ((uint64_t)tid * 0xD1B54A32D192ED03ull));
     if (nblocks <= 0) return;
-    k_synth<<<grid_for(nblocks, 128), 128, 0, s>>>(type, base, nblocks, sigma, offset, out);
+    launch(k_synth, dim3(grid_for(nblocks, 128)), dim3(128), 0, s, type, base, nblocks, sigma, offset, out);
     launched();
 }
 

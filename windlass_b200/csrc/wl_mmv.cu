@@ -20,6 +20,7 @@
 #include <mutex>
 #include "wl_common.h"
 #include "wl_kernels.h"
+#include "wl_launch.cuh"
 
 namespace wl {
 namespace k {
@@ -100,6 +101,8 @@ __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cas
 // One CTA of 64 threads per (superblock, column); each thread owns 4 consecutive values.
 __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64_t ldx, int nsb, uint8_t* __restrict__ out)
 {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float scratch[2];
     const int sb = blockIdx.x, n = blockIdx.y, t = threadIdx.x;
     const float4 v4 = *reinterpret_cast<const float4*>(x + (int64_t)n * ldx + sb * 256 + 4 * t);
@@ -202,23 +205,30 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
     const int njobs = nsb > warp ? (nsb - warp + 7) / 8 : 0;
 
+    pdl_trigger();
     if (lane == 0) {
         for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
         fence_mbar_init();
         fence_proxy_async();
     }
     __syncwarp();
-    auto issue = [&](int j, int s) {
-        const int sb = warp + 8 * j;
+    auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
         uint8_t* st = ring + s * LY::STAGE;
         mbar_expect_tx(&bars[warp][s], LY::TX);
-        tma_load_2d(st, &wmap, sb * 144, row_base + r0, &bars[warp][s]);
+        tma_load_2d(st, &wmap, (warp + 8 * j) * 144, row_base + r0, &bars[warp][s]);
+    };
+    auto issue_x = [&](int j, int s) {      // prepared activations of the same superblock, on the same barrier
+        const int sb = warp + 8 * j;
+        uint8_t* st = ring + s * LY::STAGE;
 #pragma unroll
         for (int n = 0; n < NC; ++n)
             bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
     };
     if (lane == 0)
-        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue(j, j);
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_w(j, j);
+    pdl_wait();
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
 
     // B operand of this lane: MMA column g is (column g/3, digit g%3) when packed, else column g
     const bool b_ok = PACK ? g < 3 * NC : g < NC;
@@ -312,7 +322,8 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
         __syncwarp();
         if (lane == 0 && j + LY::STAGES < njobs) {
             fence_proxy_async();        // the stage's generic reads are done before the copy engine rewrites it
-            issue(j + LY::STAGES, s);
+            issue_w(j + LY::STAGES, s);
+            issue_x(j + LY::STAGES, s);
         }
     }
     // per (row, column): ((plane 0 + plane 1) + plane 2) - min term, then the warps in order
@@ -363,7 +374,7 @@ XPrep xprep_view(void* scratch, int cols, int nc)
 
 void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s)
 {
-    k_xprep<<<dim3(cols / 256, nc), 64, 0, s>>>(x, ldx, cols / 256, p.blocks);
+    launch(k_xprep, dim3(dim3(cols / 256, nc)), dim3(64), 0, s, x, ldx, cols / 256, p.blocks);
     note_launch();
 }
 
@@ -415,7 +426,7 @@ static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, co
         attr[dev] = true;
     }
     const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(map.bytes);
-    k_mmv_q4k<NC><<<(rows + Q4_ROWS - 1) / Q4_ROWS, 256, Q4Layout<NC>::SMEM, s>>>(m, row_base, rows, nsb, p.blocks,
+    launch(k_mmv_q4k<NC>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC>::SMEM, s, m, row_base, rows, nsb, p.blocks,
                                                                                   y, ldy, err);
     note_launch();
 }
