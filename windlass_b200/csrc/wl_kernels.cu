@@ -605,74 +605,252 @@ void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows,
 // separately rounded products; softmax exponentials and their sum are in double like the reference; the weighted V
 // sum runs positions in order with separately rounded products and sums.
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void k_attention(const float* __restrict__ q, int heads, int kv_heads, int head_dim, float scale,
-                            const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos,
-                            float* __restrict__ out)
+// Attention (Transformer.cs:351-395), split over positions (flash-decoding) and shared by the query heads of one KV
+// head: CTA (range, kv head, row) stages its positions' fp16 keys and values in shared memory tile by tile (16-byte
+// cp.async, all copies of a tile in flight at once) and uses them for all G = heads/kv_heads query heads. Scores keep
+// the reference's four interleaved accumulators; exponentials are fp32 expf, the running sums double. Positions
+// 0..pos[t] of row t are cut into S equal ranges by the row's own length, so a row's result does not depend on the
+// other rows; each range keeps a running max m, sum l and unnormalised output o per head across its tiles. With
+// S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order.
+constexpr int ATT_P = 64;           // positions per tile
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_MAXG = 16;        // query heads per KV head
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
+                                                           float scale, const RowKV* __restrict__ rows, int layer,
+                                                           const int32_t* __restrict__ pos, int S,
+                                                           float* __restrict__ out, float* __restrict__ part,
+                                                           float* __restrict__ ml)
 {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ float sm[];
-    __shared__ double dscratch[32];
-    __shared__ float fscratch[32];
-    const int t = blockIdx.x / heads, h = blockIdx.x % heads;
-    const int group = heads / kv_heads, kvh = h / group;
-    const int QD = heads * head_dim, KD = kv_heads * head_dim;
+    constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
+    constexpr int CH = HD / 8;              // 16-byte chunks per row
+    constexpr int DPT = (HD + ATT_THREADS - 1) / ATT_THREADS;   // output dims per thread
+    extern __shared__ __align__(16) uint8_t smraw[];
+    uint16_t* ks = reinterpret_cast<uint16_t*>(smraw);           // [ATT_P][KP]
+    uint16_t* vs = ks + ATT_P * KP;                               // [ATT_P][KP]
+    float* qs = reinterpret_cast<float*>(vs + ATT_P * KP);       // [G][HD]
+    __shared__ float sc[ATT_MAXG][ATT_P];
+    __shared__ float tmax[ATT_MAXG], mrun[ATT_MAXG], alpha[ATT_MAXG];
+    __shared__ double tsum[ATT_MAXG], lrun[ATT_MAXG];
+    const int sp = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int G = heads / kv_heads, QD = heads * HD, KD = kv_heads * HD;
     const int n = pos[t] + 1;
-    float* qs = sm;                 // head_dim
-    float* sp = sm + head_dim;      // n scores
-    const float* qp = q + (int64_t)t * QD + (int64_t)h * head_dim;
-    for (int i = threadIdx.x; i < head_dim; i += blockDim.x) qs[i] = qp[i];
-    __syncthreads();
-    const uint16_t* K = rows[t].k + layer * rows[t].layer_stride;
-    const uint16_t* V = rows[t].v + layer * rows[t].layer_stride;
-    float mx = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        const uint16_t* kp = K + (int64_t)j * KD + (int64_t)kvh * head_dim;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-        int i = 0;
-        for (; i + 4 <= head_dim; i += 4) {
-            s0 = __fadd_rn(s0, __fmul_rn(qs[i], h2f(kp[i])));
-            s1 = __fadd_rn(s1, __fmul_rn(qs[i + 1], h2f(kp[i + 1])));
-            s2 = __fadd_rn(s2, __fmul_rn(qs[i + 2], h2f(kp[i + 2])));
-            s3 = __fadd_rn(s3, __fmul_rn(qs[i + 3], h2f(kp[i + 3])));
+    const int per = (n + S - 1) / S;
+    const int start = sp * per, end = min(n, start + per);
+    const float* qp = q + (int64_t)t * QD + (int64_t)kvh * G * HD;
+    for (int i = tid; i < G * HD; i += ATT_THREADS) qs[i] = qp[i];
+    if (tid < ATT_MAXG) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
+    const uint16_t* K = rows[t].k + (int64_t)layer * rows[t].layer_stride + (int64_t)kvh * HD;
+    const uint16_t* V = rows[t].v + (int64_t)layer * rows[t].layer_stride + (int64_t)kvh * HD;
+    float o[DPT][ATT_MAXG];
+#pragma unroll
+    for (int k2 = 0; k2 < DPT; ++k2)
+#pragma unroll
+        for (int h = 0; h < ATT_MAXG; ++h) o[k2][h] = 0.f;
+    // score work: position pl of the tile, heads hs, hs + 2, ...
+    const int pl = tid % ATT_P, hs = tid / ATT_P;
+    for (int tile0 = start; tile0 < end; tile0 += ATT_P) {
+        const int cnt = min(ATT_P, end - tile0);
+        for (int i = tid; i < cnt * CH; i += ATT_THREADS) {
+            const int r = i / CH, c = i % CH;
+            cp_async16(ks + r * KP + c * 8, K + (int64_t)(tile0 + r) * KD + c * 8);
+            cp_async16(vs + r * KP + c * 8, V + (int64_t)(tile0 + r) * KD + c * 8);
         }
-        for (; i < head_dim; ++i) s0 = __fadd_rn(s0, __fmul_rn(qs[i], h2f(kp[i])));
-        const float d = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
-        sp[j] = d;
-        mx = fmaxf(mx, d);
+        cp_async_wait_all();
+        __syncthreads();
+        {
+            float s4[ATT_MAXG / 2][4];
+#pragma unroll
+            for (int h = 0; h < ATT_MAXG / 2; ++h) s4[h][0] = s4[h][1] = s4[h][2] = s4[h][3] = 0.f;
+            if (pl < cnt) {
+                const uint16_t* kr = ks + pl * KP;
+#pragma unroll
+                for (int d0 = 0; d0 < HD; d0 += 8) {
+                    const uint4 kv8 = *reinterpret_cast<const uint4*>(kr + d0);
+                    const uint16_t* kh = reinterpret_cast<const uint16_t*>(&kv8);
+                    float kf[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) kf[e] = h2f(kh[e]);
+#pragma unroll
+                    for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
+                        const int h = hs + 2 * hh;
+                        if (h < G) {
+                            const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + d0);
+                            const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + d0 + 4);
+                            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) s4[hh][e & 3] = __fadd_rn(s4[hh][e & 3], __fmul_rn(qv[e], kf[e]));
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
+                const int h = hs + 2 * hh;
+                if (h < G)
+                    sc[h][pl] = pl < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(s4[hh][0], s4[hh][1]), __fadd_rn(s4[hh][2], s4[hh][3])), scale)
+                                         : -INFINITY;
+            }
+        }
+        __syncthreads();
+        for (int h = warp; h < G; h += ATT_THREADS / 32) {
+            float m = fmaxf(sc[h][lane], sc[h][lane + 32]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            if (lane == 0) {
+                const float mn = fmaxf(m, mrun[h]);
+                tmax[h] = mn;
+                alpha[h] = expf(mrun[h] - mn);      // 0 while no position has been seen
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
+            const int h = hs + 2 * hh;
+            if (h < G) sc[h][pl] = pl < cnt ? expf(__fsub_rn(sc[h][pl], tmax[h])) : 0.f;
+        }
+        __syncthreads();
+        for (int h = warp; h < G; h += ATT_THREADS / 32) {
+            double sum = (double)sc[h][lane] + (double)sc[h][lane + 32];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            if (lane == 0) tsum[h] = sum;
+        }
+        // o = o * e^(m_old - m_new) + sum_j p_j v_j, from the staged values
+#pragma unroll
+        for (int k2 = 0; k2 < DPT; ++k2) {
+            const int d = tid + k2 * ATT_THREADS;
+            if (d < HD) {
+#pragma unroll
+                for (int h = 0; h < ATT_MAXG; ++h)
+                    if (h < G) o[k2][h] = __fmul_rn(o[k2][h], alpha[h]);
+                for (int j = 0; j < cnt; ++j) {
+                    const float v = h2f(vs[j * KP + d]);
+#pragma unroll
+                    for (int h = 0; h < ATT_MAXG; ++h)
+                        if (h < G) o[k2][h] = __fadd_rn(o[k2][h], __fmul_rn(sc[h][j], v));
+                }
+            }
+        }
+        __syncthreads();
+        if (tid < G) {
+            lrun[tid] = lrun[tid] * (double)alpha[tid] + tsum[tid];
+            mrun[tid] = tmax[tid];
+        }
+        __syncthreads();
     }
-    mx = block_max(mx, fscratch);
-    double sum = 0;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-        const float e = (float)exp((double)__fsub_rn(sp[j], mx));
-        sp[j] = e;
-        sum += (double)e;
+#pragma unroll
+    for (int k2 = 0; k2 < DPT; ++k2) {
+        const int d = tid + k2 * ATT_THREADS;
+        if (d >= HD) continue;
+#pragma unroll
+        for (int h = 0; h < ATT_MAXG; ++h) {
+            if (h >= G) continue;
+            const int head = kvh * G + h;
+            if (S == 1) out[(int64_t)t * QD + (int64_t)head * HD + d] = (float)((double)o[k2][h] / lrun[h]);
+            else part[(((int64_t)t * heads + head) * S + sp) * HD + d] = o[k2][h];
+        }
     }
-    sum = block_sum(sum, dscratch);
-    const float inv = (float)(1.0 / sum);
+    if (S > 1 && tid < G) {
+        float* mlp = ml + (((int64_t)t * heads + kvh * G + tid) * S + sp) * 2;
+        mlp[0] = mrun[tid];
+        mlp[1] = (float)lrun[tid];
+    }
+}
+
+// Merges the S position ranges of k_attn_part in range order: out = sum_s e^(m_s-M) o_s / sum_s e^(m_s-M) l_s.
+// All loads of a thread are issued before their first use.
+__global__ void __launch_bounds__(128) k_attn_combine(int heads, int hd, int S, const float* __restrict__ part,
+                                                      const float* __restrict__ ml, float* __restrict__ out)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ double wsh[32];
+    __shared__ double Lsh;
+    const int head = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const float* mlp = ml + ((int64_t)t * heads + head) * S * 2;
+    if (tid < 32) {
+        const float m = tid < S ? mlp[2 * tid] : -INFINITY;
+        const float l = tid < S ? mlp[2 * tid + 1] : 0.f;
+        float M = m;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        const double w = l > 0.f ? exp((double)m - (double)M) : 0.0;
+        wsh[tid] = w;
+        double L = w * (double)l;
+        // fixed-order sum over the ranges
+        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (tid == 0) Lsh = L;
+    }
     __syncthreads();
-    float* op = out + (int64_t)t * QD + (int64_t)h * head_dim;
-    for (int dd = threadIdx.x; dd < head_dim; dd += blockDim.x) {
-        float acc = 0.f;
-        const uint16_t* vp = V + (int64_t)kvh * head_dim + dd;
-        for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(sp[j], inv), h2f(vp[(int64_t)j * KD])));
-        op[dd] = acc;
+    const float* pp = part + ((int64_t)t * heads + head) * S * hd;
+    for (int d = tid; d < hd; d += blockDim.x) {
+        float pv[32];
+#pragma unroll
+        for (int s2 = 0; s2 < 32; ++s2) pv[s2] = s2 < S ? pp[(int64_t)s2 * hd + d] : 0.f;
+        double acc = 0.0;
+#pragma unroll
+        for (int s2 = 0; s2 < 32; ++s2) acc += wsh[s2] * (double)pv[s2];
+        out[((int64_t)t * heads + head) * hd + d] = (float)(acc / Lsh);
+    }
+}
+
+int attention_splits(int T, int kv_heads)
+{
+    int S = (2 * 148 + T * kv_heads - 1) / (T * kv_heads);
+    S = S < 1 ? 1 : S > 32 ? 32 : S;
+    while (S > 1 && T * S > ATT_PART_ROWS) --S;
+    return S;
+}
+
+template <int HD>
+static void attn_launch(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
+                        const int32_t* pos, float* part, float* out, cudaStream_t s)
+{
+    const int G = heads / kv_heads, S = attention_splits(T, kv_heads);
+    const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        attr_set[dev] = true;
+    }
+    float* ml = part + (size_t)ATT_PART_ROWS * heads * HD;
+    launch(k_attn_part<HD>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows, layer,
+           pos, S, out, part, ml);
+    launched();
+    if (S > 1) {
+        launch(k_attn_combine, dim3(heads, T), dim3(128), 0, s, heads, HD, S, (const float*)part, (const float*)ml, out);
+        launched();
     }
 }
 
 void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, int max_n, float* out, cudaStream_t s)
+               int layer, const int32_t* pos, float* part, float* out, cudaStream_t s)
 {
     if (T <= 0) return;
-    const size_t smem = sizeof(float) * (size_t)(head_dim + max_n);
-    static bool attr_set[64] = {false};
-    int dev = 0; cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && dev < 64 && !attr_set[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set[dev] = true;
+    if (heads % kv_heads != 0 || heads / kv_heads > ATT_MAXG)
+        WL_THROW(WL_EUNSUPPORTED, "attention: more than 16 query heads per KV head");
+    switch (head_dim) {
+    case 64: attn_launch<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
+    case 80: attn_launch<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
+    case 96: attn_launch<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
+    case 128: attn_launch<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
+    case 256: attn_launch<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
+    default: WL_THROW(WL_EUNSUPPORTED, "attention: head_dim " + std::to_string(head_dim) + " (64, 80, 96, 128 or 256 are supported)");
     }
-    launch(k_attention, dim3(T * heads), dim3(128), smem, s, q, heads, kv_heads, head_dim, scale, rows, layer, pos, out);
-    launched();
 }
 
 // ------------------------------------------------------------------------------------------------------------------

@@ -54,6 +54,11 @@ constexpr size_t STATIC_SCRATCH_BYTES = 256 + xprep_bytes_c(STATIC_MAX_COLS, 8);
 void* static_scratch();
 // x[t*ldx + i] for t < nc (1..8), cols a multiple of 256.
 void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaStream_t s);
+// x[t] += o[t] * rs (when o), then y[t] = RmsNormRows(x[t]) * w for T rows of E values, and when p is given y's
+// activations prepared as xprep would (bit-identical), in one kernel. E a multiple of 256, at most 8192.
+bool norm_prep_supported(int E);
+void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
+               cudaStream_t s);
 // A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
 struct alignas(64) WeightMap {
     uint8_t bytes[128];
@@ -79,9 +84,13 @@ void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, con
 // Transformer.cs:342-348).
 void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows, int layer, const int32_t* pos,
                cudaStream_t s);
-// Attention (Transformer.cs:351-395): row t, head h attends to positions 0..pos[t] of its own cache.
+// Attention (Transformer.cs:351-395): row t, head h attends to positions 0..pos[t] of its own cache. part is a
+// workspace of attention_part_floats(heads, head_dim) floats for the split-range partials.
+constexpr int ATT_PART_ROWS = 64;   // most (row, range) pairs one call keeps partials for
+inline size_t attention_part_floats(int heads, int head_dim) { return (size_t)ATT_PART_ROWS * heads * (head_dim + 2); }
+int attention_splits(int T, int kv_heads);
 void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, int max_n, float* out, cudaStream_t s);
+               int layer, const int32_t* pos, float* part, float* out, cudaStream_t s);
 // g[i] = g[i]/(1+exp(-g[i])) * u[i] (SwiGlu, Transformer.cs:247).
 void swiglu(float* g, const float* u, int64_t n, cudaStream_t s);
 // x[i] += o[i] * rs (Transformer.cs:225,231).

@@ -87,6 +87,19 @@ __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier
 
 __device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// Fixed-order block sum: lanes by xor butterfly, then the warps in index order.
+__device__ __forceinline__ double block_sum_d(double v, double* scratch)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    double s = 0;
+    for (int i = 0; i < nw; ++i) s += scratch[i];
+    return s;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -155,6 +168,100 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
     // digit unit (non-finite input makes it NaN, so the products are NaN as the fp32 dot would be), then zero padding
     if (t == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
     if (t >= 9 && t < 9 + (XP_COL - XP_REC) / 4 - 9) rec[t] = 0u;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// residual + RmsNorm + activation prep in one pass
+// ------------------------------------------------------------------------------------------------------------------
+// One CTA per row, E/8 threads: warp w owns the 256 values of superblock w, a lane 8 consecutive values.
+// x += o * rs (Transformer.cs:225,231) when o is given; y = RmsNormRows(x) * w (Transformer.cs:454-464, sum of squares
+// in double); when prep is given, y's superblocks are also written in k_xprep's layout with the same arithmetic
+// (same maximum, digits, and the same association of the 32-value sums), so the result is bit-identical to
+// rmsnorm followed by k_xprep.
+template <bool RES, bool PREP>
+__global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const float* __restrict__ o, float rs,
+                                                    int E, const float* __restrict__ w, float eps, float* __restrict__ y,
+                                                    uint8_t* __restrict__ prep)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ double scratch[32];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i0 = warp * 256 + lane * 8;
+    float* xr = x + (int64_t)t * E + i0;
+    float4 a = *reinterpret_cast<const float4*>(xr), b = *reinterpret_cast<const float4*>(xr + 4);
+    if (RES) {
+        const float* orow = o + (int64_t)t * E + i0;
+        const float4 oa = *reinterpret_cast<const float4*>(orow), ob = *reinterpret_cast<const float4*>(orow + 4);
+        a = make_float4(__fadd_rn(a.x, __fmul_rn(oa.x, rs)), __fadd_rn(a.y, __fmul_rn(oa.y, rs)),
+                        __fadd_rn(a.z, __fmul_rn(oa.z, rs)), __fadd_rn(a.w, __fmul_rn(oa.w, rs)));
+        b = make_float4(__fadd_rn(b.x, __fmul_rn(ob.x, rs)), __fadd_rn(b.y, __fmul_rn(ob.y, rs)),
+                        __fadd_rn(b.z, __fmul_rn(ob.z, rs)), __fadd_rn(b.w, __fmul_rn(ob.w, rs)));
+        *reinterpret_cast<float4*>(xr) = a;
+        *reinterpret_cast<float4*>(xr + 4) = b;
+    }
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    double ss = 0;
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) ss += (double)v[k2] * (double)v[k2];
+    ss = block_sum_d(ss, scratch);
+    const float mean = (float)(ss / E);
+    const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
+    const float4 wa = *reinterpret_cast<const float4*>(w + i0), wb = *reinterpret_cast<const float4*>(w + i0 + 4);
+    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    float f[8];
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) f[k2] = __fmul_rn(__fmul_rn(v[k2], scale), wv[k2]);
+    float* yr = y + (int64_t)t * E + i0;
+    *reinterpret_cast<float4*>(yr) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(yr + 4) = make_float4(f[4], f[5], f[6], f[7]);
+    if (!PREP) return;
+    float m = 0.f;
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) m = fmaxf(m, fabsf(f[k2]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const bool finite = m <= 3.4e38f;
+    int e = 0;
+    if (m > 0.f && finite) frexpf(m, &e);
+    e = e < -100 ? -100 : e > 100 ? 100 : e;
+    const float up = ldexpf(1.0f, 20 - e), sup = ldexpf(1.0f, 10 - e);
+    const int nsb = E / 256;
+    uint8_t* blk = prep + ((int64_t)t * nsb + warp) * XP_COL;
+    uint32_t dg[3][2] = {};
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) {
+        const int X = finite ? __float2int_rn(f[k2] * up) : 0;
+        const int x2 = ((X + 64) & 127) - 64;
+        const int r = (X - x2) >> 7;
+        const int x1 = ((r + 64) & 127) - 64;
+        const int x0 = (r - x1) >> 7;
+        dg[0][k2 >> 2] |= (uint32_t)(x0 & 0xFF) << (8 * (k2 & 3));
+        dg[1][k2 >> 2] |= (uint32_t)(x1 & 0xFF) << (8 * (k2 & 3));
+        dg[2][k2 >> 2] |= (uint32_t)(x2 & 0xFF) << (8 * (k2 & 3));
+    }
+#pragma unroll
+    for (int d = 0; d < 3; ++d) *reinterpret_cast<uint2*>(blk + d * XP_DIGIT + 8 * lane) = make_uint2(dg[d][0], dg[d][1]);
+    if (lane < 8) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * lane) = 0u;
+    }
+    // 32-value sums with k_xprep's association: (g0+g1) per lane, then lanes xor 1, then xor 2
+    float sm = __fadd_rn(__fadd_rn(f[0] * sup, f[1] * sup), __fadd_rn(f[2] * sup, f[3] * sup));
+    const float s1 = __fadd_rn(__fadd_rn(f[4] * sup, f[5] * sup), __fadd_rn(f[6] * sup, f[7] * sup));
+    sm = __fadd_rn(sm, s1);
+    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+    const float s_next = __shfl_down_sync(0xffffffffu, sm, 4);
+    uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
+    if ((lane & 7) == 0) {
+        const __half h0 = __float2half_rn(sm), h1 = __float2half_rn(s_next);
+        const __half l0 = __float2half_rn(sm - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
+        rec[2 * (lane >> 3)] = h2_bits(__halves2half2(h0, h1));
+        rec[2 * (lane >> 3) + 1] = h2_bits(__halves2half2(l0, l1));
+    }
+    if (lane == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
+    if (lane >= 9) rec[lane] = 0u;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -362,6 +469,26 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
 // host side
 // ------------------------------------------------------------------------------------------------------------------
 size_t xprep_bytes(int cols, int nc) { return xprep_bytes_c(cols, nc); }
+
+bool norm_prep_supported(int E) { return E % 256 == 0 && E <= 8192; }
+
+void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
+               cudaStream_t s)
+{
+    if (T <= 0) return;
+    if (!norm_prep_supported(E)) WL_THROW(WL_EUNSUPPORTED, "norm_prep: the row length must be a multiple of 256, at most 8192");
+    if (p && (p->cols != E || p->nc != T)) WL_THROW(WL_EINVAL, "norm_prep: prepared-activation view does not match");
+    uint8_t* pb = p ? p->blocks : nullptr;
+    const dim3 grid(T), block(E / 8);
+    if (o) {
+        if (p) launch(k_norm_prep<true, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb);
+        else launch(k_norm_prep<true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb);
+    } else {
+        if (p) launch(k_norm_prep<false, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb);
+        else launch(k_norm_prep<false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb);
+    }
+    note_launch();
+}
 
 XPrep xprep_view(void* scratch, int cols, int nc)
 {

@@ -379,6 +379,7 @@ Model::~Model()
     hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
     for (void* p : extra_allocs_) cudaFree(p);
     if (xprep_buf_) cudaFree(xprep_buf_);
+    dfree(att_part_);
     dfree(err_d_);
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
@@ -476,6 +477,7 @@ void Model::ensure_workspace(int T, int logit_rows)
                 if (w->present()) max_cols = std::max(max_cols, w->cols);
         }
         WL_CUDA(cudaMalloc(&xprep_buf_, k::xprep_bytes(max_cols, 8)));
+        att_part_ = dalloc<float>((int64_t)k::attention_part_floats(c_.heads, c_.head_dim));
     }
     if (logit_rows > ws_logit_rows_) {
         dfree(logits_);
@@ -647,9 +649,13 @@ void Model::layer(int l, int T, int max_n)
     const int E = c_.embd, QD = c_.qdim(), KD = c_.kvdim(), HD = c_.head_dim;
     const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
     const int64_t n = (int64_t)T * E;
-    if (c_.post_norms) WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
-    else k::rmsnorm(x_, T, E, L.attn_norm.d, c_.rms_eps, xn_, stream_);
-    matmul(L.q, xn_, T, q_);
+    if (c_.post_norms) {
+        WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
+        prep_x_ = nullptr;
+    } else {
+        pre_norm(T, L.attn_norm, L.q.map.valid);
+    }
+    matmul(L.q, xn_, T, q_, 0, true);
     matmul(L.k, xn_, T, k_, 0, true);
     matmul(L.v, xn_, T, v_, 0, true);
     if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
@@ -667,24 +673,63 @@ void Model::layer(int l, int T, int max_n)
     k::kv_append(k_, v_, T, KD, rows_d_, l, pos_d_, stream_);
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
     const int mark = profile_begin();
-    k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, max_n, att_, stream_);
+    k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, att_part_, att_, stream_);
     profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
     matmul(L.o, att_, T, o_);
-    if (c_.post_norms) k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
-    k::residual(x_, o_, rs, n, stream_);
-    if (c_.post_norms) WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
-    else k::rmsnorm(x_, T, E, L.ffn_norm.d, c_.rms_eps, xn_, stream_);
+    if (c_.post_norms) {
+        k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
+        k::residual(x_, o_, rs, n, stream_);
+        WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
+        prep_x_ = nullptr;
+    } else {
+        pending_residual_ = true;           // x += o happens inside the ffn norm
+        pre_norm(T, L.ffn_norm, L.moe ? false : L.gate.map.valid);
+    }
     if (L.moe) ffn_moe(L, T);
     else ffn_dense(L, T);
-    if (c_.post_norms) k::rmsnorm(o_, T, E, L.post_ffw_norm.d, c_.rms_eps, o_, stream_);
-    k::residual(x_, o_, rs, n, stream_);
+    if (c_.post_norms) {
+        k::rmsnorm(o_, T, E, L.post_ffw_norm.d, c_.rms_eps, o_, stream_);
+        k::residual(x_, o_, rs, n, stream_);
+    } else {
+        pending_residual_ = true;           // x += o happens inside the next norm (next layer or the head)
+    }
+}
+
+// The pre-norm of a sublayer: x += o (the previous sublayer's output, when pending), xn = RmsNormRows(x) * w, and,
+// for up to eight rows read by a tensor-core matvec, xn's prepared activations, all in one kernel when the row
+// length allows.
+void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
+{
+    const int E = c_.embd;
+    const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
+    prep_x_ = nullptr;
+    if (k::norm_prep_supported(E)) {
+        const bool prep = prep_for_mma && T <= 8 && xprep_buf_;
+        k::XPrep p{};
+        if (prep) p = k::xprep_view(xprep_buf_, E, T);
+        k::norm_prep(x_, pending_residual_ ? o_ : nullptr, rs, T, E, w.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_);
+        if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = T; }
+    } else {
+        if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
+        k::rmsnorm(x_, T, E, w.d, c_.rms_eps, xn_, stream_);
+    }
+    pending_residual_ = false;
 }
 
 // Head (src/Transformer.cs:112-125): final norm and output matrix for rows first..T-1.
 void Model::head(int T, int first)
 {
     const int E = c_.embd, n = T - first;
-    k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
+    const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
+    prep_x_ = nullptr;
+    if (k::norm_prep_supported(E)) {
+        k::norm_prep(x_ + (int64_t)first * E, pending_residual_ ? o_ + (int64_t)first * E : nullptr, rs, n, E,
+                     out_norm_.d, c_.rms_eps, xn_, nullptr, stream_);
+    } else {
+        if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
+        k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
+    }
+    pending_residual_ = false;
     matmul(output_, xn_, n, logits_);
     if (c_.logit_scale != 0.f) k::scale(logits_, 1.f / c_.logit_scale, (int64_t)n * c_.vocab, stream_);
 }
@@ -706,6 +751,7 @@ void Model::upload_step(int T, const RowKV* rows, const int32_t* pos, const int3
 void Model::step_device(int T, int first, int max_n)
 {
     k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
+    pending_residual_ = false;
     for (int l = 0; l < c_.layers; ++l) layer(l, T, max_n);
     head(T, first);
 }
@@ -727,6 +773,7 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
     } else if (!cancel && !progress) step_device(T, first, max_n);
     else {
         k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
+        pending_residual_ = false;
         for (int l = 0; l < c_.layers; ++l) {
             if (cancel && *cancel) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
             layer(l, T, max_n);

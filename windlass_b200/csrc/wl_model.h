@@ -130,6 +130,7 @@ private:
     void reserve(Seq* s, int positions);
     void ensure_workspace(int T, int logit_rows);
     void layer(int l, int T, int max_n);
+    void pre_norm(int T, const Vec& w, bool prep_for_mma);
     void ffn_dense(const LayerW& L, int T);
     void ffn_moe(const LayerW& L, int T);
     void head(int T, int first);
@@ -175,9 +176,11 @@ private:
     int h_cap_ = 0;
     // activations prepared for the tensor-core matvec (k::xprep), and what they were prepared from
     void* xprep_buf_ = nullptr;
+    float* att_part_ = nullptr;         // split-range attention partials
     int* err_d_ = nullptr;              // device error word of the bounded waits
     const float* prep_x_ = nullptr;
     int prep_cols_ = 0, prep_nc_ = 0;
+    bool pending_residual_ = false;     // x += o_ not yet applied (done by the next norm)
     // CUDA graphs of decode steps
     bool use_graphs_ = true;
     std::vector<GraphEntry> graphs_;
