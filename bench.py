@@ -308,7 +308,10 @@ def main():
     q6 = m.profile_get(Q6_K)
     att = m.profile_get(40)
     trace(f"profile: q4_K {q4.launches} launches {q4.ms:.1f} ms {q4.bytes / 1e9:.2f} GB; q6_K {q6.launches} "
-          f"{q6.ms:.1f} ms {q6.bytes / 1e9:.2f} GB; attention {att.launches} {att.ms:.1f} ms")
+          f"{q6.ms:.1f} ms {q6.bytes / 1e9:.2f} GB; attention {att.launches} {att.ms:.1f} ms; " +
+          "; ".join(f"{name} {e.launches} {e.ms:.1f} ms" for name, e in
+                    (("norm", m.profile_get(41)), ("rope", m.profile_get(42)), ("swiglu", m.profile_get(43)),
+                     ("xprep", m.profile_get(44)))))
     m.profile(0)
     hbm, _, peak_kind = measured_peaks()
     achieved = q4.bytes / (q4.ms / 1e3) / 1e9 if q4.ms > 0 else None

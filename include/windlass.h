@@ -97,7 +97,11 @@ typedef struct wl_profile_entry {
     double  bytes;
 } wl_profile_entry;
 /* wl_profile_get kinds beyond the weight formats. */
-#define WL_PROFILE_ATTENTION 40
+#define WL_PROFILE_ATTENTION 40   /* attention and its range merge */
+#define WL_PROFILE_NORM      41   /* residual + RmsNorm (+ activation prep) */
+#define WL_PROFILE_ROPE      42   /* RoPE + KV append */
+#define WL_PROFILE_SWIGLU    43   /* SwiGlu (+ activation prep) */
+#define WL_PROFILE_XPREP     44   /* stand-alone activation prep of the tensor-core matvecs */
 
 /* Synthetic model (benchmarks and full-size tests): a decoder of the given shape whose weights are generated on the
  * device from a counter hash (seed, tensor, element), N(0, sigma) through Irwin-Hall(12), round-to-nearest quantized.

@@ -15,6 +15,7 @@
 #include <algorithm>
 #include "wl_kernels.h"
 #include "wl_launch.cuh"
+#include "wl_xprep.cuh"
 
 namespace wl {
 
@@ -600,10 +601,96 @@ void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows,
     launched();
 }
 
+// RoPE of q and k plus the fp16 KV append, one kernel: work items are q's rotation pairs, then k's values (rotated
+// pairs computed from both partners, unrotated dims copied), then v's values. The arithmetic is k_rope's.
+__global__ void k_rope_append(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, int heads,
+                              int kv_heads, int head_dim, int rope_dims, int neox, const int32_t* __restrict__ pos,
+                              const float* __restrict__ table, const RowKV* __restrict__ rows, int layer)
+{
+    pdl_trigger();
+    const int t = blockIdx.y, half = rope_dims / 2, kd = kv_heads * head_dim;
+    const int nq = heads * half;
+    // positions, cache rows and the rope table come from host copies, not from an earlier kernel
+    const int p = pos[t];
+    const float* cs = table + (int64_t)p * rope_dims;
+    const RowKV rk = rows[t];
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    float c = 1.f, sn = 0.f;
+    {
+        const int d = idx < nq ? idx % half : idx < nq + kd ? (idx - nq) % head_dim : rope_dims;
+        if (d < rope_dims) {
+            const int i = idx < nq ? d : neox ? (d < half ? d : d - half) : d >> 1;
+            c = cs[2 * i];
+            sn = cs[2 * i + 1];
+        }
+    }
+    pdl_wait();
+    if (idx < nq) {
+        const int h = idx / half, i = idx % half;
+        float* x = q + (int64_t)t * heads * head_dim + (int64_t)h * head_dim;
+        const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+        const float x0 = x[a], x1 = x[b];
+        x[a] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        x[b] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    } else if (idx < nq + kd) {
+        const int e = idx - nq, d = e % head_dim;
+        const float* kr = k + (int64_t)t * kd + (e - d);
+        float out = kr[d];
+        if (d < rope_dims) {
+            const bool first = neox ? d < half : (d & 1) == 0;
+            const int i = neox ? (first ? d : d - half) : d >> 1;
+            const int a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            const float x0 = kr[a], x1 = kr[b];
+            out = first ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+        }
+        rk.k[(int64_t)layer * rk.layer_stride + (int64_t)p * kd + e] = __half_as_ushort(__float2half_rn(out));
+    } else if (idx < nq + 2 * kd) {
+        const int e = idx - nq - kd;
+        rk.v[(int64_t)layer * rk.layer_stride + (int64_t)p * kd + e] = __half_as_ushort(__float2half_rn(v[(int64_t)t * kd + e]));
+    }
+}
+
+void rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim, int rope_dims,
+                 int neox, const int32_t* pos, const float* table, const RowKV* rows, int layer, cudaStream_t s)
+{
+    if (T <= 0) return;
+    const int items = heads * (rope_dims / 2) + 2 * kv_heads * head_dim;
+    launch(k_rope_append, dim3(grid_for(items, 256), T), dim3(256), 0, s, q, k, v, heads, kv_heads, head_dim, rope_dims,
+           neox, pos, table, rows, layer);
+    launched();
+}
+
+// SwiGlu (k_swiglu's arithmetic) and the prepared activations of the result, one 256-value superblock per CTA.
+__global__ void __launch_bounds__(64) k_swiglu_prep(float* __restrict__ g, const float* __restrict__ u, int F,
+                                                    uint8_t* __restrict__ prep)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float scratch[2];
+    const int sb = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const int64_t i = (int64_t)t * F + sb * 256 + 4 * tid;
+    const float4 a4 = *reinterpret_cast<const float4*>(g + i), u4 = *reinterpret_cast<const float4*>(u + i);
+    const float a[4] = {a4.x, a4.y, a4.z, a4.w}, uu[4] = {u4.x, u4.y, u4.z, u4.w};
+    float f[4];
+#pragma unroll
+    for (int k2 = 0; k2 < 4; ++k2) {
+        const float e = (float)exp(-(double)a[k2]);
+        f[k2] = __fmul_rn(__fdiv_rn(a[k2], __fadd_rn(1.0f, e)), uu[k2]);
+    }
+    *reinterpret_cast<float4*>(g + i) = make_float4(f[0], f[1], f[2], f[3]);
+    xprep_sb(f, tid, scratch, prep + ((int64_t)t * (F / 256) + sb) * XP_COL);
+}
+
+void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStream_t s)
+{
+    if (T <= 0) return;
+    if (F % 256 != 0 || p.cols != F || p.nc != T) WL_THROW(WL_EINVAL, "swiglu_prep: shape mismatch");
+    launch(k_swiglu_prep, dim3(F / 256, T), dim3(64), 0, s, g, u, F, p.blocks);
+    launched();
+}
+
 // ------------------------------------------------------------------------------------------------------------------
-// attention: one CTA per (row, head). Scores use the reference's four-accumulator dot (Transformer.cs:366-378) with
-// separately rounded products; softmax exponentials and their sum are in double like the reference; the weighted V
-// sum runs positions in order with separately rounded products and sums.
+// attention
 // ------------------------------------------------------------------------------------------------------------------
 // Attention (Transformer.cs:351-395), split over positions (flash-decoding) and shared by the query heads of one KV
 // head: CTA (range, kv head, row) stages its positions' fp16 keys and values in shared memory tile by tile (16-byte
@@ -623,41 +710,44 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <int HD>
+template <int HD, int G>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
                                                            float scale, const RowKV* __restrict__ rows, int layer,
                                                            const int32_t* __restrict__ pos, int S,
                                                            float* __restrict__ out, float* __restrict__ part,
                                                            float* __restrict__ ml)
 {
-    pdl_trigger();
-    pdl_wait();
     constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
     constexpr int CH = HD / 8;              // 16-byte chunks per row
     constexpr int DPT = (HD + ATT_THREADS - 1) / ATT_THREADS;   // output dims per thread
+    constexpr int GH = (G + 1) / 2;         // heads per thread in the score phase
     extern __shared__ __align__(16) uint8_t smraw[];
     uint16_t* ks = reinterpret_cast<uint16_t*>(smraw);           // [ATT_P][KP]
     uint16_t* vs = ks + ATT_P * KP;                               // [ATT_P][KP]
     float* qs = reinterpret_cast<float*>(vs + ATT_P * KP);       // [G][HD]
-    __shared__ float sc[ATT_MAXG][ATT_P];
-    __shared__ float tmax[ATT_MAXG], mrun[ATT_MAXG], alpha[ATT_MAXG];
-    __shared__ double tsum[ATT_MAXG], lrun[ATT_MAXG];
+    __shared__ float sc[G][ATT_P];
+    __shared__ float tmax[G], mrun[G], alpha[G];
+    __shared__ double tsum[G], lrun[G];
+    pdl_trigger();
     const int sp = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int G = heads / kv_heads, QD = heads * HD, KD = kv_heads * HD;
+    const int QD = heads * HD, KD = kv_heads * HD;
+    // positions and cache pointers come from host copies, not from an earlier kernel: read them before the wait
     const int n = pos[t] + 1;
+    const RowKV rk = rows[t];
+    pdl_wait();
     const int per = (n + S - 1) / S;
     const int start = sp * per, end = min(n, start + per);
     const float* qp = q + (int64_t)t * QD + (int64_t)kvh * G * HD;
     for (int i = tid; i < G * HD; i += ATT_THREADS) qs[i] = qp[i];
-    if (tid < ATT_MAXG) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
-    const uint16_t* K = rows[t].k + (int64_t)layer * rows[t].layer_stride + (int64_t)kvh * HD;
-    const uint16_t* V = rows[t].v + (int64_t)layer * rows[t].layer_stride + (int64_t)kvh * HD;
-    float o[DPT][ATT_MAXG];
+    if (tid < G) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
+    const uint16_t* K = rk.k + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
+    const uint16_t* V = rk.v + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
+    float o[DPT][G];
 #pragma unroll
     for (int k2 = 0; k2 < DPT; ++k2)
 #pragma unroll
-        for (int h = 0; h < ATT_MAXG; ++h) o[k2][h] = 0.f;
+        for (int h = 0; h < G; ++h) o[k2][h] = 0.f;
     // score work: position pl of the tile, heads hs, hs + 2, ...
     const int pl = tid % ATT_P, hs = tid / ATT_P;
     for (int tile0 = start; tile0 < end; tile0 += ATT_P) {
@@ -669,10 +759,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
         }
         cp_async_wait_all();
         __syncthreads();
-        {
-            float s4[ATT_MAXG / 2][4];
+        if (G > 1 || hs == 0) {
+            float s4[GH][4];
 #pragma unroll
-            for (int h = 0; h < ATT_MAXG / 2; ++h) s4[h][0] = s4[h][1] = s4[h][2] = s4[h][3] = 0.f;
+            for (int hh = 0; hh < GH; ++hh) s4[hh][0] = s4[hh][1] = s4[hh][2] = s4[hh][3] = 0.f;
             if (pl < cnt) {
                 const uint16_t* kr = ks + pl * KP;
 #pragma unroll
@@ -683,24 +773,21 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
 #pragma unroll
                     for (int e = 0; e < 8; ++e) kf[e] = h2f(kh[e]);
 #pragma unroll
-                    for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
-                        const int h = hs + 2 * hh;
-                        if (h < G) {
-                            const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + d0);
-                            const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + d0 + 4);
-                            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    for (int hh = 0; hh < GH; ++hh) {
+                        const int h = G > 1 ? hs + 2 * hh : 0;
+                        const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + d0);
+                        const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + d0 + 4);
+                        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) s4[hh][e & 3] = __fadd_rn(s4[hh][e & 3], __fmul_rn(qv[e], kf[e]));
-                        }
+                        for (int e = 0; e < 8; ++e) s4[hh][e & 3] = __fadd_rn(s4[hh][e & 3], __fmul_rn(qv[e], kf[e]));
                     }
                 }
             }
 #pragma unroll
-            for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
-                const int h = hs + 2 * hh;
-                if (h < G)
-                    sc[h][pl] = pl < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(s4[hh][0], s4[hh][1]), __fadd_rn(s4[hh][2], s4[hh][3])), scale)
-                                         : -INFINITY;
+            for (int hh = 0; hh < GH; ++hh) {
+                const int h = G > 1 ? hs + 2 * hh : 0;
+                sc[h][pl] = pl < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(s4[hh][0], s4[hh][1]), __fadd_rn(s4[hh][2], s4[hh][3])), scale)
+                                     : -INFINITY;
             }
         }
         __syncthreads();
@@ -715,10 +802,12 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
             }
         }
         __syncthreads();
+        if (G > 1 || hs == 0) {
 #pragma unroll
-        for (int hh = 0; hh < ATT_MAXG / 2; ++hh) {
-            const int h = hs + 2 * hh;
-            if (h < G) sc[h][pl] = pl < cnt ? expf(__fsub_rn(sc[h][pl], tmax[h])) : 0.f;
+            for (int hh = 0; hh < GH; ++hh) {
+                const int h = G > 1 ? hs + 2 * hh : 0;
+                sc[h][pl] = pl < cnt ? expf(__fsub_rn(sc[h][pl], tmax[h])) : 0.f;
+            }
         }
         __syncthreads();
         for (int h = warp; h < G; h += ATT_THREADS / 32) {
@@ -733,13 +822,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
             const int d = tid + k2 * ATT_THREADS;
             if (d < HD) {
 #pragma unroll
-                for (int h = 0; h < ATT_MAXG; ++h)
-                    if (h < G) o[k2][h] = __fmul_rn(o[k2][h], alpha[h]);
+                for (int h = 0; h < G; ++h) o[k2][h] = __fmul_rn(o[k2][h], alpha[h]);
                 for (int j = 0; j < cnt; ++j) {
                     const float v = h2f(vs[j * KP + d]);
 #pragma unroll
-                    for (int h = 0; h < ATT_MAXG; ++h)
-                        if (h < G) o[k2][h] = __fadd_rn(o[k2][h], __fmul_rn(sc[h][j], v));
+                    for (int h = 0; h < G; ++h) o[k2][h] = __fadd_rn(o[k2][h], __fmul_rn(sc[h][j], v));
                 }
             }
         }
@@ -755,8 +842,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
         const int d = tid + k2 * ATT_THREADS;
         if (d >= HD) continue;
 #pragma unroll
-        for (int h = 0; h < ATT_MAXG; ++h) {
-            if (h >= G) continue;
+        for (int h = 0; h < G; ++h) {
             const int head = kvh * G + h;
             if (S == 1) out[(int64_t)t * QD + (int64_t)head * HD + d] = (float)((double)o[k2][h] / lrun[h]);
             else part[(((int64_t)t * heads + head) * S + sp) * HD + d] = o[k2][h];
@@ -769,88 +855,113 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
     }
 }
 
-// Merges the S position ranges of k_attn_part in range order: out = sum_s e^(m_s-M) o_s / sum_s e^(m_s-M) l_s.
-// All loads of a thread are issued before their first use.
-__global__ void __launch_bounds__(128) k_attn_combine(int heads, int hd, int S, const float* __restrict__ part,
-                                                      const float* __restrict__ ml, float* __restrict__ out)
+// Merges the S position ranges of k_attn_part in range order for one 256-value superblock of a row's attention
+// output (64 threads, 4 consecutive values each, all within one head): M = max m_s, w_s = e^(m_s - M),
+// out = sum_s w_s o_s / sum_s w_s l_s, sums in double in range order. With prep, the superblock is also written in
+// the tensor-core matvec's activation layout. All loads of a thread are issued before their first use.
+__global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const float* __restrict__ part,
+                                                     const float* __restrict__ ml, float* __restrict__ out,
+                                                     uint8_t* __restrict__ prep)
 {
     pdl_trigger();
     pdl_wait();
-    __shared__ double wsh[32];
-    __shared__ double Lsh;
-    const int head = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
-    const float* mlp = ml + ((int64_t)t * heads + head) * S * 2;
-    if (tid < 32) {
-        const float m = tid < S ? mlp[2 * tid] : -INFINITY;
-        const float l = tid < S ? mlp[2 * tid + 1] : 0.f;
-        float M = m;
+    __shared__ float scratch[2];
+    const int sb = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const int QD = heads * hd, v = sb * 256 + 4 * tid, head = v / hd, d = v % hd;
+    const float2* mlp = reinterpret_cast<const float2*>(ml + ((int64_t)t * heads + head) * ATT_SPLITS * 2);
+    const float* pp = part + ((int64_t)t * heads + head) * ATT_SPLITS * hd + d;
+    float2 mls[ATT_SPLITS];
+    float4 ps[ATT_SPLITS];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-        const double w = l > 0.f ? exp((double)m - (double)M) : 0.0;
-        wsh[tid] = w;
-        double L = w * (double)l;
-        // fixed-order sum over the ranges
-        for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-        if (tid == 0) Lsh = L;
+    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) {
+        mls[s2] = mlp[s2];
+        ps[s2] = *reinterpret_cast<const float4*>(pp + (int64_t)s2 * hd);
     }
-    __syncthreads();
-    const float* pp = part + ((int64_t)t * heads + head) * S * hd;
-    for (int d = tid; d < hd; d += blockDim.x) {
-        float pv[32];
+    float M = -INFINITY;
 #pragma unroll
-        for (int s2 = 0; s2 < 32; ++s2) pv[s2] = s2 < S ? pp[(int64_t)s2 * hd + d] : 0.f;
-        double acc = 0.0;
+    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) M = fmaxf(M, mls[s2].x);
+    double L = 0.0, o0 = 0.0, o1 = 0.0, o2 = 0.0, o3 = 0.0;
 #pragma unroll
-        for (int s2 = 0; s2 < 32; ++s2) acc += wsh[s2] * (double)pv[s2];
-        out[((int64_t)t * heads + head) * hd + d] = (float)(acc / Lsh);
+    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) {
+        const double w = mls[s2].y > 0.f ? (double)expf(mls[s2].x - M) : 0.0;
+        L += w * (double)mls[s2].y;
+        o0 += w * (double)ps[s2].x;
+        o1 += w * (double)ps[s2].y;
+        o2 += w * (double)ps[s2].z;
+        o3 += w * (double)ps[s2].w;
     }
+    const float f[4] = {(float)(o0 / L), (float)(o1 / L), (float)(o2 / L), (float)(o3 / L)};
+    *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
+    if (prep) xprep_sb(f, tid, scratch, prep + ((int64_t)t * (QD / 256) + sb) * XP_COL);
 }
 
 int attention_splits(int T, int kv_heads)
 {
-    int S = (2 * 148 + T * kv_heads - 1) / (T * kv_heads);
-    S = S < 1 ? 1 : S > 32 ? 32 : S;
-    while (S > 1 && T * S > ATT_PART_ROWS) --S;
-    return S;
+    (void)kv_heads;
+    return T <= ATT_PART_ROWS ? ATT_SPLITS : 1;
 }
 
-template <int HD>
+template <int HD, int G>
 static void attn_launch(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                        const int32_t* pos, float* part, float* out, cudaStream_t s)
+                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
 {
-    const int G = heads / kv_heads, S = attention_splits(T, kv_heads);
+    const int S = attention_splits(T, kv_heads);
     const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr_set[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
         attr_set[dev] = true;
     }
-    float* ml = part + (size_t)ATT_PART_ROWS * heads * HD;
-    launch(k_attn_part<HD>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows, layer,
+    float* ml = part + (size_t)ATT_PART_ROWS * ATT_SPLITS * heads * HD;
+    launch(k_attn_part<HD, G>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows, layer,
            pos, S, out, part, ml);
     launched();
     if (S > 1) {
-        launch(k_attn_combine, dim3(heads, T), dim3(128), 0, s, heads, HD, S, (const float*)part, (const float*)ml, out);
+        launch(k_attn_combine, dim3(heads * HD / 256, T), dim3(64), 0, s, heads, (int)HD, (const float*)part,
+               (const float*)ml, out, prep ? prep->blocks : (uint8_t*)nullptr);
         launched();
     }
 }
 
-void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, cudaStream_t s)
+template <int HD>
+static void attn_launch_g(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
+                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
 {
-    if (T <= 0) return;
-    if (heads % kv_heads != 0 || heads / kv_heads > ATT_MAXG)
-        WL_THROW(WL_EUNSUPPORTED, "attention: more than 16 query heads per KV head");
-    switch (head_dim) {
-    case 64: attn_launch<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
-    case 80: attn_launch<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
-    case 96: attn_launch<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
-    case 128: attn_launch<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
-    case 256: attn_launch<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, s); break;
-    default: WL_THROW(WL_EUNSUPPORTED, "attention: head_dim " + std::to_string(head_dim) + " (64, 80, 96, 128 or 256 are supported)");
+    switch (heads / kv_heads) {
+    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
     }
+}
+
+bool attention_supported(int heads, int kv_heads, int head_dim)
+{
+    const int g = kv_heads > 0 && heads % kv_heads == 0 ? heads / kv_heads : 0;
+    return (g == 1 || g == 2 || g == 4 || g == 8 || g == 16) && (heads * head_dim) % 256 == 0 &&
+           (head_dim == 64 || head_dim == 80 || head_dim == 96 || head_dim == 128 || head_dim == 256);
+}
+
+bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+{
+    if (T <= 0) return false;
+    if (!attention_supported(heads, kv_heads, head_dim))
+        WL_THROW(WL_EUNSUPPORTED, "attention: unsupported head layout (1, 2, 4, 8 or 16 query heads per KV head, head_dim 64, "
+                                  "80, 96, 128 or 256, heads*head_dim a multiple of 256)");
+    if (attention_splits(T, kv_heads) == 1) prep = nullptr;
+    if (prep && (prep->cols != heads * head_dim || prep->nc != T)) WL_THROW(WL_EINVAL, "attention: prepared-activation view does not match");
+    switch (head_dim) {
+    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    }
+    return prep != nullptr;
 }
 
 // ------------------------------------------------------------------------------------------------------------------

@@ -85,12 +85,26 @@ void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, con
 void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows, int layer, const int32_t* pos,
                cudaStream_t s);
 // Attention (Transformer.cs:351-395): row t, head h attends to positions 0..pos[t] of its own cache. part is a
-// workspace of attention_part_floats(heads, head_dim) floats for the split-range partials.
-constexpr int ATT_PART_ROWS = 64;   // most (row, range) pairs one call keeps partials for
-inline size_t attention_part_floats(int heads, int head_dim) { return (size_t)ATT_PART_ROWS * heads * (head_dim + 2); }
+// workspace of attention_part_floats(heads, head_dim) floats for the split-range partials. For up to
+// ATT_PART_ROWS rows each row's positions are split into ATT_SPLITS ranges (a fixed count, so a row's result never
+// depends on the other rows); with prep (T <= 8) the output is also written as prepared activations, and the call
+// returns whether it did.
+constexpr int ATT_PART_ROWS = 64;
+constexpr int ATT_SPLITS = 16;
+inline size_t attention_part_floats(int heads, int head_dim)
+{
+    return (size_t)ATT_PART_ROWS * ATT_SPLITS * heads * (head_dim + 2);
+}
 int attention_splits(int T, int kv_heads);
-void attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, cudaStream_t s);
+bool attention_supported(int heads, int kv_heads, int head_dim);
+bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s);
+// RoPE on q (heads) and k (kv heads) of T rows, then k and v appended to the fp16 caches at pos[t] (Rope,
+// Transformer.cs:418-433, and ToHalf, :342-348), in one kernel; k is left unrotated in its buffer.
+void rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim, int rope_dims,
+                 int neox, const int32_t* pos, const float* table, const RowKV* rows, int layer, cudaStream_t s);
+// SwiGlu into g (as swiglu) for T rows of F values, and g's prepared activations (F a multiple of 256, T <= 8).
+void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStream_t s);
 // g[i] = g[i]/(1+exp(-g[i])) * u[i] (SwiGlu, Transformer.cs:247).
 void swiglu(float* g, const float* u, int64_t n, cudaStream_t s);
 // x[i] += o[i] * rs (Transformer.cs:225,231).

@@ -17,10 +17,12 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 #include "wl_common.h"
 #include "wl_kernels.h"
 #include "wl_launch.cuh"
+#include "wl_xprep.cuh"
 
 namespace wl {
 namespace k {
@@ -105,13 +107,7 @@ __device__ __forceinline__ double block_sum_d(double v, double* scratch)
 // ------------------------------------------------------------------------------------------------------------------
 // activation prep
 // ------------------------------------------------------------------------------------------------------------------
-// Per (column, superblock) one XP_COL-byte block: three planes of signed 8-bit digits of the 256 values in natural
-// order (pitch XP_DIGIT; the 32 pad bytes keep the B-fragment reads of different planes on different banks), then a
-// record at XP_REC: four (hi pair, lo pair) f16x2 words holding the sums of the eight 32-value sub-blocks, then the
-// float unit of the digits. X = round(x * 2^(20-e)) (|X| <= 2^20, e the exponent of the superblock's largest
-// magnitude) is split into balanced base-128 digits X = X0*2^14 + X1*2^7 + X2, each in [-64, 64]. The sums are taken
-// at 2^(10-e), where they fit f16 with a hi/lo split good to 2^-22.
-// One CTA of 64 threads per (superblock, column); each thread owns 4 consecutive values.
+// One CTA of 64 threads per (superblock, column); each thread owns 4 consecutive values (layout in wl_xprep.cuh).
 __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64_t ldx, int nsb, uint8_t* __restrict__ out)
 {
     pdl_trigger();
@@ -119,55 +115,8 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
     __shared__ float scratch[2];
     const int sb = blockIdx.x, n = blockIdx.y, t = threadIdx.x;
     const float4 v4 = *reinterpret_cast<const float4*>(x + (int64_t)n * ldx + sb * 256 + 4 * t);
-    float m = fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((t & 31) == 0) scratch[t >> 5] = m;
-    __syncthreads();
-    m = fmaxf(scratch[0], scratch[1]);
-    const bool finite = m <= 3.4e38f;          // false for inf and NaN
-    int e = 0;
-    if (m > 0.f && finite) frexpf(m, &e);
-    e = e < -100 ? -100 : e > 100 ? 100 : e;
-    const float up = ldexpf(1.0f, 20 - e);     // digit scale: |x| * up <= 2^20
-    const float sup = ldexpf(1.0f, 10 - e);    // sum scale: |x| * sup < 2^10
-    uint8_t* blk = out + ((int64_t)n * nsb + sb) * XP_COL;
     const float f[4] = {v4.x, v4.y, v4.z, v4.w};
-    uint32_t dg0 = 0, dg1 = 0, dg2 = 0;
-#pragma unroll
-    for (int k2 = 0; k2 < 4; ++k2) {
-        const int X = finite ? __float2int_rn(f[k2] * up) : 0;
-        const int x2 = ((X + 64) & 127) - 64;
-        const int r = (X - x2) >> 7;
-        const int x1 = ((r + 64) & 127) - 64;
-        const int x0 = (r - x1) >> 7;
-        dg0 |= (uint32_t)(x0 & 0xFF) << (8 * k2);
-        dg1 |= (uint32_t)(x1 & 0xFF) << (8 * k2);
-        dg2 |= (uint32_t)(x2 & 0xFF) << (8 * k2);
-    }
-    *reinterpret_cast<uint32_t*>(blk + 0 * XP_DIGIT + 4 * t) = dg0;
-    *reinterpret_cast<uint32_t*>(blk + 1 * XP_DIGIT + 4 * t) = dg1;
-    *reinterpret_cast<uint32_t*>(blk + 2 * XP_DIGIT + 4 * t) = dg2;
-    if (t < 8) {
-#pragma unroll
-        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * t) = 0u;
-    }
-    // sum of the 32 values of this thread's sub-block: 8 consecutive threads
-    float s = (f[0] * sup + f[1] * sup) + (f[2] * sup + f[3] * sup);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    const float s_next = __shfl_down_sync(0xffffffffu, s, 8);
-    uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
-    if ((t & 15) == 0) {
-        const __half h0 = __float2half_rn(s), h1 = __float2half_rn(s_next);
-        const __half l0 = __float2half_rn(s - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
-        rec[2 * (t >> 4)] = h2_bits(__halves2half2(h0, h1));
-        rec[2 * (t >> 4) + 1] = h2_bits(__halves2half2(l0, l1));
-    }
-    // digit unit (non-finite input makes it NaN, so the products are NaN as the fp32 dot would be), then zero padding
-    if (t == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
-    if (t >= 9 && t < 9 + (XP_COL - XP_REC) / 4 - 9) rec[t] = 0u;
+    xprep_sb(f, t, scratch, out + ((int64_t)n * nsb + sb) * XP_COL);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -184,10 +133,12 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
                                                     uint8_t* __restrict__ prep)
 {
     pdl_trigger();
-    pdl_wait();
     __shared__ double scratch[32];
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i0 = warp * 256 + lane * 8;
+    // the norm weights are written by no kernel: fetch them before waiting for the previous one
+    const float4 wa = *reinterpret_cast<const float4*>(w + i0), wb = *reinterpret_cast<const float4*>(w + i0 + 4);
+    pdl_wait();
     float* xr = x + (int64_t)t * E + i0;
     float4 a = *reinterpret_cast<const float4*>(xr), b = *reinterpret_cast<const float4*>(xr + 4);
     if (RES) {
@@ -207,7 +158,6 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
     ss = block_sum_d(ss, scratch);
     const float mean = (float)(ss / E);
     const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
-    const float4 wa = *reinterpret_cast<const float4*>(w + i0), wb = *reinterpret_cast<const float4*>(w + i0 + 4);
     const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
     float f[8];
 #pragma unroll
@@ -270,11 +220,11 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
 constexpr int Q4_ROWS = 16;                     // rows per CTA: one m16 row group, shared by the eight warps
 constexpr int Q4_TILE = Q4_ROWS * 144;          // weight bytes per stage
 
-template <int NC> struct Q4Layout {
+template <int NC, int ST = 2> struct Q4Layout {
     static constexpr int X_OFF = Q4_TILE;       // 2304, a multiple of 128
     static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;   // TMA destinations are 128-byte aligned
     static constexpr int TX = Q4_TILE + NC * XP_COL;                         // bytes the copies of one stage deliver
-    static constexpr int STAGES = 2;
+    static constexpr int STAGES = ST;
     static constexpr int SMEM = 8 * STAGES * STAGE;
 };
 
@@ -296,12 +246,12 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // Up to two columns, the 8 MMA columns hold (column, digit) pairs (one MMA per sub-block); from three columns on,
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
-template <int NC>
-__global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap, int row_base, int rows,
+template <int NC, int ST>
+__global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap, int row_base, int rows,
                                                     int nsb, const uint8_t* __restrict__ xq, float* __restrict__ y,
                                                     int64_t ldy, int* err)
 {
-    using LY = Q4Layout<NC>;
+    using LY = Q4Layout<NC, ST>;
     constexpr bool PACK = NC <= 2;
     constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block
     extern __shared__ __align__(128) uint8_t smem[];
@@ -541,21 +491,42 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
     out->valid = true;
 }
 
-template <int NC>
-static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                       int* err, cudaStream_t s)
+template <int NC, int ST>
+static void launch_q4k_st(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                          int* err, cudaStream_t s)
 {
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC, ST>::SMEM));
         attr[dev] = true;
     }
     const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(map.bytes);
-    launch(k_mmv_q4k<NC>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC>::SMEM, s, m, row_base, rows, nsb, p.blocks,
-                                                                                  y, ldy, err);
+    launch(k_mmv_q4k<NC, ST>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC, ST>::SMEM, s, m, row_base,
+           rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
+}
+
+static int q4k_stages()
+{
+    static int st = [] {
+        const char* e = getenv("WL_Q4K_STAGES");
+        const int v = e ? atoi(e) : 2;
+        return v >= 2 && v <= 4 ? v : 2;
+    }();
+    return st;
+}
+
+template <int NC>
+static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                       int* err, cudaStream_t s)
+{
+    switch (NC <= 2 ? q4k_stages() : 2) {
+    case 3: launch_q4k_st<NC, 3>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 4: launch_q4k_st<NC, 4>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
+    default: launch_q4k_st<NC, 2>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
+    }
 }
 
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y, int64_t ldy,

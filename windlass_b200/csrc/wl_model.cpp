@@ -115,6 +115,9 @@ static Config read_config(const Gguf& g)
     if (c.layers <= 0 || c.embd <= 0 || c.heads <= 0 || c.kv_heads <= 0) WL_THROW(WL_EUNSUPPORTED, "The model shape is incomplete.");
     if (c.heads % c.kv_heads != 0) WL_THROW(WL_EUNSUPPORTED, "head_count must be a multiple of head_count_kv.");
     if (c.rope_dims > c.head_dim || c.rope_dims % 2 != 0) WL_THROW(WL_EUNSUPPORTED, "Unsupported rope.dimension_count " + std::to_string(c.rope_dims) + ".");
+    if (!k::attention_supported(c.heads, c.kv_heads, c.head_dim))
+        WL_THROW(WL_EUNSUPPORTED, "Unsupported attention shape: " + std::to_string(c.heads) + " heads of " +
+                                  std::to_string(c.head_dim) + " over " + std::to_string(c.kv_heads) + " KV heads.");
     const GgufTensor* embd = g.find("token_embd.weight");
     if (!embd) WL_THROW(WL_EUNSUPPORTED, "The model has no token_embd.weight.");
     c.vocab = embd->rows();
@@ -361,6 +364,9 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
 
 void Model::finish_open()
 {
+    if (!k::attention_supported(c_.heads, c_.kv_heads, c_.head_dim))
+        WL_THROW(WL_EUNSUPPORTED, "Unsupported attention shape: " + std::to_string(c_.heads) + " heads of " +
+                                  std::to_string(c_.head_dim) + " over " + std::to_string(c_.kv_heads) + " KV heads.");
     if (!rope_table_) build_rope_table(nullptr, 0);
     build_maps();
     own_ = new_seq();
@@ -502,7 +508,9 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
             const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
             const bool same = reuse_x && T <= 8 && prep_x_ == x && prep_cols_ == w.cols && prep_nc_ == nc;
             if (!same) {
+                const int pm = profile_begin();
                 k::xprep(x + (int64_t)c0 * w.cols, w.cols, w.cols, nc, p, stream_);
+                profile_end(pm, WL_PROFILE_XPREP, 0.0);
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
@@ -587,10 +595,19 @@ void Model::check_device_error()
 void Model::ffn_dense(const LayerW& L, int T)
 {
     const int F = L.gate.rows;
-    matmul(L.gate, xn_, T, g_);
+    matmul(L.gate, xn_, T, g_, 0, true);
     matmul(L.up, xn_, T, u_, 0, true);
-    k::swiglu(g_, u_, (int64_t)T * F, stream_);
-    matmul(L.down, g_, T, o_);
+    prep_x_ = nullptr;
+    const int sm = profile_begin();
+    if (L.down.map.valid && T <= 8 && F % 256 == 0 && xprep_buf_) {
+        const k::XPrep p = k::xprep_view(xprep_buf_, F, T);
+        k::swiglu_prep(g_, u_, T, F, p, stream_);
+        prep_x_ = g_; prep_cols_ = F; prep_nc_ = T;
+    } else {
+        k::swiglu(g_, u_, (int64_t)T * F, stream_);
+    }
+    profile_end(sm, WL_PROFILE_SWIGLU, 0.0);
+    matmul(L.down, g_, T, o_, 0, true);
 }
 
 // MoeFfn (src/Transformer.cs:259-311): router, top-k, then each chosen expert runs once on the rows routed to it, in
@@ -668,14 +685,22 @@ void Model::layer(int l, int T, int max_n)
         k::rmsnorm(q_, T * c_.heads, HD, L.q_norm.d, c_.rms_eps, q_, stream_);
         k::rmsnorm(k_, T * c_.kv_heads, HD, L.k_norm.d, c_.rms_eps, k_, stream_);
     }
-    k::rope(q_, T, c_.heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_, stream_);
-    k::rope(k_, T, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_, stream_);
-    k::kv_append(k_, v_, T, KD, rows_d_, l, pos_d_, stream_);
+    const int rm = profile_begin();
+    k::rope_append(q_, k_, v_, T, c_.heads, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_,
+                   rows_d_, l, stream_);
+    profile_end(rm, WL_PROFILE_ROPE, 0.0);
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
+    // the o matvec's activations come out of the attention combine when it can prepare them
+    const bool want_prep = L.o.map.valid && T <= 8 && xprep_buf_;
+    k::XPrep ap{};
+    if (want_prep) ap = k::xprep_view(xprep_buf_, QD, T);
     const int mark = profile_begin();
-    k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, att_part_, att_, stream_);
+    const bool prepped = k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, att_part_, att_,
+                                      want_prep ? &ap : nullptr, stream_);
     profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
-    matmul(L.o, att_, T, o_);
+    prep_x_ = nullptr;
+    if (prepped) { prep_x_ = att_; prep_cols_ = QD; prep_nc_ = T; }
+    matmul(L.o, att_, T, o_, 0, true);
     if (c_.post_norms) {
         k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
         k::residual(x_, o_, rs, n, stream_);
@@ -703,6 +728,7 @@ void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
     const int E = c_.embd;
     const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
     prep_x_ = nullptr;
+    const int nm = profile_begin();
     if (k::norm_prep_supported(E)) {
         const bool prep = prep_for_mma && T <= 8 && xprep_buf_;
         k::XPrep p{};
@@ -713,6 +739,7 @@ void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
         k::rmsnorm(x_, T, E, w.d, c_.rms_eps, xn_, stream_);
     }
+    profile_end(nm, WL_PROFILE_NORM, 0.0);
     pending_residual_ = false;
 }
 
