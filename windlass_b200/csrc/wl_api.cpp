@@ -82,6 +82,22 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
         }
         return;
     }
+    if (!force_cuda_cores && wl::k::q6k_tiles_supported(type, cols) && (uintptr_t)x % 16 == 0) {
+        // scratch: [error word | prepared activations | the weights repacked into tiles]
+        const size_t xb = (wl::k::xprep_bytes(cols, 8) + 255) / 256 * 256;
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::q6k_tile_bytes(rows, cols));
+        int* err = (int*)scratch;
+        uint8_t* tiles = scratch + 256 + xb;
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        wl::k::q6k_tile(w, rows, cols, rb, tiles, s);
+        for (int c0 = 0; c0 < ncols; c0 += 8) {
+            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
+            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
+            wl::k::xprep(x + (int64_t)c0 * cols, cols, cols, nc, p, s);
+            wl::k::matvec_q6k(tiles, rows, cols, p, y + (int64_t)c0 * rows, rows, err, s);
+        }
+        return;
+    }
     wl::k::matvec(type, w, rb, rows, cols, x, cols, ncols, y, rows, s);
 }
 }  // namespace

@@ -17,7 +17,6 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
-#include <cstdlib>
 #include <mutex>
 #include "wl_common.h"
 #include "wl_kernels.h"
@@ -196,22 +195,23 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
 #pragma unroll
         for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * lane) = 0u;
     }
-    // 32-value sums with k_xprep's association: (g0+g1) per lane, then lanes xor 1, then xor 2
+    // 16- and 32-value sums with k_xprep's association: (g0+g1) per lane, then lanes xor 1 (16 values), then xor 2
     float sm = __fadd_rn(__fadd_rn(f[0] * sup, f[1] * sup), __fadd_rn(f[2] * sup, f[3] * sup));
     const float s1 = __fadd_rn(__fadd_rn(f[4] * sup, f[5] * sup), __fadd_rn(f[6] * sup, f[7] * sup));
     sm = __fadd_rn(sm, s1);
     sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+    const float s16 = sm, s16_next = __shfl_down_sync(0xffffffffu, sm, 2);
     sm += __shfl_xor_sync(0xffffffffu, sm, 2);
     const float s_next = __shfl_down_sync(0xffffffffu, sm, 4);
     uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
-    if ((lane & 7) == 0) {
-        const __half h0 = __float2half_rn(sm), h1 = __float2half_rn(s_next);
-        const __half l0 = __float2half_rn(sm - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
-        rec[2 * (lane >> 3)] = h2_bits(__halves2half2(h0, h1));
-        rec[2 * (lane >> 3) + 1] = h2_bits(__halves2half2(l0, l1));
+    if ((lane & 7) == 0) xp_store_pair(rec, 2 * (lane >> 3), 2 * (lane >> 3) + 1, sm, s_next);
+    if ((lane & 3) == 0) {
+        const int p = lane >> 2, c = p & 3, upper = p >> 2;
+        xp_store_pair(rec, XP_S16 + 4 * c + upper, XP_S16 + 4 * c + 2 + upper, s16, s16_next);
     }
     if (lane == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
-    if (lane >= 9) rec[lane] = 0u;
+    if (lane >= 9 && lane < XP_S16) rec[lane] = 0u;
+    if (lane >= XP_S16 + 16) rec[lane] = 0u;
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -416,6 +416,246 @@ __global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_c
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// Q6_K matvec
+// ------------------------------------------------------------------------------------------------------------------
+// Q6_K superblocks are 210 bytes, so a row's superblocks are only 2-byte aligned and cannot be copied by TMA. The
+// weights are therefore repacked once (k_q6k_tile) into tiles of 16 rows x one superblock (Q6_TILE = 3360 bytes,
+// 16-byte aligned), tile (r, b) at ((r * nsb) + b) * Q6_TILE, each laid out for conflict-free fragment reads:
+//   [0, 2048)     ql: per row 128 bytes; lane c's eight words (word h*4 + kk*2 + is = ql bytes 64h + 32kk + 16is +
+//                 4c..+3) sit at c*32, the two 16-byte halves swapped on odd rows
+//   [2048, 3072)  qh: per row 64 bytes; lane c's four words (word h*2 + is = qh bytes 32h + 16is + 4c..+3) at c*16
+//   [3072, 3328)  the 16 int8 sub-block scales of each row
+//   [3328, 3360)  the fp16 d of each row
+// Sub-block j (16 values 16j..16j+15: half h = j/8, quarter k = (j/2)%4, is = j%2) is one m16n8k16 integer MMA whose
+// A bytes are the 6-bit codes q (u8: ql nibble k/2, qh bits 2k..2k+1), B the activation digits; the sub-block scale
+// is applied in integers, d and the digit unit in fp32, and the -32 offset of the codes as
+// -32 * d * sum_j sc_j * sum16_j, one f16 MMA pair (hi, lo) over the 16-value sums.
+constexpr int Q6_TILE = Q6K_TILE;
+constexpr int Q6_QH = 2048, Q6_SC = 3072, Q6_D = 3328;
+
+template <int NC> struct Q6Layout {
+    static constexpr int X_OFF = (Q6_TILE + 127) / 128 * 128;   // 3456
+    static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;
+    static constexpr int TX = Q6_TILE + NC * XP_COL;
+    static constexpr int STAGES = 2;
+    static constexpr int SMEM = 8 * STAGES * STAGE;
+};
+
+__device__ __forceinline__ void imma16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+// int8 scale pair (bytes i0, i1 of w) as exact f16x2: (sc ^ 0x80) under the 0x64 exponent is 1152 + sc.
+__device__ __forceinline__ uint32_t sc_pair_h2(uint32_t w, uint32_t sel, __half2 k1152)
+{
+    return h2_bits(__hsub2(bits_h2(__byte_perm(w ^ 0x80808080u, 0x64646464u, sel)), k1152));
+}
+
+template <int NC>
+__global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ wt, int rows, int nsb,
+                                                    const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
+                                                    int* err)
+{
+    using LY = Q6Layout<NC>;
+    constexpr bool PACK = NC <= 2;
+    constexpr int ND = PACK ? 1 : 3;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
+    __shared__ float red[8][16][9];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int rt = blockIdx.x, r0 = rt * 16;
+    uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
+    const int njobs = nsb > warp ? (nsb - warp + 7) / 8 : 0;
+
+    pdl_trigger();
+    if (lane == 0) {
+        for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+        fence_proxy_async();
+    }
+    __syncwarp();
+    auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
+        uint8_t* st = ring + s * LY::STAGE;
+        mbar_expect_tx(&bars[warp][s], LY::TX);
+        bulk_load(st, wt + ((int64_t)rt * nsb + warp + 8 * j) * Q6_TILE, Q6_TILE, &bars[warp][s]);
+    };
+    auto issue_x = [&](int j, int s) {
+        const int sb = warp + 8 * j;
+        uint8_t* st = ring + s * LY::STAGE;
+#pragma unroll
+        for (int n = 0; n < NC; ++n)
+            bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
+    };
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_w(j, j);
+    pdl_wait();
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
+
+    const bool b_ok = PACK ? g < 3 * NC : g < NC;
+    const int b_off = LY::X_OFF + (PACK ? (g / 3) * XP_COL + (g % 3) * XP_DIGIT : g * XP_COL);
+    int e_col[2], e_dig[2];
+    bool e_ok[2];
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+        const int nn = 2 * c + k2;
+        e_col[k2] = PACK ? nn / 3 : nn;
+        e_dig[k2] = PACK ? nn % 3 : 0;
+        e_ok[k2] = PACK ? nn < 3 * NC : nn < NC;
+    }
+    const bool m_ok0 = 2 * c < NC, m_ok1 = 2 * c + 1 < NC;
+    // scale bytes 2c, 2c+1 (and 2c+8, 2c+9 from the second word pair) of a row's 16 scales
+    const uint32_t ssel = (uint32_t)((2 * c) & 3) | (4u << 4) | ((uint32_t)((2 * c + 1) & 3) << 8) | (4u << 12);
+    const __half2 k1152 = __float2half2_rn(1152.f);
+    const int par = (g & 1) << 4;           // odd rows keep their ql halves swapped
+
+    float facc[ND][4] = {};
+    float macc[4] = {};
+    for (int j = 0; j < njobs; ++j) {
+        const int s = j % LY::STAGES;
+        const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
+        const uint8_t* st = ring + s * LY::STAGE;
+        if (ok) {
+            uint32_t qa[8], qb[8], ha[4], hb[4];
+            {
+                const uint8_t* la = st + g * 128 + c * 32;
+                const uint8_t* lb = st + (g + 8) * 128 + c * 32;
+                const uint4 a_lo = lds128(la + par), a_hi = lds128(la + (par ^ 16));
+                const uint4 b_lo = lds128(lb + par), b_hi = lds128(lb + (par ^ 16));
+                qa[0] = a_lo.x; qa[1] = a_lo.y; qa[2] = a_lo.z; qa[3] = a_lo.w;
+                qa[4] = a_hi.x; qa[5] = a_hi.y; qa[6] = a_hi.z; qa[7] = a_hi.w;
+                qb[0] = b_lo.x; qb[1] = b_lo.y; qb[2] = b_lo.z; qb[3] = b_lo.w;
+                qb[4] = b_hi.x; qb[5] = b_hi.y; qb[6] = b_hi.z; qb[7] = b_hi.w;
+                const uint4 h0 = lds128(st + Q6_QH + g * 64 + c * 16), h1 = lds128(st + Q6_QH + (g + 8) * 64 + c * 16);
+                ha[0] = h0.x; ha[1] = h0.y; ha[2] = h0.z; ha[3] = h0.w;
+                hb[0] = h1.x; hb[1] = h1.y; hb[2] = h1.z; hb[3] = h1.w;
+            }
+            const uint4 sa = lds128(st + Q6_SC + g * 16), sb4 = lds128(st + Q6_SC + (g + 8) * 16);
+            const uint32_t swa[4] = {sa.x, sa.y, sa.z, sa.w}, swb[4] = {sb4.x, sb4.y, sb4.z, sb4.w};
+            int acc[ND][4] = {};
+#pragma unroll
+            for (int sbj = 0; sbj < 16; ++sbj) {
+                const int h = sbj >> 3, kq = (sbj >> 1) & 3, is = sbj & 1;
+                const int wi = h * 4 + (kq & 1) * 2 + is, hi = h * 2 + is;
+                const int nsh = 4 * (kq >> 1), hsh = 2 * kq;
+                const uint32_t a0 = ((qa[wi] >> nsh) & 0x0F0F0F0Fu) | (((ha[hi] >> hsh) & 0x03030303u) << 4);
+                const uint32_t a1 = ((qb[wi] >> nsh) & 0x0F0F0F0Fu) | (((hb[hi] >> hsh) & 0x03030303u) << 4);
+                const int s0 = (int)(int8_t)((swa[sbj >> 2] >> (8 * (sbj & 3))) & 0xFFu);
+                const int s1 = (int)(int8_t)((swb[sbj >> 2] >> (8 * (sbj & 3))) & 0xFFu);
+#pragma unroll
+                for (int d = 0; d < ND; ++d) {
+                    const uint32_t b = b_ok ? *reinterpret_cast<const uint32_t*>(st + b_off + d * XP_DIGIT + 16 * sbj + 4 * c) : 0u;
+                    int D[4];
+                    imma16816(D, a0, a1, b);
+                    acc[d][0] += s0 * D[0];
+                    acc[d][1] += s0 * D[1];
+                    acc[d][2] += s1 * D[2];
+                    acc[d][3] += s1 * D[3];
+                }
+            }
+            const float dd0 = h2f_(*reinterpret_cast<const uint16_t*>(st + Q6_D + 2 * g));
+            const float dd1 = h2f_(*reinterpret_cast<const uint16_t*>(st + Q6_D + 2 * (g + 8)));
+#pragma unroll
+            for (int k2 = 0; k2 < 2; ++k2) {
+                const float unit = e_ok[k2] ? *reinterpret_cast<const float*>(st + LY::X_OFF + e_col[k2] * XP_COL + XP_REC + 32) : 0.f;
+#pragma unroll
+                for (int d = 0; d < ND; ++d) {
+                    const int dig = PACK ? e_dig[k2] : d;
+                    const float f = unit * (dig == 0 ? 16384.f : dig == 1 ? 128.f : 1.f);
+                    facc[d][k2] = fmaf((float)acc[d][k2], dd0 * f, facc[d][k2]);
+                    facc[d][k2 + 2] = fmaf((float)acc[d][k2 + 2], dd1 * f, facc[d][k2 + 2]);
+                }
+            }
+            // offset term: sum_j sc_j * sum16_j, A = the scales of sub-blocks 2c, 2c+1 (k slots 2c, 2c+1) and
+            // 2c+8, 2c+9 (slots 2c+8, 2c+9), B = the hi sums, then the lo sums, of the lane's column
+            const bool hi_c = c >= 2;           // scales 2c, 2c+1 sit in word c/2, scales 2c+8, 2c+9 in word 2 + c/2
+            const uint32_t wA0 = hi_c ? sa.y : sa.x, wA1 = hi_c ? sa.w : sa.z;
+            const uint32_t wB0 = hi_c ? sb4.y : sb4.x, wB1 = hi_c ? sb4.w : sb4.z;
+            const uint32_t p00 = sc_pair_h2(wA0, ssel, k1152), p01 = sc_pair_h2(wA1, ssel, k1152);
+            const uint32_t p10 = sc_pair_h2(wB0, ssel, k1152), p11 = sc_pair_h2(wB1, ssel, k1152);
+            const uint4 bs = g < NC ? lds128(st + LY::X_OFF + g * XP_COL + XP_REC + 4 * (XP_S16 + 4 * c)) : make_uint4(0u, 0u, 0u, 0u);
+            float dn[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(dn, p00, p10, p01, p11, bs.x, bs.y);
+            mma16816(dn, p00, p10, p01, p11, bs.z, bs.w);
+            const float mu0 = m_ok0 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c) * XP_COL + XP_REC + 32) * 32768.f : 0.f;
+            const float mu1 = m_ok1 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c + 1) * XP_COL + XP_REC + 32) * 32768.f : 0.f;
+            macc[0] = fmaf(dn[0], dd0 * mu0, macc[0]);
+            macc[1] = fmaf(dn[1], dd0 * mu1, macc[1]);
+            macc[2] = fmaf(dn[2], dd1 * mu0, macc[2]);
+            macc[3] = fmaf(dn[3], dd1 * mu1, macc[3]);
+        }
+        __syncwarp();
+        if (lane == 0 && j + LY::STAGES < njobs) {
+            fence_proxy_async();
+            issue_w(j + LY::STAGES, s);
+            issue_x(j + LY::STAGES, s);
+        }
+    }
+    if (PACK) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][g + 8 * (e >> 1)][2 * c + (e & 1)] = facc[0][e];
+        if (c == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[warp][g + 8 * (e >> 1)][6 + (e & 1)] = macc[e];
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
+            if (col < NC) red[warp][row][col] = ((facc[0][e] + facc[ND > 1 ? 1 : 0][e]) + facc[ND > 2 ? 2 : 0][e]) - macc[e];
+        }
+    }
+    __syncthreads();
+    const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
+    if (col < NC && rl < 16 && r0 + rl < rows) {
+        float sum = 0.f;
+#pragma unroll
+        for (int wv = 0; wv < 8; ++wv) {
+            const float v = PACK ? ((red[wv][rl][3 * col] + red[wv][rl][3 * col + 1]) + red[wv][rl][3 * col + 2]) - red[wv][rl][6 + col]
+                                 : red[wv][rl][col];
+            sum += v;
+        }
+        y[(int64_t)col * ldy + r0 + rl] = sum;
+    }
+}
+
+// Repacks rows [0, rows) of a Q6_K matrix (row_bytes apart, nsb superblocks each) into the tile layout above; rows past
+// the end of the last tile are zero. One CTA per tile.
+__global__ void k_q6k_tile(const uint8_t* __restrict__ src, int rows, int nsb, int64_t row_bytes,
+                           uint8_t* __restrict__ dst)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int sb = blockIdx.x, rt = blockIdx.y;
+    uint8_t* out = dst + ((int64_t)rt * nsb + sb) * Q6_TILE;
+    for (int i = threadIdx.x; i < Q6_TILE; i += blockDim.x) {
+        int r, off;
+        if (i < Q6_QH) {
+            r = i >> 7;
+            const int pidx = i & 127, c = pidx >> 5, q = (pidx & 31) ^ ((r & 1) << 4);
+            const int wi = q >> 2, b = q & 3, h = wi >> 2, kk = (wi >> 1) & 1, is = wi & 1;
+            off = 64 * h + 32 * kk + 16 * is + 4 * c + b;
+        } else if (i < Q6_SC) {
+            r = (i - Q6_QH) >> 6;
+            const int pidx = (i - Q6_QH) & 63, c = pidx >> 4, q = pidx & 15;
+            const int wi = q >> 2, b = q & 3, h = wi >> 1, is = wi & 1;
+            off = 128 + 32 * h + 16 * is + 4 * c + b;
+        } else if (i < Q6_D) {
+            r = (i - Q6_SC) >> 4;
+            off = 192 + ((i - Q6_SC) & 15);
+        } else {
+            r = (i - Q6_D) >> 1;
+            off = 208 + ((i - Q6_D) & 1);
+        }
+        const int row = rt * 16 + r;
+        out[i] = row < rows ? src[(int64_t)row * row_bytes + (int64_t)sb * 210 + off] : (uint8_t)0;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------------------------
 size_t xprep_bytes(int cols, int nc) { return xprep_bytes_c(cols, nc); }
@@ -491,42 +731,21 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
     out->valid = true;
 }
 
-template <int NC, int ST>
-static void launch_q4k_st(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                          int* err, cudaStream_t s)
+template <int NC>
+static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                       int* err, cudaStream_t s)
 {
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC, ST>::SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC, 2>::SMEM));
         attr[dev] = true;
     }
     const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(map.bytes);
-    launch(k_mmv_q4k<NC, ST>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC, ST>::SMEM, s, m, row_base,
+    launch(k_mmv_q4k<NC, 2>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC, 2>::SMEM, s, m, row_base,
            rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
-}
-
-static int q4k_stages()
-{
-    static int st = [] {
-        const char* e = getenv("WL_Q4K_STAGES");
-        const int v = e ? atoi(e) : 2;
-        return v >= 2 && v <= 4 ? v : 2;
-    }();
-    return st;
-}
-
-template <int NC>
-static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                       int* err, cudaStream_t s)
-{
-    switch (NC <= 2 ? q4k_stages() : 2) {
-    case 3: launch_q4k_st<NC, 3>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 4: launch_q4k_st<NC, 4>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    default: launch_q4k_st<NC, 2>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    }
 }
 
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y, int64_t ldy,
@@ -543,6 +762,51 @@ void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols
     case 6: launch_q4k<6>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
     case 7: launch_q4k<7>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
     default: launch_q4k<8>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
+    }
+}
+
+
+int64_t q6k_tile_bytes(int rows, int cols) { return (int64_t)((rows + 15) / 16) * (cols / 256) * Q6_TILE; }
+
+bool q6k_tiles_supported(int type, int cols) { return type == 14 && cols % 256 == 0; }
+
+void q6k_tile(const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s)
+{
+    if (cols % 256 != 0 || row_bytes < (int64_t)(cols / 256) * 210) WL_THROW(WL_EINVAL, "q6k_tile: bad shape");
+    if (rows <= 0) return;
+    launch(k_q6k_tile, dim3(cols / 256, (rows + 15) / 16), dim3(256), 0, s, w, rows, cols / 256, row_bytes, tiles);
+    note_launch();
+}
+
+template <int NC>
+static void launch_q6k(const uint8_t* tiles, int rows, int nsb, const XPrep& p, float* y, int64_t ldy, int* err,
+                       cudaStream_t s)
+{
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        WL_CUDA(cudaFuncSetAttribute(k_mmv_q6k<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Layout<NC>::SMEM));
+        attr[dev] = true;
+    }
+    launch(k_mmv_q6k<NC>, dim3((rows + 15) / 16), dim3(256), Q6Layout<NC>::SMEM, s, tiles, rows, nsb,
+           (const uint8_t*)p.blocks, y, ldy, err);
+    note_launch();
+}
+
+void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s)
+{
+    if ((uintptr_t)tiles % 16 != 0) WL_THROW(WL_EINVAL, "matvec_q6k: tiles must be 16-byte aligned");
+    const int nsb = cols / 256;
+    switch (p.nc) {
+    case 1: launch_q6k<1>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 2: launch_q6k<2>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 3: launch_q6k<3>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 4: launch_q6k<4>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 5: launch_q6k<5>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 6: launch_q6k<6>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 7: launch_q6k<7>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    default: launch_q6k<8>(tiles, rows, nsb, p, y, ldy, err, s); break;
     }
 }
 

@@ -502,7 +502,8 @@ void Model::ensure_workspace(int T, int logit_rows)
 void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
 {
     (void)path;
-    if (w.map.valid && xprep_buf_) {
+    const bool q6 = w.tiles != nullptr && w.row_base % 16 == 0;
+    if ((w.map.valid || q6) && xprep_buf_) {
         for (int c0 = 0; c0 < T; c0 += 8) {
             const int nc = std::min(8, T - c0);
             const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
@@ -514,7 +515,11 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
-            k::matvec_mma(w.type, w.map, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
+            if (q6)
+                k::matvec_q6k(w.tiles + (int64_t)(w.row_base / 16) * (w.cols / 256) * k::Q6K_TILE, w.rows, w.cols, p,
+                              y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
+            else
+                k::matvec_mma(w.type, w.map, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;
@@ -569,6 +574,15 @@ void Model::build_maps()
     auto mk = [&](Weight& w) {
         if (w.present() && k::mma_supported(w.type, w.d, w.row_bytes, w.cols))
             k::make_weight_map(w.type, w.d, (int64_t)w.rows * w.experts, w.row_bytes, &w.map);
+        // Q6_K: a tile-major copy (expert slices must start on a tile)
+        if (w.present() && !w.tiles && k::q6k_tiles_supported(w.type, w.cols) && (w.experts == 1 || w.rows % 16 == 0)) {
+            const int total = w.rows * w.experts;
+            void* t = nullptr;
+            WL_CUDA(cudaMalloc(&t, (size_t)k::q6k_tile_bytes(total, w.cols)));
+            extra_allocs_.push_back(t);
+            w.tiles = (uint8_t*)t;
+            k::q6k_tile(w.d, total, w.cols, w.row_bytes, w.tiles, stream_);
+        }
     };
     for (LayerW& L : L_)
         for (Weight* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down, &L.router, &L.gate_exps, &L.up_exps,
@@ -750,14 +764,18 @@ void Model::head(int T, int first)
     const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
     prep_x_ = nullptr;
     if (k::norm_prep_supported(E)) {
+        const bool prep = (output_.map.valid || output_.tiles) && n <= 8 && xprep_buf_;
+        k::XPrep p{};
+        if (prep) p = k::xprep_view(xprep_buf_, E, n);
         k::norm_prep(x_ + (int64_t)first * E, pending_residual_ ? o_ + (int64_t)first * E : nullptr, rs, n, E,
-                     out_norm_.d, c_.rms_eps, xn_, nullptr, stream_);
+                     out_norm_.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_);
+        if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = n; }
     } else {
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
         k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
     }
     pending_residual_ = false;
-    matmul(output_, xn_, n, logits_);
+    matmul(output_, xn_, n, logits_, 0, true);
     if (c_.logit_scale != 0.f) k::scale(logits_, 1.f / c_.logit_scale, (int64_t)n * c_.vocab, stream_);
 }
 

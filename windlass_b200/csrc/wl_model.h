@@ -22,6 +22,7 @@ struct Weight {
     uint8_t* d = nullptr;
     k::WeightMap map;            // TMA map over all rows of all experts, for formats with a tensor-core matvec
     int row_base = 0;            // first row of this view inside the map (an expert slice)
+    uint8_t* tiles = nullptr;    // Q6_K repacked into 16-row tiles for the tensor-core matvec (all experts)
     bool present() const { return d != nullptr; }
     const uint8_t* expert(int e) const { return d + (int64_t)e * rows * row_bytes; }
 };

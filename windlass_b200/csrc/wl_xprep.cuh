@@ -2,10 +2,11 @@
 // activations in that form (k_xprep, and the fused swiglu and attention-combine kernels).
 //
 // Layout of the XP_COL-byte block: three planes of signed 8-bit digits of the 256 values in natural order (pitch
-// XP_DIGIT; 32 zero pad bytes each), then at XP_REC four (hi pair, lo pair) f16x2 words holding the sums of the eight
-// 32-value sub-blocks, the float unit of the digits, and zeros up to XP_COL. X = round(x * 2^(20-e)) (|X| <= 2^20, e
+// XP_DIGIT; 32 zero pad bytes each), then at XP_REC a record of f16 hi/lo sums of the 32-value and the 16-value
+// sub-blocks and the float unit of the digits (word map below). X = round(x * 2^(20-e)) (|X| <= 2^20, e
 // the exponent of the superblock's largest magnitude) is split into balanced base-128 digits X = X0*2^14 + X1*2^7 +
 // X2, each in [-64, 64]. The sums are taken at 2^(10-e), where they fit f16 with a hi/lo split good to 2^-22.
+// The 16-value sums serve Q6_K (16-value sub-blocks), the 32-value sums Q4_K.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -15,6 +16,20 @@ namespace wl {
 namespace k {
 
 __device__ __forceinline__ uint32_t xp_h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Record words (32-bit, from XP_REC): 0..7 the 32-value sums as four (hi pair, lo pair) of sub-block pairs (2c, 2c+1);
+// 8 the digit unit; XP_S16..XP_S16+15 the 16-value sums, for lane c four words [hi(2c, 2c+1), hi(2c+8, 2c+9),
+// lo(2c, 2c+1), lo(2c+8, 2c+9)] (the B fragments of an m16n8k16 MMA over the 16 sub-blocks); the rest zero.
+constexpr int XP_S16 = 12;
+
+// f16 hi/lo split of two sums a, b into rec[hi_word] = (hi a, hi b), rec[lo_word] = (lo a, lo b).
+__device__ __forceinline__ void xp_store_pair(uint32_t* rec, int hi_word, int lo_word, float a, float b)
+{
+    const __half h0 = __float2half_rn(a), h1 = __float2half_rn(b);
+    const __half l0 = __float2half_rn(a - __half2float(h0)), l1 = __float2half_rn(b - __half2float(h1));
+    rec[hi_word] = xp_h2_bits(__halves2half2(h0, h1));
+    rec[lo_word] = xp_h2_bits(__halves2half2(l0, l1));
+}
 
 // Called by the 64 threads t = 0..63 of a 64-thread CTA (it synchronises the CTA); thread t holds values 4t..4t+3.
 // scratch: two floats of shared memory.
@@ -51,22 +66,23 @@ __device__ __forceinline__ void xprep_sb(const float (&f)[4], int t, float* scra
 #pragma unroll
         for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * t) = 0u;
     }
-    // sum of the 32 values of this thread's sub-block: 8 consecutive threads
+    // sums of the 16 values (4 consecutive threads) and 32 values (8) of this thread's sub-blocks
     float s = (f[0] * sup + f[1] * sup) + (f[2] * sup + f[3] * sup);
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
+    const float s16 = s, s16_next = __shfl_down_sync(0xffffffffu, s, 4);
     s += __shfl_xor_sync(0xffffffffu, s, 4);
     const float s_next = __shfl_down_sync(0xffffffffu, s, 8);
     uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
-    if ((t & 15) == 0) {
-        const __half h0 = __float2half_rn(s), h1 = __float2half_rn(s_next);
-        const __half l0 = __float2half_rn(s - __half2float(h0)), l1 = __float2half_rn(s_next - __half2float(h1));
-        rec[2 * (t >> 4)] = xp_h2_bits(__halves2half2(h0, h1));
-        rec[2 * (t >> 4) + 1] = xp_h2_bits(__halves2half2(l0, l1));
+    if ((t & 15) == 0) xp_store_pair(rec, 2 * (t >> 4), 2 * (t >> 4) + 1, s, s_next);
+    if ((t & 7) == 0) {
+        const int p = t >> 3, c = p & 3, upper = p >> 2;
+        xp_store_pair(rec, XP_S16 + 4 * c + upper, XP_S16 + 4 * c + 2 + upper, s16, s16_next);
     }
     // digit unit (non-finite input makes it NaN, so the products are NaN as the fp32 dot would be), then zero padding
     if (t == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
-    if (t >= 9 && t < (XP_COL - XP_REC) / 4) rec[t] = 0u;
+    if (t >= 9 && t < XP_S16) rec[t] = 0u;
+    if (t >= XP_S16 + 16 && t < (XP_COL - XP_REC) / 4) rec[t] = 0u;
 }
 
 }  // namespace k
