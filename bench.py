@@ -142,8 +142,9 @@ def reference_arm(args):
 
 
 def sweep(args):
-    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the kernel time (CUDA
-    events on the launching stream, averaged over rotating weight copies whose total exceeds L2) and the weight
+    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the time of one wl_matvec
+    call (its activation prep and matvec kernels; for Q6_K also the per-call weight repack), from CUDA events around
+    replays of a CUDA graph of `iters` calls over rotating weight copies whose total exceeds L2, and the weight
     bandwidth (b <= 8) or TFLOP/s (b >= 64). One JSON line with the whole table."""
     import ctypes as C
     import numpy as np
@@ -179,23 +180,33 @@ def sweep(args):
             y = torch.empty(b, n, device="cuda")
             def run(i):
                 w = ws[i % copies]
+                cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
                 if b <= 8:
                     st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
-                                     C.c_void_p(y.data_ptr()), C.c_void_p(stream.cuda_stream))
+                                     C.c_void_p(y.data_ptr()), cs)
                 else:
                     st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
-                                     C.c_void_p(y.data_ptr()), 0, C.c_void_p(stream.cuda_stream))
+                                     C.c_void_p(y.data_ptr()), 0, cs)
                 _lib.check(st)
             for i in range(max(args.warmup, 3)):
                 run(i)
             torch.cuda.synchronize()
+            # the calls are captured into one CUDA graph so that host launch overhead is not what gets timed
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(args.iters):
+                    run(i)
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = 5
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            for i in range(args.iters):
-                run(i)
+            for _ in range(reps):
+                graph.replay()
             e1.record(stream)
             torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / args.iters
+            ms = e0.elapsed_time(e1) / (reps * args.iters)
+            del graph
             alg = nbytes + 4 * b * 2 * n
             rows.append({"format": f, "batch": b, "us": ms * 1e3, "gbs": alg / (ms / 1e3) / 1e9,
                          "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,

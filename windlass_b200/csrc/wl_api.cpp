@@ -61,40 +61,26 @@ void* export_scratch(size_t bytes)
     return ptr[dev];
 }
 
-// The forward pass's matvec rule: the tensor-core kernel where the format and alignment allow (8 columns per
-// launch, activations prepared once per chunk), else the CUDA-core kernel. force_cuda_cores selects the latter.
+// The forward pass's matvec rule: the tensor-core kernel where the format allows (the weights repacked into tiles,
+// 8 columns per launch, activations prepared once per chunk), else the CUDA-core kernel. force_cuda_cores selects
+// the latter.
 void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, int ncols, float* y, bool force_cuda_cores,
                 cudaStream_t s)
 {
     const int64_t rb = wl::row_bytes_of(type, cols);
-    if (!force_cuda_cores && wl::k::mma_supported(type, w, rb, cols) && (uintptr_t)x % 16 == 0) {
-        // scratch: [error word | prepared activations]
-        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
-        int* err = (int*)scratch;
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
-        wl::k::WeightMap map;
-        wl::k::make_weight_map(type, w, rows, rb, &map);
-        for (int c0 = 0; c0 < ncols; c0 += 8) {
-            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
-            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
-            wl::k::xprep(x + (int64_t)c0 * cols, cols, cols, nc, p, s);
-            wl::k::matvec_mma(type, map, 0, rows, cols, p, y + (int64_t)c0 * rows, rows, err, s);
-        }
-        return;
-    }
-    if (!force_cuda_cores && wl::k::q6k_tiles_supported(type, cols) && (uintptr_t)x % 16 == 0) {
+    if (!force_cuda_cores && wl::k::tiles_supported(type, cols) && (uintptr_t)x % 16 == 0) {
         // scratch: [error word | prepared activations | the weights repacked into tiles]
         const size_t xb = (wl::k::xprep_bytes(cols, 8) + 255) / 256 * 256;
-        uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::q6k_tile_bytes(rows, cols));
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::tile_bytes(type, rows, cols));
         int* err = (int*)scratch;
         uint8_t* tiles = scratch + 256 + xb;
         WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
-        wl::k::q6k_tile(w, rows, cols, rb, tiles, s);
+        wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
         for (int c0 = 0; c0 < ncols; c0 += 8) {
             const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
             const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
             wl::k::xprep(x + (int64_t)c0 * cols, cols, cols, nc, p, s);
-            wl::k::matvec_q6k(tiles, rows, cols, p, y + (int64_t)c0 * rows, rows, err, s);
+            wl::k::matvec_tiles(type, tiles, 0, rows, cols, p, y + (int64_t)c0 * rows, rows, err, s);
         }
         return;
     }

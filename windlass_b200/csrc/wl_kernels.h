@@ -73,13 +73,15 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y,
                 int64_t ldy, int* err, cudaStream_t s);
 
-// Q6_K on the tensor cores: the weights repacked once into 16-row tiles (q6k_tile_bytes bytes, 16-byte aligned), then
-// y[t*ldy + r] = W[r] . x[t] from prepared activations (same contract as matvec).
-constexpr int Q6K_TILE = 3360;     // bytes of one tile: 16 rows x one 210-byte superblock
-bool q6k_tiles_supported(int type, int cols);
-int64_t q6k_tile_bytes(int rows, int cols);
-void q6k_tile(const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
-void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s);
+// Q4_K and Q6_K on the tensor cores from tile-major weights: each 16-row x one-superblock tile contiguous and laid
+// out for the kernel's fragment reads (made once by make_tiles, tile_bytes bytes, 16-byte aligned); then
+// y[t*ldy + r] = W[row_base + r] . x[t] from prepared activations (same contract as matvec), row_base a multiple of 16.
+constexpr int Q6K_TILE = 3360;     // bytes of one Q6_K tile: 16 rows x one 210-byte superblock
+bool tiles_supported(int type, int cols);
+int64_t tile_bytes(int type, int rows, int cols);
+void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
+void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
+                  int64_t ldy, int* err, cudaStream_t s);
 
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);

@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <cstring>
 #include <mutex>
 #include "wl_common.h"
 #include "wl_kernels.h"
@@ -219,12 +220,16 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
 // ------------------------------------------------------------------------------------------------------------------
 constexpr int Q4_ROWS = 16;                     // rows per CTA: one m16 row group, shared by the eight warps
 constexpr int Q4_TILE = Q4_ROWS * 144;          // weight bytes per stage
+// Tile-major Q4_K (k_q4k_tile): per tile of 16 rows x one superblock, the 16 rows' 16-byte headers (d, dmin, scales),
+// then per 32-byte run r of codes 512 bytes in which lane (g, c) finds at lane*16 its 8 code bytes of row g and
+// then of row g+8 (raw bytes 16 + 32r + 8c ..+8), one conflict-free 16-byte read per run.
+constexpr int Q4_HDRS = Q4_ROWS * 16;
 
-template <int NC, int ST = 2> struct Q4Layout {
+template <int NC> struct Q4Layout {
     static constexpr int X_OFF = Q4_TILE;       // 2304, a multiple of 128
     static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;   // TMA destinations are 128-byte aligned
     static constexpr int TX = Q4_TILE + NC * XP_COL;                         // bytes the copies of one stage deliver
-    static constexpr int STAGES = ST;
+    static constexpr int STAGES = 2;
     static constexpr int SMEM = 8 * STAGES * STAGE;
 };
 
@@ -246,12 +251,13 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // Up to two columns, the 8 MMA columns hold (column, digit) pairs (one MMA per sub-block); from three columns on,
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
-template <int NC, int ST>
-__global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap, int row_base, int rows,
-                                                    int nsb, const uint8_t* __restrict__ xq, float* __restrict__ y,
-                                                    int64_t ldy, int* err)
+template <int NC, bool TILED>
+__global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
+                                                    const uint8_t* __restrict__ wt, int row_base, int rows, int nsb,
+                                                    const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
+                                                    int* err)
 {
-    using LY = Q4Layout<NC, ST>;
+    using LY = Q4Layout<NC>;
     constexpr bool PACK = NC <= 2;
     constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block
     extern __shared__ __align__(128) uint8_t smem[];
@@ -272,7 +278,11 @@ __global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_c
     auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
         uint8_t* st = ring + s * LY::STAGE;
         mbar_expect_tx(&bars[warp][s], LY::TX);
-        tma_load_2d(st, &wmap, (warp + 8 * j) * 144, row_base + r0, &bars[warp][s]);
+        if (TILED)
+            bulk_load(st, wt + ((int64_t)(row_base / Q4_ROWS + blockIdx.x) * nsb + warp + 8 * j) * Q4_TILE, Q4_TILE,
+                      &bars[warp][s]);
+        else
+            tma_load_2d(st, &wmap, (warp + 8 * j) * 144, row_base + r0, &bars[warp][s]);
     };
     auto issue_x = [&](int j, int s) {      // prepared activations of the same superblock, on the same barrier
         const int sb = warp + 8 * j;
@@ -312,8 +322,8 @@ __global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_c
         const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
         const uint8_t* st = ring + s * LY::STAGE;
         if (ok) {
-            const uint8_t* row0 = st + g * 144;
-            const uint8_t* row1 = st + (g + 8) * 144;
+            const uint8_t* row0 = st + g * (TILED ? 16 : 144);
+            const uint8_t* row1 = st + (g + 8) * (TILED ? 16 : 144);
             const uint4 h0 = lds128(row0), h1 = lds128(row1);
             // ScaleMinK4 for all eight sub-blocks at once: scales and mins as bytes
             const uint32_t s0lo = h0.y & 0x3F3F3F3Fu, s0hi = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
@@ -321,8 +331,15 @@ __global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_c
             int acc_lo[ND][4] = {}, acc_hi[ND][4] = {};
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                const uint2 w0 = lds64(row0 + 16 + 32 * r + 8 * c);
-                const uint2 w1 = lds64(row1 + 16 + 32 * r + 8 * c);
+                uint2 w0, w1;
+                if (TILED) {
+                    const uint4 wv = lds128(st + Q4_HDRS + r * 512 + lane * 16);
+                    w0 = make_uint2(wv.x, wv.y);
+                    w1 = make_uint2(wv.z, wv.w);
+                } else {
+                    w0 = lds64(row0 + 16 + 32 * r + 8 * c);
+                    w1 = lds64(row1 + 16 + 32 * r + 8 * c);
+                }
                 const uint32_t sw0 = r < 2 ? s0lo : s0hi, sw1 = r < 2 ? s1lo : s1hi;
                 const int kb = (2 * r) & 3;
                 const int sl0 = (int)((sw0 >> (8 * kb)) & 0xFFu), sh0 = (int)((sw0 >> (8 * kb + 8)) & 0xFFu);
@@ -412,6 +429,30 @@ __global__ void __launch_bounds__(256, ST <= 2 ? 3 : 2) k_mmv_q4k(const __grid_c
             sum += v;
         }
         y[(int64_t)col * ldy + r0 + rl] = sum;
+    }
+}
+
+// Repacks rows [0, rows) of a Q4_K matrix into the tile-major layout above; rows past the end are zero. One CTA per tile.
+__global__ void k_q4k_tile(const uint8_t* __restrict__ src, int rows, int nsb, int64_t row_bytes,
+                           uint8_t* __restrict__ dst)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int sb = blockIdx.x, rt = blockIdx.y;
+    uint8_t* out = dst + ((int64_t)rt * nsb + sb) * Q4_TILE;
+    for (int i = threadIdx.x; i < Q4_TILE; i += blockDim.x) {
+        int r, off;
+        if (i < Q4_HDRS) {
+            r = i >> 4;
+            off = i & 15;
+        } else {
+            const int j = i - Q4_HDRS, run = j >> 9, ln = (j & 511) >> 4, b = j & 15;
+            const int gg = ln >> 2, cc = ln & 3;
+            r = b < 8 ? gg : gg + 8;
+            off = 16 + 32 * run + 8 * cc + (b & 7);
+        }
+        const int row = rt * Q4_ROWS + r;
+        out[i] = row < rows ? src[(int64_t)row * row_bytes + (int64_t)sb * 144 + off] : (uint8_t)0;
     }
 }
 
@@ -731,50 +772,62 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
     out->valid = true;
 }
 
-template <int NC>
-static void launch_q4k(const WeightMap& map, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                       int* err, cudaStream_t s)
+template <int NC, bool TILED>
+static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
+                       float* y, int64_t ldy, int* err, cudaStream_t s)
 {
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC, 2>::SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
         attr[dev] = true;
     }
-    const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(map.bytes);
-    launch(k_mmv_q4k<NC, 2>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC, 2>::SMEM, s, m, row_base,
-           rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
+    launch(k_mmv_q4k<NC, TILED>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles,
+           row_base, rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
+}
+
+template <bool TILED>
+static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
+                         float* y, int64_t ldy, int* err, cudaStream_t s)
+{
+    switch (p.nc) {
+    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    }
 }
 
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y, int64_t ldy,
                 int* err, cudaStream_t s)
 {
     (void)type;
-    const int nsb = cols / 256;
-    switch (p.nc) {
-    case 1: launch_q4k<1>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 2: launch_q4k<2>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 3: launch_q4k<3>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 4: launch_q4k<4>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 5: launch_q4k<5>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 6: launch_q4k<6>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 7: launch_q4k<7>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    default: launch_q4k<8>(map, row_base, rows, nsb, p, y, ldy, err, s); break;
-    }
+    dispatch_q4k<false>(*reinterpret_cast<const CUtensorMap*>(map.bytes), nullptr, row_base, rows, cols / 256, p, y,
+                        ldy, err, s);
 }
 
 
-int64_t q6k_tile_bytes(int rows, int cols) { return (int64_t)((rows + 15) / 16) * (cols / 256) * Q6_TILE; }
+bool tiles_supported(int type, int cols) { return (type == 12 || type == 14) && cols % 256 == 0; }
 
-bool q6k_tiles_supported(int type, int cols) { return type == 14 && cols % 256 == 0; }
-
-void q6k_tile(const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s)
+int64_t tile_bytes(int type, int rows, int cols)
 {
-    if (cols % 256 != 0 || row_bytes < (int64_t)(cols / 256) * 210) WL_THROW(WL_EINVAL, "q6k_tile: bad shape");
+    return (int64_t)((rows + 15) / 16) * (cols / 256) * (type == 12 ? Q4_TILE : Q6_TILE);
+}
+
+void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s)
+{
+    if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "make_tiles: no tile layout for this type");
+    if (row_bytes < (int64_t)(cols / 256) * (type == 12 ? 144 : 210)) WL_THROW(WL_EINVAL, "make_tiles: bad row size");
     if (rows <= 0) return;
-    launch(k_q6k_tile, dim3(cols / 256, (rows + 15) / 16), dim3(256), 0, s, w, rows, cols / 256, row_bytes, tiles);
+    const dim3 grid(cols / 256, (rows + 15) / 16);
+    if (type == 12) launch(k_q4k_tile, grid, dim3(256), 0, s, w, rows, cols / 256, row_bytes, tiles);
+    else launch(k_q6k_tile, grid, dim3(256), 0, s, w, rows, cols / 256, row_bytes, tiles);
     note_launch();
 }
 
@@ -794,9 +847,9 @@ static void launch_q6k(const uint8_t* tiles, int rows, int nsb, const XPrep& p, 
     note_launch();
 }
 
-void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s)
+static void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err,
+                       cudaStream_t s)
 {
-    if ((uintptr_t)tiles % 16 != 0) WL_THROW(WL_EINVAL, "matvec_q6k: tiles must be 16-byte aligned");
     const int nsb = cols / 256;
     switch (p.nc) {
     case 1: launch_q6k<1>(tiles, rows, nsb, p, y, ldy, err, s); break;
@@ -807,6 +860,20 @@ void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float*
     case 6: launch_q6k<6>(tiles, rows, nsb, p, y, ldy, err, s); break;
     case 7: launch_q6k<7>(tiles, rows, nsb, p, y, ldy, err, s); break;
     default: launch_q6k<8>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    }
+}
+
+void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
+                  int64_t ldy, int* err, cudaStream_t s)
+{
+    if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
+    if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
+    if (type == 12) {
+        CUtensorMap none;
+        memset(&none, 0, sizeof none);
+        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s);
+    } else {
+        matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }
 }
 

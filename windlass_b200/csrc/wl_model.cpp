@@ -502,8 +502,7 @@ void Model::ensure_workspace(int T, int logit_rows)
 void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
 {
     (void)path;
-    const bool q6 = w.tiles != nullptr && w.row_base % 16 == 0;
-    if ((w.map.valid || q6) && xprep_buf_) {
+    if (w.tiles && w.row_base % 16 == 0 && xprep_buf_) {
         for (int c0 = 0; c0 < T; c0 += 8) {
             const int nc = std::min(8, T - c0);
             const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
@@ -515,11 +514,8 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
-            if (q6)
-                k::matvec_q6k(w.tiles + (int64_t)(w.row_base / 16) * (w.cols / 256) * k::Q6K_TILE, w.rows, w.cols, p,
-                              y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
-            else
-                k::matvec_mma(w.type, w.map, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_, stream_);
+            k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_,
+                            stream_);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;
@@ -572,16 +568,14 @@ static Weight slice(const Weight& w, int e)
 void Model::build_maps()
 {
     auto mk = [&](Weight& w) {
-        if (w.present() && k::mma_supported(w.type, w.d, w.row_bytes, w.cols))
-            k::make_weight_map(w.type, w.d, (int64_t)w.rows * w.experts, w.row_bytes, &w.map);
-        // Q6_K: a tile-major copy (expert slices must start on a tile)
-        if (w.present() && !w.tiles && k::q6k_tiles_supported(w.type, w.cols) && (w.experts == 1 || w.rows % 16 == 0)) {
+        // Q4_K / Q6_K: a tile-major copy for the tensor-core matvec (expert slices must start on a tile)
+        if (w.present() && !w.tiles && k::tiles_supported(w.type, w.cols) && (w.experts == 1 || w.rows % 16 == 0)) {
             const int total = w.rows * w.experts;
             void* t = nullptr;
-            WL_CUDA(cudaMalloc(&t, (size_t)k::q6k_tile_bytes(total, w.cols)));
+            WL_CUDA(cudaMalloc(&t, (size_t)k::tile_bytes(w.type, total, w.cols)));
             extra_allocs_.push_back(t);
             w.tiles = (uint8_t*)t;
-            k::q6k_tile(w.d, total, w.cols, w.row_bytes, w.tiles, stream_);
+            k::make_tiles(w.type, w.d, total, w.cols, w.row_bytes, w.tiles, stream_);
         }
     };
     for (LayerW& L : L_)
@@ -613,7 +607,7 @@ void Model::ffn_dense(const LayerW& L, int T)
     matmul(L.up, xn_, T, u_, 0, true);
     prep_x_ = nullptr;
     const int sm = profile_begin();
-    if (L.down.map.valid && T <= 8 && F % 256 == 0 && xprep_buf_) {
+    if (L.down.tiles && T <= 8 && F % 256 == 0 && xprep_buf_) {
         const k::XPrep p = k::xprep_view(xprep_buf_, F, T);
         k::swiglu_prep(g_, u_, T, F, p, stream_);
         prep_x_ = g_; prep_cols_ = F; prep_nc_ = T;
@@ -684,7 +678,7 @@ void Model::layer(int l, int T, int max_n)
         WL_CUDA(cudaMemcpyAsync(xn_, x_, sizeof(float) * n, cudaMemcpyDeviceToDevice, stream_));
         prep_x_ = nullptr;
     } else {
-        pre_norm(T, L.attn_norm, L.q.map.valid);
+        pre_norm(T, L.attn_norm, L.q.tiles != nullptr);
     }
     matmul(L.q, xn_, T, q_, 0, true);
     matmul(L.k, xn_, T, k_, 0, true);
@@ -705,7 +699,7 @@ void Model::layer(int l, int T, int max_n)
     profile_end(rm, WL_PROFILE_ROPE, 0.0);
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
     // the o matvec's activations come out of the attention combine when it can prepare them
-    const bool want_prep = L.o.map.valid && T <= 8 && xprep_buf_;
+    const bool want_prep = L.o.tiles && T <= 8 && xprep_buf_;
     k::XPrep ap{};
     if (want_prep) ap = k::xprep_view(xprep_buf_, QD, T);
     const int mark = profile_begin();
@@ -722,7 +716,7 @@ void Model::layer(int l, int T, int max_n)
         prep_x_ = nullptr;
     } else {
         pending_residual_ = true;           // x += o happens inside the ffn norm
-        pre_norm(T, L.ffn_norm, L.moe ? false : L.gate.map.valid);
+        pre_norm(T, L.ffn_norm, L.moe ? false : L.gate.tiles != nullptr);
     }
     if (L.moe) ffn_moe(L, T);
     else ffn_dense(L, T);
@@ -764,7 +758,7 @@ void Model::head(int T, int first)
     const float rs = c_.residual_scale != 0.f ? c_.residual_scale : 1.f;
     prep_x_ = nullptr;
     if (k::norm_prep_supported(E)) {
-        const bool prep = (output_.map.valid || output_.tiles) && n <= 8 && xprep_buf_;
+        const bool prep = output_.tiles && n <= 8 && xprep_buf_;
         k::XPrep p{};
         if (prep) p = k::xprep_view(xprep_buf_, E, n);
         k::norm_prep(x_ + (int64_t)first * E, pending_residual_ ? o_ + (int64_t)first * E : nullptr, rs, n, E,

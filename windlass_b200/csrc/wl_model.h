@@ -20,9 +20,8 @@ struct Weight {
     int rows = 0, cols = 0, experts = 1;
     int64_t row_bytes = 0, bytes = 0;
     uint8_t* d = nullptr;
-    k::WeightMap map;            // TMA map over all rows of all experts, for formats with a tensor-core matvec
-    int row_base = 0;            // first row of this view inside the map (an expert slice)
-    uint8_t* tiles = nullptr;    // Q6_K repacked into 16-row tiles for the tensor-core matvec (all experts)
+    int row_base = 0;            // first row of this view inside the tiles (an expert slice)
+    uint8_t* tiles = nullptr;    // Q4_K / Q6_K repacked into 16-row tiles for the tensor-core matvec (all experts)
     bool present() const { return d != nullptr; }
     const uint8_t* expert(int e) const { return d + (int64_t)e * rows * row_bytes; }
 };
