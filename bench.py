@@ -142,8 +142,8 @@ def reference_arm(args):
 
 
 def sweep(args):
-    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the time of one wl_matvec
-    call (its activation prep and matvec kernels; for Q6_K also the per-call weight repack), from CUDA events around
+    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the time of one matvec call
+    (wl_matvec_tiles on weights repacked once for Q4_K/Q6_K, else wl_matvec: activation prep + matvec), from CUDA events around
     replays of a CUDA graph of `iters` calls over rotating weight copies whose total exceeds L2, and the weight
     bandwidth (b <= 8) or TFLOP/s (b >= 64). One JSON line with the whole table."""
     import ctypes as C
@@ -175,13 +175,27 @@ def sweep(args):
                 raw[:, 0], raw[:, 1] = 0x00, 0x1C          # fp16 0.0039
                 buf.copy_(torch.from_numpy(raw.reshape(-1)))
             ws.append(buf)
+        tiled = f in ("q4_K", "q6_K")
+        if tiled:       # the model's layout: weights repacked once into tiles, so no call repacks
+            tb = C.c_int64()
+            _lib.check(L.wl_tiles_size(t, n, n, C.byref(tb)))
+            tws = []
+            for w in ws:
+                tw = torch.empty(tb.value, dtype=torch.uint8, device="cuda")
+                _lib.check(L.wl_make_tiles(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(tw.data_ptr()),
+                                           C.c_void_p(stream.cuda_stream)))
+                tws.append(tw)
+            torch.cuda.synchronize()
         for b in batches:
             x = torch.randn(b, n, device="cuda")
             y = torch.empty(b, n, device="cuda")
             def run(i):
                 w = ws[i % copies]
                 cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-                if b <= 8:
+                if b <= 8 and tiled:
+                    st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), n, n, C.c_void_p(x.data_ptr()),
+                                           b, C.c_void_p(y.data_ptr()), cs)
+                elif b <= 8:
                     st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
                                      C.c_void_p(y.data_ptr()), cs)
                 else:

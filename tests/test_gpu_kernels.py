@@ -122,3 +122,31 @@ def test_config1_full_size_matvec(wl, oracle, tname):
         y = host(dy).reshape(ncols, n)[:, sample]
         want = x.astype(np.float64) @ dec.T
         assert rel_l2(y, want) <= 1e-4, (tname, ncols, rel_l2(y, want))
+
+
+@pytest.mark.parametrize("tname", ["q4_K", "q6_K"])
+def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
+    """wl_make_tiles + wl_matvec_tiles (the model's weight layout) against the reference dot products, and bit-equal
+    to wl_matvec (which repacks per call); ragged row count (not a multiple of 16)."""
+    O = oracle
+    t = O.TYPE_OF[tname]
+    L = wl.lib()
+    rows, cols, ncols = 75, 2048, 3
+    w = weights(O, tname, rows, cols, seed=11)
+    dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
+    x = np.random.default_rng(9).standard_normal((ncols, cols)).astype(np.float32)
+    dw, dx = dev(w), dev(x.reshape(-1))
+    nb = C.c_int64()
+    wl.check(L.wl_tiles_size(t, rows, cols, C.byref(nb)))
+    assert nb.value == (rows + 15) // 16 * (cols // 256) * (2304 if tname == "q4_K" else 3360)
+    tiles = empty(nb.value, "uint8")
+    wl.check(L.wl_make_tiles(t, ptr(dw), rows, cols, ptr(tiles), None))
+    dy = empty(ncols * rows)
+    wl.check(L.wl_matvec_tiles(t, ptr(tiles), rows, cols, ptr(dx), ncols, ptr(dy), None))
+    got = host(dy).reshape(ncols, rows)
+    want = x.astype(np.float64) @ dec.T
+    for c in range(ncols):
+        assert rel_l2(got[c], want[c]) <= 1e-4, (tname, c, rel_l2(got[c], want[c]))
+    assert np.array_equal(got, _matvec(wl, t, dw, rows, cols, x, ncols))
+    with pytest.raises(wl.NotSupportedError):
+        wl.check(L.wl_tiles_size(O.TYPE_OF["q8_0"], rows, cols, C.byref(nb)))

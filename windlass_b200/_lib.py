@@ -110,6 +110,9 @@ def lib():
         "wl_dequant": (I32, [I32, P, I64, P, P]),
         "wl_matvec": (I32, [I32, P, I32, I32, P, I32, P, P]),
         "wl_matvec_static": (I32, [I32, P, I32, I32, P, I32, P, P]),
+        "wl_tiles_size": (I32, [I32, I32, I32, C.POINTER(I64)]),
+        "wl_make_tiles": (I32, [I32, P, I32, I32, P, P]),
+        "wl_matvec_tiles": (I32, [I32, P, I32, I32, P, I32, P, P]),
         "wl_matmul": (I32, [I32, P, I32, I32, P, I32, P, I32, P]),
         "wl_synth_tensor": (I32, [I32, U64, C.c_uint32, I64, I64, F, F, P, P]),
         "wl_bench_decode": (I32, [P, P, I32, I32, C.POINTER(C.c_double)]),

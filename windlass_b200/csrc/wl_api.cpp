@@ -351,6 +351,53 @@ int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t 
     });
 }
 
+int32_t wl_tiles_size(int32_t type, int32_t rows, int32_t cols, int64_t* bytes)
+{
+    return guarded([&]() -> int32_t {
+        if (!bytes) return wl::fail(WL_EINVAL, "wl_tiles_size: bytes is required");
+        if (!wl::k::tiles_supported(type, cols)) return wl::fail(WL_EUNSUPPORTED, "wl_tiles_size: no tile layout for this type and width");
+        if (rows <= 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        *bytes = wl::k::tile_bytes(type, rows, cols);
+        return WL_OK;
+    });
+}
+
+int32_t wl_make_tiles(int32_t type, const void* dev_w, int32_t rows, int32_t cols, void* dev_tiles, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (!wl::k::tiles_supported(type, cols)) return wl::fail(WL_EUNSUPPORTED, "wl_make_tiles: no tile layout for this type and width");
+        if (rows <= 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_w || !dev_tiles) return wl::fail(WL_EINVAL, "wl_make_tiles: null pointer");
+        if ((uintptr_t)dev_tiles % 16 != 0) return wl::fail(WL_EINVAL, "wl_make_tiles: dev_tiles must be 16-byte aligned");
+        wl::k::make_tiles(type, (const uint8_t*)dev_w, rows, cols, wl::row_bytes_of(type, cols), (uint8_t*)dev_tiles,
+                          (cudaStream_t)stream);
+        return WL_OK;
+    });
+}
+
+int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
+                        int32_t ncols, float* dev_y, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (!wl::k::tiles_supported(type, cols)) return wl::fail(WL_EUNSUPPORTED, "wl_matvec_tiles: no tile layout for this type and width");
+        if (rows <= 0 || ncols <= 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_tiles || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matvec_tiles: null pointer");
+        if ((uintptr_t)dev_tiles % 16 != 0 || (uintptr_t)dev_x % 16 != 0)
+            return wl::fail(WL_EINVAL, "wl_matvec_tiles: dev_tiles and dev_x must be 16-byte aligned");
+        const cudaStream_t s = (cudaStream_t)stream;
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
+        int* err = (int*)scratch;
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        for (int c0 = 0; c0 < ncols; c0 += 8) {
+            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
+            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
+            wl::k::xprep(dev_x + (int64_t)c0 * cols, cols, cols, nc, p, s);
+            wl::k::matvec_tiles(type, (const uint8_t*)dev_tiles, 0, rows, cols, p, dev_y + (int64_t)c0 * rows, rows, err, s);
+        }
+        return WL_OK;
+    });
+}
+
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                   float* dev_y, int32_t path, void* stream)
 {

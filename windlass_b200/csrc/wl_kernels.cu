@@ -701,7 +701,6 @@ void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStr
 // S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order.
 constexpr int ATT_P = 64;           // positions per tile
 constexpr int ATT_THREADS = 128;
-constexpr int ATT_MAXG = 16;        // query heads per KV head
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 {

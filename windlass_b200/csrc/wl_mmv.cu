@@ -252,7 +252,7 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
 template <int NC, bool TILED>
-__global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt, int row_base, int rows, int nsb,
                                                     const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
                                                     int* err)
@@ -262,7 +262,6 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
     constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
-    __shared__ float red[8][Q4_ROWS][9];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int r0 = blockIdx.x * Q4_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
@@ -400,22 +399,21 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
             issue_x(j + LY::STAGES, s);
         }
     }
-    // per (row, column): ((plane 0 + plane 1) + plane 2) - min term, then the warps in order
+    // per (row, column): ((plane 0 + plane 1) + plane 2) - min term, then the warps in order. Each warp's partials
+    // go to the start of its own ring, whose stages it has finished with.
+    float* red = reinterpret_cast<float*>(ring);        // [Q4_ROWS][9]
     if (PACK) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int row = g + 8 * (e >> 1), k2 = e & 1;
-            red[warp][row][2 * c + k2] = facc[0][e];
-        }
+        for (int e = 0; e < 4; ++e) red[(g + 8 * (e >> 1)) * 9 + 2 * c + (e & 1)] = facc[0][e];
         if (c == 0) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) red[warp][g + 8 * (e >> 1)][6 + (e & 1)] = macc[e];
+            for (int e = 0; e < 4; ++e) red[(g + 8 * (e >> 1)) * 9 + 6 + (e & 1)] = macc[e];
         }
     } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
-            if (col < NC) red[warp][row][col] = ((facc[0][e] + facc[ND > 1 ? 1 : 0][e]) + facc[ND > 2 ? 2 : 0][e]) - macc[e];
+            if (col < NC) red[row * 9 + col] = ((facc[0][e] + facc[ND > 1 ? 1 : 0][e]) + facc[ND > 2 ? 2 : 0][e]) - macc[e];
         }
     }
     __syncthreads();
@@ -424,8 +422,8 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q4k(const __grid_constant__ CUte
         float sum = 0.f;
 #pragma unroll
         for (int wv = 0; wv < 8; ++wv) {
-            const float v = PACK ? ((red[wv][rl][3 * col] + red[wv][rl][3 * col + 1]) + red[wv][rl][3 * col + 2]) - red[wv][rl][6 + col]
-                                 : red[wv][rl][col];
+            const float* rw = reinterpret_cast<const float*>(smem + wv * LY::STAGES * LY::STAGE) + rl * 9;
+            const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
             sum += v;
         }
         y[(int64_t)col * ldy + r0 + rl] = sum;
