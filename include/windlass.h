@@ -65,9 +65,10 @@ typedef struct wl_options {
     int32_t device;          /* CUDA device ordinal */
     int32_t max_context;     /* positions per sequence; 0 = min(model context_length, 8192) (src/Engine.cs:26,62) */
     int32_t max_batch;       /* most rows in one wl_forward_batch (BatchPlan.MaxBatch = 64, src/Batch.cs:40) */
-    int32_t resident;        /* 1: every weight resident in HBM; 0: layers streamed from pinned host memory through
-                                two device slots (src/LayerStream.cs); -1: resident when the weights fit */
-    int32_t prefill_path;    /* T > 8 prompts: 0 auto, 1 fp32 CUDA cores, 2 bf16 tensor cores (tcgen05) */
+    int32_t resident;        /* 1 or -1: every weight resident in HBM. 0 would stream layers from pinned host
+                                memory (src/LayerStream.cs); that mode is not built and wl_open returns
+                                WL_EUNSUPPORTED */
+    int32_t prefill_path;    /* T > 8 prompts: 0 auto (tensor cores where the format has them), 1 fp32 CUDA cores */
     int32_t use_graphs;      /* 1: replay decode steps from captured CUDA graphs */
     int32_t reserved[9];
 } wl_options;
@@ -189,8 +190,8 @@ int32_t wl_tiles_size(int32_t type, int32_t rows, int32_t cols, int64_t* bytes);
 int32_t wl_make_tiles(int32_t type, const void* dev_w, int32_t rows, int32_t cols, void* dev_tiles, void* stream);
 int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
                         int32_t ncols, float* dev_y, void* stream);
-/* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 1 = fp32 CUDA cores, 2 = bf16 tensor
- * cores (tcgen05, fp32 accumulate), 0 = the model's default for T. */
+/* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 1 = fp32 CUDA cores, 0 or 2 = the
+ * model's default (the integer tensor-core matvec in 8-column chunks where the format has one). */
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                   float* dev_y, int32_t path, void* stream);
 /* Synthetic weight generator of wl_open_synthetic for one tensor (rows x cols of `type`: F32, F16, Q8_0, Q4_K or

@@ -47,6 +47,8 @@ void Model::init_device(const wl_options& opt)
     WL_CUDA(cudaSetDevice(device_));
     k::init_tables();
     WL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (opt.resident == 0)
+        WL_THROW(WL_EUNSUPPORTED, "Streaming layers from host memory (resident = 0) is not built; weights are kept in HBM.");
     max_batch_ = opt.max_batch > 0 ? opt.max_batch : 64;
     use_graphs_ = opt.use_graphs != 0;
     prefill_path_ = opt.prefill_path;
@@ -501,8 +503,9 @@ void Model::ensure_workspace(int T, int logit_rows)
 // reuse_x says x is the input of the previous matmul as well, so its prepared form can be reused.
 void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
 {
-    (void)path;
-    if (w.tiles && w.row_base % 16 == 0 && xprep_buf_) {
+    // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
+    const bool cuda_cores = path == 1 || (T > 8 && prefill_path_ == 1);
+    if (!cuda_cores && w.tiles && w.row_base % 16 == 0 && xprep_buf_) {
         for (int c0 = 0; c0 < T; c0 += 8) {
             const int nc = std::min(8, T - c0);
             const k::XPrep p = k::xprep_view(xprep_buf_, w.cols, nc);
