@@ -7,7 +7,9 @@ N(0, 0.02) decoder of that shape generated on the device (wl_open_synthetic; no 
 per step, which is far larger than the 126 MB L2, so no flush is needed between steps.
 
 - value: K device-resident decode steps (wl_bench_decode: no host copies) timed with CUDA events on the model's
-  stream, max over ranks; with N GPUs each rank runs its own replica (scaling "weak").
+  stream, max over ranks. With N GPUs (torchrun, one process per GPU) the one model is split over the N GPUs by
+  tensor parallelism (rows of q/k/v, gate/up and the head; columns of o and down; two NCCL all-reduces per layer
+  over NVLink), so the work per step is fixed and N only shortens it (scaling "strong").
 - e2e: the same steps through the public call a host makes (wl_forward with host token ids in and host logits out).
 - roofline: the dominant kernel (the Q4_K fused dequant-matvec), its algorithmic bytes over its CUDA-event time,
   recorded live in a second pass over the same steps with per-launch events.
@@ -260,30 +262,35 @@ def main():
     if args.sweep:
         return sweep(args)
 
+    import datetime
+
     import numpy as np
     import torch
-    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    from windlass_b200 import tp
+    rank, world, local = tp.env_ranks()
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
+        # host plumbing only (group id, barriers, max over ranks); the model's collectives are its own NCCL group
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
 
     def barrier():
+        torch.cuda.synchronize()
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
 
-    from windlass_b200.transformer import CudaTransformer, llama70b_spec
+    from windlass_b200.transformer import llama70b_spec
     spec = llama70b_spec(layers=args.layers)
     steps, warm, B = args.steps, args.warmup, args.batch
     ctx = args.prompt + 2 * (steps + warm) + 64
     t0 = time.perf_counter()
-    trace(f"opening synthetic model, {args.layers} layers, context {ctx}")
-    m = CudaTransformer(synthetic=spec, device=local, max_context=ctx)
+    trace(f"opening synthetic model, {args.layers} layers, context {ctx}, tensor parallel over {world} GPU(s)")
+    m = tp.open_group_model(dist, local, synthetic=spec, max_context=ctx)
     load_s = time.perf_counter() - t0
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(0)          # every rank runs the same tokens
     seqs = [m.new_sequence() for _ in range(B)]
     trace(f"model ready in {load_s:.1f} s; prefill {B} x {args.prompt}")
     t0 = time.perf_counter()
@@ -301,11 +308,8 @@ def main():
         ms = m.bench_decode(seqs, steps)
         barrier()
     launches = m.stats().kernel_launches - launches0
-    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
-    value = world * steps * B / (ms_max / 1e3)
+    ms_max = tp.max_over_ranks(dist, ms)
+    value = steps * B / (ms_max / 1e3)
 
     trace(f"timed {steps} steps: {ms:.1f} ms")
     # e2e: the host-facing call, host token ids in, host logits out, every step
@@ -320,10 +324,7 @@ def main():
             m.forward_batch(seqs, toks, out=out)
     barrier()
     e2e_s = time.perf_counter() - t0
-    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e = world * steps * B / float(e2e_t.item())
+    e2e = steps * B / tp.max_over_ranks(dist, e2e_s)
 
     trace(f"e2e {e2e_s:.2f} s")
     # live roofline of the dominant kernel: per-launch CUDA events over a second pass of the same steps
@@ -332,11 +333,12 @@ def main():
     q4 = m.profile_get(Q4_K)
     q6 = m.profile_get(Q6_K)
     att = m.profile_get(40)
+    comm = m.profile_get(45)
     trace(f"profile: q4_K {q4.launches} launches {q4.ms:.1f} ms {q4.bytes / 1e9:.2f} GB; q6_K {q6.launches} "
           f"{q6.ms:.1f} ms {q6.bytes / 1e9:.2f} GB; attention {att.launches} {att.ms:.1f} ms; " +
           "; ".join(f"{name} {e.launches} {e.ms:.1f} ms" for name, e in
                     (("norm", m.profile_get(41)), ("rope", m.profile_get(42)), ("swiglu", m.profile_get(43)),
-                     ("xprep", m.profile_get(44)))))
+                     ("xprep", m.profile_get(44)), ("collectives", comm))))
     m.profile(0)
     hbm, _, peak_kind = measured_peaks()
     achieved = q4.bytes / (q4.ms / 1e3) / 1e9 if q4.ms > 0 else None
@@ -360,15 +362,17 @@ def main():
     trace("cpu baseline done")
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
-                "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "q4_K/q6_K weights, f32 compute", "data": "synthetic",
                 "config": {"workload": f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
                                        f"{args.layers} layers", "batch": B, "prompt": args.prompt,
-                           "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                           "parallelism": f"tp{world} (NCCL all-reduce x2 per layer)" if world > 1 else "1 GPU",
                            "l2": "inputs larger than L2 (39.5 GB of weights read per step)"},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                         "d2h_bytes_per_step": 4 * B * spec.vocab},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+                "collectives": {"launches": comm.launches, "ms_per_step": comm.ms / max(min(steps, 8), 1)}
+                if world > 1 else None,
                 "load_s": load_s, "prefill_s": prefill_s,
                 "prefill_tok_s": B * args.prompt / prefill_s}
         print(json.dumps(line))

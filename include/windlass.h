@@ -70,15 +70,24 @@ typedef struct wl_options {
                                 WL_EUNSUPPORTED */
     int32_t prefill_path;    /* T > 8 prompts: 0 auto (tensor cores where the format has them), 1 fp32 CUDA cores */
     int32_t use_graphs;      /* 1: replay decode steps from captured CUDA graphs */
-    int32_t reserved[9];
+    int32_t tp_size;         /* tensor parallelism: ranks that share the model, one GPU each (0 or 1 = one GPU).
+                                Every rank opens the same model with its own tp_rank and the same tp_id, and then
+                                makes the same calls with the same arguments; each call returns the full logits on
+                                every rank. Query/key/value, gate/up and the output head are split by rows, the
+                                attention output and down projections by columns, with an NCCL all-reduce after each
+                                of the latter two (dense models; head and KV-head counts divisible by tp_size). */
+    int32_t tp_rank;         /* this caller's rank, 0 .. tp_size-1 */
+    int32_t reserved[7];
+    uint8_t tp_id[128];      /* the group's id: wl_tp_unique_id on one rank, the same bytes passed to every rank */
 } wl_options;
 
 typedef struct wl_info {
     int32_t layers, embd, heads, kv_heads, head_dim, vocab, context_length, max_context;
     int32_t expert_count, expert_used, expert_ff, moe;
-    int64_t weight_bytes;    /* quantized weight bytes of all layers and the head */
+    int64_t weight_bytes;    /* quantized weight bytes of all layers and the head held by this rank */
     int64_t device_bytes;    /* device memory the model holds now */
     char arch[32];
+    int32_t tp_size, tp_rank;
 } wl_info;
 
 typedef struct wl_stats {
@@ -103,6 +112,7 @@ typedef struct wl_profile_entry {
 #define WL_PROFILE_ROPE      42   /* RoPE + KV append */
 #define WL_PROFILE_SWIGLU    43   /* SwiGlu (+ activation prep) */
 #define WL_PROFILE_XPREP     44   /* stand-alone activation prep of the tensor-core matvecs */
+#define WL_PROFILE_ALLREDUCE 45   /* tensor-parallel collectives (bytes: what each rank sends over NVLink) */
 
 /* Synthetic model (benchmarks and full-size tests): a decoder of the given shape whose weights are generated on the
  * device from a counter hash (seed, tensor, element), N(0, sigma) through Irwin-Hall(12), round-to-nearest quantized.
@@ -119,6 +129,10 @@ typedef struct wl_synth_spec {
 void        wl_options_init(wl_options* opt);
 const char* wl_last_error(void);
 const char* wl_version(void);
+/* No counterpart in the reference (it runs on one CPU): a fresh id for a tensor-parallel group (ncclGetUniqueId)
+ * into id[0..bytes), bytes >= 128. One rank calls it and hands the bytes to the others (wl_options.tp_id). Needs NCCL
+ * (libnccl.so.2, loaded on first use); without it the call returns WL_ENCCL. */
+int32_t wl_tp_unique_id(uint8_t* id, int32_t bytes);
 
 /* LayeredBackend.Load (src/Engine.cs:55-91): GgufModelFile.Open + ModelConfig.From + LayerStream + Transformer. */
 int32_t wl_open(const char* gguf_path, const wl_options* opt, wl_model** out);

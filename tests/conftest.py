@@ -3,6 +3,14 @@ import sys
 
 import pytest
 
+# PyTorch (test plumbing: gloo process groups, device buffers) is imported before libwindlass_cuda loads NCCL on
+# first tensor-parallel use, so that both share PyTorch's NCCL rather than the library pulling in the system copy
+# first and PyTorch then failing to find its newer symbols in it.
+try:
+    import torch  # noqa: F401
+except ImportError:
+    pass
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)

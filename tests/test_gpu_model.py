@@ -177,3 +177,30 @@ def test_cancel_progress_and_argument_errors(wl, oracle, tmp_path):
             m.forward([m.vocab])
         with pytest.raises(_lib.ArgumentError, match="No tokens"):
             m.forward([])
+
+
+def test_graph_replays_equal_eager_steps(wl):
+    """Decode steps replayed from captured CUDA graphs (the default, wl_options.use_graphs = 1) return bit for bit the
+    logits of the same steps launched one kernel at a time, for Forward and ForwardBatch."""
+    from windlass_b200.transformer import synth_spec
+    spec = synth_spec("llama", 2, 2048, 32, 8, 64, 4096, 8192, rope_base=500000.0, type_attn_v=14, type_embd=12, seed=7)
+    prompt = np.random.default_rng(1).integers(0, spec.vocab, 20).astype(np.int32)
+    with CudaTransformer(synthetic=spec, max_context=128, use_graphs=1) as g, \
+            CudaTransformer(synthetic=spec, max_context=128, use_graphs=0) as e:
+        lg, le = g.forward(prompt), e.forward(prompt)
+        assert np.array_equal(lg, le)
+        launches0 = g.stats().kernel_launches
+        for i in range(6):
+            t = int(np.argmax(le))
+            lg, le = g.forward([t], pos0=len(prompt) + i), e.forward([t], pos0=len(prompt) + i)
+            assert np.array_equal(lg, le), f"graph step {i} differs from the eager step"
+        assert g.stats().kernel_launches > launches0
+        sg = [g.new_sequence() for _ in range(3)]
+        se = [e.new_sequence() for _ in range(3)]
+        for k in range(3):
+            g.forward(prompt[: 5 + k], seq=sg[k])
+            e.forward(prompt[: 5 + k], seq=se[k])
+        for step in range(3):
+            bg = g.forward_batch(sg, [3 + step, 4, 5])
+            be = e.forward_batch(se, [3 + step, 4, 5])
+            assert np.array_equal(bg, be), f"graph batch step {step} differs from the eager step"

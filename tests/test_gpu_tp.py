@@ -1,0 +1,85 @@
+"""Tensor parallelism on several GPUs (one process per GPU under torchrun, NCCL over NVLink) against the CPU oracle:
+
+- the prompt's logits on every rank match the oracle within 1e-3 of their standard deviation, argmax equal;
+- configs[0] greedy decode gives the oracle's tokens;
+- every rank returns the same logits (the all-reduce and the head's all-gather leave no rank behind);
+- ForwardBatch rows equal single runs (bit-identical at 2 ranks, where each all-reduced value is one sum of two).
+
+Needs at least 2 GPUs; WL_TP_TEST_GPUS picks how many ranks (default 2).
+"""
+import os
+import signal
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from tests.test_gpu_model import compare, greedy
+from tests.tp_worker import spec_of
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_ranks(n, spec, out, steps=16, graphs=1, timeout=300):
+    """torchrun of tests/tp_worker.py on n GPUs; every rank's saved results."""
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "tp_worker.py"),
+           "--spec", spec, "--out", str(out), "--steps", str(steps), "--graphs", str(graphs)]
+    p = subprocess.Popen(cmd, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
+                         start_new_session=True)
+    try:
+        log, _ = p.communicate(timeout=timeout)
+    except subprocess.TimeoutExpired:
+        os.killpg(p.pid, signal.SIGKILL)         # torchrun and every rank it started
+        log, _ = p.communicate()
+        pytest.fail(f"tensor-parallel ranks did not finish in {timeout} s:\n{log[-4000:]}")
+    assert p.returncode == 0, f"tensor-parallel ranks failed:\n{log[-4000:]}"
+    return [dict(np.load(os.path.join(out, f"rank{r}.npz"))) for r in range(n)]
+
+
+@pytest.mark.parametrize("spec", ["config0", "gqa"])
+def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
+    n = int(os.environ.get("WL_TP_TEST_GPUS", "2"))
+    if _gpus() < n:
+        pytest.skip(f"needs {n} GPUs")
+    O = oracle
+    sp = spec_of(spec)
+    res = run_ranks(n, spec, tmp_path)
+    for r in range(1, n):
+        for k in ("prefill", "tokens", "decode", "batch"):
+            assert np.array_equal(res[r][k], res[0][k]), f"rank {r} returned other {k} than rank 0"
+    got = res[0]
+    prompt = got["prompt"]
+    path = O.write_synth(str(tmp_path / f"{spec}.gguf"), sp)
+    om = O.Model(path, max_context=256)
+    compare(got["prefill"], om.forward(prompt, all_logits=True), f"tp{n} {spec} prefill")
+    om2 = O.Model(path, max_context=256)
+    want_tokens = greedy(lambda t, p0: om2.forward(t, pos0=p0), prompt, len(got["tokens"]))
+    if spec == "config0":
+        assert list(got["tokens"]) == want_tokens, "configs[0] greedy tokens differ from the oracle"
+    # the decode logits along the GPU's own token path
+    om3 = O.Model(path, max_context=256)
+    om3.forward(prompt)
+    for i, t in enumerate(got["tokens"]):
+        compare(got["decode"][i], om3.forward([int(t)], pos0=len(prompt) + i), f"tp{n} {spec} decode step {i}")
+    if n == 2:
+        assert np.array_equal(got["batch"], got["single"]), "ForwardBatch rows differ from single runs"
+    else:
+        compare(got["batch"], got["single"], f"tp{n} {spec} batch rows")

@@ -47,13 +47,15 @@ _EXC = {WL_EINVAL: ArgumentError, WL_EUNSUPPORTED: NotSupportedError, WL_EFORMAT
 class Options(C.Structure):
     _fields_ = [("size", C.c_int32), ("device", C.c_int32), ("max_context", C.c_int32), ("max_batch", C.c_int32),
                 ("resident", C.c_int32), ("prefill_path", C.c_int32), ("use_graphs", C.c_int32),
-                ("reserved", C.c_int32 * 9)]
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("reserved", C.c_int32 * 7),
+                ("tp_id", C.c_uint8 * 128)]
 
 
 class Info(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("layers", "embd", "heads", "kv_heads", "head_dim", "vocab", "context_length",
                                           "max_context", "expert_count", "expert_used", "expert_ff", "moe")] + \
-               [("weight_bytes", C.c_int64), ("device_bytes", C.c_int64), ("arch", C.c_char * 32)]
+               [("weight_bytes", C.c_int64), ("device_bytes", C.c_int64), ("arch", C.c_char * 32),
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32)]
 
 
 class Stats(C.Structure):
@@ -98,7 +100,7 @@ def lib():
     P, I32, I64, U64, F = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_float
     sig = {
         "wl_options_init": (None, [C.POINTER(Options)]), "wl_last_error": (C.c_char_p, []),
-        "wl_version": (C.c_char_p, []),
+        "wl_version": (C.c_char_p, []), "wl_tp_unique_id": (I32, [P, I32]),
         "wl_open": (I32, [C.c_char_p, C.POINTER(Options), C.POINTER(P)]),
         "wl_open_synthetic": (I32, [C.POINTER(SynthSpec), C.POINTER(Options), C.POINTER(P)]),
         "wl_close": (I32, [P]), "wl_info_get": (I32, [P, C.POINTER(Info)]), "wl_stats_get": (I32, [P, C.POINTER(Stats)]),
@@ -137,5 +139,16 @@ def options(**kw):
     o = Options()
     lib().wl_options_init(C.byref(o))
     for k, v in kw.items():
-        setattr(o, k, v)
+        if k == "tp_id":
+            if v is not None:
+                C.memmove(o.tp_id, bytes(v), 128)
+        else:
+            setattr(o, k, v)
     return o
+
+
+def tp_unique_id():
+    """A fresh tensor-parallel group id (128 bytes; wl_tp_unique_id): one rank makes it, every rank opens with it."""
+    buf = (C.c_uint8 * 128)()
+    check(lib().wl_tp_unique_id(buf, 128))
+    return bytes(buf)

@@ -4,7 +4,7 @@
 
 Objects go to _build/ (not committed); the library lands next to this file, where windlass_b200/_lib.py loads it.
 Every source is compiled with -gencode arch=compute_100a,code=sm_100a -lineinfo, CUDA runtime linked statically,
-NCCL linked dynamically from the system library for the tensor-parallel paths.
+NCCL loaded at run time (dlopen) by the tensor-parallel paths only.
 """
 import os
 import shutil
@@ -18,7 +18,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(HERE, "libwindlass_cuda.so")
 
-SOURCES = ["wl_kernels.cu", "wl_mmv.cu", "wl_noalloc.cu", "wl_model.cpp", "wl_gguf.cpp", "wl_common.cpp", "wl_api.cpp"]
+SOURCES = ["wl_kernels.cu", "wl_mmv.cu", "wl_noalloc.cu", "wl_model.cpp", "wl_gguf.cpp", "wl_common.cpp", "wl_api.cpp",
+           "wl_nccl.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -58,7 +59,7 @@ def build(verbose=False):
         objs = list(ex.map(lambda s: _compile(s, verbose), SOURCES))
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-cudart", "static", "-lpthread"]
+    cmd = [nvcc(), "-shared", "-o", LIB] + objs + ARCH + ["-cudart", "static", "-lpthread", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

@@ -101,10 +101,21 @@ void wl_options_init(wl_options* opt)
     opt->resident = -1;
     opt->prefill_path = 0;
     opt->use_graphs = 1;
+    opt->tp_size = 1;
+    opt->tp_rank = 0;
 }
 
 const char* wl_last_error(void) { return wl::last_error_cstr(); }
 const char* wl_version(void) { return "windlass-cuda 0.1 (sm_100a)"; }
+
+int32_t wl_tp_unique_id(uint8_t* id, int32_t bytes)
+{
+    return guarded([&]() -> int32_t {
+        if (!id || bytes < wl::TP_ID_BYTES) return wl::fail(WL_EINVAL, "wl_tp_unique_id: id needs 128 bytes");
+        wl::Comm::unique_id(id);
+        return WL_OK;
+    });
+}
 
 int32_t wl_open(const char* path, const wl_options* opt, wl_model** out)
 {
@@ -144,7 +155,7 @@ int32_t wl_info_get(const wl_model* model, wl_info* info)
 {
     return guarded([&]() -> int32_t {
         if (!model || !info) return wl::fail(WL_EINVAL, "wl_info_get: model and info are required");
-        const wl::Config& c = model->m->config();
+        const wl::Config& c = model->m->full_config();
         memset(info, 0, sizeof *info);
         info->layers = c.layers; info->embd = c.embd; info->heads = c.heads; info->kv_heads = c.kv_heads;
         info->head_dim = c.head_dim; info->vocab = c.vocab; info->context_length = c.context_length;
@@ -152,6 +163,8 @@ int32_t wl_info_get(const wl_model* model, wl_info* info)
         info->expert_used = c.expert_used; info->expert_ff = c.expert_ff; info->moe = c.expert_count > 0;
         info->weight_bytes = model->m->weight_bytes(); info->device_bytes = model->m->device_bytes();
         strncpy(info->arch, c.arch.c_str(), sizeof info->arch - 1);
+        info->tp_size = model->m->tp_size();
+        info->tp_rank = model->m->tp_rank();
         return WL_OK;
     });
 }

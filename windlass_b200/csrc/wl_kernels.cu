@@ -1001,6 +1001,26 @@ void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s)
     launched();
 }
 
+__global__ void k_vocab_gather(const float* __restrict__ src, int n, int vp, int V, float* __restrict__ dst)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y;
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x) {
+        const int g = v / vp;
+        dst[(int64_t)t * V + v] = src[((int64_t)g * n + t) * vp + (v - g * vp)];
+    }
+}
+
+void vocab_gather(const float* src, int G, int n, int vp, int V, float* dst, cudaStream_t s)
+{
+    if (n <= 0 || V <= 0) return;
+    if ((int64_t)G * vp < V) WL_THROW(WL_EINVAL, "vocab_gather: parts do not cover the vocabulary");
+    int64_t gr = grid_for(V, 256); if (gr > 148 * 4) gr = 148 * 4;
+    launch(k_vocab_gather, dim3((unsigned)gr, (unsigned)n), dim3(256), 0, s, src, n, vp, V, dst);
+    launched();
+}
+
 __global__ void k_scale(float* x, float f, int64_t n)
 {
     pdl_trigger();

@@ -119,6 +119,8 @@ void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStr
 void swiglu(float* g, const float* u, int64_t n, cudaStream_t s);
 // x[i] += o[i] * rs (Transformer.cs:225,231).
 void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s);
+// The tensor-parallel head's logits: src is [G][n][vp] (rank g's rows g*vp ..), dst[t*V + v] = src[g][t][v - g*vp].
+void vocab_gather(const float* src, int G, int n, int vp, int V, float* dst, cudaStream_t s);
 // x[i] *= f.
 void scale(float* x, float f, int64_t n, cudaStream_t s);
 // Route (Transformer.cs:315-340) for T rows of n router logits: sel[t*k+j], wts[t*k+j].

@@ -54,6 +54,75 @@ void Model::init_device(const wl_options& opt)
     prefill_path_ = opt.prefill_path;
 }
 
+// Tensor parallelism (tp_size > 1): checks the shape can be split, makes c_ this rank's share of the heads and joins
+// the NCCL group (blocking until every rank has joined). Called once the configuration is known, before any weight
+// is loaded, so a model every rank would refuse fails on every rank before the group forms.
+static int tp_size_of(const wl_options& opt)
+{
+    return opt.size >= (int32_t)sizeof(wl_options) && opt.tp_size > 1 ? opt.tp_size : 1;
+}
+
+// The checks of a tensor-parallel split that need no device: they run before the device is touched, so a model that
+// every rank would refuse fails the same way on every rank, before any rank waits for the group to form.
+static void check_tp(const Config& c, const wl_options& opt)
+{
+    const int G = tp_size_of(opt);
+    if (G == 1) return;
+    const std::string g = std::to_string(G);
+    if (opt.tp_rank < 0 || opt.tp_rank >= G) WL_THROW(WL_EINVAL, "tp_rank must be 0.." + std::to_string(G - 1) + ".");
+    if (c.expert_count > 0)
+        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism is built for dense models; this one has mixture-of-experts layers.");
+    if (c.qk_norm_full || c.post_norms)
+        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism does not split " + c.arch + " (its QK-norm spans every head).");
+    if (c.heads % G || c.kv_heads % G)
+        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism over " + g + " GPUs needs head counts divisible by " + g + " (" +
+                                  std::to_string(c.heads) + " heads, " + std::to_string(c.kv_heads) + " KV heads).");
+    if (!k::attention_supported(c.heads / G, c.kv_heads / G, c.head_dim))
+        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism over " + g + " GPUs leaves an unsupported attention shape per GPU.");
+    const int vp = (c.vocab + G - 1) / G;
+    if ((int64_t)vp * (G - 1) >= c.vocab) WL_THROW(WL_EUNSUPPORTED, "The vocabulary is too small to split over " + g + " GPUs.");
+}
+
+// Tensor parallelism (tp_size > 1): makes c_ this rank's share of the heads and joins the NCCL group (blocking until
+// every rank has joined). Called once the configuration is known and checked, before any weight is loaded.
+void Model::init_tp(const wl_options& opt)
+{
+    full_ = c_;
+    check_tp(c_, opt);
+    tp_size_ = tp_size_of(opt);
+    tp_rank_ = tp_size_ > 1 ? opt.tp_rank : 0;
+    if (tp_size_ == 1) return;
+    c_.heads /= tp_size_;
+    c_.kv_heads /= tp_size_;
+    vocab_part_ = (c_.vocab + tp_size_ - 1) / tp_size_;
+    flag_d_ = dalloc<int32_t>(1);
+    flag_h_ = halloc<int32_t>(1);
+    comm_.reset(new Comm(opt.tp_id, tp_size_, tp_rank_));
+}
+
+// The cancel flag, polled between stages (Transformer.cs:99,158). Under tensor parallelism the ranks take the maximum
+// of their flags, so all of them stop at the same stage and none waits in a collective the others skipped.
+bool Model::stop_requested(volatile const int32_t* cancel)
+{
+    if (!cancel) return false;
+    if (!comm_) return *cancel != 0;
+    *flag_h_ = *cancel ? 1 : 0;
+    WL_CUDA(cudaMemcpyAsync(flag_d_, flag_h_, sizeof(int32_t), cudaMemcpyHostToDevice, stream_));
+    comm_->allreduce_max(flag_d_, 1, stream_);
+    WL_CUDA(cudaMemcpyAsync(flag_h_, flag_d_, sizeof(int32_t), cudaMemcpyDeviceToHost, stream_));
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    return *flag_h_ != 0;
+}
+
+// Sums a sublayer's partial outputs over the tensor-parallel ranks (no-op on one GPU).
+void Model::all_reduce(float* buf, int64_t n)
+{
+    if (!comm_) return;
+    const int mark = profile_begin();
+    comm_->allreduce_sum(buf, n, stream_);
+    profile_end(mark, WL_PROFILE_ALLREDUCE, 8.0 * n * (tp_size_ - 1) / tp_size_);
+}
+
 uint8_t* Model::arena_alloc(int64_t bytes)
 {
     const int64_t a = (bytes + 255) / 256 * 256;
@@ -179,29 +248,81 @@ void Model::load_from_gguf(const Gguf& g)
             WL_THROW(WL_EUNSUPPORTED, "Tensor " + n + " uses " + type_name(t.type) + ", which Windlass cannot decode yet.");
     }
 
-    // One arena for every tensor plus the fp32 copies of the vectors.
+    // One arena for every tensor (this rank's part of it under tensor parallelism) plus the fp32 copies of the
+    // vectors.
+    const int G = tp_size_;
     int64_t total = 0;
-    for (const GgufTensor& t : g.tensors()) total += (t.size + 255) / 256 * 256 + (t.elements() * 4 + 255) / 256 * 256;
+    for (const GgufTensor& t : g.tensors()) {
+        const int64_t bytes = G > 1 ? t.size / G + t.size / std::max<int64_t>(t.dims[1], 1) + 256 : t.size;
+        total += (bytes + 255) / 256 * 256 + (t.elements() * 4 / (G > 1 ? G : 1) + 255) / 256 * 256;
+    }
+    if (G > 1 && c_.tied) if (const GgufTensor* t = g.find("token_embd.weight")) total += t->size / G + t->size / t->dims[1] + 512;
     arena_ = dalloc<uint8_t>(total);
     arena_size_ = total;
 
-    auto upload = [&](const GgufTensor* t) -> Weight {
+    // split: WHOLE on every rank; ROWS this rank's 1/G of the rows; COLS its 1/G of every row's blocks; HEAD rows
+    // rank*vocab_part_ .. +vocab_part_ (the last rank's may be fewer).
+    enum Split { WHOLE, ROWS, COLS, HEAD };
+    auto upload = [&](const GgufTensor* t, Split sp) -> Weight {
         if (!t) return Weight{};
         Weight w = weight_of(*t);
-        w.d = arena_alloc(w.bytes);
-        WL_CUDA(cudaMemcpy(w.d, g.data(*t), (size_t)w.bytes, cudaMemcpyHostToDevice));
+        const uint8_t* src = g.data(*t);
+        if (G == 1 || sp == WHOLE) {
+            w.d = arena_alloc(w.bytes);
+            WL_CUDA(cudaMemcpy(w.d, src, (size_t)w.bytes, cudaMemcpyHostToDevice));
+        } else if (sp == ROWS || sp == HEAD) {
+            if (w.experts != 1) WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism does not split stacked tensors.");
+            int r0, n;
+            if (sp == HEAD) { r0 = tp_rank_ * vocab_part_; n = std::min(vocab_part_, w.rows - r0); }
+            else {
+                if (w.rows % G) WL_THROW(WL_EUNSUPPORTED, t->name + ": " + std::to_string(w.rows) + " rows do not split over " + std::to_string(G) + " GPUs.");
+                n = w.rows / G; r0 = tp_rank_ * n;
+            }
+            w.rows = n;
+            w.bytes = (int64_t)n * w.row_bytes;
+            w.d = arena_alloc(w.bytes);
+            WL_CUDA(cudaMemcpy(w.d, src + (int64_t)r0 * w.row_bytes, (size_t)w.bytes, cudaMemcpyHostToDevice));
+        } else {
+            int b = 0, bb = 0;
+            layout(w.type, &b, &bb);
+            if (w.experts != 1 || w.cols % (G * b))
+                WL_THROW(WL_EUNSUPPORTED, t->name + ": " + std::to_string(w.cols) + " columns do not split into whole " +
+                                          type_name(w.type) + " blocks over " + std::to_string(G) + " GPUs.");
+            const int64_t lrb = w.row_bytes / G;
+            w.d = arena_alloc(lrb * w.rows);
+            WL_CUDA(cudaMemcpy2D(w.d, (size_t)lrb, src + tp_rank_ * lrb, (size_t)w.row_bytes, (size_t)lrb, (size_t)w.rows,
+                                 cudaMemcpyHostToDevice));
+            w.cols /= G;
+            w.row_bytes = lrb;
+            w.bytes = lrb * w.rows;
+        }
         stats_.bytes_h2d += w.bytes;
+        weight_bytes_ += w.bytes;
         return w;
     };
-    auto vec = [&](const GgufTensor* t) -> Vec {
+    auto vec = [&](const GgufTensor* t, Split sp) -> Vec {
         Vec v;
         if (!t) return v;
-        const Weight w = upload(t);
-        v.n = (int)t->elements();
-        if (t->type == 0) v.d = (float*)w.d;
+        const uint8_t* src = g.data(*t);
+        int64_t n = t->elements(), bytes = t->size;
+        if (sp != WHOLE && G > 1) {      // a vector's split is a slice of its values (biases of split rows)
+            if (t->type != 0 && t->type != 1)
+                WL_THROW(WL_EUNSUPPORTED, t->name + " is not F32 or F16 and cannot be split over GPUs.");
+            if (n % G) WL_THROW(WL_EUNSUPPORTED, t->name + " does not split over " + std::to_string(G) + " GPUs.");
+            const int64_t esz = t->type == 0 ? 4 : 2;
+            n /= G;
+            src += tp_rank_ * n * esz;
+            bytes = n * esz;
+        }
+        uint8_t* d = arena_alloc(bytes);
+        WL_CUDA(cudaMemcpy(d, src, (size_t)bytes, cudaMemcpyHostToDevice));
+        stats_.bytes_h2d += bytes;
+        weight_bytes_ += bytes;
+        v.n = (int)n;
+        if (t->type == 0) v.d = (float*)d;
         else {
-            v.d = (float*)arena_alloc((int64_t)v.n * 4);
-            k::dequant(t->type, w.d, v.n, v.d, stream_);
+            v.d = (float*)arena_alloc(n * 4);
+            k::dequant(t->type, d, n, v.d, stream_);
         }
         return v;
     };
@@ -209,30 +330,32 @@ void Model::load_from_gguf(const Gguf& g)
     for (int l = 0; l < c_.layers; ++l) {
         LayerW& L = L_[l];
         auto T = [&](const char* n) { return g.find(layer_name(l, n)); };
-        L.attn_norm = vec(T("attn_norm.weight"));
-        L.q = upload(T("attn_q.weight")); L.k = upload(T("attn_k.weight")); L.v = upload(T("attn_v.weight"));
-        L.qb = vec(T("attn_q.bias")); L.kb = vec(T("attn_k.bias")); L.vb = vec(T("attn_v.bias"));
-        L.q_norm = vec(T("attn_q_norm.weight")); L.k_norm = vec(T("attn_k_norm.weight"));
-        L.o = upload(T("attn_output.weight"));
-        L.post_attn_norm = vec(T("post_attention_norm.weight"));
-        L.ffn_norm = vec(T("ffn_norm.weight"));
-        L.post_ffw_norm = vec(T("post_ffw_norm.weight"));
+        L.attn_norm = vec(T("attn_norm.weight"), WHOLE);
+        L.q = upload(T("attn_q.weight"), ROWS); L.k = upload(T("attn_k.weight"), ROWS); L.v = upload(T("attn_v.weight"), ROWS);
+        L.qb = vec(T("attn_q.bias"), ROWS); L.kb = vec(T("attn_k.bias"), ROWS); L.vb = vec(T("attn_v.bias"), ROWS);
+        L.q_norm = vec(T("attn_q_norm.weight"), WHOLE); L.k_norm = vec(T("attn_k_norm.weight"), WHOLE);
+        L.o = upload(T("attn_output.weight"), COLS);
+        L.post_attn_norm = vec(T("post_attention_norm.weight"), WHOLE);
+        L.ffn_norm = vec(T("ffn_norm.weight"), WHOLE);
+        L.post_ffw_norm = vec(T("post_ffw_norm.weight"), WHOLE);
         L.moe = c_.expert_count > 0 && T("ffn_gate_inp.weight");
         if (L.moe) {
-            L.router = upload(T("ffn_gate_inp.weight"));
-            L.gate_exps = upload(T("ffn_gate_exps.weight")); L.up_exps = upload(T("ffn_up_exps.weight")); L.down_exps = upload(T("ffn_down_exps.weight"));
-            L.sh_gate = upload(T("ffn_gate_shexp.weight")); L.sh_up = upload(T("ffn_up_shexp.weight")); L.sh_down = upload(T("ffn_down_shexp.weight"));
-            L.sh_gate_inp = upload(T("ffn_gate_inp_shexp.weight"));
+            L.router = upload(T("ffn_gate_inp.weight"), WHOLE);
+            L.gate_exps = upload(T("ffn_gate_exps.weight"), WHOLE); L.up_exps = upload(T("ffn_up_exps.weight"), WHOLE);
+            L.down_exps = upload(T("ffn_down_exps.weight"), WHOLE);
+            L.sh_gate = upload(T("ffn_gate_shexp.weight"), WHOLE); L.sh_up = upload(T("ffn_up_shexp.weight"), WHOLE);
+            L.sh_down = upload(T("ffn_down_shexp.weight"), WHOLE);
+            L.sh_gate_inp = upload(T("ffn_gate_inp_shexp.weight"), WHOLE);
             if (L.sh_gate.present()) c_.shared_expert_ff = L.sh_gate.rows;
         } else {
-            L.gate = upload(T("ffn_gate.weight")); L.up = upload(T("ffn_up.weight")); L.down = upload(T("ffn_down.weight"));
+            L.gate = upload(T("ffn_gate.weight"), ROWS); L.up = upload(T("ffn_up.weight"), ROWS);
+            L.down = upload(T("ffn_down.weight"), COLS);
         }
     }
-    embd_ = upload(g.find("token_embd.weight"));
-    out_norm_ = vec(g.find("output_norm.weight"));
+    embd_ = upload(g.find("token_embd.weight"), WHOLE);
+    out_norm_ = vec(g.find("output_norm.weight"), WHOLE);
     if (!out_norm_.present()) WL_THROW(WL_EUNSUPPORTED, "The model has no output_norm.weight.");
-    output_ = c_.tied ? embd_ : upload(g.find("output.weight"));
-    for (const GgufTensor& t : g.tensors()) weight_bytes_ += t.size;
+    output_ = c_.tied ? (G > 1 ? upload(g.find("token_embd.weight"), HEAD) : embd_) : upload(g.find("output.weight"), HEAD);
 
     std::vector<float> rf;
     if (const GgufTensor* t = g.find("rope_freqs.weight")) {
@@ -269,10 +392,12 @@ Model* Model::open_file(const std::string& path, const wl_options& opt)
     // a GPU.
     Gguf g(path);
     const Config c = read_config(g);
+    check_tp(c, opt);
     std::unique_ptr<Model> m(new Model());
     m->c_ = c;
     m->init_device(opt);
     m->max_context_ = opt.max_context > 0 ? opt.max_context : std::min(m->c_.context_length, 8192);
+    m->init_tp(opt);
     m->load_from_gguf(g);
     m->finish_open();
     return m.release();
@@ -286,7 +411,6 @@ enum Slot { S_ATTN_NORM = 1, S_Q, S_K, S_V, S_O, S_FFN_NORM, S_GATE, S_UP, S_DOW
 Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
 {
     std::unique_ptr<Model> m(new Model());
-    m->init_device(opt);
     Config& c = m->c_;
     c.arch = std::string(sp.arch, strnlen(sp.arch, sizeof sp.arch));
     if (c.arch != "llama" && c.arch != "qwen3" && c.arch != "qwen3moe") WL_THROW(WL_EUNSUPPORTED, "synthetic arch must be llama, qwen3 or qwen3moe");
@@ -303,25 +427,31 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
     }
     if (c.layers <= 0 || c.embd <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads || c.vocab <= 0)
         WL_THROW(WL_EINVAL, "bad synthetic shape");
+    check_tp(c, opt);
+    m->init_device(opt);
     m->max_context_ = opt.max_context > 0 ? opt.max_context : std::min(c.context_length, 8192);
     const float sigma = sp.sigma > 0 ? sp.sigma : 0.02f;
     const int QD = c.qdim(), KD = c.kvdim(), E = c.embd, F = sp.ff, NE = c.expert_count, X = c.expert_ff;
+    m->init_tp(opt);
+    const int G = m->tp_size_, rank = m->tp_rank_;
 
-    struct Plan { Weight* w; Vec* v; uint32_t tid; int type; int64_t rows, cols; int experts; };
+    // split (tensor parallelism): 0 whole, 1 rows, 2 columns, 3 output-head rows; the full tensor is generated and
+    // this rank's part copied out, so every rank holds exactly the bytes of the one-GPU model's slice.
+    struct Plan { Weight* w; Vec* v; uint32_t tid; int type; int64_t rows, cols; int experts; int split = 0; };
     std::vector<Plan> plan;
     m->L_.resize(c.layers);
     for (int l = 0; l < c.layers; ++l) {
         LayerW& L = m->L_[l];
         const uint32_t b = (uint32_t)(l + 1) << 8;
         plan.push_back({nullptr, &L.attn_norm, b | S_ATTN_NORM, 0, 1, E, 1});
-        plan.push_back({&L.q, nullptr, b | S_Q, sp.type_attn, QD, E, 1});
-        plan.push_back({&L.k, nullptr, b | S_K, sp.type_attn, KD, E, 1});
-        plan.push_back({&L.v, nullptr, b | S_V, sp.type_attn_v, KD, E, 1});
+        plan.push_back({&L.q, nullptr, b | S_Q, sp.type_attn, QD, E, 1, 1});
+        plan.push_back({&L.k, nullptr, b | S_K, sp.type_attn, KD, E, 1, 1});
+        plan.push_back({&L.v, nullptr, b | S_V, sp.type_attn_v, KD, E, 1, 1});
         if (c.qk_norm) {
             plan.push_back({nullptr, &L.q_norm, b | S_Q_NORM, 0, 1, c.head_dim, 1});
             plan.push_back({nullptr, &L.k_norm, b | S_K_NORM, 0, 1, c.head_dim, 1});
         }
-        plan.push_back({&L.o, nullptr, b | S_O, sp.type_attn, E, QD, 1});
+        plan.push_back({&L.o, nullptr, b | S_O, sp.type_attn, E, QD, 1, 2});
         plan.push_back({nullptr, &L.ffn_norm, b | S_FFN_NORM, 0, 1, E, 1});
         if (NE > 0) {
             L.moe = true;
@@ -330,34 +460,71 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
             plan.push_back({&L.up_exps, nullptr, b | S_UP_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE});
             plan.push_back({&L.down_exps, nullptr, b | S_DOWN_EXPS, sp.type_ffn_down, (int64_t)NE * E, X, NE});
         } else {
-            plan.push_back({&L.gate, nullptr, b | S_GATE, sp.type_ffn, F, E, 1});
-            plan.push_back({&L.up, nullptr, b | S_UP, sp.type_ffn, F, E, 1});
-            plan.push_back({&L.down, nullptr, b | S_DOWN, sp.type_ffn_down, E, F, 1});
+            plan.push_back({&L.gate, nullptr, b | S_GATE, sp.type_ffn, F, E, 1, 1});
+            plan.push_back({&L.up, nullptr, b | S_UP, sp.type_ffn, F, E, 1, 1});
+            plan.push_back({&L.down, nullptr, b | S_DOWN, sp.type_ffn_down, E, F, 1, 2});
         }
     }
     plan.push_back({&m->embd_, nullptr, 1, sp.type_embd, c.vocab, E, 1});
     plan.push_back({nullptr, &m->out_norm_, 2, 0, 1, E, 1});
-    plan.push_back({&m->output_, nullptr, 3, sp.type_output, c.vocab, E, 1});
+    plan.push_back({&m->output_, nullptr, 3, sp.type_output, c.vocab, E, 1, 3});
 
-    int64_t total = 0;
+    // this rank's rows [r0, r0 + nrows) and column blocks [c0, c0 + ncols) of a planned tensor
+    auto part = [&](const Plan& p, int64_t* r0, int64_t* nrows, int64_t* c0, int64_t* ncols) {
+        *r0 = 0; *nrows = p.rows; *c0 = 0; *ncols = p.cols;
+        if (G == 1 || p.split == 0) return;
+        const int blk = p.type == 0 ? 1 : p.type == 8 ? 32 : 256;
+        if (p.split == 1) {
+            if (p.rows % G) WL_THROW(WL_EUNSUPPORTED, "synthetic tensor rows do not split over " + std::to_string(G) + " GPUs");
+            *nrows = p.rows / G; *r0 = rank * *nrows;
+        } else if (p.split == 3) {
+            *r0 = (int64_t)rank * m->vocab_part_; *nrows = std::min<int64_t>(m->vocab_part_, p.rows - *r0);
+        } else {
+            if (p.cols % ((int64_t)G * blk))
+                WL_THROW(WL_EUNSUPPORTED, "synthetic tensor columns do not split into whole blocks over " + std::to_string(G) + " GPUs");
+            *ncols = p.cols / G; *c0 = rank * *ncols;
+        }
+    };
+    int64_t total = 0, tmp_bytes = 0;
     for (const Plan& p : plan) {
         const int64_t rb = row_bytes_of(p.type, p.cols);
         if (rb <= 0 || p.cols % (p.type == 0 ? 1 : p.type == 8 ? 32 : 256) != 0) WL_THROW(WL_EUNSUPPORTED, "synthetic tensor shape does not fit its type");
-        total += (rb * p.rows + 255) / 256 * 256;
+        int64_t r0, nr, c0, nc;
+        part(p, &r0, &nr, &c0, &nc);
+        total += (row_bytes_of(p.type, nc) * nr + 255) / 256 * 256;
+        if (G > 1 && p.split) tmp_bytes = std::max(tmp_bytes, rb * p.rows);
     }
     m->arena_ = dalloc<uint8_t>(total);
     m->arena_size_ = total;
-    for (const Plan& p : plan) {
-        Weight w;
-        w.type = p.type; w.cols = (int)p.cols; w.experts = p.experts; w.rows = (int)(p.rows / p.experts);
-        w.row_bytes = row_bytes_of(p.type, p.cols); w.bytes = w.row_bytes * p.rows;
-        w.d = m->arena_alloc(w.bytes);
-        const bool is_vec = p.v != nullptr;
-        k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, is_vec ? 1.0f : 0.0f, w.d, m->stream_);
-        m->weight_bytes_ += w.bytes;
-        if (is_vec) { p.v->d = (float*)w.d; p.v->n = (int)(p.rows * p.cols); }
-        else *p.w = w;
+    uint8_t* tmp = tmp_bytes ? dalloc<uint8_t>(tmp_bytes) : nullptr;
+    try {
+        for (const Plan& p : plan) {
+            int64_t r0, nr, c0, nc;
+            part(p, &r0, &nr, &c0, &nc);
+            const int64_t full_rb = row_bytes_of(p.type, p.cols);
+            Weight w;
+            w.type = p.type; w.cols = (int)nc; w.experts = p.experts; w.rows = (int)(nr / p.experts);
+            w.row_bytes = row_bytes_of(p.type, nc); w.bytes = w.row_bytes * nr;
+            w.d = m->arena_alloc(w.bytes);
+            const bool is_vec = p.v != nullptr;
+            if (G == 1 || p.split == 0) {
+                k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, is_vec ? 1.0f : 0.0f, w.d, m->stream_);
+            } else {
+                k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, 0.0f, tmp, m->stream_);
+                const int64_t cb = row_bytes_of(p.type, c0);    // byte offset of the first column block
+                WL_CUDA(cudaMemcpy2DAsync(w.d, (size_t)w.row_bytes, tmp + r0 * full_rb + cb, (size_t)full_rb,
+                                          (size_t)w.row_bytes, (size_t)nr, cudaMemcpyDeviceToDevice, m->stream_));
+            }
+            m->weight_bytes_ += w.bytes;
+            if (is_vec) { p.v->d = (float*)w.d; p.v->n = (int)(nr * nc); }
+            else *p.w = w;
+        }
+        WL_CUDA(cudaStreamSynchronize(m->stream_));
+    } catch (...) {
+        if (tmp) cudaFree(tmp);
+        throw;
     }
+    if (tmp) cudaFree(tmp);
     m->build_rope_table(nullptr, 0);
     WL_CUDA(cudaStreamSynchronize(m->stream_));
     m->finish_open();
@@ -389,6 +556,8 @@ Model::~Model()
     if (xprep_buf_) cudaFree(xprep_buf_);
     dfree(att_part_);
     dfree(err_d_);
+    dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
+    comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
@@ -490,6 +659,11 @@ void Model::ensure_workspace(int T, int logit_rows)
     if (logit_rows > ws_logit_rows_) {
         dfree(logits_);
         logits_ = dalloc<float>((int64_t)logit_rows * c_.vocab);
+        if (tp_size_ > 1) {
+            dfree(logits_part_); dfree(logits_all_);
+            logits_part_ = dalloc<float>((int64_t)logit_rows * vocab_part_);
+            logits_all_ = dalloc<float>((int64_t)tp_size_ * logit_rows * vocab_part_);
+        }
         ws_logit_rows_ = logit_rows;
         ws_gen_++;
         drop_graphs();
@@ -501,8 +675,9 @@ void Model::ensure_workspace(int T, int logit_rows)
 // ---------------------------------------------------------------------------------------------------------------------
 // y[T][rows] = W x. Formats with a tensor-core matvec take activations prepared by k::xprep (8 columns at a time);
 // reuse_x says x is the input of the previous matmul as well, so its prepared form can be reused.
-void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x)
+void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x, int64_t ldy)
 {
+    if (ldy <= 0) ldy = w.rows;
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
     const bool cuda_cores = path == 1 || (T > 8 && prefill_path_ == 1);
     if (!cuda_cores && w.tiles && w.row_base % 16 == 0 && xprep_buf_) {
@@ -517,7 +692,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
-            k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * w.rows, w.rows, err_d_,
+            k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * ldy, ldy, err_d_,
                             stream_);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
@@ -526,7 +701,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
     }
     prep_x_ = nullptr;
     const int mark = profile_begin();
-    k::matvec(w.type, w.d, w.row_bytes, w.rows, w.cols, x, w.cols, T, y, w.rows, stream_);
+    k::matvec(w.type, w.d, w.row_bytes, w.rows, w.cols, x, w.cols, T, y, ldy, stream_);
     profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows));
 }
 
@@ -619,6 +794,7 @@ void Model::ffn_dense(const LayerW& L, int T)
     }
     profile_end(sm, WL_PROFILE_SWIGLU, 0.0);
     matmul(L.down, g_, T, o_, 0, true);
+    all_reduce(o_, (int64_t)T * c_.embd);
 }
 
 // MoeFfn (src/Transformer.cs:259-311): router, top-k, then each chosen expert runs once on the rows routed to it, in
@@ -712,6 +888,7 @@ void Model::layer(int l, int T, int max_n)
     prep_x_ = nullptr;
     if (prepped) { prep_x_ = att_; prep_cols_ = QD; prep_nc_ = T; }
     matmul(L.o, att_, T, o_, 0, true);
+    all_reduce(o_, n);
     if (c_.post_norms) {
         k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
         k::residual(x_, o_, rs, n, stream_);
@@ -772,7 +949,16 @@ void Model::head(int T, int first)
         k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
     }
     pending_residual_ = false;
-    matmul(output_, xn_, n, logits_, 0, true);
+    if (comm_) {
+        // this rank's vocabulary rows, then every rank's gathered and laid out as [n][vocab]
+        matmul(output_, xn_, n, logits_part_, 0, true, vocab_part_);
+        const int mark = profile_begin();
+        comm_->allgather(logits_part_, logits_all_, (int64_t)n * vocab_part_ * 4, stream_);
+        profile_end(mark, WL_PROFILE_ALLREDUCE, 4.0 * n * vocab_part_ * (tp_size_ - 1));
+        k::vocab_gather(logits_all_, tp_size_, n, vocab_part_, c_.vocab, logits_, stream_);
+    } else {
+        matmul(output_, xn_, n, logits_, 0, true);
+    }
     if (c_.logit_scale != 0.f) k::scale(logits_, 1.f / c_.logit_scale, (int64_t)n * c_.vocab, stream_);
 }
 
@@ -810,18 +996,19 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
     int max_n = 0;
     for (int t = 0; t < T; ++t) max_n = std::max(max_n, pos[t] + 1);
     const int total = c_.layers + 1;
-    if (!progress && (!cancel || !*cancel) && graph_step(T, first)) {
+    const bool stop0 = stop_requested(cancel);
+    if (!progress && !stop0 && graph_step(T, first)) {
         // the whole step ran as one graph; a cancel flag set meanwhile is seen by the next call
     } else if (!cancel && !progress) step_device(T, first, max_n);
     else {
         k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
         pending_residual_ = false;
         for (int l = 0; l < c_.layers; ++l) {
-            if (cancel && *cancel) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+            if (l == 0 ? stop0 : stop_requested(cancel)) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
             layer(l, T, max_n);
             if (progress) { WL_CUDA(cudaStreamSynchronize(stream_)); progress(l + 1, total, user); }
         }
-        if (cancel && *cancel) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+        if (stop_requested(cancel)) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
         head(T, first);
     }
     WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include "../../include/windlass.h"
 #include "wl_kernels.h"
+#include "wl_nccl.h"
 
 namespace wl {
 
@@ -83,7 +84,12 @@ public:
     int32_t forward_batch(Seq* const* seqs, const int32_t* tokens, int N, float* out, volatile const int32_t* cancel,
                           wl_progress_fn progress, void* user);
 
+    // The model's shape; under tensor parallelism heads and kv_heads are this rank's share (full_config() has the
+    // whole model's).
     const Config& config() const { return c_; }
+    const Config& full_config() const { return full_; }
+    int tp_size() const { return tp_size_; }
+    int tp_rank() const { return tp_rank_; }
     int max_context() const { return max_context_; }
     const Stats& stats() const { return stats_; }
     int64_t graph_launches() const { return graph_launches_; }
@@ -92,8 +98,9 @@ public:
     int device() const { return device_; }
     cudaStream_t stream() const { return stream_; }
 
-    // y[T][rows] = W x[T][cols] on the model's stream; path 0 chooses by T (the forward pass's own rule).
-    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false);
+    // y[T][rows] = W x[T][cols] on the model's stream (row t at y + t*ldy, ldy 0 = rows); path 0 chooses by T (the
+    // forward pass's own rule).
+    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0);
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
@@ -124,6 +131,9 @@ private:
     void step_device(int T, int first, int max_n);
     Model() = default;
     void init_device(const wl_options& opt);
+    void init_tp(const wl_options& opt);
+    void all_reduce(float* buf, int64_t n);
+    bool stop_requested(volatile const int32_t* cancel);
     void finish_open();
     void load_from_gguf(const Gguf& g);
     void build_rope_table(const float* rope_freqs, int n_rope_freqs);
@@ -138,8 +148,16 @@ private:
                 int first_logit_row, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     uint8_t* arena_alloc(int64_t bytes);
 
-    Config c_;
+    Config c_, full_;
     int device_ = 0;
+    // tensor parallelism: this rank's share of rows (q/k/v, gate/up, the head) and columns (o, down)
+    int tp_size_ = 1, tp_rank_ = 0;
+    std::unique_ptr<Comm> comm_;
+    int vocab_part_ = 0;                  // output-head rows per rank (the last rank's may hold fewer real rows)
+    float* logits_part_ = nullptr;        // [rows][vocab_part_] this rank's head rows
+    float* logits_all_ = nullptr;         // [tp][rows][vocab_part_] every rank's, after the all-gather
+    int32_t* flag_d_ = nullptr;           // the cancel flag agreed over ranks (device, pinned host)
+    int32_t* flag_h_ = nullptr;
     int max_context_ = 0;
     int max_batch_ = 64;
     int prefill_path_ = 0;
