@@ -250,6 +250,7 @@ def main():
     ap.add_argument("--layers", type=int, default=80)
     ap.add_argument("--impl", default="windlass", choices=["windlass", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--tp-nccl-only", action="store_true", help="all-reduce with NCCL only (no fused peer-memory path)")
     ap.add_argument("--sweep", action="store_true", help="configs[1] matvec sweep instead of the decode benchmark")
     ap.add_argument("--sweep-n", type=int, default=8192)
     ap.add_argument("--formats", default="q4_K,q6_K,q8_0,iq4_xs,iq2_xxs")
@@ -288,7 +289,11 @@ def main():
     ctx = args.prompt + 2 * (steps + warm) + 64
     t0 = time.perf_counter()
     trace(f"opening synthetic model, {args.layers} layers, context {ctx}, tensor parallel over {world} GPU(s)")
-    m = tp.open_group_model(dist, local, synthetic=spec, max_context=ctx)
+    m = tp.open_group_model(dist, local, synthetic=spec, max_context=ctx, tp_nccl_only=int(args.tp_nccl_only))
+    allreduce = None
+    if world > 1:
+        allreduce = "fused into the o/down matvec and the next norm over NVLink peer memory" if m.info.tp_fused \
+            else "NCCL ncclAllReduce"
     load_s = time.perf_counter() - t0
     rng = np.random.default_rng(0)          # every rank runs the same tokens
     seqs = [m.new_sequence() for _ in range(B)]
@@ -366,7 +371,7 @@ def main():
                 "dtype": "q4_K/q6_K weights, f32 compute", "data": "synthetic",
                 "config": {"workload": f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
                                        f"{args.layers} layers", "batch": B, "prompt": args.prompt,
-                           "parallelism": f"tp{world} (NCCL all-reduce x2 per layer)" if world > 1 else "1 GPU",
+                           "parallelism": f"tp{world}, all-reduce x2 per layer: {allreduce}" if world > 1 else "1 GPU",
                            "l2": "inputs larger than L2 (39.5 GB of weights read per step)"},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                         "d2h_bytes_per_step": 4 * B * spec.vocab},

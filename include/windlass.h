@@ -77,7 +77,10 @@ typedef struct wl_options {
                                 attention output and down projections by columns, with an NCCL all-reduce after each
                                 of the latter two (dense models; head and KV-head counts divisible by tp_size). */
     int32_t tp_rank;         /* this caller's rank, 0 .. tp_size-1 */
-    int32_t reserved[7];
+    int32_t tp_nccl_only;    /* 0: decode-step all-reduces fused into the producing matvec and the consuming norm over
+                                NVLink peer memory (CUDA IPC), falling back to NCCL when the GPUs cannot map each
+                                other's memory; 1: NCCL all-reduce only */
+    int32_t reserved[6];
     uint8_t tp_id[128];      /* the group's id: wl_tp_unique_id on one rank, the same bytes passed to every rank */
 } wl_options;
 
@@ -88,6 +91,7 @@ typedef struct wl_info {
     int64_t device_bytes;    /* device memory the model holds now */
     char arch[32];
     int32_t tp_size, tp_rank;
+    int32_t tp_fused;        /* 1: decode-step all-reduces run fused over peer memory (else NCCL) */
 } wl_info;
 
 typedef struct wl_stats {

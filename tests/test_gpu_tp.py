@@ -3,7 +3,9 @@
 - the prompt's logits on every rank match the oracle within 1e-3 of their standard deviation, argmax equal;
 - configs[0] greedy decode gives the oracle's tokens;
 - every rank returns the same logits (the all-reduce and the head's all-gather leave no rank behind);
-- ForwardBatch rows equal single runs (bit-identical at 2 ranks, where each all-reduced value is one sum of two).
+- ForwardBatch rows equal single runs (bit-identical at 2 ranks, where each all-reduced value is one sum of two);
+- the decode-step all-reduces fused into the matvec and the norm over peer memory give what NCCL's give (bit for bit
+  at 2 ranks), and are the ones in use.
 
 Needs at least 2 GPUs; WL_TP_TEST_GPUS picks how many ranks (default 2).
 """
@@ -37,11 +39,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def run_ranks(n, spec, out, steps=16, graphs=1, timeout=300):
+def run_ranks(n, spec, out, steps=16, graphs=1, nccl_only=0, timeout=300):
     """torchrun of tests/tp_worker.py on n GPUs; every rank's saved results."""
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "tp_worker.py"),
-           "--spec", spec, "--out", str(out), "--steps", str(steps), "--graphs", str(graphs)]
+           "--spec", spec, "--out", str(out), "--steps", str(steps), "--graphs", str(graphs),
+           "--nccl-only", str(nccl_only)]
     p = subprocess.Popen(cmd, cwd=ROOT, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
                          start_new_session=True)
     try:
@@ -61,7 +64,16 @@ def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
         pytest.skip(f"needs {n} GPUs")
     O = oracle
     sp = spec_of(spec)
-    res = run_ranks(n, spec, tmp_path)
+    (tmp_path / "fused").mkdir()
+    (tmp_path / "nccl").mkdir()
+    res = run_ranks(n, spec, tmp_path / "fused")
+    assert all(int(r["fused"]) == 1 for r in res), "the GPUs could not map each other's memory (fused all-reduce off)"
+    ref = run_ranks(n, spec, tmp_path / "nccl", nccl_only=1)
+    assert all(int(r["fused"]) == 0 for r in ref)
+    if n == 2:
+        # two partials: the fused sum p0 + p1 and NCCL's sum are the same float operation
+        for k in ("prefill", "tokens", "decode", "batch", "single"):
+            assert np.array_equal(res[0][k], ref[0][k]), f"fused and NCCL all-reduce differ in {k}"
     for r in range(1, n):
         for k in ("prefill", "tokens", "decode", "batch"):
             assert np.array_equal(res[r][k], res[0][k]), f"rank {r} returned other {k} than rank 0"

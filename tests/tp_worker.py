@@ -30,6 +30,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--graphs", type=int, default=1)
+    ap.add_argument("--nccl-only", type=int, default=0)
     args = ap.parse_args()
 
     import torch
@@ -39,10 +40,11 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=240))
     spec = spec_of(args.spec)
-    m = tp.open_group_model(dist, local, synthetic=spec, max_context=256, use_graphs=args.graphs)
+    m = tp.open_group_model(dist, local, synthetic=spec, max_context=256, use_graphs=args.graphs,
+                            tp_nccl_only=args.nccl_only)
     assert m.info.tp_size == world and m.info.tp_rank == rank
     prompt = np.random.default_rng(0).integers(0, spec.vocab, args.prompt).astype(np.int32)
-    res = {"prompt": prompt, "prefill": m.forward(prompt, all_logits=True).copy()}
+    res = {"prompt": prompt, "prefill": m.forward(prompt, all_logits=True).copy(), "fused": m.info.tp_fused}
     toks, dec = [], []
     logits = res["prefill"][-1]
     for i in range(args.steps):

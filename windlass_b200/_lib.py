@@ -47,7 +47,8 @@ _EXC = {WL_EINVAL: ArgumentError, WL_EUNSUPPORTED: NotSupportedError, WL_EFORMAT
 class Options(C.Structure):
     _fields_ = [("size", C.c_int32), ("device", C.c_int32), ("max_context", C.c_int32), ("max_batch", C.c_int32),
                 ("resident", C.c_int32), ("prefill_path", C.c_int32), ("use_graphs", C.c_int32),
-                ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("reserved", C.c_int32 * 7),
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("tp_nccl_only", C.c_int32),
+                ("reserved", C.c_int32 * 6),
                 ("tp_id", C.c_uint8 * 128)]
 
 
@@ -55,7 +56,7 @@ class Info(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("layers", "embd", "heads", "kv_heads", "head_dim", "vocab", "context_length",
                                           "max_context", "expert_count", "expert_used", "expert_ff", "moe")] + \
                [("weight_bytes", C.c_int64), ("device_bytes", C.c_int64), ("arch", C.c_char * 32),
-                ("tp_size", C.c_int32), ("tp_rank", C.c_int32)]
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("tp_fused", C.c_int32)]
 
 
 class Stats(C.Structure):

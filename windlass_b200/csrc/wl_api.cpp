@@ -165,6 +165,7 @@ int32_t wl_info_get(const wl_model* model, wl_info* info)
         strncpy(info->arch, c.arch.c_str(), sizeof info->arch - 1);
         info->tp_size = model->m->tp_size();
         info->tp_rank = model->m->tp_rank();
+        info->tp_fused = model->m->tp_fused() ? 1 : 0;
         return WL_OK;
     });
 }

@@ -88,10 +88,14 @@ void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s
 }
 
 __global__ void k_embed(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows, int cols,
-                        const int32_t* __restrict__ tokens, float scale, float* __restrict__ x, int32_t* bad)
+                        const int32_t* __restrict__ tokens, float scale, float* __restrict__ x, int32_t* bad,
+                        unsigned long long* epoch)
 {
     pdl_trigger();
     pdl_wait();
+    // a new step: the fused all-reduces of this step take sequence numbers from the next epoch (every later kernel
+    // of the step reads it after its own wait, so after this kernel has completed)
+    if (epoch && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *epoch += 1;
     const int t = blockIdx.y;
     const int be = block_elems(type), bb = block_bytes(type);
     const int tok = tokens[t];
@@ -107,10 +111,10 @@ __global__ void k_embed(int type, const uint8_t* __restrict__ w, int64_t row_byt
 }
 
 void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const int32_t* tokens, int T,
-           float scale, float* x, int32_t* bad, cudaStream_t s)
+           float scale, float* x, int32_t* bad, cudaStream_t s, unsigned long long* epoch)
 {
     dim3 grid(grid_for(cols, 256), T);
-    launch(k_embed, dim3(grid), dim3(256), 0, s, type, w, row_bytes, rows, cols, tokens, scale, x, bad);
+    launch(k_embed, dim3(grid), dim3(256), 0, s, type, w, row_bytes, rows, cols, tokens, scale, x, bad, epoch);
     launched();
 }
 

@@ -16,6 +16,35 @@ struct RowKV {
 
 namespace k {
 
+// ---- the tensor-parallel all-reduce fused into the matvec that produces it and the norm that consumes it ----
+// Every rank holds one buffer: per slot and source rank a flag (the sequence number of the source's last published
+// partial in that slot), then per slot, source rank and column the source's partial output rows. A producing matvec
+// stores its rows into every rank's buffer (peer memory over NVLink) and its last CTA publishes the slot's flag on
+// every rank; the consuming norm waits (bounded) for every source's flag and sums the partials in rank order, so
+// every rank gets bit-identical sums. Sequence numbers are epoch * AR_STEP + index within the step; the epoch is a
+// device counter the step's embedding kernel advances, so graph replays need no host input.
+constexpr int AR_SLOTS = 4;
+constexpr int AR_MAX_RANKS = 8;
+constexpr int AR_STEP = 1024;                   // most fused all-reduces in one step
+constexpr int AR_COLS = 8;                      // columns (decode rows) one slot holds
+constexpr size_t AR_HEADER = 1024;              // flags [AR_SLOTS][AR_MAX_RANKS] u64, tickets, epoch
+constexpr size_t AR_TICKETS = 256, AR_EPOCH = 512;
+inline size_t ar_buffer_bytes(int G, int E) { return AR_HEADER + (size_t)AR_SLOTS * G * AR_COLS * E * sizeof(float); }
+struct ArOut {                                  // the producer's side
+    float* data[AR_MAX_RANKS];                  // every rank's partials region (peers' mapped into this process)
+    unsigned long long* flags[AR_MAX_RANKS];    // every rank's flags
+    unsigned* tickets;                          // this rank's per-slot CTA tickets
+    const unsigned long long* epoch;            // this rank's step counter
+    int idx, G, rank, E;
+};
+struct ArIn {                                   // the consumer's side
+    const float* data;                          // this rank's partials region
+    const unsigned long long* flags;            // this rank's flags
+    const unsigned long long* epoch;
+    int* err;                                   // set to 2 when a wait gives up
+    int idx, G, E, row0;                        // row0: first partial row the consumer's row 0 reads
+};
+
 // Copies the I-quant tables into the current device's constant memory (once per device).
 void init_tables();
 // Kernels launched by this process so far; note_launch() checks and counts a launch made in another file.
@@ -29,7 +58,7 @@ void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s
 // Rows `tokens[t]` of an embedding matrix (cols values each, row_bytes apart) decoded to x[t*cols...], times scale
 // when scale != 0 (LayerStream.EmbedRow + Transformer.cs:93-94). Out-of-range ids set *bad_token.
 void embed(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const int32_t* tokens, int T,
-           float scale, float* x, int32_t* bad_token, cudaStream_t s);
+           float scale, float* x, int32_t* bad_token, cudaStream_t s, unsigned long long* epoch = nullptr);
 
 // y[t*ldy + r] = W[r] . x[t*ldx...] for t < ncols (1..8), rows r of W (row_bytes apart). Each column is computed
 // with the same instruction sequence whatever ncols is, so a column's result does not depend on its neighbours.
@@ -57,8 +86,9 @@ void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaSt
 // x[t] += o[t] * rs (when o), then y[t] = RmsNormRows(x[t]) * w for T rows of E values, and when p is given y's
 // activations prepared as xprep would (bit-identical), in one kernel. E a multiple of 256, at most 8192.
 bool norm_prep_supported(int E);
+// With ar, o is the rank-ordered sum of the fused all-reduce's partials instead (o itself unused).
 void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
-               cudaStream_t s);
+               cudaStream_t s, const ArIn* ar = nullptr);
 // A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
 struct alignas(64) WeightMap {
     uint8_t bytes[128];
@@ -80,8 +110,9 @@ constexpr int Q6K_TILE = 3360;     // bytes of one Q6_K tile: 16 rows x one 210-
 bool tiles_supported(int type, int cols);
 int64_t tile_bytes(int type, int rows, int cols);
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
+// With ar (rows = ar->E, at most AR_COLS columns) the results go to every rank's all-reduce slot instead of y.
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s);
+                  int64_t ldy, int* err, cudaStream_t s, const ArOut* ar = nullptr);
 
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);

@@ -98,6 +98,118 @@ void Model::init_tp(const wl_options& opt)
     flag_d_ = dalloc<int32_t>(1);
     flag_h_ = halloc<int32_t>(1);
     comm_.reset(new Comm(opt.tp_id, tp_size_, tp_rank_));
+    init_fused_ar(opt);
+}
+
+// Maps every rank's all-reduce buffer into this process (CUDA IPC handles exchanged with an NCCL all-gather). All
+// ranks agree on the outcome: if any rank cannot map a peer, every rank keeps NCCL for all its all-reduces.
+void Model::init_fused_ar(const wl_options& opt)
+{
+    const int G = tp_size_;
+    if (opt.tp_nccl_only || G > k::AR_MAX_RANKS || 2 * c_.layers + 2 > k::AR_STEP || !k::norm_prep_supported(c_.embd)) return;
+    const size_t bytes = k::ar_buffer_bytes(G, c_.embd);
+    ar_buf_ = dalloc<uint8_t>((int64_t)bytes);
+    WL_CUDA(cudaMemset(ar_buf_, 0, bytes));
+    cudaIpcMemHandle_t mine;
+    int failed = cudaIpcGetMemHandle(&mine, ar_buf_) != cudaSuccess;
+    cudaGetLastError();
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t* hd = dalloc<uint8_t>(64 * G);
+    std::vector<cudaIpcMemHandle_t> all(G);
+    WL_CUDA(cudaMemcpy(hd + 64 * tp_rank_, &mine, 64, cudaMemcpyHostToDevice));
+    comm_->allgather(hd + 64 * tp_rank_, hd, 64, stream_);
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    WL_CUDA(cudaMemcpy(all.data(), hd, 64 * (size_t)G, cudaMemcpyDeviceToHost));
+    dfree(hd);
+    for (int g = 0; g < G && !failed; ++g) {
+        if (g == tp_rank_) { ar_peer_[g] = ar_buf_; continue; }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[g], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            failed = 1;
+        } else {
+            ar_peer_[g] = (uint8_t*)p;
+        }
+    }
+    *flag_h_ = failed;
+    WL_CUDA(cudaMemcpy(flag_d_, flag_h_, sizeof(int32_t), cudaMemcpyHostToDevice));
+    comm_->allreduce_max(flag_d_, 1, stream_);
+    WL_CUDA(cudaStreamSynchronize(stream_));
+    WL_CUDA(cudaMemcpy(flag_h_, flag_d_, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    ar_on_ = *flag_h_ == 0;
+    if (!ar_on_) close_fused_ar();
+}
+
+// Every rank stops using the buffers before any rank unmaps or frees its own (two NCCL barriers around the unmap).
+void Model::close_fused_ar()
+{
+    if (!ar_buf_) return;
+    auto barrier = [&] {
+        WL_CUDA(cudaStreamSynchronize(stream_));
+        comm_->allreduce_max(flag_d_, 1, stream_);
+        WL_CUDA(cudaStreamSynchronize(stream_));
+    };
+    barrier();
+    for (int g = 0; g < tp_size_; ++g) {
+        if (g != tp_rank_ && ar_peer_[g]) cudaIpcCloseMemHandle(ar_peer_[g]);
+        ar_peer_[g] = nullptr;
+    }
+    barrier();
+    dfree(ar_buf_);
+    ar_on_ = false;
+}
+
+// The output projection of a sublayer (o or down) summed over the tensor-parallel ranks into the next norm's input:
+// fused into the matvec (stores to every rank's slot) and the next norm (waits and sums) for decode steps, else the
+// matvec into o_ and an NCCL all-reduce. One GPU: the matvec into o_.
+void Model::matmul_reduce(const Weight& w, const float* x, int T)
+{
+    const int E = c_.embd;
+    if (ar_on_ && T <= k::AR_COLS && w.tiles && w.row_base % 16 == 0 && w.rows == E && xprep_buf_ && ar_idx_ < k::AR_STEP) {
+        k::ArOut ar{};
+        for (int g = 0; g < tp_size_; ++g) {
+            ar.data[g] = reinterpret_cast<float*>(ar_peer_[g] + k::AR_HEADER);
+            ar.flags[g] = reinterpret_cast<unsigned long long*>(ar_peer_[g]);
+        }
+        ar.tickets = reinterpret_cast<unsigned*>(ar_buf_ + k::AR_TICKETS);
+        ar.epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
+        ar.idx = ar_idx_++;
+        ar.G = tp_size_;
+        ar.rank = tp_rank_;
+        ar.E = E;
+        matmul(w, x, T, o_, 0, true, 0, &ar);
+        pending_ar_ = ar.idx;
+        return;
+    }
+    matmul(w, x, T, o_, 0, true);
+    all_reduce(o_, (int64_t)T * E);
+}
+
+// The consumer side of the pending fused all-reduce for rows row0 .. row0+T-1; false when none is pending.
+bool Model::pending_ar_in(int T, int row0, k::ArIn* in)
+{
+    if (pending_ar_ < 0) return false;
+    (void)T;
+    in->data = reinterpret_cast<const float*>(ar_buf_ + k::AR_HEADER);
+    in->flags = reinterpret_cast<const unsigned long long*>(ar_buf_);
+    in->epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
+    in->err = err_d_;
+    in->idx = pending_ar_;
+    in->G = tp_size_;
+    in->E = c_.embd;
+    in->row0 = row0;
+    pending_ar_ = -1;
+    return true;
+}
+
+// The start of every step: the embedding of its tokens (advancing the fused all-reduce epoch).
+void Model::begin_step(int T)
+{
+    ar_idx_ = 0;
+    pending_ar_ = -1;
+    k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_,
+             bad_d_, stream_, ar_on_ ? reinterpret_cast<unsigned long long*>(ar_buf_ + k::AR_EPOCH) : nullptr);
+    pending_residual_ = false;
 }
 
 // The cancel flag, polled between stages (Transformer.cs:99,158). Under tensor parallelism the ranks take the maximum
@@ -556,6 +668,9 @@ Model::~Model()
     if (xprep_buf_) cudaFree(xprep_buf_);
     dfree(att_part_);
     dfree(err_d_);
+    if (comm_) {
+        try { close_fused_ar(); } catch (...) {}
+    }
     dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
@@ -675,7 +790,8 @@ void Model::ensure_workspace(int T, int logit_rows)
 // ---------------------------------------------------------------------------------------------------------------------
 // y[T][rows] = W x. Formats with a tensor-core matvec take activations prepared by k::xprep (8 columns at a time);
 // reuse_x says x is the input of the previous matmul as well, so its prepared form can be reused.
-void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x, int64_t ldy)
+void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x, int64_t ldy,
+                   const k::ArOut* ar)
 {
     if (ldy <= 0) ldy = w.rows;
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
@@ -693,7 +809,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
             }
             const int mark = profile_begin();
             k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * ldy, ldy, err_d_,
-                            stream_);
+                            stream_, ar);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;
@@ -793,8 +909,7 @@ void Model::ffn_dense(const LayerW& L, int T)
         k::swiglu(g_, u_, (int64_t)T * F, stream_);
     }
     profile_end(sm, WL_PROFILE_SWIGLU, 0.0);
-    matmul(L.down, g_, T, o_, 0, true);
-    all_reduce(o_, (int64_t)T * c_.embd);
+    matmul_reduce(L.down, g_, T);
 }
 
 // MoeFfn (src/Transformer.cs:259-311): router, top-k, then each chosen expert runs once on the rows routed to it, in
@@ -887,8 +1002,7 @@ void Model::layer(int l, int T, int max_n)
     profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
     prep_x_ = nullptr;
     if (prepped) { prep_x_ = att_; prep_cols_ = QD; prep_nc_ = T; }
-    matmul(L.o, att_, T, o_, 0, true);
-    all_reduce(o_, n);
+    matmul_reduce(L.o, att_, T);
     if (c_.post_norms) {
         k::rmsnorm(o_, T, E, L.post_attn_norm.d, c_.rms_eps, o_, stream_);
         k::residual(x_, o_, rs, n, stream_);
@@ -921,7 +1035,10 @@ void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
         const bool prep = prep_for_mma && T <= 8 && xprep_buf_;
         k::XPrep p{};
         if (prep) p = k::xprep_view(xprep_buf_, E, T);
-        k::norm_prep(x_, pending_residual_ ? o_ : nullptr, rs, T, E, w.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_);
+        k::ArIn ar{};
+        const bool fused = pending_residual_ && pending_ar_in(T, 0, &ar);
+        k::norm_prep(x_, pending_residual_ ? o_ : nullptr, rs, T, E, w.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_,
+                     fused ? &ar : nullptr);
         if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = T; }
     } else {
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
@@ -941,8 +1058,10 @@ void Model::head(int T, int first)
         const bool prep = output_.tiles && n <= 8 && xprep_buf_;
         k::XPrep p{};
         if (prep) p = k::xprep_view(xprep_buf_, E, n);
+        k::ArIn ar{};
+        const bool fused = pending_residual_ && pending_ar_in(n, first, &ar);
         k::norm_prep(x_ + (int64_t)first * E, pending_residual_ ? o_ + (int64_t)first * E : nullptr, rs, n, E,
-                     out_norm_.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_);
+                     out_norm_.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_, fused ? &ar : nullptr);
         if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = n; }
     } else {
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
@@ -978,8 +1097,7 @@ void Model::upload_step(int T, const RowKV* rows, const int32_t* pos, const int3
 // Embedding, every layer and the head, all on the device (no cancel or progress points).
 void Model::step_device(int T, int first, int max_n)
 {
-    k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
-    pending_residual_ = false;
+    begin_step(T);
     for (int l = 0; l < c_.layers; ++l) layer(l, T, max_n);
     head(T, first);
 }
@@ -1001,8 +1119,7 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
         // the whole step ran as one graph; a cancel flag set meanwhile is seen by the next call
     } else if (!cancel && !progress) step_device(T, first, max_n);
     else {
-        k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_, bad_d_, stream_);
-        pending_residual_ = false;
+        begin_step(T);
         for (int l = 0; l < c_.layers; ++l) {
             if (l == 0 ? stop0 : stop_requested(cancel)) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
             layer(l, T, max_n);

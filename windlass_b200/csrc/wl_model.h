@@ -90,6 +90,7 @@ public:
     const Config& full_config() const { return full_; }
     int tp_size() const { return tp_size_; }
     int tp_rank() const { return tp_rank_; }
+    bool tp_fused() const { return ar_on_; }
     int max_context() const { return max_context_; }
     const Stats& stats() const { return stats_; }
     int64_t graph_launches() const { return graph_launches_; }
@@ -100,7 +101,8 @@ public:
 
     // y[T][rows] = W x[T][cols] on the model's stream (row t at y + t*ldy, ldy 0 = rows); path 0 chooses by T (the
     // forward pass's own rule).
-    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0);
+    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0,
+                const k::ArOut* ar = nullptr);
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
@@ -133,6 +135,11 @@ private:
     void init_device(const wl_options& opt);
     void init_tp(const wl_options& opt);
     void all_reduce(float* buf, int64_t n);
+    void init_fused_ar(const wl_options& opt);
+    void close_fused_ar();
+    void matmul_reduce(const Weight& w, const float* x, int T);
+    bool pending_ar_in(int T, int row0, k::ArIn* in);
+    void begin_step(int T);
     bool stop_requested(volatile const int32_t* cancel);
     void finish_open();
     void load_from_gguf(const Gguf& g);
@@ -158,6 +165,12 @@ private:
     float* logits_all_ = nullptr;         // [tp][rows][vocab_part_] every rank's, after the all-gather
     int32_t* flag_d_ = nullptr;           // the cancel flag agreed over ranks (device, pinned host)
     int32_t* flag_h_ = nullptr;
+    // the fused all-reduce (k::ArOut / k::ArIn): this rank's buffer and every peer's, mapped through CUDA IPC
+    uint8_t* ar_buf_ = nullptr;
+    uint8_t* ar_peer_[k::AR_MAX_RANKS] = {};
+    bool ar_on_ = false;
+    int ar_idx_ = 0;                      // fused all-reduces enqueued so far in the current step
+    int pending_ar_ = -1;                 // index of the all-reduce whose sum the next norm consumes, or -1
     int max_context_ = 0;
     int max_batch_ = 64;
     int prefill_path_ = 0;
