@@ -17,32 +17,29 @@ struct RowKV {
 namespace k {
 
 // ---- the tensor-parallel all-reduce fused into the matvec that produces it and the norm that consumes it ----
-// Every rank holds one buffer: per slot and source rank a flag (the sequence number of the source's last published
-// partial in that slot), then per slot, source rank and column the source's partial output rows. A producing matvec
-// stores its rows into every rank's buffer (peer memory over NVLink) and its last CTA publishes the slot's flag on
-// every rank; the consuming norm waits (bounded) for every source's flag and sums the partials in rank order, so
-// every rank gets bit-identical sums. Sequence numbers are epoch * AR_STEP + index within the step; the epoch is a
-// device counter the step's embedding kernel advances, so graph replays need no host input.
+// Every rank holds one buffer (mapped into every peer's process): per slot and source rank a flag, then per slot and
+// column its own partial output rows. The producing matvec writes its rows into its own slot like any output. The
+// consuming norm announces on every peer that this rank's partial for sequence number q is in place (a release
+// store into the peer's flag), waits (bounded) until every peer has announced q, then reads the peers' partials
+// over NVLink and sums all of them in rank order, so every rank gets bit-identical sums. Sequence numbers are
+// epoch * AR_STEP + index within the step; the epoch is a device counter the step's embedding kernel advances, so
+// graph replays need no host input, and the slot (the index mod AR_SLOTS) is known when the step is enqueued.
 constexpr int AR_SLOTS = 4;
 constexpr int AR_MAX_RANKS = 8;
-constexpr int AR_STEP = 1024;                   // most fused all-reduces in one step
+constexpr int AR_STEP = 1024;                   // most fused all-reduces in one step (a multiple of AR_SLOTS)
 constexpr int AR_COLS = 8;                      // columns (decode rows) one slot holds
-constexpr size_t AR_HEADER = 1024;              // flags [AR_SLOTS][AR_MAX_RANKS] u64, tickets, epoch
-constexpr size_t AR_TICKETS = 256, AR_EPOCH = 512;
-inline size_t ar_buffer_bytes(int G, int E) { return AR_HEADER + (size_t)AR_SLOTS * G * AR_COLS * E * sizeof(float); }
-struct ArOut {                                  // the producer's side
-    float* data[AR_MAX_RANKS];                  // every rank's partials region (peers' mapped into this process)
-    unsigned long long* flags[AR_MAX_RANKS];    // every rank's flags
-    unsigned* tickets;                          // this rank's per-slot CTA tickets
+constexpr size_t AR_HEADER = 1024;              // flags [AR_SLOTS][AR_MAX_RANKS] u64 at 0, the epoch u64 at AR_EPOCH
+constexpr size_t AR_EPOCH = 512;
+static_assert(AR_STEP % AR_SLOTS == 0, "the slot of an all-reduce must not depend on the epoch");
+inline size_t ar_buffer_bytes(int E) { return AR_HEADER + (size_t)AR_SLOTS * AR_COLS * E * sizeof(float); }
+inline size_t ar_slot_offset(int idx, int E) { return AR_HEADER + (size_t)(idx % AR_SLOTS) * AR_COLS * E * sizeof(float); }
+struct ArIn {
+    const float* data[AR_MAX_RANKS];            // every rank's partials region (peers' mapped into this process)
+    unsigned long long* peer_flags[AR_MAX_RANKS];   // every rank's flags (this rank announces into them)
+    const unsigned long long* flags;            // this rank's flags (the peers announce into them)
     const unsigned long long* epoch;            // this rank's step counter
-    int idx, G, rank, E;
-};
-struct ArIn {                                   // the consumer's side
-    const float* data;                          // this rank's partials region
-    const unsigned long long* flags;            // this rank's flags
-    const unsigned long long* epoch;
     int* err;                                   // set to 2 when a wait gives up
-    int idx, G, E, row0;                        // row0: first partial row the consumer's row 0 reads
+    int idx, G, rank, E, row0;                  // row0: first partial row the consumer's row 0 reads
 };
 
 // Copies the I-quant tables into the current device's constant memory (once per device).
@@ -86,7 +83,7 @@ void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaSt
 // x[t] += o[t] * rs (when o), then y[t] = RmsNormRows(x[t]) * w for T rows of E values, and when p is given y's
 // activations prepared as xprep would (bit-identical), in one kernel. E a multiple of 256, at most 8192.
 bool norm_prep_supported(int E);
-// With ar, o is the rank-ordered sum of the fused all-reduce's partials instead (o itself unused).
+// With ar, o is the rank-ordered sum of every rank's partial in the fused all-reduce's slot instead (o unused).
 void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
                cudaStream_t s, const ArIn* ar = nullptr);
 // A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
@@ -110,9 +107,8 @@ constexpr int Q6K_TILE = 3360;     // bytes of one Q6_K tile: 16 rows x one 210-
 bool tiles_supported(int type, int cols);
 int64_t tile_bytes(int type, int rows, int cols);
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
-// With ar (rows = ar->E, at most AR_COLS columns) the results go to every rank's all-reduce slot instead of y.
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, const ArOut* ar = nullptr);
+                  int64_t ldy, int* err, cudaStream_t s);
 
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);

@@ -120,39 +120,21 @@ __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* e
     return *epoch * (unsigned long long)AR_STEP + (unsigned long long)idx;
 }
 
-// This rank's partial y[col][row] into its part of every rank's slot.
-__device__ __forceinline__ void ar_store(const ArOut& ar, unsigned long long q, int col, int row, float v)
+// The consumer's side of the fused all-reduce, run by every thread of every CTA of the consuming kernel after its
+// grid-dependency wait (so this rank's producing matvec has completed): CTA 0 announces sequence number q on every
+// peer (this rank's partial sits in its own slot), then threads 0..G-1 wait for each peer's announcement of q or
+// later. A wait gives up after about half a minute, records code 2 in *err and returns (the sums are then garbage
+// and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot hang the GPU.
+__device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q)
 {
     const int slot = (int)(q % AR_SLOTS);
-    const size_t off = (((size_t)slot * ar.G + ar.rank) * AR_COLS + col) * (size_t)ar.E + row;
-    for (int g = 0; g < ar.G; ++g) ar.data[g][off] = v;
-}
-
-// Called by every thread of the CTA after its ar_store calls (stored: this thread made some): the CTA's stores are
-// made visible system-wide, and the grid's last CTA (the one that takes the last ticket) publishes sequence number q
-// in the slot's flag on every rank.
-__device__ __forceinline__ void ar_publish(const ArOut& ar, unsigned long long q, bool stored)
-{
-    if (stored) __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int slot = (int)(q % AR_SLOTS);
-        const unsigned t = atomicAdd(&ar.tickets[slot], 1u);
-        if (t == gridDim.x - 1) {
-            ar.tickets[slot] = 0u;      // the slot's next producer starts after this grid has completed
-            __threadfence_system();
-            for (int g = 0; g < ar.G; ++g) st_release_sys(ar.flags[g] + slot * AR_MAX_RANKS + ar.rank, q);
-        }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        __threadfence_system();
+        for (int g = 0; g < ar.G; ++g)
+            if (g != ar.rank) st_release_sys(ar.peer_flags[g] + slot * AR_MAX_RANKS + ar.rank, q);
     }
-}
-
-// Waits until every rank has published sequence number q (or later) in the slot; threads 0..G-1 poll one source
-// each. Gives up after about half a minute, records code 2 in *err and returns (the sums are then garbage and the
-// host reports WL_ETIMEDOUT), so a rank that never arrives cannot hang the GPU.
-__device__ __forceinline__ void ar_wait(const ArIn& ar, unsigned long long q)
-{
-    if (threadIdx.x < (unsigned)ar.G) {
-        const unsigned long long* f = ar.flags + (q % AR_SLOTS) * AR_MAX_RANKS + threadIdx.x;
+    if (threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank) {
+        const unsigned long long* f = ar.flags + slot * AR_MAX_RANKS + threadIdx.x;
         for (uint32_t n = 0; ld_acquire_sys(f) < q; ++n) {
             if (n >= (1u << 27)) { atomicExch(ar.err, 2); break; }
             if (n >= 64) __nanosleep(256);
@@ -203,15 +185,15 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
     if (RES) {
         float4 oa, ob;
         if (ar.G > 0) {
-            // the fused all-reduce: every rank's partial of this row, summed in rank order
+            // the fused all-reduce: every rank's partial of this row (peers' over NVLink), summed in rank order
             const unsigned long long q = ar_seq(ar.epoch, ar.idx);
-            ar_wait(ar, q);
-            const float* p0 = ar.data + ((size_t)(q % AR_SLOTS) * ar.G * AR_COLS + ar.row0 + t) * (size_t)E + i0;
-            oa = __ldcg(reinterpret_cast<const float4*>(p0));
-            ob = __ldcg(reinterpret_cast<const float4*>(p0 + 4));
+            ar_sync(ar, q);
+            const size_t off = ((size_t)(q % AR_SLOTS) * AR_COLS + ar.row0 + t) * (size_t)E + i0;
+            oa = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off));
+            ob = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off + 4));
             for (int src = 1; src < ar.G; ++src) {
-                const float* ps = p0 + (size_t)src * AR_COLS * E;
-                const float4 ua = __ldcg(reinterpret_cast<const float4*>(ps)), ub = __ldcg(reinterpret_cast<const float4*>(ps + 4));
+                const float* ps = ar.data[src] + off;
+                const float4 ua = __ldcv(reinterpret_cast<const float4*>(ps)), ub = __ldcv(reinterpret_cast<const float4*>(ps + 4));
                 oa = make_float4(__fadd_rn(oa.x, ua.x), __fadd_rn(oa.y, ua.y), __fadd_rn(oa.z, ua.z), __fadd_rn(oa.w, ua.w));
                 ob = make_float4(__fadd_rn(ob.x, ub.x), __fadd_rn(ob.y, ub.y), __fadd_rn(ob.z, ub.z), __fadd_rn(ob.w, ub.w));
             }
@@ -331,7 +313,7 @@ template <int NC, bool TILED>
 __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt, int row_base, int rows, int nsb,
                                                     const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
-                                                    int* err, const ArOut ar)
+                                                    int* err)
 {
     using LY = Q4Layout<NC>;
     constexpr bool PACK = NC <= 2;
@@ -494,9 +476,7 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     }
     __syncthreads();
     const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
-    const unsigned long long q = ar.G > 0 ? ar_seq(ar.epoch, ar.idx) : 0ull;
-    const bool mine = col < NC && rl < Q4_ROWS && r0 + rl < rows;
-    if (mine) {
+    if (col < NC && rl < Q4_ROWS && r0 + rl < rows) {
         float sum = 0.f;
 #pragma unroll
         for (int wv = 0; wv < 8; ++wv) {
@@ -504,10 +484,8 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
             const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
             sum += v;
         }
-        if (ar.G > 0) ar_store(ar, q, col, r0 + rl, sum);
-        else y[(int64_t)col * ldy + r0 + rl] = sum;
+        y[(int64_t)col * ldy + r0 + rl] = sum;
     }
-    if (ar.G > 0) ar_publish(ar, q, mine);
 }
 
 // Repacks rows [0, rows) of a Q4_K matrix into the tile-major layout above; rows past the end are zero. One CTA per tile.
@@ -576,7 +554,7 @@ __device__ __forceinline__ uint32_t sc_pair_h2(uint32_t w, uint32_t sel, __half2
 template <int NC>
 __global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ wt, int rows, int nsb,
                                                     const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
-                                                    int* err, const ArOut ar)
+                                                    int* err)
 {
     using LY = Q6Layout<NC>;
     constexpr bool PACK = NC <= 2;
@@ -729,9 +707,7 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ 
     }
     __syncthreads();
     const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
-    const unsigned long long q = ar.G > 0 ? ar_seq(ar.epoch, ar.idx) : 0ull;
-    const bool mine = col < NC && rl < 16 && r0 + rl < rows;
-    if (mine) {
+    if (col < NC && rl < 16 && r0 + rl < rows) {
         float sum = 0.f;
 #pragma unroll
         for (int wv = 0; wv < 8; ++wv) {
@@ -739,10 +715,8 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ 
                                  : red[wv][rl][col];
             sum += v;
         }
-        if (ar.G > 0) ar_store(ar, q, col, r0 + rl, sum);
-        else y[(int64_t)col * ldy + r0 + rl] = sum;
+        y[(int64_t)col * ldy + r0 + rl] = sum;
     }
-    if (ar.G > 0) ar_publish(ar, q, mine);
 }
 
 // Repacks rows [0, rows) of a Q6_K matrix (row_bytes apart, nsb superblocks each) into the tile layout above; rows past
@@ -793,8 +767,8 @@ void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w,
     if (p && (p->cols != E || p->nc != T)) WL_THROW(WL_EINVAL, "norm_prep: prepared-activation view does not match");
     ArIn in{};
     if (ar) {
-        if (ar->E != E || ar->row0 < 0 || ar->row0 + T > AR_COLS || ar->G < 1 || ar->G > AR_MAX_RANKS || ar->idx < 0 ||
-            ar->idx >= AR_STEP)
+        if (ar->E != E || ar->row0 < 0 || ar->row0 + T > AR_COLS || ar->G < 1 || ar->G > AR_MAX_RANKS || ar->rank < 0 ||
+            ar->rank >= ar->G || ar->idx < 0 || ar->idx >= AR_STEP)
             WL_THROW(WL_EINVAL, "norm_prep: all-reduce slot does not match");
         in = *ar;
     }
@@ -863,7 +837,7 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
 
 template <int NC, bool TILED>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                       float* y, int64_t ldy, int* err, cudaStream_t s, const ArOut& ar)
+                       float* y, int64_t ldy, int* err, cudaStream_t s)
 {
     static bool attr[64] = {false};
     int dev = 0;
@@ -873,23 +847,23 @@ static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base,
         attr[dev] = true;
     }
     launch(k_mmv_q4k<NC, TILED>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles,
-           row_base, rows, nsb, (const uint8_t*)p.blocks, y, ldy, err, ar);
+           row_base, rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
 }
 
 template <bool TILED>
 static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                         float* y, int64_t ldy, int* err, cudaStream_t s, const ArOut& ar)
+                         float* y, int64_t ldy, int* err, cudaStream_t s)
 {
     switch (p.nc) {
-    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
-    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, ar); break;
+    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
     }
 }
 
@@ -898,7 +872,7 @@ void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols
 {
     (void)type;
     dispatch_q4k<false>(*reinterpret_cast<const CUtensorMap*>(map.bytes), nullptr, row_base, rows, cols / 256, p, y,
-                        ldy, err, s, ArOut{});
+                        ldy, err, s);
 }
 
 
@@ -922,7 +896,7 @@ void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_byte
 
 template <int NC>
 static void launch_q6k(const uint8_t* tiles, int rows, int nsb, const XPrep& p, float* y, int64_t ldy, int* err,
-                       cudaStream_t s, const ArOut& ar)
+                       cudaStream_t s)
 {
     static bool attr[64] = {false};
     int dev = 0;
@@ -932,44 +906,37 @@ static void launch_q6k(const uint8_t* tiles, int rows, int nsb, const XPrep& p, 
         attr[dev] = true;
     }
     launch(k_mmv_q6k<NC>, dim3((rows + 15) / 16), dim3(256), Q6Layout<NC>::SMEM, s, tiles, rows, nsb,
-           (const uint8_t*)p.blocks, y, ldy, err, ar);
+           (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
 }
 
 static void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err,
-                       cudaStream_t s, const ArOut& ar)
+                       cudaStream_t s)
 {
     const int nsb = cols / 256;
     switch (p.nc) {
-    case 1: launch_q6k<1>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 2: launch_q6k<2>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 3: launch_q6k<3>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 4: launch_q6k<4>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 5: launch_q6k<5>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 6: launch_q6k<6>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    case 7: launch_q6k<7>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
-    default: launch_q6k<8>(tiles, rows, nsb, p, y, ldy, err, s, ar); break;
+    case 1: launch_q6k<1>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 2: launch_q6k<2>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 3: launch_q6k<3>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 4: launch_q6k<4>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 5: launch_q6k<5>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 6: launch_q6k<6>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    case 7: launch_q6k<7>(tiles, rows, nsb, p, y, ldy, err, s); break;
+    default: launch_q6k<8>(tiles, rows, nsb, p, y, ldy, err, s); break;
     }
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, const ArOut* ar)
+                  int64_t ldy, int* err, cudaStream_t s)
 {
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
-    ArOut out{};
-    if (ar) {
-        if (ar->E != rows || p.nc > AR_COLS || ar->G < 1 || ar->G > AR_MAX_RANKS || ar->rank < 0 || ar->rank >= ar->G ||
-            ar->idx < 0 || ar->idx >= AR_STEP)
-            WL_THROW(WL_EINVAL, "matvec_tiles: all-reduce slot does not match");
-        out = *ar;
-    }
     if (type == 12) {
         CUtensorMap none;
         memset(&none, 0, sizeof none);
-        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s, out);
+        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s);
     } else {
-        matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s, out);
+        matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }
 }
 

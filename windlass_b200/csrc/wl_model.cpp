@@ -107,7 +107,7 @@ void Model::init_fused_ar(const wl_options& opt)
 {
     const int G = tp_size_;
     if (opt.tp_nccl_only || G > k::AR_MAX_RANKS || 2 * c_.layers + 2 > k::AR_STEP || !k::norm_prep_supported(c_.embd)) return;
-    const size_t bytes = k::ar_buffer_bytes(G, c_.embd);
+    const size_t bytes = k::ar_buffer_bytes(c_.embd);
     ar_buf_ = dalloc<uint8_t>((int64_t)bytes);
     WL_CUDA(cudaMemset(ar_buf_, 0, bytes));
     cudaIpcMemHandle_t mine;
@@ -160,25 +160,15 @@ void Model::close_fused_ar()
 }
 
 // The output projection of a sublayer (o or down) summed over the tensor-parallel ranks into the next norm's input:
-// fused into the matvec (stores to every rank's slot) and the next norm (waits and sums) for decode steps, else the
-// matvec into o_ and an NCCL all-reduce. One GPU: the matvec into o_.
+// for decode steps the matvec writes this rank's partial into its all-reduce slot and the next norm sums every
+// rank's (k::ArIn), else the matvec writes o_ and NCCL all-reduces it. One GPU: the matvec into o_.
 void Model::matmul_reduce(const Weight& w, const float* x, int T)
 {
     const int E = c_.embd;
-    if (ar_on_ && T <= k::AR_COLS && w.tiles && w.row_base % 16 == 0 && w.rows == E && xprep_buf_ && ar_idx_ < k::AR_STEP) {
-        k::ArOut ar{};
-        for (int g = 0; g < tp_size_; ++g) {
-            ar.data[g] = reinterpret_cast<float*>(ar_peer_[g] + k::AR_HEADER);
-            ar.flags[g] = reinterpret_cast<unsigned long long*>(ar_peer_[g]);
-        }
-        ar.tickets = reinterpret_cast<unsigned*>(ar_buf_ + k::AR_TICKETS);
-        ar.epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
-        ar.idx = ar_idx_++;
-        ar.G = tp_size_;
-        ar.rank = tp_rank_;
-        ar.E = E;
-        matmul(w, x, T, o_, 0, true, 0, &ar);
-        pending_ar_ = ar.idx;
+    if (ar_on_ && T <= k::AR_COLS && w.rows == E && ar_idx_ < k::AR_STEP) {
+        const int idx = ar_idx_++;
+        matmul(w, x, T, reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E)), 0, true, E);
+        pending_ar_ = idx;
         return;
     }
     matmul(w, x, T, o_, 0, true);
@@ -190,12 +180,16 @@ bool Model::pending_ar_in(int T, int row0, k::ArIn* in)
 {
     if (pending_ar_ < 0) return false;
     (void)T;
-    in->data = reinterpret_cast<const float*>(ar_buf_ + k::AR_HEADER);
+    for (int g = 0; g < tp_size_; ++g) {
+        in->data[g] = reinterpret_cast<const float*>(ar_peer_[g] + k::AR_HEADER);
+        in->peer_flags[g] = reinterpret_cast<unsigned long long*>(ar_peer_[g]);
+    }
     in->flags = reinterpret_cast<const unsigned long long*>(ar_buf_);
     in->epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
     in->err = err_d_;
     in->idx = pending_ar_;
     in->G = tp_size_;
+    in->rank = tp_rank_;
     in->E = c_.embd;
     in->row0 = row0;
     pending_ar_ = -1;
@@ -790,8 +784,7 @@ void Model::ensure_workspace(int T, int logit_rows)
 // ---------------------------------------------------------------------------------------------------------------------
 // y[T][rows] = W x. Formats with a tensor-core matvec take activations prepared by k::xprep (8 columns at a time);
 // reuse_x says x is the input of the previous matmul as well, so its prepared form can be reused.
-void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x, int64_t ldy,
-                   const k::ArOut* ar)
+void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, bool reuse_x, int64_t ldy)
 {
     if (ldy <= 0) ldy = w.rows;
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
@@ -809,7 +802,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
             }
             const int mark = profile_begin();
             k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * ldy, ldy, err_d_,
-                            stream_, ar);
+                            stream_);
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;

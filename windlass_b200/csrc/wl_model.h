@@ -101,8 +101,7 @@ public:
 
     // y[T][rows] = W x[T][cols] on the model's stream (row t at y + t*ldy, ldy 0 = rows); path 0 chooses by T (the
     // forward pass's own rule).
-    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0,
-                const k::ArOut* ar = nullptr);
+    void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0);
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
