@@ -65,9 +65,11 @@ typedef struct wl_options {
     int32_t device;          /* CUDA device ordinal */
     int32_t max_context;     /* positions per sequence; 0 = min(model context_length, 8192) (src/Engine.cs:26,62) */
     int32_t max_batch;       /* most rows in one wl_forward_batch (BatchPlan.MaxBatch = 64, src/Batch.cs:40) */
-    int32_t resident;        /* 1 or -1: every weight resident in HBM. 0 would stream layers from pinned host
-                                memory (src/LayerStream.cs); that mode is not built and wl_open returns
-                                WL_EUNSUPPORTED */
+    int32_t resident;        /* 1 or -1: every weight resident in HBM. 0: layers stream from pinned host memory
+                                (LayerStream, src/LayerStream.cs): each layer's weights (and the output head's) are
+                                copied into one of two device slots on a copy stream while the previous layer
+                                computes; the embedding, norms and biases stay resident. Decode steps then run
+                                without CUDA graphs, and prefill_path 1 is refused */
     int32_t prefill_path;    /* T > 8 prompts: 0 auto (tensor cores where the format has them), 1 fp32 CUDA cores */
     int32_t use_graphs;      /* 1: replay decode steps from captured CUDA graphs */
     int32_t tp_size;         /* tensor parallelism: ranks that share the model, one GPU each (0 or 1 = one GPU).

@@ -98,3 +98,13 @@ def test_no_cpu_fallback_in_the_product():
             if f.endswith((".py", ".cpp", ".cu", ".h", ".cuh")):
                 src = open(os.path.join(d, f), encoding="utf-8").read()
                 assert not bad.search(src), f"{f} reaches the oracle"
+
+
+def test_streamed_layers_refuse_the_cuda_core_prefill(wl):
+    """resident = 0 keeps only the tensor-core layout of streamed weights, so prefill_path 1 is refused up front."""
+    from windlass_b200.transformer import config0_spec
+    h = C.c_void_p()
+    o = wl.options(resident=0, prefill_path=1)
+    spec = config0_spec()
+    st = wl.lib().wl_open_synthetic(C.byref(spec), C.byref(o), C.byref(h))
+    assert st == wl.WL_EUNSUPPORTED and b"prefill_path 1" in wl.lib().wl_last_error()

@@ -204,3 +204,43 @@ def test_graph_replays_equal_eager_steps(wl):
             bg = g.forward_batch(sg, [3 + step, 4, 5])
             be = e.forward_batch(se, [3 + step, 4, 5])
             assert np.array_equal(bg, be), f"graph batch step {step} differs from the eager step"
+
+
+@pytest.mark.parametrize("case", ["config0", "gqa-file", "moe"])
+def test_streamed_layers_match_resident(wl, oracle, tmp_path, case):
+    """StreamingIsExact (tests/Tests.cs:305-321): weights streamed from pinned host memory through two device slots
+    (wl_options.resident = 0, LayerStream) give bit-identical logits to resident weights for prompts, decode steps
+    and ForwardBatch, and every pass copies at least every layer's bytes."""
+    from windlass_b200.transformer import synth_spec
+    if case == "config0":
+        spec, src = config0_spec(), None
+    elif case == "gqa-file":
+        spec = synth_spec("llama", 3, 2048, 32, 8, 64, 4096, 8192, rope_base=500000.0, type_attn_v=14, type_embd=12,
+                          seed=5)
+        src = oracle.write_synth(str(tmp_path / "gqa.gguf"), spec)
+    else:
+        spec = synth_spec("qwen3moe", 2, 512, 8, 4, 64, 0, 4096, experts=8, experts_used=2, expert_ff=256,
+                          rope_base=1000000.0, type_attn_v=14, type_embd=12, seed=3)
+        src = None
+
+    def open_model(resident):
+        if src:
+            return CudaTransformer(src, max_context=128, resident=resident)
+        return CudaTransformer(synthetic=spec, max_context=128, resident=resident)
+
+    prompt = np.random.default_rng(2).integers(0, spec.vocab, 24).astype(np.int32)
+    with open_model(0) as st, open_model(1) as rs:
+        a, b = st.forward(prompt, all_logits=True), rs.forward(prompt, all_logits=True)
+        assert np.array_equal(a, b), "streamed prompt logits differ from resident ones"
+        layer_bytes = st.info.weight_bytes
+        for i in range(4):
+            t = int(np.argmax(b[-1] if i == 0 else lb))
+            h0 = st.bytes_read
+            la, lb = st.forward([t], pos0=len(prompt) + i), rs.forward([t], pos0=len(prompt) + i)
+            assert np.array_equal(la, lb), f"streamed decode step {i} differs"
+            assert st.bytes_read - h0 >= 0.5 * layer_bytes, "a streamed pass must copy the layers' weights"
+        sa, sb = [st.new_sequence() for _ in range(2)], [rs.new_sequence() for _ in range(2)]
+        for k in range(2):
+            st.forward(prompt[: 6 + k], seq=sa[k])
+            rs.forward(prompt[: 6 + k], seq=sb[k])
+        assert np.array_equal(st.forward_batch(sa, [7, 9]), rs.forward_batch(sb, [7, 9]))

@@ -43,12 +43,13 @@ template <typename T> void hfree(T*& p)
 // ---------------------------------------------------------------------------------------------------------------------
 void Model::init_device(const wl_options& opt)
 {
+    streamed_ = opt.resident == 0;
+    if (streamed_ && opt.prefill_path == 1)
+        WL_THROW(WL_EUNSUPPORTED, "Streamed layers carry the tensor-core layout only; prefill_path 1 (CUDA cores) needs resident weights.");
     device_ = opt.device;
     WL_CUDA(cudaSetDevice(device_));
     k::init_tables();
     WL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-    if (opt.resident == 0)
-        WL_THROW(WL_EUNSUPPORTED, "Streaming layers from host memory (resident = 0) is not built; weights are kept in HBM.");
     max_batch_ = opt.max_batch > 0 ? opt.max_batch : 64;
     use_graphs_ = opt.use_graphs != 0;
     prefill_path_ = opt.prefill_path;
@@ -358,13 +359,27 @@ void Model::load_from_gguf(const Gguf& g)
     // vectors.
     const int G = tp_size_;
     int64_t total = 0;
+    std::vector<int64_t> raw_upper((size_t)c_.layers + 1, 0), slot_upper((size_t)c_.layers + 1, 0);
     for (const GgufTensor& t : g.tensors()) {
         const int64_t bytes = G > 1 ? t.size / G + t.size / std::max<int64_t>(t.dims[1], 1) + 256 : t.size;
+        const int st = t.ndims >= 2 ? stage_of_name(t.name) : -1;
+        if (streamed_ && st >= 0 && st <= c_.layers) {
+            // streamed matrices: bounded by their whole size, raw and in tiles (rows rounded up to 16)
+            const int64_t rows_all = t.elements() / std::max<int64_t>(t.dims[0], 1);
+            raw_upper[(size_t)st] += (t.size + 255) / 256 * 256;
+            slot_upper[(size_t)st] += ((rows_all + 15) / 16 * 16) * (t.size / std::max<int64_t>(rows_all, 1)) + 256;
+            continue;
+        }
         total += (bytes + 255) / 256 * 256 + (t.elements() * 4 / (G > 1 ? G : 1) + 255) / 256 * 256;
     }
-    if (G > 1 && c_.tied) if (const GgufTensor* t = g.find("token_embd.weight")) total += t->size / G + t->size / t->dims[1] + 512;
+    if (G > 1 && c_.tied) if (const GgufTensor* t = g.find("token_embd.weight")) {
+        const int64_t b = t->size / G + t->size / t->dims[1] + 512;
+        if (streamed_) { raw_upper.back() += b; slot_upper.back() += (t->dims[1] + 15) / 16 * 16 * (t->size / t->dims[1]) / G + 512; }
+        else total += b;
+    }
     arena_ = dalloc<uint8_t>(total);
     arena_size_ = total;
+    if (streamed_) plan_streaming(raw_upper, slot_upper);
 
     // split: WHOLE on every rank; ROWS this rank's 1/G of the rows; COLS its 1/G of every row's blocks; HEAD rows
     // rank*vocab_part_ .. +vocab_part_ (the last rank's may be fewer).
@@ -374,7 +389,7 @@ void Model::load_from_gguf(const Gguf& g)
         Weight w = weight_of(*t);
         const uint8_t* src = g.data(*t);
         if (G == 1 || sp == WHOLE) {
-            w.d = arena_alloc(w.bytes);
+            w.d = weight_alloc(w.bytes);
             WL_CUDA(cudaMemcpy(w.d, src, (size_t)w.bytes, cudaMemcpyHostToDevice));
         } else if (sp == ROWS || sp == HEAD) {
             if (w.experts != 1) WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism does not split stacked tensors.");
@@ -386,7 +401,7 @@ void Model::load_from_gguf(const Gguf& g)
             }
             w.rows = n;
             w.bytes = (int64_t)n * w.row_bytes;
-            w.d = arena_alloc(w.bytes);
+            w.d = weight_alloc(w.bytes);
             WL_CUDA(cudaMemcpy(w.d, src + (int64_t)r0 * w.row_bytes, (size_t)w.bytes, cudaMemcpyHostToDevice));
         } else {
             int b = 0, bb = 0;
@@ -395,7 +410,7 @@ void Model::load_from_gguf(const Gguf& g)
                 WL_THROW(WL_EUNSUPPORTED, t->name + ": " + std::to_string(w.cols) + " columns do not split into whole " +
                                           type_name(w.type) + " blocks over " + std::to_string(G) + " GPUs.");
             const int64_t lrb = w.row_bytes / G;
-            w.d = arena_alloc(lrb * w.rows);
+            w.d = weight_alloc(lrb * w.rows);
             WL_CUDA(cudaMemcpy2D(w.d, (size_t)lrb, src + tp_rank_ * lrb, (size_t)w.row_bytes, (size_t)lrb, (size_t)w.rows,
                                  cudaMemcpyHostToDevice));
             w.cols /= G;
@@ -436,6 +451,7 @@ void Model::load_from_gguf(const Gguf& g)
     for (int l = 0; l < c_.layers; ++l) {
         LayerW& L = L_[l];
         auto T = [&](const char* n) { return g.find(layer_name(l, n)); };
+        cur_stage_ = l;
         L.attn_norm = vec(T("attn_norm.weight"), WHOLE);
         L.q = upload(T("attn_q.weight"), ROWS); L.k = upload(T("attn_k.weight"), ROWS); L.v = upload(T("attn_v.weight"), ROWS);
         L.qb = vec(T("attn_q.bias"), ROWS); L.kb = vec(T("attn_k.bias"), ROWS); L.vb = vec(T("attn_v.bias"), ROWS);
@@ -457,11 +473,17 @@ void Model::load_from_gguf(const Gguf& g)
             L.gate = upload(T("ffn_gate.weight"), ROWS); L.up = upload(T("ffn_up.weight"), ROWS);
             L.down = upload(T("ffn_down.weight"), COLS);
         }
+        end_stage(l, {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down, &L.router, &L.gate_exps, &L.up_exps,
+                      &L.down_exps, &L.sh_gate, &L.sh_up, &L.sh_down, &L.sh_gate_inp});
     }
+    cur_stage_ = -1;
     embd_ = upload(g.find("token_embd.weight"), WHOLE);
     out_norm_ = vec(g.find("output_norm.weight"), WHOLE);
     if (!out_norm_.present()) WL_THROW(WL_EUNSUPPORTED, "The model has no output_norm.weight.");
+    cur_stage_ = c_.layers;
     output_ = c_.tied ? (G > 1 ? upload(g.find("token_embd.weight"), HEAD) : embd_) : upload(g.find("output.weight"), HEAD);
+    end_stage(c_.layers, (c_.tied && G == 1) ? std::vector<Weight*>{} : std::vector<Weight*>{&output_});
+    finish_streaming();
 
     std::vector<float> rf;
     if (const GgufTensor* t = g.find("rope_freqs.weight")) {
@@ -591,27 +613,55 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
             *ncols = p.cols / G; *c0 = rank * *ncols;
         }
     };
+    // the stage of a planned tensor under streaming: matrices of layer l stream with stage l, the output head with
+    // the head stage; the embedding and every vector stay resident
+    auto stage_of = [&](const Plan& p) -> int {
+        if (!m->streamed_ || p.v) return -1;
+        if (p.tid >= 256) return (int)(p.tid >> 8) - 1;
+        return p.tid == 3 ? c.layers : -1;
+    };
     int64_t total = 0, tmp_bytes = 0;
+    std::vector<int64_t> raw_upper((size_t)c.layers + 1, 0), slot_upper((size_t)c.layers + 1, 0);
     for (const Plan& p : plan) {
         const int64_t rb = row_bytes_of(p.type, p.cols);
         if (rb <= 0 || p.cols % (p.type == 0 ? 1 : p.type == 8 ? 32 : 256) != 0) WL_THROW(WL_EUNSUPPORTED, "synthetic tensor shape does not fit its type");
         int64_t r0, nr, c0, nc;
         part(p, &r0, &nr, &c0, &nc);
-        total += (row_bytes_of(p.type, nc) * nr + 255) / 256 * 256;
+        const int64_t bytes = (row_bytes_of(p.type, nc) * nr + 255) / 256 * 256;
+        const int st = stage_of(p);
+        if (st >= 0) {
+            raw_upper[(size_t)st] += bytes;
+            slot_upper[(size_t)st] += (nr + 15) / 16 * 16 * row_bytes_of(p.type, nc) + 256;
+        } else {
+            total += bytes;
+        }
         if (G > 1 && p.split) tmp_bytes = std::max(tmp_bytes, rb * p.rows);
     }
     m->arena_ = dalloc<uint8_t>(total);
     m->arena_size_ = total;
+    if (m->streamed_) m->plan_streaming(raw_upper, slot_upper);
+    std::vector<Weight*> stage_ws;
     uint8_t* tmp = tmp_bytes ? dalloc<uint8_t>(tmp_bytes) : nullptr;
     try {
         for (const Plan& p : plan) {
             int64_t r0, nr, c0, nc;
             part(p, &r0, &nr, &c0, &nc);
+            const int st = stage_of(p);
+            if (st >= 0 && st != m->cur_stage_) {     // the previous stage is complete
+                if (m->cur_stage_ >= 0) m->end_stage(m->cur_stage_, stage_ws);
+                stage_ws.clear();
+                m->cur_stage_ = st;
+            }
+            if (st < 0) {
+                if (m->cur_stage_ >= 0) m->end_stage(m->cur_stage_, stage_ws);
+                stage_ws.clear();
+                m->cur_stage_ = -1;
+            }
             const int64_t full_rb = row_bytes_of(p.type, p.cols);
             Weight w;
             w.type = p.type; w.cols = (int)nc; w.experts = p.experts; w.rows = (int)(nr / p.experts);
             w.row_bytes = row_bytes_of(p.type, nc); w.bytes = w.row_bytes * nr;
-            w.d = m->arena_alloc(w.bytes);
+            w.d = m->weight_alloc(w.bytes);
             const bool is_vec = p.v != nullptr;
             if (G == 1 || p.split == 0) {
                 k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, is_vec ? 1.0f : 0.0f, w.d, m->stream_);
@@ -624,7 +674,10 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
             m->weight_bytes_ += w.bytes;
             if (is_vec) { p.v->d = (float*)w.d; p.v->n = (int)(nr * nc); }
             else *p.w = w;
+            if (st >= 0) stage_ws.push_back(p.w);
         }
+        if (m->cur_stage_ >= 0) m->end_stage(m->cur_stage_, stage_ws);
+        m->finish_streaming();
         WL_CUDA(cudaStreamSynchronize(m->stream_));
     } catch (...) {
         if (tmp) cudaFree(tmp);
@@ -665,6 +718,7 @@ Model::~Model()
     if (comm_) {
         try { close_fused_ar(); } catch (...) {}
     }
+    free_streaming();
     dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
@@ -809,6 +863,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
         return;
     }
     prep_x_ = nullptr;
+    if (w.streamed_tiles) WL_THROW(WL_EUNSUPPORTED, "a streamed weight holds tiles only and has no CUDA-core path");
     const int mark = profile_begin();
     k::matvec(w.type, w.d, w.row_bytes, w.rows, w.cols, x, w.cols, T, y, ldy, stream_);
     profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows));
@@ -1091,8 +1146,14 @@ void Model::upload_step(int T, const RowKV* rows, const int32_t* pos, const int3
 void Model::step_device(int T, int first, int max_n)
 {
     begin_step(T);
-    for (int l = 0; l < c_.layers; ++l) layer(l, T, max_n);
+    for (int l = 0; l < c_.layers; ++l) {
+        stage_acquire(l);
+        layer(l, T, max_n);
+        stage_release(l);
+    }
+    stage_acquire(c_.layers);
     head(T, first);
+    stage_release(c_.layers);
 }
 
 int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
@@ -1115,11 +1176,15 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
         begin_step(T);
         for (int l = 0; l < c_.layers; ++l) {
             if (l == 0 ? stop0 : stop_requested(cancel)) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+            stage_acquire(l);
             layer(l, T, max_n);
+            stage_release(l);
             if (progress) { WL_CUDA(cudaStreamSynchronize(stream_)); progress(l + 1, total, user); }
         }
         if (stop_requested(cancel)) { WL_CUDA(cudaStreamSynchronize(stream_)); return WL_CANCELLED; }
+        stage_acquire(c_.layers);
         head(T, first);
+        stage_release(c_.layers);
     }
     WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));
     WL_CUDA(cudaStreamSynchronize(stream_));
@@ -1137,7 +1202,10 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
 // whole context, so one graph serves every step of that shape until the workspaces are reallocated. MoE layers
 // (host-side expert grouping), profiling and per-layer progress callbacks run eagerly.
 // ---------------------------------------------------------------------------------------------------------------------
-bool Model::graphable(int T) const { return use_graphs_ && !profiling_ && c_.expert_count == 0 && T <= 8; }
+bool Model::graphable(int T) const
+{
+    return use_graphs_ && !profiling_ && !streamed_ && c_.expert_count == 0 && T <= 8;
+}
 
 // True when a graph for (T, first) exists or could be captured now (after one eager run of that shape).
 bool Model::graph_ready(int T, int first)

@@ -23,6 +23,7 @@ struct Weight {
     uint8_t* d = nullptr;
     int row_base = 0;            // first row of this view inside the tiles (an expert slice)
     uint8_t* tiles = nullptr;    // Q4_K / Q6_K repacked into 16-row tiles for the tensor-core matvec (all experts)
+    bool streamed_tiles = false; // streamed in tile layout only: d holds tiles, not GGUF rows
     bool present() const { return d != nullptr; }
     const uint8_t* expert(int e) const { return d + (int64_t)e * rows * row_bytes; }
 };
@@ -141,6 +142,16 @@ private:
     void begin_step(int T);
     bool stop_requested(volatile const int32_t* cancel);
     void finish_open();
+    // layer streaming (wl_stream.cpp)
+    int stage_of_name(const std::string& name) const;
+    void plan_streaming(const std::vector<int64_t>& raw_upper, const std::vector<int64_t>& slot_upper);
+    uint8_t* weight_alloc(int64_t bytes);
+    void end_stage(int l, const std::vector<Weight*>& ws);
+    void finish_streaming();
+    void issue_copy(int l);
+    void stage_acquire(int l);
+    void stage_release(int l);
+    void free_streaming();
     void load_from_gguf(const Gguf& g);
     void build_rope_table(const float* rope_freqs, int n_rope_freqs);
     void reserve(Seq* s, int positions);
@@ -181,6 +192,29 @@ private:
     Seq* own_ = nullptr;
     Stats stats_;
     int64_t weight_bytes_ = 0;
+
+    // layer streaming (wl_options.resident = 0): per stage (each layer, then the head) its weights in pinned host
+    // memory, laid out as the kernels read them; two device slots, stage l in slot l % 2
+    struct StageWeight {
+        Weight* w;
+        int64_t off;
+        bool tiled;
+    };
+    struct Stage {
+        std::vector<StageWeight> ws;
+        uint8_t* host = nullptr;
+        int64_t bytes = 0;
+    };
+    bool streamed_ = false;
+    std::vector<Stage> stages_;
+    int cur_stage_ = -1;                  // the stage being loaded (-1: resident weights)
+    uint8_t* staging_ = nullptr;
+    int64_t staging_size_ = 0, staging_used_ = 0;
+    uint8_t* slot_[2] = {nullptr, nullptr};
+    int64_t slot_bytes_ = 0;
+    int slot_stage_[2] = {-1, -1};        // the stage each slot holds (or is being copied)
+    cudaStream_t copy_stream_ = nullptr;
+    cudaEvent_t copied_[2] = {nullptr, nullptr}, freed_[2] = {nullptr, nullptr};
 
     // device arena holding every weight
     uint8_t* arena_ = nullptr;
