@@ -646,23 +646,20 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
         for (const Plan& p : plan) {
             int64_t r0, nr, c0, nc;
             part(p, &r0, &nr, &c0, &nc);
+            const bool is_vec = p.v != nullptr;
             const int st = stage_of(p);
-            if (st >= 0 && st != m->cur_stage_) {     // the previous stage is complete
+            // a matrix of another stage (or a resident one) completes the stage being loaded; vectors are always
+            // resident and leave it open
+            if (!is_vec && st != m->cur_stage_) {
                 if (m->cur_stage_ >= 0) m->end_stage(m->cur_stage_, stage_ws);
                 stage_ws.clear();
                 m->cur_stage_ = st;
-            }
-            if (st < 0) {
-                if (m->cur_stage_ >= 0) m->end_stage(m->cur_stage_, stage_ws);
-                stage_ws.clear();
-                m->cur_stage_ = -1;
             }
             const int64_t full_rb = row_bytes_of(p.type, p.cols);
             Weight w;
             w.type = p.type; w.cols = (int)nc; w.experts = p.experts; w.rows = (int)(nr / p.experts);
             w.row_bytes = row_bytes_of(p.type, nc); w.bytes = w.row_bytes * nr;
-            w.d = m->weight_alloc(w.bytes);
-            const bool is_vec = p.v != nullptr;
+            w.d = is_vec ? m->arena_alloc(w.bytes) : m->weight_alloc(w.bytes);
             if (G == 1 || p.split == 0) {
                 k::synth(p.type, sp.seed, p.tid, p.rows, p.cols, sigma, is_vec ? 1.0f : 0.0f, w.d, m->stream_);
             } else {

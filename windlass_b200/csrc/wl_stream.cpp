@@ -60,6 +60,7 @@ void Model::end_stage(int l, const std::vector<Weight*>& ws)
 {
     if (!streamed_) return;
     Stage& st = stages_.at((size_t)l);
+    if (st.host || !st.ws.empty()) WL_THROW(WL_EINVAL, "streaming: stage " + std::to_string(l) + " was laid out twice");
     int64_t off = 0;
     for (Weight* w : ws) {
         if (!w->present()) continue;
