@@ -70,7 +70,9 @@ typedef struct wl_options {
                                 copied into one of two device slots on a copy stream while the previous layer
                                 computes; the embedding, norms and biases stay resident. Decode steps then run
                                 without CUDA graphs, and prefill_path 1 is refused */
-    int32_t prefill_path;    /* T > 8 prompts: 0 auto (tensor cores where the format has them), 1 fp32 CUDA cores */
+    int32_t prefill_path;    /* T > 8 rows: 0 auto (Q4_K on the tcgen05 GEMM, other formats with a tensor-core
+                                matvec in 8-column chunks), 1 fp32 CUDA cores, 2 the integer tensor-core matvec in
+                                8-column chunks for every format that has one */
     int32_t use_graphs;      /* 1: replay decode steps from captured CUDA graphs */
     int32_t tp_size;         /* tensor parallelism: ranks that share the model, one GPU each (0 or 1 = one GPU).
                                 Every rank opens the same model with its own tp_rank and the same tp_id, and then
@@ -210,8 +212,9 @@ int32_t wl_tiles_size(int32_t type, int32_t rows, int32_t cols, int64_t* bytes);
 int32_t wl_make_tiles(int32_t type, const void* dev_w, int32_t rows, int32_t cols, void* dev_tiles, void* stream);
 int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
                         int32_t ncols, float* dev_y, void* stream);
-/* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 1 = fp32 CUDA cores, 0 or 2 = the
- * model's default (the integer tensor-core matvec in 8-column chunks where the format has one). */
+/* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 0 = the model's default (T > 8 rows of Q4_K
+ * on the tcgen05 GEMM, else the integer tensor-core matvec in 8-column chunks where the format has one), 1 = fp32
+ * CUDA cores, 2 = the integer tensor-core matvec in 8-column chunks. */
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                   float* dev_y, int32_t path, void* stream);
 /* Synthetic weight generator of wl_open_synthetic for one tensor (rows x cols of `type`: F32, F16, Q8_0, Q4_K or

@@ -65,9 +65,20 @@ void* export_scratch(size_t bytes)
 // 8 columns per launch, activations prepared once per chunk), else the CUDA-core kernel. force_cuda_cores selects
 // the latter.
 void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, int ncols, float* y, bool force_cuda_cores,
-                cudaStream_t s)
+                cudaStream_t s, bool allow_gemm = true)
 {
     const int64_t rb = wl::row_bytes_of(type, cols);
+    if (!force_cuda_cores && allow_gemm && ncols > 8 && wl::k::gemm_supported(type, cols)) {
+        // scratch: [error word | the activations' bf16 planes | the weights repacked into tiles]
+        const size_t xb = (wl::k::gemm_scratch_bytes(ncols, cols) + 255) / 256 * 256;
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::tile_bytes(type, rows, cols));
+        int* err = (int*)scratch;
+        uint8_t* tiles = scratch + 256 + xb;
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
+        wl::k::gemm_tiles(type, tiles, 0, rows, cols, x, cols, ncols, y, rows, scratch + 256, err, s);
+        return;
+    }
     if (!force_cuda_cores && wl::k::tiles_supported(type, cols) && (uintptr_t)x % 16 == 0) {
         // scratch: [error word | prepared activations | the weights repacked into tiles]
         const size_t xb = (wl::k::xprep_bytes(cols, 8) + 255) / 256 * 256;
@@ -422,7 +433,7 @@ int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
         if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matmul: null pointer");
         if (path < 0 || path > 2) return wl::fail(WL_EINVAL, "wl_matmul: path must be 0, 1 or 2");
         wl::k::init_tables();
-        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, T, dev_y, path == 1, (cudaStream_t)stream);
+        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, T, dev_y, path == 1, (cudaStream_t)stream, path != 2);
         return WL_OK;
     });
 }

@@ -1,0 +1,379 @@
+// Prefill / batched GEMM for Q4_K weights on the 5th-generation tensor cores (tcgen05, sm_100a):
+// y[t*ldy + r] = W[r] . x[t] for T > 8 activation rows (FastMath.Block's job in the reference, src/FastMath.cs:218-264).
+//
+// One CTA computes a 128-row x 64-token tile of y; its fp32 accumulator lives in tensor memory (64 TMEM columns).
+// Per K step of 64 values, in a 4-stage shared-memory ring:
+//   - 8 dequantizing warps read the rows' Q4_K codes and scales from the tile-major weights (two threads per row, one
+//     32-value sub-block each), rebuild every weight exactly as the reference does (d1 = d*s, m1 = dmin*m,
+//     w = d1*q - m1, each rounded in fp32) and store it as two bf16 planes, w_hi = bf16(w) and w_lo = bf16(w - w_hi),
+//     in the 128-byte-swizzled K-major layout the MMA reads;
+//   - one warp loads the tokens' bf16 planes x_hi, x_lo (written by k_split_bf16) with 2-D TMA copies (no multicast);
+//   - one thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> fp32) per 16-value slice:
+//     w_hi.x_hi + w_hi.x_lo + w_lo.x_hi. The dropped w_lo.x_lo term is below 2^-16 of each product, so the result
+//     carries fp32-level accuracy (a plain bf16 GEMM would carry 2^-9 relative error per weight);
+//   - tcgen05.commit frees each stage when its MMAs have read it; a final commit releases the epilogue.
+// The four epilogue warps (warp w owns TMEM lanes 32w..32w+31 = tile rows) read the accumulator with tcgen05.ld and
+// store y rows, coalesced along the weight rows. Every wait is bounded: a stuck wait records a code in *err (host:
+// WL_ETIMEDOUT) and the kernel runs on to its TMEM release and returns.
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+#include "wl_common.h"
+#include "wl_kernels.h"
+#include "wl_launch.cuh"
+
+namespace wl {
+namespace k {
+
+namespace {
+
+constexpr int G_BM = 128;                  // weight rows per CTA (MMA M)
+constexpr int G_BN = 64;                   // tokens per CTA (MMA N)
+constexpr int G_BK = 64;                   // values per K step: one 128-byte swizzle atom of bf16
+constexpr int G_STAGES = 4;
+constexpr int G_A_BYTES = G_BM * G_BK * 2;             // one bf16 plane of the weight tile: 16 KB
+constexpr int G_B_BYTES = G_BN * G_BK * 2;             // one bf16 plane of the token tile: 8 KB
+constexpr int G_STAGE = 2 * G_A_BYTES + 2 * G_B_BYTES; // 48 KB
+constexpr int G_DQ_WARPS = 8, G_TMA_WARP = 8, G_MMA_WARP = 9, G_THREADS = 320;
+constexpr int G_SMEM = G_STAGES * G_STAGE + 1024;      // + alignment slack (swizzle atoms need 1024-byte alignment)
+constexpr int G_TMEM_COLS = 64;
+constexpr int Q4T = 2304;                               // bytes of a 16-row x one-superblock Q4_K tile
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
+    return ok != 0;
+}
+// Bounded: gives up after 4096 polls (each may sleep up to 1 ms), records `code` in *err and raises the CTA's abort
+// flag, after which every later wait of the CTA returns at once, so a broken pipeline ends in seconds, not minutes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort)
+{
+    if (*abort) return false;
+    for (uint32_t i = 0; i < 4096u; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    atomicExch(err, code);
+    *abort = 1;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+
+// Shared-memory matrix descriptor (sm100): K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc(const void* p)
+{
+    const uint64_t addr = smem_u32(p);
+    return ((addr & 0x3FFFFull) >> 4)        // start address, 16-byte units
+           | (1ull << 16)                    // leading byte offset (unused for swizzled K-major; canonical 1)
+           | ((1024ull >> 4) << 32)          // stride byte offset: next 8-row group
+           | (1ull << 46)                    // descriptor version (sm100)
+           | (2ull << 61);                   // layout: 128-byte swizzle
+}
+
+// Instruction descriptor: kind::f16, A and B bf16, D fp32, both K-major, M = 128, N = 64.
+constexpr uint32_t G_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(G_BN >> 3) << 17) | ((uint32_t)(G_BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate)
+{
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                 ::"r"(tmem_d), "l"(a), "l"(b), "r"(G_IDESC), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+
+// The 64 fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64])
+{
+    uint32_t r[64];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+                 "%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,"
+                 "%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+                   "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+                   "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+                   "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+                   "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two weights to their bf16 hi and lo planes, packed as element pairs (lower address first).
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo)
+{
+    const __nv_bfloat16 ah = __float2bfloat16_rn(a), bh = __float2bfloat16_rn(b);
+    const __nv_bfloat16 al = __float2bfloat16_rn(__fsub_rn(a, __bfloat162float(ah)));
+    const __nv_bfloat16 bl = __float2bfloat16_rn(__fsub_rn(b, __bfloat162float(bh)));
+    hi = (uint32_t)__bfloat16_as_ushort(ah) | ((uint32_t)__bfloat16_as_ushort(bh) << 16);
+    lo = (uint32_t)__bfloat16_as_ushort(al) | ((uint32_t)__bfloat16_as_ushort(bl) << 16);
+}
+
+__global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap xh_map,
+                                                            const __grid_constant__ CUtensorMap xl_map,
+                                                            const uint8_t* __restrict__ tiles, int row_base, int rows,
+                                                            int nsb, int T, float* __restrict__ y, int64_t ldy, int* err)
+{
+    extern __shared__ uint8_t g_smem_raw[];
+    __shared__ __align__(8) uint64_t full_a[G_STAGES], full_b[G_STAGES], empty[G_STAGES], acc_full;
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+    uint8_t* smem = (uint8_t*)(((uintptr_t)g_smem_raw + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * G_BM, n0 = blockIdx.y * G_BN;
+    const int nk = nsb * 4;                 // K steps of 64 values
+
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < G_STAGES; ++s) {
+            mbar_init(&full_a[s], G_DQ_WARPS * 32);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {                        // the accumulator: 64 TMEM columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&tmem_base)), "r"(G_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp < G_DQ_WARPS) {
+        // ---- dequantizers: thread -> (row m, half h); per K step the row's 32-value sub-block 2p+h of superblock sb
+        const int t = threadIdx.x, m = t >> 1, h = t & 1, gr = m0 + m;
+        const bool live = gr < ((rows + 15) & ~15);          // tiles exist for whole 16-row groups only
+        const uint8_t* trow = tiles + ((int64_t)(row_base / 16 + gr / 16) * nsb) * Q4T;
+        const int r16 = gr & 15, hdr = r16 * 16, code = 256 + ((r16 & 7) * 4) * 16 + (r16 >> 3) * 8;
+        const int swz = m & 7;
+        uint8_t* arow = smem + (m >> 3) * 1024 + swz * 128;
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % G_STAGES;
+            if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 11, &abort_flag);
+            const int sb = i >> 2, p = i & 3;
+            uint32_t hi[16], lo[16];
+            if (live) {
+                const uint8_t* tb = trow + (int64_t)sb * Q4T;
+                const uint4 hv = __ldg(reinterpret_cast<const uint4*>(tb + hdr));
+                uint2 cv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) cv[c] = __ldg(reinterpret_cast<const uint2*>(tb + code + p * 512 + c * 16));
+                // ScaleMinK4 (src/Quants.cs:322-330) of sub-block j = 2p + h; scale byte b is byte b & 3 of word
+                // hv.y / hv.z / hv.w for b in 0-3 / 4-7 / 8-11
+                const int j = 2 * p + h, sh8 = 8 * (j & 3);
+                int s6, m6;
+                if (j < 4) {
+                    s6 = (int)((hv.y >> sh8) & 63u);
+                    m6 = (int)((hv.z >> sh8) & 63u);
+                } else {
+                    const uint32_t bj4 = (hv.w >> sh8) & 0xFFu, bjm4 = (hv.y >> sh8) & 0xFFu, bj = (hv.z >> sh8) & 0xFFu;
+                    s6 = (int)((bj4 & 0xFu) | ((bjm4 >> 6) << 4));
+                    m6 = (int)((bj4 >> 4) | ((bj >> 6) << 4));
+                }
+                const float d1 = __fmul_rn(h2f(hv.x & 0xFFFF), (float)s6), mm1 = __fmul_rn(h2f(hv.x >> 16), (float)m6);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                    for (int q2 = 0; q2 < 4; ++q2) {
+                        const uint32_t word = q2 < 2 ? cv[c].x : cv[c].y;
+                        const int sh = (q2 & 1) * 16 + (h ? 4 : 0);
+                        const float w0 = __fsub_rn(__fmul_rn(d1, (float)((word >> sh) & 15)), mm1);
+                        const float w1 = __fsub_rn(__fmul_rn(d1, (float)((word >> (sh + 8)) & 15)), mm1);
+                        split2(w0, w1, hi[c * 4 + q2], lo[c * 4 + q2]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) hi[q] = lo[q] = 0u;
+            }
+            // values 32h .. 32h+31 of the row: 16-byte chunks 4h .. 4h+3, swizzled by the row within its 8-row group
+            uint8_t* ah = arow + (size_t)s * G_STAGE;
+            uint8_t* al = ah + G_A_BYTES;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int chunk = (4 * h + c) ^ swz;
+                *reinterpret_cast<uint4*>(ah + chunk * 16) = make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+                *reinterpret_cast<uint4*>(al + chunk * 16) = make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+            }
+            fence_async_shared();           // generic-proxy writes before the tensor cores read them
+            mbar_arrive(&full_a[s]);
+        }
+    } else if (warp == G_TMA_WARP) {
+        // ---- the tokens' bf16 planes, one 64 x 64 box each per K step (rows past T read as zeros)
+        if (lane == 0) {
+            pdl_wait();                     // x_hi / x_lo are written by the preceding kernel
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % G_STAGES;
+                if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 12, &abort_flag);
+                uint8_t* st = smem + (size_t)s * G_STAGE + 2 * G_A_BYTES;
+                mbar_expect_tx(&full_b[s], 2 * G_B_BYTES);
+                tma_load_2d(st, &xh_map, i * G_BK, n0, &full_b[s]);
+                tma_load_2d(st + G_B_BYTES, &xl_map, i * G_BK, n0, &full_b[s]);
+            }
+        }
+    } else {
+        // ---- one thread issues the MMAs
+        if (lane == 0) {
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % G_STAGES;
+                const uint32_t par = (uint32_t)((i / G_STAGES) & 1);
+                mbar_wait(&full_a[s], par, err, 13, &abort_flag);
+                mbar_wait(&full_b[s], par, err, 14, &abort_flag);
+                tc_fence_after();
+                const uint8_t* st = smem + (size_t)s * G_STAGE;
+#pragma unroll
+                for (int kk = 0; kk < G_BK / 16; ++kk) {
+                    const uint64_t ah = sdesc(st + kk * 32), al = sdesc(st + G_A_BYTES + kk * 32);
+                    const uint64_t bh = sdesc(st + 2 * G_A_BYTES + kk * 32), bl = sdesc(st + 2 * G_A_BYTES + G_B_BYTES + kk * 32);
+                    umma_bf16(tmem, ah, bh, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16(tmem, ah, bl, 1u);
+                    umma_bf16(tmem, al, bh, 1u);
+                }
+                umma_commit(&empty[s]);     // the stage is free once these MMAs have read it
+            }
+            umma_commit(&acc_full);
+        }
+    }
+
+    // ---- epilogue: warps 0-3, warp w reads TMEM lanes 32w .. 32w+31 (tile rows), 64 token columns
+    if (warp < 4) {
+        mbar_wait(&acc_full, 0u, err, 15, &abort_flag);
+        tc_fence_after();
+        float v[64];
+        tmem_ld64(tmem + ((uint32_t)(32 * warp) << 16), v);
+        const int r = m0 + 32 * warp + lane;
+        if (r < rows) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+                if (n0 + j < T) y[(int64_t)(n0 + j) * ldy + r] = v[j];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G_TMEM_COLS) : "memory");
+    }
+}
+
+// x (T rows of K fp32, ldx apart) to its bf16 planes hi = bf16(x), lo = bf16(x - hi), each [T][K].
+__global__ void k_split_bf16(const float* __restrict__ x, int64_t ldx, int K, int64_t n, __nv_bfloat16* __restrict__ hi,
+                             __nv_bfloat16* __restrict__ lo)
+{
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / K, c = i - t * K;
+        const float v = x[t * ldx + c];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled()
+{
+    static std::mutex mu;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        WL_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (!p || q != cudaDriverEntryPointSuccess) WL_THROW(WL_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+        fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+// A [T][K] bf16 plane as 64 x 64 boxes with the 128-byte swizzle the MMA descriptors expect.
+CUtensorMap plane_map(const void* base, int T, int K)
+{
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {G_BK, G_BN};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) WL_THROW(WL_ECUDA, "cuTensorMapEncodeTiled (activation planes) failed (" + std::to_string((int)r) + ")");
+    return map;
+}
+
+}  // namespace
+
+bool gemm_supported(int type, int cols) { return type == 12 && cols % 256 == 0; }
+
+size_t gemm_scratch_bytes(int T, int cols) { return (size_t)2 * T * cols * 2 + 256; }
+
+void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const float* x, int64_t ldx, int T,
+                float* y, int64_t ldy, void* scratch, int* err, cudaStream_t s)
+{
+    if (!gemm_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "gemm_tiles: Q4_K with cols a multiple of 256 only");
+    if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "gemm_tiles: misaligned tiles");
+    if (T <= 0 || rows <= 0) return;
+    __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
+    __nv_bfloat16* lo = hi + (size_t)T * cols;
+    const int64_t n = (int64_t)T * cols;
+    int64_t gr = (n + 255) / 256;
+    if (gr > 148 * 8) gr = 148 * 8;
+    launch(k_split_bf16, dim3((unsigned)gr), dim3(256), 0, s, x, ldx, cols, n, hi, lo);
+    note_launch();
+    const CUtensorMap mh = plane_map(hi, T, cols), ml = plane_map(lo, T, cols);
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        WL_CUDA(cudaFuncSetAttribute(k_gemm_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM));
+        attr[dev] = true;
+    }
+    const dim3 grid((rows + G_BM - 1) / G_BM, (T + G_BN - 1) / G_BN);
+    launch(k_gemm_q4k, grid, dim3(G_THREADS), G_SMEM, s, mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    note_launch();
+}
+
+}  // namespace k
+}  // namespace wl

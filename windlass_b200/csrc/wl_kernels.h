@@ -110,6 +110,15 @@ void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_byte
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
                   int64_t ldy, int* err, cudaStream_t s);
 
+// Q4_K GEMM on the tcgen05 tensor cores for T > 8 activation rows (prefill, large batches): y[t*ldy + r] =
+// W[row_base + r] . x[t*ldx ...] from the tile-major weights, with fp32-level accuracy (bf16 hi/lo planes of both
+// operands, three MMAs per slice, fp32 accumulation in tensor memory). scratch holds gemm_scratch_bytes(T, cols) bytes
+// (the activations' bf16 planes); a stuck wait sets *err.
+bool gemm_supported(int type, int cols);
+size_t gemm_scratch_bytes(int T, int cols);
+void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const float* x, int64_t ldx, int T,
+                float* y, int64_t ldy, void* scratch, int* err, cudaStream_t s);
+
 // RmsNormRows (Transformer.cs:454-464): n rows of dim values; y may alias x.
 void rmsnorm(const float* x, int n, int dim, const float* w, float eps, float* y, cudaStream_t s);
 // y[t*n + i] += b[i] for T rows (AddBias, Transformer.cs:442-451).

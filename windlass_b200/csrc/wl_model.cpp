@@ -710,6 +710,7 @@ Model::~Model()
     hfree(h_tok_); hfree(h_pos_); hfree(h_rows_); hfree(h_sel_); hfree(h_wts_); hfree(h_etok_); hfree(h_ew_);
     for (void* p : extra_allocs_) cudaFree(p);
     if (xprep_buf_) cudaFree(xprep_buf_);
+    if (gemm_buf_) cudaFree(gemm_buf_);
     dfree(att_part_);
     dfree(err_d_);
     if (comm_) {
@@ -840,6 +841,23 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
     if (ldy <= 0) ldy = w.rows;
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
     const bool cuda_cores = path == 1 || (T > 8 && prefill_path_ == 1);
+    // more than 8 rows of Q4_K: the tcgen05 GEMM (prefill_path 2 keeps the integer matvec in 8-column chunks)
+    if (!cuda_cores && T > 8 && prefill_path_ != 2 && w.tiles && w.row_base % 16 == 0 && k::gemm_supported(w.type, w.cols)) {
+        const size_t need = k::gemm_scratch_bytes(T, w.cols);
+        if (need > gemm_buf_bytes_) {
+            WL_CUDA(cudaStreamSynchronize(stream_));
+            if (gemm_buf_) cudaFree(gemm_buf_);
+            gemm_buf_ = nullptr;
+            gemm_buf_bytes_ = 0;
+            WL_CUDA(cudaMalloc(&gemm_buf_, need));
+            gemm_buf_bytes_ = need;
+        }
+        prep_x_ = nullptr;
+        const int mark = profile_begin();
+        k::gemm_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, x, w.cols, T, y, ldy, gemm_buf_, err_d_, stream_);
+        profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows));
+        return;
+    }
     if (!cuda_cores && w.tiles && w.row_base % 16 == 0 && xprep_buf_) {
         for (int c0 = 0; c0 < T; c0 += 8) {
             const int nc = std::min(8, T - c0);

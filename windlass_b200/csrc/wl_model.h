@@ -239,6 +239,8 @@ private:
     float* h_ew_ = nullptr;
     int h_cap_ = 0;
     // activations prepared for the tensor-core matvec (k::xprep), and what they were prepared from
+    void* gemm_buf_ = nullptr;          // the tcgen05 GEMM's activation planes
+    size_t gemm_buf_bytes_ = 0;
     void* xprep_buf_ = nullptr;
     float* att_part_ = nullptr;         // split-range attention partials
     int* err_d_ = nullptr;              // device error word of the bounded waits
