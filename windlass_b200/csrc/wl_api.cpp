@@ -74,8 +74,10 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
         uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::tile_bytes(type, rows, cols));
         int* err = (int*)scratch;
         uint8_t* tiles = scratch + 256 + xb;
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        // the tiles are written by a kernel here, and the GEMM reads weights before its grid-dependency wait: the
+        // memset between them (not a kernel) makes the GEMM start only once the repack has completed
         wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
         wl::k::gemm_tiles(type, tiles, 0, rows, cols, x, cols, ncols, y, rows, scratch + 256, err, s);
         return;
     }
@@ -85,8 +87,9 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
         uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::tile_bytes(type, rows, cols));
         int* err = (int*)scratch;
         uint8_t* tiles = scratch + 256 + xb;
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        // as above: the memset after the repack keeps the matvecs' early weight reads behind it
         wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
+        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
         for (int c0 = 0; c0 < ncols; c0 += 8) {
             const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
             const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
