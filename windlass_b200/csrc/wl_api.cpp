@@ -337,7 +337,8 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
         if (rows <= 0 || cols <= 0 || ncols <= 0 || cols % b != 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
         if (!dev_w || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_matvec: null pointer");
         wl::k::init_tables();
-        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, ncols, dev_y, false, (cudaStream_t)stream);
+        // every column computed as if alone (MatMulEach): the matvec, never the GEMM
+        run_matvec(type, (const uint8_t*)dev_w, rows, cols, dev_x, ncols, dev_y, false, (cudaStream_t)stream, false);
         return WL_OK;
     });
 }

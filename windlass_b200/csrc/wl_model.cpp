@@ -842,7 +842,8 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
     const bool cuda_cores = path == 1 || (T > 8 && prefill_path_ == 1);
     // more than 8 rows of Q4_K: the tcgen05 GEMM (prefill_path 2 keeps the integer matvec in 8-column chunks)
-    if (!cuda_cores && T > 8 && prefill_path_ != 2 && w.tiles && w.row_base % 16 == 0 && k::gemm_supported(w.type, w.cols)) {
+    if (!cuda_cores && T > 8 && prefill_path_ != 2 && !each_token_ && w.tiles && w.row_base % 16 == 0 &&
+        k::gemm_supported(w.type, w.cols)) {
         const size_t need = k::gemm_scratch_bytes(T, w.cols);
         if (need > gemm_buf_bytes_) {
             WL_CUDA(cudaStreamSynchronize(stream_));
@@ -1295,7 +1296,13 @@ double Model::bench_decode(Seq* const* seqs, int N, int steps)
     int32_t* pos_all_d = dalloc<int32_t>((int64_t)steps * N);
     WL_CUDA(cudaMemcpy(pos_all_d, pos_all.data(), pos_all.size() * 4, cudaMemcpyHostToDevice));
     upload_step(N, rows.data(), pos_all.data(), toks.data());
-    // a graph is captured (or found) before the timed loop so capture costs are not timed
+    // ForwardBatch steps (every row as if alone); a graph is captured (or found) before the timed loop so capture
+    // costs are not timed
+    struct EachToken {
+        bool& f;
+        explicit EachToken(bool& b) : f(b) { f = true; }
+        ~EachToken() { f = false; }
+    } each(each_token_);
     const bool graphs = graph_ready(N, 0);
     cudaEvent_t e0, e1;
     WL_CUDA(cudaEventCreate(&e0));
@@ -1399,7 +1406,16 @@ int32_t Model::forward_batch(Seq* const* seqs, const int32_t* tokens, int N, flo
         rows[i] = RowKV{seqs[i]->kv, seqs[i]->kv + (int64_t)c_.layers * stride, stride};
     }
     stats_.batch_calls++;
-    const int32_t st = run(N, rows, pos, tokens, 0, out, cancel, progress, user);
+    // MatMulEach (src/Transformer.cs:544-561): each row bit-identical to running alone, so no GEMM for this step
+    each_token_ = true;
+    int32_t st;
+    try {
+        st = run(N, rows, pos, tokens, 0, out, cancel, progress, user);
+    } catch (...) {
+        each_token_ = false;
+        throw;
+    }
+    each_token_ = false;
     if (st == WL_OK) for (int i = 0; i < N; ++i) seqs[i]->length = pos[i] + 1;
     return st;
 }

@@ -184,6 +184,7 @@ private:
     int max_context_ = 0;
     int max_batch_ = 64;
     int prefill_path_ = 0;
+    bool each_token_ = false;             // a ForwardBatch step: every row computed as if alone (no GEMM)
     cudaStream_t stream_ = nullptr;
     std::vector<LayerW> L_;
     Weight embd_, output_;
