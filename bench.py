@@ -200,6 +200,9 @@ def sweep(args):
                 elif b <= 8:
                     st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
                                      C.c_void_p(y.data_ptr()), cs)
+                elif tiled and f == "q4_K":   # the tcgen05 GEMM on the repacked weights
+                    st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), n, n, C.c_void_p(x.data_ptr()),
+                                         b, C.c_void_p(y.data_ptr()), cs)
                 else:
                     st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
                                      C.c_void_p(y.data_ptr()), 0, cs)

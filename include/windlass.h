@@ -212,6 +212,11 @@ int32_t wl_tiles_size(int32_t type, int32_t rows, int32_t cols, int64_t* bytes);
 int32_t wl_make_tiles(int32_t type, const void* dev_w, int32_t rows, int32_t cols, void* dev_tiles, void* stream);
 int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
                         int32_t ncols, float* dev_y, void* stream);
+/* No counterpart in the reference: the tcgen05 GEMM (Q4_K only) on tile-major weights made by wl_make_tiles, for
+ * T > 8 rows: dev_y[t*rows + r] = W[r] . dev_x[t]. The activations' bf16 hi/lo planes go to a scratch the library
+ * keeps per device (grown on demand). Other formats return WL_EUNSUPPORTED. */
+int32_t wl_gemm_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
+                      float* dev_y, void* stream);
 /* Transformer.MatMul for T input rows (src/Transformer.cs:483-537): path 0 = the model's default (T > 8 rows of Q4_K
  * on the tcgen05 GEMM, else the integer tensor-core matvec in 8-column chunks where the format has one), 1 = fp32
  * CUDA cores, 2 = the integer tensor-core matvec in 8-column chunks. */

@@ -427,6 +427,23 @@ int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32
     });
 }
 
+int32_t wl_gemm_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
+                      float* dev_y, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (!wl::k::gemm_supported(type, cols)) return wl::fail(WL_EUNSUPPORTED, "wl_gemm_tiles: Q4_K with cols a multiple of 256 only");
+        if (rows <= 0 || T <= 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
+        if (!dev_tiles || !dev_x || !dev_y) return wl::fail(WL_EINVAL, "wl_gemm_tiles: null pointer");
+        if ((uintptr_t)dev_tiles % 16 != 0) return wl::fail(WL_EINVAL, "wl_gemm_tiles: dev_tiles must be 16-byte aligned");
+        const cudaStream_t s = (cudaStream_t)stream;
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::gemm_scratch_bytes(T, cols));
+        WL_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), s));
+        wl::k::gemm_tiles(type, (const uint8_t*)dev_tiles, 0, rows, cols, dev_x, cols, T, dev_y, rows, scratch + 256,
+                          (int*)scratch, s);
+        return WL_OK;
+    });
+}
+
 int32_t wl_matmul(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                   float* dev_y, int32_t path, void* stream)
 {
