@@ -1,12 +1,14 @@
 // Prefill / batched GEMM for Q4_K weights on the 5th-generation tensor cores (tcgen05, sm_100a):
 // y[t*ldy + r] = W[r] . x[t] for T > 8 activation rows (FastMath.Block's job in the reference, src/FastMath.cs:218-264).
 //
-// One CTA computes a 128-row x 64-token tile of y; its fp32 accumulator lives in tensor memory (64 TMEM columns).
-// Per K step of 64 values, in a 4-stage shared-memory ring:
-//   - 8 dequantizing warps read the rows' Q4_K codes and scales from the tile-major weights (two threads per row, one
-//     32-value sub-block each), rebuild every weight exactly as the reference does (d1 = d*s, m1 = dmin*m,
-//     w = d1*q - m1, each rounded in fp32) and store it as two bf16 planes, w_hi = bf16(w) and w_lo = bf16(w - w_hi),
-//     in the 128-byte-swizzled K-major layout the MMA reads;
+// One CTA computes a 128-row x 128-token tile of y; its fp32 accumulator lives in tensor memory (128 TMEM columns).
+// Per K step of 64 values, in a 3-stage shared-memory ring (64 KB a stage) fed by a 4-stage ring of raw weights:
+//   - one warp copies the step's raw Q4_K bytes of the CTA's eight 16-row tiles (each tile's 256 header bytes and the
+//     512 code bytes of the step's 64 values) into the raw ring with 1-D bulk copies, ahead of their use;
+//   - 8 dequantizing warps read those bytes from shared memory (two threads per row, one 32-value sub-block each),
+//     rebuild every weight exactly as the reference does (d1 = d*s, m1 = dmin*m, w = d1*q - m1, each rounded in fp32)
+//     and store it as two bf16 planes, w_hi = bf16(w) and w_lo = bf16(w - w_hi), in the 128-byte-swizzled K-major
+//     layout the MMA reads;
 //   - one warp loads the tokens' bf16 planes x_hi, x_lo (written by k_split_bf16) with 2-D TMA copies (no multicast);
 //   - one thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> fp32) per 16-value slice:
 //     w_hi.x_hi + w_hi.x_lo + w_lo.x_hi. The dropped w_lo.x_lo term is below 2^-16 of each product, so the result
@@ -31,15 +33,18 @@ namespace k {
 namespace {
 
 constexpr int G_BM = 128;                  // weight rows per CTA (MMA M)
-constexpr int G_BN = 64;                   // tokens per CTA (MMA N)
+constexpr int G_BN = 128;                  // tokens per CTA (MMA N)
 constexpr int G_BK = 64;                   // values per K step: one 128-byte swizzle atom of bf16
-constexpr int G_STAGES = 4;
+constexpr int G_STAGES = 3;
+constexpr int G_RAW_STAGES = 4;
 constexpr int G_A_BYTES = G_BM * G_BK * 2;             // one bf16 plane of the weight tile: 16 KB
-constexpr int G_B_BYTES = G_BN * G_BK * 2;             // one bf16 plane of the token tile: 8 KB
-constexpr int G_STAGE = 2 * G_A_BYTES + 2 * G_B_BYTES; // 48 KB
-constexpr int G_DQ_WARPS = 8, G_TMA_WARP = 8, G_MMA_WARP = 9, G_THREADS = 320;
-constexpr int G_SMEM = G_STAGES * G_STAGE + 1024;      // + alignment slack (swizzle atoms need 1024-byte alignment)
-constexpr int G_TMEM_COLS = 64;
+constexpr int G_B_BYTES = G_BN * G_BK * 2;             // one bf16 plane of the token tile: 16 KB
+constexpr int G_STAGE = 2 * G_A_BYTES + 2 * G_B_BYTES; // 64 KB
+constexpr int G_RAW_TILE = 256 + 512;                   // a 16-row tile's headers and one K step's code bytes
+constexpr int G_RAW_STAGE = (G_BM / 16) * G_RAW_TILE;   // 6 KB
+constexpr int G_DQ_WARPS = 8, G_TMA_WARP = 8, G_RAW_WARP = 9, G_MMA_WARP = 10, G_THREADS = 352;
+constexpr int G_SMEM = G_STAGES * G_STAGE + G_RAW_STAGES * G_RAW_STAGE + 1024;   // + alignment slack (1024 B atoms)
+constexpr int G_TMEM_COLS = 128;
 constexpr int Q4T = 2304;                               // bytes of a 16-row x one-superblock Q4_K tile
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -77,6 +82,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -94,7 +105,7 @@ __device__ __forceinline__ uint64_t sdesc(const void* p)
            | (2ull << 61);                   // layout: 128-byte swizzle
 }
 
-// Instruction descriptor: kind::f16, A and B bf16, D fp32, both K-major, M = 128, N = 64.
+// Instruction descriptor: kind::f16, A and B bf16, D fp32, both K-major, M = 128, N = 128.
 constexpr uint32_t G_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(G_BN >> 3) << 17) | ((uint32_t)(G_BM >> 4) << 24);
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate)
@@ -153,12 +164,16 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
 {
     extern __shared__ uint8_t g_smem_raw[];
     __shared__ __align__(8) uint64_t full_a[G_STAGES], full_b[G_STAGES], empty[G_STAGES], acc_full;
+    __shared__ __align__(8) uint64_t raw_full[G_RAW_STAGES], raw_empty[G_RAW_STAGES];
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     uint8_t* smem = (uint8_t*)(((uintptr_t)g_smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* raw = smem + G_STAGES * G_STAGE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * G_BM, n0 = blockIdx.y * G_BN;
     const int nk = nsb * 4;                 // K steps of 64 values
+    // 16-row weight tiles of this CTA that exist (the last CTA of a matrix may have fewer than eight)
+    const int live_tiles = min(G_BM / 16, (rows + 15) / 16 - m0 / 16);
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -167,11 +182,15 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
         }
+        for (int s = 0; s < G_RAW_STAGES; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], G_DQ_WARPS * 32);
+        }
         mbar_init(&acc_full, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {                        // the accumulator: 64 TMEM columns x 128 lanes
+    if (warp == 0) {                        // the accumulator: 128 TMEM columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&tmem_base)), "r"(G_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -183,23 +202,28 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
 
     if (warp < G_DQ_WARPS) {
         // ---- dequantizers: thread -> (row m, half h); per K step the row's 32-value sub-block 2p+h of superblock sb
-        const int t = threadIdx.x, m = t >> 1, h = t & 1, gr = m0 + m;
-        const bool live = gr < ((rows + 15) & ~15);          // tiles exist for whole 16-row groups only
-        const uint8_t* trow = tiles + ((int64_t)(row_base / 16 + gr / 16) * nsb) * Q4T;
-        const int r16 = gr & 15, hdr = r16 * 16, code = 256 + ((r16 & 7) * 4) * 16 + (r16 >> 3) * 8;
+        const int t = threadIdx.x, m = t >> 1, h = t & 1;
+        const bool live = (m >> 4) < live_tiles;
+        const int r16 = m & 15, hdr = (m >> 4) * G_RAW_TILE + r16 * 16;
+        const int code = (m >> 4) * G_RAW_TILE + 256 + ((r16 & 7) * 4) * 16 + (r16 >> 3) * 8;
         const int swz = m & 7;
         uint8_t* arow = smem + (m >> 3) * 1024 + swz * 128;
         for (int i = 0; i < nk; ++i) {
-            const int s = i % G_STAGES;
-            if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 11, &abort_flag);
-            const int sb = i >> 2, p = i & 3;
+            const int s = i % G_STAGES, rs = i % G_RAW_STAGES;
+            const int p = i & 3;
             uint32_t hi[16], lo[16];
+            mbar_wait(&raw_full[rs], (uint32_t)((i / G_RAW_STAGES) & 1), err, 16, &abort_flag);
+            uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+            uint2 cv[4] = {};
             if (live) {
-                const uint8_t* tb = trow + (int64_t)sb * Q4T;
-                const uint4 hv = __ldg(reinterpret_cast<const uint4*>(tb + hdr));
-                uint2 cv[4];
+                const uint8_t* rb = raw + rs * G_RAW_STAGE;
+                hv = *reinterpret_cast<const uint4*>(rb + hdr);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) cv[c] = __ldg(reinterpret_cast<const uint2*>(tb + code + p * 512 + c * 16));
+                for (int c = 0; c < 4; ++c) cv[c] = *reinterpret_cast<const uint2*>(rb + code + c * 16);
+            }
+            mbar_arrive(&raw_empty[rs]);    // the raw bytes are in registers: the slot may be refilled
+            if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 11, &abort_flag);
+            if (live) {
                 // ScaleMinK4 (src/Quants.cs:322-330) of sub-block j = 2p + h; scale byte b is byte b & 3 of word
                 // hv.y / hv.z / hv.w for b in 0-3 / 4-7 / 8-11
                 const int j = 2 * p + h, sh8 = 8 * (j & 3);
@@ -240,8 +264,24 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
             fence_async_shared();           // generic-proxy writes before the tensor cores read them
             mbar_arrive(&full_a[s]);
         }
+    } else if (warp == G_RAW_WARP) {
+        // ---- raw weights: per K step and live 16-row tile, its headers and the step's 512 code bytes
+        if (lane == 0) {
+            const uint8_t* t0 = tiles + ((int64_t)(row_base / 16 + m0 / 16) * nsb) * Q4T;
+            for (int i = 0; i < nk; ++i) {
+                const int rs = i % G_RAW_STAGES, sb = i >> 2, p = i & 3;
+                if (i >= G_RAW_STAGES) mbar_wait(&raw_empty[rs], (uint32_t)(((i / G_RAW_STAGES) + 1) & 1), err, 17, &abort_flag);
+                uint8_t* dst = raw + rs * G_RAW_STAGE;
+                mbar_expect_tx(&raw_full[rs], (uint32_t)(live_tiles * G_RAW_TILE));
+                for (int tt = 0; tt < live_tiles; ++tt) {
+                    const uint8_t* tb = t0 + ((int64_t)tt * nsb + sb) * Q4T;
+                    bulk_load(dst + tt * G_RAW_TILE, tb, 256, &raw_full[rs]);
+                    bulk_load(dst + tt * G_RAW_TILE + 256, tb + 256 + p * 512, 512, &raw_full[rs]);
+                }
+            }
+        }
     } else if (warp == G_TMA_WARP) {
-        // ---- the tokens' bf16 planes, one 64 x 64 box each per K step (rows past T read as zeros)
+        // ---- the tokens' bf16 planes, one 64-value x 128-token box each per K step (rows past T read as zeros)
         if (lane == 0) {
             pdl_wait();                     // x_hi / x_lo are written by the preceding kernel
             for (int i = 0; i < nk; ++i) {
@@ -277,17 +317,22 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
         }
     }
 
-    // ---- epilogue: warps 0-3, warp w reads TMEM lanes 32w .. 32w+31 (tile rows), 64 token columns
+    // ---- epilogue: warps 0-3, warp w reads TMEM lanes 32w .. 32w+31 (tile rows), 128 token columns in two halves
     if (warp < 4) {
         mbar_wait(&acc_full, 0u, err, 15, &abort_flag);
         tc_fence_after();
-        float v[64];
-        tmem_ld64(tmem + ((uint32_t)(32 * warp) << 16), v);
         const int r = m0 + 32 * warp + lane;
-        if (r < rows) {
 #pragma unroll
-            for (int j = 0; j < 64; ++j)
-                if (n0 + j < T) y[(int64_t)(n0 + j) * ldy + r] = v[j];
+        for (int half = 0; half < 2; ++half) {
+            float v[64];
+            tmem_ld64(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(64 * half), v);
+            if (r < rows) {
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    const int n = n0 + 64 * half + j;
+                    if (n < T) y[(int64_t)n * ldy + r] = v[j];
+                }
+            }
         }
     }
     tc_fence_before();
