@@ -110,6 +110,12 @@ void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_byte
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
                   int64_t ldy, int* err, cudaStream_t s);
 
+// Two Q4_K matrices with the same columns and activations (q and k, gate and up) in one tensor-core matvec launch:
+// y_a[t*ldy_a + r] = A[row_base_a + r] . x[t], y_b likewise; each row's result is the one matvec_tiles gives.
+void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_a, int64_t ldy_a, const uint8_t* tiles_b,
+                   int row_base_b, int rows_b, float* y_b, int64_t ldy_b, int cols, const XPrep& p, int* err,
+                   cudaStream_t s);
+
 // Q4_K GEMM on the tcgen05 tensor cores for T > 8 activation rows (prefill, large batches): y[t*ldy + r] =
 // W[row_base + r] . x[t*ldx ...] from the tile-major weights, with fp32-level accuracy (bf16 hi/lo planes of both
 // operands, three MMAs per slice, fp32 accumulation in tensor memory). scratch holds gemm_scratch_bytes(T, cols) bytes

@@ -13,6 +13,7 @@
 // Determinism. The eight warps of a CTA cover disjoint superblocks of the same rows and are summed in warp order,
 // and every column goes through the same fp32 operations whatever the number of columns beside it, so a column's
 // result never depends on the other columns of the launch.
+#include <climits>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -291,6 +292,15 @@ template <int NC> struct Q4Layout {
     static constexpr int SMEM = 8 * STAGES * STAGE;
 };
 
+// The second matrix of a two-matrix Q4_K matvec launch (same columns and activations as the first).
+struct MvSeg {
+    const uint8_t* wt;
+    int row_base, rows;
+    int first_ctas;             // CTAs of the first matrix; INT_MAX: one matrix
+    float* y;
+    int64_t ldy;
+};
+
 __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1)
 {
@@ -311,9 +321,9 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // result does not depend on how many columns share the launch.
 template <int NC, bool TILED>
 __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
-                                                    const uint8_t* __restrict__ wt, int row_base, int rows, int nsb,
-                                                    const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
-                                                    int* err)
+                                                    const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
+                                                    const uint8_t* __restrict__ xq, float* __restrict__ y_a,
+                                                    int64_t ldy_a, int* err, const MvSeg seg)
 {
     using LY = Q4Layout<NC>;
     constexpr bool PACK = NC <= 2;
@@ -321,7 +331,14 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const int r0 = blockIdx.x * Q4_ROWS;
+    // two matrices with the same input in one launch: CTAs past the first matrix's row tiles take the second's
+    const bool second = TILED && (int)blockIdx.x >= seg.first_ctas;
+    const int bx = second ? (int)blockIdx.x - seg.first_ctas : (int)blockIdx.x;
+    const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
+    const int row_base = second ? seg.row_base : row_base_a, rows = second ? seg.rows : rows_a;
+    float* __restrict__ y = second ? seg.y : y_a;
+    const int64_t ldy = second ? seg.ldy : ldy_a;
+    const int r0 = bx * Q4_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
     const int njobs = nsb > warp ? (nsb - warp + 7) / 8 : 0;
 
@@ -336,7 +353,7 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
         uint8_t* st = ring + s * LY::STAGE;
         mbar_expect_tx(&bars[warp][s], LY::TX);
         if (TILED)
-            bulk_load(st, wt + ((int64_t)(row_base / Q4_ROWS + blockIdx.x) * nsb + warp + 8 * j) * Q4_TILE, Q4_TILE,
+            bulk_load(st, wt + ((int64_t)(row_base / Q4_ROWS + bx) * nsb + warp + 8 * j) * Q4_TILE, Q4_TILE,
                       &bars[warp][s]);
         else
             tma_load_2d(st, &wmap, (warp + 8 * j) * 144, row_base + r0, &bars[warp][s]);
@@ -837,7 +854,7 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
 
 template <int NC, bool TILED>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                       float* y, int64_t ldy, int* err, cudaStream_t s)
+                       float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
     static bool attr[64] = {false};
     int dev = 0;
@@ -846,24 +863,25 @@ static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base,
         WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
         attr[dev] = true;
     }
-    launch(k_mmv_q4k<NC, TILED>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles,
-           row_base, rows, nsb, (const uint8_t*)p.blocks, y, ldy, err);
+    const int ctas = (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
+    launch(k_mmv_q4k<NC, TILED>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
+           (const uint8_t*)p.blocks, y, ldy, err, seg);
     note_launch();
 }
 
 template <bool TILED>
 static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                         float* y, int64_t ldy, int* err, cudaStream_t s)
+                         float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
     switch (p.nc) {
-    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
-    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s); break;
+    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     }
 }
 
@@ -872,7 +890,7 @@ void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols
 {
     (void)type;
     dispatch_q4k<false>(*reinterpret_cast<const CUtensorMap*>(map.bytes), nullptr, row_base, rows, cols / 256, p, y,
-                        ldy, err, s);
+                        ldy, err, s, MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0});
 }
 
 
@@ -926,6 +944,19 @@ static void matvec_q6k(const uint8_t* tiles, int rows, int cols, const XPrep& p,
     }
 }
 
+void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_a, int64_t ldy_a, const uint8_t* tiles_b,
+                   int row_base_b, int rows_b, float* y_b, int64_t ldy_b, int cols, const XPrep& p, int* err,
+                   cudaStream_t s)
+{
+    if ((uintptr_t)tiles_a % 16 != 0 || (uintptr_t)tiles_b % 16 != 0 || row_base_a % 16 != 0 || row_base_b % 16 != 0)
+        WL_THROW(WL_EINVAL, "matvec_tiles2: misaligned tiles");
+    if (!tiles_supported(12, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles2: Q4_K with cols a multiple of 256 only");
+    CUtensorMap none;
+    memset(&none, 0, sizeof none);
+    const MvSeg seg{tiles_b, row_base_b, rows_b, (rows_a + Q4_ROWS - 1) / Q4_ROWS, y_b, ldy_b};
+    dispatch_q4k<true>(none, tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, err, s, seg);
+}
+
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
                   int64_t ldy, int* err, cudaStream_t s)
 {
@@ -934,7 +965,8 @@ void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int co
     if (type == 12) {
         CUtensorMap none;
         memset(&none, 0, sizeof none);
-        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s);
+        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
+                           MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0});
     } else {
         matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }

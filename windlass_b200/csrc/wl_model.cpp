@@ -885,6 +885,29 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
     profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows));
 }
 
+void Model::matmul2(const Weight& a, const Weight& b, const float* x, int T, float* ya, float* yb)
+{
+    const bool pair = T <= 8 && a.present() && b.present() && a.type == 12 && b.type == 12 && a.tiles && b.tiles &&
+                      a.cols == b.cols && a.row_base % 16 == 0 && b.row_base % 16 == 0 && xprep_buf_;
+    if (!pair) {
+        matmul(a, x, T, ya, 0, true);
+        matmul(b, x, T, yb, 0, true);
+        return;
+    }
+    const k::XPrep p = k::xprep_view(xprep_buf_, a.cols, T);
+    if (!(prep_x_ == x && prep_cols_ == a.cols && prep_nc_ == T)) {
+        const int pm = profile_begin();
+        k::xprep(x, a.cols, a.cols, T, p, stream_);
+        profile_end(pm, WL_PROFILE_XPREP, 0.0);
+        prep_x_ = x; prep_cols_ = a.cols; prep_nc_ = T;
+    }
+    const int mark = profile_begin();
+    k::matvec_tiles2(a.tiles, a.row_base, a.rows, ya, a.rows, b.tiles, b.row_base, b.rows, yb, b.rows, a.cols, p, err_d_,
+                     stream_);
+    profile_end(mark, a.type, (double)a.rows * a.row_bytes + (double)b.rows * b.row_bytes +
+                                  4.0 * T * ((double)a.cols + a.rows + b.rows));
+}
+
 // Starts a profiled region (an event pair around launches on the model's stream); -1 when profiling is off.
 int Model::profile_begin()
 {
@@ -961,8 +984,7 @@ void Model::check_device_error()
 void Model::ffn_dense(const LayerW& L, int T)
 {
     const int F = L.gate.rows;
-    matmul(L.gate, xn_, T, g_, 0, true);
-    matmul(L.up, xn_, T, u_, 0, true);
+    matmul2(L.gate, L.up, xn_, T, g_, u_);
     prep_x_ = nullptr;
     const int sm = profile_begin();
     if (L.down.tiles && T <= 8 && F % 256 == 0 && xprep_buf_) {
@@ -1038,8 +1060,7 @@ void Model::layer(int l, int T, int max_n)
     } else {
         pre_norm(T, L.attn_norm, L.q.tiles != nullptr);
     }
-    matmul(L.q, xn_, T, q_, 0, true);
-    matmul(L.k, xn_, T, k_, 0, true);
+    matmul2(L.q, L.k, xn_, T, q_, k_);
     matmul(L.v, xn_, T, v_, 0, true);
     if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
     if (L.kb.present()) k::add_bias(k_, L.kb.d, T, KD, stream_);

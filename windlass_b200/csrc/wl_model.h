@@ -103,6 +103,9 @@ public:
     // y[T][rows] = W x[T][cols] on the model's stream (row t at y + t*ldy, ldy 0 = rows); path 0 chooses by T (the
     // forward pass's own rule).
     void matmul(const Weight& w, const float* x, int T, float* y, int path = 0, bool reuse_x = false, int64_t ldy = 0);
+    // ya = A x and yb = B x for two matrices with the same input (q and k, gate and up): one tensor-core launch for
+    // decode steps when both are tiled Q4_K, else two matmuls. Each row's result is what matmul gives.
+    void matmul2(const Weight& a, const Weight& b, const float* x, int T, float* ya, float* yb);
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
