@@ -175,7 +175,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
     // 16-row weight tiles of this CTA that exist (the last CTA of a matrix may have fewer than eight)
     const int live_tiles = min(G_BM / 16, (rows + 15) / 16 - m0 / 16);
 
-    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
             mbar_init(&full_a[s], G_DQ_WARPS * 32);
@@ -283,7 +282,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
     } else if (warp == G_TMA_WARP) {
         // ---- the tokens' bf16 planes, one 64-value x 128-token box each per K step (rows past T read as zeros)
         if (lane == 0) {
-            pdl_wait();                     // x_hi / x_lo are written by the preceding kernel
             for (int i = 0; i < nk; ++i) {
                 const int s = i % G_STAGES;
                 if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 12, &abort_flag);
@@ -416,7 +414,10 @@ void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols
         attr[dev] = true;
     }
     const dim3 grid((rows + G_BM - 1) / G_BM, (T + G_BN - 1) / G_BN);
-    launch(k_gemm_q4k, grid, dim3(G_THREADS), G_SMEM, s, mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    // A plain launch, and the kernel does not trigger its dependents: no other kernel overlaps a GEMM. With programmatic
+    // dependent launch on both sides, consecutive GEMMs (each with its own activation-plane tensor maps) overlapped
+    // and gave wrong sums now and then (1-3 % relative error in a 2-layer prefill, never with either side serialised).
+    k_gemm_q4k<<<grid, G_THREADS, G_SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
     note_launch();
 }
 

@@ -1,6 +1,7 @@
 // Kernel launches with programmatic dependent launch (PDL).
 //
-// Every kernel of the library is launched with programmatic stream serialisation allowed, and every kernel starts
+// Every kernel of the library but the tcgen05 GEMM (wl_gemm.cu, launched plainly and never overlapped) is launched
+// with programmatic stream serialisation allowed, and every such kernel starts
 // with pdl_trigger() then pdl_wait(): the next kernel on the stream may be scheduled as soon as all CTAs of this one
 // have started, and it waits in pdl_wait() until this one has completed and its writes are visible. A kernel does
 // nothing before its pdl_wait() except work that reads no buffer another kernel writes (the weight copies of the
