@@ -862,6 +862,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
 // output (64 threads, 4 consecutive values each, all within one head): M = max m_s, w_s = e^(m_s - M),
 // out = sum_s w_s o_s / sum_s w_s l_s, sums in double in range order. With prep, the superblock is also written in
 // the tensor-core matvec's activation layout. All loads of a thread are issued before their first use.
+template <int S>
 __global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const float* __restrict__ part,
                                                      const float* __restrict__ ml, float* __restrict__ out,
                                                      uint8_t* __restrict__ prep)
@@ -871,27 +872,38 @@ __global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const fl
     __shared__ float scratch[2];
     const int sb = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
     const int QD = heads * hd, v = sb * 256 + 4 * tid, head = v / hd, d = v % hd;
-    const float2* mlp = reinterpret_cast<const float2*>(ml + ((int64_t)t * heads + head) * ATT_SPLITS * 2);
-    const float* pp = part + ((int64_t)t * heads + head) * ATT_SPLITS * hd + d;
-    float2 mls[ATT_SPLITS];
-    float4 ps[ATT_SPLITS];
-#pragma unroll
-    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) {
-        mls[s2] = mlp[s2];
-        ps[s2] = *reinterpret_cast<const float4*>(pp + (int64_t)s2 * hd);
-    }
+    const float2* mlp = reinterpret_cast<const float2*>(ml + ((int64_t)t * heads + head) * S * 2);
+    const float* pp = part + ((int64_t)t * heads + head) * S * hd + d;
+    // ranges in groups of 16, each group's loads issued before their first use
+    constexpr int GR = S < 16 ? S : 16;
     float M = -INFINITY;
 #pragma unroll
-    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) M = fmaxf(M, mls[s2].x);
+    for (int g0 = 0; g0 < S; g0 += GR) {
+        float2 mls[GR];
+#pragma unroll
+        for (int s2 = 0; s2 < GR; ++s2) mls[s2] = mlp[g0 + s2];
+#pragma unroll
+        for (int s2 = 0; s2 < GR; ++s2) M = fmaxf(M, mls[s2].x);
+    }
     double L = 0.0, o0 = 0.0, o1 = 0.0, o2 = 0.0, o3 = 0.0;
 #pragma unroll
-    for (int s2 = 0; s2 < ATT_SPLITS; ++s2) {
-        const double w = mls[s2].y > 0.f ? (double)expf(mls[s2].x - M) : 0.0;
-        L += w * (double)mls[s2].y;
-        o0 += w * (double)ps[s2].x;
-        o1 += w * (double)ps[s2].y;
-        o2 += w * (double)ps[s2].z;
-        o3 += w * (double)ps[s2].w;
+    for (int g0 = 0; g0 < S; g0 += GR) {
+        float2 mls[GR];
+        float4 ps[GR];
+#pragma unroll
+        for (int s2 = 0; s2 < GR; ++s2) {
+            mls[s2] = mlp[g0 + s2];
+            ps[s2] = *reinterpret_cast<const float4*>(pp + (int64_t)(g0 + s2) * hd);
+        }
+#pragma unroll
+        for (int s2 = 0; s2 < GR; ++s2) {
+            const double w = mls[s2].y > 0.f ? (double)expf(mls[s2].x - M) : 0.0;
+            L += w * (double)mls[s2].y;
+            o0 += w * (double)ps[s2].x;
+            o1 += w * (double)ps[s2].y;
+            o2 += w * (double)ps[s2].z;
+            o3 += w * (double)ps[s2].w;
+        }
     }
     const float f[4] = {(float)(o0 / L), (float)(o1 / L), (float)(o2 / L), (float)(o3 / L)};
     *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
@@ -900,8 +912,7 @@ __global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const fl
 
 int attention_splits(int T, int kv_heads)
 {
-    (void)kv_heads;
-    return T <= ATT_PART_ROWS ? ATT_SPLITS : 1;
+    return T <= ATT_PART_ROWS ? attention_splits_for(kv_heads) : 1;
 }
 
 template <int HD, int G>
@@ -917,13 +928,15 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
         WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
         attr_set[dev] = true;
     }
-    float* ml = part + (size_t)ATT_PART_ROWS * ATT_SPLITS * heads * HD;
+    float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
     launch(k_attn_part<HD, G>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows, layer,
            pos, S, out, part, ml);
     launched();
     if (S > 1) {
-        launch(k_attn_combine, dim3(heads * HD / 256, T), dim3(64), 0, s, heads, (int)HD, (const float*)part,
-               (const float*)ml, out, prep ? prep->blocks : (uint8_t*)nullptr);
+        auto comb = S == 16 ? k_attn_combine<16> : S == 32 ? k_attn_combine<32> : k_attn_combine<64>;
+        if (S != 16 && S != 32 && S != 64) WL_THROW(WL_EINVAL, "attention: unexpected range count");
+        launch(comb, dim3(heads * HD / 256, T), dim3(64), 0, s, heads, (int)HD, (const float*)part, (const float*)ml,
+               out, prep ? prep->blocks : (uint8_t*)nullptr);
         launched();
     }
 }

@@ -137,15 +137,22 @@ void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, con
 void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows, int layer, const int32_t* pos,
                cudaStream_t s);
 // Attention (Transformer.cs:351-395): row t, head h attends to positions 0..pos[t] of its own cache. part is a
-// workspace of attention_part_floats(heads, head_dim) floats for the split-range partials. For up to
-// ATT_PART_ROWS rows each row's positions are split into ATT_SPLITS ranges (a fixed count, so a row's result never
-// depends on the other rows); with prep (T <= 8) the output is also written as prepared activations, and the call
+// workspace of attention_part_floats(heads, kv_heads, head_dim) floats for the split-range partials. For up to
+// ATT_PART_ROWS rows each row's positions are split into S ranges, S fixed by the model's KV-head count (16 at 8 or
+// more KV heads, up to 64 at one, so that S x kv_heads CTAs cover the SMs): a row's result never depends on the
+// other rows; with prep (T <= 8) the output is also written as prepared activations, and the call
 // returns whether it did.
 constexpr int ATT_PART_ROWS = 64;
-constexpr int ATT_SPLITS = 16;
-inline size_t attention_part_floats(int heads, int head_dim)
+constexpr int ATT_SPLITS = 16;                  // S at 8 or more KV heads
+constexpr int ATT_MAX_SPLITS = 64;
+inline int attention_splits_for(int kv_heads)
 {
-    return (size_t)ATT_PART_ROWS * ATT_SPLITS * heads * (head_dim + 2);
+    const int s = 128 / (kv_heads > 0 ? kv_heads : 1);
+    return s < ATT_SPLITS ? ATT_SPLITS : s > ATT_MAX_SPLITS ? ATT_MAX_SPLITS : s;
+}
+inline size_t attention_part_floats(int heads, int kv_heads, int head_dim)
+{
+    return (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (head_dim + 2);
 }
 int attention_splits(int T, int kv_heads);
 bool attention_supported(int heads, int kv_heads, int head_dim);

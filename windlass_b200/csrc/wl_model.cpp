@@ -815,7 +815,7 @@ void Model::ensure_workspace(int T, int logit_rows)
                 if (w->present()) max_cols = std::max(max_cols, w->cols);
         }
         WL_CUDA(cudaMalloc(&xprep_buf_, k::xprep_bytes(max_cols, 8)));
-        att_part_ = dalloc<float>((int64_t)k::attention_part_floats(c_.heads, c_.head_dim));
+        att_part_ = dalloc<float>((int64_t)k::attention_part_floats(c_.heads, c_.kv_heads, c_.head_dim));
     }
     if (logit_rows > ws_logit_rows_) {
         dfree(logits_);
