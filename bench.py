@@ -309,6 +309,10 @@ def main():
     ap.add_argument("--batches", default="1,4,8,64")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--streamed", action="store_true", help="configs[3] (a): layers streamed from pinned host memory")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one GPU runs the shapes one rank holds under tensor parallelism over N GPUs (no exchange)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -338,8 +342,12 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    from windlass_b200.transformer import llama70b_spec
+    from windlass_b200.transformer import llama70b_spec, synth_spec
     spec = llama70b_spec(layers=args.layers)
+    if args.shard_of > 1:
+        g = args.shard_of
+        spec = synth_spec("llama", args.layers, 8192, 64 // g, 8 // g, 128, 28672 // g, 128256 // g, 8192,
+                          rope_base=500000.0, type_attn_v=14, type_embd=12)
     steps, warm, B = args.steps, args.warmup, args.batch
     ctx = args.prompt + 2 * (steps + warm) + 64
     t0 = time.perf_counter()
@@ -365,8 +373,12 @@ def main():
     trace(f"kernel launches before the timed region: {launches0}")
     barrier()
     with ClockSampler(local) as clk:
+        if args.profile_range:
+            torch.cuda.profiler.start()
         ms = m.bench_decode(seqs, steps)
         barrier()
+        if args.profile_range:
+            torch.cuda.profiler.stop()
     launches = m.stats().kernel_launches - launches0
     ms_max = tp.max_over_ranks(dist, ms)
     value = steps * B / (ms_max / 1e3)
@@ -424,8 +436,11 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warm,
                 "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "q4_K/q6_K weights, f32 compute", "data": "synthetic",
-                "config": {"workload": f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
-                                       f"{args.layers} layers", "batch": B, "prompt": args.prompt,
+                "config": {"workload": (f"decode b{B}, one TP{args.shard_of} rank's shard of the Llama-3.3-70B-shaped "
+                                        f"Q4_K_M decoder on one GPU (no exchange), {args.layers} layers")
+                           if args.shard_of > 1 else
+                           f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
+                           f"{args.layers} layers", "batch": B, "prompt": args.prompt,
                            "parallelism": f"tp{world}, all-reduce x2 per layer: {allreduce}" if world > 1 else "1 GPU",
                            "l2": "inputs larger than L2 (39.5 GB of weights read per step)"},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,

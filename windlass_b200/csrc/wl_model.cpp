@@ -887,8 +887,17 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
 
 void Model::matmul2(const Weight& a, const Weight& b, const float* x, int T, float* ya, float* yb)
 {
+    // one launch when the pair fits in about two waves of CTAs (16-row tiles; up to 4 CTAs per SM for one or two
+    // columns): that is where the second matrix would otherwise run as a small separate launch. Longer matrices run
+    // as two launches, which programmatic dependent launch already overlaps.
+    static const int sms = [] {
+        int dev = 0, n = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n;
+    }();
     const bool pair = T <= 8 && a.present() && b.present() && a.type == 12 && b.type == 12 && a.tiles && b.tiles &&
-                      a.cols == b.cols && a.row_base % 16 == 0 && b.row_base % 16 == 0 && xprep_buf_;
+                      a.cols == b.cols && a.row_base % 16 == 0 && b.row_base % 16 == 0 && xprep_buf_ &&
+                      (a.rows + 15) / 16 + (b.rows + 15) / 16 <= 8 * sms;
     if (!pair) {
         matmul(a, x, T, ya, 0, true);
         matmul(b, x, T, yb, 0, true);
