@@ -80,7 +80,10 @@ typedef struct wl_options {
                                 every rank. Query/key/value, gate/up and the output head are split by rows, the
                                 attention output and down projections by columns, with an NCCL all-reduce after each
                                 of the latter two (dense models; head and KV-head counts divisible by tp_size). */
-    int32_t tp_rank;         /* this caller's rank, 0 .. tp_size-1 */
+    int32_t tp_rank;         /* this caller's rank, 0 .. tp_size-1; or -1: this one wl_model spans all tp_size GPUs
+                                (devices device .. device+tp_size-1), one shard and one host thread per GPU inside
+                                this process, for hosts that run a single process (tp_id is then not read). Every
+                                call runs all shards at once; progress callbacks come on the calling thread */
     int32_t tp_nccl_only;    /* 0: decode-step all-reduces fused into the producing matvec and the consuming norm over
                                 NVLink peer memory (CUDA IPC), falling back to NCCL when the GPUs cannot map each
                                 other's memory; 1: NCCL all-reduce only */

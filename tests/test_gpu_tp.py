@@ -95,3 +95,29 @@ def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
         assert np.array_equal(got["batch"], got["single"]), "ForwardBatch rows differ from single runs"
     else:
         compare(got["batch"], got["single"], f"tp{n} {spec} batch rows")
+
+
+def test_in_process_group_matches_process_ranks(wl, tmp_path):
+    """tp_rank = -1: one wl_model spanning the GPUs inside this process (one host thread per GPU, peers reached by
+    pointer) returns bit for bit what the one-process-per-GPU ranks return, fused all-reduce included."""
+    from windlass_b200.transformer import CudaTransformer
+    n = int(os.environ.get("WL_TP_TEST_GPUS", "2"))
+    if _gpus() < n:
+        pytest.skip(f"needs {n} GPUs")
+    ranks = run_ranks(n, "gqa", tmp_path)
+    sp = spec_of("gqa")
+    with CudaTransformer(synthetic=sp, max_context=256, tp_size=n, tp_rank=-1) as m:
+        assert m.info.tp_size == n and m.info.tp_rank == -1 and m.info.tp_fused == 1
+        prompt = ranks[0]["prompt"]
+        assert np.array_equal(m.forward(prompt, all_logits=True), ranks[0]["prefill"])
+        for i, t in enumerate(ranks[0]["tokens"]):
+            assert np.array_equal(m.forward([int(t)], pos0=len(prompt) + i), ranks[0]["decode"][i]), f"step {i}"
+        s1, s2 = m.new_sequence(), m.new_sequence()
+        m.forward(prompt[:7], seq=s1)
+        m.forward(prompt[3:20], seq=s2)
+        assert np.array_equal(m.forward_batch([s1, s2], [11, 22]), ranks[0]["batch"])
+        stages = []
+        m.forward(prompt[:5], seq=s1, on_stage=lambda d, tot: stages.append(d))
+        assert stages[-1] == sp.layers + 1
+        s1.close()
+        s2.close()

@@ -1,5 +1,6 @@
 // The C ABI of libwindlass_cuda (include/windlass.h): argument checks, exception-to-status translation, and the
 // kernel-level test exports. No function aborts or exits; failures return a status and set wl_last_error().
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -7,19 +8,34 @@
 #include "../../include/windlass.h"
 #include "wl_common.h"
 #include "wl_kernels.h"
+#include "wl_group.h"
 #include "wl_model.h"
 
 namespace wl { const char* last_error_cstr(); }
 
+// m: the model, or shard 0 of g (one model spanning several GPUs in this process, wl_options.tp_rank = -1).
 struct wl_model {
     wl::Model* m;
+    wl::Group* g;
 };
+// s: the sequence, or shard 0's of a group model, shards[i] shard i's.
 struct wl_seq {
     wl::Seq* s;
     wl_model* owner;
+    std::vector<wl::Seq*> shards;
 };
 
 namespace {
+bool in_process_group(const wl_options& o)
+{
+    return o.size >= (int32_t)sizeof(wl_options) && o.tp_size > 1 && o.tp_rank == -1;
+}
+
+// The sequence of shard g (shard 0: the sequence itself).
+wl::Seq* shard_seq(wl_seq* seq, int g) { return g == 0 ? seq->s : seq->shards[(size_t)g]; }
+
+void noop_progress(int32_t, int32_t, void*) {}
+
 template <typename F> int32_t guarded(F&& f)
 {
     try {
@@ -137,8 +153,13 @@ int32_t wl_open(const char* path, const wl_options* opt, wl_model** out)
         if (!path || !out) return wl::fail(WL_EINVAL, "wl_open: path and out are required");
         *out = nullptr;
         const wl_options o = opt ? *opt : defaults();
+        if (in_process_group(o)) {
+            wl::Group* g = wl::Group::open(path, nullptr, o);
+            *out = new wl_model{&g->shard(0), g};
+            return WL_OK;
+        }
         wl::Model* m = wl::Model::open_file(path, o);
-        *out = new wl_model{m};
+        *out = new wl_model{m, nullptr};
         return WL_OK;
     });
 }
@@ -149,8 +170,13 @@ int32_t wl_open_synthetic(const wl_synth_spec* spec, const wl_options* opt, wl_m
         if (!spec || !out) return wl::fail(WL_EINVAL, "wl_open_synthetic: spec and out are required");
         *out = nullptr;
         const wl_options o = opt ? *opt : defaults();
+        if (in_process_group(o)) {
+            wl::Group* g = wl::Group::open(nullptr, spec, o);
+            *out = new wl_model{&g->shard(0), g};
+            return WL_OK;
+        }
         wl::Model* m = wl::Model::open_synthetic(*spec, o);
-        *out = new wl_model{m};
+        *out = new wl_model{m, nullptr};
         return WL_OK;
     });
 }
@@ -159,7 +185,8 @@ int32_t wl_close(wl_model* model)
 {
     return guarded([&]() -> int32_t {
         if (!model) return WL_OK;
-        delete model->m;
+        if (model->g) delete model->g;
+        else delete model->m;
         delete model;
         return WL_OK;
     });
@@ -178,7 +205,9 @@ int32_t wl_info_get(const wl_model* model, wl_info* info)
         info->weight_bytes = model->m->weight_bytes(); info->device_bytes = model->m->device_bytes();
         strncpy(info->arch, c.arch.c_str(), sizeof info->arch - 1);
         info->tp_size = model->m->tp_size();
-        info->tp_rank = model->m->tp_rank();
+        info->tp_rank = model->g ? -1 : model->m->tp_rank();
+        if (model->g)
+            for (int g = 1; g < model->g->size(); ++g) info->device_bytes += model->g->shard(g).device_bytes();
         info->tp_fused = model->m->tp_fused() ? 1 : 0;
         return WL_OK;
     });
@@ -200,11 +229,20 @@ int32_t wl_bench_decode(wl_model* model, wl_seq* const* seqs, int32_t N, int32_t
 {
     return guarded([&]() -> int32_t {
         if (!model || !seqs || !device_ms) return wl::fail(WL_EINVAL, "wl_bench_decode: model, seqs and device_ms are required");
-        std::vector<wl::Seq*> ss((size_t)(N > 0 ? N : 0));
-        for (int i = 0; i < N; ++i) {
+        for (int i = 0; i < N; ++i)
             if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_bench_decode: a sequence belongs to another model");
-            ss[(size_t)i] = seqs[i]->s;
+        if (model->g) {
+            std::vector<double> ms((size_t)model->g->size(), 0.0);
+            model->g->run([&](int g) {
+                std::vector<wl::Seq*> ss((size_t)(N > 0 ? N : 0));
+                for (int i = 0; i < N; ++i) ss[(size_t)i] = shard_seq(seqs[i], g);
+                ms[(size_t)g] = model->g->shard(g).bench_decode(ss.data(), N, steps);
+            });
+            *device_ms = *std::max_element(ms.begin(), ms.end());
+            return WL_OK;
         }
+        std::vector<wl::Seq*> ss((size_t)(N > 0 ? N : 0));
+        for (int i = 0; i < N; ++i) ss[(size_t)i] = seqs[i]->s;
         *device_ms = model->m->bench_decode(ss.data(), N, steps);
         return WL_OK;
     });
@@ -214,7 +252,8 @@ int32_t wl_profile(wl_model* model, int32_t on)
 {
     return guarded([&]() -> int32_t {
         if (!model) return wl::fail(WL_EINVAL, "wl_profile: model is required");
-        model->m->set_profiling(on != 0);
+        if (model->g) model->g->run([&](int g) { model->g->shard(g).set_profiling(on != 0); });
+        else model->m->set_profiling(on != 0);
         return WL_OK;
     });
 }
@@ -232,7 +271,12 @@ int32_t wl_seq_new(wl_model* model, wl_seq** out)
 {
     return guarded([&]() -> int32_t {
         if (!model || !out) return wl::fail(WL_EINVAL, "wl_seq_new: model and out are required");
-        *out = new wl_seq{model->m->new_seq(), model};
+        wl_seq* q = new wl_seq{model->m->new_seq(), model, {}};
+        if (model->g) {
+            q->shards.push_back(q->s);
+            for (int g = 1; g < model->g->size(); ++g) q->shards.push_back(model->g->shard(g).new_seq());
+        }
+        *out = q;
         return WL_OK;
     });
 }
@@ -241,6 +285,8 @@ int32_t wl_seq_free(wl_seq* seq)
 {
     return guarded([&]() -> int32_t {
         if (!seq) return WL_OK;
+        if (seq->owner->g)
+            for (int g = 1; g < seq->owner->g->size(); ++g) seq->owner->g->shard(g).free_seq(seq->shards[(size_t)g]);
         seq->owner->m->free_seq(seq->s);
         delete seq;
         return WL_OK;
@@ -252,7 +298,12 @@ int32_t wl_seq_truncate(wl_seq* seq, int32_t n)
 {
     return guarded([&]() -> int32_t {
         if (!seq) return wl::fail(WL_EINVAL, "wl_seq_truncate: seq is required");
-        if (n < seq->s->length) seq->s->length = n < 0 ? 0 : n;
+        if (seq->shards.empty()) {
+            if (n < seq->s->length) seq->s->length = n < 0 ? 0 : n;
+        } else {
+            for (wl::Seq* s : seq->shards)
+                if (n < s->length) s->length = n < 0 ? 0 : n;
+        }
         return WL_OK;
     });
 }
@@ -270,8 +321,11 @@ int32_t wl_truncate(wl_model* model, int32_t n)
 {
     return guarded([&]() -> int32_t {
         if (!model) return wl::fail(WL_EINVAL, "wl_truncate: model is required");
-        wl::Seq* s = model->m->own();
-        if (n < s->length) s->length = n < 0 ? 0 : n;
+        const int G = model->g ? model->g->size() : 1;
+        for (int g = 0; g < G; ++g) {
+            wl::Seq* s = model->g ? model->g->shard(g).own() : model->m->own();
+            if (n < s->length) s->length = n < 0 ? 0 : n;
+        }
         return WL_OK;
     });
 }
@@ -292,7 +346,23 @@ int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t 
         if (model && T == 0) return wl::fail(WL_EINVAL, "No tokens to run.");
         if (!model || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward: model, tokens and logits_out are required");
         if (seq && seq->owner != model) return wl::fail(WL_EINVAL, "wl_forward: the sequence belongs to another model");
-        const int32_t st = model->m->forward(seq ? seq->s : nullptr, tokens, T, pos0, all_logits != 0, logits_out, cancel, progress, user);
+        int32_t st;
+        if (model->g) {
+            // every shard runs the same call; shard 0's logits are returned and its thread (the caller) reports
+            // progress; the others take the same path (a progress callback that does nothing)
+            std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+            const size_t rows = all_logits ? (size_t)T : 1;
+            model->g->run([&](int g) {
+                wl::Model& m = model->g->shard(g);
+                float* out = g == 0 ? logits_out : model->g->scratch(g, rows * (size_t)m.config().vocab);
+                sts[(size_t)g] = m.forward(seq ? shard_seq(seq, g) : nullptr, tokens, T, pos0, all_logits != 0, out,
+                                           cancel, g == 0 ? progress : (progress ? noop_progress : nullptr),
+                                           g == 0 ? user : nullptr);
+            });
+            st = sts[0];
+        } else {
+            st = model->m->forward(seq ? seq->s : nullptr, tokens, T, pos0, all_logits != 0, logits_out, cancel, progress, user);
+        }
         if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
         return st;
     });
@@ -304,12 +374,26 @@ int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* to
     return guarded([&]() -> int32_t {
         if (!model || !seqs || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward_batch: model, seqs, tokens and logits_out are required");
         if (N <= 0) return wl::fail(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
-        std::vector<wl::Seq*> ss((size_t)N);
-        for (int i = 0; i < N; ++i) {
+        for (int i = 0; i < N; ++i)
             if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_forward_batch: a sequence belongs to another model");
-            ss[(size_t)i] = seqs[i]->s;
+        int32_t st;
+        if (model->g) {
+            std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+            model->g->run([&](int g) {
+                wl::Model& m = model->g->shard(g);
+                std::vector<wl::Seq*> ss((size_t)N);
+                for (int i = 0; i < N; ++i) ss[(size_t)i] = shard_seq(seqs[i], g);
+                float* out = g == 0 ? logits_out : model->g->scratch(g, (size_t)N * m.config().vocab);
+                sts[(size_t)g] = m.forward_batch(ss.data(), tokens, N, out, cancel,
+                                                 g == 0 ? progress : (progress ? noop_progress : nullptr),
+                                                 g == 0 ? user : nullptr);
+            });
+            st = sts[0];
+        } else {
+            std::vector<wl::Seq*> ss((size_t)N);
+            for (int i = 0; i < N; ++i) ss[(size_t)i] = seqs[i]->s;
+            st = model->m->forward_batch(ss.data(), tokens, N, logits_out, cancel, progress, user);
         }
-        const int32_t st = model->m->forward_batch(ss.data(), tokens, N, logits_out, cancel, progress, user);
         if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
         return st;
     });

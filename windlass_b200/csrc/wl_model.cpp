@@ -6,6 +6,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <unistd.h>
 #include "wl_common.h"
 #include "wl_gguf.h"
 
@@ -102,8 +103,10 @@ void Model::init_tp(const wl_options& opt)
     init_fused_ar(opt);
 }
 
-// Maps every rank's all-reduce buffer into this process (CUDA IPC handles exchanged with an NCCL all-gather). All
-// ranks agree on the outcome: if any rank cannot map a peer, every rank keeps NCCL for all its all-reduces.
+// Maps every rank's all-reduce buffer into this process. Ranks exchange (process id, device, pointer, CUDA IPC
+// handle) with an NCCL all-gather: a peer in another process is mapped through its IPC handle, a peer in this process
+// (one wl_model spanning several GPUs) is reached through its pointer once peer access to its device is on. All ranks
+// agree on the outcome: if any rank cannot reach a peer, every rank keeps NCCL for all its all-reduces.
 void Model::init_fused_ar(const wl_options& opt)
 {
     const int G = tp_size_;
@@ -111,25 +114,47 @@ void Model::init_fused_ar(const wl_options& opt)
     const size_t bytes = k::ar_buffer_bytes(c_.embd);
     ar_buf_ = dalloc<uint8_t>((int64_t)bytes);
     WL_CUDA(cudaMemset(ar_buf_, 0, bytes));
-    cudaIpcMemHandle_t mine;
-    int failed = cudaIpcGetMemHandle(&mine, ar_buf_) != cudaSuccess;
+    struct PeerRec {
+        cudaIpcMemHandle_t handle;
+        uint64_t ptr;
+        int64_t pid;
+        int32_t device, ok;
+        uint8_t pad[128 - 64 - 24];
+    };
+    static_assert(sizeof(PeerRec) == 128, "peer record size");
+    PeerRec mine{};
+    mine.ok = cudaIpcGetMemHandle(&mine.handle, ar_buf_) == cudaSuccess;
     cudaGetLastError();
-    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
-    uint8_t* hd = dalloc<uint8_t>(64 * G);
-    std::vector<cudaIpcMemHandle_t> all(G);
-    WL_CUDA(cudaMemcpy(hd + 64 * tp_rank_, &mine, 64, cudaMemcpyHostToDevice));
-    comm_->allgather(hd + 64 * tp_rank_, hd, 64, stream_);
+    mine.ptr = (uint64_t)(uintptr_t)ar_buf_;
+    mine.pid = (int64_t)getpid();
+    mine.device = device_;
+    uint8_t* hd = dalloc<uint8_t>(128 * G);
+    std::vector<PeerRec> all(G);
+    WL_CUDA(cudaMemcpy(hd + 128 * tp_rank_, &mine, 128, cudaMemcpyHostToDevice));
+    comm_->allgather(hd + 128 * tp_rank_, hd, 128, stream_);
     WL_CUDA(cudaStreamSynchronize(stream_));
-    WL_CUDA(cudaMemcpy(all.data(), hd, 64 * (size_t)G, cudaMemcpyDeviceToHost));
+    WL_CUDA(cudaMemcpy(all.data(), hd, 128 * (size_t)G, cudaMemcpyDeviceToHost));
     dfree(hd);
+    int failed = 0;
     for (int g = 0; g < G && !failed; ++g) {
+        ar_ipc_[g] = false;
         if (g == tp_rank_) { ar_peer_[g] = ar_buf_; continue; }
+        if (all[g].pid == mine.pid) {
+            int can = 0;
+            if (cudaDeviceCanAccessPeer(&can, device_, all[g].device) != cudaSuccess || !can) { failed = 1; break; }
+            const cudaError_t e = cudaDeviceEnablePeerAccess(all[g].device, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) failed = 1;
+            cudaGetLastError();
+            if (!failed) ar_peer_[g] = (uint8_t*)(uintptr_t)all[g].ptr;
+            continue;
+        }
         void* p = nullptr;
-        if (cudaIpcOpenMemHandle(&p, all[g], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        if (!all[g].ok || cudaIpcOpenMemHandle(&p, all[g].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
             cudaGetLastError();
             failed = 1;
         } else {
             ar_peer_[g] = (uint8_t*)p;
+            ar_ipc_[g] = true;
         }
     }
     *flag_h_ = failed;
@@ -138,22 +163,30 @@ void Model::init_fused_ar(const wl_options& opt)
     WL_CUDA(cudaStreamSynchronize(stream_));
     WL_CUDA(cudaMemcpy(flag_h_, flag_d_, sizeof(int32_t), cudaMemcpyDeviceToHost));
     ar_on_ = *flag_h_ == 0;
-    if (!ar_on_) close_fused_ar();
+    if (!ar_on_) {
+        // every rank takes this path together, so the orderly close's collectives meet
+        opened_ = true;
+        close_fused_ar();
+        opened_ = false;
+    }
 }
 
 // Every rank stops using the buffers before any rank unmaps or frees its own (two NCCL barriers around the unmap).
 void Model::close_fused_ar()
 {
     if (!ar_buf_) return;
+    // a model whose open did not complete has run no step: nothing reads the buffers, and its peers may be gone
     auto barrier = [&] {
         WL_CUDA(cudaStreamSynchronize(stream_));
+        if (!opened_) return;
         comm_->allreduce_max(flag_d_, 1, stream_);
         WL_CUDA(cudaStreamSynchronize(stream_));
     };
     barrier();
     for (int g = 0; g < tp_size_; ++g) {
-        if (g != tp_rank_ && ar_peer_[g]) cudaIpcCloseMemHandle(ar_peer_[g]);
+        if (g != tp_rank_ && ar_peer_[g] && ar_ipc_[g]) cudaIpcCloseMemHandle(ar_peer_[g]);
         ar_peer_[g] = nullptr;
+        ar_ipc_[g] = false;
     }
     barrier();
     dfree(ar_buf_);
@@ -695,6 +728,7 @@ void Model::finish_open()
     if (!rope_table_) build_rope_table(nullptr, 0);
     build_maps();
     own_ = new_seq();
+    opened_ = true;
 }
 
 Model::~Model()

@@ -92,6 +92,9 @@ public:
     int tp_size() const { return tp_size_; }
     int tp_rank() const { return tp_rank_; }
     bool tp_fused() const { return ar_on_; }
+    // This shard leaves its group without the collectives of an orderly close (its peers are gone or leave the same
+    // way, and no step has run): used when a group fails to open.
+    void detach_group() { opened_ = false; }
     int max_context() const { return max_context_; }
     const Stats& stats() const { return stats_; }
     int64_t graph_launches() const { return graph_launches_; }
@@ -181,6 +184,7 @@ private:
     // the fused all-reduce (k::ArOut / k::ArIn): this rank's buffer and every peer's, mapped through CUDA IPC
     uint8_t* ar_buf_ = nullptr;
     uint8_t* ar_peer_[k::AR_MAX_RANKS] = {};
+    bool ar_ipc_[k::AR_MAX_RANKS] = {};   // mapped through CUDA IPC (another process), else a pointer in this one
     bool ar_on_ = false;
     int ar_idx_ = 0;                      // fused all-reduces enqueued so far in the current step
     int pending_ar_ = -1;                 // index of the all-reduce whose sum the next norm consumes, or -1
@@ -210,6 +214,7 @@ private:
         int64_t bytes = 0;
     };
     bool streamed_ = false;
+    bool opened_ = false;                 // open completed: closing meets the other ranks in collectives
     std::vector<Stage> stages_;
     int cur_stage_ = -1;                  // the stage being loaded (-1: resident weights)
     uint8_t* staging_ = nullptr;
