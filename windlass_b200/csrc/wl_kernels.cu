@@ -885,7 +885,12 @@ __global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const fl
 #pragma unroll
         for (int s2 = 0; s2 < GR; ++s2) M = fmaxf(M, mls[s2].x);
     }
-    double L = 0.0, o0 = 0.0, o1 = 0.0, o2 = 0.0, o3 = 0.0;
+    // with more than 16 ranges, NA interleaved accumulator sets (range s into set s % NA) shorten the dependent
+    // chains of double adds; the sets are added in set order, so the result stays fixed for a given S
+    constexpr int NA = S > 16 ? 4 : 1;
+    double L[NA], o0[NA], o1[NA], o2[NA], o3[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) L[a] = o0[a] = o1[a] = o2[a] = o3[a] = 0.0;
 #pragma unroll
     for (int g0 = 0; g0 < S; g0 += GR) {
         float2 mls[GR];
@@ -897,15 +902,24 @@ __global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const fl
         }
 #pragma unroll
         for (int s2 = 0; s2 < GR; ++s2) {
+            const int a = s2 % NA;
             const double w = mls[s2].y > 0.f ? (double)expf(mls[s2].x - M) : 0.0;
-            L += w * (double)mls[s2].y;
-            o0 += w * (double)ps[s2].x;
-            o1 += w * (double)ps[s2].y;
-            o2 += w * (double)ps[s2].z;
-            o3 += w * (double)ps[s2].w;
+            L[a] += w * (double)mls[s2].y;
+            o0[a] += w * (double)ps[s2].x;
+            o1[a] += w * (double)ps[s2].y;
+            o2[a] += w * (double)ps[s2].z;
+            o3[a] += w * (double)ps[s2].w;
         }
     }
-    const float f[4] = {(float)(o0 / L), (float)(o1 / L), (float)(o2 / L), (float)(o3 / L)};
+#pragma unroll
+    for (int a = 1; a < NA; ++a) {
+        L[0] += L[a];
+        o0[0] += o0[a];
+        o1[0] += o1[a];
+        o2[0] += o2[a];
+        o3[0] += o3[a];
+    }
+    const float f[4] = {(float)(o0[0] / L[0]), (float)(o1[0] / L[0]), (float)(o2[0] / L[0]), (float)(o3[0] / L[0])};
     *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
     if (prep) xprep_sb(f, tid, scratch, prep + ((int64_t)t * (QD / 256) + sb) * XP_COL);
 }
