@@ -152,16 +152,17 @@ def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
         wl.check(L.wl_tiles_size(O.TYPE_OF["q8_0"], rows, cols, C.byref(nb)))
 
 
+@pytest.mark.parametrize("tname", ["q4_K", "q6_K"])
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 9), (100, 512, 64), (300, 1024, 65), (16, 256, 130),
                                           (2048, 2048, 200)])
-def test_tcgen05_gemm_matches_reference(wl, oracle, rows, cols, T):
-    """T > 8 rows of Q4_K run on the tcgen05 GEMM (bf16 hi/lo planes, fp32 accumulation in tensor memory): within
-    1e-4 relative L2 of the decoded weights' float64 products, like the matvec, on ragged row counts (not multiples
-    of the 128-row tile or of 16), token counts around the 64-token tile, and against the integer tensor-core matvec
-    in 8-column chunks (path 2)."""
+def test_tcgen05_gemm_matches_reference(wl, oracle, tname, rows, cols, T):
+    """T > 8 rows of Q4_K or Q6_K run on the tcgen05 GEMM (bf16 hi/lo planes, fp32 accumulation in tensor memory):
+    within 1e-4 relative L2 of the decoded weights' float64 products, like the matvec, on ragged row counts (not
+    multiples of the 128-row tile or of 16), token counts around the 128-token tile, and against the integer
+    tensor-core matvec in 8-column chunks (path 2)."""
     O = oracle
-    t = O.TYPE_OF["q4_K"]
-    w = weights(O, "q4_K", rows, cols, seed=rows + T)
+    t = O.TYPE_OF[tname]
+    w = weights(O, tname, rows, cols, seed=rows + T)
     dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
     x = np.random.default_rng(T).standard_normal((T, cols)).astype(np.float32)
     dw, dx = dev(w), dev(x.reshape(-1))

@@ -35,17 +35,30 @@ namespace {
 constexpr int G_BM = 128;                  // weight rows per CTA (MMA M)
 constexpr int G_BN = 128;                  // tokens per CTA (MMA N)
 constexpr int G_BK = 64;                   // values per K step: one 128-byte swizzle atom of bf16
-constexpr int G_STAGES = 3;
-constexpr int G_RAW_STAGES = 4;
 constexpr int G_A_BYTES = G_BM * G_BK * 2;             // one bf16 plane of the weight tile: 16 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;             // one bf16 plane of the token tile: 16 KB
 constexpr int G_STAGE = 2 * G_A_BYTES + 2 * G_B_BYTES; // 64 KB
-constexpr int G_RAW_TILE = 256 + 512;                   // a 16-row tile's headers and one K step's code bytes
-constexpr int G_RAW_STAGE = (G_BM / 16) * G_RAW_TILE;   // 6 KB
 constexpr int G_DQ_WARPS = 8, G_TMA_WARP = 8, G_RAW_WARP = 9, G_MMA_WARP = 10, G_THREADS = 352;
-constexpr int G_SMEM = G_STAGES * G_STAGE + G_RAW_STAGES * G_RAW_STAGE + 1024;   // + alignment slack (1024 B atoms)
 constexpr int G_TMEM_COLS = 128;
 constexpr int Q4T = 2304;                               // bytes of a 16-row x one-superblock Q4_K tile
+constexpr int Q6T = 3360;                               // bytes of a 16-row x one-superblock Q6_K tile
+
+// Per weight format: the A/B ring depth and the raw ring. Q4_K stages one K step of each 16-row tile at a time (its
+// 256 header bytes and the step's 512 code bytes); Q6_K stages whole tiles (one superblock = four K steps), its
+// quarter-superblock bytes being interleaved across the tile for the matvec's fragment reads.
+template <int WT> struct GemmFmt;
+template <> struct GemmFmt<12> {
+    static constexpr int STAGES = 3, RAW_STAGES = 4, STEPS_PER_RAW = 1;
+    static constexpr int RAW_TILE = 256 + 512, TILE = Q4T;
+    static constexpr int RAW_STAGE = (G_BM / 16) * RAW_TILE;                          // 6 KB
+    static constexpr int SMEM = STAGES * G_STAGE + RAW_STAGES * RAW_STAGE + 1024;     // + 1024-byte alignment slack
+};
+template <> struct GemmFmt<14> {
+    static constexpr int STAGES = 2, RAW_STAGES = 2, STEPS_PER_RAW = 4;
+    static constexpr int RAW_TILE = Q6T, TILE = Q6T;
+    static constexpr int RAW_STAGE = (G_BM / 16) * RAW_TILE;                          // 26.25 KB
+    static constexpr int SMEM = STAGES * G_STAGE + RAW_STAGES * RAW_STAGE + 1024;
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -157,11 +170,15 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
     lo = (uint32_t)__bfloat16_as_ushort(al) | ((uint32_t)__bfloat16_as_ushort(bl) << 16);
 }
 
-__global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap xh_map,
+template <int WT>
+__global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ CUtensorMap xh_map,
                                                             const __grid_constant__ CUtensorMap xl_map,
                                                             const uint8_t* __restrict__ tiles, int row_base, int rows,
                                                             int nsb, int T, float* __restrict__ y, int64_t ldy, int* err)
 {
+    using F = GemmFmt<WT>;
+    constexpr int G_STAGES = F::STAGES, G_RAW_STAGES = F::RAW_STAGES, G_RAW_STAGE = F::RAW_STAGE;
+    constexpr int SPR = F::STEPS_PER_RAW;
     extern __shared__ uint8_t g_smem_raw[];
     __shared__ __align__(8) uint64_t full_a[G_STAGES], full_b[G_STAGES], empty[G_STAGES], acc_full;
     __shared__ __align__(8) uint64_t raw_full[G_RAW_STAGES], raw_empty[G_RAW_STAGES];
@@ -200,29 +217,31 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
     const uint32_t tmem = tmem_base;
 
     if (warp < G_DQ_WARPS) {
-        // ---- dequantizers: thread -> (row m, half h); per K step the row's 32-value sub-block 2p+h of superblock sb
+        // ---- dequantizers: thread -> (row m, half h); per K step 32 values of the row: 32h .. 32h+31
         const int t = threadIdx.x, m = t >> 1, h = t & 1;
         const bool live = (m >> 4) < live_tiles;
-        const int r16 = m & 15, hdr = (m >> 4) * G_RAW_TILE + r16 * 16;
-        const int code = (m >> 4) * G_RAW_TILE + 256 + ((r16 & 7) * 4) * 16 + (r16 >> 3) * 8;
+        const int r16 = m & 15, tile_off = (m >> 4) * F::RAW_TILE;
         const int swz = m & 7;
         uint8_t* arow = smem + (m >> 3) * 1024 + swz * 128;
         for (int i = 0; i < nk; ++i) {
-            const int s = i % G_STAGES, rs = i % G_RAW_STAGES;
+            const int s = i % G_STAGES, rstep = i / SPR, rs = rstep % G_RAW_STAGES;
             const int p = i & 3;
             uint32_t hi[16], lo[16];
-            mbar_wait(&raw_full[rs], (uint32_t)((i / G_RAW_STAGES) & 1), err, 16, &abort_flag);
-            uint4 hv = make_uint4(0u, 0u, 0u, 0u);
-            uint2 cv[4] = {};
-            if (live) {
-                const uint8_t* rb = raw + rs * G_RAW_STAGE;
-                hv = *reinterpret_cast<const uint4*>(rb + hdr);
+            if (i % SPR == 0) mbar_wait(&raw_full[rs], (uint32_t)((rstep / G_RAW_STAGES) & 1), err, 16, &abort_flag);
+            const uint8_t* rb = raw + rs * G_RAW_STAGE + tile_off;
+            float wv[32];
+            if (WT == 12) {
+                // Q4_K (src/Quants.cs:333-350): the step's run of the row holds values 64p .. 64p+63; this thread's
+                // 32 are sub-block 2p+h (low nibbles for h = 0, high for h = 1) of code bytes 32p .. 32p+31
+                uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+                uint2 cv[4] = {};
+                if (live) {
+                    hv = *reinterpret_cast<const uint4*>(rb + r16 * 16);
+                    const int code = 256 + ((r16 & 7) * 4) * 16 + (r16 >> 3) * 8;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) cv[c] = *reinterpret_cast<const uint2*>(rb + code + c * 16);
-            }
-            mbar_arrive(&raw_empty[rs]);    // the raw bytes are in registers: the slot may be refilled
-            if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 11, &abort_flag);
-            if (live) {
+                    for (int c = 0; c < 4; ++c) cv[c] = *reinterpret_cast<const uint2*>(rb + code + c * 16);
+                }
+                if (i % SPR == SPR - 1) mbar_arrive(&raw_empty[rs]);    // the bytes are in registers
                 // ScaleMinK4 (src/Quants.cs:322-330) of sub-block j = 2p + h; scale byte b is byte b & 3 of word
                 // hv.y / hv.z / hv.w for b in 0-3 / 4-7 / 8-11
                 const int j = 2 * p + h, sh8 = 8 * (j & 3);
@@ -237,19 +256,54 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
                 }
                 const float d1 = __fmul_rn(h2f(hv.x & 0xFFFF), (float)s6), mm1 = __fmul_rn(h2f(hv.x >> 16), (float)m6);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                    for (int q2 = 0; q2 < 4; ++q2) {
-                        const uint32_t word = q2 < 2 ? cv[c].x : cv[c].y;
-                        const int sh = (q2 & 1) * 16 + (h ? 4 : 0);
-                        const float w0 = __fsub_rn(__fmul_rn(d1, (float)((word >> sh) & 15)), mm1);
-                        const float w1 = __fsub_rn(__fmul_rn(d1, (float)((word >> (sh + 8)) & 15)), mm1);
-                        split2(w0, w1, hi[c * 4 + q2], lo[c * 4 + q2]);
+                    for (int b = 0; b < 8; ++b) {
+                        const uint32_t word = b < 4 ? cv[c].x : cv[c].y;
+                        const int q = (int)((word >> (8 * (b & 3) + (h ? 4 : 0))) & 15u);
+                        wv[c * 8 + b] = __fsub_rn(__fmul_rn(d1, (float)q), mm1);
                     }
-                }
             } else {
+                // Q6_K (src/Quants.cs:373-396): the step covers quarters 2(p&1), 2(p&1)+1 of half k = p/2; this
+                // thread's 32 values are quarter Q = 2(p&1) + h: value l (0..31) has the low code bits in nibble p&1
+                // of ql byte 64k + 32h + l, the high two in bits 2Q of qh byte 32k + l, the scale sc[8k + l/16 + 2Q].
+                // In the tile, ql byte 64k + 32kk + 16is + 4c + b of row r is at r*128 + c*32 + 4*((4k + 2kk + is)
+                // ^ 4(r&1)) + b, qh byte 32k + 16is + 4c + b at 2048 + r*64 + c*16 + 4*(2k + is) + b.
+                const int k = p >> 1, Q = 2 * (p & 1) + h;
+                uint32_t qlw[2][4] = {}, qhw[2][4] = {};
+                int sc0 = 0, sc1 = 0;
+                float d = 0.f;
+                if (live) {
 #pragma unroll
-                for (int q = 0; q < 16; ++q) hi[q] = lo[q] = 0u;
+                    for (int is = 0; is < 2; ++is)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            qlw[is][c] = *reinterpret_cast<const uint32_t*>(rb + r16 * 128 + c * 32 + 4 * ((4 * k + 2 * h + is) ^ ((r16 & 1) << 2)));
+                            qhw[is][c] = *reinterpret_cast<const uint32_t*>(rb + 2048 + r16 * 64 + c * 16 + 4 * (2 * k + is));
+                        }
+                    const int8_t* sc = reinterpret_cast<const int8_t*>(rb + 3072 + r16 * 16 + 8 * k + 2 * Q);
+                    sc0 = sc[0];
+                    sc1 = sc[1];
+                    d = h2f(*reinterpret_cast<const uint16_t*>(rb + 3328 + r16 * 2));
+                }
+                if (i % SPR == SPR - 1) mbar_arrive(&raw_empty[rs]);
+                const float ds[2] = {__fmul_rn(d, (float)sc0), __fmul_rn(d, (float)sc1)};
+#pragma unroll
+                for (int is = 0; is < 2; ++is)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int lo4 = (int)((qlw[is][c] >> (8 * b + 4 * (p & 1))) & 15u);
+                            const int hi2 = (int)((qhw[is][c] >> (8 * b + 2 * Q)) & 3u);
+                            wv[16 * is + 4 * c + b] = __fmul_rn(ds[is], (float)((lo4 | (hi2 << 4)) - 32));
+                        }
+            }
+            if (i >= G_STAGES) mbar_wait(&empty[s], (uint32_t)(((i / G_STAGES) + 1) & 1), err, 11, &abort_flag);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                if (live) split2(wv[2 * q], wv[2 * q + 1], hi[q], lo[q]);
+                else hi[q] = lo[q] = 0u;
             }
             // values 32h .. 32h+31 of the row: 16-byte chunks 4h .. 4h+3, swizzled by the row within its 8-row group
             uint8_t* ah = arow + (size_t)s * G_STAGE;
@@ -264,18 +318,25 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm_q4k(const __grid_constant
             mbar_arrive(&full_a[s]);
         }
     } else if (warp == G_RAW_WARP) {
-        // ---- raw weights: per K step and live 16-row tile, its headers and the step's 512 code bytes
+        // ---- raw weights into the raw ring: Q4_K per K step and live 16-row tile its headers and the step's 512
+        // code bytes; Q6_K per superblock the live tiles whole
         if (lane == 0) {
-            const uint8_t* t0 = tiles + ((int64_t)(row_base / 16 + m0 / 16) * nsb) * Q4T;
-            for (int i = 0; i < nk; ++i) {
-                const int rs = i % G_RAW_STAGES, sb = i >> 2, p = i & 3;
-                if (i >= G_RAW_STAGES) mbar_wait(&raw_empty[rs], (uint32_t)(((i / G_RAW_STAGES) + 1) & 1), err, 17, &abort_flag);
+            const uint8_t* t0 = tiles + ((int64_t)(row_base / 16 + m0 / 16) * nsb) * F::TILE;
+            const int nraw = nk / SPR;
+            for (int r = 0; r < nraw; ++r) {
+                const int rs = r % G_RAW_STAGES;
+                if (r >= G_RAW_STAGES) mbar_wait(&raw_empty[rs], (uint32_t)(((r / G_RAW_STAGES) + 1) & 1), err, 17, &abort_flag);
                 uint8_t* dst = raw + rs * G_RAW_STAGE;
-                mbar_expect_tx(&raw_full[rs], (uint32_t)(live_tiles * G_RAW_TILE));
+                mbar_expect_tx(&raw_full[rs], (uint32_t)(live_tiles * F::RAW_TILE));
                 for (int tt = 0; tt < live_tiles; ++tt) {
-                    const uint8_t* tb = t0 + ((int64_t)tt * nsb + sb) * Q4T;
-                    bulk_load(dst + tt * G_RAW_TILE, tb, 256, &raw_full[rs]);
-                    bulk_load(dst + tt * G_RAW_TILE + 256, tb + 256 + p * 512, 512, &raw_full[rs]);
+                    if (WT == 12) {
+                        const int sb = r >> 2, p = r & 3;
+                        const uint8_t* tb = t0 + ((int64_t)tt * nsb + sb) * F::TILE;
+                        bulk_load(dst + tt * F::RAW_TILE, tb, 256, &raw_full[rs]);
+                        bulk_load(dst + tt * F::RAW_TILE + 256, tb + 256 + p * 512, 512, &raw_full[rs]);
+                    } else {
+                        bulk_load(dst + tt * F::RAW_TILE, t0 + ((int64_t)tt * nsb + r) * F::TILE, F::TILE, &raw_full[rs]);
+                    }
                 }
             }
         }
@@ -388,14 +449,14 @@ CUtensorMap plane_map(const void* base, int T, int K)
 
 }  // namespace
 
-bool gemm_supported(int type, int cols) { return type == 12 && cols % 256 == 0; }
+bool gemm_supported(int type, int cols) { return (type == 12 || type == 14) && cols % 256 == 0; }
 
 size_t gemm_scratch_bytes(int T, int cols) { return (size_t)2 * T * cols * 2 + 256; }
 
 void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const float* x, int64_t ldx, int T,
                 float* y, int64_t ldy, void* scratch, int* err, cudaStream_t s)
 {
-    if (!gemm_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "gemm_tiles: Q4_K with cols a multiple of 256 only");
+    if (!gemm_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "gemm_tiles: Q4_K or Q6_K with cols a multiple of 256 only");
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "gemm_tiles: misaligned tiles");
     if (T <= 0 || rows <= 0) return;
     __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
@@ -410,14 +471,19 @@ void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_gemm_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_gemm<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<12>::SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_gemm<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<14>::SMEM));
         attr[dev] = true;
     }
     const dim3 grid((rows + G_BM - 1) / G_BM, (T + G_BN - 1) / G_BN);
     // A plain launch, and the kernel does not trigger its dependents: no other kernel overlaps a GEMM. With programmatic
     // dependent launch on both sides, consecutive GEMMs (each with its own activation-plane tensor maps) overlapped
     // and gave wrong sums now and then (1-3 % relative error in a 2-layer prefill, never with either side serialised).
-    k_gemm_q4k<<<grid, G_THREADS, G_SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    if (type == 12)
+        k_gemm<12><<<grid, G_THREADS, GemmFmt<12>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    else
+        k_gemm<14><<<grid, G_THREADS, GemmFmt<14>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    WL_CUDA(cudaGetLastError());
     note_launch();
 }
 
