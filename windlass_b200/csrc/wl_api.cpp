@@ -399,6 +399,17 @@ int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* to
     });
 }
 
+int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms)
+{
+    return guarded([&]() -> int32_t {
+        if (wait_ms <= 0 || wait_ms > 10000) return wl::fail(WL_EINVAL, "wl_selftest_allreduce_timeout: wait_ms must be 1..10000");
+        WL_CUDA(cudaSetDevice(device));
+        const int code = wl::k::selftest_ar_wait((long long)wait_ms * 1000000LL);
+        if (code == 2) return wl::fail(WL_ETIMEDOUT, "a device-side wait gave up (code 2): a tensor-parallel peer did not arrive");
+        return wl::fail(WL_ECUDA, "the all-reduce wait did not give up (code " + std::to_string(code) + ")");
+    });
+}
+
 int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream)
 {
     return guarded([&]() -> int32_t {

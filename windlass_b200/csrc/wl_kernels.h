@@ -40,7 +40,12 @@ struct ArIn {
     const unsigned long long* epoch;            // this rank's step counter
     int* err;                                   // set to 2 when a wait gives up
     int idx, G, rank, E, row0;                  // row0: first partial row the consumer's row 0 reads
+    long long wait_ns;                          // how long a wait for a peer may last before it gives up
 };
+constexpr long long AR_WAIT_NS = 10000000000LL; // 10 s: far beyond any skew between ranks that are running
+// Runs the fused all-reduce's consumer on this GPU against a peer that never announces (a flag nothing sets), with
+// its wait limited to wait_ns: returns the error code the kernel recorded (2 when the wait gave up, as it must).
+int selftest_ar_wait(long long wait_ns);
 
 // Copies the I-quant tables into the current device's constant memory (once per device).
 void init_tables();

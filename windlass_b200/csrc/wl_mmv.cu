@@ -116,6 +116,13 @@ __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned l
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* epoch, int idx)
 {
     return *epoch * (unsigned long long)AR_STEP + (unsigned long long)idx;
@@ -136,9 +143,12 @@ __device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q)
     }
     if (threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank) {
         const unsigned long long* f = ar.flags + slot * AR_MAX_RANKS + threadIdx.x;
+        const unsigned long long t0 = globaltimer_ns();
         for (uint32_t n = 0; ld_acquire_sys(f) < q; ++n) {
-            if (n >= (1u << 27)) { atomicExch(ar.err, 2); break; }
-            if (n >= 64) __nanosleep(256);
+            if (n >= 64) {
+                if ((long long)(globaltimer_ns() - t0) > ar.wait_ns) { atomicExch(ar.err, 2); break; }
+                __nanosleep(256);
+            }
         }
     }
     __syncthreads();
@@ -799,6 +809,49 @@ void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w,
         else launch(k_norm_prep<false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in);
     }
     note_launch();
+}
+
+int selftest_ar_wait(long long wait_ns)
+{
+    // one row of 256 values, the all-reduce of two ranks where this GPU is rank 0 and rank 1 never runs: rank 0's
+    // announcement lands in its own flags (it is its own "peer" here) and its wait for rank 1's announcement of the
+    // current sequence number (epoch 1, index 0) can only run out
+    const int E = 256;
+    const size_t arb = ar_buffer_bytes(E);
+    uint8_t* buf = nullptr;
+    float *x = nullptr, *w = nullptr, *y = nullptr;
+    int* err = nullptr;
+    int code = -1;
+    WL_CUDA(cudaMalloc(&buf, arb));
+    try {
+        WL_CUDA(cudaMalloc(&x, 3 * E * sizeof(float)));
+        w = x + E;
+        y = w + E;
+        WL_CUDA(cudaMalloc(&err, sizeof(int)));
+        WL_CUDA(cudaMemset(buf, 0, arb));
+        WL_CUDA(cudaMemset(x, 0, 3 * E * sizeof(float)));
+        WL_CUDA(cudaMemset(err, 0, sizeof(int)));
+        const unsigned long long epoch = 1;
+        WL_CUDA(cudaMemcpy(buf + AR_EPOCH, &epoch, sizeof epoch, cudaMemcpyHostToDevice));
+        ArIn in{};
+        for (int g = 0; g < 2; ++g) {
+            in.data[g] = reinterpret_cast<const float*>(buf + AR_HEADER);
+            in.peer_flags[g] = reinterpret_cast<unsigned long long*>(buf);
+        }
+        in.flags = reinterpret_cast<const unsigned long long*>(buf);
+        in.epoch = reinterpret_cast<const unsigned long long*>(buf + AR_EPOCH);
+        in.err = err;
+        in.idx = 0; in.G = 2; in.rank = 0; in.E = E; in.row0 = 0;
+        in.wait_ns = wait_ns;
+        norm_prep(x, nullptr, 1.0f, 1, E, w, 1e-5f, y, nullptr, 0, &in);
+        WL_CUDA(cudaDeviceSynchronize());
+        WL_CUDA(cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost));
+    } catch (...) {
+        cudaFree(buf); if (x) cudaFree(x); if (err) cudaFree(err);
+        throw;
+    }
+    cudaFree(buf); cudaFree(x); cudaFree(err);
+    return code;
 }
 
 XPrep xprep_view(void* scratch, int cols, int nc)

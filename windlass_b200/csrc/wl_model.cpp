@@ -226,6 +226,7 @@ bool Model::pending_ar_in(int T, int row0, k::ArIn* in)
     in->rank = tp_rank_;
     in->E = c_.embd;
     in->row0 = row0;
+    in->wait_ns = k::AR_WAIT_NS;
     pending_ar_ = -1;
     return true;
 }
