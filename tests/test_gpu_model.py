@@ -260,3 +260,31 @@ def test_repeated_prompts_are_deterministic(wl):
             assert np.array_equal(o, outs[0]), f"prefill {i} differs from the first"
         rel = float(np.linalg.norm(outs[0] - want) / np.linalg.norm(want))
         assert rel <= 1e-4, rel
+
+
+def test_moe_decode_steps_on_the_device(wl):
+    """Decode steps of a mixture-of-experts model keep the router's choice on the device (one grouped matvec launch
+    per projection over every token-expert pair, CUDA graphs allowed). Each step's logits are bit for bit those of
+    the same positions in a prompt run through the host-grouped path (prefill_path 2: every column as if alone), for
+    single steps and ForwardBatch, and ExpertRuns counts the distinct experts each step runs."""
+    from windlass_b200.transformer import synth_spec
+    spec = synth_spec("qwen3moe", 2, 512, 8, 4, 64, 0, 4096, experts=16, experts_used=4, expert_ff=256,
+                      rope_base=1000000.0, type_attn_v=14, type_embd=12, seed=11)
+    toks = np.random.default_rng(4).integers(0, spec.vocab, 12).astype(np.int32)
+    with CudaTransformer(synthetic=spec, max_context=64, prefill_path=2) as host_path, \
+            CudaTransformer(synthetic=spec, max_context=64) as dev_path:
+        want = host_path.forward(toks, all_logits=True)
+        for i, t in enumerate(toks):
+            before = dev_path.expert_runs
+            got = dev_path.forward([int(t)], pos0=i)
+            assert np.array_equal(got, want[i]), f"decode step {i} differs from the host-grouped path"
+            assert dev_path.expert_runs - before == 2 * 4          # 2 layers x 4 distinct experts for one token
+        s = [dev_path.new_sequence() for _ in range(3)]
+        for k in range(3):
+            dev_path.forward(toks[: 4 + k], seq=s[k])
+        batch = dev_path.forward_batch(s, [toks[4], toks[5], toks[6]])
+        ref = host_path.new_sequence()
+        for k in range(3):
+            ref.truncate(0)
+            row = host_path.forward(np.append(toks[: 4 + k], toks[4 + k]).astype(np.int32), seq=ref, all_logits=True)[-1]
+            assert np.array_equal(batch[k], row), f"batch row {k} differs"

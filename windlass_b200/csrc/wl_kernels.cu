@@ -1145,6 +1145,63 @@ void scatter_add(float* outp, const float* ye, const int32_t* toks, const float*
     launched();
 }
 
+__global__ void k_moe_combine(const float* __restrict__ y, const int32_t* __restrict__ sel, const float* __restrict__ wts,
+                              int K, int E, float* __restrict__ out)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y;
+    // token t's experts in ascending id order (the order the reference's per-expert loop adds them)
+    int order[16];
+    for (int j = 0; j < K; ++j) order[j] = j;
+    for (int a = 1; a < K; ++a)
+        for (int b = a; b > 0 && sel[t * K + order[b]] < sel[t * K + order[b - 1]]; --b) {
+            const int tmp = order[b]; order[b] = order[b - 1]; order[b - 1] = tmp;
+        }
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < E; d += gridDim.x * blockDim.x) {
+        float o = 0.0f;
+        for (int j = 0; j < K; ++j) {
+            const int i = t * K + order[j];
+            o = __fadd_rn(o, __fmul_rn(wts[i], y[(int64_t)i * E + d]));
+        }
+        out[(int64_t)t * E + d] = o;
+    }
+}
+
+void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s)
+{
+    if (T <= 0) return;
+    if (K < 1 || K > 16) WL_THROW(WL_EINVAL, "moe_combine: 1..16 experts per token");
+    launch(k_moe_combine, dim3(grid_for(E, 256), T), dim3(256), 0, s, y, sel, wts, K, E, out);
+    launched();
+}
+
+__global__ void k_count_experts(const int32_t* __restrict__ sel, int n, unsigned long long* count)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned int seen[8];
+    if (threadIdx.x < 8) seen[threadIdx.x] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = sel[i];
+        if (e >= 0 && e < 256) atomicOr(&seen[e >> 5], 1u << (e & 31));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long c = 0;
+        for (int w = 0; w < 8; ++w) c += (unsigned long long)__popc(seen[w]);
+        *count += c;
+    }
+}
+
+void count_experts(const int32_t* sel, int n, unsigned long long* count, cudaStream_t s)
+{
+    if (n <= 0) return;
+    launch(k_count_experts, dim3(1), dim3(128), 0, s, sel, n, count);
+    launched();
+}
+
 __global__ void k_shared_expert_add(float* outp, const float* __restrict__ sh, const float* __restrict__ gl, int E)
 {
     pdl_trigger();

@@ -121,6 +121,18 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
                    int row_base_b, int rows_b, float* y_b, int64_t ldy_b, int cols, const XPrep& p, int* err,
                    cudaStream_t s);
 
+// The mixture-of-experts grouped matvec (Q4_K experts, one activation column per pair): for every pair i < npairs
+// (token i / K and its expert sel[i], read on the device), y[i*ldy + r] = E_sel[i][r] . x[col] for the expert's
+// expert_rows rows (expert e's rows start at row_base + e * expert_rows of the tiles), col = i / K when x_per_token
+// else i. Each pair's result is the one a matvec of that expert alone gives.
+void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
+                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s);
+// MoeFfn's weighted sum (src/Transformer.cs:289-293) from the pairs' outputs: out[t] = sum over token t's K experts in
+// ascending expert order of wts[t*K+j] * y[(t*K+j)*E ...], each step a separately rounded multiply and add from 0.
+void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s);
+// Adds to *count the number of distinct experts among sel[0 .. n) (Transformer.ExpertRuns, src/Transformer.cs:287).
+void count_experts(const int32_t* sel, int n, unsigned long long* count, cudaStream_t s);
+
 // Q4_K GEMM on the tcgen05 tensor cores for T > 8 activation rows (prefill, large batches): y[t*ldy + r] =
 // W[row_base + r] . x[t*ldx ...] from the tile-major weights, with fp32-level accuracy (bf16 hi/lo planes of both
 // operands, three MMAs per slice, fp32 accumulation in tensor memory). scratch holds gemm_scratch_bytes(T, cols) bytes

@@ -309,6 +309,12 @@ struct MvSeg {
     int first_ctas;             // CTAs of the first matrix; INT_MAX: one matrix
     float* y;
     int64_t ldy;
+    // pair mode (sel != nullptr): the mixture-of-experts grouped matvec. CTA b serves pair b / tiles_per_pair (a
+    // token and one of its K chosen experts) and that expert's row tile b % tiles_per_pair; the expert id is
+    // sel[pair] (written by the router kernel), its rows start at row_base + id * rows, the activations are column
+    // pair / K (x_per_token) or column pair of the prepared input, and the output row is y + pair * ldy.
+    const int32_t* sel;
+    int K, tiles_per_pair, x_per_token;
 };
 
 __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -342,12 +348,22 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     // two matrices with the same input in one launch: CTAs past the first matrix's row tiles take the second's
-    const bool second = TILED && (int)blockIdx.x >= seg.first_ctas;
-    const int bx = second ? (int)blockIdx.x - seg.first_ctas : (int)blockIdx.x;
+    const bool second = TILED && !seg.sel && (int)blockIdx.x >= seg.first_ctas;
+    int bx = second ? (int)blockIdx.x - seg.first_ctas : (int)blockIdx.x;
     const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
-    const int row_base = second ? seg.row_base : row_base_a, rows = second ? seg.rows : rows_a;
+    int row_base = second ? seg.row_base : row_base_a;
+    const int rows = second ? seg.rows : rows_a;
     float* __restrict__ y = second ? seg.y : y_a;
     const int64_t ldy = second ? seg.ldy : ldy_a;
+    if (TILED && seg.sel) {
+        // grouped experts: the expert ids come from the router kernel, so wait for it before the first weight copy
+        pdl_wait();
+        const int pair = (int)blockIdx.x / seg.tiles_per_pair;
+        bx = (int)blockIdx.x % seg.tiles_per_pair;
+        row_base = row_base_a + seg.sel[pair] * rows_a;
+        xq += (int64_t)(seg.x_per_token ? pair / seg.K : pair) * nsb * XP_COL;
+        y = y_a + (int64_t)pair * ldy_a;
+    }
     const int r0 = bx * Q4_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
     const int njobs = nsb > warp ? (nsb - warp + 7) / 8 : 0;
@@ -916,7 +932,8 @@ static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base,
         WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
         attr[dev] = true;
     }
-    const int ctas = (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
+    const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas
+                             : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     launch(k_mmv_q4k<NC, TILED>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
            (const uint8_t*)p.blocks, y, ldy, err, seg);
     note_launch();
@@ -943,7 +960,7 @@ void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols
 {
     (void)type;
     dispatch_q4k<false>(*reinterpret_cast<const CUtensorMap*>(map.bytes), nullptr, row_base, rows, cols / 256, p, y,
-                        ldy, err, s, MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0});
+                        ldy, err, s, MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0});
 }
 
 
@@ -1006,8 +1023,24 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
     if (!tiles_supported(12, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles2: Q4_K with cols a multiple of 256 only");
     CUtensorMap none;
     memset(&none, 0, sizeof none);
-    const MvSeg seg{tiles_b, row_base_b, rows_b, (rows_a + Q4_ROWS - 1) / Q4_ROWS, y_b, ldy_b};
+    const MvSeg seg{tiles_b, row_base_b, rows_b, (rows_a + Q4_ROWS - 1) / Q4_ROWS, y_b, ldy_b, nullptr, 0, 1, 0};
     dispatch_q4k<true>(none, tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, err, s, seg);
+}
+
+void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
+                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s)
+{
+    if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0 || expert_rows % 16 != 0)
+        WL_THROW(WL_EINVAL, "matvec_pairs: experts must start on 16-row tiles");
+    if (!tiles_supported(12, cols) || p.cols != cols) WL_THROW(WL_EUNSUPPORTED, "matvec_pairs: Q4_K with matching activations only");
+    if (npairs <= 0) return;
+    if (x_per_token ? (npairs + K - 1) / K > p.nc : npairs > p.nc) WL_THROW(WL_EINVAL, "matvec_pairs: too few activation columns");
+    CUtensorMap none;
+    memset(&none, 0, sizeof none);
+    const int tiles_per_pair = expert_rows / Q4_ROWS;
+    // first_ctas carries the pair count (the CTA count is pairs x tiles per pair)
+    const MvSeg seg{nullptr, 0, 0, npairs, nullptr, 0, sel, K, tiles_per_pair, x_per_token ? 1 : 0};
+    launch_q4k<1, true>(none, tiles, row_base, expert_rows, cols / 256, p, y, ldy, err, s, seg);
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
@@ -1019,7 +1052,7 @@ void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int co
         CUtensorMap none;
         memset(&none, 0, sizeof none);
         dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
-                           MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0});
+                           MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0});
     } else {
         matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }

@@ -753,6 +753,8 @@ Model::~Model()
     }
     free_streaming();
     dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
+    dfree(pg_); dfree(pu_); dfree(py_); dfree(expert_count_d_);
+    if (pprep_) cudaFree(pprep_);
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
@@ -1012,11 +1014,23 @@ void Model::build_maps()
         err_d_ = dalloc<int>(1);
         WL_CUDA(cudaMemset(err_d_, 0, sizeof(int)));
     }
+    if (c_.expert_count > 0 && !expert_count_d_) {
+        expert_count_d_ = dalloc<unsigned long long>(1);
+        WL_CUDA(cudaMemset(expert_count_d_, 0, sizeof(unsigned long long)));
+    }
 }
 
 // A bounded device wait that gave up leaves a code in err_d_; report it once the stream is idle.
 void Model::check_device_error()
 {
+    if (expert_count_d_) {
+        unsigned long long n = 0;
+        WL_CUDA(cudaMemcpy(&n, expert_count_d_, sizeof n, cudaMemcpyDeviceToHost));
+        if (n) {
+            stats_.expert_runs += (int64_t)n;
+            WL_CUDA(cudaMemset(expert_count_d_, 0, sizeof n));
+        }
+    }
     int e = 0;
     WL_CUDA(cudaMemcpy(&e, err_d_, sizeof(int), cudaMemcpyDeviceToHost));
     if (e != 0) {
@@ -1040,6 +1054,53 @@ void Model::ffn_dense(const LayerW& L, int T)
     }
     profile_end(sm, WL_PROFILE_SWIGLU, 0.0);
     matmul_reduce(L.down, g_, T);
+}
+
+// Decode steps of a mixture-of-experts layer stay on the device when the experts are tiled Q4_K (whole 16-row tiles
+// per expert) and there is no shared expert: the router's choice never goes to the host, so the step can also be a
+// CUDA graph.
+bool Model::moe_on_device(const LayerW& L, int T) const
+{
+    const Weight &g = L.gate_exps, &u = L.up_exps, &d = L.down_exps;
+    return L.moe && T <= 8 && !L.sh_gate.present() && xprep_buf_ && g.tiles && u.tiles && d.tiles && g.type == 12 &&
+           u.type == 12 && d.type == 12 && g.rows % 16 == 0 && d.rows % 16 == 0 && g.cols == c_.embd &&
+           d.cols == g.rows && g.row_base == 0 && u.row_base == 0 && d.row_base == 0;
+}
+
+// MoeFfn on the device: router matvec, top-k (k_route), then one grouped matvec launch each for gate, up and down over
+// every (token, chosen expert) pair, the experts' ids read on the device, and the weighted sum per token in
+// ascending expert order, the order the reference adds them (src/Transformer.cs:280-293). Each pair's expert output
+// is the bits the host path's per-expert matvec gives, so the result is too.
+void Model::ffn_moe_device(const LayerW& L, int T)
+{
+    const int E = c_.embd, K = c_.expert_used, X = L.gate_exps.rows, NP = T * K;
+    if (NP > pair_cap_) {
+        WL_CUDA(cudaStreamSynchronize(stream_));
+        dfree(pg_); dfree(pu_); dfree(py_);
+        if (pprep_) cudaFree(pprep_);
+        pprep_ = nullptr;
+        const int cap = 8 * K;
+        pg_ = dalloc<float>((int64_t)cap * X);
+        pu_ = dalloc<float>((int64_t)cap * X);
+        py_ = dalloc<float>((int64_t)cap * E);
+        WL_CUDA(cudaMalloc(&pprep_, k::xprep_bytes(X, cap)));
+        pair_cap_ = cap;
+        ws_gen_++;
+        drop_graphs();
+    }
+    const k::XPrep px = k::xprep_view(xprep_buf_, E, T);        // xn_, prepared by the ffn norm
+    matmul(L.router, xn_, T, router_);
+    k::route(router_, T, c_.expert_count, K, c_.expert_weights_norm ? 1 : 0, sel_, wts_, stream_);
+    k::count_experts(sel_, NP, expert_count_d_, stream_);
+    const int mark = profile_begin();
+    k::matvec_pairs(L.gate_exps.tiles, 0, X, E, sel_, NP, K, true, px, pg_, X, err_d_, stream_);
+    k::matvec_pairs(L.up_exps.tiles, 0, X, E, sel_, NP, K, true, px, pu_, X, err_d_, stream_);
+    const k::XPrep pp = k::xprep_view(pprep_, X, NP);
+    k::swiglu_prep(pg_, pu_, NP, X, pp, stream_);
+    k::matvec_pairs(L.down_exps.tiles, 0, E, X, sel_, NP, K, false, pp, py_, E, err_d_, stream_);
+    profile_end(mark, 12, (double)NP * ((double)L.gate_exps.row_bytes * X * 2 + (double)L.down_exps.row_bytes * E));
+    k::moe_combine(py_, sel_, wts_, T, K, E, o_, stream_);
+    prep_x_ = nullptr;
 }
 
 // MoeFfn (src/Transformer.cs:259-311): router, top-k, then each chosen expert runs once on the rows routed to it, in
@@ -1139,10 +1200,14 @@ void Model::layer(int l, int T, int max_n)
         prep_x_ = nullptr;
     } else {
         pending_residual_ = true;           // x += o happens inside the ffn norm
-        pre_norm(T, L.ffn_norm, L.moe ? false : L.gate.tiles != nullptr);
+        pre_norm(T, L.ffn_norm, L.moe ? moe_on_device(L, T) : L.gate.tiles != nullptr);
     }
-    if (L.moe) ffn_moe(L, T);
-    else ffn_dense(L, T);
+    if (L.moe) {
+        if (moe_on_device(L, T)) ffn_moe_device(L, T);
+        else ffn_moe(L, T);
+    } else {
+        ffn_dense(L, T);
+    }
     if (c_.post_norms) {
         k::rmsnorm(o_, T, E, L.post_ffw_norm.d, c_.rms_eps, o_, stream_);
         k::residual(x_, o_, rs, n, stream_);
@@ -1285,7 +1350,10 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
 // ---------------------------------------------------------------------------------------------------------------------
 bool Model::graphable(int T) const
 {
-    return use_graphs_ && !profiling_ && !streamed_ && c_.expert_count == 0 && T <= 8;
+    if (!use_graphs_ || profiling_ || streamed_ || T > 8) return false;
+    for (const LayerW& L : L_)
+        if (L.moe && !moe_on_device(L, T)) return false;   // the host-side expert grouping syncs
+    return true;
 }
 
 // True when a graph for (T, first) exists or could be captured now (after one eager run of that shape).

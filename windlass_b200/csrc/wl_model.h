@@ -166,6 +166,8 @@ private:
     void pre_norm(int T, const Vec& w, bool prep_for_mma);
     void ffn_dense(const LayerW& L, int T);
     void ffn_moe(const LayerW& L, int T);
+    bool moe_on_device(const LayerW& L, int T) const;
+    void ffn_moe_device(const LayerW& L, int T);
     void head(int T, int first);
     int32_t run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
                 int first_logit_row, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
@@ -248,6 +250,12 @@ private:
     float* h_ew_ = nullptr;
     int h_cap_ = 0;
     // activations prepared for the tensor-core matvec (k::xprep), and what they were prepared from
+    // the device-side mixture-of-experts path of decode steps: per (token, chosen expert) pair its gate, up and
+    // down outputs, the prepared SwiGLU outputs, and a device count of the experts run
+    float *pg_ = nullptr, *pu_ = nullptr, *py_ = nullptr;
+    void* pprep_ = nullptr;
+    int pair_cap_ = 0;
+    unsigned long long* expert_count_d_ = nullptr;
     void* gemm_buf_ = nullptr;          // the tcgen05 GEMM's activation planes
     size_t gemm_buf_bytes_ = 0;
     void* xprep_buf_ = nullptr;
