@@ -256,7 +256,7 @@ def streamed(args):
         best = min(best, e0.elapsed_time(e1))
     h2d_gbs = (1 << 30) / (best / 1e3) / 1e9
     del src, dst
-    spec = llama70b_spec(layers=args.layers)
+    spec = llama70b_spec(layers=args.layers or 80)
     t0 = time.perf_counter()
     trace(f"opening the streamed model ({args.layers} layers)")
     m = CudaTransformer(synthetic=spec, max_context=args.prompt + 64, resident=0)
@@ -299,7 +299,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--prompt", type=int, default=1024)
-    ap.add_argument("--layers", type=int, default=80)
+    ap.add_argument("--layers", type=int, default=0, help="decoder layers (0: the configuration's own count)")
     ap.add_argument("--impl", default="windlass", choices=["windlass", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--tp-nccl-only", action="store_true", help="all-reduce with NCCL only (no fused peer-memory path)")
@@ -309,6 +309,8 @@ def main():
     ap.add_argument("--batches", default="1,4,8,64")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--streamed", action="store_true", help="configs[3] (a): layers streamed from pinned host memory")
+    ap.add_argument("--model", default="70b", choices=["70b", "8b", "moe"],
+                    help="70b: configs[3] (the headline); 8b: configs[2]; moe: configs[4] (Qwen3-MoE shape)")
     ap.add_argument("--shard-of", type=int, default=0,
                     help="one GPU runs the shapes one rank holds under tensor parallelism over N GPUs (no exchange)")
     ap.add_argument("--profile-range", action="store_true",
@@ -342,8 +344,18 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    from windlass_b200.transformer import llama70b_spec, synth_spec
-    spec = llama70b_spec(layers=args.layers)
+    from windlass_b200.transformer import llama70b_spec, llama8b_spec, qwen3moe_spec, synth_spec
+    if args.model == "8b":
+        spec = llama8b_spec()
+        if args.layers:
+            spec.layers = args.layers
+    elif args.model == "moe":
+        spec = qwen3moe_spec(layers=args.layers or 48)
+    else:
+        spec = llama70b_spec(layers=args.layers or 80)
+    args.layers = spec.layers
+    names = {"70b": "Llama-3.3-70B-shaped Q4_K_M (configs[3] b)", "8b": "Llama-3-8B-shaped Q4_K_M (configs[2])",
+             "moe": "Qwen3-MoE-shaped, 128 experts top-8 (configs[4])"}
     if args.shard_of > 1:
         g = args.shard_of
         spec = synth_spec("llama", args.layers, 8192, 64 // g, 8 // g, 128, 28672 // g, 128256 // g, 8192,
@@ -429,7 +441,7 @@ def main():
 
     trace("profiled pass done")
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and args.model == "70b" and not args.shard_of:
         cpu = cpu_baseline()
     trace("cpu baseline done")
     if rank == 0:
@@ -439,10 +451,11 @@ def main():
                 "config": {"workload": (f"decode b{B}, one TP{args.shard_of} rank's shard of the Llama-3.3-70B-shaped "
                                         f"Q4_K_M decoder on one GPU (no exchange), {args.layers} layers")
                            if args.shard_of > 1 else
-                           f"decode b{B}, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), HBM-resident, "
-                           f"{args.layers} layers", "batch": B, "prompt": args.prompt,
+                           f"decode b{B}, {names[args.model]}, HBM-resident, {args.layers} layers",
+                           "batch": B, "prompt": args.prompt,
                            "parallelism": f"tp{world}, all-reduce x2 per layer: {allreduce}" if world > 1 else "1 GPU",
-                           "l2": "inputs larger than L2 (39.5 GB of weights read per step)"},
+                           "l2": "inputs larger than L2 (each step reads the layers' weights: 39.5 GB at 70B, 4.4 GB at 8B, "
+                                 "1.8 GB or more for the MoE)"},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                         "d2h_bytes_per_step": 4 * B * spec.vocab},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
