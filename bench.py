@@ -10,7 +10,9 @@ per step, which is far larger than the 126 MB L2, so no flush is needed between 
   stream, max over ranks. With N GPUs (torchrun, one process per GPU) the one model is split over the N GPUs by
   tensor parallelism (rows of q/k/v, gate/up and the head; columns of o and down; two NCCL all-reduces per layer
   over NVLink), so the work per step is fixed and N only shortens it (scaling "strong").
-- e2e: the same steps through the public call a host makes (wl_forward with host token ids in and host logits out).
+- e2e: the same steps through the public call a greedy host makes (wl_forward_argmax / wl_forward_batch_argmax:
+  host token ids in, each row's greedy id back, fed to the next step), with the logits-returning wl_forward and the
+  device-chained wl_generate_greedy beside it.
 - roofline: the dominant kernel (the Q4_K fused dequant-matvec), its algorithmic bytes over its CUDA-event time,
   recorded live in a second pass over the same steps with per-launch events.
 - cpu_baseline: the reference's CPU arithmetic (the C oracle) on the box's cores, one decoder layer of the same
@@ -31,7 +33,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s @70B-shape Q4_K_M b1/b8; Q4_K matvec HBM GB/s vs ~8 TB/s"
 Q4_K, Q6_K = 12, 14
-LAYER_BYTES_70B = 483.5e6   # per decoder layer (SURVEY 8d arithmetic: q, k, o, gate, up, down Q4_K + v Q6_K)
+LAYER_BYTES_70B = 483.5e6   # per decoder layer: q, k, o, gate, up, down Q4_K + v Q6_K
 
 
 def measured_peaks():
@@ -361,7 +363,7 @@ def main():
         spec = synth_spec("llama", args.layers, 8192, 64 // g, 8 // g, 128, 28672 // g, 128256 // g, 8192,
                           rope_base=500000.0, type_attn_v=14, type_embd=12)
     steps, warm, B = args.steps, args.warmup, args.batch
-    ctx = args.prompt + 2 * (steps + warm) + 64
+    ctx = args.prompt + warm + 4 * steps + 80       # warm-up, timed, three e2e loops, the profiled pass
     t0 = time.perf_counter()
     trace(f"opening synthetic model, {args.layers} layers, context {ctx}, tensor parallel over {world} GPU(s)")
     m = tp.open_group_model(dist, local, synthetic=spec, max_context=ctx, tp_nccl_only=int(args.tp_nccl_only))
@@ -396,8 +398,23 @@ def main():
     value = steps * B / (ms_max / 1e3)
 
     trace(f"timed {steps} steps: {ms:.1f} ms")
-    # e2e: the host-facing call, host token ids in, host logits out, every step
+    # e2e through the host-facing calls, every step's token ids in from host memory and its result back to host
+    # memory. The headline is the greedy serving loop's call (wl_forward_argmax / wl_forward_batch_argmax: the id of
+    # each row comes back and is the next step's token); beside it the logits-returning Forward (V floats per row
+    # back, Sampler on the host) and, at b1, the device-chained greedy decode (wl_generate_greedy, ids read back
+    # every 16 steps).
     toks = rng.integers(0, spec.vocab, B).astype(np.int32)
+    ids = np.empty(B, dtype=np.int32)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        if B == 1:
+            toks[0] = m.forward_argmax(toks, pos0=seqs[0].length, seq=seqs[0], out=ids)
+        else:
+            toks = m.forward_batch_argmax(seqs, toks, out=ids).copy()
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    e2e = steps * B / tp.max_over_ranks(dist, e2e_s)
     out = np.empty(B * spec.vocab, dtype=np.float32)
     barrier()
     t0 = time.perf_counter()
@@ -407,10 +424,16 @@ def main():
         else:
             m.forward_batch(seqs, toks, out=out)
     barrier()
-    e2e_s = time.perf_counter() - t0
-    e2e = steps * B / tp.max_over_ranks(dist, e2e_s)
+    e2e_logits = steps * B / tp.max_over_ranks(dist, time.perf_counter() - t0)
+    e2e_chained = None
+    if B == 1:
+        barrier()
+        t0 = time.perf_counter()
+        got = m.generate_greedy(int(toks[0]), steps, chunk=16, seq=seqs[0])
+        barrier()
+        e2e_chained = len(got) / tp.max_over_ranks(dist, time.perf_counter() - t0)
 
-    trace(f"e2e {e2e_s:.2f} s")
+    trace(f"e2e {e2e_s:.2f} s ({e2e:.1f} tok/s); logits-returning {e2e_logits:.1f} tok/s; chained {e2e_chained}")
     # live roofline of the dominant kernel: per-launch CUDA events over a second pass of the same steps
     m.profile(1)
     m.bench_decode(seqs, min(steps, 8))
@@ -456,8 +479,12 @@ def main():
                            "parallelism": f"tp{world}, all-reduce x2 per layer: {allreduce}" if world > 1 else "1 GPU",
                            "l2": "inputs larger than L2 (each step reads the layers' weights: 39.5 GB at 70B, 4.4 GB at 8B, "
                                  "1.8 GB or more for the MoE)"},
-                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                        "d2h_bytes_per_step": 4 * B * spec.vocab},
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                        "call": "wl_forward_argmax" if B == 1 else "wl_forward_batch_argmax",
+                        "logits_returning": {"value": e2e_logits, "call": "wl_forward" if B == 1 else
+                                             "wl_forward_batch", "d2h_bytes_per_step": 4 * B * spec.vocab},
+                        "device_chained": {"value": e2e_chained, "call": "wl_generate_greedy, chunk 16"}
+                        if e2e_chained else None},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
                 "collectives": {"launches": comm.launches, "ms_per_step": comm.ms / max(min(steps, 8), 1)}
                 if world > 1 else None,

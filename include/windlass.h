@@ -176,6 +176,31 @@ int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t 
 int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N, float* logits_out,
                          volatile const int32_t* cancel, wl_progress_fn progress, void* user);
 
+/* ---- greedy selection on the device (the caller of Forward, src/Engine.cs:135-250, with Sampler.Sample at
+ * temperature 0, :356-360, and the guess-ahead check's Argmax, :329-334). Each id is the lowest index of the largest
+ * logit (strict > in index order: ties go to the lower id, NaNs never win, and a NaN at index 0 makes the answer 0),
+ * the same bits as the host rule applied to the logits the logits-returning call gives. ---- */
+
+/* wl_forward, returning ids instead of logits: ids_out[0] = the last row's argmax (all_rows = 0), or ids_out[t] =
+ * row t's for every t < T (all_rows != 0; the guess-ahead check of Engine.cs:207-216). Same arguments, errors,
+ * cancel and progress behaviour. */
+int32_t wl_forward_argmax(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
+                          int32_t all_rows, int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress,
+                          void* user);
+/* wl_forward_batch, returning ids_out[i] = the argmax of row i. */
+int32_t wl_forward_batch_argmax(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
+                                int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+/* Greedy decode of seq (NULL = the model's own) chained on the device, the decode loop of Engine.cs:187-203 at
+ * temperature 0: step s forwards `token` (s = 0) or ids_out[s-1] at the sequence's next position and writes the
+ * argmax of its logits to ids_out[s]. The id never visits the host between steps: `chunk` steps (0 = 16, at most 64)
+ * run back to back before their ids are read. Ends after the first id found in stop_ids[0..n_stop) (kept as the last
+ * id) or after max_new steps; *n_out = the ids written, and the sequence grows by *n_out (every step forwarded one
+ * token). cancel is read before each chunk; a cancelled call returns WL_CANCELLED with *n_out and the sequence at
+ * the steps completed. */
+int32_t wl_generate_greedy(wl_model* model, wl_seq* seq, int32_t token, int32_t max_new, const int32_t* stop_ids,
+                           int32_t n_stop, int32_t chunk, int32_t* ids_out, int32_t* n_out,
+                           volatile const int32_t* cancel);
+
 /* ---- benchmark and profiling exports (no counterpart in the reference, which has no device) ---- */
 
 /* Runs `steps` decode steps of the N sequences seqs[0..N) with token ids already on the device (the same ids every
@@ -194,6 +219,10 @@ int32_t wl_profile_get(wl_model* model, int32_t type, wl_profile_entry* out);
  * limited to wait_ms. The wait gives up, the kernel returns, and the call returns WL_ETIMEDOUT with the device still
  * usable, which is what a rank sees when a peer dies between steps. (Real waits are limited to 10 s.) */
 int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms);
+
+/* The greedy choice of wl_forward_argmax on `rows` rows of V device floats: dev_ids[r] = the lowest index of row r's
+ * largest value (Argmax, src/Engine.cs:329-334; a NaN at index 0 gives 0). Synchronous on `stream`. */
+int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream);
 
 /* Quants.DecodeRow (src/Quants.cs:32-52, src/IQuants.cs:27-42): n values of `type` to fp32, bit-exact. */
 int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream);

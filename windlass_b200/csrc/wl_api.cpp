@@ -339,32 +339,101 @@ int32_t wl_length(const wl_model* model, int32_t* n)
     });
 }
 
+namespace {
+// wl_forward and wl_forward_argmax: rows come back as logits (logits_out) or as their argmax (ids_out).
+int32_t forward_rows(const char* fn, wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
+                     int32_t all_rows, float* logits_out, int32_t* ids_out, volatile const int32_t* cancel,
+                     wl_progress_fn progress, void* user)
+{
+    if (model && T == 0) return wl::fail(WL_EINVAL, "No tokens to run.");
+    if (!model || !tokens || !(logits_out || ids_out))
+        return wl::fail(WL_EINVAL, std::string(fn) + ": model, tokens and " + (ids_out || !logits_out ? "ids_out" : "logits_out") + " are required");
+    if (seq && seq->owner != model) return wl::fail(WL_EINVAL, std::string(fn) + ": the sequence belongs to another model");
+    auto call = [&](wl::Model& m, wl::Seq* s, float* out, int32_t* ids, wl_progress_fn pf, void* u) {
+        return ids ? m.forward_argmax(s, tokens, T, pos0, all_rows != 0, ids, cancel, pf, u)
+                   : m.forward(s, tokens, T, pos0, all_rows != 0, out, cancel, pf, u);
+    };
+    int32_t st;
+    if (model->g) {
+        // every shard runs the same call; shard 0's results are returned and its thread (the caller) reports
+        // progress; the others take the same path (a progress callback that does nothing)
+        std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+        const size_t rows = all_rows ? (size_t)T : 1;
+        model->g->run([&](int g) {
+            wl::Model& m = model->g->shard(g);
+            float* out = nullptr;
+            int32_t* ids = nullptr;
+            if (g == 0) { out = logits_out; ids = ids_out; }
+            else if (ids_out) ids = reinterpret_cast<int32_t*>(model->g->scratch(g, rows));
+            else out = model->g->scratch(g, rows * (size_t)m.config().vocab);
+            sts[(size_t)g] = call(m, seq ? shard_seq(seq, g) : nullptr, out, ids,
+                                  g == 0 ? progress : (progress ? noop_progress : nullptr), g == 0 ? user : nullptr);
+        });
+        st = sts[0];
+    } else {
+        st = call(*model->m, seq ? seq->s : nullptr, logits_out, ids_out, progress, user);
+    }
+    if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
+    return st;
+}
+
+int32_t forward_batch_rows(const char* fn, wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
+                           float* logits_out, int32_t* ids_out, volatile const int32_t* cancel,
+                           wl_progress_fn progress, void* user)
+{
+    if (!model || !seqs || !tokens || !(logits_out || ids_out))
+        return wl::fail(WL_EINVAL, std::string(fn) + ": model, seqs, tokens and " + (ids_out || !logits_out ? "ids_out" : "logits_out") + " are required");
+    if (N <= 0) return wl::fail(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
+    for (int i = 0; i < N; ++i)
+        if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, std::string(fn) + ": a sequence belongs to another model");
+    auto call = [&](wl::Model& m, wl::Seq* const* ss, float* out, int32_t* ids, wl_progress_fn pf, void* u) {
+        return ids ? m.forward_batch_argmax(ss, tokens, N, ids, cancel, pf, u)
+                   : m.forward_batch(ss, tokens, N, out, cancel, pf, u);
+    };
+    int32_t st;
+    if (model->g) {
+        std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+        model->g->run([&](int g) {
+            wl::Model& m = model->g->shard(g);
+            std::vector<wl::Seq*> ss((size_t)N);
+            for (int i = 0; i < N; ++i) ss[(size_t)i] = shard_seq(seqs[i], g);
+            float* out = nullptr;
+            int32_t* ids = nullptr;
+            if (g == 0) { out = logits_out; ids = ids_out; }
+            else if (ids_out) ids = reinterpret_cast<int32_t*>(model->g->scratch(g, (size_t)N));
+            else out = model->g->scratch(g, (size_t)N * m.config().vocab);
+            sts[(size_t)g] = call(m, ss.data(), out, ids, g == 0 ? progress : (progress ? noop_progress : nullptr),
+                                  g == 0 ? user : nullptr);
+        });
+        st = sts[0];
+    } else {
+        std::vector<wl::Seq*> ss((size_t)N);
+        for (int i = 0; i < N; ++i) ss[(size_t)i] = seqs[i]->s;
+        st = call(*model->m, ss.data(), logits_out, ids_out, progress, user);
+    }
+    if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
+    return st;
+}
+}  // namespace
+
 int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0, int32_t all_logits,
                    float* logits_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
 {
     return guarded([&]() -> int32_t {
-        if (model && T == 0) return wl::fail(WL_EINVAL, "No tokens to run.");
-        if (!model || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward: model, tokens and logits_out are required");
-        if (seq && seq->owner != model) return wl::fail(WL_EINVAL, "wl_forward: the sequence belongs to another model");
-        int32_t st;
-        if (model->g) {
-            // every shard runs the same call; shard 0's logits are returned and its thread (the caller) reports
-            // progress; the others take the same path (a progress callback that does nothing)
-            std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
-            const size_t rows = all_logits ? (size_t)T : 1;
-            model->g->run([&](int g) {
-                wl::Model& m = model->g->shard(g);
-                float* out = g == 0 ? logits_out : model->g->scratch(g, rows * (size_t)m.config().vocab);
-                sts[(size_t)g] = m.forward(seq ? shard_seq(seq, g) : nullptr, tokens, T, pos0, all_logits != 0, out,
-                                           cancel, g == 0 ? progress : (progress ? noop_progress : nullptr),
-                                           g == 0 ? user : nullptr);
-            });
-            st = sts[0];
-        } else {
-            st = model->m->forward(seq ? seq->s : nullptr, tokens, T, pos0, all_logits != 0, logits_out, cancel, progress, user);
-        }
-        if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
-        return st;
+        if (!logits_out && model && T != 0) return wl::fail(WL_EINVAL, "wl_forward: model, tokens and logits_out are required");
+        return forward_rows("wl_forward", model, seq, tokens, T, pos0, all_logits, logits_out, nullptr, cancel,
+                            progress, user);
+    });
+}
+
+int32_t wl_forward_argmax(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
+                          int32_t all_rows, int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress,
+                          void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!ids_out && model && T != 0) return wl::fail(WL_EINVAL, "wl_forward_argmax: model, tokens and ids_out are required");
+        return forward_rows("wl_forward_argmax", model, seq, tokens, T, pos0, all_rows, nullptr, ids_out, cancel,
+                            progress, user);
     });
 }
 
@@ -372,27 +441,45 @@ int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* to
                          volatile const int32_t* cancel, wl_progress_fn progress, void* user)
 {
     return guarded([&]() -> int32_t {
-        if (!model || !seqs || !tokens || !logits_out) return wl::fail(WL_EINVAL, "wl_forward_batch: model, seqs, tokens and logits_out are required");
-        if (N <= 0) return wl::fail(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
-        for (int i = 0; i < N; ++i)
-            if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_forward_batch: a sequence belongs to another model");
+        if (!logits_out) return wl::fail(WL_EINVAL, "wl_forward_batch: model, seqs, tokens and logits_out are required");
+        return forward_batch_rows("wl_forward_batch", model, seqs, tokens, N, logits_out, nullptr, cancel, progress, user);
+    });
+}
+
+int32_t wl_forward_batch_argmax(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
+                                int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!ids_out) return wl::fail(WL_EINVAL, "wl_forward_batch_argmax: model, seqs, tokens and ids_out are required");
+        return forward_batch_rows("wl_forward_batch_argmax", model, seqs, tokens, N, nullptr, ids_out, cancel, progress,
+                                  user);
+    });
+}
+
+int32_t wl_generate_greedy(wl_model* model, wl_seq* seq, int32_t token, int32_t max_new, const int32_t* stop_ids,
+                           int32_t n_stop, int32_t chunk, int32_t* ids_out, int32_t* n_out,
+                           volatile const int32_t* cancel)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !n_out || (max_new > 0 && !ids_out))
+            return wl::fail(WL_EINVAL, "wl_generate_greedy: model, ids_out and n_out are required");
+        if (seq && seq->owner != model) return wl::fail(WL_EINVAL, "wl_generate_greedy: the sequence belongs to another model");
         int32_t st;
         if (model->g) {
-            std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+            const int G = model->g->size();
+            std::vector<int32_t> sts((size_t)G, WL_OK), ns((size_t)G, 0);
             model->g->run([&](int g) {
                 wl::Model& m = model->g->shard(g);
-                std::vector<wl::Seq*> ss((size_t)N);
-                for (int i = 0; i < N; ++i) ss[(size_t)i] = shard_seq(seqs[i], g);
-                float* out = g == 0 ? logits_out : model->g->scratch(g, (size_t)N * m.config().vocab);
-                sts[(size_t)g] = m.forward_batch(ss.data(), tokens, N, out, cancel,
-                                                 g == 0 ? progress : (progress ? noop_progress : nullptr),
-                                                 g == 0 ? user : nullptr);
+                int32_t* ids = g == 0 ? ids_out
+                                      : reinterpret_cast<int32_t*>(model->g->scratch(g, (size_t)std::max(max_new, 1)));
+                sts[(size_t)g] = m.generate_greedy(seq ? shard_seq(seq, g) : nullptr, token, max_new, stop_ids, n_stop,
+                                                   chunk, ids, &ns[(size_t)g], cancel);
             });
             st = sts[0];
+            *n_out = ns[0];
         } else {
-            std::vector<wl::Seq*> ss((size_t)N);
-            for (int i = 0; i < N; ++i) ss[(size_t)i] = seqs[i]->s;
-            st = model->m->forward_batch(ss.data(), tokens, N, logits_out, cancel, progress, user);
+            st = model->m->generate_greedy(seq ? seq->s : nullptr, token, max_new, stop_ids, n_stop, chunk, ids_out,
+                                           n_out, cancel);
         }
         if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
         return st;
@@ -407,6 +494,29 @@ int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms)
         const int code = wl::k::selftest_ar_wait((long long)wait_ms * 1000000LL);
         if (code == 2) return wl::fail(WL_ETIMEDOUT, "a device-side wait gave up (code 2): a tensor-parallel peer did not arrive");
         return wl::fail(WL_ECUDA, "the all-reduce wait did not give up (code " + std::to_string(code) + ")");
+    });
+}
+
+int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (V <= 0 || rows <= 0 || rows > 65535) return wl::fail(WL_EINVAL, "wl_argmax: V and rows must be positive (rows <= 65535)");
+        if (!dev_logits || !dev_ids) return wl::fail(WL_EINVAL, "wl_argmax: null pointer");
+        const cudaStream_t s = (cudaStream_t)stream;
+        void* scratch = nullptr;
+        const size_t kb = sizeof(unsigned long long) * (size_t)rows, cb = sizeof(unsigned) * (size_t)rows;
+        WL_CUDA(cudaMalloc(&scratch, kb + cb));
+        try {
+            WL_CUDA(cudaMemsetAsync(scratch, 0, kb + cb, s));
+            wl::k::argmax(dev_logits, V, rows, (unsigned long long*)scratch, (unsigned*)((char*)scratch + kb), dev_ids,
+                          nullptr, nullptr, s);
+            WL_CUDA(cudaStreamSynchronize(s));
+        } catch (...) {
+            cudaFree(scratch);
+            throw;
+        }
+        WL_CUDA(cudaFree(scratch));
+        return WL_OK;
     });
 }
 

@@ -1069,6 +1069,77 @@ void scale(float* x, float f, int64_t n, cudaStream_t s)
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// greedy selection
+// ------------------------------------------------------------------------------------------------------------------
+// Sampler.Sample at temperature 0 (src/Engine.cs:356-360) and the guess-ahead check's Argmax (:329-334) scan
+// best = 0; for i = 1..n-1: if (x[i] > x[best]) best = i. Its result is the lowest index of the largest non-NaN
+// value, except that a NaN at index 0 is never replaced (every comparison with it is false), so the answer is 0 then;
+// -0 and +0 compare equal. Here every candidate becomes one 64-bit key, ordered value above, inverted index below, so
+// the largest key is the largest value at its lowest index: the blocks of a row each fold their range of the row
+// and merge it into the row's key with atomicMax; the last block to finish (a counter per row) reads the key, applies
+// the index-0 rule and resets key and counter for the next launch.
+__device__ __forceinline__ unsigned long long argmax_key(float f, int v)
+{
+    unsigned b = __float_as_uint(f);
+    if (b == 0x80000000u) b = 0u;                           // -0 compares equal to +0
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);         // order-preserving for every non-NaN float; never 0
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - (unsigned)v);
+}
+
+__global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int V, int chunk,
+                                                unsigned long long* key, unsigned* count, int32_t* ids,
+                                                int32_t* next_tok, int32_t* next_pos)
+{
+    __shared__ unsigned long long red[8];
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.y;
+    const float* x = logits + (int64_t)r * V;
+    const int v0 = blockIdx.x * chunk, v1 = min(V, v0 + chunk);
+    unsigned long long best = 0;                            // 0: no candidate (NaN or empty range)
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+        const float f = x[v];
+        if (!isnan(f)) best = max(best, argmax_key(f, v));
+    }
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = max(best, red[w]);
+    if (best) atomicMax(&key[r], best);
+    __threadfence();
+    if (atomicAdd(&count[r], 1u) != gridDim.x - 1) return;
+    __threadfence();
+    const unsigned long long k = atomicExch(&key[r], 0ull);
+    count[r] = 0u;
+    const int id = (k == 0 || isnan(x[0])) ? 0 : (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull));
+    ids[r] = id;
+    if (next_tok) {                                         // a chained decode step: the next token at the next position
+        next_tok[r] = id;
+        next_pos[r] += 1;
+    }
+}
+
+int64_t argmax_blocks(int V, int n)
+{
+    const int64_t per_row = std::max<int64_t>(1, (2 * 148 + n - 1) / n);
+    const int64_t chunk = std::max<int64_t>(2048, ((V + per_row - 1) / per_row + 255) / 256 * 256);
+    return (V + chunk - 1) / chunk;
+}
+
+void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned* count, int32_t* ids,
+            int32_t* next_tok, int32_t* next_pos, cudaStream_t s)
+{
+    if (n <= 0 || V <= 0) return;
+    if (n > 65535) WL_THROW(WL_EINVAL, "argmax: too many rows");
+    const int64_t blocks = argmax_blocks(V, n);
+    const int chunk = (int)((V + blocks - 1) / blocks);
+    launch(k_argmax, dim3((unsigned)blocks, (unsigned)n), dim3(256), 0, s, logits, V, chunk, key, count, ids,
+           next_tok, next_pos);
+    launched();
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // mixture of experts
 // ------------------------------------------------------------------------------------------------------------------
 // Route: one thread per token, the reference's sequential arithmetic (softmax with double exp and sum, greedy top-k

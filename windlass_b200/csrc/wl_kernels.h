@@ -189,6 +189,13 @@ void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s);
 void vocab_gather(const float* src, int G, int n, int vp, int V, float* dst, cudaStream_t s);
 // x[i] *= f.
 void scale(float* x, float f, int64_t n, cudaStream_t s);
+// Greedy selection on n rows of V logits (Sampler.Sample at temperature 0, Engine.cs:356-360; Argmax, :329-334):
+// ids[r] = the lowest index of row r's largest value (0 when x[0] is NaN). key[n] and count[n] are zero before the
+// launch and after it. With next_tok set, next_tok[r] = ids[r] and next_pos[r] += 1 (a chained decode step).
+void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned* count, int32_t* ids,
+            int32_t* next_tok, int32_t* next_pos, cudaStream_t s);
+// Blocks per row of that launch (for tests of its arithmetic).
+int64_t argmax_blocks(int V, int n);
 // Route (Transformer.cs:315-340) for T rows of n router logits: sel[t*k+j], wts[t*k+j].
 void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s);
 // outp[t*E + d] += w * ye[i*E + d] for the gathered rows i of one expert (MoeFfn, Transformer.cs:289-293).

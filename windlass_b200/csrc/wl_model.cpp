@@ -754,6 +754,7 @@ Model::~Model()
     free_streaming();
     dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
     dfree(pg_); dfree(pu_); dfree(py_); dfree(expert_count_d_);
+    dfree(ids_d_); dfree(amax_key_); dfree(amax_count_); dfree(gen_d_); hfree(h_ids_); hfree(h_gen_);
     if (pprep_) cudaFree(pprep_);
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
@@ -855,8 +856,14 @@ void Model::ensure_workspace(int T, int logit_rows)
         att_part_ = dalloc<float>((int64_t)k::attention_part_floats(c_.heads, c_.kv_heads, c_.head_dim));
     }
     if (logit_rows > ws_logit_rows_) {
-        dfree(logits_);
+        dfree(logits_); dfree(ids_d_); dfree(amax_key_); dfree(amax_count_); hfree(h_ids_);
         logits_ = dalloc<float>((int64_t)logit_rows * c_.vocab);
+        ids_d_ = dalloc<int32_t>(logit_rows);
+        amax_key_ = dalloc<unsigned long long>(logit_rows);
+        amax_count_ = dalloc<unsigned>(logit_rows);
+        WL_CUDA(cudaMemset(amax_key_, 0, sizeof(unsigned long long) * (size_t)logit_rows));
+        WL_CUDA(cudaMemset(amax_count_, 0, sizeof(unsigned) * (size_t)logit_rows));
+        h_ids_ = halloc<int32_t>(logit_rows);
         if (tp_size_ > 1) {
             dfree(logits_part_); dfree(logits_all_);
             logits_part_ = dalloc<float>((int64_t)logit_rows * vocab_part_);
@@ -1015,8 +1022,9 @@ void Model::build_maps()
         WL_CUDA(cudaMemset(err_d_, 0, sizeof(int)));
     }
     if (c_.expert_count > 0 && !expert_count_d_) {
-        expert_count_d_ = dalloc<unsigned long long>(1);
-        WL_CUDA(cudaMemset(expert_count_d_, 0, sizeof(unsigned long long)));
+        // [0] the count, [1] where a graph capture keeps it while its warm-up run repeats a step
+        expert_count_d_ = dalloc<unsigned long long>(2);
+        WL_CUDA(cudaMemset(expert_count_d_, 0, 2 * sizeof(unsigned long long)));
     }
 }
 
@@ -1303,7 +1311,8 @@ void Model::step_device(int T, int first, int max_n)
 }
 
 int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
-                   int first, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+                   int first, float* out, int32_t* ids, volatile const int32_t* cancel, wl_progress_fn progress,
+                   void* user)
 {
     const auto t0 = std::chrono::steady_clock::now();
     for (int t = 0; t < T; ++t)
@@ -1332,8 +1341,15 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
         head(T, first);
         stage_release(c_.layers);
     }
-    WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));
-    WL_CUDA(cudaStreamSynchronize(stream_));
+    if (ids) {
+        k::argmax(logits_, c_.vocab, T - first, amax_key_, amax_count_, ids_d_, nullptr, nullptr, stream_);
+        WL_CUDA(cudaMemcpyAsync(h_ids_, ids_d_, sizeof(int32_t) * (size_t)(T - first), cudaMemcpyDeviceToHost, stream_));
+        WL_CUDA(cudaStreamSynchronize(stream_));
+        for (int r = 0; r < T - first; ++r) ids[r] = h_ids_[r];
+    } else {
+        WL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * (size_t)(T - first) * c_.vocab, cudaMemcpyDeviceToHost, stream_));
+        WL_CUDA(cudaStreamSynchronize(stream_));
+    }
     check_device_error();
     flush_profile();
     if (progress) progress(total, total, user);
@@ -1362,8 +1378,15 @@ bool Model::graph_ready(int T, int first)
     if (!graphable(T)) return false;
     for (const GraphEntry& g : graphs_)
         if (g.T == T && g.first == first && g.gen == ws_gen_) return true;
-    // capture: kernels set their launch attributes during an eager run first
+    // capture: kernels set their launch attributes during an eager run first; that run repeats the step the graph
+    // then runs, so the experts it counts are taken back
+    if (expert_count_d_)
+        WL_CUDA(cudaMemcpyAsync(expert_count_d_ + 1, expert_count_d_, sizeof(unsigned long long),
+                                cudaMemcpyDeviceToDevice, stream_));
     step_device(T, first, max_context_);
+    if (expert_count_d_)
+        WL_CUDA(cudaMemcpyAsync(expert_count_d_, expert_count_d_ + 1, sizeof(unsigned long long),
+                                cudaMemcpyDeviceToDevice, stream_));
     const int64_t l0 = k::launches();
     cudaGraph_t graph = nullptr;
     WL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
@@ -1498,6 +1521,18 @@ wl_profile_entry Model::profile(int type)
 int32_t Model::forward(Seq* sq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out,
                        volatile const int32_t* cancel, wl_progress_fn progress, void* user)
 {
+    return forward_impl(sq, tokens, T, pos0, all_logits, out, nullptr, cancel, progress, user);
+}
+
+int32_t Model::forward_argmax(Seq* sq, const int32_t* tokens, int T, int pos0, bool all_rows, int32_t* ids,
+                              volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return forward_impl(sq, tokens, T, pos0, all_rows, nullptr, ids, cancel, progress, user);
+}
+
+int32_t Model::forward_impl(Seq* sq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out, int32_t* ids,
+                            volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
     if (!sq) sq = own_;
     if (T <= 0) WL_THROW(WL_EINVAL, "No tokens to run.");
     if (pos0 < 0 || pos0 > sq->length) WL_THROW(WL_EINVAL, "pos0 is past the cached positions.");
@@ -1511,7 +1546,7 @@ int32_t Model::forward(Seq* sq, const int32_t* tokens, int T, int pos0, bool all
     std::vector<int32_t> pos(T);
     for (int t = 0; t < T; ++t) pos[t] = pos0 + t;
     stats_.forward_calls++;
-    const int32_t st = run(T, rows, pos, tokens, all_logits ? 0 : T - 1, out, cancel, progress, user);
+    const int32_t st = run(T, rows, pos, tokens, all_logits ? 0 : T - 1, out, ids, cancel, progress, user);
     if (st == WL_OK) sq->length = pos0 + T;
     return st;
 }
@@ -1519,6 +1554,18 @@ int32_t Model::forward(Seq* sq, const int32_t* tokens, int T, int pos0, bool all
 // Transformer.ForwardBatch (src/Transformer.cs:132-170).
 int32_t Model::forward_batch(Seq* const* seqs, const int32_t* tokens, int N, float* out, volatile const int32_t* cancel,
                              wl_progress_fn progress, void* user)
+{
+    return forward_batch_impl(seqs, tokens, N, out, nullptr, cancel, progress, user);
+}
+
+int32_t Model::forward_batch_argmax(Seq* const* seqs, const int32_t* tokens, int N, int32_t* ids,
+                                    volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return forward_batch_impl(seqs, tokens, N, nullptr, ids, cancel, progress, user);
+}
+
+int32_t Model::forward_batch_impl(Seq* const* seqs, const int32_t* tokens, int N, float* out, int32_t* ids,
+                                  volatile const int32_t* cancel, wl_progress_fn progress, void* user)
 {
     if (N <= 0 || !seqs) WL_THROW(WL_EINVAL, "ForwardBatch needs one token for each sequence.");
     if (N > max_batch_) WL_THROW(WL_EINVAL, "ForwardBatch takes at most " + std::to_string(max_batch_) + " sequences.");
@@ -1543,7 +1590,7 @@ int32_t Model::forward_batch(Seq* const* seqs, const int32_t* tokens, int N, flo
     each_token_ = true;
     int32_t st;
     try {
-        st = run(N, rows, pos, tokens, 0, out, cancel, progress, user);
+        st = run(N, rows, pos, tokens, 0, out, ids, cancel, progress, user);
     } catch (...) {
         each_token_ = false;
         throw;
@@ -1551,6 +1598,78 @@ int32_t Model::forward_batch(Seq* const* seqs, const int32_t* tokens, int N, flo
     each_token_ = false;
     if (st == WL_OK) for (int i = 0; i < N; ++i) seqs[i]->length = pos[i] + 1;
     return st;
+}
+
+// LayeredBackend.Generate's decode loop at temperature 0 (src/Engine.cs:187-203) with the token chained on the device:
+// each step is the T = 1 pass (a CUDA graph when the model allows one) followed by the argmax, which writes the id
+// to the step's slot, to the token buffer the next step embeds from, and advances the position buffer. The host
+// launches `chunk` steps without waiting, then reads their ids: a stop id ends the call there (the steps launched
+// after it are dropped; what they wrote to the KV cache lies past the sequence's length). The cancel flag is read
+// before each chunk (under tensor parallelism by every rank, so all stop together).
+int32_t Model::generate_greedy(Seq* sq, int32_t token, int max_new, const int32_t* stop, int n_stop, int chunk,
+                               int32_t* ids, int32_t* n_out, volatile const int32_t* cancel)
+{
+    constexpr int MAX_CHUNK = 64;
+    if (!sq) sq = own_;
+    *n_out = 0;
+    if (max_new < 0) WL_THROW(WL_EINVAL, "max_new must not be negative.");
+    if (n_stop < 0 || (n_stop > 0 && !stop)) WL_THROW(WL_EINVAL, "The stop ids are missing.");
+    if (chunk < 0 || chunk > MAX_CHUNK) WL_THROW(WL_EINVAL, "chunk must be 0 (the default, 16) up to 64.");
+    if (token < 0 || token >= c_.vocab)
+        WL_THROW(WL_EINVAL, "Token id " + std::to_string(token) + " is outside the vocabulary.");
+    if (max_new == 0) return WL_OK;
+    if (chunk == 0) chunk = 16;
+    const int len = sq->length;
+    if ((int64_t)len + max_new > max_context_)
+        WL_THROW(WL_EINVAL, "The prompt and reply need " + std::to_string((int64_t)len + max_new) +
+                                " positions; the context is " + std::to_string(max_context_) + ".");
+    WL_CUDA(cudaSetDevice(device_));
+    const auto t0 = std::chrono::steady_clock::now();
+    reserve(sq, len + max_new);
+    ensure_workspace(1, 1);
+    if (!gen_d_) {
+        gen_d_ = dalloc<int32_t>(MAX_CHUNK);
+        h_gen_ = halloc<int32_t>(MAX_CHUNK);
+    }
+    const int64_t stride = (int64_t)sq->capacity * c_.kvdim();
+    const RowKV row{sq->kv, sq->kv + (int64_t)c_.layers * stride, stride};
+    upload_step(1, &row, &len, &token);
+    stats_.forward_calls++;
+    int done = 0;
+    while (done < max_new) {
+        if (stop_requested(cancel)) {
+            WL_CUDA(cudaStreamSynchronize(stream_));
+            sq->length = len + done;
+            *n_out = done;
+            return WL_CANCELLED;
+        }
+        const int c = std::min(chunk, max_new - done);
+        for (int j = 0; j < c; ++j) {
+            if (!graph_step(1, 0)) step_device(1, 0, len + done + j + 1);
+            k::argmax(logits_, c_.vocab, 1, amax_key_, amax_count_, gen_d_ + j, tok_d_, pos_d_, stream_);
+        }
+        WL_CUDA(cudaMemcpyAsync(h_gen_, gen_d_, sizeof(int32_t) * (size_t)c, cudaMemcpyDeviceToHost, stream_));
+        WL_CUDA(cudaStreamSynchronize(stream_));
+        check_device_error();
+        for (int j = 0; j < c; ++j) {
+            ids[done] = h_gen_[j];
+            ++done;
+            for (int i = 0; i < n_stop; ++i)
+                if (stop[i] == h_gen_[j]) {
+                    sq->length = len + done;
+                    *n_out = done;
+                    stats_.tokens += done;
+                    flush_profile();
+                    return WL_OK;
+                }
+        }
+    }
+    sq->length = len + done;
+    *n_out = done;
+    stats_.tokens += done;
+    flush_profile();
+    stats_.last_forward_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return WL_OK;
 }
 
 }  // namespace wl

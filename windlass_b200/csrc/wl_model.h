@@ -84,6 +84,19 @@ public:
                     volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     int32_t forward_batch(Seq* const* seqs, const int32_t* tokens, int N, float* out, volatile const int32_t* cancel,
                           wl_progress_fn progress, void* user);
+    // The same passes with the greedy choice made on the device: ids (host) gets each returned row's argmax
+    // (Sampler.Sample at temperature 0, src/Engine.cs:356-360) instead of its logits.
+    int32_t forward_argmax(Seq* seq, const int32_t* tokens, int T, int pos0, bool all_rows, int32_t* ids,
+                           volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    int32_t forward_batch_argmax(Seq* const* seqs, const int32_t* tokens, int N, int32_t* ids,
+                                 volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    // Greedy decode chained on the device (the loop of LayeredBackend.Generate, src/Engine.cs:187-203, at
+    // temperature 0 without guesses): step s forwards `token` (s = 0) or ids[s-1] at the sequence's next position and
+    // writes the argmax to ids[s]; the argmax becomes the next step's token in device memory, so up to `chunk` steps
+    // run back to back before the host reads their ids. Stops after a stop id or max_new steps; *n = steps kept, and
+    // the sequence grows by *n.
+    int32_t generate_greedy(Seq* seq, int32_t token, int max_new, const int32_t* stop, int n_stop, int chunk,
+                            int32_t* ids, int32_t* n, volatile const int32_t* cancel);
 
     // The model's shape; under tensor parallelism heads and kv_heads are this rank's share (full_config() has the
     // whole model's).
@@ -169,8 +182,14 @@ private:
     bool moe_on_device(const LayerW& L, int T) const;
     void ffn_moe_device(const LayerW& L, int T);
     void head(int T, int first);
+    // One pass; the rows from first_logit_row on come back as logits (out) or as their argmax (ids).
     int32_t run(int T, const std::vector<RowKV>& rows, const std::vector<int32_t>& pos, const int32_t* tokens,
-                int first_logit_row, float* out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+                int first_logit_row, float* out, int32_t* ids, volatile const int32_t* cancel, wl_progress_fn progress,
+                void* user);
+    int32_t forward_impl(Seq* seq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out, int32_t* ids,
+                         volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    int32_t forward_batch_impl(Seq* const* seqs, const int32_t* tokens, int N, float* out, int32_t* ids,
+                               volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     uint8_t* arena_alloc(int64_t bytes);
 
     Config c_, full_;
@@ -238,6 +257,14 @@ private:
     float *g_ = nullptr, *u_ = nullptr, *logits_ = nullptr, *router_ = nullptr, *wts_ = nullptr;
     float *xe_ = nullptr, *ye_ = nullptr, *ge_ = nullptr, *ue_ = nullptr, *moe_out_ = nullptr, *sh_gl_ = nullptr;
     int32_t *tok_d_ = nullptr, *pos_d_ = nullptr, *sel_ = nullptr, *bad_d_ = nullptr, *etok_d_ = nullptr;
+    // greedy selection: per logit row its argmax, merge key and block counter (zero between launches), and the
+    // chained decode's ids with their pinned host copy
+    int32_t* ids_d_ = nullptr;
+    unsigned long long* amax_key_ = nullptr;
+    unsigned* amax_count_ = nullptr;
+    int32_t* h_ids_ = nullptr;
+    int32_t* gen_d_ = nullptr;
+    int32_t* h_gen_ = nullptr;
     float* ew_d_ = nullptr;
     RowKV* rows_d_ = nullptr;
     // pinned host staging

@@ -3,6 +3,10 @@
     CudaTransformer(path)              LayeredBackend.Load -> new Transformer      (src/Engine.cs:55-91)
       .forward(tokens, pos0, all_logits, cancel, on_stage, seq)  Transformer.Forward  (src/Transformer.cs:77-109)
       .forward_batch(seqs, tokens, cancel, on_stage)             Transformer.ForwardBatch (src/Transformer.cs:132-170)
+      .forward_argmax / .forward_batch_argmax                     the same, with Sampler.Sample at temperature 0
+                                                                  (src/Engine.cs:356-360) done on the device
+      .generate_greedy(token, max_new, stop_ids)                  the greedy decode loop (src/Engine.cs:187-203),
+                                                                  token ids chained on the device
       .truncate(n), .length                                       Transformer.Truncate / Length (:57, :28)
       .new_sequence() -> Sequence (.length, .truncate(n))         Transformer.NewSequence (:60), Sequence (src/Batch.cs)
       .expert_runs, .bytes_read                                   Transformer.ExpertRuns (:27), LayerStream.BytesRead
@@ -139,6 +143,45 @@ class CudaTransformer:
                                int(all_logits), out.ctypes.data_as(C.c_void_p), cancel.ptr if cancel else None, cb,
                                None))
         return out.reshape(T, self.vocab) if all_logits else out
+
+    def forward_argmax(self, tokens, pos0=0, all_rows=False, cancel=None, on_stage=None, seq=None, out=None):
+        """forward() with the greedy choice made on the device (Sampler.Sample at temperature 0,
+        src/Engine.cs:356-360): the last row's argmax as an int, or every row's as an int32 array (all_rows, the
+        guess-ahead check of src/Engine.cs:207-216)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        T = int(tokens.size)
+        if out is None:
+            out = np.empty(T if all_rows else 1, dtype=np.int32)
+        cb = _lib.PROGRESS(lambda d, t, u: on_stage(d, t)) if on_stage else _lib.PROGRESS()
+        check(lib().wl_forward_argmax(self._h, seq._h if seq is not None else None, tokens.ctypes.data_as(C.c_void_p),
+                                      T, pos0, int(all_rows), out.ctypes.data_as(C.c_void_p),
+                                      cancel.ptr if cancel else None, cb, None))
+        return out if all_rows else int(out[0])
+
+    def forward_batch_argmax(self, seqs, tokens, cancel=None, on_stage=None, out=None):
+        """forward_batch() returning each row's argmax (int32 array of N)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        N = int(tokens.size)
+        arr = (C.c_void_p * max(N, 1))(*[s._h for s in seqs])
+        if out is None:
+            out = np.empty(max(N, 1), dtype=np.int32)
+        cb = _lib.PROGRESS(lambda d, t, u: on_stage(d, t)) if on_stage else _lib.PROGRESS()
+        check(lib().wl_forward_batch_argmax(self._h, arr, tokens.ctypes.data_as(C.c_void_p), N,
+                                            out.ctypes.data_as(C.c_void_p), cancel.ptr if cancel else None, cb, None))
+        return out[:N]
+
+    def generate_greedy(self, token, max_new, stop_ids=(), chunk=0, cancel=None, seq=None):
+        """Greedy decode chained on the device (the loop of src/Engine.cs:187-203 at temperature 0): forwards
+        `token`, then each produced id, at the sequence's next positions; returns the produced ids (int32 array), which
+        end at the first stop id or after max_new. The sequence grows by their count."""
+        out = np.empty(max(int(max_new), 1), dtype=np.int32)
+        stop = np.ascontiguousarray(list(stop_ids), dtype=np.int32)
+        n = C.c_int32()
+        check(lib().wl_generate_greedy(self._h, seq._h if seq is not None else None, int(token), int(max_new),
+                                       stop.ctypes.data_as(C.c_void_p) if stop.size else None, int(stop.size),
+                                       int(chunk), out.ctypes.data_as(C.c_void_p), C.byref(n),
+                                       cancel.ptr if cancel else None))
+        return out[:n.value].copy()
 
     def bench_decode(self, seqs, steps):
         """Device milliseconds of `steps` device-resident decode steps of `seqs` (no host copies)."""
