@@ -224,6 +224,12 @@ int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms);
  * largest value (Argmax, src/Engine.cs:329-334; a NaN at index 0 gives 0). Synchronous on `stream`. */
 int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream);
 
+/* Synchronises `device` and reports whether a device-side wait of a kernel-level export (wl_matvec, wl_matvec_tiles,
+ * wl_matvec_static, wl_gemm_tiles, wl_matmul) gave up since the last report: WL_ETIMEDOUT (and the code) if one did,
+ * else WL_OK. The waits are bounded at 2 s of device time, so this is a stalled copy, not a slow one. The model's own
+ * calls report such a wait themselves. */
+int32_t wl_kernel_status(int32_t device);
+
 /* Quants.DecodeRow (src/Quants.cs:32-52, src/IQuants.cs:27-42): n values of `type` to fp32, bit-exact. */
 int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream);
 /* Transformer.MatMulEach / Quants.DotRow (src/Transformer.cs:544-561, src/Quants.cs:67-187): y[t*rows + r] =

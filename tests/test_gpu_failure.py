@@ -25,7 +25,8 @@ def test_allreduce_wait_for_a_missing_peer_times_out(wl, oracle):
     rows, cols = 64, 512
     w = weights(O, "q4_K", rows, cols)
     x = np.random.default_rng(0).standard_normal((1, cols)).astype(np.float32)
-    dy = empty(rows)
-    wl.check(wl.lib().wl_matvec(t, ptr(dev(w)), rows, cols, ptr(dev(x.reshape(-1))), 1, ptr(dy), None))
+    dw, dx, dy = dev(w), dev(x.reshape(-1)), empty(rows)      # held: a freed temporary's memory would be reused
+    wl.check(wl.lib().wl_matvec(t, ptr(dw), rows, cols, ptr(dx), 1, ptr(dy), None))
+    wl.check(wl.lib().wl_kernel_status(0))
     want = x.astype(np.float64) @ O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64).T
     assert rel_l2(host(dy), want[0]) <= 1e-4

@@ -173,3 +173,8 @@ def test_tcgen05_gemm_matches_reference(wl, oracle, tname, rows, cols, T):
     want = x.astype(np.float64) @ dec.T
     assert rel_l2(y, want) <= 1e-4, rel_l2(y, want)
     assert rel_l2(y, y2) <= 1e-4
+
+
+def test_zz_no_kernel_level_wait_gave_up(wl):
+    """After every kernel-level call above, no bounded device-side wait gave up (wl_kernel_status)."""
+    wl.check(wl.lib().wl_kernel_status(0))

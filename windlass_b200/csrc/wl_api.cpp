@@ -60,21 +60,34 @@ wl_options defaults()
 }
 
 // Per-device scratch of the kernel-level exports (the model keeps its own workspaces).
+// Per device: the kernel-level exports' scratch, whose first word is the error word of their bounded waits, and the
+// codes collected from it before it moved (it is reallocated when a call needs more).
+std::mutex g_scratch_mu;
+void* g_scratch[64] = {};
+size_t g_scratch_size[64] = {};
+int g_scratch_code[64] = {};
+
 void* export_scratch(size_t bytes)
 {
-    static std::mutex mu;
-    static void* ptr[64] = {};
-    static size_t size[64] = {};
     int dev = 0;
     WL_CUDA(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> lock(mu);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
     if (dev >= 64) WL_THROW(WL_EINVAL, "device ordinal out of range");
-    if (size[dev] < bytes) {
-        if (ptr[dev]) { WL_CUDA(cudaDeviceSynchronize()); cudaFree(ptr[dev]); ptr[dev] = nullptr; size[dev] = 0; }
-        WL_CUDA(cudaMalloc(&ptr[dev], bytes));
-        size[dev] = bytes;
+    if (g_scratch_size[dev] < bytes) {
+        if (g_scratch[dev]) {
+            WL_CUDA(cudaDeviceSynchronize());
+            int e = 0;
+            WL_CUDA(cudaMemcpy(&e, g_scratch[dev], sizeof e, cudaMemcpyDeviceToHost));
+            if (e && !g_scratch_code[dev]) g_scratch_code[dev] = e;
+            cudaFree(g_scratch[dev]);
+            g_scratch[dev] = nullptr;
+            g_scratch_size[dev] = 0;
+        }
+        WL_CUDA(cudaMalloc(&g_scratch[dev], bytes));
+        WL_CUDA(cudaMemset(g_scratch[dev], 0, 256));
+        g_scratch_size[dev] = bytes;
     }
-    return ptr[dev];
+    return g_scratch[dev];
 }
 
 // The forward pass's matvec rule: the tensor-core kernel where the format allows (the weights repacked into tiles,
@@ -93,7 +106,7 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
         // the tiles are written by a kernel here, and the GEMM reads weights before its grid-dependency wait: the
         // memset between them (not a kernel) makes the GEMM start only once the repack has completed
         wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launches behind all earlier work
         wl::k::gemm_tiles(type, tiles, 0, rows, cols, x, cols, ncols, y, rows, scratch + 256, err, s);
         return;
     }
@@ -105,7 +118,7 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
         uint8_t* tiles = scratch + 256 + xb;
         // as above: the memset after the repack keeps the matvecs' early weight reads behind it
         wl::k::make_tiles(type, w, rows, cols, rb, tiles, s);
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launches behind all earlier work
         for (int c0 = 0; c0 < ncols; c0 += 8) {
             const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
             const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
@@ -497,6 +510,37 @@ int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms)
     });
 }
 
+int32_t wl_kernel_status(int32_t device)
+{
+    return guarded([&]() -> int32_t {
+        if (device < 0 || device >= 64) return wl::fail(WL_EINVAL, "wl_kernel_status: device ordinal out of range");
+        WL_CUDA(cudaSetDevice(device));
+        WL_CUDA(cudaDeviceSynchronize());
+        int code = 0;
+        {
+            std::lock_guard<std::mutex> lock(g_scratch_mu);
+            code = g_scratch_code[device];
+            g_scratch_code[device] = 0;
+            if (g_scratch[device]) {
+                int e = 0;
+                WL_CUDA(cudaMemcpy(&e, g_scratch[device], sizeof e, cudaMemcpyDeviceToHost));
+                if (e) {
+                    if (!code) code = e;
+                    WL_CUDA(cudaMemset(g_scratch[device], 0, sizeof e));
+                }
+            }
+        }
+        int e = 0;
+        WL_CUDA(cudaMemcpy(&e, wl::k::static_scratch(), sizeof e, cudaMemcpyDeviceToHost));
+        if (e) {
+            if (!code) code = e;
+            WL_CUDA(cudaMemset(wl::k::static_scratch(), 0, sizeof e));
+        }
+        if (code) return wl::fail(WL_ETIMEDOUT, "a device-side wait of a kernel-level call gave up (code " + std::to_string(code) + ")");
+        return WL_OK;
+    });
+}
+
 int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream)
 {
     return guarded([&]() -> int32_t {
@@ -572,7 +616,7 @@ int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t 
         const cudaStream_t st = (cudaStream_t)stream;
         uint8_t* scratch = (uint8_t*)wl::k::static_scratch();
         int* err = (int*)scratch;
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), st));   // orders the launches behind all earlier work
         wl::k::WeightMap map;
         wl::k::make_weight_map(type, (const uint8_t*)dev_w, rows, rb, &map);
         for (int c0 = 0; c0 < ncols; c0 += 8) {
@@ -621,7 +665,7 @@ int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32
         const cudaStream_t s = (cudaStream_t)stream;
         uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
         int* err = (int*)scratch;
-        WL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launches behind all earlier work
         for (int c0 = 0; c0 < ncols; c0 += 8) {
             const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
             const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
@@ -642,7 +686,7 @@ int32_t wl_gemm_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t
         if ((uintptr_t)dev_tiles % 16 != 0) return wl::fail(WL_EINVAL, "wl_gemm_tiles: dev_tiles must be 16-byte aligned");
         const cudaStream_t s = (cudaStream_t)stream;
         uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::gemm_scratch_bytes(T, cols));
-        WL_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), s));
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launch behind all earlier work
         wl::k::gemm_tiles(type, (const uint8_t*)dev_tiles, 0, rows, cols, dev_x, cols, T, dev_y, rows, scratch + 256,
                           (int*)scratch, s);
         return WL_OK;

@@ -81,18 +81,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
     return ok != 0;
 }
-// Bounded: gives up after 4096 polls (each may sleep up to 1 ms), records `code` in *err and raises the CTA's abort
-// flag, after which every later wait of the CTA returns at once, so a broken pipeline ends in seconds, not minutes.
+__device__ __forceinline__ unsigned long long gtime_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded by time: gives up after 2 s of %globaltimer (a poll may return well before its sleep hint, so the limit is
+// not a poll count), records `code` in *err and raises the CTA's abort flag, after which every later wait of the CTA
+// returns at once, so a broken pipeline ends in seconds, not minutes, and a slow one never gives up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort)
 {
     if (*abort) return false;
-    for (uint32_t i = 0; i < 4096u; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtime_ns();
+    while (!mbar_try_wait(bar, parity)) {
         if (*abort) return false;
+        if (gtime_ns() - t0 > 2000000000ull) {
+            atomicExch(err, code);
+            *abort = 1;
+            return false;
+        }
     }
-    atomicExch(err, code);
-    *abort = 1;
-    return false;
+    return true;
 }
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)

@@ -63,14 +63,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
-// Waits for the phase with the given parity; gives up after 4096 polls (each poll sleeps up to 1 ms, so at most a few
-// seconds), records the failure in *err and returns false.
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with the given parity for up to MBAR_WAIT_NS of %globaltimer time, then records the failure in
+// *err and returns false. The limit is on time, not on polls (a poll may return well before its sleep hint), so only a
+// copy that never lands gives up, never a slow one.
+constexpr unsigned long long MBAR_WAIT_NS = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code)
 {
-    for (uint32_t i = 0; i < 4096u; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    atomicExch(err, code);
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > MBAR_WAIT_NS) {
+            atomicExch(err, code);
+            return false;
+        }
+    return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
@@ -114,13 +127,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v)
 {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long globaltimer_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* epoch, int idx)
