@@ -75,9 +75,12 @@ def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
         for k in ("prefill", "tokens", "decode", "batch", "single"):
             assert np.array_equal(res[0][k], ref[0][k]), f"fused and NCCL all-reduce differ in {k}"
     for r in range(1, n):
-        for k in ("prefill", "tokens", "decode", "batch"):
+        for k in ("prefill", "tokens", "decode", "batch", "chained", "argmax"):
             assert np.array_equal(res[r][k], res[0][k]), f"rank {r} returned other {k} than rank 0"
     got = res[0]
+    # device greedy: the chained decode and the per-step device argmax follow the host argmax's token path
+    assert list(got["chained"]) == list(got["tokens"][1:]), "device-chained greedy decode differs from the host loop"
+    assert list(got["argmax"][:-1]) == list(got["tokens"][1:]), "device argmax differs from the host argmax"
     prompt = got["prompt"]
     path = O.write_synth(str(tmp_path / f"{spec}.gguf"), sp)
     om = O.Model(path, max_context=256)
@@ -112,6 +115,9 @@ def test_in_process_group_matches_process_ranks(wl, tmp_path):
         assert np.array_equal(m.forward(prompt, all_logits=True), ranks[0]["prefill"])
         for i, t in enumerate(ranks[0]["tokens"]):
             assert np.array_equal(m.forward([int(t)], pos0=len(prompt) + i), ranks[0]["decode"][i]), f"step {i}"
+        m.truncate(len(prompt))
+        toks = ranks[0]["tokens"]
+        assert list(m.generate_greedy(int(toks[0]), len(toks) - 1, chunk=5)) == list(ranks[0]["chained"])
         s1, s2 = m.new_sequence(), m.new_sequence()
         m.forward(prompt[:7], seq=s1)
         m.forward(prompt[3:20], seq=s2)

@@ -1,7 +1,8 @@
 """One rank of the tensor-parallel GPU tests, launched by tests/test_gpu_tp.py under torchrun (one process per GPU).
 
-Every rank opens the same synthetic model split over all ranks (wl_options.tp_*), runs a prompt, a greedy decode and
-a ForwardBatch step with the same arguments, and saves what its calls returned to <out>/rank<r>.npz.
+Every rank opens the same synthetic model split over all ranks (wl_options.tp_*), runs a prompt, a greedy decode (by
+host argmax, then chained on the device) and a ForwardBatch step with the same arguments, and saves what its calls
+returned to <out>/rank<r>.npz.
 """
 import argparse
 import datetime
@@ -54,6 +55,10 @@ def main():
         dec.append(logits)
     res["tokens"] = np.array(toks, dtype=np.int32)
     res["decode"] = np.stack(dec)
+    # the same decode with the greedy choice made and chained on the device (every rank takes the same steps)
+    m.truncate(args.prompt)
+    res["chained"] = m.generate_greedy(toks[0], args.steps - 1, chunk=5)
+    res["argmax"] = np.array([m.forward_argmax([t], pos0=args.prompt + i) for i, t in enumerate(toks)], dtype=np.int32)
     # ForwardBatch: two sequences with different prompts, one step, against each run alone
     s1, s2 = m.new_sequence(), m.new_sequence()
     m.forward(prompt[:7], seq=s1)
