@@ -253,7 +253,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
 #pragma unroll
                     for (int c = 0; c < 4; ++c) cv[c] = *reinterpret_cast<const uint2*>(rb + code + c * 16);
                 }
-                if (i % SPR == SPR - 1) mbar_arrive(&raw_empty[rs]);    // the bytes are in registers
                 // ScaleMinK4 (src/Quants.cs:322-330) of sub-block j = 2p + h; scale byte b is byte b & 3 of word
                 // hv.y / hv.z / hv.w for b in 0-3 / 4-7 / 8-11
                 const int j = 2 * p + h, sh8 = 8 * (j & 3);
@@ -298,7 +297,6 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
                     sc1 = sc[1];
                     d = h2f(*reinterpret_cast<const uint16_t*>(rb + 3328 + r16 * 2));
                 }
-                if (i % SPR == SPR - 1) mbar_arrive(&raw_empty[rs]);
                 const float ds[2] = {__fmul_rn(d, (float)sc0), __fmul_rn(d, (float)sc1)};
 #pragma unroll
                 for (int is = 0; is < 2; ++is)
@@ -326,8 +324,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
                 *reinterpret_cast<uint4*>(ah + chunk * 16) = make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
                 *reinterpret_cast<uint4*>(al + chunk * 16) = make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
             }
-            fence_async_shared();           // generic-proxy writes before the tensor cores read them
+            // the generic-proxy accesses of this step (the stores above, the raw reads before them) are ordered
+            // before the async proxy's: the tensor cores read the planes, the bulk copies refill the raw slot
+            fence_async_shared();
             mbar_arrive(&full_a[s]);
+            if (i % SPR == SPR - 1) mbar_arrive(&raw_empty[rs]);
         }
     } else if (warp == G_RAW_WARP) {
         // ---- raw weights into the raw ring: Q4_K per K step and live 16-row tile its headers and the step's 512
@@ -337,7 +338,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
             const int nraw = nk / SPR;
             for (int r = 0; r < nraw; ++r) {
                 const int rs = r % G_RAW_STAGES;
-                if (r >= G_RAW_STAGES) mbar_wait(&raw_empty[rs], (uint32_t)(((r / G_RAW_STAGES) + 1) & 1), err, 17, &abort_flag);
+                if (r >= G_RAW_STAGES) {
+                    mbar_wait(&raw_empty[rs], (uint32_t)(((r / G_RAW_STAGES) + 1) & 1), err, 17, &abort_flag);
+                    fence_async_shared();   // the dequantizers' reads of the slot before the copy engine rewrites it
+                }
                 uint8_t* dst = raw + rs * G_RAW_STAGE;
                 mbar_expect_tx(&raw_full[rs], (uint32_t)(live_tiles * F::RAW_TILE));
                 for (int tt = 0; tt < live_tiles; ++tt) {
