@@ -176,6 +176,18 @@ int32_t wl_forward(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t 
 int32_t wl_forward_batch(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N, float* logits_out,
                          volatile const int32_t* cancel, wl_progress_fn progress, void* user);
 
+/* One pass over several sequences' new tokens at once: a decode step that new prompts join (continuous batching, the
+ * reference's roadmap item "prompts joining a running batch", which its BatchEngine does not do). Sequence seqs[i]
+ * takes counts[i] >= 1 tokens at positions length(seqs[i]).. ; tokens holds them sequence after sequence (sum of
+ * counts). logits_out (N*vocab host floats) gets each sequence's last row in sequence order, or, when ids_out is not
+ * NULL, ids_out[i] gets that row's greedy id instead (logits_out may then be NULL). Each row attends to its own
+ * sequence only; a row's result equals that sequence's own wl_forward of the same tokens (bit for bit when the step
+ * has at most 8 rows; beyond that the rows run on the tensor-core GEMM, as a prompt does). Cancel and progress as in
+ * wl_forward; a cancelled step leaves every sequence's length unchanged. */
+int32_t wl_forward_mixed(wl_model* model, wl_seq* const* seqs, const int32_t* counts, int32_t N, const int32_t* tokens,
+                         float* logits_out, int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress,
+                         void* user);
+
 /* ---- greedy selection on the device (the caller of Forward, src/Engine.cs:135-250, with Sampler.Sample at
  * temperature 0, :356-360, and the guess-ahead check's Argmax, :329-334). Each id is the lowest index of the largest
  * logit (strict > in index order: ties go to the lower id, NaNs never win, and a NaN at index 0 makes the answer 0),

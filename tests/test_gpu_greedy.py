@@ -6,7 +6,8 @@ src/Engine.cs:356-360, and Argmax, :329-334: best = 0; if x[i] > x[best] then be
 - wl_forward_argmax / wl_forward_batch_argmax give the argmax of the logits wl_forward / wl_forward_batch return;
 - wl_generate_greedy (the decode loop of src/Engine.cs:187-203 with the id chained on the device) gives the tokens
   of a host loop of forward + argmax, and leaves the sequence where that loop does, across chunk boundaries, with
-  stop ids, cancel and after further forwards; on configs[0] it gives the oracle's greedy tokens.
+  stop ids, cancel and after further forwards; on configs[0] it gives the oracle's greedy tokens;
+- wl_forward_mixed (prompts joining a decode step) gives each sequence's own pass.
 """
 import ctypes as C
 
@@ -212,3 +213,62 @@ def test_generate_greedy_moe_device_path(wl, oracle, tmp_path):
         got = m.generate_greedy(first, 20, chunk=7, seq=b)
         assert list(got) == want
         assert m.expert_runs - runs == 20 * 2 * 2          # 20 steps x 2 layers x 2 chosen experts
+
+
+def test_forward_mixed_rows_equal_each_sequence_alone(wl, oracle, config0_file):
+    """wl_forward_mixed (prompts joining a decode step): each sequence's last row equals that sequence's own pass,
+    bit for bit up to 8 rows (every row on the per-column matvec), and within the prompt tolerance beyond (rows on
+    the tensor-core GEMM); lengths advance by each count; the argmax form returns the rows' greedy ids."""
+    from tests.test_gpu_model import compare
+    rng = np.random.default_rng(5)
+    toks = [rng.integers(0, 4096, n).astype(np.int32) for n in (9, 6, 40)]
+    with CudaTransformer(config0_file, max_context=256) as m:
+        mixed = [m.new_sequence() for _ in range(3)]
+        alone = [m.new_sequence() for _ in range(3)]
+        for s, a, t in zip(mixed, alone, toks):
+            m.forward(t[:5], seq=s)
+            m.forward(t[:5], seq=a)
+        # 8 rows: sequence 0 decodes one token, 1 takes a 1-token step, 2 joins with 6 prompt tokens
+        for step in range(3):              # the same shape again: the captured graph serves it
+            parts = [toks[0][5 + step:6 + step], toks[1][5:6] if step == 0 else np.array([7 + step], np.int32),
+                     toks[2][5 + 6 * step: 11 + 6 * step]]
+            got = m.forward_mixed(mixed, parts)
+            for i in range(3):
+                want = m.forward(parts[i], pos0=alone[i].length, seq=alone[i])
+                assert np.array_equal(got[i], want), f"step {step}: mixed row {i} differs from its own pass"
+            assert [s.length for s in mixed] == [a.length for a in alone]
+        # 24 rows: the GEMM path for the step, the matvec for the single-token pass alone
+        parts = [toks[0][8:9], np.array([99], np.int32), toks[2][23:40]]
+        ids = m.forward_mixed(mixed, parts, argmax=True)
+        wants = [m.forward(p, pos0=a.length, seq=a) for p, a in zip(parts, alone)]
+        for i, s in enumerate(mixed):
+            s.truncate(s.length - len(parts[i]))
+        got = m.forward_mixed(mixed, parts)
+        compare(got, np.stack(wants), "mixed step on the GEMM", rel=1e-3)
+        assert list(ids) == [oracle.argmax(r) for r in got]
+        assert [s.length for s in mixed] == [a.length for a in alone]
+        # argument errors
+        with pytest.raises(_lib.ArgumentError):
+            m.forward_mixed([mixed[0], mixed[0]], [[1], [2]])
+        with pytest.raises(_lib.ArgumentError):
+            m.forward_mixed(mixed[:2], [[1], []])
+        with pytest.raises(_lib.ArgumentError):
+            m.forward_mixed(mixed[:1], [list(range(300))])
+
+
+def test_forward_mixed_matches_oracle(wl, oracle, config0_file):
+    """Each sequence of a mixed step against the CPU oracle's own pass over that sequence."""
+    from tests.test_gpu_model import compare
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, 4096, n).astype(np.int32) for n in (3, 7, 12)]
+    joins = [rng.integers(0, 4096, n).astype(np.int32) for n in (1, 1, 5)]
+    with CudaTransformer(config0_file, max_context=128) as m:
+        seqs = [m.new_sequence() for _ in range(3)]
+        for s, p in zip(seqs, prompts):
+            m.forward(p, seq=s)
+        got = m.forward_mixed(seqs, joins)
+    for i in range(3):
+        om = oracle.Model(config0_file, max_context=128)
+        om.forward(prompts[i])
+        want = om.forward(joins[i], pos0=len(prompts[i]))
+        compare(got[i], want, f"mixed sequence {i}")

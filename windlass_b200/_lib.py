@@ -112,6 +112,7 @@ def lib():
         "wl_forward_batch": (I32, [P, P, P, I32, P, P, PROGRESS, P]),
         "wl_forward_argmax": (I32, [P, P, P, I32, I32, I32, P, P, PROGRESS, P]),
         "wl_forward_batch_argmax": (I32, [P, P, P, I32, P, P, PROGRESS, P]),
+        "wl_forward_mixed": (I32, [P, P, P, I32, P, P, P, P, PROGRESS, P]),
         "wl_generate_greedy": (I32, [P, P, I32, I32, P, I32, I32, P, C.POINTER(I32), P]),
         "wl_argmax": (I32, [P, I32, I32, P, P]), "wl_kernel_status": (I32, [I32]),
         "wl_dequant": (I32, [I32, P, I64, P, P]),

@@ -469,6 +469,44 @@ int32_t wl_forward_batch_argmax(wl_model* model, wl_seq* const* seqs, const int3
     });
 }
 
+int32_t wl_forward_mixed(wl_model* model, wl_seq* const* seqs, const int32_t* counts, int32_t N, const int32_t* tokens,
+                         float* logits_out, int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress,
+                         void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !seqs || !counts || !tokens || (!logits_out && !ids_out))
+            return wl::fail(WL_EINVAL, "wl_forward_mixed: model, seqs, counts, tokens and logits_out or ids_out are required");
+        if (N <= 0) return wl::fail(WL_EINVAL, "A mixed step needs at least one sequence.");
+        for (int i = 0; i < N; ++i)
+            if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, "wl_forward_mixed: a sequence belongs to another model");
+        int32_t st;
+        if (model->g) {
+            std::vector<int32_t> sts((size_t)model->g->size(), WL_OK);
+            model->g->run([&](int g) {
+                wl::Model& m = model->g->shard(g);
+                std::vector<wl::Seq*> ss((size_t)N);
+                for (int i = 0; i < N; ++i) ss[(size_t)i] = shard_seq(seqs[i], g);
+                float* out = nullptr;
+                int32_t* ids = nullptr;
+                if (g == 0) { out = ids_out ? nullptr : logits_out; ids = ids_out; }
+                else if (ids_out) ids = reinterpret_cast<int32_t*>(model->g->scratch(g, (size_t)N));
+                else out = model->g->scratch(g, (size_t)N * m.config().vocab);
+                sts[(size_t)g] = m.forward_mixed(ss.data(), counts, N, tokens, out, ids, cancel,
+                                                 g == 0 ? progress : (progress ? noop_progress : nullptr),
+                                                 g == 0 ? user : nullptr);
+            });
+            st = sts[0];
+        } else {
+            std::vector<wl::Seq*> ss((size_t)N);
+            for (int i = 0; i < N; ++i) ss[(size_t)i] = seqs[i]->s;
+            st = model->m->forward_mixed(ss.data(), counts, N, tokens, ids_out ? nullptr : logits_out, ids_out, cancel,
+                                         progress, user);
+        }
+        if (st == WL_CANCELLED) return wl::fail(st, "The operation was canceled.");
+        return st;
+    });
+}
+
 int32_t wl_generate_greedy(wl_model* model, wl_seq* seq, int32_t token, int32_t max_new, const int32_t* stop_ids,
                            int32_t n_stop, int32_t chunk, int32_t* ids_out, int32_t* n_out,
                            volatile const int32_t* cancel)

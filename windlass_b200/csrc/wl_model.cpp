@@ -1600,6 +1600,59 @@ int32_t Model::forward_batch_impl(Seq* const* seqs, const int32_t* tokens, int N
     return st;
 }
 
+// Several sequences' new tokens in one pass. Every row carries its own position and KV-cache row table, and within a
+// layer all rows' K/V are appended before any row attends, so the order of the rows is free: the rows before each
+// sequence's last token come first, then the N last rows in sequence order, and the head runs on those N only.
+int32_t Model::forward_mixed(Seq* const* seqs, const int32_t* counts, int N, const int32_t* tokens, float* out,
+                             int32_t* ids, volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    if (N <= 0 || !seqs || !counts) WL_THROW(WL_EINVAL, "A mixed step needs at least one sequence.");
+    if (N > max_batch_) WL_THROW(WL_EINVAL, "A mixed step takes at most " + std::to_string(max_batch_) + " sequences.");
+    WL_CUDA(cudaSetDevice(device_));
+    int64_t total = 0;
+    for (int i = 0; i < N; ++i) {
+        Seq* sq = seqs[i];
+        if (!sq || sq->model != this) WL_THROW(WL_EINVAL, "A sequence of another model was passed.");
+        for (int j = 0; j < i; ++j) if (seqs[j] == sq) WL_THROW(WL_EINVAL, "A sequence can appear once in a mixed step.");
+        if (counts[i] <= 0) WL_THROW(WL_EINVAL, "Every sequence of a mixed step needs at least one token.");
+        if ((int64_t)sq->length + counts[i] > max_context_)
+            WL_THROW(WL_EINVAL, "The prompt and reply need " + std::to_string((int64_t)sq->length + counts[i]) +
+                                    " positions; the context is " + std::to_string(max_context_) + ".");
+        total += counts[i];
+    }
+    if (total > (1 << 20)) WL_THROW(WL_EINVAL, "A mixed step of more than 2^20 tokens.");
+    const int T = (int)total;
+    std::vector<RowKV> row(N);
+    for (int i = 0; i < N; ++i) {
+        reserve(seqs[i], seqs[i]->length + counts[i]);
+        const int64_t stride = (int64_t)seqs[i]->capacity * c_.kvdim();
+        row[i] = RowKV{seqs[i]->kv, seqs[i]->kv + (int64_t)c_.layers * stride, stride};
+    }
+    std::vector<RowKV> rows((size_t)T);
+    std::vector<int32_t> pos((size_t)T), toks((size_t)T);
+    int k = 0;
+    int64_t off = 0;
+    for (int i = 0; i < N; ++i) {
+        for (int j = 0; j + 1 < counts[i]; ++j, ++k) {
+            rows[k] = row[i];
+            pos[k] = seqs[i]->length + j;
+            toks[k] = tokens[off + j];
+        }
+        off += counts[i];
+    }
+    off = 0;
+    for (int i = 0; i < N; ++i, ++k) {
+        off += counts[i];
+        rows[k] = row[i];
+        pos[k] = seqs[i]->length + counts[i] - 1;
+        toks[k] = tokens[off - 1];
+    }
+    stats_.batch_calls++;
+    const int32_t st = run(T, rows, pos, toks.data(), T - N, out, ids, cancel, progress, user);
+    if (st == WL_OK) for (int i = 0; i < N; ++i) seqs[i]->length += counts[i];
+    return st;
+}
+
 // LayeredBackend.Generate's decode loop at temperature 0 (src/Engine.cs:187-203) with the token chained on the device:
 // each step is the T = 1 pass (a CUDA graph when the model allows one) followed by the argmax, which writes the id
 // to the step's slot, to the token buffer the next step embeds from, and advances the position buffer. The host

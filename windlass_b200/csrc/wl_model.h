@@ -90,6 +90,11 @@ public:
                            volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     int32_t forward_batch_argmax(Seq* const* seqs, const int32_t* tokens, int N, int32_t* ids,
                                  volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    // One pass over several sequences' new tokens at once (a decode step that prompts join: continuous batching):
+    // sequence i takes counts[i] tokens at its next positions, tokens holding them sequence after sequence; out (or
+    // ids) gets each sequence's last row, in sequence order. Each row attends to its own sequence only.
+    int32_t forward_mixed(Seq* const* seqs, const int32_t* counts, int N, const int32_t* tokens, float* out,
+                          int32_t* ids, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     // Greedy decode chained on the device (the loop of LayeredBackend.Generate, src/Engine.cs:187-203, at
     // temperature 0 without guesses): step s forwards `token` (s = 0) or ids[s-1] at the sequence's next position and
     // writes the argmax to ids[s]; the argmax becomes the next step's token in device memory, so up to `chunk` steps

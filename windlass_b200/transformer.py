@@ -170,6 +170,26 @@ class CudaTransformer:
                                             out.ctypes.data_as(C.c_void_p), cancel.ptr if cancel else None, cb, None))
         return out[:N]
 
+    def forward_mixed(self, seqs, token_lists, cancel=None, on_stage=None, argmax=False):
+        """One pass over several sequences' new tokens (a decode step that prompts join): sequence i takes
+        token_lists[i]; returns each sequence's last-row logits ([N][vocab]), or its greedy id (argmax=True)."""
+        N = len(seqs)
+        counts = np.array([len(t) for t in token_lists], dtype=np.int32)
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.int32) for t in token_lists]) if N else
+                                    np.zeros(0, dtype=np.int32), dtype=np.int32)
+        arr = (C.c_void_p * max(N, 1))(*[s._h for s in seqs])
+        cb = _lib.PROGRESS(lambda d, t, u: on_stage(d, t)) if on_stage else _lib.PROGRESS()
+        if argmax:
+            ids = np.empty(max(N, 1), dtype=np.int32)
+            check(lib().wl_forward_mixed(self._h, arr, counts.ctypes.data_as(C.c_void_p), N,
+                                         toks.ctypes.data_as(C.c_void_p), None, ids.ctypes.data_as(C.c_void_p),
+                                         cancel.ptr if cancel else None, cb, None))
+            return ids[:N]
+        out = np.empty(max(N, 1) * self.vocab, dtype=np.float32)
+        check(lib().wl_forward_mixed(self._h, arr, counts.ctypes.data_as(C.c_void_p), N, toks.ctypes.data_as(C.c_void_p),
+                                     out.ctypes.data_as(C.c_void_p), None, cancel.ptr if cancel else None, cb, None))
+        return out[: N * self.vocab].reshape(N, self.vocab)
+
     def generate_greedy(self, token, max_new, stop_ids=(), chunk=0, cancel=None, seq=None):
         """Greedy decode chained on the device (the loop of src/Engine.cs:187-203 at temperature 0): forwards
         `token`, then each produced id, at the sequence's next positions; returns the produced ids (int32 array), which
