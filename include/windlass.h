@@ -242,6 +242,12 @@ int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev
  * calls report such a wait themselves. */
 int32_t wl_kernel_status(int32_t device);
 
+/* Transformer.Route (src/Transformer.cs:315-340) on the device for T tokens of n <= 256 router logits (device
+ * floats, [T][n]): dev_sel[t*k + j] = the j-th expert picked, dev_wts[t*k + j] = its probability (renormalised over
+ * the k picks when renorm != 0), k <= 32. Synchronous on `stream`. */
+int32_t wl_route(const float* dev_logits, int32_t T, int32_t n, int32_t k, int32_t renorm, int32_t* dev_sel,
+                 float* dev_wts, void* stream);
+
 /* Quants.DecodeRow (src/Quants.cs:32-52, src/IQuants.cs:27-42): n values of `type` to fp32, bit-exact. */
 int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_out, void* stream);
 /* Transformer.MatMulEach / Quants.DotRow (src/Transformer.cs:544-561, src/Quants.cs:67-187): y[t*rows + r] =

@@ -178,3 +178,25 @@ def test_tcgen05_gemm_matches_reference(wl, oracle, tname, rows, cols, T):
 def test_zz_no_kernel_level_wait_gave_up(wl):
     """After every kernel-level call above, no bounded device-side wait gave up (wl_kernel_status)."""
     wl.check(wl.lib().wl_kernel_status(0))
+
+
+@pytest.mark.parametrize("n,k,renorm", [(128, 8, 1), (8, 2, 1), (60, 4, 0), (256, 32, 1), (3, 3, 1)])
+def test_route_matches_oracle(wl, oracle, n, k, renorm):
+    """Transformer.Route (src/Transformer.cs:315-340) on the device, bit for bit against the oracle's restatement, on
+    random router logits, on logits with ties (equal probabilities: the lower expert id first) and on all -inf rows
+    (every probability NaN: ids 0, 1, ... in order)."""
+    rng = np.random.default_rng(n * 31 + k)
+    T = 37
+    lg = (rng.standard_normal((T, n)) * 3).astype(np.float32)
+    lg[1, :] = 0.5                                     # every expert tied
+    lg[2, ::2] = 1.25                                  # half of them tied at the top
+    lg[3, :] = -np.inf
+    lg[4, [n - 1, 0]] = 40.0
+    d_lg = dev(lg.reshape(-1))
+    d_sel, d_w = empty(T * k, "int32"), empty(T * k)
+    wl.check(wl.lib().wl_route(ptr(d_lg), T, n, k, renorm, ptr(d_sel), ptr(d_w), None))
+    sel, w = host(d_sel).reshape(T, k), host(d_w).reshape(T, k)
+    for t in range(T):
+        ws, ww, _ = oracle.route(lg[t], k, renorm)
+        assert list(sel[t]) == list(ws), (t, list(sel[t]), list(ws))
+        assert np.array_equal(w[t].view(np.uint32), ww.view(np.uint32)) or (np.isnan(w[t]).all() and np.isnan(ww).all()), t

@@ -579,6 +579,19 @@ int32_t wl_kernel_status(int32_t device)
     });
 }
 
+int32_t wl_route(const float* dev_logits, int32_t T, int32_t n, int32_t k, int32_t renorm, int32_t* dev_sel,
+                 float* dev_wts, void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (T <= 0 || n <= 0 || n > 256 || k <= 0 || k > 32 || k > n)
+            return wl::fail(WL_EINVAL, "wl_route: T >= 1, 1 <= k <= min(n, 32), n <= 256");
+        if (!dev_logits || !dev_sel || !dev_wts) return wl::fail(WL_EINVAL, "wl_route: null pointer");
+        wl::k::route(dev_logits, T, n, k, renorm, dev_sel, dev_wts, (cudaStream_t)stream);
+        WL_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+        return WL_OK;
+    });
+}
+
 int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream)
 {
     return guarded([&]() -> int32_t {

@@ -1142,42 +1142,70 @@ void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned
 // ------------------------------------------------------------------------------------------------------------------
 // mixture of experts
 // ------------------------------------------------------------------------------------------------------------------
-// Route: one thread per token, the reference's sequential arithmetic (softmax with double exp and sum, greedy top-k
-// with ties to the lower id, renormalisation clamped at 6.103515625e-5).
-__global__ void k_route(const float* __restrict__ logits, int T, int n, int k, int renorm, int32_t* sel, float* wts)
+// Route (Transformer.cs:315-340): one CTA per token, one thread per expert (n <= 256). The maximum (NaNs never win)
+// and the exponentials are element-wise, so their results do not depend on the order; the double sum runs on one
+// thread in expert order, as the reference's loop does. The reference's greedy top-k picks, among the experts not yet
+// taken, the largest probability at its lowest id, so the expert of rank r under (probability descending, id
+// ascending) is its pick number r: each thread counts the experts ranked before it and the k lowest ranks write
+// their picks. (When the sum is NaN every probability is NaN, every comparison fails and the reference picks ids
+// 0, 1, ... in order: NaNs rank by id.) The chosen sum is added in pick order and the renormalisation divides by it
+// clamped at 6.103515625e-5, as the reference does.
+__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int n, int k, int renorm,
+                                               int32_t* __restrict__ sel, float* __restrict__ wts)
 {
+    __shared__ float p[256];
+    __shared__ float red[8];
+    __shared__ float picked[32];
+    __shared__ float inv_s;
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= T) return;
-    const float* lg = logits + (int64_t)t * n;
-    float p[256];
-    bool taken[256];
-    float mx = -INFINITY;
-    for (int i = 0; i < n; ++i) if (lg[i] > mx) mx = lg[i];
-    double sum = 0;
-    for (int i = 0; i < n; ++i) { p[i] = (float)exp((double)__fsub_rn(lg[i], mx)); sum += p[i]; taken[i] = false; }
-    const float inv = (float)(1.0 / sum);
-    for (int i = 0; i < n; ++i) p[i] = __fmul_rn(p[i], inv);
-    float chosen = 0.f;
-    for (int j = 0; j < k; ++j) {
-        int best = -1;
-        for (int i = 0; i < n; ++i) if (!taken[i] && (best < 0 || p[i] > p[best])) best = i;
-        taken[best] = true;
-        sel[(int64_t)t * k + j] = best;
-        wts[(int64_t)t * k + j] = p[best];
-        chosen = __fadd_rn(chosen, p[best]);
+    const int t = blockIdx.x, i = threadIdx.x, lane = i & 31, warp = i >> 5;
+    const float v = i < n ? logits[(int64_t)t * n + i] : -INFINITY;
+    float m = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    float mx = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+    if (i < n) p[i] = (float)exp((double)__fsub_rn(v, mx));
+    __syncthreads();
+    if (i == 0) {
+        double sum = 0;
+        for (int j = 0; j < n; ++j) sum += p[j];
+        inv_s = (float)(1.0 / sum);
     }
-    if (renorm) {
-        const float div = fmaxf(chosen, 6.103515625e-5f);
-        for (int j = 0; j < k; ++j) wts[(int64_t)t * k + j] = __fdiv_rn(wts[(int64_t)t * k + j], div);
+    __syncthreads();
+    const float pi = i < n ? __fmul_rn(p[i], inv_s) : 0.f;
+    __syncthreads();
+    if (i < n) p[i] = pi;
+    __syncthreads();
+    if (i < n) {
+        const bool nan_i = isnan(pi);
+        int rank = 0;
+        for (int j = 0; j < n; ++j) {
+            const float q = p[j];
+            rank += (q > pi) || ((q == pi || nan_i) && j < i);
+        }
+        if (rank < k) {
+            sel[(int64_t)t * k + rank] = i;
+            picked[rank] = pi;
+        }
+    }
+    __syncthreads();
+    if (i == 0) {
+        float chosen = 0.f;
+        for (int j = 0; j < k; ++j) chosen = __fadd_rn(chosen, picked[j]);
+        const float div = isnan(chosen) ? chosen : fmaxf(chosen, 6.103515625e-5f);
+        for (int j = 0; j < k; ++j) wts[(int64_t)t * k + j] = renorm ? __fdiv_rn(picked[j], div) : picked[j];
     }
 }
 
 void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s)
 {
     if (T <= 0) return;
-    launch(k_route, dim3(grid_for(T, 64)), dim3(64), 0, s, logits, T, n, k, renorm, sel, wts);
+    if (n <= 0 || n > 256 || k <= 0 || k > 32 || k > n) WL_THROW(WL_EUNSUPPORTED, "route: 1..256 experts, 1..32 chosen");
+    launch(k_route, dim3((unsigned)T), dim3((unsigned)((n + 31) / 32 * 32)), 0, s, logits, n, k, renorm, sel, wts);
     launched();
 }
 
