@@ -343,6 +343,35 @@ __device__ __forceinline__ void unit_iq2xxs(const uint8_t* __restrict__ row, int
     }
 }
 
+// F32 rows (the MoE router and other small float matrices): a unit is 32 consecutive values, read as eight 16-byte
+// vectors; the products are summed in value order, as the generic path sums them.
+template <int NC>
+__device__ __forceinline__ void unit_f32(const uint8_t* __restrict__ row, int u, const float* __restrict__ x,
+                                         int64_t ldx, float (&acc)[NC])
+{
+    const float* wr = reinterpret_cast<const float*>(row) + 32 * u;
+    float w[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 v = ld4(wr + 4 * q);
+        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float* xt = x + t * ldx + 32 * u;
+        float a = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 xv = ld4(xt + 4 * q);
+            a += w[4 * q] * xv.x;
+            a += w[4 * q + 1] * xv.y;
+            a += w[4 * q + 2] * xv.z;
+            a += w[4 * q + 3] * xv.w;
+        }
+        acc[t] += a;
+    }
+}
+
 // Any decodable type, 32 values per unit, through the exact element decoder.
 template <int NC>
 __device__ __forceinline__ void unit_generic(int type, const uint8_t* __restrict__ row, int u, int cols,
@@ -365,7 +394,7 @@ __device__ __forceinline__ void unit_generic(int type, const uint8_t* __restrict
     }
 }
 
-enum { MV_GENERIC = 0, MV_Q4K = 1, MV_Q6K = 2, MV_Q8_0 = 3, MV_IQ4XS = 4, MV_IQ2XXS = 5 };
+enum { MV_GENERIC = 0, MV_Q4K = 1, MV_Q6K = 2, MV_Q8_0 = 3, MV_IQ4XS = 4, MV_IQ2XXS = 5, MV_F32 = 6 };
 
 template <int KIND, int NC>
 __global__ void __launch_bounds__(128) k_matvec(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows,
@@ -396,6 +425,9 @@ __global__ void __launch_bounds__(128) k_matvec(int type, const uint8_t* __restr
     } else if (KIND == MV_IQ2XXS) {
         const int units = cols >> 5;
         for (int u = lane; u < units; u += 32) unit_iq2xxs<NC>(wr, u, x, ldx, acc);
+    } else if (KIND == MV_F32) {
+        const int units = cols >> 5;
+        for (int u = lane; u < units; u += 32) unit_f32<NC>(wr, u, x, ldx, acc);
     } else {
         const int units = (cols + 31) >> 5;
         for (int u = lane; u < units; u += 32) unit_generic<NC>(type, wr, u, cols, x, ldx, acc);
@@ -443,6 +475,7 @@ void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, c
         else if (type == 8 && xa && w2 && cols % 32 == 0) launch_mv<MV_Q8_0>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else if (type == 23 && xa && w8 && cols % 256 == 0) launch_mv<MV_IQ4XS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else if (type == 16 && xa && w2 && cols % 256 == 0) launch_mv<MV_IQ2XXS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 0 && xa && w16 && cols % 32 == 0) launch_mv<MV_F32>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else launch_mv<MV_GENERIC>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         launched();
     }
@@ -664,6 +697,99 @@ void rope_append(float* q, const float* k, const float* v, int T, int heads, int
     launched();
 }
 
+// Per-head QK-norm (Transformer.cs:197-201, RmsNormRows per head) fused with NEOX RoPE over the whole head and the
+// KV append: one warp per (row, head), q heads first, then kv heads, whose warps also append the value head. Lane l
+// holds values l, l + 32, ... of the head, the order k_rmsnorm8 gives them with 32 threads, and takes the same steps:
+// the double sum of squares per lane in that order, the lanes by xor butterfly, the scale and the two rounded
+// products; NEOX pairs (i, i + HD/2) then sit in one lane, rotated with k_rope_append's arithmetic. So q, the cache's K
+// and V are bit for bit those of k_rmsnorm8 twice and k_rope_append.
+template <int HD>
+__global__ void __launch_bounds__(128) k_qknorm_rope_append(float* __restrict__ q, const float* __restrict__ k,
+                                                            const float* __restrict__ v, int heads, int kv_heads,
+                                                            const float* __restrict__ qw, const float* __restrict__ kw,
+                                                            float eps, const int32_t* __restrict__ pos,
+                                                            const float* __restrict__ table,
+                                                            const RowKV* __restrict__ rows, int layer)
+{
+    constexpr int NV = HD / 32, NP = HD / 64, HALF = HD / 2;
+    pdl_trigger();
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int hw = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (hw >= heads + kv_heads) {
+        pdl_wait();
+        return;
+    }
+    const bool isq = hw < heads;
+    const int h = isq ? hw : hw - heads;
+    // positions, cache rows, the rope table and the norm weights are written by no kernel: read them before the wait
+    const int p = pos[t];
+    const RowKV rk = rows[t];
+    const float* cs = table + (int64_t)p * HD;
+    const float* w = isq ? qw : kw;
+    float wv[NV], c[NP], sn[NP];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) wv[j] = w[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        c[j] = cs[2 * (lane + 32 * j)];
+        sn[j] = cs[2 * (lane + 32 * j) + 1];
+    }
+    pdl_wait();
+    const int kd = kv_heads * HD;
+    const float* src = isq ? q + ((int64_t)t * heads + h) * HD : k + (int64_t)t * kd + (int64_t)h * HD;
+    float x[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) x[j] = src[lane + 32 * j];
+    double ss = 0;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) ss += (double)x[j] * (double)x[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float mean = (float)(ss / HD);
+    const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
+    float y[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) y[j] = __fmul_rn(__fmul_rn(x[j], scale), wv[j]);
+    float r[NV];
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+        const float x0 = y[j], x1 = y[j + NP];
+        r[j] = __fsub_rn(__fmul_rn(x0, c[j]), __fmul_rn(x1, sn[j]));
+        r[j + NP] = __fadd_rn(__fmul_rn(x0, sn[j]), __fmul_rn(x1, c[j]));
+    }
+    static_assert(HALF == 32 * NP, "pairs (i, i + HD/2) must sit in one lane");
+    if (isq) {
+        float* dst = q + ((int64_t)t * heads + h) * HD;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) dst[lane + 32 * j] = r[j];
+    } else {
+        const int64_t base = (int64_t)layer * rk.layer_stride + (int64_t)p * kd + (int64_t)h * HD;
+        const float* vs = v + (int64_t)t * kd + (int64_t)h * HD;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            rk.k[base + lane + 32 * j] = __half_as_ushort(__float2half_rn(r[j]));
+            rk.v[base + lane + 32 * j] = __half_as_ushort(__float2half_rn(vs[lane + 32 * j]));
+        }
+    }
+}
+
+bool qknorm_rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim,
+                        int rope_dims, int neox, const float* qw, const float* kw, float eps, const int32_t* pos,
+                        const float* table, const RowKV* rows, int layer, cudaStream_t s)
+{
+    if (!neox || rope_dims != head_dim || (head_dim != 64 && head_dim != 128 && head_dim != 256)) return false;
+    if (T <= 0) return true;
+    const dim3 grid((unsigned)((heads + kv_heads + 3) / 4), (unsigned)T);
+    if (head_dim == 64)
+        launch(k_qknorm_rope_append<64>, grid, dim3(128), 0, s, q, k, v, heads, kv_heads, qw, kw, eps, pos, table, rows, layer);
+    else if (head_dim == 128)
+        launch(k_qknorm_rope_append<128>, grid, dim3(128), 0, s, q, k, v, heads, kv_heads, qw, kw, eps, pos, table, rows, layer);
+    else
+        launch(k_qknorm_rope_append<256>, grid, dim3(128), 0, s, q, k, v, heads, kv_heads, qw, kw, eps, pos, table, rows, layer);
+    launched();
+    return true;
+}
+
 // SwiGlu (k_swiglu's arithmetic) and the prepared activations of the result, one 256-value superblock per CTA.
 __global__ void __launch_bounds__(64) k_swiglu_prep(float* __restrict__ g, const float* __restrict__ u, int F,
                                                     uint8_t* __restrict__ prep)
@@ -859,69 +985,86 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
 }
 
 // Merges the S position ranges of k_attn_part in range order for one 256-value superblock of a row's attention
-// output (64 threads, 4 consecutive values each, all within one head): M = max m_s, w_s = e^(m_s - M),
-// out = sum_s w_s o_s / sum_s w_s l_s, sums in double in range order. With prep, the superblock is also written in
-// the tensor-core matvec's activation layout. All loads of a thread are issued before their first use.
+// output: M = max m_s, w_s = e^(m_s - M), out = sum_s w_s o_s / sum_s w_s l_s, in double. Up to 16 ranges one
+// thread per 4 consecutive values (64 threads) adds them in range order. Beyond 16, the ranges go to NA = 4
+// accumulator sets (range s into set s % NA, each set in range order), which shortens the dependent chains of double
+// adds: the four sets of a value run on four adjacent lanes (256 threads), each lane loading only its own ranges, and
+// lane 0 of the four adds the sets in set order, so the result is fixed for a given S. With prep, the superblock is
+// also written in the tensor-core matvec's activation layout. All loads of a thread are issued before their first use.
 template <int S>
-__global__ void __launch_bounds__(64) k_attn_combine(int heads, int hd, const float* __restrict__ part,
-                                                     const float* __restrict__ ml, float* __restrict__ out,
-                                                     uint8_t* __restrict__ prep)
+__global__ void __launch_bounds__(S > 16 ? 256 : 64) k_attn_combine(int heads, int hd, const float* __restrict__ part,
+                                                                    const float* __restrict__ ml,
+                                                                    float* __restrict__ out, uint8_t* __restrict__ prep)
 {
+    constexpr int NA = S > 16 ? 4 : 1;
+    constexpr int SPT = S / NA;                 // ranges per thread
     pdl_trigger();
     pdl_wait();
     __shared__ float scratch[2];
-    const int sb = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
-    const int QD = heads * hd, v = sb * 256 + 4 * tid, head = v / hd, d = v % hd;
+    __shared__ float4 fs[NA > 1 ? 64 : 1];
+    const int sb = blockIdx.x, t = blockIdx.y;
+    const int vt = (int)threadIdx.x / NA, a = (int)threadIdx.x % NA;
+    const int QD = heads * hd, v = sb * 256 + 4 * vt, head = v / hd, d = v % hd;
     const float2* mlp = reinterpret_cast<const float2*>(ml + ((int64_t)t * heads + head) * S * 2);
     const float* pp = part + ((int64_t)t * heads + head) * S * hd + d;
-    // ranges in groups of 16, each group's loads issued before their first use
-    constexpr int GR = S < 16 ? S : 16;
+    float2 mls[SPT];
+    float4 ps[SPT];
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) {
+        mls[j] = mlp[a + NA * j];
+        ps[j] = *reinterpret_cast<const float4*>(pp + (int64_t)(a + NA * j) * hd);
+    }
     float M = -INFINITY;
 #pragma unroll
-    for (int g0 = 0; g0 < S; g0 += GR) {
-        float2 mls[GR];
-#pragma unroll
-        for (int s2 = 0; s2 < GR; ++s2) mls[s2] = mlp[g0 + s2];
-#pragma unroll
-        for (int s2 = 0; s2 < GR; ++s2) M = fmaxf(M, mls[s2].x);
+    for (int j = 0; j < SPT; ++j) M = fmaxf(M, mls[j].x);
+    if (NA > 1) {
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
     }
-    // with more than 16 ranges, NA interleaved accumulator sets (range s into set s % NA) shorten the dependent
-    // chains of double adds; the sets are added in set order, so the result stays fixed for a given S
-    constexpr int NA = S > 16 ? 4 : 1;
-    double L[NA], o0[NA], o1[NA], o2[NA], o3[NA];
+    double L = 0.0, o0 = 0.0, o1 = 0.0, o2 = 0.0, o3 = 0.0;
 #pragma unroll
-    for (int a = 0; a < NA; ++a) L[a] = o0[a] = o1[a] = o2[a] = o3[a] = 0.0;
+    for (int j = 0; j < SPT; ++j) {
+        const double w = mls[j].y > 0.f ? (double)expf(mls[j].x - M) : 0.0;
+        L += w * (double)mls[j].y;
+        o0 += w * (double)ps[j].x;
+        o1 += w * (double)ps[j].y;
+        o2 += w * (double)ps[j].z;
+        o3 += w * (double)ps[j].w;
+    }
+    if (NA > 1) {
+        double Ls[NA], a0[NA], a1[NA], a2[NA], a3[NA];
 #pragma unroll
-    for (int g0 = 0; g0 < S; g0 += GR) {
-        float2 mls[GR];
-        float4 ps[GR];
-#pragma unroll
-        for (int s2 = 0; s2 < GR; ++s2) {
-            mls[s2] = mlp[g0 + s2];
-            ps[s2] = *reinterpret_cast<const float4*>(pp + (int64_t)(g0 + s2) * hd);
+        for (int k2 = 1; k2 < NA; ++k2) {
+            Ls[k2] = __shfl_down_sync(0xffffffffu, L, k2);
+            a0[k2] = __shfl_down_sync(0xffffffffu, o0, k2);
+            a1[k2] = __shfl_down_sync(0xffffffffu, o1, k2);
+            a2[k2] = __shfl_down_sync(0xffffffffu, o2, k2);
+            a3[k2] = __shfl_down_sync(0xffffffffu, o3, k2);
         }
 #pragma unroll
-        for (int s2 = 0; s2 < GR; ++s2) {
-            const int a = s2 % NA;
-            const double w = mls[s2].y > 0.f ? (double)expf(mls[s2].x - M) : 0.0;
-            L[a] += w * (double)mls[s2].y;
-            o0[a] += w * (double)ps[s2].x;
-            o1[a] += w * (double)ps[s2].y;
-            o2[a] += w * (double)ps[s2].z;
-            o3[a] += w * (double)ps[s2].w;
+        for (int k2 = 1; k2 < NA; ++k2) {
+            L += Ls[k2];
+            o0 += a0[k2];
+            o1 += a1[k2];
+            o2 += a2[k2];
+            o3 += a3[k2];
         }
     }
-#pragma unroll
-    for (int a = 1; a < NA; ++a) {
-        L[0] += L[a];
-        o0[0] += o0[a];
-        o1[0] += o1[a];
-        o2[0] += o2[a];
-        o3[0] += o3[a];
+    const float f[4] = {(float)(o0 / L), (float)(o1 / L), (float)(o2 / L), (float)(o3 / L)};
+    if (a == 0) *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
+    if (!prep) return;
+    uint8_t* blk = prep + ((int64_t)t * (QD / 256) + sb) * XP_COL;
+    if (NA == 1) {
+        xprep_sb(f, vt, scratch, blk);
+        return;
     }
-    const float f[4] = {(float)(o0[0] / L[0]), (float)(o1[0] / L[0]), (float)(o2[0] / L[0]), (float)(o3[0] / L[0])};
-    *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
-    if (prep) xprep_sb(f, tid, scratch, prep + ((int64_t)t * (QD / 256) + sb) * XP_COL);
+    if (a == 0) fs[vt] = make_float4(f[0], f[1], f[2], f[3]);
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        const float4 g = fs[threadIdx.x];
+        const float fv[4] = {g.x, g.y, g.z, g.w};
+        xprep_sb<true>(fv, (int)threadIdx.x, scratch, blk);
+    }
 }
 
 int attention_splits(int T, int kv_heads)
@@ -949,8 +1092,8 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
     if (S > 1) {
         auto comb = S == 16 ? k_attn_combine<16> : S == 32 ? k_attn_combine<32> : k_attn_combine<64>;
         if (S != 16 && S != 32 && S != 64) WL_THROW(WL_EINVAL, "attention: unexpected range count");
-        launch(comb, dim3(heads * HD / 256, T), dim3(64), 0, s, heads, (int)HD, (const float*)part, (const float*)ml,
-               out, prep ? prep->blocks : (uint8_t*)nullptr);
+        launch(comb, dim3(heads * HD / 256, T), dim3(S > 16 ? 256 : 64), 0, s, heads, (int)HD, (const float*)part,
+               (const float*)ml, out, prep ? prep->blocks : (uint8_t*)nullptr);
         launched();
     }
 }

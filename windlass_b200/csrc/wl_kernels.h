@@ -127,6 +127,10 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
 // else i. Each pair's result is the one a matvec of that expert alone gives.
 void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
                   bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s);
+// Gate and up of every pair in one launch: matvec_pairs of A into ya and of B (same shape, stacked the same way) into
+// yb, activations per token (x_per_token), each CTA's result what matvec_pairs gives.
+void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_rows, int cols, const int32_t* sel,
+                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s);
 // MoeFfn's weighted sum (src/Transformer.cs:289-293) from the pairs' outputs: out[t] = sum over token t's K experts in
 // ascending expert order of wts[t*K+j] * y[(t*K+j)*E ...], each step a separately rounded multiply and add from 0.
 void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s);
@@ -179,6 +183,11 @@ bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
 // Transformer.cs:418-433, and ToHalf, :342-348), in one kernel; k is left unrotated in its buffer.
 void rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim, int rope_dims,
                  int neox, const int32_t* pos, const float* table, const RowKV* rows, int layer, cudaStream_t s);
+// Per-head QK-norm then rope_append in one kernel, bit for bit the two rmsnorm passes and rope_append; false (nothing
+// launched) unless the rope is NEOX over the whole head and head_dim is 64, 128 or 256.
+bool qknorm_rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim,
+                        int rope_dims, int neox, const float* qw, const float* kw, float eps, const int32_t* pos,
+                        const float* table, const RowKV* rows, int layer, cudaStream_t s);
 // SwiGlu into g (as swiglu) for T rows of F values, and g's prepared activations (F a multiple of 256, T <= 8).
 void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStream_t s);
 // g[i] = g[i]/(1+exp(-g[i])) * u[i] (SwiGlu, Transformer.cs:247).

@@ -362,13 +362,20 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     float* __restrict__ y = second ? seg.y : y_a;
     const int64_t ldy = second ? seg.ldy : ldy_a;
     if (TILED && seg.sel) {
-        // grouped experts: the expert ids come from the router kernel, so wait for it before the first weight copy
+        // grouped experts: the expert ids come from the router kernel, so wait for it before the first weight copy.
+        // With seg.wt the launch covers a second stacked matrix of the same shape (up after gate): its CTAs follow
+        // the first matrix's and write seg.y.
         pdl_wait();
-        const int pair = (int)blockIdx.x / seg.tiles_per_pair;
-        bx = (int)blockIdx.x % seg.tiles_per_pair;
+        int b = (int)blockIdx.x;
+        const int per = seg.first_ctas * seg.tiles_per_pair;
+        const bool up = seg.wt && b >= per;
+        if (up) b -= per;
+        const int pair = b / seg.tiles_per_pair;
+        bx = b % seg.tiles_per_pair;
+        if (up) wt = seg.wt;
         row_base = row_base_a + seg.sel[pair] * rows_a;
         xq += (int64_t)(seg.x_per_token ? pair / seg.K : pair) * nsb * XP_COL;
-        y = y_a + (int64_t)pair * ldy_a;
+        y = (up ? seg.y : y_a) + (int64_t)pair * (up ? seg.ldy : ldy_a);
     }
     const int r0 = bx * Q4_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
@@ -938,7 +945,7 @@ static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base,
         WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
         attr[dev] = true;
     }
-    const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas
+    const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas * (seg.wt ? 2 : 1)
                              : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     launch(k_mmv_q4k<NC, TILED>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
            (const uint8_t*)p.blocks, y, ldy, err, seg);
@@ -1047,6 +1054,21 @@ void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols,
     // first_ctas carries the pair count (the CTA count is pairs x tiles per pair)
     const MvSeg seg{nullptr, 0, 0, npairs, nullptr, 0, sel, K, tiles_per_pair, x_per_token ? 1 : 0};
     launch_q4k<1, true>(none, tiles, row_base, expert_rows, cols / 256, p, y, ldy, err, s, seg);
+}
+
+void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_rows, int cols, const int32_t* sel,
+                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s)
+{
+    if ((uintptr_t)tiles_a % 16 != 0 || (uintptr_t)tiles_b % 16 != 0 || expert_rows % 16 != 0)
+        WL_THROW(WL_EINVAL, "matvec_pairs2: experts must start on 16-row tiles");
+    if (!tiles_supported(12, cols) || p.cols != cols) WL_THROW(WL_EUNSUPPORTED, "matvec_pairs2: Q4_K with matching activations only");
+    if (npairs <= 0) return;
+    if ((npairs + K - 1) / K > p.nc) WL_THROW(WL_EINVAL, "matvec_pairs2: too few activation columns");
+    CUtensorMap none;
+    memset(&none, 0, sizeof none);
+    const int tiles_per_pair = expert_rows / Q4_ROWS;
+    const MvSeg seg{tiles_b, 0, expert_rows, npairs, yb, ldy, sel, K, tiles_per_pair, 1};
+    launch_q4k<1, true>(none, tiles_a, 0, expert_rows, cols / 256, p, ya, ldy, err, s, seg);
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,

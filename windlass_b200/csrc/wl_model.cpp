@@ -1101,8 +1101,7 @@ void Model::ffn_moe_device(const LayerW& L, int T)
     k::route(router_, T, c_.expert_count, K, c_.expert_weights_norm ? 1 : 0, sel_, wts_, stream_);
     k::count_experts(sel_, NP, expert_count_d_, stream_);
     const int mark = profile_begin();
-    k::matvec_pairs(L.gate_exps.tiles, 0, X, E, sel_, NP, K, true, px, pg_, X, err_d_, stream_);
-    k::matvec_pairs(L.up_exps.tiles, 0, X, E, sel_, NP, K, true, px, pu_, X, err_d_, stream_);
+    k::matvec_pairs2(L.gate_exps.tiles, L.up_exps.tiles, X, E, sel_, NP, K, px, pg_, pu_, X, err_d_, stream_);
     const k::XPrep pp = k::xprep_view(pprep_, X, NP);
     k::swiglu_prep(pg_, pu_, NP, X, pp, stream_);
     k::matvec_pairs(L.down_exps.tiles, 0, E, X, sel_, NP, K, false, pp, py_, E, err_d_, stream_);
@@ -1178,16 +1177,23 @@ void Model::layer(int l, int T, int max_n)
     if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
     if (L.kb.present()) k::add_bias(k_, L.kb.d, T, KD, stream_);
     if (L.vb.present()) k::add_bias(v_, L.vb.d, T, KD, stream_);
+    const int rm = profile_begin();
+    bool roped = false;
     if (c_.qk_norm_full) {
         k::rmsnorm(q_, T, QD, L.q_norm.d, c_.rms_eps, q_, stream_);
         k::rmsnorm(k_, T, KD, L.k_norm.d, c_.rms_eps, k_, stream_);
     } else if (c_.qk_norm) {
-        k::rmsnorm(q_, T * c_.heads, HD, L.q_norm.d, c_.rms_eps, q_, stream_);
-        k::rmsnorm(k_, T * c_.kv_heads, HD, L.k_norm.d, c_.rms_eps, k_, stream_);
+        // per-head norms and the rope in one kernel where the rope covers whole NEOX heads (qwen3, qwen3moe)
+        roped = k::qknorm_rope_append(q_, k_, v_, T, c_.heads, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0,
+                                      L.q_norm.d, L.k_norm.d, c_.rms_eps, pos_d_, rope_table_, rows_d_, l, stream_);
+        if (!roped) {
+            k::rmsnorm(q_, T * c_.heads, HD, L.q_norm.d, c_.rms_eps, q_, stream_);
+            k::rmsnorm(k_, T * c_.kv_heads, HD, L.k_norm.d, c_.rms_eps, k_, stream_);
+        }
     }
-    const int rm = profile_begin();
-    k::rope_append(q_, k_, v_, T, c_.heads, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_, rope_table_,
-                   rows_d_, l, stream_);
+    if (!roped)
+        k::rope_append(q_, k_, v_, T, c_.heads, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_,
+                       rope_table_, rows_d_, l, stream_);
     profile_end(rm, WL_PROFILE_ROPE, 0.0);
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
     // the o matvec's activations come out of the attention combine when it can prepare them
