@@ -341,7 +341,8 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // Up to two columns, the 8 MMA columns hold (column, digit) pairs (one MMA per sub-block); from three columns on,
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
-template <int NC, bool TILED>
+// PAIRS: the grouped-expert form (seg.sel set), compiled apart so that the dense matvec carries none of its code.
+template <int NC, bool TILED, bool PAIRS>
 __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
                                                     const uint8_t* __restrict__ xq, float* __restrict__ y_a,
@@ -361,7 +362,17 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     const int rows = second ? seg.rows : rows_a;
     float* __restrict__ y = second ? seg.y : y_a;
     const int64_t ldy = second ? seg.ldy : ldy_a;
-    if (TILED && seg.sel) {
+    if (TILED && seg.sel && !PAIRS) {
+        // (the single-matrix grouped form; launches use the PAIRS instantiation below, this keeps the dense
+        // instantiation's code, and so its register allocation, as it was)
+        pdl_wait();
+        const int pair = (int)blockIdx.x / seg.tiles_per_pair;
+        bx = (int)blockIdx.x % seg.tiles_per_pair;
+        row_base = row_base_a + seg.sel[pair] * rows_a;
+        xq += (int64_t)(seg.x_per_token ? pair / seg.K : pair) * nsb * XP_COL;
+        y = y_a + (int64_t)pair * ldy_a;
+    }
+    if (TILED && PAIRS) {
         // grouped experts: the expert ids come from the router kernel, so wait for it before the first weight copy.
         // With seg.wt the launch covers a second stacked matrix of the same shape (up after gate): its CTAs follow
         // the first matrix's and write seg.y.
@@ -934,7 +945,7 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
     out->valid = true;
 }
 
-template <int NC, bool TILED>
+template <int NC, bool TILED, bool PAIRS = false>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                        float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
@@ -942,12 +953,14 @@ static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base,
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4Layout<NC>::SMEM));
+        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED, PAIRS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Q4Layout<NC>::SMEM));
         attr[dev] = true;
     }
     const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas * (seg.wt ? 2 : 1)
                              : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
-    launch(k_mmv_q4k<NC, TILED>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
+    if (PAIRS != (seg.sel != nullptr)) WL_THROW(WL_EINVAL, "matvec: the grouped-expert form needs the expert ids");
+    launch(k_mmv_q4k<NC, TILED, PAIRS>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
            (const uint8_t*)p.blocks, y, ldy, err, seg);
     note_launch();
 }
@@ -1053,7 +1066,7 @@ void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols,
     const int tiles_per_pair = expert_rows / Q4_ROWS;
     // first_ctas carries the pair count (the CTA count is pairs x tiles per pair)
     const MvSeg seg{nullptr, 0, 0, npairs, nullptr, 0, sel, K, tiles_per_pair, x_per_token ? 1 : 0};
-    launch_q4k<1, true>(none, tiles, row_base, expert_rows, cols / 256, p, y, ldy, err, s, seg);
+    launch_q4k<1, true, true>(none, tiles, row_base, expert_rows, cols / 256, p, y, ldy, err, s, seg);
 }
 
 void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_rows, int cols, const int32_t* sel,
@@ -1068,7 +1081,7 @@ void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_ro
     memset(&none, 0, sizeof none);
     const int tiles_per_pair = expert_rows / Q4_ROWS;
     const MvSeg seg{tiles_b, 0, expert_rows, npairs, yb, ldy, sel, K, tiles_per_pair, 1};
-    launch_q4k<1, true>(none, tiles_a, 0, expert_rows, cols / 256, p, ya, ldy, err, s, seg);
+    launch_q4k<1, true, true>(none, tiles_a, 0, expert_rows, cols / 256, p, ya, ldy, err, s, seg);
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
