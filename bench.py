@@ -138,8 +138,9 @@ def reference_arm(args):
     value = args.steps / sum(per_step)
     out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(per_step) / args.steps,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/f32", "data": "synthetic",
-           "config": {"workload": "decode b1, Llama-3.3-70B-shaped Q4_K_M (configs[3]), CPU", "batch": 1},
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_K/f32", "data": "synthetic",
+           "config": {"workload": "decode b1, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), the reference's CPU "
+                                  "arithmetic (C oracle) on the host cores", "batch": 1, "prompt": args.prompt},
            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
