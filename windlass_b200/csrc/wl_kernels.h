@@ -89,8 +89,15 @@ void xprep(const float* x, int64_t ldx, int cols, int nc, const XPrep& p, cudaSt
 // activations prepared as xprep would (bit-identical), in one kernel. E a multiple of 256, at most 8192.
 bool norm_prep_supported(int E);
 // With ar, o is the rank-ordered sum of every rank's partial in the fused all-reduce's slot instead (o unused).
+// With moe, o is the mixture-of-experts combine of each row's K chosen experts (moe_combine's arithmetic, o unused).
+struct MoeIn {
+    const float* y = nullptr;       // [T*K][E] the chosen experts' outputs, pair t*K + j
+    const int32_t* sel = nullptr;   // [T*K] expert ids
+    const float* wts = nullptr;     // [T*K] weights
+    int K = 0;
+};
 void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
-               cudaStream_t s, const ArIn* ar = nullptr);
+               cudaStream_t s, const ArIn* ar = nullptr, const MoeIn* moe = nullptr);
 // A TMA tensor map over a weight matrix (CUtensorMap, 128 bytes, 64-byte aligned), made once per matrix.
 struct alignas(64) WeightMap {
     uint8_t bytes[128];

@@ -185,10 +185,13 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
 // in double); when prep is given, y's superblocks are also written in k_xprep's layout with the same arithmetic
 // (same maximum, digits, and the same association of the 32-value sums), so the result is bit-identical to
 // rmsnorm followed by k_xprep.
-template <bool RES, bool PREP>
+// MOE: o is not read; each row's o is instead the mixture-of-experts combine of its K chosen experts' outputs (moe.y
+// rows t*K + j, weights moe.wts), added in ascending expert id one rounded multiply and add at a time from zero,
+// k_moe_combine's arithmetic, so the combine needs no launch of its own.
+template <bool RES, bool PREP, bool MOE>
 __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const float* __restrict__ o, float rs,
                                                     int E, const float* __restrict__ w, float eps, float* __restrict__ y,
-                                                    uint8_t* __restrict__ prep, const ArIn ar)
+                                                    uint8_t* __restrict__ prep, const ArIn ar, const MoeIn moe)
 {
     pdl_trigger();
     __shared__ double scratch[32];
@@ -201,7 +204,27 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
     float4 a = *reinterpret_cast<const float4*>(xr), b = *reinterpret_cast<const float4*>(xr + 4);
     if (RES) {
         float4 oa, ob;
-        if (ar.G > 0) {
+        if (MOE) {
+            const int K = moe.K;
+            int order[16];
+            for (int j = 0; j < K; ++j) order[j] = j;
+            for (int a2 = 1; a2 < K; ++a2)
+                for (int b2 = a2; b2 > 0 && moe.sel[t * K + order[b2]] < moe.sel[t * K + order[b2 - 1]]; --b2) {
+                    const int tmp = order[b2]; order[b2] = order[b2 - 1]; order[b2 - 1] = tmp;
+                }
+            float ov[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int j = 0; j < K; ++j) {
+                const int i = t * K + order[j];
+                const float wt = moe.wts[i];
+                const float* yr = moe.y + (int64_t)i * E + i0;
+                const float4 ya = *reinterpret_cast<const float4*>(yr), yb = *reinterpret_cast<const float4*>(yr + 4);
+                const float yv[8] = {ya.x, ya.y, ya.z, ya.w, yb.x, yb.y, yb.z, yb.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ov[e] = __fadd_rn(ov[e], __fmul_rn(wt, yv[e]));
+            }
+            oa = make_float4(ov[0], ov[1], ov[2], ov[3]);
+            ob = make_float4(ov[4], ov[5], ov[6], ov[7]);
+        } else if (ar.G > 0) {
             // the fused all-reduce: every rank's partial of this row (peers' over NVLink), summed in rank order
             const unsigned long long q = ar_seq(ar.epoch, ar.idx);
             ar_sync(ar, q);
@@ -827,8 +850,10 @@ size_t xprep_bytes(int cols, int nc) { return xprep_bytes_c(cols, nc); }
 bool norm_prep_supported(int E) { return E % 256 == 0 && E <= 8192; }
 
 void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w, float eps, float* y, const XPrep* p,
-               cudaStream_t s, const ArIn* ar)
+               cudaStream_t s, const ArIn* ar, const MoeIn* moe)
 {
+    if (moe && (ar || !moe->y || !moe->sel || !moe->wts || moe->K < 1 || moe->K > 16))
+        WL_THROW(WL_EINVAL, "norm_prep: the expert combine takes 1..16 experts per row and no all-reduce");
     if (T <= 0) return;
     if (!norm_prep_supported(E)) WL_THROW(WL_EUNSUPPORTED, "norm_prep: the row length must be a multiple of 256, at most 8192");
     if (p && (p->cols != E || p->nc != T)) WL_THROW(WL_EINVAL, "norm_prep: prepared-activation view does not match");
@@ -841,12 +866,16 @@ void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w,
     }
     uint8_t* pb = p ? p->blocks : nullptr;
     const dim3 grid(T), block(E / 8);
-    if (o || ar) {
-        if (p) launch(k_norm_prep<true, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in);
-        else launch(k_norm_prep<true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in);
+    const MoeIn mi = moe ? *moe : MoeIn{};
+    if (moe) {
+        if (p) launch(k_norm_prep<true, true, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch(k_norm_prep<true, false, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+    } else if (o || ar) {
+        if (p) launch(k_norm_prep<true, true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch(k_norm_prep<true, false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
     } else {
-        if (p) launch(k_norm_prep<false, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in);
-        else launch(k_norm_prep<false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in);
+        if (p) launch(k_norm_prep<false, true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch(k_norm_prep<false, false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
     }
     note_launch();
 }

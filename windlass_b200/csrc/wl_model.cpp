@@ -239,6 +239,7 @@ void Model::begin_step(int T)
     k::embed(embd_.type, embd_.d, embd_.row_bytes, embd_.rows, c_.embd, tok_d_, T, c_.embedding_scale, x_,
              bad_d_, stream_, ar_on_ ? reinterpret_cast<unsigned long long*>(ar_buf_ + k::AR_EPOCH) : nullptr);
     pending_residual_ = false;
+    pending_moe_ = false;
 }
 
 // The cancel flag, polled between stages (Transformer.cs:99,158). Under tensor parallelism the ranks take the maximum
@@ -1106,7 +1107,13 @@ void Model::ffn_moe_device(const LayerW& L, int T)
     k::swiglu_prep(pg_, pu_, NP, X, pp, stream_);
     k::matvec_pairs(L.down_exps.tiles, 0, E, X, sel_, NP, K, false, pp, py_, E, err_d_, stream_);
     profile_end(mark, 12, (double)NP * ((double)L.gate_exps.row_bytes * X * 2 + (double)L.down_exps.row_bytes * E));
-    k::moe_combine(py_, sel_, wts_, T, K, E, o_, stream_);
+    if (k::norm_prep_supported(E) && !c_.post_norms && K <= 16) {
+        // the next norm (the next layer's or the head's) combines the experts' outputs as it adds the residual
+        pending_moe_ = true;
+        moe_in_ = k::MoeIn{py_, sel_, wts_, K};
+    } else {
+        k::moe_combine(py_, sel_, wts_, T, K, E, o_, stream_);
+    }
     prep_x_ = nullptr;
 }
 
@@ -1245,8 +1252,9 @@ void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
         if (prep) p = k::xprep_view(xprep_buf_, E, T);
         k::ArIn ar{};
         const bool fused = pending_residual_ && pending_ar_in(T, 0, &ar);
+        const bool moe = pending_residual_ && pending_moe_;
         k::norm_prep(x_, pending_residual_ ? o_ : nullptr, rs, T, E, w.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_,
-                     fused ? &ar : nullptr);
+                     fused ? &ar : nullptr, moe ? &moe_in_ : nullptr);
         if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = T; }
     } else {
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
@@ -1254,6 +1262,7 @@ void Model::pre_norm(int T, const Vec& w, bool prep_for_mma)
     }
     profile_end(nm, WL_PROFILE_NORM, 0.0);
     pending_residual_ = false;
+    pending_moe_ = false;
 }
 
 // Head (src/Transformer.cs:112-125): final norm and output matrix for rows first..T-1.
@@ -1268,14 +1277,21 @@ void Model::head(int T, int first)
         if (prep) p = k::xprep_view(xprep_buf_, E, n);
         k::ArIn ar{};
         const bool fused = pending_residual_ && pending_ar_in(n, first, &ar);
+        k::MoeIn mi = moe_in_;          // the head's rows first.. take their own pairs
+        mi.y += (int64_t)first * mi.K * E;
+        mi.sel += (int64_t)first * mi.K;
+        mi.wts += (int64_t)first * mi.K;
+        const bool moe = pending_residual_ && pending_moe_;
         k::norm_prep(x_ + (int64_t)first * E, pending_residual_ ? o_ + (int64_t)first * E : nullptr, rs, n, E,
-                     out_norm_.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_, fused ? &ar : nullptr);
+                     out_norm_.d, c_.rms_eps, xn_, prep ? &p : nullptr, stream_, fused ? &ar : nullptr,
+                     moe ? &mi : nullptr);
         if (prep) { prep_x_ = xn_; prep_cols_ = E; prep_nc_ = n; }
     } else {
         if (pending_residual_) k::residual(x_, o_, rs, (int64_t)T * E, stream_);
         k::rmsnorm(x_ + (int64_t)first * E, n, E, out_norm_.d, c_.rms_eps, xn_, stream_);
     }
     pending_residual_ = false;
+    pending_moe_ = false;
     if (comm_) {
         // this rank's vocabulary rows, then every rank's gathered and laid out as [n][vocab]
         matmul(output_, xn_, n, logits_part_, 0, true, vocab_part_);

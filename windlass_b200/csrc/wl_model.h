@@ -296,6 +296,8 @@ private:
     const float* prep_x_ = nullptr;
     int prep_cols_ = 0, prep_nc_ = 0;
     bool pending_residual_ = false;     // x += o_ not yet applied (done by the next norm)
+    bool pending_moe_ = false;          // ... and o_ is the expert combine of moe_in_, computed by that norm
+    k::MoeIn moe_in_{};
     // CUDA graphs of decode steps
     bool use_graphs_ = true;
     std::vector<GraphEntry> graphs_;
