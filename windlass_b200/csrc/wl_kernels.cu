@@ -1294,7 +1294,8 @@ void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned
 // 0, 1, ... in order: NaNs rank by id.) The chosen sum is added in pick order and the renormalisation divides by it
 // clamped at 6.103515625e-5, as the reference does.
 __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int n, int k, int renorm,
-                                               int32_t* __restrict__ sel, float* __restrict__ wts)
+                                               int32_t* __restrict__ sel, float* __restrict__ wts,
+                                               unsigned long long* __restrict__ count)
 {
     __shared__ float p[256];
     __shared__ float red[8];
@@ -1341,14 +1342,18 @@ __global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits,
         for (int j = 0; j < k; ++j) chosen = __fadd_rn(chosen, picked[j]);
         const float div = isnan(chosen) ? chosen : fmaxf(chosen, 6.103515625e-5f);
         for (int j = 0; j < k; ++j) wts[(int64_t)t * k + j] = renorm ? __fdiv_rn(picked[j], div) : picked[j];
+        if (count) *count += (unsigned long long)k;     // one token: its k picks are k distinct experts
     }
 }
 
-void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s)
+void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s,
+           unsigned long long* count_one)
 {
     if (T <= 0) return;
     if (n <= 0 || n > 256 || k <= 0 || k > 32 || k > n) WL_THROW(WL_EUNSUPPORTED, "route: 1..256 experts, 1..32 chosen");
-    launch(k_route, dim3((unsigned)T), dim3((unsigned)((n + 31) / 32 * 32)), 0, s, logits, n, k, renorm, sel, wts);
+    if (count_one && T != 1) WL_THROW(WL_EINVAL, "route: the expert count of one token only");
+    launch(k_route, dim3((unsigned)T), dim3((unsigned)((n + 31) / 32 * 32)), 0, s, logits, n, k, renorm, sel, wts,
+           count_one);
     launched();
 }
 

@@ -213,7 +213,10 @@ void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned
 // Blocks per row of that launch (for tests of its arithmetic).
 int64_t argmax_blocks(int V, int n);
 // Route (Transformer.cs:315-340) for T rows of n router logits: sel[t*k+j], wts[t*k+j].
-void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s);
+// With count_one (T = 1 only), *count_one += k: a single token's picks are k distinct experts, so the step needs no
+// count_experts launch.
+void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, float* wts, cudaStream_t s,
+           unsigned long long* count_one = nullptr);
 // outp[t*E + d] += w * ye[i*E + d] for the gathered rows i of one expert (MoeFfn, Transformer.cs:289-293).
 void scatter_add(float* outp, const float* ye, const int32_t* toks, const float* w, int n, int E, cudaStream_t s);
 // xe[i*E..] = xn[toks[i]*E..].

@@ -1099,8 +1099,9 @@ void Model::ffn_moe_device(const LayerW& L, int T)
     }
     const k::XPrep px = k::xprep_view(xprep_buf_, E, T);        // xn_, prepared by the ffn norm
     matmul(L.router, xn_, T, router_);
-    k::route(router_, T, c_.expert_count, K, c_.expert_weights_norm ? 1 : 0, sel_, wts_, stream_);
-    k::count_experts(sel_, NP, expert_count_d_, stream_);
+    k::route(router_, T, c_.expert_count, K, c_.expert_weights_norm ? 1 : 0, sel_, wts_, stream_,
+             T == 1 ? expert_count_d_ : nullptr);
+    if (T > 1) k::count_experts(sel_, NP, expert_count_d_, stream_);
     const int mark = profile_begin();
     k::matvec_pairs2(L.gate_exps.tiles, L.up_exps.tiles, X, E, sel_, NP, K, px, pg_, pu_, X, err_d_, stream_);
     const k::XPrep pp = k::xprep_view(pprep_, X, NP);
