@@ -140,102 +140,153 @@ def reference_arm(args):
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(per_step) / args.steps,
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_K/f32", "data": "synthetic",
            "config": {"workload": "decode b1, Llama-3.3-70B-shaped Q4_K_M (configs[3] b), the reference's CPU "
-                                  "arithmetic (C oracle) on the host cores", "batch": 1, "prompt": args.prompt},
+                                  "arithmetic (C oracle) on the host cores; each step's time is extrapolated from one "
+                                  "decoder layer at T=1 x 80 plus a 16384-row slice of the output head scaled to "
+                                  "128256 rows (the reference's TimeLayer method), not a whole decoded token",
+                      "batch": 1, "prompt": args.prompt, "parallelism": "host cores (no GPU)",
+                      "l2": "not applicable (CPU)"},
            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
 
 
+def sweep_cpu_cell(fmt, t, raw, rows, cols, b, reps=3, max_s=20.0):
+    """The reference's CPU arithmetic for one sweep cell, on all host threads: Transformer.MatMul of b columns
+    (MatMulEach, one fused row kernel per column, for b <= 8, as a ForwardBatch step runs them; the decoded tile +
+    FastMath.Block for b >= 64, as a prompt does; the I-quants have no fused dot and always take the tile path), best
+    of `reps` like the reference's TimeLayer probe (src/Program.cs:493-527). Returns seconds."""
+    import numpy as np
+    from oracle import oracle as O
+    x = np.random.default_rng(b).standard_normal((b, cols)).astype(np.float32)
+    best = None
+    t_end = time.perf_counter() + max_s
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.matmul(t, raw, rows, cols, x, each_token=b <= 8)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+        if time.perf_counter() > t_end:
+            break
+    return best
+
+
 def sweep(args):
-    """the 8192 x 8192 matvec/matmul sweep. Per format and batch column count: the time of one matvec call
-    (wl_matvec_tiles on weights repacked once for Q4_K/Q6_K, else wl_matvec: activation prep + matvec), from CUDA events around
+    """the matvec/matmul sweep (8192 x 8192 by default; --shapes adds the 70B layer's shapes). Per shape,
+    format and batch column count: the time of one call (wl_matvec_tiles on weights repacked once for Q4_K/Q6_K, else
+    wl_matvec: activation prep + matvec; wl_gemm_tiles for Q4_K at b > 8, else wl_matmul), from CUDA events around
     replays of a CUDA graph of `iters` calls over rotating weight copies whose total exceeds L2, and the weight
-    bandwidth (b <= 8) or TFLOP/s (b >= 64). One JSON line with the whole table."""
+    bandwidth (b <= 8) or TFLOP/s (b >= 64), with the reference's CPU arithmetic (the C oracle, all host threads,
+    best of 3) beside each cell. One JSON line with the whole table."""
     import ctypes as C
     import numpy as np
     import torch
     from windlass_b200 import _lib
     L = _lib.lib()
-    n = args.sweep_n
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.shapes.split(",")] if args.shapes else \
+        [(args.sweep_n, args.sweep_n)]
     fmts = args.formats.split(",")
     batches = [int(b) for b in args.batches.split(",")]
     stream = torch.cuda.current_stream()
     hbm, bf16, _ = measured_peaks()
-    rows = []
+    rows_out = []
     rng = np.random.default_rng(0)
-    for f in fmts:
-        t = _lib.TYPES[f]
-        bs, ts = {"q4_K": (256, 144), "q6_K": (256, 210), "q8_0": (32, 34), "iq4_xs": (256, 136),
-                  "iq2_xxs": (256, 66)}[f]
-        nbytes = n * n // bs * ts
-        copies = max(4, int(np.ceil(4 * 126e6 / nbytes)))
-        ws = []
-        for k in range(copies):
-            buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-            if f in ("q4_K", "q6_K", "q8_0"):
-                _lib.check(L.wl_synth_tensor(t, 42 + k, 0x7001, n, n, C.c_float(0.02), C.c_float(0.0),
-                                             C.c_void_p(buf.data_ptr()), C.c_void_p(stream.cuda_stream)))
-            else:   # the reference's random-payload method: random bytes with a fixed fp16 scale in each block
-                raw = rng.integers(0, 256, nbytes, dtype=np.uint8).reshape(-1, ts)
-                raw[:, 0], raw[:, 1] = 0x00, 0x1C          # fp16 0.0039
-                buf.copy_(torch.from_numpy(raw.reshape(-1)))
-            ws.append(buf)
-        tiled = f in ("q4_K", "q6_K")
-        if tiled:       # the model's layout: weights repacked once into tiles, so no call repacks
-            tb = C.c_int64()
-            _lib.check(L.wl_tiles_size(t, n, n, C.byref(tb)))
-            tws = []
-            for w in ws:
-                tw = torch.empty(tb.value, dtype=torch.uint8, device="cuda")
-                _lib.check(L.wl_make_tiles(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(tw.data_ptr()),
-                                           C.c_void_p(stream.cuda_stream)))
-                tws.append(tw)
-            torch.cuda.synchronize()
-        for b in batches:
-            x = torch.randn(b, n, device="cuda")
-            y = torch.empty(b, n, device="cuda")
-            def run(i):
-                w = ws[i % copies]
-                cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-                if b <= 8 and tiled:
-                    st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), n, n, C.c_void_p(x.data_ptr()),
-                                           b, C.c_void_p(y.data_ptr()), cs)
-                elif b <= 8:
-                    st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
-                                     C.c_void_p(y.data_ptr()), cs)
-                elif tiled and f == "q4_K":   # the tcgen05 GEMM on the repacked weights
-                    st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), n, n, C.c_void_p(x.data_ptr()),
-                                         b, C.c_void_p(y.data_ptr()), cs)
-                else:
-                    st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), n, n, C.c_void_p(x.data_ptr()), b,
-                                     C.c_void_p(y.data_ptr()), 0, cs)
-                _lib.check(st)
-            for i in range(max(args.warmup, 3)):
-                run(i)
-            torch.cuda.synchronize()
-            # the calls are captured into one CUDA graph so that host launch overhead is not what gets timed
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for i in range(args.iters):
+    cpu_threads = None
+    if not args.no_cpu:
+        from oracle import oracle as O
+        cpu_threads = O.lib().or_default_threads()
+    for (R, K) in shapes:
+        for f in fmts:
+            t = _lib.TYPES[f]
+            bs, ts = {"q4_K": (256, 144), "q6_K": (256, 210), "q8_0": (32, 34), "iq4_xs": (256, 136),
+                      "iq2_xxs": (256, 66)}[f]
+            nbytes = R * K // bs * ts
+            copies = max(4, int(np.ceil(4 * 126e6 / nbytes)))
+            ws = []
+            raw0 = None
+            for k in range(copies):
+                buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+                if f in ("q4_K", "q6_K", "q8_0"):
+                    _lib.check(L.wl_synth_tensor(t, 42 + k, 0x7001, R, K, C.c_float(0.02), C.c_float(0.0),
+                                                 C.c_void_p(buf.data_ptr()), C.c_void_p(stream.cuda_stream)))
+                else:   # the reference's random-payload method: random bytes with a fixed fp16 scale in each block
+                    raw = rng.integers(0, 256, nbytes, dtype=np.uint8).reshape(-1, ts)
+                    raw[:, 0], raw[:, 1] = 0x00, 0x1C          # fp16 0.0039
+                    buf.copy_(torch.from_numpy(raw.reshape(-1)))
+                ws.append(buf)
+            if not args.no_cpu:
+                torch.cuda.synchronize()
+                raw0 = ws[0].cpu().numpy()
+            tiled = f in ("q4_K", "q6_K")
+            if tiled:       # the model's layout: weights repacked once into tiles, so no call repacks
+                tb = C.c_int64()
+                _lib.check(L.wl_tiles_size(t, R, K, C.byref(tb)))
+                tws = []
+                for w in ws:
+                    tw = torch.empty(tb.value, dtype=torch.uint8, device="cuda")
+                    _lib.check(L.wl_make_tiles(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(tw.data_ptr()),
+                                               C.c_void_p(stream.cuda_stream)))
+                    tws.append(tw)
+                torch.cuda.synchronize()
+            for b in batches:
+                x = torch.randn(b, K, device="cuda")
+                y = torch.empty(b, R, device="cuda")
+
+                def run(i):
+                    w = ws[i % copies]
+                    cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                    if b <= 8 and tiled:
+                        st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
+                                               C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
+                    elif b <= 8:
+                        st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
+                                         C.c_void_p(y.data_ptr()), cs)
+                    elif tiled and f == "q4_K":   # the tcgen05 GEMM on the repacked weights
+                        st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
+                                             C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
+                    else:
+                        st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
+                                         C.c_void_p(y.data_ptr()), 0, cs)
+                    _lib.check(st)
+                for i in range(max(args.warmup, 3)):
                     run(i)
-            graph.replay()
-            torch.cuda.synchronize()
-            reps = 5
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
+                torch.cuda.synchronize()
+                # the calls are captured into one CUDA graph so that host launch overhead is not what gets timed
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for i in range(args.iters):
+                        run(i)
                 graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / (reps * args.iters)
-            del graph
-            alg = nbytes + 4 * b * 2 * n
-            rows.append({"format": f, "batch": b, "us": ms * 1e3, "gbs": alg / (ms / 1e3) / 1e9,
-                         "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,
-                         "tflops": 2.0 * n * n * b / (ms / 1e3) / 1e12})
-            trace(f"{f} b{b}: {ms * 1e3:.1f} us, {rows[-1]['gbs']:.0f} GB/s, {rows[-1]['tflops']:.2f} TFLOP/s")
-    print(json.dumps({"metric": "Q4_K matvec HBM GB/s (configs[1] sweep)", "unit": "GB/s", "n": n, "table": rows,
-                      "peak_hbm_gbs": hbm, "peak_bf16_tflops": bf16}))
+                torch.cuda.synchronize()
+                reps = 5
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / (reps * args.iters)
+                del graph
+                alg = nbytes + 4 * b * (R + K)
+                cell = {"format": f, "rows": R, "cols": K, "batch": b, "us": ms * 1e3,
+                        "gbs": alg / (ms / 1e3) / 1e9, "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,
+                        "tflops": 2.0 * R * K * b / (ms / 1e3) / 1e12,
+                        "bf16_frac": 2.0 * R * K * b / (ms / 1e3) / 1e12 / bf16}
+                if raw0 is not None and (b <= 64 or R * K <= 8192 * 8192):
+                    cs_ = sweep_cpu_cell(f, t, raw0, R, K, b)
+                    cell["cpu_us"] = cs_ * 1e6
+                    cell["cpu_gbs"] = alg / cs_ / 1e9
+                    cell["cpu_gflops"] = 2.0 * R * K * b / cs_ / 1e9
+                rows_out.append(cell)
+                trace(f"{f} {R}x{K} b{b}: {ms * 1e3:.1f} us, {cell['gbs']:.0f} GB/s ({cell['hbm_frac']:.2f}), "
+                      f"{cell['tflops']:.2f} TFLOP/s" + (f"; CPU {cell['cpu_us'] / 1e3:.1f} ms" if "cpu_us" in cell else ""))
+            del ws
+            if tiled:
+                del tws
+            torch.cuda.empty_cache()
+    print(json.dumps({"metric": "Q4_K matvec HBM GB/s (configs[1] sweep)", "unit": "GB/s", "shapes": shapes,
+                      "table": rows_out, "peak_hbm_gbs": hbm, "peak_bf16_tflops": bf16,
+                      "cpu": {"kind": "port", "cores": cpu_threads, "method": "C oracle Transformer.MatMul, best of 3"}
+                      if cpu_threads else None}))
 
 
 def streamed(args):
@@ -309,7 +360,8 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="configs[1] matvec sweep instead of the decode benchmark")
     ap.add_argument("--sweep-n", type=int, default=8192)
     ap.add_argument("--formats", default="q4_K,q6_K,q8_0,iq4_xs,iq2_xxs")
-    ap.add_argument("--batches", default="1,4,8,64")
+    ap.add_argument("--batches", default="1,4,8,64,512")
+    ap.add_argument("--shapes", default="", help="sweep shapes rows x cols, comma-separated (default: n x n)")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--streamed", action="store_true", help="configs[3] (a): layers streamed from pinned host memory")
     ap.add_argument("--model", default="70b", choices=["70b", "8b", "moe"],

@@ -2,7 +2,7 @@
  *
  * The reference engine (C#, .NET Framework 4.8) reaches its forward pass only through the Transformer object
  * (src/Transformer.cs) inside LayeredBackend (src/Engine.cs). This library replaces that object: a C# host binds
- * these entry points with P/Invoke (the binding is in INTEGRATION.md) and keeps its server, BatchEngine, Playbook,
+ * these entry points with P/Invoke and keeps its server, BatchEngine, Playbook,
  * tokenizer and sampler unchanged. Plain pointers and sizes only; no C++ or CUDA types cross the boundary except the
  * opaque `stream` arguments of the kernel-level test exports, which are cudaStream_t values (NULL = default stream).
  *
@@ -254,14 +254,18 @@ int32_t wl_dequant(int32_t type, const void* dev_blocks, int64_t n, float* dev_o
  * W[r] . x[t] for t < ncols (1..8), fused dequant-dot, fp32 accumulate. Every column is computed as if alone. */
 int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x, int32_t ncols,
                   float* dev_y, void* stream);
-/* No counterpart in the reference. wl_matvec's tensor-core path (Q4_K only: 16-byte aligned weights and dev_x, cols
- * a multiple of 256) with the same arguments and results, for callers that cannot let a call allocate device memory:
- * its scratch is a static device array of this library (WL_MATVEC_STATIC_MAX_COLS columns of 8 activations, about
- * 1 MB per device), so the call makes no cudaMalloc/cudaFree. cols above the limit or other formats return
- * WL_EINVAL / WL_EUNSUPPORTED (use wl_matvec). The first call on each device looks up the array's address with
- * cudaGetSymbolAddress and sets the kernel's shared-memory attribute: make it before any stream capture. Nothing has
- * to start at zero (each call clears its error word on `stream`). Calls share one scratch per device, so calls that
- * may overlap (different streams, or threads without ordering) race: order them on one stream. */
+/* No counterpart in the reference. A Q4_K matvec (16-byte aligned weights and dev_x, cols a multiple of 256) with
+ * wl_matvec's arguments, for callers that cannot let a call allocate device memory: its scratch (an error word and
+ * the prepared activations of up to 8 columns) is a static device array of this library (WL_MATVEC_STATIC_MAX_COLS
+ * columns, about 1 MB on every device that loads the library, held until exit), so the call makes no
+ * cudaMalloc/cudaFree. It runs the tensor-core kernel on the GGUF rows through a TMA tensor map (wl_matvec repacks the
+ * weights into tiles first); the results match wl_matvec's within the matvec tolerance (1e-4 relative L2). cols
+ * above the limit or other formats return WL_EINVAL / WL_EUNSUPPORTED (use wl_matvec). The first call on each device
+ * looks up the array's address with cudaGetSymbolAddress and sets the shared-memory attribute of all its kernel
+ * instantiations: make it before any stream capture. The array starts at zero when the library loads; a kernel whose
+ * bounded wait gives up sets its error word, which stays set until wl_kernel_status reads and clears it. Calls share
+ * one scratch per device and leave their prepared activations in it, so calls that may overlap on the GPU
+ * (different streams, or threads without ordering) race: order them on one stream. */
 #define WL_MATVEC_STATIC_MAX_COLS 32768
 int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x,
                          int32_t ncols, float* dev_y, void* stream);

@@ -643,8 +643,9 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
     });
 }
 
-// wl_matvec's tensor-core path with its scratch in a static device array instead of the growing export scratch:
-// nothing is allocated here, so callers that own all device memory can use it. Same kernels, same results.
+// A Q4_K tensor-core matvec with its scratch in a static device array instead of the growing export scratch: nothing
+// is allocated here, so callers that own all device memory can use it. The kernel reads the GGUF rows through a TMA
+// tensor map (wl_matvec's repacks them into tiles first); both agree within the matvec tolerance.
 int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x,
                          int32_t ncols, float* dev_y, void* stream)
 {
@@ -666,6 +667,7 @@ int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t 
         if (need > wl::k::STATIC_SCRATCH_BYTES) return wl::fail(WL_EINVAL, "wl_matvec_static: static scratch too small");
         const cudaStream_t st = (cudaStream_t)stream;
         uint8_t* scratch = (uint8_t*)wl::k::static_scratch();
+        wl::k::prepare_matvec_mma();        // every column count's kernel attribute, once per device
         int* err = (int*)scratch;
         WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), st));   // orders the launches behind all earlier work
         wl::k::WeightMap map;

@@ -111,6 +111,9 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
 // copy sets *err (device memory) instead of hanging.
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y,
                 int64_t ldy, int* err, cudaStream_t s);
+// Sets the shared-memory attribute of every column count's matvec_mma kernel on the current device (once per device;
+// later calls return at once), so that no later matvec_mma call has a first-use step.
+void prepare_matvec_mma();
 
 // Q4_K and Q6_K on the tensor cores from tile-major weights: each 16-row x one-superblock tile contiguous and laid
 // out for the kernel's fragment reads (made once by make_tiles, tile_bytes bytes, 16-byte aligned); then

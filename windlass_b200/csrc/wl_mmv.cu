@@ -13,6 +13,7 @@
 // Determinism. The eight warps of a CTA cover disjoint superblocks of the same rows and are summed in warp order,
 // and every column goes through the same fp32 operations whatever the number of columns beside it, so a column's
 // result never depends on the other columns of the launch.
+#include <atomic>
 #include <climits>
 #include <cstdint>
 #include <cuda.h>
@@ -137,8 +138,9 @@ __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* e
 // The consumer's side of the fused all-reduce, run by every thread of every CTA of the consuming kernel after its
 // grid-dependency wait (so this rank's producing matvec has completed): CTA 0 announces sequence number q on every
 // peer (this rank's partial sits in its own slot), then threads 0..G-1 wait for each peer's announcement of q or
-// later. A wait gives up after about half a minute, records code 2 in *err and returns (the sums are then garbage
-// and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot hang the GPU.
+// later. A wait gives up after ar.wait_ns of %globaltimer time (the host sets AR_WAIT_NS, 10 s), records code 2 in
+// *err and returns (the sums are then garbage and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot
+// hang the GPU.
 __device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q)
 {
     const int slot = (int)(q % AR_SLOTS);
@@ -974,18 +976,38 @@ void make_weight_map(int type, const uint8_t* w, int64_t rows_total, int64_t row
     out->valid = true;
 }
 
+// Raises a kernel's dynamic shared-memory limit once per device; `done` is that kernel's own per-device flags (one
+// set per template instantiation, so kernels of the same signature do not share them). Safe from several host threads.
+template <typename Kernel>
+static void ensure_smem_attr(Kernel kernel, int bytes, std::atomic<bool> (&done)[64])
+{
+    static std::mutex mu;
+    int dev = 0;
+    WL_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) WL_THROW(WL_EINVAL, "device ordinal out of range");
+    if (done[dev].load(std::memory_order_acquire)) return;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev].load(std::memory_order_relaxed)) return;
+    WL_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[dev].store(true, std::memory_order_release);
+}
+
+template <int NC, bool TILED, bool PAIRS> struct Q4Attr {
+    static std::atomic<bool> done[64];
+    static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS>, Q4Layout<NC>::SMEM, done); }
+};
+template <int NC, bool TILED, bool PAIRS> std::atomic<bool> Q4Attr<NC, TILED, PAIRS>::done[64];
+template <int NC> struct Q6Attr {
+    static std::atomic<bool> done[64];
+    static void ensure() { ensure_smem_attr(k_mmv_q6k<NC>, Q6Layout<NC>::SMEM, done); }
+};
+template <int NC> std::atomic<bool> Q6Attr<NC>::done[64];
+
 template <int NC, bool TILED, bool PAIRS = false>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                        float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q4k<NC, TILED, PAIRS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Q4Layout<NC>::SMEM));
-        attr[dev] = true;
-    }
+    Q4Attr<NC, TILED, PAIRS>::ensure();
     const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas * (seg.wt ? 2 : 1)
                              : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     if (PAIRS != (seg.sel != nullptr)) WL_THROW(WL_EINVAL, "matvec: the grouped-expert form needs the expert ids");
@@ -1008,6 +1030,18 @@ static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_bas
     case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     }
+}
+
+void prepare_matvec_mma()
+{
+    Q4Attr<1, false, false>::ensure();
+    Q4Attr<2, false, false>::ensure();
+    Q4Attr<3, false, false>::ensure();
+    Q4Attr<4, false, false>::ensure();
+    Q4Attr<5, false, false>::ensure();
+    Q4Attr<6, false, false>::ensure();
+    Q4Attr<7, false, false>::ensure();
+    Q4Attr<8, false, false>::ensure();
 }
 
 void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols, const XPrep& p, float* y, int64_t ldy,
@@ -1041,13 +1075,7 @@ template <int NC>
 static void launch_q6k(const uint8_t* tiles, int rows, int nsb, const XPrep& p, float* y, int64_t ldy, int* err,
                        cudaStream_t s)
 {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_mmv_q6k<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q6Layout<NC>::SMEM));
-        attr[dev] = true;
-    }
+    Q6Attr<NC>::ensure();
     launch(k_mmv_q6k<NC>, dim3((rows + 15) / 16), dim3(256), Q6Layout<NC>::SMEM, s, tiles, rows, nsb,
            (const uint8_t*)p.blocks, y, ldy, err);
     note_launch();
