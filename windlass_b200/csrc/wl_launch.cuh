@@ -34,5 +34,27 @@ inline void launch(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaS
     WL_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...));
 }
 
+// The same with thread-block clusters of cluster_x CTAs along x (gridDim.x a multiple of cluster_x).
+template <typename... P, typename... A>
+inline void launch_cluster(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster_x,
+                           A&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    WL_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...));
+}
+
 }  // namespace k
 }  // namespace wl

@@ -117,6 +117,20 @@ __device__ __forceinline__ double block_sum_d(double v, double* scratch)
     return s;
 }
 
+// ---- thread-block cluster helpers ----
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// A double in the shared memory of CTA `rank` of this cluster, at the address p has in this CTA.
+__device__ __forceinline__ double ld_cluster_f64(const double* p, uint32_t rank)
+{
+    uint32_t ra;
+    double v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(ra) : "memory");
+    return v;
+}
+
 // ---- fused tensor-parallel all-reduce (layout and protocol in wl_kernels.h) ----
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
 {
@@ -136,15 +150,15 @@ __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* e
 }
 
 // The consumer's side of the fused all-reduce, run by every thread of every CTA of the consuming kernel after its
-// grid-dependency wait (so this rank's producing matvec has completed): CTA 0 announces sequence number q on every
+// grid-dependency wait (so this rank's producing matvec has completed): one CTA announces sequence number q on every
 // peer (this rank's partial sits in its own slot), then threads 0..G-1 wait for each peer's announcement of q or
 // later. A wait gives up after ar.wait_ns of %globaltimer time (the host sets AR_WAIT_NS, 10 s), records code 2 in
 // *err and returns (the sums are then garbage and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot
 // hang the GPU.
-__device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q)
+__device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q, bool announcer)
 {
     const int slot = (int)(q % AR_SLOTS);
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (announcer && threadIdx.x == 0) {
         __threadfence_system();
         for (int g = 0; g < ar.G; ++g)
             if (g != ar.rank) st_release_sys(ar.peer_flags[g] + slot * AR_MAX_RANKS + ar.rank, q);
@@ -182,23 +196,28 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
 // ------------------------------------------------------------------------------------------------------------------
 // residual + RmsNorm + activation prep in one pass
 // ------------------------------------------------------------------------------------------------------------------
-// One CTA per row, E/8 threads: warp w owns the 256 values of superblock w, a lane 8 consecutive values.
+// A cluster of gridDim.x CTAs per row (row blockIdx.y): CTA r of the cluster owns superblocks r*W .. r*W+W-1 of the
+// row (W = blockDim.x / 32), warp w superblock r*W + w, a lane 8 consecutive values. Spreading a row over several SMs
+// spreads its loads, and under tensor parallelism each CTA pulls only its own slice of every peer's partial.
 // x += o * rs (Transformer.cs:225,231) when o is given; y = RmsNormRows(x) * w (Transformer.cs:454-464, sum of squares
-// in double); when prep is given, y's superblocks are also written in k_xprep's layout with the same arithmetic
-// (same maximum, digits, and the same association of the 32-value sums), so the result is bit-identical to
-// rmsnorm followed by k_xprep.
+// in double: lanes by xor butterfly, then warps in order, then the cluster's CTAs in order, through distributed
+// shared memory, so every CTA of the row gets the same sum); when prep is given, y's superblocks are also written in
+// k_xprep's layout with the same arithmetic (same maximum, digits, and the same association of the 32-value sums),
+// so the result is bit-identical to rmsnorm followed by k_xprep.
 // MOE: o is not read; each row's o is instead the mixture-of-experts combine of its K chosen experts' outputs (moe.y
 // rows t*K + j, weights moe.wts), added in ascending expert id one rounded multiply and add at a time from zero,
 // k_moe_combine's arithmetic, so the combine needs no launch of its own.
 template <bool RES, bool PREP, bool MOE>
-__global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const float* __restrict__ o, float rs,
-                                                    int E, const float* __restrict__ w, float eps, float* __restrict__ y,
-                                                    uint8_t* __restrict__ prep, const ArIn ar, const MoeIn moe)
+__global__ void __launch_bounds__(256) k_norm_prep(float* __restrict__ x, const float* __restrict__ o, float rs,
+                                                   int E, const float* __restrict__ w, float eps, float* __restrict__ y,
+                                                   uint8_t* __restrict__ prep, const ArIn ar, const MoeIn moe)
 {
     pdl_trigger();
-    __shared__ double scratch[32];
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i0 = warp * 256 + lane * 8;
+    __shared__ double wsum[8];
+    __shared__ double cta_sum, row_sum;
+    const int t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int C = gridDim.x, sb = blockIdx.x * nw + warp;
+    const int i0 = sb * 256 + lane * 8;
     // the norm weights are written by no kernel: fetch them before waiting for the previous one
     const float4 wa = *reinterpret_cast<const float4*>(w + i0), wb = *reinterpret_cast<const float4*>(w + i0 + 4);
     pdl_wait();
@@ -229,7 +248,7 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
         } else if (ar.G > 0) {
             // the fused all-reduce: every rank's partial of this row (peers' over NVLink), summed in rank order
             const unsigned long long q = ar_seq(ar.epoch, ar.idx);
-            ar_sync(ar, q);
+            ar_sync(ar, q, blockIdx.x == 0 && blockIdx.y == 0);
             const size_t off = ((size_t)(q % AR_SLOTS) * AR_COLS + ar.row0 + t) * (size_t)E + i0;
             oa = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off));
             ob = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off + 4));
@@ -255,8 +274,26 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
     double ss = 0;
 #pragma unroll
     for (int k2 = 0; k2 < 8; ++k2) ss += (double)v[k2] * (double)v[k2];
-    ss = block_sum_d(ss, scratch);
-    const float mean = (float)(ss / E);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) wsum[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double cs = 0;
+        for (int i = 0; i < nw; ++i) cs += wsum[i];
+        cta_sum = cs;
+    }
+    // every CTA's partial in place (and every CTA of the cluster running) before any reads another's
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    if (threadIdx.x == 0) {
+        double tot = 0;
+        for (int r = 0; r < C; ++r) tot += ld_cluster_f64(&cta_sum, (uint32_t)r);
+        row_sum = tot;
+    }
+    cluster_arrive_relaxed();       // this CTA is done with the others' shared memory (waited for before exit)
+    __syncthreads();
+    const float mean = (float)(row_sum / E);
     const float scale = __fdiv_rn(1.0f, (float)sqrt((double)__fadd_rn(mean, eps)));
     const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
     float f[8];
@@ -265,54 +302,56 @@ __global__ void __launch_bounds__(1024) k_norm_prep(float* __restrict__ x, const
     float* yr = y + (int64_t)t * E + i0;
     *reinterpret_cast<float4*>(yr) = make_float4(f[0], f[1], f[2], f[3]);
     *reinterpret_cast<float4*>(yr + 4) = make_float4(f[4], f[5], f[6], f[7]);
-    if (!PREP) return;
-    float m = 0.f;
+    if (PREP) {
+        float m = 0.f;
 #pragma unroll
-    for (int k2 = 0; k2 < 8; ++k2) m = fmaxf(m, fabsf(f[k2]));
+        for (int k2 = 0; k2 < 8; ++k2) m = fmaxf(m, fabsf(f[k2]));
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const bool finite = m <= 3.4e38f;
-    int e = 0;
-    if (m > 0.f && finite) frexpf(m, &e);
-    e = e < -100 ? -100 : e > 100 ? 100 : e;
-    const float up = ldexpf(1.0f, 20 - e), sup = ldexpf(1.0f, 10 - e);
-    const int nsb = E / 256;
-    uint8_t* blk = prep + ((int64_t)t * nsb + warp) * XP_COL;
-    uint32_t dg[3][2] = {};
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const bool finite = m <= 3.4e38f;
+        int e = 0;
+        if (m > 0.f && finite) frexpf(m, &e);
+        e = e < -100 ? -100 : e > 100 ? 100 : e;
+        const float up = ldexpf(1.0f, 20 - e), sup = ldexpf(1.0f, 10 - e);
+        const int nsb = E / 256;
+        uint8_t* blk = prep + ((int64_t)t * nsb + sb) * XP_COL;
+        uint32_t dg[3][2] = {};
 #pragma unroll
-    for (int k2 = 0; k2 < 8; ++k2) {
-        const int X = finite ? __float2int_rn(f[k2] * up) : 0;
-        const int x2 = ((X + 64) & 127) - 64;
-        const int r = (X - x2) >> 7;
-        const int x1 = ((r + 64) & 127) - 64;
-        const int x0 = (r - x1) >> 7;
-        dg[0][k2 >> 2] |= (uint32_t)(x0 & 0xFF) << (8 * (k2 & 3));
-        dg[1][k2 >> 2] |= (uint32_t)(x1 & 0xFF) << (8 * (k2 & 3));
-        dg[2][k2 >> 2] |= (uint32_t)(x2 & 0xFF) << (8 * (k2 & 3));
+        for (int k2 = 0; k2 < 8; ++k2) {
+            const int X = finite ? __float2int_rn(f[k2] * up) : 0;
+            const int x2 = ((X + 64) & 127) - 64;
+            const int r = (X - x2) >> 7;
+            const int x1 = ((r + 64) & 127) - 64;
+            const int x0 = (r - x1) >> 7;
+            dg[0][k2 >> 2] |= (uint32_t)(x0 & 0xFF) << (8 * (k2 & 3));
+            dg[1][k2 >> 2] |= (uint32_t)(x1 & 0xFF) << (8 * (k2 & 3));
+            dg[2][k2 >> 2] |= (uint32_t)(x2 & 0xFF) << (8 * (k2 & 3));
+        }
+#pragma unroll
+        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint2*>(blk + d * XP_DIGIT + 8 * lane) = make_uint2(dg[d][0], dg[d][1]);
+        if (lane < 8) {
+#pragma unroll
+            for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * lane) = 0u;
+        }
+        // 16- and 32-value sums with k_xprep's association: (g0+g1) per lane, then lanes xor 1 (16 values), then xor 2
+        float sm = __fadd_rn(__fadd_rn(f[0] * sup, f[1] * sup), __fadd_rn(f[2] * sup, f[3] * sup));
+        const float s1 = __fadd_rn(__fadd_rn(f[4] * sup, f[5] * sup), __fadd_rn(f[6] * sup, f[7] * sup));
+        sm = __fadd_rn(sm, s1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        const float s16 = sm, s16_next = __shfl_down_sync(0xffffffffu, sm, 2);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        const float s_next = __shfl_down_sync(0xffffffffu, sm, 4);
+        uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
+        if ((lane & 7) == 0) xp_store_pair(rec, 2 * (lane >> 3), 2 * (lane >> 3) + 1, sm, s_next);
+        if ((lane & 3) == 0) {
+            const int p = lane >> 2, c = p & 3, upper = p >> 2;
+            xp_store_pair(rec, XP_S16 + 4 * c + upper, XP_S16 + 4 * c + 2 + upper, s16, s16_next);
+        }
+        if (lane == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
+        if (lane >= 9 && lane < XP_S16) rec[lane] = 0u;
+        if (lane >= XP_S16 + 16) rec[lane] = 0u;
     }
-#pragma unroll
-    for (int d = 0; d < 3; ++d) *reinterpret_cast<uint2*>(blk + d * XP_DIGIT + 8 * lane) = make_uint2(dg[d][0], dg[d][1]);
-    if (lane < 8) {
-#pragma unroll
-        for (int d = 0; d < 3; ++d) *reinterpret_cast<uint32_t*>(blk + d * XP_DIGIT + 256 + 4 * lane) = 0u;
-    }
-    // 16- and 32-value sums with k_xprep's association: (g0+g1) per lane, then lanes xor 1 (16 values), then xor 2
-    float sm = __fadd_rn(__fadd_rn(f[0] * sup, f[1] * sup), __fadd_rn(f[2] * sup, f[3] * sup));
-    const float s1 = __fadd_rn(__fadd_rn(f[4] * sup, f[5] * sup), __fadd_rn(f[6] * sup, f[7] * sup));
-    sm = __fadd_rn(sm, s1);
-    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-    const float s16 = sm, s16_next = __shfl_down_sync(0xffffffffu, sm, 2);
-    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-    const float s_next = __shfl_down_sync(0xffffffffu, sm, 4);
-    uint32_t* rec = reinterpret_cast<uint32_t*>(blk + XP_REC);
-    if ((lane & 7) == 0) xp_store_pair(rec, 2 * (lane >> 3), 2 * (lane >> 3) + 1, sm, s_next);
-    if ((lane & 3) == 0) {
-        const int p = lane >> 2, c = p & 3, upper = p >> 2;
-        xp_store_pair(rec, XP_S16 + 4 * c + upper, XP_S16 + 4 * c + 2 + upper, s16, s16_next);
-    }
-    if (lane == 8) rec[8] = __float_as_uint(finite ? ldexpf(1.0f, e - 20) : __int_as_float(0x7fc00000));
-    if (lane >= 9 && lane < XP_S16) rec[lane] = 0u;
-    if (lane >= XP_S16 + 16) rec[lane] = 0u;
+    cluster_wait_acquire();         // no CTA leaves while another may still read its partial
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -577,6 +616,307 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
             sum += v;
         }
         y[(int64_t)col * ldy + r0 + rl] = sum;
+    }
+}
+
+// ---- the dual-group form (the decode matvec of the model's dense Q4_K matrices) ----
+// A CTA owns 32-row pairs of 16-row groups of the tile-major layout. Its work is a contiguous range [u_lo, u_hi) of
+// units (row pair rp, superblock sb), u = rp * nsb + sb:
+// - plain launch: one row pair per CTA and split `part` of P equal contiguous superblock ranges (P > 1 only for
+//   matrices with very few rows), partial `part` written at y + part * pstride;
+// - stream-K launch (SK): exactly gridDim.x CTAs (as many as the SMs hold at once) with equal unit ranges, so that
+//   matrices whose row pairs do not divide evenly over the SMs still keep every SM equally busy. A CTA's range then
+//   covers parts of at most two row pairs; each part's sums go to partial slot (CTA - first CTA of that row pair),
+//   and the consumer adds a row pair's 1 to 3 partials in slot order (ksplit_parts gives the count).
+// Warp w takes units u_lo + w, u_lo + w + NW, ...; each stage of its ring holds both groups' tiles of one superblock
+// and the superblock's prepared activations, so the activation fragments, the digit units, the min-term operand, the
+// barrier wait and the copies serve 32 rows. Each group's arithmetic is k_mmv_q4k's, so a row's result does not
+// depend on the other group or the other columns.
+template <int NC, int NW, int NS> struct Q4Layout2 {
+    static constexpr int X_OFF = 2 * Q4_TILE;   // 4608, a multiple of 128
+    static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;
+    static constexpr int STAGES = NS;
+    static constexpr int RED = NW * 2 * Q4_ROWS * 9 * 4;   // a warp's sums of its first row pair, per warp
+    static constexpr int SMEM = NW * STAGES * STAGE + RED;
+};
+
+// The second matrix of a two-matrix dual-group launch (same columns and activations as the first; P = 1).
+struct MvSeg2 {
+    const uint8_t* wt;
+    int row_base, rows;
+    int first_ctas;             // CTAs of the first matrix; INT_MAX: one matrix
+    float* y;
+    int64_t ldy;
+};
+
+__device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int n) { return (int)(((u + 1) * n - 1) / U); }
+
+template <int NC, int NW, int NS, bool SK>
+__global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_q4k2(
+    const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb, const uint8_t* __restrict__ xq,
+    float* __restrict__ y_a, int64_t ldy_a, int P, int64_t pstride, int* err, const MvSeg2 seg)
+{
+    using LY = Q4Layout2<NC, NW, NS>;
+    constexpr bool PACK = NC <= 2;
+    constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block and group
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[NW][LY::STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const bool second = !SK && (int)blockIdx.x >= seg.first_ctas;
+    const int bx = second ? (int)blockIdx.x - seg.first_ctas : (int)blockIdx.x;
+    const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
+    const int row_base = second ? seg.row_base : row_base_a;
+    const int rows = second ? seg.rows : rows_a;
+    float* __restrict__ y = second ? seg.y : y_a;
+    const int64_t ldy = second ? seg.ldy : ldy_a;
+    const int n_rp = (rows + 31) / 32;
+    const int64_t U = (int64_t)n_rp * nsb;
+    int64_t u_lo, u_hi;
+    int part = 0;
+    if (SK) {
+        u_lo = (int64_t)bx * U / gridDim.x;
+        u_hi = (int64_t)(bx + 1) * U / gridDim.x;
+    } else {
+        const int Pq = second ? 1 : P;
+        const int rp = bx / Pq;
+        part = bx % Pq;
+        u_lo = (int64_t)rp * nsb + (int64_t)nsb * part / Pq;
+        u_hi = (int64_t)rp * nsb + (int64_t)nsb * (part + 1) / Pq;
+    }
+    const int rpA = (int)(u_lo / nsb), rpB = u_hi > u_lo ? (int)((u_hi - 1) / nsb) : rpA;
+    const int cnt = (int)(u_hi - u_lo);
+    const int njobs = cnt > warp ? (cnt - warp + NW - 1) / NW : 0;
+    const int tile_row0 = row_base / Q4_ROWS;
+    uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
+    float* red0 = reinterpret_cast<float*>(smem + NW * LY::STAGES * LY::STAGE) + warp * 2 * Q4_ROWS * 9;
+
+    pdl_trigger();
+    if (lane == 0) {
+        for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+        fence_proxy_async();
+    }
+    __syncwarp();
+    auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
+        uint8_t* st = ring + s * LY::STAGE;
+        const int64_t u = u_lo + warp + (int64_t)NW * j;
+        const int rp = (int)(u / nsb), sb = (int)(u - (int64_t)rp * nsb);
+        const bool two = rp * 32 + 16 < rows;
+        const int64_t t0 = (int64_t)(tile_row0 + 2 * rp) * nsb + sb;
+        mbar_expect_tx(&bars[warp][s], (two ? 2 : 1) * Q4_TILE + NC * XP_COL);
+        bulk_load(st, wt + t0 * Q4_TILE, Q4_TILE, &bars[warp][s]);
+        if (two) bulk_load(st + Q4_TILE, wt + (t0 + nsb) * Q4_TILE, Q4_TILE, &bars[warp][s]);
+    };
+    auto issue_x = [&](int j, int s) {      // prepared activations of the same superblock, on the same barrier
+        const int64_t u = u_lo + warp + (int64_t)NW * j;
+        const int sb = (int)(u % nsb);
+        uint8_t* st = ring + s * LY::STAGE;
+#pragma unroll
+        for (int n = 0; n < NC; ++n)
+            bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
+    };
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_w(j, j);
+    pdl_wait();
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
+
+    const bool b_ok = PACK ? g < 3 * NC : g < NC;
+    const int b_off = LY::X_OFF + (PACK ? (g / 3) * XP_COL + (g % 3) * XP_DIGIT : g * XP_COL);
+    // per D column 2c+k2 of this lane: the digit unit's word offset and its factor, fixed over the loop
+    int u_off[2];
+    float u_fac[2][ND];
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+        const int nn = 2 * c + k2;
+        const bool ok = PACK ? nn < 3 * NC : nn < NC;
+        const int col = PACK ? nn / 3 : nn;
+        u_off[k2] = LY::X_OFF + (ok ? col : 0) * XP_COL + XP_REC + 32;
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            const int dig = PACK ? nn % 3 : d;
+            u_fac[k2][d] = ok ? (dig == 0 ? 1024.f : dig == 1 ? 8.f : 0.0625f) : 0.f;
+        }
+    }
+    const bool m_ok0 = 2 * c < NC, m_ok1 = 2 * c + 1 < NC;
+    const int mu_off0 = LY::X_OFF + (m_ok0 ? 2 * c : 0) * XP_COL + XP_REC + 32;
+    const int mu_off1 = LY::X_OFF + (m_ok1 ? 2 * c + 1 : 0) * XP_COL + XP_REC + 32;
+    const float mu_fac0 = m_ok0 ? 1024.f : 0.f, mu_fac1 = m_ok1 ? 1024.f : 0.f;
+    const uint32_t msel = (uint32_t)((2 * c) & 3) | (4u << 4) | ((uint32_t)((2 * c + 1) & 3) << 8) | (4u << 12);
+    const __half2 k1024 = __float2half2_rn(1024.f);
+
+    float facc[2][ND][4] = {};
+    float macc[2][4] = {};
+    // the sums of both groups to a red area [2][Q4_ROWS][9]: ((plane 0 + plane 1) + plane 2) - min term per (row,
+    // column); packed layouts keep the planes and the min term apart, for the final sum's fixed order
+    auto flush = [&](float* red) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            float* rq = red + q * Q4_ROWS * 9;
+            if (PACK) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) rq[(g + 8 * (e >> 1)) * 9 + 2 * c + (e & 1)] = facc[q][0][e];
+                if (c == 0) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) rq[(g + 8 * (e >> 1)) * 9 + 6 + (e & 1)] = macc[q][e];
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
+                    if (col < NC)
+                        rq[row * 9 + col] = ((facc[q][0][e] + facc[q][ND > 1 ? 1 : 0][e]) + facc[q][ND > 2 ? 2 : 0][e]) -
+                                            macc[q][e];
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+#pragma unroll
+            for (int d = 0; d < ND; ++d)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) facc[q][d][e] = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) macc[q][e] = 0.f;
+        }
+    };
+    bool in_b = false;                          // the accumulators hold row pair rpB (else rpA)
+    for (int j = 0; j < njobs; ++j) {
+        const int s = j % LY::STAGES;
+        const int64_t u = u_lo + warp + (int64_t)NW * j;
+        const int rp = (int)(u / nsb);
+        if (SK && rp != rpA && !in_b) {         // crossing into the CTA's second row pair
+            flush(red0);
+            in_b = true;
+        }
+        const int ngrp = rp * 32 + 16 < rows ? 2 : 1;
+        const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
+        const uint8_t* st = ring + s * LY::STAGE;
+        if (ok) {
+            uint4 h0[2], h1[2];
+            uint32_t s0lo[2], s0hi[2], s1lo[2], s1hi[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                if (q < ngrp) {
+                    h0[q] = lds128(st + q * Q4_TILE + g * 16);
+                    h1[q] = lds128(st + q * Q4_TILE + (g + 8) * 16);
+                } else {
+                    h0[q] = make_uint4(0u, 0u, 0u, 0u);
+                    h1[q] = h0[q];
+                }
+                s0lo[q] = h0[q].y & 0x3F3F3F3Fu;
+                s0hi[q] = (h0[q].w & 0x0F0F0F0Fu) | ((h0[q].y >> 2) & 0x30303030u);
+                s1lo[q] = h1[q].y & 0x3F3F3F3Fu;
+                s1hi[q] = (h1[q].w & 0x0F0F0F0Fu) | ((h1[q].y >> 2) & 0x30303030u);
+            }
+            int acc_lo[2][ND][4] = {}, acc_hi[2][ND][4] = {};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                uint2 bf[2][ND];
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                    for (int d = 0; d < ND; ++d)
+                        bf[hh][d] = b_ok ? lds64(st + b_off + d * XP_DIGIT + 32 * (2 * r + hh) + 8 * c) : make_uint2(0u, 0u);
+                const int kb = (2 * r) & 3;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    if (q >= ngrp) break;
+                    const uint4 wv = lds128(st + q * Q4_TILE + Q4_HDRS + r * 512 + lane * 16);
+                    const uint32_t sw0 = r < 2 ? s0lo[q] : s0hi[q], sw1 = r < 2 ? s1lo[q] : s1hi[q];
+                    const int sl0 = (int)((sw0 >> (8 * kb)) & 0xFFu), sh0 = (int)((sw0 >> (8 * kb + 8)) & 0xFFu);
+                    const int sl1 = (int)((sw1 >> (8 * kb)) & 0xFFu), sh1 = (int)((sw1 >> (8 * kb + 8)) & 0xFFu);
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint32_t mask = hh ? 0xF0F0F0F0u : 0x0F0F0F0Fu;   // high nibbles stay in place: 16q
+                        const uint32_t a0 = wv.x & mask, a1 = wv.z & mask, a2 = wv.y & mask, a3 = wv.w & mask;
+                        const int sa = hh ? sh0 : sl0, sb2 = hh ? sh1 : sl1;
+#pragma unroll
+                        for (int d = 0; d < ND; ++d) {
+                            int D[4];
+                            imma16832(D, a0, a1, a2, a3, bf[hh][d].x, bf[hh][d].y);
+                            int (&acc)[4] = hh ? acc_hi[q][d] : acc_lo[q][d];
+                            acc[0] += sa * D[0];
+                            acc[1] += sa * D[1];
+                            acc[2] += sb2 * D[2];
+                            acc[3] += sb2 * D[3];
+                        }
+                    }
+                }
+            }
+            // digit planes: 16 * sum_j s_j sum(q X) = 16 acc_lo + acc_hi (exact); unit * 2^(14 - 7 digit) / 16
+            float fu[2][ND];
+#pragma unroll
+            for (int k2 = 0; k2 < 2; ++k2) {
+                const float unit = *reinterpret_cast<const float*>(st + u_off[k2]);
+#pragma unroll
+                for (int d = 0; d < ND; ++d) fu[k2][d] = unit * u_fac[k2][d];
+            }
+            // min term operands shared by the groups: B = the lane's column's hi sums (slots 0..7), lo sums (8..15)
+            const uint2 bs = g < NC ? lds64(st + LY::X_OFF + g * XP_COL + XP_REC + 8 * c) : make_uint2(0u, 0u);
+            const float mu0 = *reinterpret_cast<const float*>(st + mu_off0) * mu_fac0;
+            const float mu1 = *reinterpret_cast<const float*>(st + mu_off1) * mu_fac1;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                if (q >= ngrp) break;
+                const float dd0 = h2f_((uint16_t)(h0[q].x & 0xFFFF)), dm0 = h2f_((uint16_t)(h0[q].x >> 16));
+                const float dd1 = h2f_((uint16_t)(h1[q].x & 0xFFFF)), dm1 = h2f_((uint16_t)(h1[q].x >> 16));
+#pragma unroll
+                for (int k2 = 0; k2 < 2; ++k2)
+#pragma unroll
+                    for (int d = 0; d < ND; ++d) {
+                        facc[q][d][k2] = fmaf((float)(acc_lo[q][d][k2] * 16 + acc_hi[q][d][k2]), dd0 * fu[k2][d],
+                                              facc[q][d][k2]);
+                        facc[q][d][k2 + 2] = fmaf((float)(acc_lo[q][d][k2 + 2] * 16 + acc_hi[q][d][k2 + 2]),
+                                                  dd1 * fu[k2][d], facc[q][d][k2 + 2]);
+                    }
+                const uint32_t m0lo = h0[q].z & 0x3F3F3F3Fu;
+                const uint32_t m0hi = ((h0[q].w >> 4) & 0x0F0F0F0Fu) | ((h0[q].z >> 2) & 0x30303030u);
+                const uint32_t m1lo = h1[q].z & 0x3F3F3F3Fu;
+                const uint32_t m1hi = ((h1[q].w >> 4) & 0x0F0F0F0Fu) | ((h1[q].z >> 2) & 0x30303030u);
+                const uint32_t mp0 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m0lo : m0hi, 0x64646464u, msel)), k1024));
+                const uint32_t mp1 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m1lo : m1hi, 0x64646464u, msel)), k1024));
+                float dn[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(dn, mp0, mp1, mp0, mp1, bs.x, bs.y);
+                macc[q][0] = fmaf(dn[0], dm0 * mu0, macc[q][0]);
+                macc[q][1] = fmaf(dn[1], dm0 * mu1, macc[q][1]);
+                macc[q][2] = fmaf(dn[2], dm1 * mu0, macc[q][2]);
+                macc[q][3] = fmaf(dn[3], dm1 * mu1, macc[q][3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && j + LY::STAGES < njobs) {
+            fence_proxy_async();        // the stage's generic reads are done before the copy engine rewrites it
+            issue_w(j + LY::STAGES, s);
+            issue_x(j + LY::STAGES, s);
+        }
+    }
+    // red0: this warp's sums of rpA; the start of its ring (whose stages it has finished with): its sums of rpB
+    float* red1 = reinterpret_cast<float*>(ring);
+    if (!in_b) flush(red0);                     // (a warp with no unit of rpB leaves zeros for it)
+    flush(red1);
+    __syncthreads();
+    const int nseg = rpB != rpA ? 2 : 1;
+    for (int sg = 0; sg < nseg; ++sg) {
+        const int rp = sg ? rpB : rpA;
+        const int slot = SK ? bx - sk_cta_of((int64_t)rp * nsb, U, gridDim.x) : part;
+#pragma unroll
+        for (int pass = 0; pass < (8 + NW - 1) / NW; ++pass) {
+            const int idx = threadIdx.x + pass * 32 * NW;
+            const int rl = idx >> 3, col = idx & 7;     // rl: row 0..31 of the row pair
+            if (idx < 256 && col < NC && rp * 32 + rl < rows) {
+                float sum = 0.f;
+#pragma unroll
+                for (int wv = 0; wv < NW; ++wv) {
+                    const float* rw = (sg ? reinterpret_cast<const float*>(smem + wv * LY::STAGES * LY::STAGE)
+                                          : reinterpret_cast<const float*>(smem + NW * LY::STAGES * LY::STAGE) +
+                                                wv * 2 * Q4_ROWS * 9) + rl * 9;
+                    const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
+                    sum += v;
+                }
+                y[(int64_t)slot * pstride + (int64_t)col * ldy + rp * 32 + rl] = sum;
+            }
+        }
     }
 }
 
@@ -867,17 +1207,23 @@ void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w,
         in = *ar;
     }
     uint8_t* pb = p ? p->blocks : nullptr;
-    const dim3 grid(T), block(E / 8);
+    // a cluster of C CTAs per row, C the largest divisor of the row's superblock count up to 8 (the portable cluster
+    // size), each CTA a warp per superblock
+    const int nsb = E / 256;
+    int C = 1;
+    for (int c = 8; c >= 1; --c)
+        if (nsb % c == 0) { C = c; break; }
+    const dim3 grid(C, T), block(32 * (nsb / C));
     const MoeIn mi = moe ? *moe : MoeIn{};
     if (moe) {
-        if (p) launch(k_norm_prep<true, true, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
-        else launch(k_norm_prep<true, false, true>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        if (p) launch_cluster(k_norm_prep<true, true, true>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch_cluster(k_norm_prep<true, false, true>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
     } else if (o || ar) {
-        if (p) launch(k_norm_prep<true, true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
-        else launch(k_norm_prep<true, false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        if (p) launch_cluster(k_norm_prep<true, true, false>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch_cluster(k_norm_prep<true, false, false>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
     } else {
-        if (p) launch(k_norm_prep<false, true, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
-        else launch(k_norm_prep<false, false, false>, grid, block, 0, s, x, o, rs, E, w, eps, y, pb, in, mi);
+        if (p) launch_cluster(k_norm_prep<false, true, false>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
+        else launch_cluster(k_norm_prep<false, false, false>, grid, block, 0, s, C, x, o, rs, E, w, eps, y, pb, in, mi);
     }
     note_launch();
 }
@@ -997,6 +1343,11 @@ template <int NC, bool TILED, bool PAIRS> struct Q4Attr {
     static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS>, Q4Layout<NC>::SMEM, done); }
 };
 template <int NC, bool TILED, bool PAIRS> std::atomic<bool> Q4Attr<NC, TILED, PAIRS>::done[64];
+template <int NC, int NW, int NS, bool SK> struct Q4Attr2 {
+    static std::atomic<bool> done[64];
+    static void ensure() { ensure_smem_attr(k_mmv_q4k2<NC, NW, NS, SK>, Q4Layout2<NC, NW, NS>::SMEM, done); }
+};
+template <int NC, int NW, int NS, bool SK> std::atomic<bool> Q4Attr2<NC, NW, NS, SK>::done[64];
 template <int NC> struct Q6Attr {
     static std::atomic<bool> done[64];
     static void ensure() { ensure_smem_attr(k_mmv_q6k<NC>, Q6Layout<NC>::SMEM, done); }
@@ -1030,6 +1381,62 @@ static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_bas
     case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     }
+}
+
+template <int NC, int NW, int NS, bool SK>
+static void launch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                        int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg, int sk_ctas)
+{
+    Q4Attr2<NC, NW, NS, SK>::ensure();
+    const int ctas = SK ? sk_ctas : (rows + 31) / 32 * P + (seg.wt ? (seg.rows + 31) / 32 : 0);
+    launch(k_mmv_q4k2<NC, NW, NS, SK>, dim3(ctas), dim3(32 * NW), Q4Layout2<NC, NW, NS>::SMEM, s, tiles, row_base, rows,
+           nsb, (const uint8_t*)p.blocks, y, ldy, P, pstride, err, seg);
+    note_launch();
+}
+
+template <int NW, int NS, bool SK>
+static void dispatch_q4k2_cfg(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y,
+                              int64_t ldy, int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg,
+                              int sk_ctas = 0)
+{
+    switch (p.nc) {
+    case 1: launch_q4k2<1, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 2: launch_q4k2<2, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 3: launch_q4k2<3, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 4: launch_q4k2<4, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 5: launch_q4k2<5, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 6: launch_q4k2<6, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    case 7: launch_q4k2<7, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    default: launch_q4k2<8, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
+    }
+}
+
+// The launch shape of the dual-group matvec for a matrix, from graph-timed sweeps on B200 (8192 x 8192, 9216 x 8192,
+// 8192 x 28672, 28672 x 8192 and the tensor-parallel shards): 8 warps with two stages each (two CTAs per SM) for
+// matrices of up to 4 x SMs row pairs, where the 32-row CTAs barely fill the GPU; 4 warps with two stages (four CTAs
+// per SM, twice the superblocks per warp) for taller ones, 7-10 % faster on 28672 x 8192. Deeper rings cost CTAs per
+// SM and were slower on every shape.
+static int sm_count()
+{
+    static std::atomic<int> n{0};
+    int v = n.load(std::memory_order_relaxed);
+    if (!v) {
+        int dev = 0;
+        v = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n.store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
+static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                          int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg)
+{
+    const int rp = (rows + 31) / 32 * P + (seg.wt ? (seg.rows + 31) / 32 : 0);
+    if (rp >= 4 * sm_count() && P == 1 && !seg.wt)
+        dispatch_q4k2_cfg<4, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
+    else
+        dispatch_q4k2_cfg<8, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
 }
 
 void prepare_matvec_mma()
@@ -1104,10 +1511,8 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
     if ((uintptr_t)tiles_a % 16 != 0 || (uintptr_t)tiles_b % 16 != 0 || row_base_a % 16 != 0 || row_base_b % 16 != 0)
         WL_THROW(WL_EINVAL, "matvec_tiles2: misaligned tiles");
     if (!tiles_supported(12, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles2: Q4_K with cols a multiple of 256 only");
-    CUtensorMap none;
-    memset(&none, 0, sizeof none);
-    const MvSeg seg{tiles_b, row_base_b, rows_b, (rows_a + Q4_ROWS - 1) / Q4_ROWS, y_b, ldy_b, nullptr, 0, 1, 0};
-    dispatch_q4k<true>(none, tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, err, s, seg);
+    const MvSeg2 seg{tiles_b, row_base_b, rows_b, (rows_a + 31) / 32, y_b, ldy_b};
+    dispatch_q4k2(tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, 1, 0, err, s, seg);
 }
 
 void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
@@ -1142,15 +1547,14 @@ void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_ro
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s)
+                  int64_t ldy, int* err, cudaStream_t s, int P, int64_t pstride)
 {
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
+    if (P < 1 || P > cols / 256 || (type != 12 && P != 1)) WL_THROW(WL_EINVAL, "matvec_tiles: bad split count");
     if (type == 12) {
-        CUtensorMap none;
-        memset(&none, 0, sizeof none);
-        dispatch_q4k<true>(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
-                           MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0});
+        dispatch_q4k2(tiles, row_base, rows, cols / 256, p, y, ldy, P, pstride, err, s,
+                      MvSeg2{nullptr, 0, 0, INT_MAX, nullptr, 0});
     } else {
         matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }
