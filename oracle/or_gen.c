@@ -374,6 +374,88 @@ int or_write_tiny(const char* path, const char* arch, int type, int flags, int l
 #undef K
 }
 
+/* C#'s default float formatting for the fixture names (round-trip shortest form, no exponent for these values). */
+static void cs_float(char* out, size_t n, float v)
+{
+    for (int prec = 1; prec <= 9; ++prec) {
+        snprintf(out, n, "%.*g", prec, (double)v);
+        if ((float)strtod(out, NULL) == v) return;
+    }
+}
+
+/* TinyArchs.Build (tests/TinyArchs.cs:31-106): tiny Granite and OLMo 2 models and the Llama twin of a Granite model.
+ * es/rs/as/ls: the Granite scales (0 = key left out); omit_post_ffw: leave out post_ffw_norm (olmo2); short_qnorm:
+ * attn_q_norm covers one head (olmo2). */
+int or_write_tiny_arch(const char* path, const char* arch, int type, int tied, int layers, int embd, int heads,
+                       int kv_heads, int ff, float es, float rs, float as, float ls, int omit_post_ffw, int short_qnorm,
+                       uint64_t seed)
+{
+    or_rng rng; or_rng_init(&rng, seed);
+    gw w; memset(&w, 0, sizeof w);
+    char a[64], key[128], name[256];
+    snprintf(a, sizeof a, "%s.", arch);
+    const int olmo = strcmp(arch, "olmo2") == 0, granite = strcmp(arch, "granite") == 0;
+    const int hd = embd / heads, E = embd, qd = heads * hd, kd = kv_heads * hd, F = ff;
+    char scaled[160] = "";
+    if (es != 0 || rs != 0 || as != 0 || ls != 0) {
+        char f0[32], f1[32], f2[32], f3[32];
+        cs_float(f0, sizeof f0, es); cs_float(f1, sizeof f1, rs); cs_float(f2, sizeof f2, as); cs_float(f3, sizeof f3, ls);
+        snprintf(scaled, sizeof scaled, "-scaled%s_%s_%s_%s", f0, f1, f2, f3);
+    }
+    snprintf(name, sizeof name, "tiny-arch-%s-%s%s%s%s%s-s%llu", arch, type_name(type), tied ? "-tied" : "", scaled,
+             omit_post_ffw ? "-nopost_ffw_norm" : "", short_qnorm ? "-shortq" : "", (unsigned long long)seed);
+    gw_str(&w, "general.architecture", arch);
+    gw_str(&w, "general.name", name);
+    gw_u32(&w, "general.alignment", 32);
+#define K(s) (snprintf(key, sizeof key, "%s%s", a, s), key)
+    gw_u32(&w, K("block_count"), (uint32_t)layers);
+    gw_u32(&w, K("context_length"), 512);
+    gw_u32(&w, K("embedding_length"), (uint32_t)E);
+    gw_u32(&w, K("feed_forward_length"), (uint32_t)F);
+    gw_u32(&w, K("attention.head_count"), (uint32_t)heads);
+    gw_u32(&w, K("attention.head_count_kv"), (uint32_t)kv_heads);
+    gw_f32(&w, K("attention.layer_norm_rms_epsilon"), 1e-5f);
+    gw_f32(&w, K("rope.freq_base"), 500000.0f);
+    if (!olmo) gw_u32(&w, K("rope.dimension_count"), (uint32_t)hd);
+    if (granite) {
+        if (es != 0) gw_f32(&w, K("embedding_scale"), es);
+        if (rs != 0) gw_f32(&w, K("residual_scale"), rs);
+        if (as != 0) gw_f32(&w, K("attention.scale"), as);
+        if (ls != 0) gw_f32(&w, K("logit_scale"), ls);
+    }
+#undef K
+    int vocab;
+    add_bpe_meta(&w, 1, &vocab);
+    int64_t len; uint8_t* d;
+    d = mat(&rng, type, vocab, E, 1.0f, &len); gw_tensor(&w, "token_embd.weight", type, d, len, 2, E, vocab, 1);
+    for (int l = 0; l < layers; l++) {
+        char p[32]; snprintf(p, sizeof p, "blk.%d.", l);
+#define N(s) (snprintf(name, sizeof name, "%s%s", p, s), name)
+        if (!olmo) { d = normv(&rng, E, &len); gw_tensor(&w, N("attn_norm.weight"), OR_F32, d, len, 1, E, 1, 1); }
+        d = mat(&rng, type, qd, E, 0.08f, &len); gw_tensor(&w, N("attn_q.weight"), type, d, len, 2, E, qd, 1);
+        d = mat(&rng, type, kd, E, 0.08f, &len); gw_tensor(&w, N("attn_k.weight"), type, d, len, 2, E, kd, 1);
+        d = mat(&rng, type, kd, E, 0.08f, &len); gw_tensor(&w, N("attn_v.weight"), type, d, len, 2, E, kd, 1);
+        if (olmo) {
+            const int qn = short_qnorm ? hd : qd;
+            d = normv(&rng, qn, &len); gw_tensor(&w, N("attn_q_norm.weight"), OR_F32, d, len, 1, qn, 1, 1);
+            d = normv(&rng, kd, &len); gw_tensor(&w, N("attn_k_norm.weight"), OR_F32, d, len, 1, kd, 1, 1);
+        }
+        d = mat(&rng, type, E, qd, 0.08f, &len); gw_tensor(&w, N("attn_output.weight"), type, d, len, 2, qd, E, 1);
+        if (olmo) { d = normv(&rng, E, &len); gw_tensor(&w, N("post_attention_norm.weight"), OR_F32, d, len, 1, E, 1, 1); }
+        else { d = normv(&rng, E, &len); gw_tensor(&w, N("ffn_norm.weight"), OR_F32, d, len, 1, E, 1, 1); }
+        d = mat(&rng, type, F, E, 0.08f, &len); gw_tensor(&w, N("ffn_gate.weight"), type, d, len, 2, E, F, 1);
+        d = mat(&rng, type, F, E, 0.08f, &len); gw_tensor(&w, N("ffn_up.weight"), type, d, len, 2, E, F, 1);
+        d = mat(&rng, type, E, F, 0.06f, &len); gw_tensor(&w, N("ffn_down.weight"), type, d, len, 2, F, E, 1);
+        if (olmo && !omit_post_ffw) { d = normv(&rng, E, &len); gw_tensor(&w, N("post_ffw_norm.weight"), OR_F32, d, len, 1, E, 1, 1); }
+#undef N
+    }
+    d = normv(&rng, E, &len); gw_tensor(&w, "output_norm.weight", OR_F32, d, len, 1, E, 1, 1);
+    if (!tied) { d = mat(&rng, type, vocab, E, 0.08f, &len); gw_tensor(&w, "output.weight", type, d, len, 2, E, vocab, 1); }
+    int rc = gw_save(&w, path);
+    gw_free(&w);
+    return rc;
+}
+
 /* TinyMoe.Build (tests/TinyMoe.cs:51-153). */
 int or_write_tiny_moe(const char* path, const char* layout, int ty, int tied, int layers, int E, int heads, int kv_heads,
                       int experts, int used, int X, int SH, int DF, int norm_key, uint32_t dense_mask, int dense_twin, uint64_t seed)

@@ -139,6 +139,26 @@ static int bind_layers(or_model* m, char* err, int errlen)
         L->moe = c->expert_count > 0 && L->router.present;
         if (!L->q.present || !L->k.present || !L->v.present || !L->o.present) { seterr(err, errlen, "layer is missing attention tensors"); return -1; }
         if (!c->post_norms && (!L->attn_norm.present || !L->ffn_norm.present)) { seterr(err, errlen, "layer is missing norm tensors"); return -1; }
+        if (c->post_norms) {
+            /* ModelConfig.Olmo2LayerTensors (src/ModelConfig.cs:115) and the whole-vector QK norm (:102-105) */
+            static const char* olmo2[] = { "attn_q_norm", "attn_k_norm", "post_attention_norm", "post_ffw_norm" };
+            const wview* need[] = { &L->q_norm, &L->k_norm, &L->post_attn_norm, &L->post_ffw_norm };
+            for (int i = 0; i < 4; i++)
+                if (!need[i]->present) {
+                    char msg[160];
+                    snprintf(msg, sizeof msg, "Layer %d has no %s.weight (unsupported layout).", l, olmo2[i]);
+                    seterr(err, errlen, msg);
+                    return -1;
+                }
+        }
+        if (c->qk_norm_full && (L->q_norm.rows * L->q_norm.cols != c->heads * c->head_dim ||
+                                L->k_norm.rows * L->k_norm.cols != c->kv_heads * c->head_dim)) {
+            char msg[200];
+            snprintf(msg, sizeof msg, "Layer %d: attn_q_norm/attn_k_norm must cover the whole Q and K vectors (%d and %d).", l,
+                     c->heads * c->head_dim, c->kv_heads * c->head_dim);
+            seterr(err, errlen, msg);
+            return -1;
+        }
         if (L->moe) {
             if (!L->gate_exps.present || !L->up_exps.present || !L->down_exps.present) { seterr(err, errlen, "MoE layer is missing expert tensors"); return -1; }
             c->expert_ff = L->gate_exps.rows;

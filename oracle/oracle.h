@@ -101,6 +101,11 @@ int  or_matrix(or_rng* r, int type, int rows, int cols, float rms, uint8_t* out)
  * 4 rope_freqs. Returns 0 or -1. */
 int  or_write_tiny(const char* path, const char* arch, int type, int flags, int layers, int embd, int heads,
                    int kv_heads, int ff, uint64_t seed);
+/* TinyArchs.Build (tests/TinyArchs.cs:31-106): arch granite | olmo2 | llama (the Granite twin); the Granite scales
+ * (0 = key left out), omit_post_ffw and short_qnorm make the OLMo 2 files the reference must refuse. */
+int  or_write_tiny_arch(const char* path, const char* arch, int type, int tied, int layers, int embd, int heads,
+                        int kv_heads, int ff, float es, float rs, float as, float ls, int omit_post_ffw, int short_qnorm,
+                        uint64_t seed);
 /* TinyMoe.Build (tests/TinyMoe.cs:51-153). layout: llama|mixtral|qwen2moe|qwen3moe. dense_mask: bit l set =
  * layer l has a plain FFN. norm_key: -1 absent, 0/1 written. dense_twin: write the one-expert dense twin. */
 int  or_write_tiny_moe(const char* path, const char* layout, int type, int tied, int layers, int embd, int heads,

@@ -76,6 +76,7 @@ def lib():
             "or_matrix": (I, [P, I, I, I, F, P]),
             "or_write_tiny": (I, [S, S, I, I, I, I, I, I, I, U64]),
             "or_write_tiny_moe": (I, [S, S, I, I, I, I, I, I, I, I, I, I, I, I, C.c_uint32, I, U64]),
+            "or_write_tiny_arch": (I, [S, S, I, I, I, I, I, I, I, F, F, F, F, I, I, U64]),
             "or_synth_tensor": (I, [I, U64, C.c_uint32, I64, I64, F, F, P, I]),
             "or_quantize_block": (None, [I, P, P]),
             "or_model_open": (P, [S, I, I, C.c_char_p, I]), "or_model_close": (None, [P]),
@@ -198,6 +199,17 @@ def write_tiny_moe(path, layout="llama", type=Q8_0, tied=False, layers=2, embd=2
         mask |= 1 << l
     if lib().or_write_tiny_moe(path.encode(), layout.encode(), type, int(tied), layers, embd, heads, kv_heads, experts,
                                used, expert_ff, shared_ff, dense_ff, norm_key, mask, int(dense_twin), seed):
+        raise IOError(f"cannot write {path}")
+    return path
+
+
+def write_tiny_arch(path, arch="granite", type=Q8_0, tied=False, layers=2, embd=256, heads=4, kv_heads=2, ff=512,
+                    embedding_scale=0.0, residual_scale=0.0, attention_scale=0.0, logit_scale=0.0, omit_post_ffw=False,
+                    short_qnorm=False, seed=1):
+    """TinyArchs.Build (tests/TinyArchs.cs): a tiny Granite or OLMo 2 model, or the Llama twin of a Granite one."""
+    if lib().or_write_tiny_arch(path.encode(), arch.encode(), type, int(tied), layers, embd, heads, kv_heads, ff,
+                                embedding_scale, residual_scale, attention_scale, logit_scale, int(omit_post_ffw),
+                                int(short_qnorm), seed):
         raise IOError(f"cannot write {path}")
     return path
 

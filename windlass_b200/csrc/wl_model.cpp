@@ -384,6 +384,14 @@ void Model::load_from_gguf(const Gguf& g)
             c_.expert_ff = (int)gate->dims[1];
         }
     }
+    if (c_.qk_norm_full)        // the whole-vector QK norm (src/ModelConfig.cs:102-105)
+        for (int l = 0; l < c_.layers; ++l) {
+            const GgufTensor* qn = g.find(layer_name(l, "attn_q_norm.weight"));
+            const GgufTensor* kn = g.find(layer_name(l, "attn_k_norm.weight"));
+            if (!qn || !kn || qn->elements() != c_.qdim() || kn->elements() != c_.kvdim())
+                WL_THROW(WL_EUNSUPPORTED, "Layer " + std::to_string(l) + ": attn_q_norm/attn_k_norm must cover the whole Q and K vectors (" +
+                                          std::to_string(c_.qdim()) + " and " + std::to_string(c_.kvdim()) + ").");
+        }
     for (const GgufTensor& t : g.tensors()) {
         const std::string& n = t.name;
         if (n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0 && t.ndims >= 2 && !can_decode(t.type))
