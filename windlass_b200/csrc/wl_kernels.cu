@@ -839,12 +839,61 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <int HD, int G>
+// k_attn_combine's merge of the S ranges for 4 consecutive output values at value v of row t (same arithmetic and
+// order: the maximum over the ranges, then NA accumulator sets of ranges s = a, a + NA, ... in range order, the
+// sets added in set order), reading the partials through L2 (other CTAs wrote them).
+template <int S>
+__device__ __forceinline__ void attn_merge4(const float* __restrict__ part, const float* __restrict__ ml, int t,
+                                            int heads, int hd, int v, float (&f)[4])
+{
+    constexpr int NA = S > 16 ? 4 : 1;
+    constexpr int SPT = S / NA;
+    const int head = v / hd, d = v % hd;
+    const float2* mlp = reinterpret_cast<const float2*>(ml + ((int64_t)t * heads + head) * S * 2);
+    const float* pp = part + ((int64_t)t * heads + head) * S * hd + d;
+    float M = -INFINITY;
+#pragma unroll 16
+    for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(mlp + s).x);
+    double Lt = 0.0, t0 = 0.0, t1 = 0.0, t2 = 0.0, t3 = 0.0;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        double L = 0.0, o0 = 0.0, o1 = 0.0, o2 = 0.0, o3 = 0.0;
+#pragma unroll 16
+        for (int j = 0; j < SPT; ++j) {
+            const int s = a + NA * j;
+            const float2 m = __ldcg(mlp + s);
+            const float4 ps = __ldcg(reinterpret_cast<const float4*>(pp + (int64_t)s * hd));
+            const double w = m.y > 0.f ? (double)expf(m.x - M) : 0.0;
+            L += w * (double)m.y;
+            o0 += w * (double)ps.x;
+            o1 += w * (double)ps.y;
+            o2 += w * (double)ps.z;
+            o3 += w * (double)ps.w;
+        }
+        if (a == 0) {
+            Lt = L; t0 = o0; t1 = o1; t2 = o2; t3 = o3;
+        } else {
+            Lt += L; t0 += o0; t1 += o1; t2 += o2; t3 += o3;
+        }
+    }
+    f[0] = (float)(t0 / Lt);
+    f[1] = (float)(t1 / Lt);
+    f[2] = (float)(t2 / Lt);
+    f[3] = (float)(t3 / Lt);
+}
+
+// MERGE (S > 1, G * HD a multiple of 256): after writing its range's partials, each CTA takes a ticket on its row's
+// counter for its KV head; the CTA that takes the last of the S tickets merges the S ranges of the group's G heads
+// (attn_merge4: bit for bit k_attn_combine) and writes the output and, with prep, its prepared activations (the
+// group's G * HD values are whole superblocks), then resets the counter for the next launch, so no combine launch is
+// needed.
+template <int HD, int G, bool MERGE>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
                                                            float scale, const RowKV* __restrict__ rows, int layer,
                                                            const int32_t* __restrict__ pos, int S,
                                                            float* __restrict__ out, float* __restrict__ part,
-                                                           float* __restrict__ ml)
+                                                           float* __restrict__ ml, int* __restrict__ tickets,
+                                                           uint8_t* __restrict__ prep)
 {
     constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
     constexpr int CH = HD / 8;              // 16-byte chunks per row
@@ -982,6 +1031,32 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
         mlp[0] = mrun[tid];
         mlp[1] = (float)lrun[tid];
     }
+    if (!MERGE || S == 1) return;
+    __shared__ int last;
+    __shared__ float pscratch[2][2];
+    __threadfence();                // this CTA's partials are visible GPU-wide before its ticket
+    __syncthreads();
+    if (tid == 0) {
+        int* ctr = tickets + t * kv_heads + kvh;
+        last = atomicAdd(ctr, 1) == S - 1;
+        if (last) *ctr = 0;         // every range has taken its ticket: ready for the next launch
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    constexpr int GV = G * HD;      // the group's values: GV / 256 whole superblocks
+    const int v0 = kvh * GV, grp = tid >> 6, t64 = tid & 63;
+    for (int r = 0; r < (GV + 511) / 512; ++r) {
+        const int sbl = 2 * r + grp;                    // superblock of the group this half of the CTA serves
+        if (sbl * 256 >= GV) continue;                  // (uniform per half)
+        const int v = v0 + sbl * 256 + 4 * t64;
+        float f[4];
+        if (S == 16) attn_merge4<16>(part, ml, t, heads, HD, v, f);
+        else if (S == 32) attn_merge4<32>(part, ml, t, heads, HD, v, f);
+        else attn_merge4<64>(part, ml, t, heads, HD, v, f);
+        *reinterpret_cast<float4*>(out + (int64_t)t * QD + v) = make_float4(f[0], f[1], f[2], f[3]);
+        if (prep) xprep_sb<true>(f, t64, pscratch[grp], prep + ((int64_t)t * (QD / 256) + v / 256) * XP_COL, 1 + grp);
+    }
 }
 
 // Merges the S position ranges of k_attn_part in range order for one 256-value superblock of a row's attention
@@ -1078,16 +1153,30 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
 {
     const int S = attention_splits(T, kv_heads);
     const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
+    static std::mutex mu;
     static bool attr_set[64] = {false};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-        attr_set[dev] = true;
+    WL_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 64 && !attr_set[dev]) {
+            WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            attr_set[dev] = true;
+        }
     }
     float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
-    launch(k_attn_part<HD, G>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows, layer,
-           pos, S, out, part, ml);
+    int* tickets = reinterpret_cast<int*>(part + (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (HD + 2));
+    // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks
+    constexpr bool can_merge = (G * HD) % 256 == 0;
+    if (S > 1 && can_merge) {
+        launch(k_attn_part<HD, G, true>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale,
+               rows, layer, pos, S, out, part, ml, tickets, prep ? prep->blocks : (uint8_t*)nullptr);
+        launched();
+        return;
+    }
+    launch(k_attn_part<HD, G, false>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows,
+           layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
     launched();
     if (S > 1) {
         auto comb = S == 16 ? k_attn_combine<16> : S == 32 ? k_attn_combine<32> : k_attn_combine<64>;

@@ -183,9 +183,12 @@ inline int attention_splits_for(int kv_heads)
     const int s = 128 / (kv_heads > 0 ? kv_heads : 1);
     return s < ATT_SPLITS ? ATT_SPLITS : s > ATT_MAX_SPLITS ? ATT_MAX_SPLITS : s;
 }
+// The partials, their (max, sum) pairs, then one ticket counter per (row, KV head); the counters must be zero when the
+// workspace is first used (each merging CTA resets its counter for the next launch).
 inline size_t attention_part_floats(int heads, int kv_heads, int head_dim)
 {
-    return (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (head_dim + 2);
+    return (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (head_dim + 2) +
+           (size_t)ATT_PART_ROWS * kv_heads;
 }
 int attention_splits(int T, int kv_heads);
 bool attention_supported(int heads, int kv_heads, int head_dim);

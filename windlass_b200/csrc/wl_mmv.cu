@@ -364,12 +364,12 @@ constexpr int Q4_TILE = Q4_ROWS * 144;          // weight bytes per stage
 // then of row g+8 (raw bytes 16 + 32r + 8c ..+8), one conflict-free 16-byte read per run.
 constexpr int Q4_HDRS = Q4_ROWS * 16;
 
-template <int NC> struct Q4Layout {
+template <int NC, int NW = 8> struct Q4Layout {
     static constexpr int X_OFF = Q4_TILE;       // 2304, a multiple of 128
     static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;   // TMA destinations are 128-byte aligned
     static constexpr int TX = Q4_TILE + NC * XP_COL;                         // bytes the copies of one stage deliver
     static constexpr int STAGES = 2;
-    static constexpr int SMEM = 8 * STAGES * STAGE;
+    static constexpr int SMEM = NW * STAGES * STAGE;
 };
 
 // The second matrix of a two-matrix Q4_K matvec launch (same columns and activations as the first).
@@ -398,7 +398,7 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
 
 __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
 
-// One CTA per 16 rows; warp w takes superblocks w, w+8, ... of those rows. Per superblock and 32-value sub-block
+// One CTA per 16 rows; warp w of its NW warps takes superblocks w, w+NW, ... of those rows. Per superblock and 32-value sub-block
 // one integer MMA (u8 codes x s8 activation digits, exact int32) gives sum(q*X); the 6-bit sub-block scales are
 // applied in integers; the superblock's d and the digit unit are applied in fp32 per digit plane; the min term
 // dmin * sum_j m_j * sum(x_j) is one f16 MMA over the hi/lo sub-block sums.
@@ -406,17 +406,17 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
 // PAIRS: the grouped-expert form (seg.sel set), compiled apart so that the dense matvec carries none of its code.
-template <int NC, bool TILED, bool PAIRS>
-__global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
+template <int NC, bool TILED, bool PAIRS, int NW = 8>
+__global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
                                                     const uint8_t* __restrict__ xq, float* __restrict__ y_a,
                                                     int64_t ldy_a, int* err, const MvSeg seg)
 {
-    using LY = Q4Layout<NC>;
+    using LY = Q4Layout<NC, NW>;
     constexpr bool PACK = NC <= 2;
     constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[8][LY::STAGES];
+    __shared__ __align__(8) uint64_t bars[NW][LY::STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     // two matrices with the same input in one launch: CTAs past the first matrix's row tiles take the second's
     const bool second = TILED && !seg.sel && (int)blockIdx.x >= seg.first_ctas;
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
     }
     const int r0 = bx * Q4_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
-    const int njobs = nsb > warp ? (nsb - warp + 7) / 8 : 0;
+    const int njobs = nsb > warp ? (nsb - warp + NW - 1) / NW : 0;
 
     pdl_trigger();
     if (lane == 0) {
@@ -467,13 +467,13 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
         uint8_t* st = ring + s * LY::STAGE;
         mbar_expect_tx(&bars[warp][s], LY::TX);
         if (TILED)
-            bulk_load(st, wt + ((int64_t)(row_base / Q4_ROWS + bx) * nsb + warp + 8 * j) * Q4_TILE, Q4_TILE,
+            bulk_load(st, wt + ((int64_t)(row_base / Q4_ROWS + bx) * nsb + warp + NW * j) * Q4_TILE, Q4_TILE,
                       &bars[warp][s]);
         else
-            tma_load_2d(st, &wmap, (warp + 8 * j) * 144, row_base + r0, &bars[warp][s]);
+            tma_load_2d(st, &wmap, (warp + NW * j) * 144, row_base + r0, &bars[warp][s]);
     };
     auto issue_x = [&](int j, int s) {      // prepared activations of the same superblock, on the same barrier
-        const int sb = warp + 8 * j;
+        const int sb = warp + NW * j;
         uint8_t* st = ring + s * LY::STAGE;
 #pragma unroll
         for (int n = 0; n < NC; ++n)
@@ -606,11 +606,11 @@ __global__ void __launch_bounds__(256, NC <= 2 ? 4 : 2) k_mmv_q4k(const __grid_c
         }
     }
     __syncthreads();
-    const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;
+    const int rl = threadIdx.x >> 3, col = threadIdx.x & 7;     // NW >= 4: every (row, column) has a thread
     if (col < NC && rl < Q4_ROWS && r0 + rl < rows) {
         float sum = 0.f;
 #pragma unroll
-        for (int wv = 0; wv < 8; ++wv) {
+        for (int wv = 0; wv < NW; ++wv) {
             const float* rw = reinterpret_cast<const float*>(smem + wv * LY::STAGES * LY::STAGE) + rl * 9;
             const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
             sum += v;
@@ -1338,11 +1338,11 @@ static void ensure_smem_attr(Kernel kernel, int bytes, std::atomic<bool> (&done)
     done[dev].store(true, std::memory_order_release);
 }
 
-template <int NC, bool TILED, bool PAIRS> struct Q4Attr {
+template <int NC, bool TILED, bool PAIRS, int NW = 8> struct Q4Attr {
     static std::atomic<bool> done[64];
-    static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS>, Q4Layout<NC>::SMEM, done); }
+    static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS, NW>, Q4Layout<NC, NW>::SMEM, done); }
 };
-template <int NC, bool TILED, bool PAIRS> std::atomic<bool> Q4Attr<NC, TILED, PAIRS>::done[64];
+template <int NC, bool TILED, bool PAIRS, int NW> std::atomic<bool> Q4Attr<NC, TILED, PAIRS, NW>::done[64];
 template <int NC, int NW, int NS, bool SK> struct Q4Attr2 {
     static std::atomic<bool> done[64];
     static void ensure() { ensure_smem_attr(k_mmv_q4k2<NC, NW, NS, SK>, Q4Layout2<NC, NW, NS>::SMEM, done); }
@@ -1354,32 +1354,32 @@ template <int NC> struct Q6Attr {
 };
 template <int NC> std::atomic<bool> Q6Attr<NC>::done[64];
 
-template <int NC, bool TILED, bool PAIRS = false>
+template <int NC, bool TILED, bool PAIRS = false, int NW = 8>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                        float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
-    Q4Attr<NC, TILED, PAIRS>::ensure();
+    Q4Attr<NC, TILED, PAIRS, NW>::ensure();
     const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas * (seg.wt ? 2 : 1)
                              : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     if (PAIRS != (seg.sel != nullptr)) WL_THROW(WL_EINVAL, "matvec: the grouped-expert form needs the expert ids");
-    launch(k_mmv_q4k<NC, TILED, PAIRS>, dim3(ctas), dim3(256), Q4Layout<NC>::SMEM, s, m, tiles, row_base, rows, nsb,
-           (const uint8_t*)p.blocks, y, ldy, err, seg);
+    launch(k_mmv_q4k<NC, TILED, PAIRS, NW>, dim3(ctas), dim3(32 * NW), Q4Layout<NC, NW>::SMEM, s, m, tiles, row_base,
+           rows, nsb, (const uint8_t*)p.blocks, y, ldy, err, seg);
     note_launch();
 }
 
-template <bool TILED>
+template <bool TILED, int NW = 8>
 static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                          float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
     switch (p.nc) {
-    case 1: launch_q4k<1, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 2: launch_q4k<2, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 3: launch_q4k<3, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 4: launch_q4k<4, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 5: launch_q4k<5, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 6: launch_q4k<6, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 7: launch_q4k<7, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    default: launch_q4k<8, TILED>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 1: launch_q4k<1, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 2: launch_q4k<2, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 3: launch_q4k<3, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 4: launch_q4k<4, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 5: launch_q4k<5, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 6: launch_q4k<6, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 7: launch_q4k<7, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    default: launch_q4k<8, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
     }
 }
 
@@ -1437,6 +1437,16 @@ static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb,
         dispatch_q4k2_cfg<4, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
     else
         dispatch_q4k2_cfg<8, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
+}
+
+// The model's decode matvec on tile-major Q4_K: one 16-row CTA per row tile. In a decode step every matvec follows a
+// small kernel, and CTAs this size start under programmatic dependent launch while that kernel still runs (four fit
+// beside it on an SM) and stream their first stages meanwhile; the 32-row form above, faster back to back, lost 6 %
+// of the 70B step for that reason (measured on B200).
+static void dispatch_q4k16(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
+                           float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
+{
+    dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
 }
 
 void prepare_matvec_mma()
@@ -1511,8 +1521,10 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
     if ((uintptr_t)tiles_a % 16 != 0 || (uintptr_t)tiles_b % 16 != 0 || row_base_a % 16 != 0 || row_base_b % 16 != 0)
         WL_THROW(WL_EINVAL, "matvec_tiles2: misaligned tiles");
     if (!tiles_supported(12, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles2: Q4_K with cols a multiple of 256 only");
-    const MvSeg2 seg{tiles_b, row_base_b, rows_b, (rows_a + 31) / 32, y_b, ldy_b};
-    dispatch_q4k2(tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, 1, 0, err, s, seg);
+    CUtensorMap none;
+    memset(&none, 0, sizeof none);
+    const MvSeg seg{tiles_b, row_base_b, rows_b, (rows_a + Q4_ROWS - 1) / Q4_ROWS, y_b, ldy_b, nullptr, 0, 1, 0};
+    dispatch_q4k16(none, tiles_a, row_base_a, rows_a, cols / 256, p, y_a, ldy_a, err, s, seg);
 }
 
 void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
@@ -1552,7 +1564,12 @@ void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int co
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
     if (P < 1 || P > cols / 256 || (type != 12 && P != 1)) WL_THROW(WL_EINVAL, "matvec_tiles: bad split count");
-    if (type == 12) {
+    if (type == 12 && P == 1) {
+        CUtensorMap none;
+        memset(&none, 0, sizeof none);
+        dispatch_q4k16(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
+                       MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0});
+    } else if (type == 12) {
         dispatch_q4k2(tiles, row_base, rows, cols / 256, p, y, ldy, P, pstride, err, s,
                       MvSeg2{nullptr, 0, 0, INT_MAX, nullptr, 0});
     } else {

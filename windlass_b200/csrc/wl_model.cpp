@@ -862,7 +862,9 @@ void Model::ensure_workspace(int T, int logit_rows)
                 if (w->present()) max_cols = std::max(max_cols, w->cols);
         }
         WL_CUDA(cudaMalloc(&xprep_buf_, k::xprep_bytes(max_cols, 8)));
-        att_part_ = dalloc<float>((int64_t)k::attention_part_floats(c_.heads, c_.kv_heads, c_.head_dim));
+        const size_t apf = k::attention_part_floats(c_.heads, c_.kv_heads, c_.head_dim);
+        att_part_ = dalloc<float>((int64_t)apf);
+        WL_CUDA(cudaMemset(att_part_, 0, sizeof(float) * apf));     // the merge tickets start at zero
     }
     if (logit_rows > ws_logit_rows_) {
         dfree(logits_); dfree(ids_d_); dfree(amax_key_); dfree(amax_count_); hfree(h_ids_);

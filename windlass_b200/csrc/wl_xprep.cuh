@@ -31,17 +31,18 @@ __device__ __forceinline__ void xp_store_pair(uint32_t* rec, int hi_word, int lo
     rec[lo_word] = xp_h2_bits(__halves2half2(l0, l1));
 }
 
-// Called by the 64 threads t = 0..63 of a 64-thread CTA (it synchronises the CTA), or with NAMED by threads 0..63 of
-// a larger CTA (they synchronise on named barrier 1 alone); thread t holds values 4t..4t+3. scratch: two floats of
+// Called by the 64 threads t = 0..63 of a 64-thread CTA (it synchronises the CTA), or with NAMED by 64 threads of a
+// larger CTA (they synchronise on named barrier bar_id alone); thread t holds values 4t..4t+3. scratch: two floats of
 // shared memory.
 template <bool NAMED = false>
-__device__ __forceinline__ void xprep_sb(const float (&f)[4], int t, float* scratch, uint8_t* __restrict__ blk)
+__device__ __forceinline__ void xprep_sb(const float (&f)[4], int t, float* scratch, uint8_t* __restrict__ blk,
+                                         int bar_id = 1)
 {
     float m = fmaxf(fmaxf(fabsf(f[0]), fabsf(f[1])), fmaxf(fabsf(f[2]), fabsf(f[3])));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((t & 31) == 0) scratch[t >> 5] = m;
-    if (NAMED) asm volatile("bar.sync 1, 64;" ::: "memory");
+    if (NAMED) asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
     else __syncthreads();
     m = fmaxf(scratch[0], scratch[1]);
     const bool finite = m <= 3.4e38f;          // false for inf and NaN
