@@ -13,8 +13,8 @@ per step, which is far larger than the 126 MB L2, so no flush is needed between 
 - e2e: the same steps through the public call a greedy host makes (wl_forward_argmax / wl_forward_batch_argmax:
   host token ids in, each row's greedy id back, fed to the next step), with the logits-returning wl_forward and the
   device-chained wl_generate_greedy beside it.
-- roofline: the dominant kernel (the Q4_K fused dequant-matvec), its algorithmic bytes over its CUDA-event time,
-  recorded live in a second pass over the same steps with per-launch events.
+- roofline: the dominant kernel (the Q4_K fused dequant-matvec): the step's own Q4_K launches replayed alone as a
+  CUDA graph (wl_bench_matvecs), their algorithmic bytes per step over their CUDA-event time per step.
 - cpu_baseline: the reference's CPU arithmetic (the C oracle) on the box's cores, one decoder layer of the same
   shape plus a slice of the output head, scaled to a whole token.
 --impl reference prints the CPU arm alone (rank 0; other ranks exit 0).
@@ -487,35 +487,32 @@ def main():
         e2e_chained = len(got) / tp.max_over_ranks(dist, time.perf_counter() - t0)
 
     trace(f"e2e {e2e_s:.2f} s ({e2e:.1f} tok/s); logits-returning {e2e_logits:.1f} tok/s; chained {e2e_chained}")
-    # live roofline of the dominant kernel: per-launch CUDA events over a second pass of the same steps
-    m.profile(1)
-    m.bench_decode(seqs, min(steps, 8))
-    q4 = m.profile_get(Q4_K)
-    q6 = m.profile_get(Q6_K)
-    att = m.profile_get(40)
-    comm = m.profile_get(45)
-    trace(f"profile: q4_K {q4.launches} launches {q4.ms:.1f} ms {q4.bytes / 1e9:.2f} GB; q6_K {q6.launches} "
-          f"{q6.ms:.1f} ms {q6.bytes / 1e9:.2f} GB; attention {att.launches} {att.ms:.1f} ms; " +
-          "; ".join(f"{name} {e.launches} {e.ms:.1f} ms" for name, e in
-                    (("norm", m.profile_get(41)), ("rope", m.profile_get(42)), ("swiglu", m.profile_get(43)),
-                     ("xprep", m.profile_get(44)), ("collectives", comm))))
-    m.profile(0)
+    # live roofline of the dominant kernel: the step's own Q4_K matvec launches (same weights, shapes, pairings and
+    # order) captured into a graph and replayed alone, timed with CUDA events on the model's stream
+    barrier()
+    mv_steps = min(steps, 16)
+    mv_ms, mv_bytes = m.bench_matvecs(B, mv_steps)
+    mv_ms = tp.max_over_ranks(dist, mv_ms)
+    kernel_ms_per_step = mv_ms / mv_steps
+    trace(f"Q4_K matvec launches alone: {kernel_ms_per_step:.3f} ms per step for {mv_bytes / 1e9:.2f} GB "
+          f"(the whole step {ms_max / steps:.3f} ms)")
     hbm, _, peak_kind = measured_peaks()
-    achieved = q4.bytes / (q4.ms / 1e3) / 1e9 if q4.ms > 0 else None
+    achieved = mv_bytes / (kernel_ms_per_step / 1e3) / 1e9
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "q4k_matvec_traffic.txt")
     if os.path.exists(tfile):
         for line in open(tfile):
             if line.startswith("dram_bytes_per_byte_algorithmic"):
-                traffic = float(line.split()[1]) * q4.bytes / max(q4.launches, 1)
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm if achieved else None, "traffic": traffic,
-                "kernel": "k_mmv_q4k (TMA-staged tensor-core Q4_K matvec)", "peak_source": peak_kind,
-                "launches": q4.launches, "avg_launch_us": 1e3 * q4.ms / max(q4.launches, 1),
-                "bytes_per_launch": q4.bytes / max(q4.launches, 1),
-                "q6k_achieved_gbs": q6.bytes / (q6.ms / 1e3) / 1e9 if q6.ms > 0 else None}
+                traffic = float(line.split()[1]) * mv_bytes
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": traffic, "traffic_scope": "per step (the step's Q4_K launches), from the DRAM bytes per "
+                "algorithmic byte of an ncu capture of the step's launches (profiles/q4k_matvec_traffic.txt)",
+                "kernel": "k_mmv_q4k (tensor-core Q4_K matvec)", "peak_source": peak_kind,
+                "kernel_ms_per_step": kernel_ms_per_step, "bytes_per_step": mv_bytes,
+                "timing": "the step's Q4_K matvec launches replayed alone as a CUDA graph (wl_bench_matvecs), "
+                          "CUDA events; per GPU under tensor parallelism"}
 
-    trace("profiled pass done")
+    trace("kernel timing done")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.model == "70b" and not args.shard_of:
         cpu = cpu_baseline()
@@ -539,8 +536,6 @@ def main():
                         "device_chained": {"value": e2e_chained, "call": "wl_generate_greedy, chunk 16"}
                         if e2e_chained else None},
                 "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
-                "collectives": {"launches": comm.launches, "ms_per_step": comm.ms / max(min(steps, 8), 1)}
-                if world > 1 else None,
                 "load_s": load_s, "prefill_s": prefill_s,
                 "prefill_tok_s": B * args.prompt / prefill_s}
         print(json.dumps(line))

@@ -219,6 +219,12 @@ int32_t wl_generate_greedy(wl_model* model, wl_seq* seq, int32_t token, int32_t 
  * step, taken from a seeded draw), no host copies, and returns the device time of the whole loop measured with CUDA
  * events on the model's stream. Sequence lengths advance by `steps`. */
 int32_t wl_bench_decode(wl_model* model, wl_seq* const* seqs, int32_t N, int32_t steps, double* device_ms);
+/* No counterpart in the reference: the Q4_K matvec launches of one decode step of T rows (1..8; the step's weights,
+ * shapes, pairings and order), captured into a CUDA graph and replayed `steps` times alone, for the dominant kernel's
+ * rate inside a step. Returns the device milliseconds of the replays (the maximum over the GPUs of a tensor-parallel
+ * model) and the algorithmic bytes per step of those launches (this GPU's share). Outputs go to the model's scratch
+ * rows; sequences are untouched. */
+int32_t wl_bench_matvecs(wl_model* model, int32_t T, int32_t steps, double* device_ms, double* bytes_per_step);
 /* on != 0 records CUDA events around every matvec/matmul launch (and clears the counters); 0 stops. */
 int32_t wl_profile(wl_model* model, int32_t on);
 /* The counters of weight format `type` (see wl_profile_entry). */

@@ -127,6 +127,7 @@ def lib():
         "wl_selftest_allreduce_timeout": (I32, [I32, I32]),
         "wl_synth_tensor": (I32, [I32, U64, C.c_uint32, I64, I64, F, F, P, P]),
         "wl_bench_decode": (I32, [P, P, I32, I32, C.POINTER(C.c_double)]),
+        "wl_bench_matvecs": (I32, [P, I32, I32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "wl_profile": (I32, [P, I32]), "wl_profile_get": (I32, [P, I32, C.POINTER(ProfileEntry)]),
     }
     for name, (res, args) in sig.items():

@@ -261,6 +261,22 @@ int32_t wl_bench_decode(wl_model* model, wl_seq* const* seqs, int32_t N, int32_t
     });
 }
 
+int32_t wl_bench_matvecs(wl_model* model, int32_t T, int32_t steps, double* device_ms, double* bytes_per_step)
+{
+    return guarded([&]() -> int32_t {
+        if (!model || !device_ms) return wl::fail(WL_EINVAL, "wl_bench_matvecs: model and device_ms are required");
+        if (model->g) {
+            std::vector<double> ms((size_t)model->g->size(), 0.0), by((size_t)model->g->size(), 0.0);
+            model->g->run([&](int g) { ms[(size_t)g] = model->g->shard(g).bench_matvecs(T, steps, &by[(size_t)g]); });
+            *device_ms = *std::max_element(ms.begin(), ms.end());
+            if (bytes_per_step) *bytes_per_step = by[0];
+            return WL_OK;
+        }
+        *device_ms = model->m->bench_matvecs(T, steps, bytes_per_step);
+        return WL_OK;
+    });
+}
+
 int32_t wl_profile(wl_model* model, int32_t on)
 {
     return guarded([&]() -> int32_t {

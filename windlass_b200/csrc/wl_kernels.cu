@@ -830,7 +830,6 @@ void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStr
 // other rows; each range keeps a running max m, sum l and unnormalised output o per head across its tiles. With
 // S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order.
 constexpr int ATT_P = 64;           // positions per tile
-constexpr int ATT_THREADS = 128;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 {
@@ -843,7 +842,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // order: the maximum over the ranges, then NA accumulator sets of ranges s = a, a + NA, ... in range order, the
 // sets added in set order), reading the partials through L2 (other CTAs wrote them).
 template <int S>
-__device__ __forceinline__ void attn_merge4(const float* __restrict__ part, const float* __restrict__ ml, int t,
+__device__ __noinline__ void attn_merge4(const float* __restrict__ part, const float* __restrict__ ml, int t,
                                             int heads, int hd, int v, float (&f)[4])
 {
     constexpr int NA = S > 16 ? 4 : 1;
@@ -887,18 +886,28 @@ __device__ __forceinline__ void attn_merge4(const float* __restrict__ part, cons
 // (attn_merge4: bit for bit k_attn_combine) and writes the output and, with prep, its prepared activations (the
 // group's G * HD values are whole superblocks), then resets the counter for the next launch, so no combine launch is
 // needed.
-template <int HD, int G, bool MERGE>
-__global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
-                                                           float scale, const RowKV* __restrict__ rows, int layer,
-                                                           const int32_t* __restrict__ pos, int S,
-                                                           float* __restrict__ out, float* __restrict__ part,
-                                                           float* __restrict__ ml, int* __restrict__ tickets,
-                                                           uint8_t* __restrict__ prep)
+// Threads of an attention CTA: half a thread per (head, dim) of the group, 128 to 512, a multiple of 64, so that the
+// 64 positions of a tile times the G heads spread over every thread in the score phase and the G * HD outputs over
+// every thread in the value phase (at decode a CTA is alone on its SM, and more warps hide more latency).
+constexpr int attn_threads(int HD, int G)
+{
+    return (G * HD / 2) >= 512 ? 512 : (G * HD / 2) <= 128 ? 128 : (G * HD / 2) / 64 * 64;
+}
+
+template <int HD, int G, bool MERGE, int NT = attn_threads(HD, G)>
+__global__ void __launch_bounds__(NT, 1) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
+                                                  float scale, const RowKV* __restrict__ rows, int layer,
+                                                  const int32_t* __restrict__ pos, int S,
+                                                  float* __restrict__ out, float* __restrict__ part,
+                                                  float* __restrict__ ml, int* __restrict__ tickets,
+                                                  uint8_t* __restrict__ prep)
 {
     constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
     constexpr int CH = HD / 8;              // 16-byte chunks per row
-    constexpr int DPT = (HD + ATT_THREADS - 1) / ATT_THREADS;   // output dims per thread
-    constexpr int GH = (G + 1) / 2;         // heads per thread in the score phase
+    constexpr int HS = NT / ATT_P;          // score phase: a thread per position and heads hs, hs + HS, ...
+    constexpr int GH = (G + HS - 1) / HS;
+    constexpr int VI = G * HD;              // value phase: items (dim, head), item tid + NT * k of each thread
+    constexpr int IPT = (VI + NT - 1) / NT;
     extern __shared__ __align__(16) uint8_t smraw[];
     uint16_t* ks = reinterpret_cast<uint16_t*>(smraw);           // [ATT_P][KP]
     uint16_t* vs = ks + ATT_P * KP;                               // [ATT_P][KP]
@@ -917,33 +926,37 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
     const int per = (n + S - 1) / S;
     const int start = sp * per, end = min(n, start + per);
     const float* qp = q + (int64_t)t * QD + (int64_t)kvh * G * HD;
-    for (int i = tid; i < G * HD; i += ATT_THREADS) qs[i] = qp[i];
+    for (int i = tid; i < G * HD; i += NT) qs[i] = qp[i];
     if (tid < G) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
     const uint16_t* K = rk.k + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
     const uint16_t* V = rk.v + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
-    float o[DPT][G];
+    float o[IPT];
+    int od[IPT], oh[IPT];
 #pragma unroll
-    for (int k2 = 0; k2 < DPT; ++k2)
-#pragma unroll
-        for (int h = 0; h < G; ++h) o[k2][h] = 0.f;
-    // score work: position pl of the tile, heads hs, hs + 2, ...
+    for (int k2 = 0; k2 < IPT; ++k2) {
+        const int item = tid + NT * k2;
+        od[k2] = item % HD;
+        oh[k2] = item < VI ? item / HD : -1;
+        o[k2] = 0.f;
+    }
     const int pl = tid % ATT_P, hs = tid / ATT_P;
     for (int tile0 = start; tile0 < end; tile0 += ATT_P) {
         const int cnt = min(ATT_P, end - tile0);
-        for (int i = tid; i < cnt * CH; i += ATT_THREADS) {
+        for (int i = tid; i < cnt * CH; i += NT) {
             const int r = i / CH, c = i % CH;
             cp_async16(ks + r * KP + c * 8, K + (int64_t)(tile0 + r) * KD + c * 8);
             cp_async16(vs + r * KP + c * 8, V + (int64_t)(tile0 + r) * KD + c * 8);
         }
         cp_async_wait_all();
         __syncthreads();
-        if (G > 1 || hs == 0) {
+        // scores: the reference's four interleaved accumulators per (head, position), each on one thread
+        {
             float s4[GH][4];
 #pragma unroll
             for (int hh = 0; hh < GH; ++hh) s4[hh][0] = s4[hh][1] = s4[hh][2] = s4[hh][3] = 0.f;
-            if (pl < cnt) {
+            if (pl < cnt && hs < G) {
                 const uint16_t* kr = ks + pl * KP;
-#pragma unroll
+#pragma unroll 2
                 for (int d0 = 0; d0 < HD; d0 += 8) {
                     const uint4 kv8 = *reinterpret_cast<const uint4*>(kr + d0);
                     const uint16_t* kh = reinterpret_cast<const uint16_t*>(&kv8);
@@ -952,24 +965,27 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
                     for (int e = 0; e < 8; ++e) kf[e] = h2f(kh[e]);
 #pragma unroll
                     for (int hh = 0; hh < GH; ++hh) {
-                        const int h = G > 1 ? hs + 2 * hh : 0;
-                        const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + d0);
-                        const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + d0 + 4);
-                        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                        const int h = hs + HS * hh;
+                        if (h < G) {
+                            const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + d0);
+                            const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + d0 + 4);
+                            const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) s4[hh][e & 3] = __fadd_rn(s4[hh][e & 3], __fmul_rn(qv[e], kf[e]));
+                            for (int e = 0; e < 8; ++e) s4[hh][e & 3] = __fadd_rn(s4[hh][e & 3], __fmul_rn(qv[e], kf[e]));
+                        }
                     }
                 }
             }
 #pragma unroll
             for (int hh = 0; hh < GH; ++hh) {
-                const int h = G > 1 ? hs + 2 * hh : 0;
-                sc[h][pl] = pl < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(s4[hh][0], s4[hh][1]), __fadd_rn(s4[hh][2], s4[hh][3])), scale)
-                                     : -INFINITY;
+                const int h = hs + HS * hh;
+                if (h < G)
+                    sc[h][pl] = pl < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(s4[hh][0], s4[hh][1]), __fadd_rn(s4[hh][2], s4[hh][3])), scale)
+                                         : -INFINITY;
             }
         }
         __syncthreads();
-        for (int h = warp; h < G; h += ATT_THREADS / 32) {
+        for (int h = warp; h < G; h += NT / 32) {
             float m = fmaxf(sc[h][lane], sc[h][lane + 32]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
@@ -980,33 +996,27 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
             }
         }
         __syncthreads();
-        if (G > 1 || hs == 0) {
 #pragma unroll
-            for (int hh = 0; hh < GH; ++hh) {
-                const int h = G > 1 ? hs + 2 * hh : 0;
-                sc[h][pl] = pl < cnt ? expf(__fsub_rn(sc[h][pl], tmax[h])) : 0.f;
-            }
+        for (int hh = 0; hh < GH; ++hh) {
+            const int h = hs + HS * hh;
+            if (h < G) sc[h][pl] = pl < cnt ? expf(__fsub_rn(sc[h][pl], tmax[h])) : 0.f;
         }
         __syncthreads();
-        for (int h = warp; h < G; h += ATT_THREADS / 32) {
+        for (int h = warp; h < G; h += NT / 32) {
             double sum = (double)sc[h][lane] + (double)sc[h][lane + 32];
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
             if (lane == 0) tsum[h] = sum;
         }
-        // o = o * e^(m_old - m_new) + sum_j p_j v_j, from the staged values
+        // o = o * e^(m_old - m_new) + sum_j p_j v_j per (dim, head) item, positions in order, from the staged values
 #pragma unroll
-        for (int k2 = 0; k2 < DPT; ++k2) {
-            const int d = tid + k2 * ATT_THREADS;
-            if (d < HD) {
-#pragma unroll
-                for (int h = 0; h < G; ++h) o[k2][h] = __fmul_rn(o[k2][h], alpha[h]);
-                for (int j = 0; j < cnt; ++j) {
-                    const float v = h2f(vs[j * KP + d]);
-#pragma unroll
-                    for (int h = 0; h < G; ++h) o[k2][h] = __fadd_rn(o[k2][h], __fmul_rn(sc[h][j], v));
-                }
-            }
+        for (int k2 = 0; k2 < IPT; ++k2) {
+            if (oh[k2] < 0) continue;
+            const int d = od[k2], h = oh[k2];
+            float acc = __fmul_rn(o[k2], alpha[h]);
+#pragma unroll 4
+            for (int j = 0; j < cnt; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[h][j], h2f(vs[j * KP + d])));
+            o[k2] = acc;
         }
         __syncthreads();
         if (tid < G) {
@@ -1016,15 +1026,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
         __syncthreads();
     }
 #pragma unroll
-    for (int k2 = 0; k2 < DPT; ++k2) {
-        const int d = tid + k2 * ATT_THREADS;
-        if (d >= HD) continue;
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-            const int head = kvh * G + h;
-            if (S == 1) out[(int64_t)t * QD + (int64_t)head * HD + d] = (float)((double)o[k2][h] / lrun[h]);
-            else part[(((int64_t)t * heads + head) * S + sp) * HD + d] = o[k2][h];
-        }
+    for (int k2 = 0; k2 < IPT; ++k2) {
+        if (oh[k2] < 0) continue;
+        const int d = od[k2], head = kvh * G + oh[k2];
+        if (S == 1) out[(int64_t)t * QD + (int64_t)head * HD + d] = (float)((double)o[k2] / lrun[oh[k2]]);
+        else part[(((int64_t)t * heads + head) * S + sp) * HD + d] = o[k2];
     }
     if (S > 1 && tid < G) {
         float* mlp = ml + (((int64_t)t * heads + kvh * G + tid) * S + sp) * 2;
@@ -1032,8 +1038,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
         mlp[1] = (float)lrun[tid];
     }
     if (!MERGE || S == 1) return;
+    constexpr int NG = NT / 64;     // 64-thread groups, a superblock each per round
     __shared__ int last;
-    __shared__ float pscratch[2][2];
+    __shared__ float pscratch[NG][2];
     __threadfence();                // this CTA's partials are visible GPU-wide before its ticket
     __syncthreads();
     if (tid == 0) {
@@ -1046,9 +1053,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_part(const float* __restri
     __threadfence();
     constexpr int GV = G * HD;      // the group's values: GV / 256 whole superblocks
     const int v0 = kvh * GV, grp = tid >> 6, t64 = tid & 63;
-    for (int r = 0; r < (GV + 511) / 512; ++r) {
-        const int sbl = 2 * r + grp;                    // superblock of the group this half of the CTA serves
-        if (sbl * 256 >= GV) continue;                  // (uniform per half)
+    for (int r = 0; r < (GV / 256 + NG - 1) / NG; ++r) {
+        const int sbl = NG * r + grp;                   // superblock of the group this 64-thread group serves
+        if (sbl * 256 >= GV) continue;                  // (uniform per group)
         const int v = v0 + sbl * 256 + 4 * t64;
         float f[4];
         if (S == 16) attn_merge4<16>(part, ml, t, heads, HD, v, f);
@@ -1162,21 +1169,33 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
         if (dev < 64 && !attr_set[dev]) {
             WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
             WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, false, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
             attr_set[dev] = true;
         }
     }
     float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
     int* tickets = reinterpret_cast<int*>(part + (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (HD + 2));
-    // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks
+    // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks. Wide CTAs
+    // (attn_threads) when the grid leaves most SMs with one CTA (a decode step of one or two rows); otherwise 128
+    // threads, several CTAs per SM. Both give the same bits: every score and every (dim, head) sum is one thread's.
     constexpr bool can_merge = (G * HD) % 256 == 0;
+    constexpr int WIDE = attn_threads(HD, G);
+    const bool wide = (int64_t)S * kv_heads * T <= 2 * 148;
+    const dim3 grid(S, kv_heads, T);
+    uint8_t* pb = prep ? prep->blocks : (uint8_t*)nullptr;
     if (S > 1 && can_merge) {
-        launch(k_attn_part<HD, G, true>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale,
-               rows, layer, pos, S, out, part, ml, tickets, prep ? prep->blocks : (uint8_t*)nullptr);
+        if (wide) launch(k_attn_part<HD, G, true, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows, layer,
+                         pos, S, out, part, ml, tickets, pb);
+        else launch(k_attn_part<HD, G, true, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos,
+                    S, out, part, ml, tickets, pb);
         launched();
         return;
     }
-    launch(k_attn_part<HD, G, false>, dim3(S, kv_heads, T), dim3(ATT_THREADS), smem, s, q, heads, kv_heads, scale, rows,
-           layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+    if (wide) launch(k_attn_part<HD, G, false, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows, layer,
+                     pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+    else launch(k_attn_part<HD, G, false, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos, S,
+                out, part, ml, tickets, (uint8_t*)nullptr);
     launched();
     if (S > 1) {
         auto comb = S == 16 ? k_attn_combine<16> : S == 32 ? k_attn_combine<32> : k_attn_combine<64>;

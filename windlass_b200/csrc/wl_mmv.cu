@@ -1442,11 +1442,17 @@ static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb,
 // The model's decode matvec on tile-major Q4_K: one 16-row CTA per row tile. In a decode step every matvec follows a
 // small kernel, and CTAs this size start under programmatic dependent launch while that kernel still runs (four fit
 // beside it on an SM) and stream their first stages meanwhile; the 32-row form above, faster back to back, lost 6 %
-// of the 70B step for that reason (measured on B200).
+// of the 70B step for that reason. Eight warps per CTA for up to 8 x SMs row tiles at one or two columns; four warps
+// (twice the superblocks per warp, twice the CTAs per SM) for taller matrices and from three columns on, where a
+// CTA's stages grow with the columns (measured in the 70B step on B200: 0.8 % at b1, 8 % at b8).
 static void dispatch_q4k16(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                            float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
-    dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
+    const int tiles_n = (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
+    if (p.nc >= 3 || tiles_n >= 8 * sm_count())
+        dispatch_q4k<true, 4>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
+    else
+        dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
 }
 
 void prepare_matvec_mma()

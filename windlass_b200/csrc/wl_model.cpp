@@ -942,17 +942,10 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
 
 void Model::matmul2(const Weight& a, const Weight& b, const float* x, int T, float* ya, float* yb)
 {
-    // one launch when the pair fits in about two waves of CTAs (16-row tiles; up to 4 CTAs per SM for one or two
-    // columns): that is where the second matrix would otherwise run as a small separate launch. Longer matrices run
-    // as two launches, which programmatic dependent launch already overlaps.
-    static const int sms = [] {
-        int dev = 0, n = 148;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        return n;
-    }();
+    // one launch for both matrices at decode: the second matrix's CTAs follow the first's with no launch boundary
+    // between them (measured on the 70B step: 4 us a layer less than two launches for gate and up)
     const bool pair = T <= 8 && a.present() && b.present() && a.type == 12 && b.type == 12 && a.tiles && b.tiles &&
-                      a.cols == b.cols && a.row_base % 16 == 0 && b.row_base % 16 == 0 && xprep_buf_ &&
-                      (a.rows + 15) / 16 + (b.rows + 15) / 16 <= 8 * sms;
+                      a.cols == b.cols && a.row_base % 16 == 0 && b.row_base % 16 == 0 && xprep_buf_;
     if (!pair) {
         matmul(a, x, T, ya, 0, true);
         matmul(b, x, T, yb, 0, true);
@@ -1512,6 +1505,81 @@ double Model::bench_decode(Seq* const* seqs, int N, int steps)
     flush_profile();
     for (int i = 0; i < N; ++i) seqs[i]->length = len[i] + steps;
     stats_.tokens += (int64_t)N * steps;
+    return ms;
+}
+
+// The Q4_K matvec launches of one decode step of T rows, with the step's weights, shapes, column counts, pairings and
+// order (q and k, o, gate and up, down per layer), captured into a CUDA graph and replayed `steps` times alone: the
+// dominant kernel's own rate, with the programmatic-launch overlap between consecutive matvecs that the step has
+// between its kernels. The activations are whatever the prepared-activation buffer holds (the timing does not depend
+// on them); outputs go to the model's scratch rows. Returns the device milliseconds of the replays and, through bytes,
+// the matvecs' algorithmic bytes per step (weights + activations in + outputs).
+double Model::bench_matvecs(int T, int steps, double* bytes)
+{
+    if (T < 1 || T > 8 || steps <= 0) WL_THROW(WL_EINVAL, "wl_bench_matvecs: 1 <= T <= 8 and steps > 0");
+    WL_CUDA(cudaSetDevice(device_));
+    ensure_workspace(T, T);
+    if (!xprep_buf_) WL_THROW(WL_EUNSUPPORTED, "wl_bench_matvecs: the model has no tensor-core matvec");
+    double total = 0.0;
+    auto q4 = [](const Weight& w) { return w.present() && w.type == 12 && w.tiles; };
+    auto count = [&](const Weight& w) {
+        if (q4(w)) total += (double)w.rows * w.row_bytes + 4.0 * T * ((double)w.cols + w.rows);
+    };
+    // the launches of one step; the prepared activations are taken as already made for every input, so no prep
+    // kernel runs (matmul and matmul2 reuse a matching prepared input)
+    auto launches = [&]() {
+        for (const LayerW& L : L_) {
+            if (L.moe) continue;
+            float* dummy = xn_;
+            auto ready = [&](int cols) { prep_x_ = dummy; prep_cols_ = cols; prep_nc_ = T; };
+            if (q4(L.q) && q4(L.k)) { ready(L.q.cols); matmul2(L.q, L.k, dummy, T, q_, k_); }
+            if (q4(L.o)) { ready(L.o.cols); matmul(L.o, dummy, T, o_, 0, true); }
+            if (q4(L.gate) && q4(L.up)) { ready(L.gate.cols); matmul2(L.gate, L.up, dummy, T, g_, u_); }
+            if (q4(L.down)) { ready(L.down.cols); matmul(L.down, dummy, T, o_, 0, true); }
+        }
+        prep_x_ = nullptr;
+    };
+    for (const LayerW& L : L_) {
+        if (L.moe) continue;
+        if (q4(L.q) && q4(L.k)) { count(L.q); count(L.k); }
+        count(L.o);
+        if (q4(L.gate) && q4(L.up)) { count(L.gate); count(L.up); }
+        count(L.down);
+    }
+    launches();                         // eager first: kernel attributes are set outside the capture
+    const int64_t l0 = k::launches();
+    cudaGraph_t graph = nullptr;
+    WL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+        launches();
+    } catch (...) {
+        cudaStreamEndCapture(stream_, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+    }
+    WL_CUDA(cudaStreamEndCapture(stream_, &graph));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    WL_CUDA(e);
+    const int64_t nodes = k::launches() - l0;
+    k::uncount_launches(nodes);
+    WL_CUDA(cudaGraphLaunch(exec, stream_));        // warm
+    cudaEvent_t e0, e1;
+    WL_CUDA(cudaEventCreate(&e0));
+    WL_CUDA(cudaEventCreate(&e1));
+    WL_CUDA(cudaEventRecord(e0, stream_));
+    for (int i = 0; i < steps; ++i) WL_CUDA(cudaGraphLaunch(exec, stream_));
+    WL_CUDA(cudaEventRecord(e1, stream_));
+    WL_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    WL_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(exec);
+    graph_launches_ += nodes * (steps + 1);
+    check_device_error();
+    if (bytes) *bytes = total;
     return ms;
 }
 

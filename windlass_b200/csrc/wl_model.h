@@ -130,6 +130,7 @@ public:
 
     // Device-resident decode loop for benchmarks: returns the device milliseconds of `steps` steps.
     double bench_decode(Seq* const* seqs, int N, int steps);
+    double bench_matvecs(int T, int steps, double* bytes);
     void set_profiling(bool on);
     wl_profile_entry profile(int type);
 

@@ -210,6 +210,12 @@ class CudaTransformer:
         check(lib().wl_bench_decode(self._h, arr, len(seqs), steps, C.byref(ms)))
         return ms.value
 
+    def bench_matvecs(self, T, steps):
+        """(device ms, bytes per step) of the step's Q4_K matvec launches replayed alone (wl_bench_matvecs)."""
+        ms, by = C.c_double(), C.c_double()
+        check(lib().wl_bench_matvecs(self._h, int(T), int(steps), C.byref(ms), C.byref(by)))
+        return ms.value, by.value
+
     def profile(self, on):
         check(lib().wl_profile(self._h, int(on)))
 
