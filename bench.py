@@ -170,11 +170,29 @@ def sweep_cpu_cell(fmt, t, raw, rows, cols, b, reps=3, max_s=20.0):
     return best
 
 
+def sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args):
+    """One row of the sweep table: the GPU time per call, its rates and fractions, and the CPU cell beside it."""
+    alg = nbytes + 4 * b * (R + K)
+    cell = {"format": f, "rows": R, "cols": K, "batch": b, "us": ms * 1e3,
+            "gbs": alg / (ms / 1e3) / 1e9, "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,
+            "tflops": 2.0 * R * K * b / (ms / 1e3) / 1e12,
+            "bf16_frac": 2.0 * R * K * b / (ms / 1e3) / 1e12 / bf16}
+    if raw0 is not None and (b <= 64 or R * K <= 8192 * 8192):
+        cs_ = sweep_cpu_cell(f, t, raw0, R, K, b)
+        cell["cpu_us"] = cs_ * 1e6
+        cell["cpu_gbs"] = alg / cs_ / 1e9
+        cell["cpu_gflops"] = 2.0 * R * K * b / cs_ / 1e9
+    trace(f"{f} {R}x{K} b{b}: {ms * 1e3:.1f} us, {cell['gbs']:.0f} GB/s ({cell['hbm_frac']:.2f}), "
+          f"{cell['tflops']:.2f} TFLOP/s" + (f"; CPU {cell['cpu_us'] / 1e3:.1f} ms" if "cpu_us" in cell else ""))
+    return cell
+
+
 def sweep(args):
     """the matvec/matmul sweep (8192 x 8192 by default; --shapes adds the 70B layer's shapes). Per shape,
-    format and batch column count: the time of one call (wl_matvec_tiles on weights repacked once for Q4_K/Q6_K, else
-    wl_matvec: activation prep + matvec; wl_gemm_tiles for Q4_K at b > 8, else wl_matmul), from CUDA events around
-    replays of a CUDA graph of `iters` calls over rotating weight copies whose total exceeds L2, and the weight
+    format and batch column count: the time of one call over rotating weight copies whose total exceeds L2. Q4_K and
+    Q6_K at b <= 8: the decode matvec on weights repacked once, launches back to back as in a decode step
+    (wl_bench_matvec_tiles); other formats at b <= 8: wl_matvec (activation prep + matvec); b > 8: wl_gemm_tiles for
+    Q4_K, else wl_matmul; the last two from CUDA events around replays of a CUDA graph of `iters` calls. Then the weight
     bandwidth (b <= 8) or TFLOP/s (b >= 64), with the reference's CPU arithmetic (the C oracle, all host threads,
     best of 3) beside each cell. One JSON line with the whole table."""
     import ctypes as C
@@ -230,6 +248,18 @@ def sweep(args):
             for b in batches:
                 x = torch.randn(b, K, device="cuda")
                 y = torch.empty(b, R, device="cuda")
+                if b <= 8 and tiled:
+                    # the decode matvec as it runs inside a step: launches back to back over rotating copies, one
+                    # CUDA graph (wl_bench_matvec_tiles), activations prepared once
+                    arr = (C.c_void_p * len(tws))(*[tw.data_ptr() for tw in tws])
+                    dms = C.c_double()
+                    n_it = args.iters * 5
+                    _lib.check(L.wl_bench_matvec_tiles(t, arr, len(tws), R, K, C.c_void_p(x.data_ptr()), b,
+                                                       C.c_void_p(y.data_ptr()), n_it, C.byref(dms),
+                                                       C.c_void_p(stream.cuda_stream)))
+                    ms = dms.value / n_it
+                    rows_out.append(sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args))
+                    continue
 
                 def run(i):
                     w = ws[i % copies]
@@ -266,19 +296,7 @@ def sweep(args):
                 torch.cuda.synchronize()
                 ms = e0.elapsed_time(e1) / (reps * args.iters)
                 del graph
-                alg = nbytes + 4 * b * (R + K)
-                cell = {"format": f, "rows": R, "cols": K, "batch": b, "us": ms * 1e3,
-                        "gbs": alg / (ms / 1e3) / 1e9, "hbm_frac": alg / (ms / 1e3) / 1e9 / hbm,
-                        "tflops": 2.0 * R * K * b / (ms / 1e3) / 1e12,
-                        "bf16_frac": 2.0 * R * K * b / (ms / 1e3) / 1e12 / bf16}
-                if raw0 is not None and (b <= 64 or R * K <= 8192 * 8192):
-                    cs_ = sweep_cpu_cell(f, t, raw0, R, K, b)
-                    cell["cpu_us"] = cs_ * 1e6
-                    cell["cpu_gbs"] = alg / cs_ / 1e9
-                    cell["cpu_gflops"] = 2.0 * R * K * b / cs_ / 1e9
-                rows_out.append(cell)
-                trace(f"{f} {R}x{K} b{b}: {ms * 1e3:.1f} us, {cell['gbs']:.0f} GB/s ({cell['hbm_frac']:.2f}), "
-                      f"{cell['tflops']:.2f} TFLOP/s" + (f"; CPU {cell['cpu_us'] / 1e3:.1f} ms" if "cpu_us" in cell else ""))
+                rows_out.append(sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args))
             del ws
             if tiled:
                 del tws

@@ -284,6 +284,14 @@ int32_t wl_tiles_size(int32_t type, int32_t rows, int32_t cols, int64_t* bytes);
 int32_t wl_make_tiles(int32_t type, const void* dev_w, int32_t rows, int32_t cols, void* dev_tiles, void* stream);
 int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
                         int32_t ncols, float* dev_y, void* stream);
+/* No counterpart in the reference: the standalone rate of the decode matvec. The activations (ncols of 1..8) are
+ * prepared once, then `iters` wl_matvec_tiles launches over the tile buffers dev_tiles[i % copies] (each made by
+ * wl_make_tiles from a rows x cols matrix; several copies whose total exceeds L2 keep the reads in HBM) run back to
+ * back as one CUDA graph on an internal stream, as they follow each other inside a decode step; device_ms is the
+ * CUDA-event time of the whole graph. dev_y receives the last launch's product. */
+int32_t wl_bench_matvec_tiles(int32_t type, const void* const* dev_tiles, int32_t copies, int32_t rows, int32_t cols,
+                              const float* dev_x, int32_t ncols, float* dev_y, int32_t iters, double* device_ms,
+                              void* stream);
 /* No counterpart in the reference: wl_matvec_tiles (Q4_K) with the superblocks of every row split into `parts` equal
  * contiguous ranges (1 <= parts <= cols / 256), as the model runs matrices with few rows: dev_y_parts holds parts
  * partial products, dev_y_parts[p*ncols*rows + t*rows + r], whose sum in order p = 0, 1, ... is W[r] . x[t]. */

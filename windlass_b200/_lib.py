@@ -122,6 +122,7 @@ def lib():
         "wl_make_tiles": (I32, [I32, P, I32, I32, P, P]),
         "wl_matvec_tiles": (I32, [I32, P, I32, I32, P, I32, P, P]),
         "wl_matvec_tiles_split": (I32, [I32, P, I32, I32, P, I32, I32, P, P]),
+        "wl_bench_matvec_tiles": (I32, [I32, P, I32, I32, I32, P, I32, P, I32, C.POINTER(C.c_double), P]),
         "wl_matmul": (I32, [I32, P, I32, I32, P, I32, P, I32, P]),
         "wl_gemm_tiles": (I32, [I32, P, I32, I32, P, I32, P, P]),
         "wl_selftest_allreduce_timeout": (I32, [I32, I32]),

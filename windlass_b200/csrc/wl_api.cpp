@@ -745,6 +745,78 @@ int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32
     });
 }
 
+int32_t wl_bench_matvec_tiles(int32_t type, const void* const* dev_tiles, int32_t copies, int32_t rows, int32_t cols,
+                              const float* dev_x, int32_t ncols, float* dev_y, int32_t iters, double* device_ms,
+                              void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (!wl::k::tiles_supported(type, cols))
+            return wl::fail(WL_EUNSUPPORTED, "wl_bench_matvec_tiles: no tile layout for this type and width");
+        if (rows <= 0 || ncols <= 0 || ncols > 8 || copies <= 0 || iters <= 0)
+            return wl::fail(WL_EINVAL, "wl_bench_matvec_tiles: rows, copies, iters > 0 and 1 <= ncols <= 8");
+        if (!dev_tiles || !dev_x || !dev_y || !device_ms) return wl::fail(WL_EINVAL, "wl_bench_matvec_tiles: null pointer");
+        for (int i = 0; i < copies; ++i)
+            if (!dev_tiles[i] || (uintptr_t)dev_tiles[i] % 16 != 0)
+                return wl::fail(WL_EINVAL, "wl_bench_matvec_tiles: every tile buffer must be 16-byte aligned");
+        if ((uintptr_t)dev_x % 16 != 0) return wl::fail(WL_EINVAL, "wl_bench_matvec_tiles: dev_x must be 16-byte aligned");
+        const cudaStream_t s = (cudaStream_t)stream;
+        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
+        int* err = (int*)scratch;
+        const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, ncols);
+        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launches behind all earlier work
+        wl::k::xprep(dev_x, cols, cols, ncols, p, s);
+        auto run = [&]() {
+            for (int i = 0; i < iters; ++i)
+                wl::k::matvec_tiles(type, (const uint8_t*)dev_tiles[i % copies], 0, rows, cols, p, dev_y, rows, err, s);
+        };
+        run();                          // kernel attributes are set outside the capture
+        cudaStream_t cs = nullptr;
+        WL_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        try {
+            cudaEvent_t dep = nullptr;
+            WL_CUDA(cudaEventCreateWithFlags(&dep, cudaEventDisableTiming));
+            WL_CUDA(cudaEventRecord(dep, s));
+            WL_CUDA(cudaStreamWaitEvent(cs, dep, 0));
+            cudaEventDestroy(dep);
+            cudaGraph_t graph = nullptr;
+            const int64_t l0 = wl::k::launches();
+            WL_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+            for (int i = 0; i < iters; ++i)
+                wl::k::matvec_tiles(type, (const uint8_t*)dev_tiles[i % copies], 0, rows, cols, p, dev_y, rows, err, cs);
+            WL_CUDA(cudaStreamEndCapture(cs, &graph));
+            wl::k::uncount_launches(wl::k::launches() - l0);
+            const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            WL_CUDA(ie);
+            WL_CUDA(cudaGraphLaunch(exec, cs));     // warm
+            WL_CUDA(cudaEventCreate(&e0));
+            WL_CUDA(cudaEventCreate(&e1));
+            WL_CUDA(cudaEventRecord(e0, cs));
+            WL_CUDA(cudaGraphLaunch(exec, cs));
+            WL_CUDA(cudaEventRecord(e1, cs));
+            WL_CUDA(cudaEventSynchronize(e1));
+            float ms = 0.f;
+            WL_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+            *device_ms = ms;
+        } catch (...) {
+            if (exec) cudaGraphExecDestroy(exec);
+            if (e0) cudaEventDestroy(e0);
+            if (e1) cudaEventDestroy(e1);
+            cudaStreamSynchronize(cs);
+            cudaStreamDestroy(cs);
+            throw;
+        }
+        cudaGraphExecDestroy(exec);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        WL_CUDA(cudaStreamSynchronize(cs));
+        cudaStreamDestroy(cs);
+        return WL_OK;
+    });
+}
+
 int32_t wl_matvec_tiles_split(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
                               int32_t ncols, int32_t parts, float* dev_y_parts, void* stream)
 {

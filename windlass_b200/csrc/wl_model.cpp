@@ -51,6 +51,9 @@ void Model::init_device(const wl_options& opt)
     WL_CUDA(cudaSetDevice(device_));
     k::init_tables();
     WL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    WL_CUDA(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
+    WL_CUDA(cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming));
+    WL_CUDA(cudaEventCreateWithFlags(&join_ev_, cudaEventDisableTiming));
     max_batch_ = opt.max_batch > 0 ? opt.max_batch : 64;
     use_graphs_ = opt.use_graphs != 0;
     prefill_path_ = opt.prefill_path;
@@ -745,6 +748,7 @@ Model::~Model()
 {
     if (device_ >= 0) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (side_) cudaStreamSynchronize(side_);
     drop_graphs();
     if (own_) free_seq(own_);
     dfree(arena_); dfree(rope_table_);
@@ -768,6 +772,9 @@ Model::~Model()
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+    if (fork_ev_) cudaEventDestroy(fork_ev_);
+    if (join_ev_) cudaEventDestroy(join_ev_);
+    if (side_) cudaStreamDestroy(side_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -1183,8 +1190,27 @@ void Model::layer(int l, int T, int max_n)
     } else {
         pre_norm(T, L.attn_norm, L.q.tiles != nullptr);
     }
-    matmul2(L.q, L.k, xn_, T, q_, k_);
-    matmul(L.v, xn_, T, v_, 0, true);
+    // at decode the small v matvec runs on a side stream beside the q+k launch (it reads the same prepared input and
+    // writes only v), filling the SMs that the q+k launch's last CTAs leave idle; RoPE waits for both
+    const bool fork = T <= 8 && L.v.tiles && !streamed_ && prep_x_ == xn_ && prep_nc_ == T && prep_cols_ == L.v.cols;
+    if (fork) {
+        WL_CUDA(cudaEventRecord(fork_ev_, stream_));
+        WL_CUDA(cudaStreamWaitEvent(side_, fork_ev_, 0));
+        std::swap(stream_, side_);
+        try {
+            matmul(L.v, xn_, T, v_, 0, true);
+        } catch (...) {
+            std::swap(stream_, side_);
+            throw;
+        }
+        std::swap(stream_, side_);
+        WL_CUDA(cudaEventRecord(join_ev_, side_));
+        matmul2(L.q, L.k, xn_, T, q_, k_);
+        WL_CUDA(cudaStreamWaitEvent(stream_, join_ev_, 0));
+    } else {
+        matmul2(L.q, L.k, xn_, T, q_, k_);
+        matmul(L.v, xn_, T, v_, 0, true);
+    }
     if (L.qb.present()) k::add_bias(q_, L.qb.d, T, QD, stream_);
     if (L.kb.present()) k::add_bias(k_, L.kb.d, T, KD, stream_);
     if (L.vb.present()) k::add_bias(v_, L.vb.d, T, KD, stream_);

@@ -220,6 +220,9 @@ private:
     int prefill_path_ = 0;
     bool each_token_ = false;             // a ForwardBatch step: every row computed as if alone (no GEMM)
     cudaStream_t stream_ = nullptr;
+    // decode steps run the v matvec on side_ (forked after the pre-norm, joined before RoPE) beside q and k
+    cudaStream_t side_ = nullptr;
+    cudaEvent_t fork_ev_ = nullptr, join_ev_ = nullptr;
     std::vector<LayerW> L_;
     Weight embd_, output_;
     Vec out_norm_;
