@@ -1041,16 +1041,18 @@ __global__ void __launch_bounds__(NT, 1) k_attn_part(const float* __restrict__ q
     constexpr int NG = NT / 64;     // 64-thread groups, a superblock each per round
     __shared__ int last;
     __shared__ float pscratch[NG][2];
-    __threadfence();                // this CTA's partials are visible GPU-wide before its ticket
+    // the CTA's partials (written by many threads, ordered before thread 0 by the barrier) are released GPU-wide
+    // with thread 0's ticket; the CTA that takes the last ticket acquires every range's partials with it
     __syncthreads();
     if (tid == 0) {
         int* ctr = tickets + t * kv_heads + kvh;
-        last = atomicAdd(ctr, 1) == S - 1;
+        int ticket;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(ticket) : "l"(ctr) : "memory");
+        last = ticket == S - 1;
         if (last) *ctr = 0;         // every range has taken its ticket: ready for the next launch
     }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     constexpr int GV = G * HD;      // the group's values: GV / 256 whole superblocks
     const int v0 = kvh * GV, grp = tid >> 6, t64 = tid & 63;
     for (int r = 0; r < (GV / 256 + NG - 1) / NG; ++r) {
