@@ -202,6 +202,29 @@ int32_t wl_forward_argmax(wl_model* model, wl_seq* seq, const int32_t* tokens, i
 /* wl_forward_batch, returning ids_out[i] = the argmax of row i. */
 int32_t wl_forward_batch_argmax(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
                                 int32_t* ids_out, volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+
+/* ---- sampling on the device (Sampler.Sample, src/Engine.cs:361-380: the decode loop's choice, :187 and :202, and
+ * the batching loop's, src/BatchEngine.cs:164-172). The caller keeps the random generator: `draw` is its next uniform double in [0, 1) (Random.NextDouble()),
+ * taken only when temperature > 0, as the reference takes one. temperature <= 0 gives the greedy id (the draw is not
+ * read). Otherwise p[i] = exp((logit[i] - max) / temperature) in double; top_p >= 1 picks the first id at which the
+ * running sum of p in index order reaches draw * sum(p); top_p < 1 orders ids by p descending, keeps the shortest
+ * prefix whose running sum reaches top_p * sum(p), and picks the first id of it at which the running sum reaches
+ * draw * (the prefix's sum). The sums are tree-ordered prefix sums where the reference adds one term at a time, and
+ * equal probabilities keep ascending ids (a stable sort) where the reference's unstable Array.Sort orders them its
+ * own way: a choice can differ only when the draw falls within a few units in the last place of the boundary between
+ * two ids, or among exactly equal probabilities. ---- */
+
+/* wl_forward returning the last row's sampled id in *id_out (WL_EINVAL for a draw outside [0, 1) at temperature > 0).
+ * Same arguments, errors, cancel and progress behaviour otherwise. */
+int32_t wl_forward_sample(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
+                          double temperature, double top_p, double draw, int32_t* id_out,
+                          volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+/* wl_forward_batch returning ids_out[i] = row i sampled with temperature[i], top_p[i] and draws[i] (each batch job's
+ * own options and generator, src/BatchEngine.cs:164-172). */
+int32_t wl_forward_batch_sample(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
+                                const double* temperature, const double* top_p, const double* draws, int32_t* ids_out,
+                                volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+
 /* Greedy decode of seq (NULL = the model's own) chained on the device, the decode loop of Engine.cs:187-203 at
  * temperature 0: step s forwards `token` (s = 0) or ids_out[s-1] at the sequence's next position and writes the
  * argmax of its logits to ids_out[s]. The id never visits the host between steps: `chunk` steps (0 = 16, at most 64)
@@ -241,6 +264,11 @@ int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms);
 /* The greedy choice of wl_forward_argmax on `rows` rows of V device floats: dev_ids[r] = the lowest index of row r's
  * largest value (Argmax, src/Engine.cs:329-334; a NaN at index 0 gives 0). Synchronous on `stream`. */
 int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev_ids, void* stream);
+
+/* Sampler.Sample of the sampled forward calls on V device floats: *dev_id = the chosen id. Synchronous on `stream`;
+ * allocates its workspace (about 48 bytes a logit) for the call. */
+int32_t wl_sample(const float* dev_logits, int32_t V, double temperature, double top_p, double draw, int32_t* dev_id,
+                  void* stream);
 
 /* Synchronises `device` and reports whether a device-side wait of a kernel-level export (wl_matvec, wl_matvec_tiles,
  * wl_matvec_static, wl_gemm_tiles, wl_matmul) gave up since the last report: WL_ETIMEDOUT (and the code) if one did,

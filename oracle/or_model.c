@@ -597,3 +597,70 @@ int or_argmax(const float* logits, int n)
     for (int i = 1; i < n; i++) if (logits[i] > logits[best]) best = i;
     return best;
 }
+
+/* Sampler.Sample (Engine.cs:361-380) with the generator's uniform draw passed in (rng.NextDouble(), read only at
+ * temperature > 0). The sums run one term at a time in the reference's order. Array.Sort(keys, idx) on keys -p is an
+ * unstable introsort whose order among equal probabilities is the .NET runtime's own; this restatement orders them
+ * by ascending id (a total order: p descending, then id ascending), the order the device's stable radix sort gives.
+ * *margin (optional) = the distance, relative to sum(p), from the draw's running remainder (and, for top_p < 1, from
+ * the nucleus limit) to the nearest boundary between two ids around the choice: the choice is the same under any
+ * summation order whose rounding error stays below it. 0 when the choice fell back (no prefix reached the target). */
+typedef struct { double p; int id; } or_samp_item;
+
+static int or_samp_cmp(const void* a, const void* b)
+{
+    const or_samp_item* x = (const or_samp_item*)a;
+    const or_samp_item* y = (const or_samp_item*)b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return (x->id > y->id) - (x->id < y->id);
+}
+
+int or_sample(const float* logits, int n, double temperature, double top_p, double draw, double* margin)
+{
+    int best = or_argmax(logits, n);
+    if (margin) *margin = 1.0;
+    if (temperature <= 0) return best;
+    float max = logits[best];
+    double* p = (double*)malloc(sizeof(double) * (size_t)n);
+    double sum = 0;
+    for (int i = 0; i < n; i++) {
+        float d = logits[i] - max;
+        p[i] = exp((double)d / temperature);
+        sum += p[i];
+    }
+    int out = -1;
+    double m = 0;
+    if (top_p >= 1.0) {
+        double r = draw * sum;
+        for (int i = 0; i < n; i++) {
+            double before = r;
+            r -= p[i];
+            if (r <= 0) { out = i; m = fmin(before, -r) / sum; break; }
+        }
+        if (out < 0) out = best;
+    } else {
+        or_samp_item* it = (or_samp_item*)malloc(sizeof(or_samp_item) * (size_t)n);
+        for (int i = 0; i < n; i++) { it[i].p = p[i]; it[i].id = i; }
+        qsort(it, (size_t)n, sizeof(or_samp_item), or_samp_cmp);
+        double cum = 0, limit = top_p * sum, mn = 0;
+        int k = 0;
+        while (k < n) {
+            double before = cum;
+            cum += it[k].p;
+            k++;
+            if (cum >= limit) { mn = fmin(limit - before, cum - limit) / sum; break; }
+        }
+        double pick = draw * cum;
+        for (int i = 0; i < k; i++) {
+            double before = pick;
+            pick -= it[i].p;
+            if (pick <= 0) { out = it[i].id; m = fmin(fmin(before, -pick) / sum, mn); break; }
+        }
+        if (out < 0) out = it[0].id;
+        free(it);
+    }
+    free(p);
+    if (margin) *margin = m;
+    return out;
+}

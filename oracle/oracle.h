@@ -154,6 +154,9 @@ void or_route(const float* logits, int n, int k, int renorm, int32_t* sel, float
 void or_rmsnorm_rows(const float* x, int n, int dim, const float* w, float eps, float* y);
 /* Greedy pick of Sampler.Sample (Engine.cs:356-360): the first index of the largest logit. */
 int or_argmax(const float* logits, int n);
+/* Sampler.Sample (Engine.cs:361-380) with the generator's uniform draw passed in; *margin (optional) = the relative
+ * distance of the draw (and the nucleus limit) from the nearest boundary between ids around the choice. */
+int or_sample(const float* logits, int n, double temperature, double top_p, double draw, double* margin);
 
 /* Stage-level hooks for the bounded CPU baseline: one decoder layer of the model on T rows of x (in place),
  * positions pos0.., appending to seq. Returns 0 or -1. */

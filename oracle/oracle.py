@@ -89,6 +89,7 @@ def lib():
             "or_route": (None, [P, I, I, I, P, P, P]),
             "or_rmsnorm_rows": (None, [P, I, I, P, F, P]),
             "or_argmax": (I, [P, I]),
+            "or_sample": (I, [P, I, C.c_double, C.c_double, C.c_double, P]),
             "or_layer": (I, [P, I, P, I, I, P, C.c_char_p, I]),
             "or_default_threads": (I, []),
             "or_synth_gguf": (P, [C.POINTER(SynthSpec), I, I]),
@@ -243,6 +244,15 @@ def route(logits, k, renorm):
 def argmax(logits):
     logits = np.ascontiguousarray(logits, dtype=np.float32)
     return lib().or_argmax(_ptr(logits), logits.size)
+
+
+def sample(logits, temperature, top_p, draw):
+    """Sampler.Sample (Engine.cs:361-380) with the uniform draw passed in: (id, margin), margin the relative distance
+    of the draw (and the nucleus limit) from the nearest boundary between two ids around the choice."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    m = C.c_double(0.0)
+    i = lib().or_sample(_ptr(logits), logits.size, float(temperature), float(top_p), float(draw), C.byref(m))
+    return i, m.value
 
 
 def write_synth(path, spec, threads=0):

@@ -113,6 +113,9 @@ def lib():
         "wl_forward_argmax": (I32, [P, P, P, I32, I32, I32, P, P, PROGRESS, P]),
         "wl_forward_batch_argmax": (I32, [P, P, P, I32, P, P, PROGRESS, P]),
         "wl_forward_mixed": (I32, [P, P, P, I32, P, P, P, P, PROGRESS, P]),
+        "wl_forward_sample": (I32, [P, P, P, I32, I32, C.c_double, C.c_double, C.c_double, P, P, PROGRESS, P]),
+        "wl_forward_batch_sample": (I32, [P, P, P, I32, P, P, P, P, P, PROGRESS, P]),
+        "wl_sample": (I32, [P, I32, C.c_double, C.c_double, C.c_double, P, P]),
         "wl_generate_greedy": (I32, [P, P, I32, I32, P, I32, I32, P, C.POINTER(I32), P]),
         "wl_argmax": (I32, [P, I32, I32, P, P]), "wl_route": (I32, [P, I32, I32, I32, I32, P, P, P]), "wl_kernel_status": (I32, [I32]),
         "wl_dequant": (I32, [I32, P, I64, P, P]),

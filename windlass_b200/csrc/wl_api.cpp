@@ -369,16 +369,18 @@ int32_t wl_length(const wl_model* model, int32_t* n)
 }
 
 namespace {
-// wl_forward and wl_forward_argmax: rows come back as logits (logits_out) or as their argmax (ids_out).
+// wl_forward, wl_forward_argmax and wl_forward_sample: rows come back as logits (logits_out), as their argmax
+// (ids_out) or as ids sampled with the options in samp (ids_out and samp).
 int32_t forward_rows(const char* fn, wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
                      int32_t all_rows, float* logits_out, int32_t* ids_out, volatile const int32_t* cancel,
-                     wl_progress_fn progress, void* user)
+                     wl_progress_fn progress, void* user, const wl::Model::SampleRows* samp = nullptr)
 {
     if (model && T == 0) return wl::fail(WL_EINVAL, "No tokens to run.");
     if (!model || !tokens || !(logits_out || ids_out))
         return wl::fail(WL_EINVAL, std::string(fn) + ": model, tokens and " + (ids_out || !logits_out ? "ids_out" : "logits_out") + " are required");
     if (seq && seq->owner != model) return wl::fail(WL_EINVAL, std::string(fn) + ": the sequence belongs to another model");
     auto call = [&](wl::Model& m, wl::Seq* s, float* out, int32_t* ids, wl_progress_fn pf, void* u) {
+        if (ids && samp) return m.forward_sample(s, tokens, T, pos0, *samp, ids, cancel, pf, u);
         return ids ? m.forward_argmax(s, tokens, T, pos0, all_rows != 0, ids, cancel, pf, u)
                    : m.forward(s, tokens, T, pos0, all_rows != 0, out, cancel, pf, u);
     };
@@ -408,7 +410,7 @@ int32_t forward_rows(const char* fn, wl_model* model, wl_seq* seq, const int32_t
 
 int32_t forward_batch_rows(const char* fn, wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
                            float* logits_out, int32_t* ids_out, volatile const int32_t* cancel,
-                           wl_progress_fn progress, void* user)
+                           wl_progress_fn progress, void* user, const wl::Model::SampleRows* samp = nullptr)
 {
     if (!model || !seqs || !tokens || !(logits_out || ids_out))
         return wl::fail(WL_EINVAL, std::string(fn) + ": model, seqs, tokens and " + (ids_out || !logits_out ? "ids_out" : "logits_out") + " are required");
@@ -416,6 +418,7 @@ int32_t forward_batch_rows(const char* fn, wl_model* model, wl_seq* const* seqs,
     for (int i = 0; i < N; ++i)
         if (!seqs[i] || seqs[i]->owner != model) return wl::fail(WL_EINVAL, std::string(fn) + ": a sequence belongs to another model");
     auto call = [&](wl::Model& m, wl::Seq* const* ss, float* out, int32_t* ids, wl_progress_fn pf, void* u) {
+        if (ids && samp) return m.forward_batch_sample(ss, tokens, N, *samp, ids, cancel, pf, u);
         return ids ? m.forward_batch_argmax(ss, tokens, N, ids, cancel, pf, u)
                    : m.forward_batch(ss, tokens, N, out, cancel, pf, u);
     };
@@ -482,6 +485,35 @@ int32_t wl_forward_batch_argmax(wl_model* model, wl_seq* const* seqs, const int3
         if (!ids_out) return wl::fail(WL_EINVAL, "wl_forward_batch_argmax: model, seqs, tokens and ids_out are required");
         return forward_batch_rows("wl_forward_batch_argmax", model, seqs, tokens, N, nullptr, ids_out, cancel, progress,
                                   user);
+    });
+}
+
+int32_t wl_forward_sample(wl_model* model, wl_seq* seq, const int32_t* tokens, int32_t T, int32_t pos0,
+                          double temperature, double top_p, double draw, int32_t* id_out,
+                          volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!id_out && model && T != 0) return wl::fail(WL_EINVAL, "wl_forward_sample: model, tokens and id_out are required");
+        if (temperature > 0.0 && !(draw >= 0.0 && draw < 1.0)) return wl::fail(WL_EINVAL, "wl_forward_sample: the draw must be in [0, 1)");
+        const wl::Model::SampleRows sr{&temperature, &top_p, &draw};
+        return forward_rows("wl_forward_sample", model, seq, tokens, T, pos0, 0, nullptr, id_out, cancel, progress,
+                            user, &sr);
+    });
+}
+
+int32_t wl_forward_batch_sample(wl_model* model, wl_seq* const* seqs, const int32_t* tokens, int32_t N,
+                                const double* temperature, const double* top_p, const double* draws, int32_t* ids_out,
+                                volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    return guarded([&]() -> int32_t {
+        if (!ids_out || !temperature || !top_p || !draws)
+            return wl::fail(WL_EINVAL, "wl_forward_batch_sample: model, seqs, tokens, temperature, top_p, draws and ids_out are required");
+        for (int i = 0; i < N; ++i)
+            if (temperature[i] > 0.0 && !(draws[i] >= 0.0 && draws[i] < 1.0))
+                return wl::fail(WL_EINVAL, "wl_forward_batch_sample: every draw must be in [0, 1)");
+        const wl::Model::SampleRows sr{temperature, top_p, draws};
+        return forward_batch_rows("wl_forward_batch_sample", model, seqs, tokens, N, nullptr, ids_out, cancel,
+                                  progress, user, &sr);
     });
 }
 
@@ -627,6 +659,29 @@ int32_t wl_argmax(const float* dev_logits, int32_t V, int32_t rows, int32_t* dev
             throw;
         }
         WL_CUDA(cudaFree(scratch));
+        return WL_OK;
+    });
+}
+
+int32_t wl_sample(const float* dev_logits, int32_t V, double temperature, double top_p, double draw, int32_t* dev_id,
+                  void* stream)
+{
+    return guarded([&]() -> int32_t {
+        if (V <= 0) return wl::fail(WL_EINVAL, "wl_sample: V must be positive");
+        if (!dev_logits || !dev_id) return wl::fail(WL_EINVAL, "wl_sample: null pointer");
+        if (temperature > 0.0 && !(draw >= 0.0 && draw < 1.0)) return wl::fail(WL_EINVAL, "wl_sample: the draw must be in [0, 1)");
+        const cudaStream_t s = (cudaStream_t)stream;
+        void* ws = nullptr;
+        WL_CUDA(cudaMalloc(&ws, wl::k::sample_workspace_bytes(V)));
+        try {
+            wl::k::sample_workspace_init(ws, s);
+            wl::k::sample(dev_logits, V, temperature, top_p, draw, ws, dev_id, s);
+            WL_CUDA(cudaStreamSynchronize(s));
+        } catch (...) {
+            cudaFree(ws);
+            throw;
+        }
+        WL_CUDA(cudaFree(ws));
         return WL_OK;
     });
 }

@@ -220,6 +220,14 @@ void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned
             int32_t* next_tok, int32_t* next_pos, cudaStream_t s);
 // Blocks per row of that launch (for tests of its arithmetic).
 int64_t argmax_blocks(int V, int n);
+// Sampler.Sample (src/Engine.cs:361-380) on one row of V device logits with the host's uniform draw in [0, 1) (its
+// rng.NextDouble(); unused at temperature <= 0): *out_id (device) = the chosen id. ws is sample_workspace_bytes(V)
+// of device memory, its first 256 bytes zeroed once by sample_workspace_init; rows sampled one after another on one
+// stream may share it.
+size_t sample_workspace_bytes(int V);
+void sample_workspace_init(void* ws, cudaStream_t s);
+void sample(const float* logits, int V, double temperature, double top_p, double draw, void* ws, int32_t* out_id,
+            cudaStream_t s);
 // Route (Transformer.cs:315-340) for T rows of n router logits: sel[t*k+j], wts[t*k+j].
 // With count_one (T = 1 only), *count_one += k: a single token's picks are k distinct experts, so the step needs no
 // count_experts launch.

@@ -768,6 +768,7 @@ Model::~Model()
     dfree(logits_part_); dfree(logits_all_); dfree(flag_d_); hfree(flag_h_);
     dfree(pg_); dfree(pu_); dfree(py_); dfree(expert_count_d_);
     dfree(ids_d_); dfree(amax_key_); dfree(amax_count_); dfree(gen_d_); hfree(h_ids_); hfree(h_gen_);
+    dfree(sample_ws_);
     if (pprep_) cudaFree(pprep_);
     comm_.reset();           // after the graphs that hold its collectives
     for (const ProfileMark& m : marks_) { cudaEventDestroy(m.start); cudaEventDestroy(m.stop); }
@@ -1393,7 +1394,18 @@ int32_t Model::run(int T, const std::vector<RowKV>& rows, const std::vector<int3
         head(T, first);
         stage_release(c_.layers);
     }
-    if (ids) {
+    if (ids && sampling_) {
+        if (!sample_ws_) {
+            sample_ws_ = dalloc<uint8_t>((int64_t)k::sample_workspace_bytes(c_.vocab));
+            k::sample_workspace_init(sample_ws_, stream_);
+        }
+        for (int r = 0; r < T - first; ++r)
+            k::sample(logits_ + (int64_t)r * c_.vocab, c_.vocab, sampling_->temperature[r], sampling_->top_p[r],
+                      sampling_->draw[r], sample_ws_, ids_d_ + r, stream_);
+        WL_CUDA(cudaMemcpyAsync(h_ids_, ids_d_, sizeof(int32_t) * (size_t)(T - first), cudaMemcpyDeviceToHost, stream_));
+        WL_CUDA(cudaStreamSynchronize(stream_));
+        for (int r = 0; r < T - first; ++r) ids[r] = h_ids_[r];
+    } else if (ids) {
         k::argmax(logits_, c_.vocab, T - first, amax_key_, amax_count_, ids_d_, nullptr, nullptr, stream_);
         WL_CUDA(cudaMemcpyAsync(h_ids_, ids_d_, sizeof(int32_t) * (size_t)(T - first), cudaMemcpyDeviceToHost, stream_));
         WL_CUDA(cudaStreamSynchronize(stream_));
@@ -1655,6 +1667,39 @@ int32_t Model::forward_argmax(Seq* sq, const int32_t* tokens, int T, int pos0, b
                               volatile const int32_t* cancel, wl_progress_fn progress, void* user)
 {
     return forward_impl(sq, tokens, T, pos0, all_rows, nullptr, ids, cancel, progress, user);
+}
+
+namespace {
+// Sets a model's sampling options for one call and clears them however the call ends.
+struct SamplingScope {
+    const Model::SampleRows*& slot;
+    SamplingScope(const Model::SampleRows*& s, const Model::SampleRows* v) : slot(s) { slot = v; }
+    ~SamplingScope() { slot = nullptr; }
+};
+
+void check_sample_rows(const Model::SampleRows& sr, int n)
+{
+    if (!sr.temperature || !sr.top_p || !sr.draw) WL_THROW(WL_EINVAL, "Sampling needs a temperature, top_p and draw for each row.");
+    for (int r = 0; r < n; ++r)
+        if (sr.temperature[r] > 0.0 && !(sr.draw[r] >= 0.0 && sr.draw[r] < 1.0))
+            WL_THROW(WL_EINVAL, "A sampling draw must be in [0, 1).");
+}
+}  // namespace
+
+int32_t Model::forward_sample(Seq* sq, const int32_t* tokens, int T, int pos0, const SampleRows& sr, int32_t* id,
+                              volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    check_sample_rows(sr, 1);
+    SamplingScope scope(sampling_, &sr);
+    return forward_impl(sq, tokens, T, pos0, false, nullptr, id, cancel, progress, user);
+}
+
+int32_t Model::forward_batch_sample(Seq* const* seqs, const int32_t* tokens, int N, const SampleRows& sr, int32_t* ids,
+                                    volatile const int32_t* cancel, wl_progress_fn progress, void* user)
+{
+    check_sample_rows(sr, N);
+    SamplingScope scope(sampling_, &sr);
+    return forward_batch_impl(seqs, tokens, N, nullptr, ids, cancel, progress, user);
 }
 
 int32_t Model::forward_impl(Seq* sq, const int32_t* tokens, int T, int pos0, bool all_logits, float* out, int32_t* ids,

@@ -90,6 +90,18 @@ public:
                            volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     int32_t forward_batch_argmax(Seq* const* seqs, const int32_t* tokens, int N, int32_t* ids,
                                  volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    // The same passes with Sampler.Sample (src/Engine.cs:361-380) made on the device: returned row r is sampled with
+    // temperature[r], top_p[r] and the host's uniform draw[r] in [0, 1) (its rng.NextDouble(), unused at temperature
+    // <= 0), and ids gets the chosen id.
+    struct SampleRows {
+        const double* temperature;
+        const double* top_p;
+        const double* draw;
+    };
+    int32_t forward_sample(Seq* seq, const int32_t* tokens, int T, int pos0, const SampleRows& sr, int32_t* id,
+                           volatile const int32_t* cancel, wl_progress_fn progress, void* user);
+    int32_t forward_batch_sample(Seq* const* seqs, const int32_t* tokens, int N, const SampleRows& sr, int32_t* ids,
+                                 volatile const int32_t* cancel, wl_progress_fn progress, void* user);
     // One pass over several sequences' new tokens at once (a decode step that prompts join: continuous batching):
     // sequence i takes counts[i] tokens at its next positions, tokens holding them sequence after sequence; out (or
     // ids) gets each sequence's last row, in sequence order. Each row attends to its own sequence only.
@@ -272,6 +284,10 @@ private:
     unsigned long long* amax_key_ = nullptr;
     unsigned* amax_count_ = nullptr;
     int32_t* h_ids_ = nullptr;
+    // device sampling: the rows' options during a forward_sample / forward_batch_sample call, and the sampler's
+    // workspace (one row's, made at the first sampled call; its first 256 bytes stay zero between rows)
+    const SampleRows* sampling_ = nullptr;
+    void* sample_ws_ = nullptr;
     int32_t* gen_d_ = nullptr;
     int32_t* h_gen_ = nullptr;
     float* ew_d_ = nullptr;

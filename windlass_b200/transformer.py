@@ -170,6 +170,33 @@ class CudaTransformer:
                                             out.ctypes.data_as(C.c_void_p), cancel.ptr if cancel else None, cb, None))
         return out[:N]
 
+    def forward_sample(self, tokens, temperature, top_p, draw, pos0=0, cancel=None, on_stage=None, seq=None):
+        """forward() with Sampler.Sample (src/Engine.cs:361-380) made on the device: the last row's sampled id.
+        draw is the caller's uniform double in [0, 1) (rng.NextDouble(), drawn only at temperature > 0)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(1, dtype=np.int32)
+        cb = _lib.PROGRESS(lambda d, t, u: on_stage(d, t)) if on_stage else _lib.PROGRESS()
+        check(lib().wl_forward_sample(self._h, seq._h if seq is not None else None, tokens.ctypes.data_as(C.c_void_p),
+                                      int(tokens.size), pos0, float(temperature), float(top_p), float(draw),
+                                      out.ctypes.data_as(C.c_void_p), cancel.ptr if cancel else None, cb, None))
+        return int(out[0])
+
+    def forward_batch_sample(self, seqs, tokens, temperature, top_p, draws, cancel=None, on_stage=None):
+        """forward_batch() returning each row sampled on the device with its own temperature, top_p and draw
+        (arrays of N, or scalars for every row): an int32 array of N ids."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        N = int(tokens.size)
+        arr = (C.c_void_p * max(N, 1))(*[s._h for s in seqs])
+        t, p, d = (np.ascontiguousarray(np.broadcast_to(np.asarray(v, dtype=np.float64), (max(N, 1),)))
+                   for v in (temperature, top_p, draws))
+        out = np.empty(max(N, 1), dtype=np.int32)
+        cb = _lib.PROGRESS(lambda d_, t_, u: on_stage(d_, t_)) if on_stage else _lib.PROGRESS()
+        check(lib().wl_forward_batch_sample(self._h, arr, tokens.ctypes.data_as(C.c_void_p), N,
+                                            t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+                                            d.ctypes.data_as(C.c_void_p), out.ctypes.data_as(C.c_void_p),
+                                            cancel.ptr if cancel else None, cb, None))
+        return out[:N]
+
     def forward_mixed(self, seqs, token_lists, cancel=None, on_stage=None, argmax=False):
         """One pass over several sequences' new tokens (a decode step that prompts join): sequence i takes
         token_lists[i]; returns each sequence's last-row logits ([N][vocab]), or its greedy id (argmax=True)."""
