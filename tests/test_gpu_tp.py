@@ -64,6 +64,8 @@ def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
         pytest.skip(f"needs {n} GPUs")
     O = oracle
     sp = spec_of(spec)
+    if sp.ff % (n * (32 if sp.type_ffn_down == O.Q8_0 else 256)):
+        pytest.skip(f"{spec}'s ffn_down columns ({sp.ff}) do not split into whole blocks over {n} GPUs")
     (tmp_path / "fused").mkdir()
     (tmp_path / "nccl").mkdir()
     res = run_ranks(n, spec, tmp_path / "fused")

@@ -151,18 +151,16 @@ __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* e
 
 // The consumer's side of the fused all-reduce, run by every thread of every CTA of the consuming kernel after its
 // grid-dependency wait (so this rank's producing matvec has completed): one CTA announces sequence number q on every
-// peer (this rank's partial sits in its own slot), then threads 0..G-1 wait for each peer's announcement of q or
-// later. A wait gives up after ar.wait_ns of %globaltimer time (the host sets AR_WAIT_NS, 10 s), records code 2 in
+// peer (this rank's partial sits in its own slot), lane g of its first warp storing to peer g, so that the G - 1
+// system-scope releases go out as one warp instruction rather than one after another (each waits for the stores
+// before it to reach their peer); then threads 0..G-1 wait for each peer's announcement of q or later. A wait gives up after ar.wait_ns of %globaltimer time (the host sets AR_WAIT_NS, 10 s), records code 2 in
 // *err and returns (the sums are then garbage and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot
 // hang the GPU.
 __device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q, bool announcer)
 {
     const int slot = (int)(q % AR_SLOTS);
-    if (announcer && threadIdx.x == 0) {
-        __threadfence_system();
-        for (int g = 0; g < ar.G; ++g)
-            if (g != ar.rank) st_release_sys(ar.peer_flags[g] + slot * AR_MAX_RANKS + ar.rank, q);
-    }
+    if (announcer && threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank)
+        st_release_sys(ar.peer_flags[threadIdx.x] + slot * AR_MAX_RANKS + ar.rank, q);
     if (threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank) {
         const unsigned long long* f = ar.flags + slot * AR_MAX_RANKS + threadIdx.x;
         const unsigned long long t0 = globaltimer_ns();
@@ -250,14 +248,24 @@ __global__ void __launch_bounds__(256) k_norm_prep(float* __restrict__ x, const 
             const unsigned long long q = ar_seq(ar.epoch, ar.idx);
             ar_sync(ar, q, blockIdx.x == 0 && blockIdx.y == 0);
             const size_t off = ((size_t)(q % AR_SLOTS) * AR_COLS + ar.row0 + t) * (size_t)E + i0;
-            oa = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off));
-            ob = __ldcv(reinterpret_cast<const float4*>(ar.data[0] + off + 4));
-            for (int src = 1; src < ar.G; ++src) {
-                const float* ps = ar.data[src] + off;
-                const float4 ua = __ldcv(reinterpret_cast<const float4*>(ps)), ub = __ldcv(reinterpret_cast<const float4*>(ps + 4));
-                oa = make_float4(__fadd_rn(oa.x, ua.x), __fadd_rn(oa.y, ua.y), __fadd_rn(oa.z, ua.z), __fadd_rn(oa.w, ua.w));
-                ob = make_float4(__fadd_rn(ob.x, ub.x), __fadd_rn(ob.y, ub.y), __fadd_rn(ob.z, ub.z), __fadd_rn(ob.w, ub.w));
-            }
+            // every rank's loads first (in flight together over NVLink), then the sums in rank order
+            float4 ua[AR_MAX_RANKS], ub[AR_MAX_RANKS];
+#pragma unroll
+            for (int src = 0; src < AR_MAX_RANKS; ++src)
+                if (src < ar.G) {
+                    ua[src] = __ldcv(reinterpret_cast<const float4*>(ar.data[src] + off));
+                    ub[src] = __ldcv(reinterpret_cast<const float4*>(ar.data[src] + off + 4));
+                }
+            oa = ua[0];
+            ob = ub[0];
+#pragma unroll
+            for (int src = 1; src < AR_MAX_RANKS; ++src)
+                if (src < ar.G) {
+                    oa = make_float4(__fadd_rn(oa.x, ua[src].x), __fadd_rn(oa.y, ua[src].y), __fadd_rn(oa.z, ua[src].z),
+                                     __fadd_rn(oa.w, ua[src].w));
+                    ob = make_float4(__fadd_rn(ob.x, ub[src].x), __fadd_rn(ob.y, ub[src].y), __fadd_rn(ob.z, ub[src].z),
+                                     __fadd_rn(ob.w, ub[src].w));
+                }
         } else {
             const float* orow = o + (int64_t)t * E + i0;
             oa = *reinterpret_cast<const float4*>(orow);
