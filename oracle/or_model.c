@@ -604,7 +604,8 @@ int or_argmax(const float* logits, int n)
  * by ascending id (a total order: p descending, then id ascending), the order the device's stable radix sort gives.
  * *margin (optional) = the distance, relative to sum(p), from the draw's running remainder (and, for top_p < 1, from
  * the nucleus limit) to the nearest boundary between two ids around the choice: the choice is the same under any
- * summation order whose rounding error stays below it. 0 when the choice fell back (no prefix reached the target). */
+ * summation order whose rounding error stays below it (the boundary before the first id is an exact zero and does
+ * not count). 0 when the choice fell back (no prefix reached the target). */
 typedef struct { double p; int id; } or_samp_item;
 
 static int or_samp_cmp(const void* a, const void* b)
@@ -636,7 +637,7 @@ int or_sample(const float* logits, int n, double temperature, double top_p, doub
         for (int i = 0; i < n; i++) {
             double before = r;
             r -= p[i];
-            if (r <= 0) { out = i; m = fmin(before, -r) / sum; break; }
+            if (r <= 0) { out = i; m = (i == 0 ? -r : fmin(before, -r)) / sum; break; }
         }
         if (out < 0) out = best;
     } else {
@@ -649,13 +650,13 @@ int or_sample(const float* logits, int n, double temperature, double top_p, doub
             double before = cum;
             cum += it[k].p;
             k++;
-            if (cum >= limit) { mn = fmin(limit - before, cum - limit) / sum; break; }
+            if (cum >= limit) { mn = (k == 1 ? cum - limit : fmin(limit - before, cum - limit)) / sum; break; }
         }
         double pick = draw * cum;
         for (int i = 0; i < k; i++) {
             double before = pick;
             pick -= it[i].p;
-            if (pick <= 0) { out = it[i].id; m = fmin(fmin(before, -pick) / sum, mn); break; }
+            if (pick <= 0) { out = it[i].id; m = fmin((i == 0 ? -pick : fmin(before, -pick)) / sum, mn); break; }
         }
         if (out < 0) out = it[0].id;
         free(it);

@@ -152,6 +152,42 @@ def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
         wl.check(L.wl_tiles_size(O.TYPE_OF["q8_0"], rows, cols, C.byref(nb)))
 
 
+@pytest.mark.parametrize("rows,cols", [(75, 2048), (1000, 256), (4099, 1024), (19000, 512), (8192, 8192)])
+def test_tile_matvec_columns_independent_of_batch(wl, oracle, rows, cols):
+    """A column's result from wl_matvec_tiles does not depend on how many columns share the call: at every column
+    count 1..8 each column equals the one-column call on that column bit for bit (the decode step's rows equal
+    single-sequence steps, tests/BatchTests.cs:29-94), on ragged rows, fewer superblocks than the warps that share a
+    row (1000 x 256), and row counts on both sides of the launch-shape threshold (19000 rows: 1188 row tiles);
+    within 1e-4 relative L2 of the float64 products."""
+    O = oracle
+    t = O.Q4_K
+    L = wl.lib()
+    w = weights(O, "q4_K", rows, cols, seed=rows + cols)
+    x = np.random.default_rng(rows).standard_normal((8, cols)).astype(np.float32)
+    dw, dx = dev(w), dev(x.reshape(-1))
+    nb = C.c_int64()
+    wl.check(L.wl_tiles_size(t, rows, cols, C.byref(nb)))
+    tiles = empty(nb.value, "uint8")
+    wl.check(L.wl_make_tiles(t, ptr(dw), rows, cols, ptr(tiles), None))
+    one = []
+    for c in range(8):
+        dy = empty(rows)
+        wl.check(L.wl_matvec_tiles(t, ptr(tiles), rows, cols, ptr(dev(x[c])), 1, ptr(dy), None))
+        one.append(host(dy))
+    one = np.stack(one)
+    if rows * cols <= 4096 * 4096:
+        dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
+        want = x.astype(np.float64) @ dec.T
+        for c in range(8):
+            assert rel_l2(one[c], want[c]) <= 1e-4, (c, rel_l2(one[c], want[c]))
+    for n in range(2, 9):
+        dy = empty(n * rows)
+        wl.check(L.wl_matvec_tiles(t, ptr(tiles), rows, cols, ptr(dx), n, ptr(dy), None))
+        got = host(dy).reshape(n, rows)
+        for c in range(n):
+            assert np.array_equal(got[c].view(np.uint32), one[c].view(np.uint32)), (n, c)
+
+
 @pytest.mark.parametrize("tname", ["q4_K", "q6_K"])
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 9), (100, 512, 64), (300, 1024, 65), (16, 256, 130),
                                           (2048, 2048, 200)])

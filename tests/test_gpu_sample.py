@@ -122,7 +122,7 @@ def test_forward_sample_is_sample_of_forward(wl, oracle, config0_file):
         tok = None
         for i in range(6):
             toks = prompt if i == 0 else [tok]
-            lg = m.forward(toks, seq=a)
+            lg = m.forward(toks, seq=a, pos0=a.length)
             t, p, d = (0.8, 0.9, float(rng.random())) if i % 2 else (1.2, 1.0, float(rng.random()))
             want, margin = oracle.sample(lg, t, p, d)
             got = m.forward_sample(toks, t, p, d, seq=b, pos0=b.length)
@@ -131,7 +131,7 @@ def test_forward_sample_is_sample_of_forward(wl, oracle, config0_file):
             assert b.length == a.length
             tok = want
         # temperature 0 is the greedy id, whatever the draw
-        lg = m.forward([tok], seq=a)
+        lg = m.forward([tok], seq=a, pos0=a.length)
         assert m.forward_sample([tok], 0.0, 0.5, 3.0, seq=b, pos0=b.length) == oracle.argmax(lg)
         with pytest.raises(_lib.ArgumentError):
             m.forward_sample([tok], 1.0, 1.0, 1.0, seq=b, pos0=b.length)

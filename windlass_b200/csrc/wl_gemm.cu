@@ -419,8 +419,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
 }
 
 // x (T rows of K fp32, ldx apart) to its bf16 planes hi = bf16(x), lo = bf16(x - hi), each [T][K].
-__global__ void k_split_bf16(const float* __restrict__ x, int64_t ldx, int K, int64_t n, __nv_bfloat16* __restrict__ hi,
-                             __nv_bfloat16* __restrict__ lo)
+__global__ void k_split_bf16(const float* x, int64_t ldx, int K, int64_t n, __nv_bfloat16* hi,
+                             __nv_bfloat16* lo)
 {
     pdl_trigger();
     pdl_wait();

@@ -69,7 +69,7 @@ void uncount_launches(int64_t n) { g_launches.fetch_sub(n, std::memory_order_rel
 // ------------------------------------------------------------------------------------------------------------------
 // dequant / embedding (bit-exact)
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void k_dequant(int type, const uint8_t* __restrict__ blocks, int64_t n, float* __restrict__ out)
+__global__ void k_dequant(int type, const uint8_t* blocks, int64_t n, float* out)
 {
     pdl_trigger();
     pdl_wait();
@@ -88,7 +88,7 @@ void dequant(int type, const void* blocks, int64_t n, float* out, cudaStream_t s
 }
 
 __global__ void k_embed(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows, int cols,
-                        const int32_t* __restrict__ tokens, float scale, float* __restrict__ x, int32_t* bad,
+                        const int32_t* tokens, float scale, float* x, int32_t* bad,
                         unsigned long long* epoch)
 {
     pdl_trigger();
@@ -398,8 +398,8 @@ enum { MV_GENERIC = 0, MV_Q4K = 1, MV_Q6K = 2, MV_Q8_0 = 3, MV_IQ4XS = 4, MV_IQ2
 
 template <int KIND, int NC>
 __global__ void __launch_bounds__(128) k_matvec(int type, const uint8_t* __restrict__ w, int64_t row_bytes, int rows,
-                                                int cols, const float* __restrict__ x, int64_t ldx,
-                                                float* __restrict__ y, int64_t ldy)
+                                                int cols, const float* x, int64_t ldx,
+                                                float* y, int64_t ldy)
 {
     pdl_trigger();
     pdl_wait();
@@ -587,7 +587,7 @@ void add_bias(float* y, const float* b, int T, int n, cudaStream_t s)
     launched();
 }
 
-__global__ void k_rope(float* x, int heads, int head_dim, int rope_dims, int neox, const int32_t* __restrict__ pos,
+__global__ void k_rope(float* x, int heads, int head_dim, int rope_dims, int neox, const int32_t* pos,
                        const float* __restrict__ table)
 {
     pdl_trigger();
@@ -615,8 +615,8 @@ void rope(float* x, int T, int heads, int head_dim, int rope_dims, int neox, con
     launched();
 }
 
-__global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, int kd,
-                            const RowKV* __restrict__ rows, int layer, const int32_t* __restrict__ pos)
+__global__ void k_kv_append(const float* k, const float* v, int kd,
+                            const RowKV* rows, int layer, const int32_t* pos)
 {
     pdl_trigger();
     pdl_wait();
@@ -640,9 +640,9 @@ void kv_append(const float* k, const float* v, int T, int kd, const RowKV* rows,
 
 // RoPE of q and k plus the fp16 KV append, one kernel: work items are q's rotation pairs, then k's values (rotated
 // pairs computed from both partners, unrotated dims copied), then v's values. The arithmetic is k_rope's.
-__global__ void k_rope_append(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, int heads,
-                              int kv_heads, int head_dim, int rope_dims, int neox, const int32_t* __restrict__ pos,
-                              const float* __restrict__ table, const RowKV* __restrict__ rows, int layer)
+__global__ void k_rope_append(float* q, const float* k, const float* v, int heads,
+                              int kv_heads, int head_dim, int rope_dims, int neox, const int32_t* pos,
+                              const float* __restrict__ table, const RowKV* rows, int layer)
 {
     pdl_trigger();
     const int t = blockIdx.y, half = rope_dims / 2, kd = kv_heads * head_dim;
@@ -704,12 +704,12 @@ void rope_append(float* q, const float* k, const float* v, int T, int heads, int
 // products; NEOX pairs (i, i + HD/2) then sit in one lane, rotated with k_rope_append's arithmetic. So q, the cache's K
 // and V are bit for bit those of k_rmsnorm8 twice and k_rope_append.
 template <int HD>
-__global__ void __launch_bounds__(128) k_qknorm_rope_append(float* __restrict__ q, const float* __restrict__ k,
-                                                            const float* __restrict__ v, int heads, int kv_heads,
+__global__ void __launch_bounds__(128) k_qknorm_rope_append(float* q, const float* k,
+                                                            const float* v, int heads, int kv_heads,
                                                             const float* __restrict__ qw, const float* __restrict__ kw,
-                                                            float eps, const int32_t* __restrict__ pos,
+                                                            float eps, const int32_t* pos,
                                                             const float* __restrict__ table,
-                                                            const RowKV* __restrict__ rows, int layer)
+                                                            const RowKV* rows, int layer)
 {
     constexpr int NV = HD / 32, NP = HD / 64, HALF = HD / 2;
     pdl_trigger();
@@ -791,8 +791,8 @@ bool qknorm_rope_append(float* q, const float* k, const float* v, int T, int hea
 }
 
 // SwiGlu (k_swiglu's arithmetic) and the prepared activations of the result, one 256-value superblock per CTA.
-__global__ void __launch_bounds__(64) k_swiglu_prep(float* __restrict__ g, const float* __restrict__ u, int F,
-                                                    uint8_t* __restrict__ prep)
+__global__ void __launch_bounds__(64) k_swiglu_prep(float* g, const float* u, int F,
+                                                    uint8_t* prep)
 {
     pdl_trigger();
     pdl_wait();
@@ -895,12 +895,12 @@ constexpr int attn_threads(int HD, int G)
 }
 
 template <int HD, int G, bool MERGE, int NT = attn_threads(HD, G)>
-__global__ void __launch_bounds__(NT, 1) k_attn_part(const float* __restrict__ q, int heads, int kv_heads,
-                                                  float scale, const RowKV* __restrict__ rows, int layer,
-                                                  const int32_t* __restrict__ pos, int S,
-                                                  float* __restrict__ out, float* __restrict__ part,
-                                                  float* __restrict__ ml, int* __restrict__ tickets,
-                                                  uint8_t* __restrict__ prep)
+__global__ void __launch_bounds__(NT, 1) k_attn_part(const float* q, int heads, int kv_heads,
+                                                  float scale, const RowKV* rows, int layer,
+                                                  const int32_t* pos, int S,
+                                                  float* out, float* part,
+                                                  float* ml, int* tickets,
+                                                  uint8_t* prep)
 {
     constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
     constexpr int CH = HD / 8;              // 16-byte chunks per row
@@ -1076,9 +1076,9 @@ __global__ void __launch_bounds__(NT, 1) k_attn_part(const float* __restrict__ q
 // lane 0 of the four adds the sets in set order, so the result is fixed for a given S. With prep, the superblock is
 // also written in the tensor-core matvec's activation layout. All loads of a thread are issued before their first use.
 template <int S>
-__global__ void __launch_bounds__(S > 16 ? 256 : 64) k_attn_combine(int heads, int hd, const float* __restrict__ part,
-                                                                    const float* __restrict__ ml,
-                                                                    float* __restrict__ out, uint8_t* __restrict__ prep)
+__global__ void __launch_bounds__(S > 16 ? 256 : 64) k_attn_combine(int heads, int hd, const float* part,
+                                                                    const float* ml,
+                                                                    float* out, uint8_t* prep)
 {
     constexpr int NA = S > 16 ? 4 : 1;
     constexpr int SPT = S / NA;                 // ranges per thread
@@ -1250,7 +1250,7 @@ bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
 // ------------------------------------------------------------------------------------------------------------------
 // elementwise
 // ------------------------------------------------------------------------------------------------------------------
-__global__ void k_swiglu(float* g, const float* __restrict__ u, int64_t n)
+__global__ void k_swiglu(float* g, const float* u, int64_t n)
 {
     pdl_trigger();
     pdl_wait();
@@ -1269,7 +1269,7 @@ void swiglu(float* g, const float* u, int64_t n, cudaStream_t s)
     launched();
 }
 
-__global__ void k_residual(float* x, const float* __restrict__ o, float rs, int64_t n)
+__global__ void k_residual(float* x, const float* o, float rs, int64_t n)
 {
     pdl_trigger();
     pdl_wait();
@@ -1285,7 +1285,7 @@ void residual(float* x, const float* o, float rs, int64_t n, cudaStream_t s)
     launched();
 }
 
-__global__ void k_vocab_gather(const float* __restrict__ src, int n, int vp, int V, float* __restrict__ dst)
+__global__ void k_vocab_gather(const float* src, int n, int vp, int V, float* dst)
 {
     pdl_trigger();
     pdl_wait();
@@ -1339,7 +1339,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float f, int v)
     return ((unsigned long long)b << 32) | (0xFFFFFFFFu - (unsigned)v);
 }
 
-__global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int V, int chunk,
+__global__ void __launch_bounds__(256) k_argmax(const float* logits, int V, int chunk,
                                                 unsigned long long* key, unsigned* count, int32_t* ids,
                                                 int32_t* next_tok, int32_t* next_pos)
 {
@@ -1403,9 +1403,9 @@ void argmax(const float* logits, int V, int n, unsigned long long* key, unsigned
 // their picks. (When the sum is NaN every probability is NaN, every comparison fails and the reference picks ids
 // 0, 1, ... in order: NaNs rank by id.) The chosen sum is added in pick order and the renormalisation divides by it
 // clamped at 6.103515625e-5, as the reference does.
-__global__ void __launch_bounds__(256) k_route(const float* __restrict__ logits, int n, int k, int renorm,
-                                               int32_t* __restrict__ sel, float* __restrict__ wts,
-                                               unsigned long long* __restrict__ count)
+__global__ void __launch_bounds__(256) k_route(const float* logits, int n, int k, int renorm,
+                                               int32_t* sel, float* wts,
+                                               unsigned long long* count)
 {
     __shared__ float p[256];
     __shared__ float red[8];
@@ -1467,7 +1467,7 @@ void route(const float* logits, int T, int n, int k, int renorm, int32_t* sel, f
     launched();
 }
 
-__global__ void k_gather_rows(float* xe, const float* __restrict__ xn, const int32_t* __restrict__ toks, int n, int E)
+__global__ void k_gather_rows(float* xe, const float* xn, const int32_t* toks, int n, int E)
 {
     pdl_trigger();
     pdl_wait();
@@ -1483,8 +1483,8 @@ void gather_rows(float* xe, const float* xn, const int32_t* toks, int n, int E, 
     launched();
 }
 
-__global__ void k_scatter_add(float* outp, const float* __restrict__ ye, const int32_t* __restrict__ toks,
-                              const float* __restrict__ w, int E)
+__global__ void k_scatter_add(float* outp, const float* ye, const int32_t* toks,
+                              const float* w, int E)
 {
     pdl_trigger();
     pdl_wait();
@@ -1502,8 +1502,8 @@ void scatter_add(float* outp, const float* ye, const int32_t* toks, const float*
     launched();
 }
 
-__global__ void k_moe_combine(const float* __restrict__ y, const int32_t* __restrict__ sel, const float* __restrict__ wts,
-                              int K, int E, float* __restrict__ out)
+__global__ void k_moe_combine(const float* y, const int32_t* sel, const float* wts,
+                              int K, int E, float* out)
 {
     pdl_trigger();
     pdl_wait();
@@ -1533,7 +1533,7 @@ void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, in
     launched();
 }
 
-__global__ void k_count_experts(const int32_t* __restrict__ sel, int n, unsigned long long* count)
+__global__ void k_count_experts(const int32_t* sel, int n, unsigned long long* count)
 {
     pdl_trigger();
     pdl_wait();
@@ -1559,7 +1559,7 @@ void count_experts(const int32_t* sel, int n, unsigned long long* count, cudaStr
     launched();
 }
 
-__global__ void k_shared_expert_add(float* outp, const float* __restrict__ sh, const float* __restrict__ gl, int E)
+__global__ void k_shared_expert_add(float* outp, const float* sh, const float* gl, int E)
 {
     pdl_trigger();
     pdl_wait();
@@ -1706,7 +1706,7 @@ __device__ void quant_q6_k(const float* x, uint8_t* out)
     }
 }
 
-__global__ void k_synth(int type, uint64_t base, int64_t nblocks, float sigma, float offset, uint8_t* __restrict__ out)
+__global__ void k_synth(int type, uint64_t base, int64_t nblocks, float sigma, float offset, uint8_t* out)
 {
     pdl_trigger();
     pdl_wait();

@@ -180,7 +180,7 @@ __device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q, bo
 // activation prep
 // ------------------------------------------------------------------------------------------------------------------
 // One CTA of 64 threads per (superblock, column); each thread owns 4 consecutive values (layout in wl_xprep.cuh).
-__global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64_t ldx, int nsb, uint8_t* __restrict__ out)
+__global__ void __launch_bounds__(64) k_xprep(const float* x, int64_t ldx, int nsb, uint8_t* out)
 {
     pdl_trigger();
     pdl_wait();
@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(64) k_xprep(const float* __restrict__ x, int64
 // rows t*K + j, weights moe.wts), added in ascending expert id one rounded multiply and add at a time from zero,
 // k_moe_combine's arithmetic, so the combine needs no launch of its own.
 template <bool RES, bool PREP, bool MOE>
-__global__ void __launch_bounds__(256) k_norm_prep(float* __restrict__ x, const float* __restrict__ o, float rs,
-                                                   int E, const float* __restrict__ w, float eps, float* __restrict__ y,
-                                                   uint8_t* __restrict__ prep, const ArIn ar, const MoeIn moe)
+__global__ void __launch_bounds__(256) k_norm_prep(float* x, const float* o, float rs,
+                                                   int E, const float* __restrict__ w, float eps, float* y,
+                                                   uint8_t* prep, const ArIn ar, const MoeIn moe)
 {
     pdl_trigger();
     __shared__ double wsum[8];
@@ -417,7 +417,7 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 template <int NC, bool TILED, bool PAIRS, int NW = 8>
 __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
-                                                    const uint8_t* __restrict__ xq, float* __restrict__ y_a,
+                                                    const uint8_t* xq, float* y_a,
                                                     int64_t ldy_a, int* err, const MvSeg seg)
 {
     using LY = Q4Layout<NC, NW>;
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(c
     const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
     int row_base = second ? seg.row_base : row_base_a;
     const int rows = second ? seg.rows : rows_a;
-    float* __restrict__ y = second ? seg.y : y_a;
+    float* y = second ? seg.y : y_a;
     const int64_t ldy = second ? seg.ldy : ldy_a;
     if (TILED && seg.sel && !PAIRS) {
         // (the single-matrix grouped form; launches use the PAIRS instantiation below, this keeps the dense
@@ -661,8 +661,8 @@ __device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int n) { return (
 
 template <int NC, int NW, int NS, bool SK>
 __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_q4k2(
-    const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb, const uint8_t* __restrict__ xq,
-    float* __restrict__ y_a, int64_t ldy_a, int P, int64_t pstride, int* err, const MvSeg2 seg)
+    const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb, const uint8_t* xq,
+    float* y_a, int64_t ldy_a, int P, int64_t pstride, int* err, const MvSeg2 seg)
 {
     using LY = Q4Layout2<NC, NW, NS>;
     constexpr bool PACK = NC <= 2;
@@ -675,7 +675,7 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_q4k2(
     const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
     const int row_base = second ? seg.row_base : row_base_a;
     const int rows = second ? seg.rows : rows_a;
-    float* __restrict__ y = second ? seg.y : y_a;
+    float* y = second ? seg.y : y_a;
     const int64_t ldy = second ? seg.ldy : ldy_a;
     const int n_rp = (rows + 31) / 32;
     const int64_t U = (int64_t)n_rp * nsb;
@@ -929,8 +929,8 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_q4k2(
 }
 
 // Repacks rows [0, rows) of a Q4_K matrix into the tile-major layout above; rows past the end are zero. One CTA per tile.
-__global__ void k_q4k_tile(const uint8_t* __restrict__ src, int rows, int nsb, int64_t row_bytes,
-                           uint8_t* __restrict__ dst)
+__global__ void k_q4k_tile(const uint8_t* src, int rows, int nsb, int64_t row_bytes,
+                           uint8_t* dst)
 {
     pdl_trigger();
     pdl_wait();
@@ -993,7 +993,7 @@ __device__ __forceinline__ uint32_t sc_pair_h2(uint32_t w, uint32_t sel, __half2
 
 template <int NC>
 __global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ wt, int rows, int nsb,
-                                                    const uint8_t* __restrict__ xq, float* __restrict__ y, int64_t ldy,
+                                                    const uint8_t* xq, float* y, int64_t ldy,
                                                     int* err)
 {
     using LY = Q6Layout<NC>;
@@ -1161,8 +1161,8 @@ __global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ 
 
 // Repacks rows [0, rows) of a Q6_K matrix (row_bytes apart, nsb superblocks each) into the tile layout above; rows past
 // the end of the last tile are zero. One CTA per tile.
-__global__ void k_q6k_tile(const uint8_t* __restrict__ src, int rows, int nsb, int64_t row_bytes,
-                           uint8_t* __restrict__ dst)
+__global__ void k_q6k_tile(const uint8_t* src, int rows, int nsb, int64_t row_bytes,
+                           uint8_t* dst)
 {
     pdl_trigger();
     pdl_wait();
@@ -1451,13 +1451,17 @@ static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb,
 // small kernel, and CTAs this size start under programmatic dependent launch while that kernel still runs (four fit
 // beside it on an SM) and stream their first stages meanwhile; the 32-row form above, faster back to back, lost 6 %
 // of the 70B step for that reason. Eight warps per CTA for up to 8 x SMs row tiles at one or two columns; four warps
-// (twice the superblocks per warp, twice the CTAs per SM) for taller matrices and from three columns on, where a
-// CTA's stages grow with the columns (measured in the 70B step on B200: 0.8 % at b1, 8 % at b8).
+// (twice the superblocks per warp, twice the CTAs per SM) for taller matrices. The warp count fixes how a row's
+// superblocks are grouped and added, so it depends on the matrix alone, never on the column count: a decode step's
+// rows then equal single-sequence steps bit for bit. (An earlier version took four warps for every matrix from three
+// columns on, 8 % faster at 8 columns, but its 8192-row matrices then grouped a row's superblocks by four where a
+// single-sequence step groups them by eight.)
 static void dispatch_q4k16(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                            float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
 {
     const int tiles_n = (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
-    if (p.nc >= 3 || tiles_n >= 8 * sm_count())
+    const int nw = tiles_n >= 8 * sm_count() ? 4 : 8;
+    if (nw == 4)
         dispatch_q4k<true, 4>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
     else
         dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);

@@ -28,9 +28,9 @@ namespace {
 // p[i] = exp((x[i] - x[best]) / temperature) (float difference, as the reference's float arithmetic gives it, then
 // the double division and exponential); ids[i] = i. The first thread also resets the nucleus to every id (V - 1, the
 // reference's k = n when no prefix reaches the limit) and the crossing position to "none".
-__global__ void k_samp_prob(const float* __restrict__ x, int V, const int32_t* __restrict__ best, double temperature,
-                            double* __restrict__ p, int32_t* __restrict__ ids, int32_t* __restrict__ nucleus,
-                            int32_t* __restrict__ pos)
+__global__ void k_samp_prob(const float* x, int V, const int32_t* best, double temperature,
+                            double* p, int32_t* ids, int32_t* nucleus,
+                            int32_t* pos)
 {
     pdl_trigger();
     pdl_wait();
@@ -50,8 +50,8 @@ __global__ void k_samp_prob(const float* __restrict__ x, int V, const int32_t* _
 // position]. The minimum (an atomic one over the positions where the running sum crosses the target) keeps the
 // answer the first crossing even where a tree-ordered prefix sum steps down by a unit in the last place over a zero
 // term.
-__global__ void k_samp_cross(const double* __restrict__ pre, int n, const int32_t* __restrict__ nucleus,
-                             const double* __restrict__ total, double scale, int32_t* __restrict__ out)
+__global__ void k_samp_cross(const double* pre, int n, const int32_t* nucleus,
+                             const double* total, double scale, int32_t* out)
 {
     pdl_trigger();
     pdl_wait();
@@ -64,8 +64,8 @@ __global__ void k_samp_cross(const double* __restrict__ pre, int n, const int32_
 
 // The chosen id: ids[*pos] (or *pos itself in index order), and where no position crossed, the reference's fallback:
 // the first id of the nucleus (ids[0]) or, in index order, the greedy id.
-__global__ void k_samp_final(const int32_t* __restrict__ pos, const int32_t* __restrict__ ids,
-                             const int32_t* __restrict__ best, int32_t* __restrict__ out)
+__global__ void k_samp_final(const int32_t* pos, const int32_t* ids,
+                             const int32_t* best, int32_t* out)
 {
     pdl_trigger();
     pdl_wait();
