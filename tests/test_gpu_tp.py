@@ -5,7 +5,8 @@
 - every rank returns the same logits (the all-reduce and the head's all-gather leave no rank behind);
 - ForwardBatch rows equal single runs (bit-identical at 2 ranks, where each all-reduced value is one sum of two);
 - the decode-step all-reduces fused into the matvec and the norm over peer memory give what NCCL's give (bit for bit
-  at 2 ranks), and are the ones in use.
+  at 2 ranks), and are the ones in use;
+- a Qwen3-MoE-shaped model with whole experts placed on each GPU (the "moe" case) meets all of the above.
 
 Needs at least 2 GPUs; WL_TP_TEST_GPUS picks how many ranks (default 2).
 """
@@ -57,7 +58,7 @@ def run_ranks(n, spec, out, steps=16, graphs=1, nccl_only=0, timeout=300):
     return [dict(np.load(os.path.join(out, f"rank{r}.npz"))) for r in range(n)]
 
 
-@pytest.mark.parametrize("spec", ["config0", "gqa"])
+@pytest.mark.parametrize("spec", ["config0", "gqa", "moe"])
 def test_tensor_parallel_matches_oracle(wl, oracle, tmp_path, spec):
     n = int(os.environ.get("WL_TP_TEST_GPUS", "2"))
     if _gpus() < n:

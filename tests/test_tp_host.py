@@ -32,16 +32,17 @@ def test_unique_id_is_fresh(wl):
 
 @pytest.mark.parametrize("case", ["rank", "heads", "moe", "vocab"])
 def test_split_checks_fail_before_any_device_work(wl, case):
-    from windlass_b200.transformer import config0_spec, qwen3moe_spec, synth_spec
+    from windlass_b200.transformer import config0_spec, synth_spec
     if case == "rank":        # rank outside 0..tp_size-1
         st, msg = _open_synth(wl, config0_spec(), tp_size=2, tp_rank=2)
         assert st == wl.WL_EINVAL and "tp_rank" in msg
     elif case == "heads":     # 8 heads do not split over 3 GPUs
         st, msg = _open_synth(wl, config0_spec(), tp_size=3, tp_rank=0)
         assert st == wl.WL_EUNSUPPORTED and "divisible by 3" in msg
-    elif case == "moe":       # expert layers are not split
-        st, msg = _open_synth(wl, qwen3moe_spec(layers=1), tp_size=2, tp_rank=1)
-        assert st == wl.WL_EUNSUPPORTED and "mixture-of-experts" in msg
+    elif case == "moe":       # whole experts per GPU: 6 experts do not split over 4 GPUs
+        st, msg = _open_synth(wl, synth_spec("qwen3moe", 1, 1024, 16, 8, 128, 0, 8192, experts=6, experts_used=2,
+                                             expert_ff=512), tp_size=4, tp_rank=1)
+        assert st == wl.WL_EUNSUPPORTED and "6 experts" in msg
     else:                     # a vocabulary too small for the ranks
         st, msg = _open_synth(wl, synth_spec("llama", 1, 2048, 32, 8, 64, 2048, 5), tp_size=8, tp_rank=0)
         assert st == wl.WL_EUNSUPPORTED and "vocabulary" in msg

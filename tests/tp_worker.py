@@ -19,6 +19,10 @@ def spec_of(name):
     from windlass_b200.transformer import config0_spec, synth_spec
     if name == "config0":
         return config0_spec()
+    if name == "moe":
+        # Qwen3-MoE layers at small size: 16 experts top-4 (whole experts per GPU), QK-norm, head_dim 128
+        return synth_spec("qwen3moe", 2, 1024, 16, 8, 128, 0, 8192, experts=16, experts_used=4, expert_ff=512,
+                          rope_base=1000000.0, rms_eps=1e-6, type_attn_v=14, type_embd=12, seed=5)
     # GQA with Q6_K attn_v and head, the Q4_K_M mix of the 8B/70B shapes at small size
     return synth_spec("llama", 2, 2048, 32, 8, 64, 4096, 8192, rope_base=500000.0, type_attn_v=14, type_embd=12,
                       seed=7)

@@ -1503,7 +1503,7 @@ void scatter_add(float* outp, const float* ye, const int32_t* toks, const float*
 }
 
 __global__ void k_moe_combine(const float* y, const int32_t* sel, const float* wts,
-                              int K, int E, float* out)
+                              int K, int E, float* out, int e_lo, int e_n)
 {
     pdl_trigger();
     pdl_wait();
@@ -1519,17 +1519,20 @@ __global__ void k_moe_combine(const float* y, const int32_t* sel, const float* w
         float o = 0.0f;
         for (int j = 0; j < K; ++j) {
             const int i = t * K + order[j];
+            const int ex = sel[i] - e_lo;
+            if (ex < 0 || ex >= e_n) continue;          // another GPU's expert
             o = __fadd_rn(o, __fmul_rn(wts[i], y[(int64_t)i * E + d]));
         }
         out[(int64_t)t * E + d] = o;
     }
 }
 
-void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s)
+void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s,
+                 int e_lo, int e_n)
 {
     if (T <= 0) return;
     if (K < 1 || K > 16) WL_THROW(WL_EINVAL, "moe_combine: 1..16 experts per token");
-    launch(k_moe_combine, dim3(grid_for(E, 256), T), dim3(256), 0, s, y, sel, wts, K, E, out);
+    launch(k_moe_combine, dim3(grid_for(E, 256), T), dim3(256), 0, s, y, sel, wts, K, E, out, e_lo, e_n);
     launched();
 }
 

@@ -1,6 +1,7 @@
 // Launch wrappers of the device kernels (all defined in wl_kernels.cu). Every wrapper enqueues on `stream` and
 // returns without synchronising; shapes are checked by the callers (wl_model.cpp, wl_api.cpp).
 #pragma once
+#include <climits>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -136,16 +137,23 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
 // The mixture-of-experts grouped matvec (Q4_K experts, one activation column per pair): for every pair i < npairs
 // (token i / K and its expert sel[i], read on the device), y[i*ldy + r] = E_sel[i][r] . x[col] for the expert's
 // expert_rows rows (expert e's rows start at row_base + e * expert_rows of the tiles), col = i / K when x_per_token
-// else i. Each pair's result is the one a matvec of that expert alone gives.
+// else i. Each pair's result is the one a matvec of that expert alone gives. Under tensor parallelism the tiles hold
+// experts e_lo .. e_lo + e_n - 1 only (local expert e - e_lo at row_base + (e - e_lo) * expert_rows), and the pairs of
+// other experts are skipped: their outputs are not written.
 void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
-                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s);
+                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s, int e_lo = 0,
+                  int e_n = INT_MAX);
 // Gate and up of every pair in one launch: matvec_pairs of A into ya and of B (same shape, stacked the same way) into
 // yb, activations per token (x_per_token), each CTA's result what matvec_pairs gives.
 void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_rows, int cols, const int32_t* sel,
-                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s);
+                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s,
+                   int e_lo = 0, int e_n = INT_MAX);
 // MoeFfn's weighted sum (src/Transformer.cs:289-293) from the pairs' outputs: out[t] = sum over token t's K experts in
 // ascending expert order of wts[t*K+j] * y[(t*K+j)*E ...], each step a separately rounded multiply and add from 0.
-void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s);
+// Under tensor parallelism only the experts e_lo .. e_lo + e_n - 1 this GPU holds are added (the ranks' sums are
+// then all-reduced).
+void moe_combine(const float* y, const int32_t* sel, const float* wts, int T, int K, int E, float* out, cudaStream_t s,
+                 int e_lo = 0, int e_n = INT_MAX);
 // Adds to *count the number of distinct experts among sel[0 .. n) (Transformer.ExpertRuns, src/Transformer.cs:287).
 void count_experts(const int32_t* sel, int n, unsigned long long* count, cudaStream_t s);
 

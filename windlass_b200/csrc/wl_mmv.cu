@@ -393,6 +393,9 @@ struct MvSeg {
     // pair / K (x_per_token) or column pair of the prepared input, and the output row is y + pair * ldy.
     const int32_t* sel;
     int K, tiles_per_pair, x_per_token;
+    // under tensor parallelism a GPU holds experts e_lo .. e_lo + e_n - 1 only (stacked from row_base): a pair whose
+    // expert lives on another GPU is skipped (its CTAs return at once)
+    int e_lo = 0, e_n = INT_MAX;
 };
 
 __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -456,7 +459,9 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(c
         const int pair = b / seg.tiles_per_pair;
         bx = b % seg.tiles_per_pair;
         if (up) wt = seg.wt;
-        row_base = row_base_a + seg.sel[pair] * rows_a;
+        const int ex = seg.sel[pair] - seg.e_lo;
+        if (ex < 0 || ex >= seg.e_n) return;        // an expert of another GPU
+        row_base = row_base_a + ex * rows_a;
         xq += (int64_t)(seg.x_per_token ? pair / seg.K : pair) * nsb * XP_COL;
         y = (up ? seg.y : y_a) + (int64_t)pair * (up ? seg.ldy : ldy_a);
     }
@@ -1546,7 +1551,7 @@ void matvec_tiles2(const uint8_t* tiles_a, int row_base_a, int rows_a, float* y_
 }
 
 void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols, const int32_t* sel, int npairs, int K,
-                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s)
+                  bool x_per_token, const XPrep& p, float* y, int64_t ldy, int* err, cudaStream_t s, int e_lo, int e_n)
 {
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0 || expert_rows % 16 != 0)
         WL_THROW(WL_EINVAL, "matvec_pairs: experts must start on 16-row tiles");
@@ -1557,12 +1562,13 @@ void matvec_pairs(const uint8_t* tiles, int row_base, int expert_rows, int cols,
     memset(&none, 0, sizeof none);
     const int tiles_per_pair = expert_rows / Q4_ROWS;
     // first_ctas carries the pair count (the CTA count is pairs x tiles per pair)
-    const MvSeg seg{nullptr, 0, 0, npairs, nullptr, 0, sel, K, tiles_per_pair, x_per_token ? 1 : 0};
+    const MvSeg seg{nullptr, 0, 0, npairs, nullptr, 0, sel, K, tiles_per_pair, x_per_token ? 1 : 0, e_lo, e_n};
     launch_q4k<1, true, true>(none, tiles, row_base, expert_rows, cols / 256, p, y, ldy, err, s, seg);
 }
 
 void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_rows, int cols, const int32_t* sel,
-                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s)
+                   int npairs, int K, const XPrep& p, float* ya, float* yb, int64_t ldy, int* err, cudaStream_t s,
+                   int e_lo, int e_n)
 {
     if ((uintptr_t)tiles_a % 16 != 0 || (uintptr_t)tiles_b % 16 != 0 || expert_rows % 16 != 0)
         WL_THROW(WL_EINVAL, "matvec_pairs2: experts must start on 16-row tiles");
@@ -1572,7 +1578,7 @@ void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_ro
     CUtensorMap none;
     memset(&none, 0, sizeof none);
     const int tiles_per_pair = expert_rows / Q4_ROWS;
-    const MvSeg seg{tiles_b, 0, expert_rows, npairs, yb, ldy, sel, K, tiles_per_pair, 1};
+    const MvSeg seg{tiles_b, 0, expert_rows, npairs, yb, ldy, sel, K, tiles_per_pair, 1, e_lo, e_n};
     launch_q4k<1, true, true>(none, tiles_a, 0, expert_rows, cols / 256, p, ya, ldy, err, s, seg);
 }
 

@@ -75,8 +75,9 @@ static void check_tp(const Config& c, const wl_options& opt)
     if (G == 1) return;
     const std::string g = std::to_string(G);
     if (opt.tp_rank < 0 || opt.tp_rank >= G) WL_THROW(WL_EINVAL, "tp_rank must be 0.." + std::to_string(G - 1) + ".");
-    if (c.expert_count > 0)
-        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism is built for dense models; this one has mixture-of-experts layers.");
+    if (c.expert_count % G)
+        WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism over " + g + " GPUs places whole experts on each GPU and needs an "
+                                  "expert count divisible by " + g + " (" + std::to_string(c.expert_count) + " experts).");
     if (c.qk_norm_full || c.post_norms)
         WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism does not split " + c.arch + " (its QK-norm spans every head).");
     if (c.heads % G || c.kv_heads % G)
@@ -99,6 +100,10 @@ void Model::init_tp(const wl_options& opt)
     if (tp_size_ == 1) return;
     c_.heads /= tp_size_;
     c_.kv_heads /= tp_size_;
+    if (c_.expert_count > 0) {
+        e_n_ = c_.expert_count / tp_size_;
+        e_lo_ = tp_rank_ * e_n_;
+    }
     vocab_part_ = (c_.vocab + tp_size_ - 1) / tp_size_;
     flag_d_ = dalloc<int32_t>(1);
     flag_h_ = halloc<int32_t>(1);
@@ -428,8 +433,9 @@ void Model::load_from_gguf(const Gguf& g)
     if (streamed_) plan_streaming(raw_upper, slot_upper);
 
     // split: WHOLE on every rank; ROWS this rank's 1/G of the rows; COLS its 1/G of every row's blocks; HEAD rows
-    // rank*vocab_part_ .. +vocab_part_ (the last rank's may be fewer).
-    enum Split { WHOLE, ROWS, COLS, HEAD };
+    // rank*vocab_part_ .. +vocab_part_ (the last rank's may be fewer); EXPERTS a stacked tensor's experts
+    // e_lo_ .. e_lo_ + e_n_ - 1, whole.
+    enum Split { WHOLE, ROWS, COLS, HEAD, EXPERTS };
     auto upload = [&](const GgufTensor* t, Split sp) -> Weight {
         if (!t) return Weight{};
         Weight w = weight_of(*t);
@@ -437,6 +443,14 @@ void Model::load_from_gguf(const Gguf& g)
         if (G == 1 || sp == WHOLE) {
             w.d = weight_alloc(w.bytes);
             WL_CUDA(cudaMemcpy(w.d, src, (size_t)w.bytes, cudaMemcpyHostToDevice));
+        } else if (sp == EXPERTS) {
+            if (w.experts != c_.expert_count || w.experts % G)
+                WL_THROW(WL_EUNSUPPORTED, t->name + ": its experts do not split over " + std::to_string(G) + " GPUs.");
+            const int64_t per = (int64_t)w.rows * w.row_bytes;
+            w.experts = e_n_;
+            w.bytes = per * e_n_;
+            w.d = weight_alloc(w.bytes);
+            WL_CUDA(cudaMemcpy(w.d, src + (int64_t)e_lo_ * per, (size_t)w.bytes, cudaMemcpyHostToDevice));
         } else if (sp == ROWS || sp == HEAD) {
             if (w.experts != 1) WL_THROW(WL_EUNSUPPORTED, "Tensor parallelism does not split stacked tensors.");
             int r0, n;
@@ -509,8 +523,8 @@ void Model::load_from_gguf(const Gguf& g)
         L.moe = c_.expert_count > 0 && T("ffn_gate_inp.weight");
         if (L.moe) {
             L.router = upload(T("ffn_gate_inp.weight"), WHOLE);
-            L.gate_exps = upload(T("ffn_gate_exps.weight"), WHOLE); L.up_exps = upload(T("ffn_up_exps.weight"), WHOLE);
-            L.down_exps = upload(T("ffn_down_exps.weight"), WHOLE);
+            L.gate_exps = upload(T("ffn_gate_exps.weight"), EXPERTS); L.up_exps = upload(T("ffn_up_exps.weight"), EXPERTS);
+            L.down_exps = upload(T("ffn_down_exps.weight"), EXPERTS);
             L.sh_gate = upload(T("ffn_gate_shexp.weight"), WHOLE); L.sh_up = upload(T("ffn_up_shexp.weight"), WHOLE);
             L.sh_down = upload(T("ffn_down_shexp.weight"), WHOLE);
             L.sh_gate_inp = upload(T("ffn_gate_inp_shexp.weight"), WHOLE);
@@ -630,9 +644,10 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
         if (NE > 0) {
             L.moe = true;
             plan.push_back({&L.router, nullptr, b | S_ROUTER, 0, NE, E, 1});
-            plan.push_back({&L.gate_exps, nullptr, b | S_GATE_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE});
-            plan.push_back({&L.up_exps, nullptr, b | S_UP_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE});
-            plan.push_back({&L.down_exps, nullptr, b | S_DOWN_EXPS, sp.type_ffn_down, (int64_t)NE * E, X, NE});
+            // under tensor parallelism rank r keeps experts r*NE/G .., which are contiguous rows of the stack
+            plan.push_back({&L.gate_exps, nullptr, b | S_GATE_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE, 1});
+            plan.push_back({&L.up_exps, nullptr, b | S_UP_EXPS, sp.type_ffn, (int64_t)NE * X, E, NE, 1});
+            plan.push_back({&L.down_exps, nullptr, b | S_DOWN_EXPS, sp.type_ffn_down, (int64_t)NE * E, X, NE, 1});
         } else {
             plan.push_back({&L.gate, nullptr, b | S_GATE, sp.type_ffn, F, E, 1, 1});
             plan.push_back({&L.up, nullptr, b | S_UP, sp.type_ffn, F, E, 1, 1});
@@ -703,7 +718,9 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
             }
             const int64_t full_rb = row_bytes_of(p.type, p.cols);
             Weight w;
-            w.type = p.type; w.cols = (int)nc; w.experts = p.experts; w.rows = (int)(nr / p.experts);
+            w.type = p.type; w.cols = (int)nc;
+            w.experts = G > 1 && p.split == 1 && p.experts > 1 ? p.experts / G : p.experts;
+            w.rows = (int)(nr / w.experts);
             w.row_bytes = row_bytes_of(p.type, nc); w.bytes = w.row_bytes * nr;
             w.d = is_vec ? m->arena_alloc(w.bytes) : m->weight_alloc(w.bytes);
             if (G == 1 || p.split == 0) {
@@ -1114,12 +1131,27 @@ void Model::ffn_moe_device(const LayerW& L, int T)
              T == 1 ? expert_count_d_ : nullptr);
     if (T > 1) k::count_experts(sel_, NP, expert_count_d_, stream_);
     const int mark = profile_begin();
-    k::matvec_pairs2(L.gate_exps.tiles, L.up_exps.tiles, X, E, sel_, NP, K, px, pg_, pu_, X, err_d_, stream_);
+    // under tensor parallelism the pairs of experts held by other GPUs are skipped here (their rows of pg_, pu_ and
+    // py_ are left as they are and never read)
+    k::matvec_pairs2(L.gate_exps.tiles, L.up_exps.tiles, X, E, sel_, NP, K, px, pg_, pu_, X, err_d_, stream_, e_lo_,
+                     e_n_);
     const k::XPrep pp = k::xprep_view(pprep_, X, NP);
     k::swiglu_prep(pg_, pu_, NP, X, pp, stream_);
-    k::matvec_pairs(L.down_exps.tiles, 0, E, X, sel_, NP, K, false, pp, py_, E, err_d_, stream_);
+    k::matvec_pairs(L.down_exps.tiles, 0, E, X, sel_, NP, K, false, pp, py_, E, err_d_, stream_, e_lo_, e_n_);
     profile_end(mark, 12, (double)NP * ((double)L.gate_exps.row_bytes * X * 2 + (double)L.down_exps.row_bytes * E));
-    if (k::norm_prep_supported(E) && !c_.post_norms && K <= 16) {
+    if (tp_size_ > 1) {
+        // this GPU's experts' weighted sum, then the sum over the GPUs: fused into the next norm through this rank's
+        // all-reduce slot (decode steps), else NCCL
+        if (ar_on_ && T <= k::AR_COLS && ar_idx_ < k::AR_STEP) {
+            const int idx = ar_idx_++;
+            k::moe_combine(py_, sel_, wts_, T, K, E, reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E)),
+                           stream_, e_lo_, e_n_);
+            pending_ar_ = idx;
+        } else {
+            k::moe_combine(py_, sel_, wts_, T, K, E, o_, stream_, e_lo_, e_n_);
+            all_reduce(o_, (int64_t)T * E);
+        }
+    } else if (k::norm_prep_supported(E) && !c_.post_norms && K <= 16) {
         // the next norm (the next layer's or the head's) combines the experts' outputs as it adds the residual
         pending_moe_ = true;
         moe_in_ = k::MoeIn{py_, sel_, wts_, K};
@@ -1158,15 +1190,16 @@ void Model::ffn_moe(const LayerW& L, int T)
         const int n = count[e];
         if (n == 0) continue;
         stats_.expert_runs++;
+        if (e - e_lo_ < 0 || e - e_lo_ >= e_n_) continue;     // another GPU's expert (tensor parallelism)
         const int32_t* toks = etok_d_ + start[e];
         k::gather_rows(xe_, xn_, toks, n, E, stream_);
-        matmul(slice(L.gate_exps, e), xe_, n, ge_);
-        matmul(slice(L.up_exps, e), xe_, n, ue_, 0, true);
+        matmul(slice(L.gate_exps, e - e_lo_), xe_, n, ge_);
+        matmul(slice(L.up_exps, e - e_lo_), xe_, n, ue_, 0, true);
         k::swiglu(ge_, ue_, (int64_t)n * X, stream_);
-        matmul(slice(L.down_exps, e), ge_, n, ye_);
+        matmul(slice(L.down_exps, e - e_lo_), ge_, n, ye_);
         k::scatter_add(moe_out_, ye_, toks, ew_d_ + start[e], n, E, stream_);
     }
-    if (L.sh_gate.present()) {
+    if (L.sh_gate.present() && tp_rank_ == 0) {     // the shared expert once (on the first GPU under TP)
         const int SF = L.sh_gate.rows;
         matmul(L.sh_gate, xn_, T, g_);
         matmul(L.sh_up, xn_, T, u_, 0, true);
@@ -1176,6 +1209,7 @@ void Model::ffn_moe(const LayerW& L, int T)
         k::shared_expert_add(moe_out_, o_, L.sh_gate_inp.present() ? sh_gl_ : nullptr, T, E, stream_);
     }
     WL_CUDA(cudaMemcpyAsync(o_, moe_out_, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToDevice, stream_));
+    all_reduce(o_, (int64_t)T * E);         // the sum over the GPUs' experts (no-op on one GPU)
 }
 
 // Layer (src/Transformer.cs:177-232).

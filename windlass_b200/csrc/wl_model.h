@@ -214,6 +214,8 @@ private:
     int device_ = 0;
     // tensor parallelism: this rank's share of rows (q/k/v, gate/up, the head) and columns (o, down)
     int tp_size_ = 1, tp_rank_ = 0;
+    // the routed experts this GPU holds: e_lo_ .. e_lo_ + e_n_ - 1 (all of them on one GPU)
+    int e_lo_ = 0, e_n_ = 1 << 30;
     std::unique_ptr<Comm> comm_;
     int vocab_part_ = 0;                  // output-head rows per rank (the last rank's may hold fewer real rows)
     float* logits_part_ = nullptr;        // [rows][vocab_part_] this rank's head rows
