@@ -18,33 +18,50 @@ struct RowKV {
 namespace k {
 
 // ---- the tensor-parallel all-reduce fused into the matvec that produces it and the norm that consumes it ----
-// Every rank holds one buffer (mapped into every peer's process): per slot and source rank a flag, then per slot and
-// column its own partial output rows. The producing matvec writes its rows into its own slot like any output. The
-// consuming norm announces on every peer that this rank's partial for sequence number q is in place (a release
-// store into the peer's flag), waits (bounded) until every peer has announced q, then reads the peers' partials
-// over NVLink and sums all of them in rank order, so every rank gets bit-identical sums. Sequence numbers are
-// epoch * AR_STEP + index within the step; the epoch is a device counter the step's embedding kernel advances, so
-// graph replays need no host input, and the slot (the index mod AR_SLOTS) is known when the step is enqueued.
+// Every rank holds one buffer, mapped into every peer's process. The producer of a partial pushes each of its output
+// values into every rank's buffer (its own included) as an 8-byte element {value bits, flag}, the flag derived from
+// the all-reduce's sequence number q; an element is written by one 8-byte store, so a reader that sees the flag also
+// sees the value, and neither side needs a fence, a separate announcement or a read over NVLink. The consuming norm
+// polls its own buffer (bounded in time) until every rank's elements of its rows carry q's flag, then sums the ranks'
+// values in rank order, so every rank gets bit-identical sums. The Q4_K decode matvec stores the elements from its
+// epilogue (ArOut); any other producer writes its partial into this rank's staging slot and ar_push sends it.
+// Sequence numbers are epoch * AR_STEP + index within the step; the epoch is a device counter the step's embedding
+// kernel advances, so graph replays need no host input, and the slot (the index mod AR_SLOTS) is known when the step
+// is enqueued. A rank writes slot q % AR_SLOTS of a peer only after its own all-reduce q - 1 has received the peer's
+// q - 1 values, which the peer produced after its consumer of q - 2 had finished: two slots would do, four are kept.
+// Layout: header (the epoch u64 at AR_EPOCH), staging [AR_SLOTS][AR_COLS][E] f32, then the pushed elements
+// [AR_SLOTS][AR_MAX_RANKS source][AR_COLS][E] u64. The buffer starts zeroed: flags always have the top bit set.
 constexpr int AR_SLOTS = 4;
 constexpr int AR_MAX_RANKS = 8;
 constexpr int AR_STEP = 1024;                   // most fused all-reduces in one step (a multiple of AR_SLOTS)
 constexpr int AR_COLS = 8;                      // columns (decode rows) one slot holds
-constexpr size_t AR_HEADER = 1024;              // flags [AR_SLOTS][AR_MAX_RANKS] u64 at 0, the epoch u64 at AR_EPOCH
+constexpr size_t AR_HEADER = 1024;              // the epoch u64 at AR_EPOCH
 constexpr size_t AR_EPOCH = 512;
 static_assert(AR_STEP % AR_SLOTS == 0, "the slot of an all-reduce must not depend on the epoch");
-inline size_t ar_buffer_bytes(int E) { return AR_HEADER + (size_t)AR_SLOTS * AR_COLS * E * sizeof(float); }
 inline size_t ar_slot_offset(int idx, int E) { return AR_HEADER + (size_t)(idx % AR_SLOTS) * AR_COLS * E * sizeof(float); }
+inline size_t ar_ll_offset(int E) { return AR_HEADER + (size_t)AR_SLOTS * AR_COLS * E * sizeof(float); }
+inline size_t ar_buffer_bytes(int E)
+{
+    return ar_ll_offset(E) + (size_t)AR_SLOTS * AR_MAX_RANKS * AR_COLS * E * sizeof(unsigned long long);
+}
+// The producer's side: every rank's pushed-element region (peers' mapped into this process) and this rank's epoch.
+struct ArOut {
+    unsigned long long* ll[AR_MAX_RANKS];
+    const unsigned long long* epoch;
+    int idx, G, rank, E;
+};
+// The consumer's side: this rank's pushed-element region.
 struct ArIn {
-    const float* data[AR_MAX_RANKS];            // every rank's partials region (peers' mapped into this process)
-    unsigned long long* peer_flags[AR_MAX_RANKS];   // every rank's flags (this rank announces into them)
-    const unsigned long long* flags;            // this rank's flags (the peers announce into them)
+    const unsigned long long* ll;
     const unsigned long long* epoch;            // this rank's step counter
     int* err;                                   // set to 2 when a wait gives up
     int idx, G, rank, E, row0;                  // row0: first partial row the consumer's row 0 reads
     long long wait_ns;                          // how long a wait for a peer may last before it gives up
 };
 constexpr long long AR_WAIT_NS = 10000000000LL; // 10 s: far beyond any skew between ranks that are running
-// Runs the fused all-reduce's consumer on this GPU against a peer that never announces (a flag nothing sets), with
+// Pushes T rows of E floats (src, row-major) into every rank's elements of all-reduce ao.idx, source ao.rank.
+void ar_push(const float* src, int T, const ArOut& ao, cudaStream_t s);
+// Runs the fused all-reduce's consumer on this GPU against a peer that never pushes (elements nothing writes), with
 // its wait limited to wait_ns: returns the error code the kernel recorded (2 when the wait gave up, as it must).
 int selftest_ar_wait(long long wait_ns);
 
@@ -125,8 +142,9 @@ int64_t tile_bytes(int type, int rows, int cols);
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
 // P > 1 (Q4_K only, P <= cols / 256) splits the superblocks into P equal contiguous ranges and writes P partial
 // outputs, partial i at y + i * pstride; their sum in order 0..P-1 is the product.
+// With ao (Q4_K, P = 1 only) the outputs are not written to y but pushed as all-reduce ao.idx's elements.
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, int P = 1, int64_t pstride = 0);
+                  int64_t ldy, int* err, cudaStream_t s, int P = 1, int64_t pstride = 0, const ArOut* ao = nullptr);
 
 // Two Q4_K matrices with the same columns and activations (q and k, gate and up) in one tensor-core matvec launch:
 // y_a[t*ldy_a + r] = A[row_base_a + r] . x[t], y_b likewise; each row's result is the one matvec_tiles gives.

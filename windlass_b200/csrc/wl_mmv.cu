@@ -25,84 +25,12 @@
 #include "wl_kernels.h"
 #include "wl_launch.cuh"
 #include "wl_xprep.cuh"
+#include "wl_mma.cuh"
 
 namespace wl {
 namespace k {
 
 namespace {
-
-__device__ __forceinline__ float h2f_(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1)
-{
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};\n"
-                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
-{
-    uint32_t ok;
-    // the suspend-time hint (ns) lets the warp sleep until the phase completes instead of spinning
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u) : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ unsigned long long globaltimer_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Waits for the phase with the given parity for up to MBAR_WAIT_NS of %globaltimer time, then records the failure in
-// *err and returns false. The limit is on time, not on polls (a poll may return well before its sleep hint), so only a
-// copy that never lands gives up, never a slow one.
-constexpr unsigned long long MBAR_WAIT_NS = 2000000000ull;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code)
-{
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity))
-        if (globaltimer_ns() - t0 > MBAR_WAIT_NS) {
-            atomicExch(err, code);
-            return false;
-        }
-    return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
-{
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-                 ::"r"(smem_u32(dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-
-__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // Fixed-order block sum: lanes by xor butterfly, then the warps in index order.
 __device__ __forceinline__ double block_sum_d(double v, double* scratch)
@@ -132,46 +60,67 @@ __device__ __forceinline__ double ld_cluster_f64(const double* p, uint32_t rank)
 }
 
 // ---- fused tensor-parallel all-reduce (layout and protocol in wl_kernels.h) ----
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p)
-{
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v)
-{
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 __device__ __forceinline__ unsigned long long ar_seq(const unsigned long long* epoch, int idx)
 {
     return *epoch * (unsigned long long)AR_STEP + (unsigned long long)idx;
 }
 
-// The consumer's side of the fused all-reduce, run by every thread of every CTA of the consuming kernel after its
-// grid-dependency wait (so this rank's producing matvec has completed): one CTA announces sequence number q on every
-// peer (this rank's partial sits in its own slot), lane g of its first warp storing to peer g, so that the G - 1
-// system-scope releases go out as one warp instruction rather than one after another (each waits for the stores
-// before it to reach their peer); then threads 0..G-1 wait for each peer's announcement of q or later. A wait gives up after ar.wait_ns of %globaltimer time (the host sets AR_WAIT_NS, 10 s), records code 2 in
-// *err and returns (the sums are then garbage and the host reports WL_ETIMEDOUT), so a rank that never arrives cannot
-// hang the GPU.
-__device__ __forceinline__ void ar_sync(const ArIn& ar, unsigned long long q, bool announcer)
+// The flag of sequence number q's elements: its low 31 bits with the top bit set, so a zeroed buffer matches no flag
+// (a slot is rewritten every AR_SLOTS all-reduces, far within the 2^31 period).
+__device__ __forceinline__ uint32_t ar_flag(unsigned long long q) { return (uint32_t)(q & 0x7FFFFFFFull) | 0x80000000u; }
+
+__device__ __forceinline__ size_t ar_elem(unsigned long long q, int src, int col, int E)
 {
-    const int slot = (int)(q % AR_SLOTS);
-    if (announcer && threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank)
-        st_release_sys(ar.peer_flags[threadIdx.x] + slot * AR_MAX_RANKS + ar.rank, q);
-    if (threadIdx.x < (unsigned)ar.G && threadIdx.x != (unsigned)ar.rank) {
-        const unsigned long long* f = ar.flags + slot * AR_MAX_RANKS + threadIdx.x;
-        const unsigned long long t0 = globaltimer_ns();
-        for (uint32_t n = 0; ld_acquire_sys(f) < q; ++n) {
-            if (n >= 64) {
-                if ((long long)(globaltimer_ns() - t0) > ar.wait_ns) { atomicExch(ar.err, 2); break; }
-                __nanosleep(256);
-            }
+    return (((size_t)(q % AR_SLOTS) * AR_MAX_RANKS + src) * AR_COLS + col) * (size_t)E;
+}
+
+// One element {value, flag}: a single 8-byte store, so value and flag arrive together.
+__device__ __forceinline__ void st_elem(unsigned long long* p, float v, uint32_t flag)
+{
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(flag) : "memory");
+}
+// Two elements in one 16-byte store.
+__device__ __forceinline__ void st_elem2(unsigned long long* p, float v0, float v1, uint32_t flag)
+{
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(v0)), "r"(flag),
+                 "r"(__float_as_uint(v1)), "r"(flag) : "memory");
+}
+// Two elements (x, z the values, y, w the flags); each 8-byte half is read whole.
+__device__ __forceinline__ uint4 ld_elem2(const unsigned long long* p)
+{
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p) : "memory");
+    return v;
+}
+
+// Element (col, row) of this rank's partial of all-reduce ao.idx, pushed into every rank's buffer. Out of line: the
+// Q4_K matvec that calls it from its epilogue then keeps the main loop's register allocation.
+__device__ __noinline__ void ar_push_elem(const ArOut& ao, int col, int row, float v)
+{
+    const unsigned long long q = ar_seq(ao.epoch, ao.idx);
+    const uint32_t fl = ar_flag(q);
+    const size_t off = ar_elem(q, ao.rank, col, ao.E) + row;
+#pragma unroll
+    for (int g = 0; g < AR_MAX_RANKS; ++g)
+        if (g < ao.G) st_elem(ao.ll[g] + off, v, fl);
+}
+
+// Polls two elements until both carry `flag`, for up to ar.wait_ns of %globaltimer time; then records code 2 in *err
+// and returns what it read (the sums are then garbage and the host reports WL_ETIMEDOUT), so a rank that never pushes
+// cannot hang the GPU. Once any wait of this rank has given up, later waits return at once.
+__device__ __noinline__ uint4 ar_wait_elem2(const unsigned long long* p, uint32_t flag, const ArIn ar)
+{
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t n = 0;; ++n) {
+        const uint4 v = ld_elem2(p);
+        if (v.y == flag && v.w == flag) return v;
+        if (n >= 32) {
+            if (*(volatile int*)ar.err != 0) return v;
+            if ((long long)(globaltimer_ns() - t0) > ar.wait_ns) { atomicExch(ar.err, 2); return v; }
+            __nanosleep(64);
         }
     }
-    __syncthreads();
 }
 
 }  // namespace
@@ -196,7 +145,7 @@ __global__ void __launch_bounds__(64) k_xprep(const float* x, int64_t ldx, int n
 // ------------------------------------------------------------------------------------------------------------------
 // A cluster of gridDim.x CTAs per row (row blockIdx.y): CTA r of the cluster owns superblocks r*W .. r*W+W-1 of the
 // row (W = blockDim.x / 32), warp w superblock r*W + w, a lane 8 consecutive values. Spreading a row over several SMs
-// spreads its loads, and under tensor parallelism each CTA pulls only its own slice of every peer's partial.
+// spreads its loads, and under tensor parallelism each CTA polls only its own slice of the ranks' pushed partials.
 // x += o * rs (Transformer.cs:225,231) when o is given; y = RmsNormRows(x) * w (Transformer.cs:454-464, sum of squares
 // in double: lanes by xor butterfly, then warps in order, then the cluster's CTAs in order, through distributed
 // shared memory, so every CTA of the row gets the same sum); when prep is given, y's superblocks are also written in
@@ -244,28 +193,37 @@ __global__ void __launch_bounds__(256) k_norm_prep(float* x, const float* o, flo
             oa = make_float4(ov[0], ov[1], ov[2], ov[3]);
             ob = make_float4(ov[4], ov[5], ov[6], ov[7]);
         } else if (ar.G > 0) {
-            // the fused all-reduce: every rank's partial of this row (peers' over NVLink), summed in rank order
+            // the fused all-reduce: every rank's partial of this row, pushed into this rank's buffer, summed in rank
+            // order; each rank's four 16-byte loads are issued before any is checked
             const unsigned long long q = ar_seq(ar.epoch, ar.idx);
-            ar_sync(ar, q, blockIdx.x == 0 && blockIdx.y == 0);
-            const size_t off = ((size_t)(q % AR_SLOTS) * AR_COLS + ar.row0 + t) * (size_t)E + i0;
-            // every rank's loads first (in flight together over NVLink), then the sums in rank order
-            float4 ua[AR_MAX_RANKS], ub[AR_MAX_RANKS];
+            const uint32_t fl = ar_flag(q);
+            float ov[8];
 #pragma unroll
-            for (int src = 0; src < AR_MAX_RANKS; ++src)
-                if (src < ar.G) {
-                    ua[src] = __ldcv(reinterpret_cast<const float4*>(ar.data[src] + off));
-                    ub[src] = __ldcv(reinterpret_cast<const float4*>(ar.data[src] + off + 4));
-                }
-            oa = ua[0];
-            ob = ub[0];
+            for (int h = 0; h < AR_MAX_RANKS; h += 4) {
+                uint4 ln[4][4];
 #pragma unroll
-            for (int src = 1; src < AR_MAX_RANKS; ++src)
-                if (src < ar.G) {
-                    oa = make_float4(__fadd_rn(oa.x, ua[src].x), __fadd_rn(oa.y, ua[src].y), __fadd_rn(oa.z, ua[src].z),
-                                     __fadd_rn(oa.w, ua[src].w));
-                    ob = make_float4(__fadd_rn(ob.x, ub[src].x), __fadd_rn(ob.y, ub[src].y), __fadd_rn(ob.z, ub[src].z),
-                                     __fadd_rn(ob.w, ub[src].w));
-                }
+                for (int src = h; src < h + 4; ++src)
+                    if (src < ar.G) {
+                        const unsigned long long* pe = ar.ll + ar_elem(q, src, ar.row0 + t, E) + i0;
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; ++k4) ln[src - h][k4] = ld_elem2(pe + 2 * k4);
+                    }
+#pragma unroll
+                for (int src = h; src < h + 4; ++src)
+                    if (src < ar.G) {
+                        const unsigned long long* pe = ar.ll + ar_elem(q, src, ar.row0 + t, E) + i0;
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; ++k4) {
+                            uint4 v = ln[src - h][k4];
+                            if (v.y != fl || v.w != fl) v = ar_wait_elem2(pe + 2 * k4, fl, ar);
+                            const float v0 = __uint_as_float(v.x), v1 = __uint_as_float(v.z);
+                            ov[2 * k4] = src == 0 ? v0 : __fadd_rn(ov[2 * k4], v0);
+                            ov[2 * k4 + 1] = src == 0 ? v1 : __fadd_rn(ov[2 * k4 + 1], v1);
+                        }
+                    }
+            }
+            oa = make_float4(ov[0], ov[1], ov[2], ov[3]);
+            ob = make_float4(ov[4], ov[5], ov[6], ov[7]);
         } else {
             const float* orow = o + (int64_t)t * E + i0;
             oa = *reinterpret_cast<const float4*>(orow);
@@ -407,8 +365,6 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
-__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
-
 // One CTA per 16 rows; warp w of its NW warps takes superblocks w, w+NW, ... of those rows. Per superblock and 32-value sub-block
 // one integer MMA (u8 codes x s8 activation digits, exact int32) gives sum(q*X); the 6-bit sub-block scales are
 // applied in integers; the superblock's d and the digit unit are applied in fp32 per digit plane; the min term
@@ -417,11 +373,11 @@ __device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
 // PAIRS: the grouped-expert form (seg.sel set), compiled apart so that the dense matvec carries none of its code.
-template <int NC, bool TILED, bool PAIRS, int NW = 8>
+template <int NC, bool TILED, bool PAIRS, int NW = 8, bool AR = false>
 __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
                                                     const uint8_t* xq, float* y_a,
-                                                    int64_t ldy_a, int* err, const MvSeg seg)
+                                                    int64_t ldy_a, int* err, const MvSeg seg, const ArOut ao)
 {
     using LY = Q4Layout<NC, NW>;
     constexpr bool PACK = NC <= 2;
@@ -628,7 +584,11 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(c
             const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
             sum += v;
         }
-        y[(int64_t)col * ldy + r0 + rl] = sum;
+        if constexpr (AR) {
+            ar_push_elem(ao, col, r0 + rl, sum);     // a fused all-reduce's partial: pushed into every rank's buffer
+        } else {
+            y[(int64_t)col * ldy + r0 + rl] = sum;
+        }
     }
 }
 
@@ -1198,6 +1158,25 @@ __global__ void k_q6k_tile(const uint8_t* src, int rows, int nsb, int64_t row_by
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// the fused all-reduce's push for producers other than the Q4_K decode matvec
+// ------------------------------------------------------------------------------------------------------------------
+// Row blockIdx.y of src (E floats) into every rank's elements of all-reduce ao.idx, source ao.rank: a thread per two
+// consecutive values, one 16-byte store per rank.
+__global__ void __launch_bounds__(128) k_ar_push(const float* src, const ArOut ao)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y, i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    const float2 v = *reinterpret_cast<const float2*>(src + (int64_t)t * ao.E + i);
+    const unsigned long long q = ar_seq(ao.epoch, ao.idx);
+    const uint32_t fl = ar_flag(q);
+    const size_t off = ar_elem(q, ao.rank, t, ao.E) + i;
+#pragma unroll
+    for (int g = 0; g < AR_MAX_RANKS; ++g)
+        if (g < ao.G) st_elem2(ao.ll[g] + off, v.x, v.y, fl);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------------------------
 size_t xprep_bytes(int cols, int nc) { return xprep_bytes_c(cols, nc); }
@@ -1243,9 +1222,9 @@ void norm_prep(float* x, const float* o, float rs, int T, int E, const float* w,
 
 int selftest_ar_wait(long long wait_ns)
 {
-    // one row of 256 values, the all-reduce of two ranks where this GPU is rank 0 and rank 1 never runs: rank 0's
-    // announcement lands in its own flags (it is its own "peer" here) and its wait for rank 1's announcement of the
-    // current sequence number (epoch 1, index 0) can only run out
+    // one row of 256 values, the all-reduce of two ranks where this GPU is rank 0 and rank 1 never runs: rank 0 pushes
+    // its own elements of the current sequence number (epoch 1, index 0) into its buffer, and the consumer's wait for
+    // rank 1's elements can only run out
     const int E = 256;
     const size_t arb = ar_buffer_bytes(E);
     uint8_t* buf = nullptr;
@@ -1263,13 +1242,15 @@ int selftest_ar_wait(long long wait_ns)
         WL_CUDA(cudaMemset(err, 0, sizeof(int)));
         const unsigned long long epoch = 1;
         WL_CUDA(cudaMemcpy(buf + AR_EPOCH, &epoch, sizeof epoch, cudaMemcpyHostToDevice));
+        unsigned long long* ll = reinterpret_cast<unsigned long long*>(buf + ar_ll_offset(E));
+        ArOut out{};
+        out.ll[0] = ll;
+        out.epoch = reinterpret_cast<const unsigned long long*>(buf + AR_EPOCH);
+        out.idx = 0; out.G = 1; out.rank = 0; out.E = E;
+        ar_push(x, 1, out, 0);
         ArIn in{};
-        for (int g = 0; g < 2; ++g) {
-            in.data[g] = reinterpret_cast<const float*>(buf + AR_HEADER);
-            in.peer_flags[g] = reinterpret_cast<unsigned long long*>(buf);
-        }
-        in.flags = reinterpret_cast<const unsigned long long*>(buf);
-        in.epoch = reinterpret_cast<const unsigned long long*>(buf + AR_EPOCH);
+        in.ll = ll;
+        in.epoch = out.epoch;
         in.err = err;
         in.idx = 0; in.G = 2; in.rank = 0; in.E = E; in.row0 = 0;
         in.wait_ns = wait_ns;
@@ -1282,6 +1263,16 @@ int selftest_ar_wait(long long wait_ns)
     }
     cudaFree(buf); cudaFree(x); cudaFree(err);
     return code;
+}
+
+void ar_push(const float* src, int T, const ArOut& ao, cudaStream_t s)
+{
+    if (T <= 0) return;
+    if (T > AR_COLS || ao.G < 1 || ao.G > AR_MAX_RANKS || ao.rank < 0 || ao.rank >= ao.G || ao.E % 256 != 0 ||
+        ao.idx < 0 || ao.idx >= AR_STEP)
+        WL_THROW(WL_EINVAL, "ar_push: all-reduce slot does not match");
+    launch(k_ar_push, dim3(ao.E / 256, T), dim3(128), 0, s, src, ao);
+    note_launch();
 }
 
 XPrep xprep_view(void* scratch, int cols, int nc)
@@ -1351,11 +1342,11 @@ static void ensure_smem_attr(Kernel kernel, int bytes, std::atomic<bool> (&done)
     done[dev].store(true, std::memory_order_release);
 }
 
-template <int NC, bool TILED, bool PAIRS, int NW = 8> struct Q4Attr {
+template <int NC, bool TILED, bool PAIRS, int NW = 8, bool AR = false> struct Q4Attr {
     static std::atomic<bool> done[64];
-    static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS, NW>, Q4Layout<NC, NW>::SMEM, done); }
+    static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS, NW, AR>, Q4Layout<NC, NW>::SMEM, done); }
 };
-template <int NC, bool TILED, bool PAIRS, int NW> std::atomic<bool> Q4Attr<NC, TILED, PAIRS, NW>::done[64];
+template <int NC, bool TILED, bool PAIRS, int NW, bool AR> std::atomic<bool> Q4Attr<NC, TILED, PAIRS, NW, AR>::done[64];
 template <int NC, int NW, int NS, bool SK> struct Q4Attr2 {
     static std::atomic<bool> done[64];
     static void ensure() { ensure_smem_attr(k_mmv_q4k2<NC, NW, NS, SK>, Q4Layout2<NC, NW, NS>::SMEM, done); }
@@ -1369,30 +1360,38 @@ template <int NC> std::atomic<bool> Q6Attr<NC>::done[64];
 
 template <int NC, bool TILED, bool PAIRS = false, int NW = 8>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                       float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
+                       float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg, const ArOut& ao = ArOut{})
 {
+    if (TILED && !PAIRS && ao.G > 0) {
+        // the fused all-reduce's producer: its own instantiation, so the one-GPU kernels keep their register allocation
+        Q4Attr<NC, true, false, NW, true>::ensure();
+        launch(k_mmv_q4k<NC, true, false, NW, true>, dim3((rows + Q4_ROWS - 1) / Q4_ROWS), dim3(32 * NW),
+               Q4Layout<NC, NW>::SMEM, s, m, tiles, row_base, rows, nsb, (const uint8_t*)p.blocks, y, ldy, err, seg, ao);
+        note_launch();
+        return;
+    }
     Q4Attr<NC, TILED, PAIRS, NW>::ensure();
     const int ctas = seg.sel ? seg.tiles_per_pair * seg.first_ctas * (seg.wt ? 2 : 1)
                              : (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     if (PAIRS != (seg.sel != nullptr)) WL_THROW(WL_EINVAL, "matvec: the grouped-expert form needs the expert ids");
     launch(k_mmv_q4k<NC, TILED, PAIRS, NW>, dim3(ctas), dim3(32 * NW), Q4Layout<NC, NW>::SMEM, s, m, tiles, row_base,
-           rows, nsb, (const uint8_t*)p.blocks, y, ldy, err, seg);
+           rows, nsb, (const uint8_t*)p.blocks, y, ldy, err, seg, ao);
     note_launch();
 }
 
 template <bool TILED, int NW = 8>
 static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                         float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
+                         float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg, const ArOut& ao = ArOut{})
 {
     switch (p.nc) {
-    case 1: launch_q4k<1, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 2: launch_q4k<2, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 3: launch_q4k<3, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 4: launch_q4k<4, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 5: launch_q4k<5, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 6: launch_q4k<6, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    case 7: launch_q4k<7, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
-    default: launch_q4k<8, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg); break;
+    case 1: launch_q4k<1, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 2: launch_q4k<2, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 3: launch_q4k<3, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 4: launch_q4k<4, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 5: launch_q4k<5, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 6: launch_q4k<6, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    case 7: launch_q4k<7, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
+    default: launch_q4k<8, TILED, false, NW>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao); break;
     }
 }
 
@@ -1462,14 +1461,14 @@ static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb,
 // columns on, 8 % faster at 8 columns, but its 8192-row matrices then grouped a row's superblocks by four where a
 // single-sequence step groups them by eight.)
 static void dispatch_q4k16(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
-                           float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg)
+                           float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg, const ArOut& ao = ArOut{})
 {
     const int tiles_n = (rows + Q4_ROWS - 1) / Q4_ROWS + (seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0);
     const int nw = tiles_n >= 8 * sm_count() ? 4 : 8;
     if (nw == 4)
-        dispatch_q4k<true, 4>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
+        dispatch_q4k<true, 4>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao);
     else
-        dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
+        dispatch_q4k<true, 8>(m, tiles, row_base, rows, nsb, p, y, ldy, err, s, seg, ao);
 }
 
 void prepare_matvec_mma()
@@ -1583,16 +1582,19 @@ void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_ro
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, int P, int64_t pstride)
+                  int64_t ldy, int* err, cudaStream_t s, int P, int64_t pstride, const ArOut* ao)
 {
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
     if (P < 1 || P > cols / 256 || (type != 12 && P != 1)) WL_THROW(WL_EINVAL, "matvec_tiles: bad split count");
+    if (ao && (type != 12 || P != 1 || ao->G < 1 || ao->G > AR_MAX_RANKS || ao->rank < 0 || ao->rank >= ao->G ||
+               ao->E != rows || p.nc > AR_COLS || ao->idx < 0 || ao->idx >= AR_STEP))
+        WL_THROW(WL_EINVAL, "matvec_tiles: the all-reduce push does not match");
     if (type == 12 && P == 1) {
         CUtensorMap none;
         memset(&none, 0, sizeof none);
         dispatch_q4k16(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
-                       MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0});
+                       MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0}, ao ? *ao : ArOut{});
     } else if (type == 12) {
         dispatch_q4k2(tiles, row_base, rows, cols / 256, p, y, ldy, P, pstride, err, s,
                       MvSeg2{nullptr, 0, 0, INT_MAX, nullptr, 0});

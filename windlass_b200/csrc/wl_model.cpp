@@ -202,14 +202,26 @@ void Model::close_fused_ar()
 }
 
 // The output projection of a sublayer (o or down) summed over the tensor-parallel ranks into the next norm's input:
-// for decode steps the matvec writes this rank's partial into its all-reduce slot and the next norm sums every
-// rank's (k::ArIn), else the matvec writes o_ and NCCL all-reduces it. One GPU: the matvec into o_.
+// for decode steps this rank's partial is pushed into every rank's all-reduce buffer (by the Q4_K decode matvec's
+// epilogue, else staged and pushed by k::ar_push) and the next norm sums every rank's (k::ArIn), else the matvec
+// writes o_ and NCCL all-reduces it. One GPU: the matvec into o_.
 void Model::matmul_reduce(const Weight& w, const float* x, int T)
 {
     const int E = c_.embd;
     if (ar_on_ && T <= k::AR_COLS && w.rows == E && ar_idx_ < k::AR_STEP) {
         const int idx = ar_idx_++;
-        matmul(w, x, T, reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E)), 0, true, E);
+        const k::ArOut ao = ar_out(idx);
+        float* stage = reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E));
+        ar_out_ = &ao;
+        ar_out_done_ = false;
+        try {
+            matmul(w, x, T, stage, 0, true, E);
+        } catch (...) {
+            ar_out_ = nullptr;
+            throw;
+        }
+        ar_out_ = nullptr;
+        if (!ar_out_done_) k::ar_push(stage, T, ao, stream_);
         pending_ar_ = idx;
         return;
     }
@@ -217,16 +229,26 @@ void Model::matmul_reduce(const Weight& w, const float* x, int T)
     all_reduce(o_, (int64_t)T * E);
 }
 
+// The producer side of fused all-reduce idx: every rank's pushed-element region.
+k::ArOut Model::ar_out(int idx) const
+{
+    k::ArOut ao{};
+    for (int g = 0; g < tp_size_; ++g)
+        ao.ll[g] = reinterpret_cast<unsigned long long*>(ar_peer_[g] + k::ar_ll_offset(c_.embd));
+    ao.epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
+    ao.idx = idx;
+    ao.G = tp_size_;
+    ao.rank = tp_rank_;
+    ao.E = c_.embd;
+    return ao;
+}
+
 // The consumer side of the pending fused all-reduce for rows row0 .. row0+T-1; false when none is pending.
 bool Model::pending_ar_in(int T, int row0, k::ArIn* in)
 {
     if (pending_ar_ < 0) return false;
     (void)T;
-    for (int g = 0; g < tp_size_; ++g) {
-        in->data[g] = reinterpret_cast<const float*>(ar_peer_[g] + k::AR_HEADER);
-        in->peer_flags[g] = reinterpret_cast<unsigned long long*>(ar_peer_[g]);
-    }
-    in->flags = reinterpret_cast<const unsigned long long*>(ar_buf_);
+    in->ll = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::ar_ll_offset(c_.embd));
     in->epoch = reinterpret_cast<const unsigned long long*>(ar_buf_ + k::AR_EPOCH);
     in->err = err_d_;
     in->idx = pending_ar_;
@@ -951,8 +973,10 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
                 prep_x_ = x; prep_cols_ = w.cols; prep_nc_ = nc;
             }
             const int mark = profile_begin();
+            const bool push = ar_out_ && w.type == 12 && T <= 8;
             k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * ldy, ldy, err_d_,
-                            stream_);
+                            stream_, 1, 0, push ? ar_out_ : nullptr);
+            if (push) ar_out_done_ = true;
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
         if (T > 8) prep_x_ = nullptr;
@@ -1144,8 +1168,9 @@ void Model::ffn_moe_device(const LayerW& L, int T)
         // all-reduce slot (decode steps), else NCCL
         if (ar_on_ && T <= k::AR_COLS && ar_idx_ < k::AR_STEP) {
             const int idx = ar_idx_++;
-            k::moe_combine(py_, sel_, wts_, T, K, E, reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E)),
-                           stream_, e_lo_, e_n_);
+            float* stage = reinterpret_cast<float*>(ar_buf_ + k::ar_slot_offset(idx, E));
+            k::moe_combine(py_, sel_, wts_, T, K, E, stage, stream_, e_lo_, e_n_);
+            k::ar_push(stage, T, ar_out(idx), stream_);
             pending_ar_ = idx;
         } else {
             k::moe_combine(py_, sel_, wts_, T, K, E, o_, stream_, e_lo_, e_n_);

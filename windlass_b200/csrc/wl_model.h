@@ -176,6 +176,7 @@ private:
     void close_fused_ar();
     void matmul_reduce(const Weight& w, const float* x, int T);
     bool pending_ar_in(int T, int row0, k::ArIn* in);
+    k::ArOut ar_out(int idx) const;
     void begin_step(int T);
     bool stop_requested(volatile const int32_t* cancel);
     void finish_open();
@@ -229,6 +230,8 @@ private:
     bool ar_on_ = false;
     int ar_idx_ = 0;                      // fused all-reduces enqueued so far in the current step
     int pending_ar_ = -1;                 // index of the all-reduce whose sum the next norm consumes, or -1
+    const k::ArOut* ar_out_ = nullptr;    // set while matmul_reduce runs: the Q4_K decode matvec pushes into it
+    bool ar_out_done_ = false;            // the matvec pushed (else matmul_reduce pushes the staged partial)
     int max_context_ = 0;
     int max_batch_ = 64;
     int prefill_path_ = 0;
