@@ -189,10 +189,11 @@ def sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args):
 
 def sweep(args):
     """the matvec/matmul sweep (8192 x 8192 by default; --shapes adds the 70B layer's shapes). Per shape,
-    format and batch column count: the time of one call over rotating weight copies whose total exceeds L2. Q4_K and
-    Q6_K at b <= 8: the decode matvec on weights repacked once, launches back to back as in a decode step
-    (wl_bench_matvec_tiles); other formats at b <= 8: wl_matvec (activation prep + matvec); b > 8: wl_gemm_tiles for
-    Q4_K, else wl_matmul; the last two from CUDA events around replays of a CUDA graph of `iters` calls. Then the weight
+    format and batch column count: the time of one call over rotating weight copies whose total exceeds L2, on weights
+    repacked once into tiles (the model's layout). b <= 8: the decode matvec, launches back to back as in a decode step
+    (wl_bench_matvec_tiles); b > 8: the tcgen05 GEMM for Q4_K and Q6_K (wl_gemm_tiles), the integer tensor-core matvec
+    8 columns a launch for Q8_0, IQ4_XS and IQ2_XXS (wl_matvec_tiles); those from CUDA events around replays of a CUDA
+    graph of `iters` calls. Then the weight
     bandwidth (b <= 8) or TFLOP/s (b >= 64), with the reference's CPU arithmetic (the C oracle, all host threads,
     best of 3) beside each cell. One JSON line with the whole table."""
     import ctypes as C
@@ -234,7 +235,7 @@ def sweep(args):
             if not args.no_cpu:
                 torch.cuda.synchronize()
                 raw0 = ws[0].cpu().numpy()
-            tiled = f in ("q4_K", "q6_K")
+            tiled = f in ("q4_K", "q6_K", "q8_0", "iq4_xs", "iq2_xxs")
             if tiled:       # the model's layout: weights repacked once into tiles, so no call repacks
                 tb = C.c_int64()
                 _lib.check(L.wl_tiles_size(t, R, K, C.byref(tb)))
@@ -270,9 +271,12 @@ def sweep(args):
                     elif b <= 8:
                         st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
                                          C.c_void_p(y.data_ptr()), cs)
-                    elif tiled and f == "q4_K":   # the tcgen05 GEMM on the repacked weights
+                    elif tiled and f in ("q4_K", "q6_K"):   # the tcgen05 GEMM on the repacked weights
                         st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
                                              C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
+                    elif tiled:     # the integer tensor-core matvec, 8 columns a launch, on the repacked weights
+                        st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
+                                               C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
                     else:
                         st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
                                          C.c_void_p(y.data_ptr()), 0, cs)

@@ -124,7 +124,10 @@ def test_config1_full_size_matvec(wl, oracle, tname):
         assert rel_l2(y, want) <= 1e-4, (tname, ncols, rel_l2(y, want))
 
 
-@pytest.mark.parametrize("tname", ["q4_K", "q6_K"])
+TILE_BYTES = {"q4_K": 2304, "q6_K": 3360, "q8_0": 4352, "iq4_xs": 2208, "iq2_xxs": 1056}
+
+
+@pytest.mark.parametrize("tname", ["q4_K", "q6_K", "q8_0", "iq4_xs", "iq2_xxs"])
 def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
     """wl_make_tiles + wl_matvec_tiles (the model's weight layout) against the reference dot products, and bit-equal
     to wl_matvec (which repacks per call); ragged row count (not a multiple of 16)."""
@@ -138,7 +141,7 @@ def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
     dw, dx = dev(w), dev(x.reshape(-1))
     nb = C.c_int64()
     wl.check(L.wl_tiles_size(t, rows, cols, C.byref(nb)))
-    assert nb.value == (rows + 15) // 16 * (cols // 256) * (2304 if tname == "q4_K" else 3360)
+    assert nb.value == (rows + 15) // 16 * (cols // 256) * TILE_BYTES[tname]
     tiles = empty(nb.value, "uint8")
     wl.check(L.wl_make_tiles(t, ptr(dw), rows, cols, ptr(tiles), None))
     dy = empty(ncols * rows)
@@ -149,20 +152,25 @@ def test_tile_layout_matvec_matches_reference(wl, oracle, tname):
         assert rel_l2(got[c], want[c]) <= 1e-4, (tname, c, rel_l2(got[c], want[c]))
     assert np.array_equal(got, _matvec(wl, t, dw, rows, cols, x, ncols))
     with pytest.raises(wl.NotSupportedError):
-        wl.check(L.wl_tiles_size(O.TYPE_OF["q8_0"], rows, cols, C.byref(nb)))
+        wl.check(L.wl_tiles_size(O.TYPE_OF["q5_K"], rows, cols, C.byref(nb)))
+    with pytest.raises(wl.NotSupportedError):
+        wl.check(L.wl_tiles_size(t, rows, cols + 32, C.byref(nb)))
 
 
-@pytest.mark.parametrize("rows,cols", [(75, 2048), (1000, 256), (4099, 1024), (19000, 512), (8192, 8192)])
-def test_tile_matvec_columns_independent_of_batch(wl, oracle, rows, cols):
-    """A column's result from wl_matvec_tiles does not depend on how many columns share the call: at every column
+@pytest.mark.parametrize("tname,rows,cols", [("q4_K", 75, 2048), ("q4_K", 1000, 256), ("q4_K", 4099, 1024),
+                                             ("q4_K", 19000, 512), ("q4_K", 8192, 8192), ("q8_0", 75, 2048),
+                                             ("q8_0", 19000, 512), ("iq4_xs", 1000, 256), ("iq4_xs", 4099, 1024),
+                                             ("iq2_xxs", 75, 2048), ("iq2_xxs", 19000, 512)])
+def test_tile_matvec_columns_independent_of_batch(wl, oracle, tname, rows, cols):
+    """For each tiled format, a column's result from wl_matvec_tiles does not depend on how many columns share the call: at every column
     count 1..8 each column equals the one-column call on that column bit for bit (the decode step's rows equal
     single-sequence steps, tests/BatchTests.cs:29-94), on ragged rows, fewer superblocks than the warps that share a
     row (1000 x 256), and row counts on both sides of the launch-shape threshold (19000 rows: 1188 row tiles);
     within 1e-4 relative L2 of the float64 products."""
     O = oracle
-    t = O.Q4_K
+    t = O.TYPE_OF[tname]
     L = wl.lib()
-    w = weights(O, "q4_K", rows, cols, seed=rows + cols)
+    w = weights(O, tname, rows, cols, seed=rows + cols)
     x = np.random.default_rng(rows).standard_normal((8, cols)).astype(np.float32)
     dw, dx = dev(w), dev(x.reshape(-1))
     nb = C.c_int64()

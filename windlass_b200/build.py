@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(HERE, "libwindlass_cuda.so")
 
-SOURCES = ["wl_kernels.cu", "wl_mmv.cu", "wl_noalloc.cu", "wl_model.cpp", "wl_gguf.cpp", "wl_common.cpp", "wl_api.cpp",
+SOURCES = ["wl_kernels.cu", "wl_mmv.cu", "wl_mmv_i8.cu", "wl_noalloc.cu", "wl_model.cpp", "wl_gguf.cpp", "wl_common.cpp", "wl_api.cpp",
            "wl_nccl.cpp", "wl_stream.cpp", "wl_gemm.cu", "wl_group.cpp", "wl_sample.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -47,6 +47,7 @@ void init_tables()
     WL_CUDA(cudaMemcpyToSymbol(g_iq2xxs_grid, WL_IQ2XXS_GRID, sizeof(WL_IQ2XXS_GRID)));
     WL_CUDA(cudaMemcpyToSymbol(g_ksigns, WL_KSIGNS_IQ2XS, sizeof(WL_KSIGNS_IQ2XS)));
     WL_CUDA(cudaMemcpyToSymbol(g_kvalues, WL_KVALUES_IQ4NL, sizeof(WL_KVALUES_IQ4NL)));
+    init_i8_tables();
     if (dev < 64) done |= 1ull << dev;
 }
 

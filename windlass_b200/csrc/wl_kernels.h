@@ -138,6 +138,15 @@ void prepare_matvec_mma();
 // y[t*ldy + r] = W[row_base + r] . x[t] from prepared activations (same contract as matvec), row_base a multiple of 16.
 constexpr int Q6K_TILE = 3360;     // bytes of one Q6_K tile: 16 rows x one 210-byte superblock
 bool tiles_supported(int type, int cols);
+// Q8_0, IQ4_XS and IQ2_XXS (type 8, 23, 16) in the same scheme (wl_mmv_i8.cu): tiles of 16 rows x 256 values, an
+// integer tensor-core matvec over the values decoded to int8; tiles_supported, tile_bytes, make_tiles and matvec_tiles
+// cover them too.
+bool i8_tiles_supported(int type, int cols);
+int64_t i8_tile_bytes(int type, int rows, int cols);
+void make_i8_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
+void matvec_i8_tiles(int type, const uint8_t* tiles, int rows, int cols, const XPrep& p, float* y, int64_t ldy, int* err,
+                     cudaStream_t s);
+void init_i8_tables();
 int64_t tile_bytes(int type, int rows, int cols);
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
 // P > 1 (Q4_K only, P <= cols / 256) splits the superblocks into P equal contiguous ranges and writes P partial

@@ -440,7 +440,9 @@ void Model::load_from_gguf(const Gguf& g)
             // streamed matrices: bounded by their whole size, raw and in tiles (rows rounded up to 16)
             const int64_t rows_all = t.elements() / std::max<int64_t>(t.dims[0], 1);
             raw_upper[(size_t)st] += (t.size + 255) / 256 * 256;
-            slot_upper[(size_t)st] += ((rows_all + 15) / 16 * 16) * (t.size / std::max<int64_t>(rows_all, 1)) + 256;
+            int64_t laid = ((rows_all + 15) / 16 * 16) * (t.size / std::max<int64_t>(rows_all, 1));
+            if (k::tiles_supported(t.type, t.cols())) laid = std::max(laid, k::tile_bytes(t.type, (int)rows_all, t.cols()));
+            slot_upper[(size_t)st] += laid + 256;
             continue;
         }
         total += (bytes + 255) / 256 * 256 + (t.elements() * 4 / (G > 1 ? G : 1) + 255) / 256 * 256;
@@ -714,7 +716,9 @@ Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
         const int st = stage_of(p);
         if (st >= 0) {
             raw_upper[(size_t)st] += bytes;
-            slot_upper[(size_t)st] += (nr + 15) / 16 * 16 * row_bytes_of(p.type, nc) + 256;
+            int64_t laid = (nr + 15) / 16 * 16 * row_bytes_of(p.type, nc);
+            if (k::tiles_supported(p.type, (int)nc)) laid = std::max(laid, k::tile_bytes(p.type, (int)nr, (int)nc));
+            slot_upper[(size_t)st] += laid + 256;
         } else {
             total += bytes;
         }
@@ -1055,8 +1059,10 @@ static Weight slice(const Weight& w, int e)
 void Model::build_maps()
 {
     auto mk = [&](Weight& w) {
-        // Q4_K / Q6_K: a tile-major copy for the tensor-core matvec (expert slices must start on a tile)
-        if (w.present() && !w.tiles && k::tiles_supported(w.type, w.cols) && (w.experts == 1 || w.rows % 16 == 0)) {
+        // Q4_K / Q6_K, Q8_0, IQ4_XS, IQ2_XXS: a tile-major copy for the tensor-core matvec (expert slices must start
+        // on a tile; only Q4_K and Q6_K experts are read from tiles)
+        if (w.present() && !w.tiles && k::tiles_supported(w.type, w.cols) &&
+            (w.experts == 1 || ((w.type == 12 || w.type == 14) && w.rows % 16 == 0))) {
             const int total = w.rows * w.experts;
             void* t = nullptr;
             WL_CUDA(cudaMalloc(&t, (size_t)k::tile_bytes(w.type, total, w.cols)));

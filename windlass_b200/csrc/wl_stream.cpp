@@ -65,7 +65,8 @@ void Model::end_stage(int l, const std::vector<Weight*>& ws)
     for (Weight* w : ws) {
         if (!w->present()) continue;
         const int total_rows = w->rows * w->experts;
-        const bool tiled = k::tiles_supported(w->type, w->cols) && (w->experts == 1 || w->rows % 16 == 0);
+        const bool tiled = k::tiles_supported(w->type, w->cols) &&
+                           (w->experts == 1 || ((w->type == 12 || w->type == 14) && w->rows % 16 == 0));
         const int64_t bytes = tiled ? k::tile_bytes(w->type, total_rows, w->cols) : w->bytes;
         if (off + bytes > slot_bytes_) WL_THROW(WL_ENOMEM, "streaming: a stage does not fit its slot");
         if (tiled) k::make_tiles(w->type, w->d, total_rows, w->cols, w->row_bytes, slot_[0] + off, stream_);
