@@ -256,8 +256,8 @@ int32_t wl_profile_get(wl_model* model, int32_t type, wl_profile_entry* out);
 /* ---- kernel-level exports for tests and benchmarks (device pointers, stream = cudaStream_t or NULL) ---- */
 
 /* No counterpart in the reference. Failure detection of the tensor-parallel all-reduce without a GPU fault: runs the
- * all-reduce's consumer kernel on `device` against a peer rank that never announces (a flag nothing sets), its wait
- * limited to wait_ms. The wait gives up, the kernel returns, and the call returns WL_ETIMEDOUT with the device still
+ * all-reduce's consumer kernel on `device` against a peer rank that never pushes its partial (elements nothing
+ * writes), its wait limited to wait_ms. The wait gives up, the kernel returns, and the call returns WL_ETIMEDOUT with the device still
  * usable, which is what a rank sees when a peer dies between steps. (Real waits are limited to 10 s.) */
 int32_t wl_selftest_allreduce_timeout(int32_t device, int32_t wait_ms);
 

@@ -1,5 +1,5 @@
 """Failure detection without a GPU fault: the tensor-parallel all-reduce's device-side wait for a peer is bounded in
-time. Run on one GPU against a peer that never arrives (a flag nothing sets), the wait gives up after its limit, the
+time. Run on one GPU against a peer that never arrives (elements nothing writes), the wait gives up after its limit, the
 call reports WL_ETIMEDOUT, and the device stays usable for the next call."""
 import ctypes as C
 import time

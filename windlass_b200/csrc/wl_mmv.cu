@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include "wl_common.h"
@@ -589,6 +590,230 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(c
         } else {
             y[(int64_t)col * ldy + r0 + rl] = sum;
         }
+    }
+}
+
+// ---- the persistent form (six to eight columns) ----
+// At many columns, a 16-row CTA that streams every superblock's prepared activations for NC columns (992 bytes
+// each) next to 2304 bytes of weights is bound by its stage count and the CTAs resident per SM rather than by HBM:
+// 8192 x 8192 at 8 columns took 20 us in four partial waves. Here a grid of as many CTAs as fit at once walks the row
+// tiles in pairs (pair p = tiles 2p, 2p + 1 of one matrix; a matrix with an odd tile count ends in a single), CTA b
+// taking pairs b, b + gridDim.x, ...: each stage holds both tiles of one superblock and the activations once, every
+// warp's ring runs on across pairs, and the activation fragments of a sub-block serve both tiles. Warp w still takes
+// superblocks w, w + NW, ... of every row, each tile's arithmetic is k_mmv_q4k's (the same integer MMAs, fp32
+// operations and order, planes added ((0 + 1) + 2) - min, warps in order), so every row equals k_mmv_q4k's bit for bit.
+template <int NC, int NW> struct Q4LayoutP {
+    static constexpr int X_OFF = 2 * Q4_TILE;
+    static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;
+    static constexpr int STAGES = 2;
+    static constexpr int RED = NW * 2 * Q4_ROWS * 9 * 4;
+    static constexpr int SMEM = NW * STAGES * STAGE + RED;
+};
+
+template <int NC, int NW>
+__global__ void __launch_bounds__(32 * NW, 1) k_mmv_q4kp(const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a,
+                                                        int nsb, const uint8_t* xq, float* y_a, int64_t ldy_a,
+                                                        int* err, const MvSeg seg)
+{
+    static_assert(NC >= 3 && NC <= 8, "the persistent form serves three to eight columns");
+    using LY = Q4LayoutP<NC, NW>;
+    constexpr int ND = 3;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[NW][LY::STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int tiles_a = (rows_a + Q4_ROWS - 1) / Q4_ROWS;
+    const int pairs_a = (tiles_a + 1) / 2;
+    const int tiles_b = seg.wt ? (seg.rows + Q4_ROWS - 1) / Q4_ROWS : 0;
+    const int pairs = pairs_a + (tiles_b + 1) / 2;
+    const int G = (int)gridDim.x;
+    const int npair = pairs > (int)blockIdx.x ? (pairs - (int)blockIdx.x + G - 1) / G : 0;
+    const int per = nsb > warp ? (nsb - warp + NW - 1) / NW : 0;     // this warp's superblocks of a row
+    const int njobs = npair * per;
+    uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
+    float* red = reinterpret_cast<float*>(smem + NW * LY::STAGES * LY::STAGE);     // [NW][2][Q4_ROWS][9]
+
+    // pair q (global index): its matrix, first tile (in that matrix's tile numbering) and tile count
+    struct PairOf {
+        const uint8_t* wt;
+        int tile0, ntile, rows;
+        float* y;
+        int64_t ldy;
+    };
+    auto pair_of = [&](int q) -> PairOf {
+        PairOf r;
+        if (q < pairs_a) {
+            r.wt = wt_a; r.tile0 = row_base_a / Q4_ROWS + 2 * q; r.ntile = min(2, tiles_a - 2 * q);
+            r.rows = rows_a - 2 * q * Q4_ROWS; r.y = y_a + 2 * q * Q4_ROWS; r.ldy = ldy_a;
+        } else {
+            const int qb = q - pairs_a;
+            r.wt = seg.wt; r.tile0 = seg.row_base / Q4_ROWS + 2 * qb; r.ntile = min(2, tiles_b - 2 * qb);
+            r.rows = seg.rows - 2 * qb * Q4_ROWS; r.y = seg.y + 2 * qb * Q4_ROWS; r.ldy = seg.ldy;
+        }
+        return r;
+    };
+    auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
+        const int k = j / per, sb = warp + NW * (j - k * per);
+        const PairOf pr = pair_of((int)blockIdx.x + k * G);
+        uint8_t* st = ring + s * LY::STAGE;
+        mbar_expect_tx(&bars[warp][s], pr.ntile * Q4_TILE + NC * XP_COL);
+        for (int q = 0; q < pr.ntile; ++q)
+            bulk_load(st + q * Q4_TILE, pr.wt + ((int64_t)(pr.tile0 + q) * nsb + sb) * Q4_TILE, Q4_TILE, &bars[warp][s]);
+    };
+    auto issue_x = [&](int j, int s) {      // the superblock's prepared activations, on the same barrier
+        const int sb = warp + NW * (j % per);
+        uint8_t* st = ring + s * LY::STAGE;
+#pragma unroll
+        for (int n = 0; n < NC; ++n)
+            bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
+    };
+
+    pdl_trigger();
+    if (lane == 0) {
+        for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+        fence_proxy_async();
+    }
+    __syncwarp();
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_w(j, j);
+    pdl_wait();
+    if (lane == 0)
+        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
+
+    const bool b_ok = g < NC;
+    const int b_off = LY::X_OFF + g * XP_COL;
+    const bool m_ok0 = 2 * c < NC, m_ok1 = 2 * c + 1 < NC;
+    const uint32_t msel = (uint32_t)((2 * c) & 3) | (4u << 4) | ((uint32_t)((2 * c + 1) & 3) << 8) | (4u << 12);
+    const __half2 k1024 = __float2half2_rn(1024.f);
+
+    int j = 0;
+    for (int k = 0; k < npair; ++k) {
+        const PairOf pr = pair_of((int)blockIdx.x + k * G);
+        float facc[2][ND][4] = {};
+        float macc[2][4] = {};
+        for (int i = 0; i < per; ++i, ++j) {
+            const int s = j % LY::STAGES;
+            const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
+            const uint8_t* st = ring + s * LY::STAGE;
+            if (ok) {
+                uint4 h0[2], h1[2];
+                uint32_t s0lo[2], s0hi[2], s1lo[2], s1hi[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    if (q < pr.ntile) {
+                        h0[q] = lds128(st + q * Q4_TILE + g * 16);
+                        h1[q] = lds128(st + q * Q4_TILE + (g + 8) * 16);
+                    } else {
+                        h0[q] = make_uint4(0u, 0u, 0u, 0u);
+                        h1[q] = h0[q];
+                    }
+                    s0lo[q] = h0[q].y & 0x3F3F3F3Fu;
+                    s0hi[q] = (h0[q].w & 0x0F0F0F0Fu) | ((h0[q].y >> 2) & 0x30303030u);
+                    s1lo[q] = h1[q].y & 0x3F3F3F3Fu;
+                    s1hi[q] = (h1[q].w & 0x0F0F0F0Fu) | ((h1[q].y >> 2) & 0x30303030u);
+                }
+                int acc_lo[2][ND][4] = {}, acc_hi[2][ND][4] = {};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    uint2 bf[2][ND];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                        for (int d = 0; d < ND; ++d)
+                            bf[hh][d] = b_ok ? lds64(st + b_off + d * XP_DIGIT + 32 * (2 * r + hh) + 8 * c) : make_uint2(0u, 0u);
+                    const int kb = (2 * r) & 3;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        if (q >= pr.ntile) break;
+                        const uint4 wv = lds128(st + q * Q4_TILE + Q4_HDRS + r * 512 + lane * 16);
+                        const uint32_t sw0 = r < 2 ? s0lo[q] : s0hi[q], sw1 = r < 2 ? s1lo[q] : s1hi[q];
+                        const int sl0 = (int)((sw0 >> (8 * kb)) & 0xFFu), sh0 = (int)((sw0 >> (8 * kb + 8)) & 0xFFu);
+                        const int sl1 = (int)((sw1 >> (8 * kb)) & 0xFFu), sh1 = (int)((sw1 >> (8 * kb + 8)) & 0xFFu);
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            const uint32_t mask = hh ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                            const uint32_t a0 = wv.x & mask, a1 = wv.z & mask, a2 = wv.y & mask, a3 = wv.w & mask;
+                            const int sa = hh ? sh0 : sl0, sb2 = hh ? sh1 : sl1;
+#pragma unroll
+                            for (int d = 0; d < ND; ++d) {
+                                int D[4];
+                                imma16832(D, a0, a1, a2, a3, bf[hh][d].x, bf[hh][d].y);
+                                int (&acc)[4] = hh ? acc_hi[q][d] : acc_lo[q][d];
+                                acc[0] += sa * D[0];
+                                acc[1] += sa * D[1];
+                                acc[2] += sb2 * D[2];
+                                acc[3] += sb2 * D[3];
+                            }
+                        }
+                    }
+                }
+                // digit planes: unit * 2^(14 - 7 digit) / 16 per (column, digit), as k_mmv_q4k forms it
+                float fu[2][ND];
+#pragma unroll
+                for (int k2 = 0; k2 < 2; ++k2) {
+                    const int col = 2 * c + k2;
+                    const float unit = col < NC ? *reinterpret_cast<const float*>(st + LY::X_OFF + col * XP_COL + XP_REC + 32) : 0.f;
+#pragma unroll
+                    for (int d = 0; d < ND; ++d) fu[k2][d] = unit * (d == 0 ? 1024.f : d == 1 ? 8.f : 0.0625f);
+                }
+                const uint2 bs = g < NC ? lds64(st + LY::X_OFF + g * XP_COL + XP_REC + 8 * c) : make_uint2(0u, 0u);
+                const float mu0 = m_ok0 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c) * XP_COL + XP_REC + 32) * 1024.f : 0.f;
+                const float mu1 = m_ok1 ? *reinterpret_cast<const float*>(st + LY::X_OFF + (2 * c + 1) * XP_COL + XP_REC + 32) * 1024.f : 0.f;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    if (q >= pr.ntile) break;
+                    const float dd0 = h2f_((uint16_t)(h0[q].x & 0xFFFF)), dm0 = h2f_((uint16_t)(h0[q].x >> 16));
+                    const float dd1 = h2f_((uint16_t)(h1[q].x & 0xFFFF)), dm1 = h2f_((uint16_t)(h1[q].x >> 16));
+#pragma unroll
+                    for (int k2 = 0; k2 < 2; ++k2)
+#pragma unroll
+                        for (int d = 0; d < ND; ++d) {
+                            facc[q][d][k2] = fmaf((float)(acc_lo[q][d][k2] * 16 + acc_hi[q][d][k2]), dd0 * fu[k2][d],
+                                                  facc[q][d][k2]);
+                            facc[q][d][k2 + 2] = fmaf((float)(acc_lo[q][d][k2 + 2] * 16 + acc_hi[q][d][k2 + 2]),
+                                                      dd1 * fu[k2][d], facc[q][d][k2 + 2]);
+                        }
+                    const uint32_t m0lo = h0[q].z & 0x3F3F3F3Fu;
+                    const uint32_t m0hi = ((h0[q].w >> 4) & 0x0F0F0F0Fu) | ((h0[q].z >> 2) & 0x30303030u);
+                    const uint32_t m1lo = h1[q].z & 0x3F3F3F3Fu;
+                    const uint32_t m1hi = ((h1[q].w >> 4) & 0x0F0F0F0Fu) | ((h1[q].z >> 2) & 0x30303030u);
+                    const uint32_t mp0 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m0lo : m0hi, 0x64646464u, msel)), k1024));
+                    const uint32_t mp1 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m1lo : m1hi, 0x64646464u, msel)), k1024));
+                    float dn[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(dn, mp0, mp1, mp0, mp1, bs.x, bs.y);
+                    macc[q][0] = fmaf(dn[0], dm0 * mu0, macc[q][0]);
+                    macc[q][1] = fmaf(dn[1], dm0 * mu1, macc[q][1]);
+                    macc[q][2] = fmaf(dn[2], dm1 * mu0, macc[q][2]);
+                    macc[q][3] = fmaf(dn[3], dm1 * mu1, macc[q][3]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && j + LY::STAGES < njobs) {
+                fence_proxy_async();        // the stage's generic reads are done before the copy engine rewrites it
+                issue_w(j + LY::STAGES, s);
+                issue_x(j + LY::STAGES, s);
+            }
+        }
+        // this warp's sums of the pair: ((plane 0 + plane 1) + plane 2) - min per (row, column)
+        float* rw = red + warp * 2 * Q4_ROWS * 9;
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
+                if (col < NC) rw[(q * Q4_ROWS + row) * 9 + col] = ((facc[q][0][e] + facc[q][1][e]) + facc[q][2][e]) - macc[q][e];
+            }
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < 2 * Q4_ROWS * 8; idx += 32 * NW) {
+            const int rl = idx >> 3, col = idx & 7;     // rl: row 0..31 of the pair
+            if (col < NC && rl < pr.ntile * Q4_ROWS && rl < pr.rows) {
+                float sum = 0.f;
+#pragma unroll
+                for (int wv = 0; wv < NW; ++wv) sum += red[(wv * 2 * Q4_ROWS + rl) * 9 + col];
+                pr.y[(int64_t)col * pr.ldy + rl] = sum;
+            }
+        }
+        __syncthreads();                            // the red area is free for the next pair
     }
 }
 
@@ -1358,10 +1583,55 @@ template <int NC> struct Q6Attr {
 };
 template <int NC> std::atomic<bool> Q6Attr<NC>::done[64];
 
+static int sm_count();
+
+// The persistent form's grid: as many CTAs as fit on the GPU at once (per device, from the occupancy query), at most
+// one per tile pair.
+template <int NC, int NW> struct Q4AttrP {
+    static std::atomic<bool> done[64];
+    static std::atomic<int> per_sm[64];
+    static int ensure()
+    {
+        ensure_smem_attr(k_mmv_q4kp<NC, NW>, Q4LayoutP<NC, NW>::SMEM, done);
+        int dev = 0;
+        WL_CUDA(cudaGetDevice(&dev));
+        int n = per_sm[dev].load(std::memory_order_relaxed);
+        if (!n) {
+            WL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_mmv_q4kp<NC, NW>, 32 * NW, Q4LayoutP<NC, NW>::SMEM));
+            if (n < 1) WL_THROW(WL_ECUDA, "matvec: the persistent Q4_K kernel does not fit an SM");
+            per_sm[dev].store(n, std::memory_order_relaxed);
+        }
+        return n;
+    }
+};
+template <int NC, int NW> std::atomic<bool> Q4AttrP<NC, NW>::done[64];
+template <int NC, int NW> std::atomic<int> Q4AttrP<NC, NW>::per_sm[64];
+
+template <int NC, int NW>
+static void launch_q4kp(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
+                        int* err, cudaStream_t s, const MvSeg& seg)
+{
+    const int per_sm = Q4AttrP<NC, NW>::ensure();
+    const int pairs = ((rows + Q4_ROWS - 1) / Q4_ROWS + 1) / 2 + (seg.wt ? ((seg.rows + Q4_ROWS - 1) / Q4_ROWS + 1) / 2 : 0);
+    const int grid = std::max(1, std::min(pairs, sm_count() * per_sm));
+    launch(k_mmv_q4kp<NC, NW>, dim3(grid), dim3(32 * NW), Q4LayoutP<NC, NW>::SMEM, s, tiles, row_base, rows, nsb,
+           (const uint8_t*)p.blocks, y, ldy, err, seg);
+    note_launch();
+}
+
 template <int NC, bool TILED, bool PAIRS = false, int NW = 8>
 static void launch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p,
                        float* y, int64_t ldy, int* err, cudaStream_t s, const MvSeg& seg, const ArOut& ao = ArOut{})
 {
+    if constexpr (TILED && !PAIRS && NC >= 6) {
+        // six or more columns on tile-major weights: the persistent paired-tile form (same bits per row; measured on
+        // 8192 x 8192: 16.4 against 20.0 us at 8 columns, while at 3 and 4 columns, where the 16-row form fits two
+        // CTAs an SM and this one a single, 15.6 against 13.5 us)
+        if (ao.G == 0 && !seg.sel) {
+            launch_q4kp<NC, NW>(tiles, row_base, rows, nsb, p, y, ldy, err, s, seg);
+            return;
+        }
+    }
     if (TILED && !PAIRS && ao.G > 0) {
         // the fused all-reduce's producer: its own instantiation, so the one-GPU kernels keep their register allocation
         Q4Attr<NC, true, false, NW, true>::ensure();
@@ -1492,15 +1762,23 @@ void matvec_mma(int type, const WeightMap& map, int row_base, int rows, int cols
 }
 
 
-bool tiles_supported(int type, int cols) { return (type == 12 || type == 14) && cols % 256 == 0; }
+bool tiles_supported(int type, int cols)
+{
+    return ((type == 12 || type == 14) && cols % 256 == 0) || i8_tiles_supported(type, cols);
+}
 
 int64_t tile_bytes(int type, int rows, int cols)
 {
+    if (i8_tiles_supported(type, cols)) return i8_tile_bytes(type, rows, cols);
     return (int64_t)((rows + 15) / 16) * (cols / 256) * (type == 12 ? Q4_TILE : Q6_TILE);
 }
 
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s)
 {
+    if (i8_tiles_supported(type, cols)) {
+        make_i8_tiles(type, w, rows, cols, row_bytes, tiles, s);
+        return;
+    }
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "make_tiles: no tile layout for this type");
     if (row_bytes < (int64_t)(cols / 256) * (type == 12 ? 144 : 210)) WL_THROW(WL_EINVAL, "make_tiles: bad row size");
     if (rows <= 0) return;
@@ -1590,6 +1868,11 @@ void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int co
     if (ao && (type != 12 || P != 1 || ao->G < 1 || ao->G > AR_MAX_RANKS || ao->rank < 0 || ao->rank >= ao->G ||
                ao->E != rows || p.nc > AR_COLS || ao->idx < 0 || ao->idx >= AR_STEP))
         WL_THROW(WL_EINVAL, "matvec_tiles: the all-reduce push does not match");
+    if (i8_tiles_supported(type, cols)) {
+        const int64_t tb = i8_tile_bytes(type, 16, cols);
+        matvec_i8_tiles(type, tiles + (int64_t)(row_base / 16) * tb, rows, cols, p, y, ldy, err, s);
+        return;
+    }
     if (type == 12 && P == 1) {
         CUtensorMap none;
         memset(&none, 0, sizeof none);
