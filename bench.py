@@ -262,44 +262,61 @@ def sweep(args):
                     rows_out.append(sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args))
                     continue
 
-                def run(i):
+                def run(i, mode):
                     w = ws[i % copies]
                     cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-                    if b <= 8 and tiled:
+                    if mode == "gemm":     # the tcgen05 GEMM on the repacked weights
+                        st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
+                                             C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
+                    elif mode == "tiles":  # the integer tensor-core matvec, 8 columns a launch, on the repacked weights
                         st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
                                                C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
                     elif b <= 8:
                         st = L.wl_matvec(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
                                          C.c_void_p(y.data_ptr()), cs)
-                    elif tiled and f in ("q4_K", "q6_K"):   # the tcgen05 GEMM on the repacked weights
-                        st = L.wl_gemm_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
-                                             C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
-                    elif tiled:     # the integer tensor-core matvec, 8 columns a launch, on the repacked weights
-                        st = L.wl_matvec_tiles(t, C.c_void_p(tws[i % copies].data_ptr()), R, K,
-                                               C.c_void_p(x.data_ptr()), b, C.c_void_p(y.data_ptr()), cs)
                     else:
                         st = L.wl_matmul(t, C.c_void_p(w.data_ptr()), R, K, C.c_void_p(x.data_ptr()), b,
                                          C.c_void_p(y.data_ptr()), 0, cs)
                     _lib.check(st)
-                for i in range(max(args.warmup, 3)):
-                    run(i)
-                torch.cuda.synchronize()
-                # the calls are captured into one CUDA graph so that host launch overhead is not what gets timed
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
-                    for i in range(args.iters):
-                        run(i)
-                graph.replay()
-                torch.cuda.synchronize()
-                reps = 5
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                for _ in range(reps):
+
+                def timed(mode):
+                    for i in range(max(args.warmup, 3)):
+                        run(i, mode)
+                    torch.cuda.synchronize()
+                    # the calls are captured into one CUDA graph so that host launch overhead is not what gets timed
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        for i in range(args.iters):
+                            run(i, mode)
                     graph.replay()
-                e1.record(stream)
-                torch.cuda.synchronize()
-                ms = e0.elapsed_time(e1) / (reps * args.iters)
-                del graph
+                    torch.cuda.synchronize()
+                    reps = 5
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(reps):
+                        graph.replay()
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    del graph
+                    return e0.elapsed_time(e1) / (reps * args.iters)
+
+                paths = {}
+                if tiled and f in ("q4_K", "q6_K"):
+                    # both prompt paths; the library takes the GEMM from gemm_min_rows rows on (81 Q4_K, 57 Q6_K)
+                    paths["gemm"] = timed("gemm")
+                    paths["tiles"] = timed("tiles")
+                    lib_path = "gemm" if b >= {"q4_K": 81, "q6_K": 57}[f] else "tiles"
+                else:
+                    lib_path = "tiles" if tiled else "raw"
+                    paths[lib_path] = timed(lib_path)
+                ms = paths[lib_path]
+                cell = sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args)
+                cell["path"] = {"gemm": "tcgen05 GEMM", "tiles": "integer tensor-core matvec, 8 columns a launch",
+                                "raw": "wl_matvec / wl_matmul"}[lib_path]
+                for k_, v_ in paths.items():
+                    cell[k_ + "_us"] = v_ * 1e3
+                rows_out.append(cell)
+                continue
                 rows_out.append(sweep_cell(f, R, K, b, ms, nbytes, hbm, bf16, raw0, t, args))
             del ws
             if tiled:

@@ -200,23 +200,31 @@ def test_tile_matvec_columns_independent_of_batch(wl, oracle, tname, rows, cols)
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 9), (100, 512, 64), (300, 1024, 65), (16, 256, 130),
                                           (2048, 2048, 200)])
 def test_tcgen05_gemm_matches_reference(wl, oracle, tname, rows, cols, T):
-    """T > 8 rows of Q4_K or Q6_K run on the tcgen05 GEMM (bf16 hi/lo planes, fp32 accumulation in tensor memory):
+    """Rows of Q4_K or Q6_K on the tcgen05 GEMM (bf16 hi/lo planes, fp32 accumulation in tensor memory):
     within 1e-4 relative L2 of the decoded weights' float64 products, like the matvec, on ragged row counts (not
     multiples of the 128-row tile or of 16), token counts around the 128-token tile, and against the integer
     tensor-core matvec in 8-column chunks (path 2)."""
     O = oracle
     t = O.TYPE_OF[tname]
+    L = wl.lib()
     w = weights(O, tname, rows, cols, seed=rows + T)
     dec = O.decode(t, w, rows * cols).reshape(rows, cols).astype(np.float64)
     x = np.random.default_rng(T).standard_normal((T, cols)).astype(np.float32)
     dw, dx = dev(w), dev(x.reshape(-1))
-    dy, dy2 = empty(T * rows), empty(T * rows)
-    wl.check(wl.lib().wl_matmul(t, ptr(dw), rows, cols, ptr(dx), T, ptr(dy), 0, None))
-    wl.check(wl.lib().wl_matmul(t, ptr(dw), rows, cols, ptr(dx), T, ptr(dy2), 2, None))
-    y, y2 = host(dy).reshape(T, rows), host(dy2).reshape(T, rows)
+    nb = C.c_int64()
+    wl.check(L.wl_tiles_size(t, rows, cols, C.byref(nb)))
+    tiles = empty(nb.value, "uint8")
+    wl.check(L.wl_make_tiles(t, ptr(dw), rows, cols, ptr(tiles), None))
+    dy, dy2, dy3 = empty(T * rows), empty(T * rows), empty(T * rows)
+    wl.check(L.wl_gemm_tiles(t, ptr(tiles), rows, cols, ptr(dx), T, ptr(dy), None))
+    wl.check(L.wl_matmul(t, ptr(dw), rows, cols, ptr(dx), T, ptr(dy2), 2, None))
+    wl.check(L.wl_matmul(t, ptr(dw), rows, cols, ptr(dx), T, ptr(dy3), 0, None))
+    y, y2, y3 = (host(d).reshape(T, rows) for d in (dy, dy2, dy3))
     want = x.astype(np.float64) @ dec.T
     assert rel_l2(y, want) <= 1e-4, rel_l2(y, want)
     assert rel_l2(y, y2) <= 1e-4
+    # the library's own rule (GEMM from gemm_min_rows rows on, the 8-column matvec below) gives one of the two
+    assert np.array_equal(y3, y if T >= {"q4_K": 81, "q6_K": 57}[tname] else y2)
 
 
 def test_zz_no_kernel_level_wait_gave_up(wl):

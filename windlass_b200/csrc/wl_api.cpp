@@ -97,7 +97,7 @@ void run_matvec(int type, const uint8_t* w, int rows, int cols, const float* x, 
                 cudaStream_t s, bool allow_gemm = true)
 {
     const int64_t rb = wl::row_bytes_of(type, cols);
-    if (!force_cuda_cores && allow_gemm && ncols > 8 && wl::k::gemm_supported(type, cols)) {
+    if (!force_cuda_cores && allow_gemm && ncols >= wl::k::gemm_min_rows(type) && wl::k::gemm_supported(type, cols)) {
         // scratch: [error word | the activations' bf16 planes | the weights repacked into tiles]
         const size_t xb = (wl::k::gemm_scratch_bytes(ncols, cols) + 255) / 256 * 256;
         uint8_t* scratch = (uint8_t*)export_scratch(256 + xb + (size_t)wl::k::tile_bytes(type, rows, cols));

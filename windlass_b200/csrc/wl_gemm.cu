@@ -467,6 +467,8 @@ CUtensorMap plane_map(const void* base, int T, int K)
 
 bool gemm_supported(int type, int cols) { return (type == 12 || type == 14) && cols % 256 == 0; }
 
+int gemm_min_rows(int type) { return type == 14 ? 57 : 81; }
+
 size_t gemm_scratch_bytes(int T, int cols) { return (size_t)2 * T * cols * 2 + 256; }
 
 void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const float* x, int64_t ldx, int T,

@@ -189,6 +189,10 @@ void count_experts(const int32_t* sel, int n, unsigned long long* count, cudaStr
 // operands, three MMAs per slice, fp32 accumulation in tensor memory). scratch holds gemm_scratch_bytes(T, cols) bytes
 // (the activations' bf16 planes); a stuck wait sets *err.
 bool gemm_supported(int type, int cols);
+// Fewer rows than this go through the integer tensor-core matvec in 8-column launches instead: the GEMM's time hardly
+// depends on T up to its 128-token tile (8192 x 8192 Q4_K: about 200 us at 16 or 64 tokens), against about 19 us a
+// chunk of eight for the matvec (measured on B200: crossing near 88 rows for Q4_K, 60 for Q6_K).
+int gemm_min_rows(int type);
 size_t gemm_scratch_bytes(int T, int cols);
 void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const float* x, int64_t ldx, int T,
                 float* y, int64_t ldy, void* scratch, int* err, cudaStream_t s);
