@@ -948,8 +948,8 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
     // path 1 (or prefill_path 1 for prompts): the fp32 CUDA-core kernel
     const bool cuda_cores = path == 1 || (T > 8 && prefill_path_ == 1);
     // more than 8 rows of Q4_K: the tcgen05 GEMM (prefill_path 2 keeps the integer matvec in 8-column chunks)
-    if (!cuda_cores && T > 8 && prefill_path_ != 2 && !each_token_ && w.tiles && w.row_base % 16 == 0 &&
-        k::gemm_supported(w.type, w.cols)) {
+    if (!cuda_cores && T >= k::gemm_min_rows(w.type) && prefill_path_ != 2 && !each_token_ && w.tiles &&
+        w.row_base % 16 == 0 && k::gemm_supported(w.type, w.cols)) {
         const size_t need = k::gemm_scratch_bytes(T, w.cols);
         if (need > gemm_buf_bytes_) {
             WL_CUDA(cudaStreamSynchronize(stream_));
