@@ -349,10 +349,24 @@ def streamed(args):
         best = min(best, e0.elapsed_time(e1))
     h2d_gbs = (1 << 30) / (best / 1e3) / 1e9
     del src, dst
-    spec = llama70b_spec(layers=args.layers or 80)
+    from windlass_b200.transformer import llama8b_spec
+    spec = llama8b_spec() if args.model == "8b" else llama70b_spec(layers=args.layers or 80)
+    path = None
+    if args.stream_file:
+        # the model as a GGUF file (written here from the synthetic generator), every stage read from it at each use
+        import tempfile
+        from windlass_b200 import gguf_writer
+        tmpdir = tempfile.mkdtemp(prefix="wl_stream_")
+        path = os.path.join(tmpdir, "model.gguf")
+        t0 = time.perf_counter()
+        file_bytes = gguf_writer.write(path, spec)
+        trace(f"wrote {file_bytes / 1e9:.2f} GB to {path} in {time.perf_counter() - t0:.1f} s")
     t0 = time.perf_counter()
-    trace(f"opening the streamed model ({args.layers} layers)")
-    m = CudaTransformer(synthetic=spec, max_context=args.prompt + 64, resident=0)
+    trace(f"opening the streamed model ({spec.layers} layers)")
+    if path:
+        m = CudaTransformer(path, max_context=args.prompt + 64, resident=0, stream_file=1)
+    else:
+        m = CudaTransformer(synthetic=spec, max_context=args.prompt + 64, resident=0)
     load_s = time.perf_counter() - t0
     s = m.new_sequence()
     rng = np.random.default_rng(0)
@@ -365,16 +379,24 @@ def streamed(args):
     ms = m.bench_decode([s], args.steps)
     moved = m.bytes_read - b0
     achieved = moved / (ms / 1e3) / 1e9
-    print(json.dumps({"metric": "decode tok/s @70B-shape Q4_K_M b1, layers streamed from pinned host memory "
-                                "(configs[3] a)", "value": args.steps / (ms / 1e3), "unit": "tok/s",
+    shape = "8B" if args.model == "8b" else "70B"
+    source = "read from the GGUF file at every use (stream_file)" if path else "streamed from pinned host memory"
+    print(json.dumps({"metric": f"decode tok/s @{shape}-shape Q4_K_M b1, layers {source}"
+                                + ("" if args.model == "8b" else " (configs[3] a)"),
+                      "value": args.steps / (ms / 1e3), "unit": "tok/s",
                       "ms_per_step": ms / args.steps, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
                       "h2d_bytes_per_step": moved / args.steps,
-                      "roofline": {"bound": "pcie", "achieved": achieved, "peak": h2d_gbs, "unit": "GB/s",
-                                   "frac": achieved / h2d_gbs,
+                      "roofline": {"bound": "storage" if path else "pcie", "achieved": achieved,
+                                   "peak": None if path else h2d_gbs, "unit": "GB/s",
+                                   "frac": None if path else achieved / h2d_gbs,
+                                   "h2d_copy_gbs": h2d_gbs,
                                    "peak_source": "measured in this run: 1 GiB pinned host to device copy"},
                       "prefill_tok_s": args.prompt / prefill_s, "load_s": load_s}))
     s.close()
     m.close()
+    if path:
+        os.remove(path)
+        os.rmdir(os.path.dirname(path))
 
 
 def trace(msg):
@@ -403,6 +425,8 @@ def main():
     ap.add_argument("--shapes", default="", help="sweep shapes rows x cols, comma-separated (default: n x n)")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--streamed", action="store_true", help="configs[3] (a): layers streamed from pinned host memory")
+    ap.add_argument("--stream-file", action="store_true",
+                    help="with --streamed: write the model as a GGUF file and read every stage from it at each use")
     ap.add_argument("--model", default="70b", choices=["70b", "8b", "moe"],
                     help="70b: configs[3] (the headline); 8b: configs[2]; moe: configs[4] (Qwen3-MoE shape)")
     ap.add_argument("--shard-of", type=int, default=0,

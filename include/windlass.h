@@ -87,7 +87,12 @@ typedef struct wl_options {
     int32_t tp_nccl_only;    /* 0: decode-step all-reduces fused into the producing matvec and the consuming norm over
                                 NVLink peer memory (CUDA IPC), falling back to NCCL when the GPUs cannot map each
                                 other's memory; 1: NCCL all-reduce only */
-    int32_t reserved[6];
+    int32_t stream_file;     /* with resident = 0 and a model opened from a GGUF file (one GPU): 1 reads each stage
+                                from the file at every use (LayerStream.Acquire's reads, src/LayerStream.cs:182-232):
+                                8 MB chunks through a ring of four pinned buffers, O_DIRECT where the file system
+                                allows it, on a reader thread that overlaps the reads with the copies, so the host
+                                holds no copy of the model; 0 lays every stage out once in pinned host memory */
+    int32_t reserved[5];
     uint8_t tp_id[128];      /* the group's id: wl_tp_unique_id on one rank, the same bytes passed to every rank */
 } wl_options;
 

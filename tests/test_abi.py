@@ -108,3 +108,18 @@ def test_streamed_layers_refuse_the_cuda_core_prefill(wl):
     spec = config0_spec()
     st = wl.lib().wl_open_synthetic(C.byref(spec), C.byref(o), C.byref(h))
     assert st == wl.WL_EUNSUPPORTED and b"prefill_path 1" in wl.lib().wl_last_error()
+
+
+def test_stream_file_needs_a_streamed_file_model(wl, oracle, tmp_path):
+    """stream_file = 1 reads the layers from the model's GGUF file: refused with resident weights, for a synthetic model
+    (no file) and for a value other than 0 or 1, before any device work."""
+    from windlass_b200.transformer import config0_spec
+    h = C.c_void_p()
+    spec = config0_spec()
+    st = wl.lib().wl_open_synthetic(C.byref(spec), C.byref(wl.options(resident=0, stream_file=1)), C.byref(h))
+    assert st == wl.WL_EINVAL and b"synthetic model" in wl.lib().wl_last_error()
+    path = oracle.write_synth(str(tmp_path / "c0.gguf"), spec)
+    st = wl.lib().wl_open(path.encode(), C.byref(wl.options(resident=1, stream_file=1)), C.byref(h))
+    assert st == wl.WL_EINVAL and b"resident = 0" in wl.lib().wl_last_error()
+    st = wl.lib().wl_open(path.encode(), C.byref(wl.options(resident=0, stream_file=2)), C.byref(h))
+    assert st == wl.WL_EINVAL and b"0 or 1" in wl.lib().wl_last_error()

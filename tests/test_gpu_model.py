@@ -211,26 +211,28 @@ def test_graph_replays_equal_eager_steps(wl):
             assert np.array_equal(bg, be), f"graph batch step {step} differs from the eager step"
 
 
-@pytest.mark.parametrize("case", ["config0", "gqa-file", "moe"])
+@pytest.mark.parametrize("case", ["config0", "gqa-file", "gqa-read-file", "moe-read-file", "moe"])
 def test_streamed_layers_match_resident(wl, oracle, tmp_path, case):
-    """StreamingIsExact (tests/Tests.cs:305-321): weights streamed from pinned host memory through two device slots
-    (wl_options.resident = 0, LayerStream) give bit-identical logits to resident weights for prompts, decode steps
-    and ForwardBatch, and every pass copies at least every layer's bytes."""
+    """StreamingIsExact (tests/Tests.cs:305-321): weights streamed through two device slots (wl_options.resident = 0,
+    LayerStream), from pinned host memory or read from the GGUF file at every use (stream_file = 1, the
+    "read-file" cases), give bit-identical logits to resident weights for prompts, decode steps and ForwardBatch, and
+    every pass copies at least every layer's bytes."""
     from windlass_b200.transformer import synth_spec
+    read_file = case.endswith("read-file")
     if case == "config0":
         spec, src = config0_spec(), None
-    elif case == "gqa-file":
+    elif case.startswith("gqa"):
         spec = synth_spec("llama", 3, 2048, 32, 8, 64, 4096, 8192, rope_base=500000.0, type_attn_v=14, type_embd=12,
                           seed=5)
         src = oracle.write_synth(str(tmp_path / "gqa.gguf"), spec)
     else:
         spec = synth_spec("qwen3moe", 2, 512, 8, 4, 64, 0, 4096, experts=8, experts_used=2, expert_ff=256,
                           rope_base=1000000.0, type_attn_v=14, type_embd=12, seed=3)
-        src = None
+        src = oracle.write_synth(str(tmp_path / "moe.gguf"), spec) if read_file else None
 
     def open_model(resident):
         if src:
-            return CudaTransformer(src, max_context=128, resident=resident)
+            return CudaTransformer(src, max_context=128, resident=resident, stream_file=int(read_file and resident == 0))
         return CudaTransformer(synthetic=spec, max_context=128, resident=resident)
 
     prompt = np.random.default_rng(2).integers(0, spec.vocab, 24).astype(np.int32)

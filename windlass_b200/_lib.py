@@ -48,7 +48,7 @@ class Options(C.Structure):
     _fields_ = [("size", C.c_int32), ("device", C.c_int32), ("max_context", C.c_int32), ("max_batch", C.c_int32),
                 ("resident", C.c_int32), ("prefill_path", C.c_int32), ("use_graphs", C.c_int32),
                 ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("tp_nccl_only", C.c_int32),
-                ("reserved", C.c_int32 * 6),
+                ("stream_file", C.c_int32), ("reserved", C.c_int32 * 5),
                 ("tp_id", C.c_uint8 * 128)]
 
 

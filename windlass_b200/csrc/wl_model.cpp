@@ -42,9 +42,16 @@ template <typename T> void hfree(T*& p)
 // ---------------------------------------------------------------------------------------------------------------------
 // open / close
 // ---------------------------------------------------------------------------------------------------------------------
+static int tp_size_of(const wl_options& opt);
+
 void Model::init_device(const wl_options& opt)
 {
     streamed_ = opt.resident == 0;
+    stream_file_ = streamed_ && opt.stream_file == 1;
+    if (opt.stream_file != 0 && opt.stream_file != 1) WL_THROW(WL_EINVAL, "stream_file must be 0 or 1.");
+    if (opt.stream_file == 1 && !streamed_) WL_THROW(WL_EINVAL, "stream_file needs resident = 0 (streamed layers).");
+    if (stream_file_ && tp_size_of(opt) > 1)
+        WL_THROW(WL_EUNSUPPORTED, "stream_file streams one GPU's layers; tensor parallelism keeps its shards resident or in pinned memory.");
     if (streamed_ && opt.prefill_path == 1)
         WL_THROW(WL_EUNSUPPORTED, "Streamed layers carry the tensor-core layout only; prefill_path 1 (CUDA cores) needs resident weights.");
     device_ = opt.device;
@@ -467,6 +474,7 @@ void Model::load_from_gguf(const Gguf& g)
         if (G == 1 || sp == WHOLE) {
             w.d = weight_alloc(w.bytes);
             WL_CUDA(cudaMemcpy(w.d, src, (size_t)w.bytes, cudaMemcpyHostToDevice));
+            if (stream_file_ && cur_stage_ >= 0) file_src_.push_back({(int64_t)(w.d - staging_), {t->offset, t->size}});
         } else if (sp == EXPERTS) {
             if (w.experts != c_.expert_count || w.experts % G)
                 WL_THROW(WL_EUNSUPPORTED, t->name + ": its experts do not split over " + std::to_string(G) + " GPUs.");
@@ -607,6 +615,7 @@ Model* Model::open_file(const std::string& path, const wl_options& opt)
     check_tp(c, opt);
     std::unique_ptr<Model> m(new Model());
     m->c_ = c;
+    m->file_path_ = path;
     m->init_device(opt);
     m->max_context_ = opt.max_context > 0 ? opt.max_context : std::min(m->c_.context_length, 8192);
     m->init_tp(opt);
@@ -622,6 +631,7 @@ enum Slot { S_ATTN_NORM = 1, S_Q, S_K, S_V, S_O, S_FFN_NORM, S_GATE, S_UP, S_DOW
 
 Model* Model::open_synthetic(const wl_synth_spec& sp, const wl_options& opt)
 {
+    if (opt.stream_file != 0) WL_THROW(WL_EINVAL, "stream_file reads the layers from a GGUF file; a synthetic model has none.");
     std::unique_ptr<Model> m(new Model());
     Config& c = m->c_;
     c.arch = std::string(sp.arch, strnlen(sp.arch, sizeof sp.arch));

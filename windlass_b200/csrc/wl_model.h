@@ -255,12 +255,30 @@ private:
         int64_t off;
         bool tiled;
     };
+    // file-backed streaming: a stage's tensor as the reader fetches it (its GGUF bytes at file_off; tiled ones land
+    // in the staging area at raw_off and are repacked into the slot, the rest go to the slot directly)
+    struct FileItem {
+        int64_t file_off, bytes, raw_off, slot_off;
+        Weight* w;
+        bool tiled;
+        int rows_total;
+    };
     struct Stage {
         std::vector<StageWeight> ws;
+        std::vector<FileItem> file;
         uint8_t* host = nullptr;
         int64_t bytes = 0;
     };
     bool streamed_ = false;
+    bool stream_file_ = false;            // stages read from the GGUF file at every use (wl_options.stream_file)
+    std::string file_path_;
+    // the tensors uploaded into the staging area while the current stage loads: staging offset -> (file offset, bytes)
+    std::vector<std::pair<int64_t, std::pair<int64_t, int64_t>>> file_src_;
+    struct FileReader;
+    FileReader* reader_ = nullptr;
+    void reader_loop();
+    void reader_fetch(int l);
+    void reader_wait(int l);
     bool opened_ = false;                 // open completed: closing meets the other ranks in collectives
     std::vector<Stage> stages_;
     int cur_stage_ = -1;                  // the stage being loaded (-1: resident weights)

@@ -71,13 +71,14 @@ class Sequence:
 
 class CudaTransformer:
     def __init__(self, path=None, synthetic=None, device=0, max_context=0, max_batch=64, prefill_path=0, resident=-1,
-                 use_graphs=1, tp_size=1, tp_rank=0, tp_id=None, tp_nccl_only=0):
+                 use_graphs=1, tp_size=1, tp_rank=0, tp_id=None, tp_nccl_only=0, stream_file=0):
         """tp_size > 1: this process is rank tp_rank of a tensor-parallel group whose ranks all open the same model
         with the same tp_id (windlass_b200.tp) and then make the same calls; each call returns the full logits.
-        tp_nccl_only=1 keeps every all-reduce on NCCL instead of the fused peer-memory path."""
+        tp_nccl_only=1 keeps every all-reduce on NCCL instead of the fused peer-memory path. resident=0 streams the
+        layers; with stream_file=1 (a GGUF path, one GPU) each stage is read from the file at every use."""
         opt = _lib.options(device=device, max_context=max_context, max_batch=max_batch, prefill_path=prefill_path,
                            resident=resident, use_graphs=use_graphs, tp_size=tp_size, tp_rank=tp_rank, tp_id=tp_id,
-                           tp_nccl_only=tp_nccl_only)
+                           tp_nccl_only=tp_nccl_only, stream_file=stream_file)
         h = C.c_void_p()
         if synthetic is not None:
             check(lib().wl_open_synthetic(C.byref(synthetic), C.byref(opt), C.byref(h)))
