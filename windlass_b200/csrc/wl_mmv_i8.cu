@@ -12,8 +12,9 @@
 //   IQ4_XS   (src/IQuants.cs:61-80)    4-bit codes looked up in the IQ4_NL table with byte permutes; the 6-bit
 //                                      sub-block scale ls - 32 is applied in integers, d in fp32 per superblock;
 //   IQ2_XXS  (src/IQuants.cs:148-170)  each 8-value group is a grid row (8 magnitudes) with 7 sign bits and a parity
-//                                      bit; the 4-bit scale s enters as the integer 2s + 1, d / 8 in fp32, since
-//                                      d * (0.5 + s) * 0.25 = d * (2s + 1) / 8.
+//                                      bit, read as two words of a table of every grid half-row under every four
+//                                      signs (32 KB, in shared memory); the 4-bit scale s enters as the integer
+//                                      2s + 1, d / 8 in fp32, since d * (0.5 + s) * 0.25 = d * (2s + 1) / 8.
 // One or two columns pack (column, digit) pairs into the MMA's 8 columns; from three columns on each digit plane is
 // its own MMA over the columns. Either way every (column, digit) goes through the same fp32 operations, and the
 // planes are added ((0 + 1) + 2) and the warps in warp order, so a column's result does not depend on the other
@@ -32,7 +33,9 @@
 namespace wl {
 namespace k {
 
-__device__ uint64_t g_i8_iq2xxs_grid[256];
+// IQ2_XXS grid rows with their signs applied, per half: [grid index][4 sign bits] -> the four signed values of bytes
+// 0..3 (lo) or 4..7 (hi) of the grid row, so a lane's decode of an 8-value group is two table reads
+__device__ uint32_t g_i8_iq2_lo[256 * 16], g_i8_iq2_hi[256 * 16];
 
 namespace {
 
@@ -98,13 +101,6 @@ __device__ __forceinline__ uint32_t iq4_lookup(uint32_t w, uint32_t w4, const Iq
     return (r1 & r2) ^ m;
 }
 
-// Four signed values from four magnitudes (bytes of g) and four sign bits s (bit j negates byte j).
-__device__ __forceinline__ uint32_t apply_signs(uint32_t g, uint32_t s)
-{
-    const uint32_t m = ((s * 0x00204081u) & 0x01010101u) * 0xFFu;   // bytes 0xFF where the sign bit is set
-    return (g ^ m) + (m & 0x01010101u);                             // two's complement of those bytes (no carries)
-}
-
 template <int T, int NC, int NW>
 __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_i8(const uint8_t* __restrict__ wt, int rows,
                                                                            int nsb, const uint8_t* xq, float* y,
@@ -116,7 +112,7 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_i8(con
     constexpr int ND = PACK ? 1 : 3;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[NW][LY::STAGES];
-    __shared__ uint64_t grid_s[T == 16 ? 256 : 1];
+    __shared__ __align__(16) uint32_t sgn_lo[T == 16 ? 4096 : 4], sgn_hi[T == 16 ? 4096 : 4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int r0 = blockIdx.x * I8_ROWS;
     uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
@@ -124,7 +120,10 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_i8(con
 
     pdl_trigger();
     if (T == 16)
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) grid_s[i] = g_i8_iq2xxs_grid[i];
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+            reinterpret_cast<uint4*>(sgn_lo)[i] = reinterpret_cast<const uint4*>(g_i8_iq2_lo)[i];
+            reinterpret_cast<uint4*>(sgn_hi)[i] = reinterpret_cast<const uint4*>(g_i8_iq2_hi)[i];
+        }
     if (lane == 0) {
         for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
         fence_mbar_init();
@@ -147,7 +146,7 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_i8(con
     pdl_wait();
     if (lane == 0)
         for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
-    if (T == 16) __syncthreads();           // the grid table is in place
+    if (T == 16) __syncthreads();           // the signed grid tables are in place
 
     const bool b_ok = PACK ? g < 3 * NC : g < NC;
     const int b_off = LY::X_OFF + (PACK ? (g / 3) * XP_COL + (g % 3) * XP_DIGIT : g * XP_COL);
@@ -239,11 +238,11 @@ __global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_i8(con
 #pragma unroll
                         for (int rr = 0; rr < 2; ++rr) {
                             const uint2 q = rr ? q1 : q0;
-                            const uint64_t gv = grid_s[(q.x >> (8 * c)) & 0xFFu];
+                            const uint32_t gi = ((q.x >> (8 * c)) & 0xFFu) << 4;
                             const uint32_t s7 = (q.y >> (7 * c)) & 127u;
-                            const uint32_t sg = s7 | ((__popc(s7) & 1u) << 7);
-                            a[rr][0] = apply_signs((uint32_t)gv, sg & 0xFu);
-                            a[rr][1] = apply_signs((uint32_t)(gv >> 32), sg >> 4);
+                            const uint32_t sg = s7 | ((__popc(s7) & 1u) << 7);    // the eighth bit: even parity
+                            a[rr][0] = sgn_lo[gi | (sg & 0xFu)];
+                            a[rr][1] = sgn_hi[gi | (sg >> 4)];
                             sc[rr] = 2 * (int)(q.y >> 28) + 1;
                         }
 #pragma unroll
@@ -441,7 +440,21 @@ int64_t i8_tile_bytes(int type, int rows, int cols)
 
 void init_i8_tables()
 {
-    WL_CUDA(cudaMemcpyToSymbol(g_i8_iq2xxs_grid, WL_IQ2XXS_GRID, sizeof(WL_IQ2XXS_GRID)));
+    // the IQ2_XXS grid rows with every combination of four signs applied, per half of the row
+    static uint32_t lo[256 * 16], hi[256 * 16];
+    for (int gi = 0; gi < 256; ++gi)
+        for (int sg = 0; sg < 16; ++sg) {
+            uint32_t l = 0, h = 0;
+            for (int b = 0; b < 4; ++b) {
+                const int ml = (int)((WL_IQ2XXS_GRID[gi] >> (8 * b)) & 0xFF), mh = (int)((WL_IQ2XXS_GRID[gi] >> (8 * (b + 4))) & 0xFF);
+                l |= (uint32_t)(uint8_t)(int8_t)((sg >> b) & 1 ? -ml : ml) << (8 * b);
+                h |= (uint32_t)(uint8_t)(int8_t)((sg >> b) & 1 ? -mh : mh) << (8 * b);
+            }
+            lo[gi * 16 + sg] = l;
+            hi[gi * 16 + sg] = h;
+        }
+    WL_CUDA(cudaMemcpyToSymbol(g_i8_iq2_lo, lo, sizeof lo));
+    WL_CUDA(cudaMemcpyToSymbol(g_i8_iq2_hi, hi, sizeof hi));
 }
 
 void make_i8_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s)
