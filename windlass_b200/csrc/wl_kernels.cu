@@ -1010,14 +1010,33 @@ __global__ void __launch_bounds__(NT, 1) k_attn_part(const float* q, int heads, 
             if (lane == 0) tsum[h] = sum;
         }
         // o = o * e^(m_old - m_new) + sum_j p_j v_j per (dim, head) item, positions in order, from the staged values
+        if constexpr (NT % HD == 0) {
+            // a thread's items share their dimension (one V element a position, converted once for all its heads);
+            // the items' sums advance together, each still adding the positions in order
+            const int d = tid % HD;
+            float acc[IPT];
 #pragma unroll
-        for (int k2 = 0; k2 < IPT; ++k2) {
-            if (oh[k2] < 0) continue;
-            const int d = od[k2], h = oh[k2];
-            float acc = __fmul_rn(o[k2], alpha[h]);
+            for (int k2 = 0; k2 < IPT; ++k2) acc[k2] = oh[k2] >= 0 ? __fmul_rn(o[k2], alpha[oh[k2]]) : 0.f;
+#pragma unroll 2
+            for (int j = 0; j < cnt; ++j) {
+                const float vj = h2f(vs[j * KP + d]);
+#pragma unroll
+                for (int k2 = 0; k2 < IPT; ++k2)
+                    if (oh[k2] >= 0) acc[k2] = __fadd_rn(acc[k2], __fmul_rn(sc[oh[k2]][j], vj));
+            }
+#pragma unroll
+            for (int k2 = 0; k2 < IPT; ++k2)
+                if (oh[k2] >= 0) o[k2] = acc[k2];
+        } else {
+#pragma unroll
+            for (int k2 = 0; k2 < IPT; ++k2) {
+                if (oh[k2] < 0) continue;
+                const int d = od[k2], h = oh[k2];
+                float acc = __fmul_rn(o[k2], alpha[h]);
 #pragma unroll 4
-            for (int j = 0; j < cnt; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[h][j], h2f(vs[j * KP + d])));
-            o[k2] = acc;
+                for (int j = 0; j < cnt; ++j) acc = __fadd_rn(acc, __fmul_rn(sc[h][j], h2f(vs[j * KP + d])));
+                o[k2] = acc;
+            }
         }
         __syncthreads();
         if (tid < G) {
@@ -1180,11 +1199,12 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
     float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
     int* tickets = reinterpret_cast<int*>(part + (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (HD + 2));
     // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks. Wide CTAs
-    // (attn_threads) when the grid leaves most SMs with one CTA (a decode step of one or two rows); otherwise 128
-    // threads, several CTAs per SM. Both give the same bits: every score and every (dim, head) sum is one thread's.
+    // (attn_threads) for decode steps (up to 8 rows: a wide CTA's threads carry a quarter of the dependent sums of a
+    // 128-thread one, and an SM holds twice the warps) and small grids; otherwise 128 threads, several CTAs per SM.
+    // Both give the same bits: every score and every (dim, head) sum is one thread's.
     constexpr bool can_merge = (G * HD) % 256 == 0;
     constexpr int WIDE = attn_threads(HD, G);
-    const bool wide = (int64_t)S * kv_heads * T <= 2 * 148;
+    const bool wide = T <= 8 || (int64_t)S * kv_heads * T <= 2 * 148;
     const dim3 grid(S, kv_heads, T);
     uint8_t* pb = prep ? prep->blocks : (uint8_t*)nullptr;
     if (S > 1 && can_merge) {
