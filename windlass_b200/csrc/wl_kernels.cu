@@ -830,7 +830,7 @@ void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStr
 // 0..pos[t] of row t are cut into S equal ranges by the row's own length, so a row's result does not depend on the
 // other rows; each range keeps a running max m, sum l and unnormalised output o per head across its tiles. With
 // S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order.
-constexpr int ATT_P = 64;           // positions per tile
+constexpr int ATT_P = 128;          // positions per tile (a range of a decode row up to 2048 positions is one tile)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
 {
@@ -888,7 +888,7 @@ __device__ __noinline__ void attn_merge4(const float* __restrict__ part, const f
 // group's G * HD values are whole superblocks), then resets the counter for the next launch, so no combine launch is
 // needed.
 // Threads of an attention CTA: half a thread per (head, dim) of the group, 128 to 512, a multiple of 64, so that the
-// 64 positions of a tile times the G heads spread over every thread in the score phase and the G * HD outputs over
+// positions of a tile times the G heads spread over every thread in the score phase and the G * HD outputs over
 // every thread in the value phase (at decode a CTA is alone on its SM, and more warps hide more latency).
 constexpr int attn_threads(int HD, int G)
 {
@@ -987,7 +987,9 @@ __global__ void __launch_bounds__(NT, 1) k_attn_part(const float* q, int heads, 
         }
         __syncthreads();
         for (int h = warp; h < G; h += NT / 32) {
-            float m = fmaxf(sc[h][lane], sc[h][lane + 32]);
+            float m = sc[h][lane];
+#pragma unroll
+            for (int i = 1; i < ATT_P / 32; ++i) m = fmaxf(m, sc[h][lane + 32 * i]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
             if (lane == 0) {
@@ -1004,7 +1006,9 @@ __global__ void __launch_bounds__(NT, 1) k_attn_part(const float* q, int heads, 
         }
         __syncthreads();
         for (int h = warp; h < G; h += NT / 32) {
-            double sum = (double)sc[h][lane] + (double)sc[h][lane + 32];
+            double sum = (double)sc[h][lane];
+#pragma unroll
+            for (int i = 1; i < ATT_P / 32; ++i) sum += (double)sc[h][lane + 32 * i];
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
             if (lane == 0) tsum[h] = sum;
