@@ -308,8 +308,8 @@ int32_t wl_matvec(int32_t type, const void* dev_w, int32_t rows, int32_t cols, c
 #define WL_MATVEC_STATIC_MAX_COLS 32768
 int32_t wl_matvec_static(int32_t type, const void* dev_w, int32_t rows, int32_t cols, const float* dev_x,
                          int32_t ncols, float* dev_y, void* stream);
-/* No counterpart in the reference: the tile-major weight layout the tensor-core matvec reads (Q4_K and Q6_K, cols a
- * multiple of 256; every 16 rows x one superblock contiguous). The model repacks its weights this way once at load;
+/* No counterpart in the reference: the tile-major weight layout the tensor-core matvec reads (Q4_K, Q6_K, Q8_0,
+ * IQ4_XS and IQ2_XXS, cols a multiple of 256; every 16 rows x one 256-value superblock contiguous). The model repacks its weights this way once at load;
  * these let a caller do the same and then run matvecs without a per-call repack. wl_tiles_size gives the bytes
  * (rows rounded up to 16), wl_make_tiles fills dev_tiles (16-byte aligned) from GGUF rows, wl_matvec_tiles is
  * wl_matvec on the tiles (dev_x 16-byte aligned). Other formats return WL_EUNSUPPORTED. */
