@@ -198,7 +198,7 @@ def test_tile_matvec_columns_independent_of_batch(wl, oracle, tname, rows, cols)
 
 @pytest.mark.parametrize("tname", ["q4_K", "q6_K"])
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 9), (100, 512, 64), (300, 1024, 65), (16, 256, 130),
-                                          (2048, 2048, 200)])
+                                          (2048, 2048, 200), (300, 1024, 600)])
 def test_tcgen05_gemm_matches_reference(wl, oracle, tname, rows, cols, T):
     """Rows of Q4_K or Q6_K on the tcgen05 GEMM (bf16 hi/lo planes, fp32 accumulation in tensor memory):
     within 1e-4 relative L2 of the decoded weights' float64 products, like the matvec, on ragged row counts (not

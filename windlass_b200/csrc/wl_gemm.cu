@@ -1,8 +1,10 @@
 // Prefill / batched GEMM for Q4_K weights on the 5th-generation tensor cores (tcgen05, sm_100a):
 // y[t*ldy + r] = W[r] . x[t] for T > 8 activation rows (FastMath.Block's job in the reference, src/FastMath.cs:218-264).
 //
-// One CTA computes a 128-row x 128-token tile of y; its fp32 accumulator lives in tensor memory (128 TMEM columns).
-// Per K step of 64 values, in a 3-stage shared-memory ring (64 KB a stage) fed by a 4-stage ring of raw weights:
+// One CTA computes a 128-row x BN-token tile of y (BN = 128, or 256 for Q4_K prompts of more than 128 rows, so that
+// each weight is dequantized once per 256 tokens); its fp32 accumulator lives in tensor memory (BN TMEM columns).
+// Per K step of 64 values, in a shared-memory ring (3 stages of 64 KB at BN = 128, 2 of 96 KB at 256) fed by a
+// 4-stage ring of raw weights:
 //   - one warp copies the step's raw Q4_K bytes of the CTA's eight 16-row tiles (each tile's 256 header bytes and the
 //     512 code bytes of the step's 64 values) into the raw ring with 1-D bulk copies, ahead of their use;
 //   - 8 dequantizing warps read those bytes from shared memory (two threads per row, one 32-value sub-block each),
@@ -33,32 +35,32 @@ namespace k {
 namespace {
 
 constexpr int G_BM = 128;                  // weight rows per CTA (MMA M)
-constexpr int G_BN = 128;                  // tokens per CTA (MMA N)
 constexpr int G_BK = 64;                   // values per K step: one 128-byte swizzle atom of bf16
 constexpr int G_A_BYTES = G_BM * G_BK * 2;             // one bf16 plane of the weight tile: 16 KB
-constexpr int G_B_BYTES = G_BN * G_BK * 2;             // one bf16 plane of the token tile: 16 KB
-constexpr int G_STAGE = 2 * G_A_BYTES + 2 * G_B_BYTES; // 64 KB
+template <int BN> constexpr int g_b_bytes() { return BN * G_BK * 2; }                 // one bf16 plane: 16 or 32 KB
+template <int BN> constexpr int g_stage() { return 2 * G_A_BYTES + 2 * g_b_bytes<BN>(); } // 64 or 96 KB
 constexpr int G_DQ_WARPS = 8, G_TMA_WARP = 8, G_RAW_WARP = 9, G_MMA_WARP = 10, G_THREADS = 352;
-constexpr int G_TMEM_COLS = 128;
 constexpr int Q4T = 2304;                               // bytes of a 16-row x one-superblock Q4_K tile
 constexpr int Q6T = 3360;                               // bytes of a 16-row x one-superblock Q6_K tile
 
 // Per weight format: the A/B ring depth and the raw ring. Q4_K stages one K step of each 16-row tile at a time (its
 // 256 header bytes and the step's 512 code bytes); Q6_K stages whole tiles (one superblock = four K steps), its
 // quarter-superblock bytes being interleaved across the tile for the matvec's fragment reads.
-template <int WT> struct GemmFmt;
-template <> struct GemmFmt<12> {
-    static constexpr int STAGES = 3, RAW_STAGES = 4, STEPS_PER_RAW = 1;
+template <int WT, int BN> struct GemmFmt;
+template <int BN> struct GemmFmt<12, BN> {
+    static constexpr int STAGES = BN == 128 ? 3 : 2, RAW_STAGES = 4, STEPS_PER_RAW = 1;
     static constexpr int RAW_TILE = 256 + 512, TILE = Q4T;
     static constexpr int RAW_STAGE = (G_BM / 16) * RAW_TILE;                          // 6 KB
-    static constexpr int SMEM = STAGES * G_STAGE + RAW_STAGES * RAW_STAGE + 1024;     // + 1024-byte alignment slack
+    static constexpr int SMEM = STAGES * g_stage<BN>() + RAW_STAGES * RAW_STAGE + 1024; // + 1024-byte alignment slack
 };
-template <> struct GemmFmt<14> {
+template <int BN> struct GemmFmt<14, BN> {
+    static_assert(BN == 128, "Q6_K's whole-tile raw ring leaves room for 128-token stages only");
     static constexpr int STAGES = 2, RAW_STAGES = 2, STEPS_PER_RAW = 4;
     static constexpr int RAW_TILE = Q6T, TILE = Q6T;
     static constexpr int RAW_STAGE = (G_BM / 16) * RAW_TILE;                          // 26.25 KB
-    static constexpr int SMEM = STAGES * G_STAGE + RAW_STAGES * RAW_STAGE + 1024;
+    static constexpr int SMEM = STAGES * g_stage<BN>() + RAW_STAGES * RAW_STAGE + 1024;
 };
+static_assert(GemmFmt<12, 256>::SMEM <= 227 * 1024, "Q4_K 256-token stages must fit one CTA's shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -130,14 +132,18 @@ __device__ __forceinline__ uint64_t sdesc(const void* p)
            | (2ull << 61);                   // layout: 128-byte swizzle
 }
 
-// Instruction descriptor: kind::f16, A and B bf16, D fp32, both K-major, M = 128, N = 128.
-constexpr uint32_t G_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(G_BN >> 3) << 17) | ((uint32_t)(G_BM >> 4) << 24);
+// Instruction descriptor: kind::f16, A and B bf16, D fp32, both K-major, M = 128, N = BN.
+template <int BN> constexpr uint32_t g_idesc()
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(G_BM >> 4) << 24);
+}
 
+template <int BN>
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate)
 {
     asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                  " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-                 ::"r"(tmem_d), "l"(a), "l"(b), "r"(G_IDESC), "r"(accumulate) : "memory");
+                 ::"r"(tmem_d), "l"(a), "l"(b), "r"(g_idesc<BN>()), "r"(accumulate) : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar)
 {
@@ -182,14 +188,16 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
     lo = (uint32_t)__bfloat16_as_ushort(al) | ((uint32_t)__bfloat16_as_ushort(bl) << 16);
 }
 
-template <int WT>
+template <int WT, int BN>
 __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ CUtensorMap xh_map,
                                                             const __grid_constant__ CUtensorMap xl_map,
                                                             const uint8_t* __restrict__ tiles, int row_base, int rows,
                                                             int nsb, int T, float* __restrict__ y, int64_t ldy, int* err)
 {
-    using F = GemmFmt<WT>;
+    using F = GemmFmt<WT, BN>;
     constexpr int G_STAGES = F::STAGES, G_RAW_STAGES = F::RAW_STAGES, G_RAW_STAGE = F::RAW_STAGE;
+    constexpr int G_STAGE = g_stage<BN>(), G_B_BYTES = g_b_bytes<BN>();
+    constexpr int G_TMEM_COLS = BN;             // the fp32 accumulator: BN columns x 128 lanes
     constexpr int SPR = F::STEPS_PER_RAW;
     extern __shared__ uint8_t g_smem_raw[];
     __shared__ __align__(8) uint64_t full_a[G_STAGES], full_b[G_STAGES], empty[G_STAGES], acc_full;
@@ -199,7 +207,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
     uint8_t* smem = (uint8_t*)(((uintptr_t)g_smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* raw = smem + G_STAGES * G_STAGE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * G_BM, n0 = blockIdx.y * G_BN;
+    const int m0 = blockIdx.x * G_BM, n0 = blockIdx.y * BN;
     const int nk = nsb * 4;                 // K steps of 64 values
     // 16-row weight tiles of this CTA that exist (the last CTA of a matrix may have fewer than eight)
     const int live_tiles = min(G_BM / 16, (rows + 15) / 16 - m0 / 16);
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {                        // the accumulator: 128 TMEM columns x 128 lanes
+    if (warp == 0) {                        // the accumulator: BN TMEM columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&tmem_base)), "r"(G_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -357,7 +365,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
             }
         }
     } else if (warp == G_TMA_WARP) {
-        // ---- the tokens' bf16 planes, one 64-value x 128-token box each per K step (rows past T read as zeros)
+        // ---- the tokens' bf16 planes, one 64-value x BN-token box each per K step (rows past T read as zeros)
         if (lane == 0) {
             for (int i = 0; i < nk; ++i) {
                 const int s = i % G_STAGES;
@@ -382,9 +390,9 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
                 for (int kk = 0; kk < G_BK / 16; ++kk) {
                     const uint64_t ah = sdesc(st + kk * 32), al = sdesc(st + G_A_BYTES + kk * 32);
                     const uint64_t bh = sdesc(st + 2 * G_A_BYTES + kk * 32), bl = sdesc(st + 2 * G_A_BYTES + G_B_BYTES + kk * 32);
-                    umma_bf16(tmem, ah, bh, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_bf16(tmem, ah, bl, 1u);
-                    umma_bf16(tmem, al, bh, 1u);
+                    umma_bf16<BN>(tmem, ah, bh, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16<BN>(tmem, ah, bl, 1u);
+                    umma_bf16<BN>(tmem, al, bh, 1u);
                 }
                 umma_commit(&empty[s]);     // the stage is free once these MMAs have read it
             }
@@ -392,13 +400,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) k_gemm(const __grid_constant__ C
         }
     }
 
-    // ---- epilogue: warps 0-3, warp w reads TMEM lanes 32w .. 32w+31 (tile rows), 128 token columns in two halves
+    // ---- epilogue: warps 0-3, warp w reads TMEM lanes 32w .. 32w+31 (tile rows), BN token columns 64 at a time
     if (warp < 4) {
         mbar_wait(&acc_full, 0u, err, 15, &abort_flag);
         tc_fence_after();
         const int r = m0 + 32 * warp + lane;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < BN / 64; ++half) {
             float v[64];
             tmem_ld64(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(64 * half), v);
             if (r < rows) {
@@ -448,13 +456,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled()
     return fn;
 }
 
-// A [T][K] bf16 plane as 64 x 64 boxes with the 128-byte swizzle the MMA descriptors expect.
-CUtensorMap plane_map(const void* base, int T, int K)
+// A [T][K] bf16 plane as 64-value x bn-token boxes with the 128-byte swizzle the MMA descriptors expect.
+CUtensorMap plane_map(const void* base, int T, int K, int bn)
 {
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {G_BK, G_BN};
+    const cuuint32_t box[2] = {G_BK, (cuuint32_t)bn};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode_tiled()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -484,23 +492,33 @@ void gemm_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols
     if (gr > 148 * 8) gr = 148 * 8;
     launch(k_split_bf16, dim3((unsigned)gr), dim3(256), 0, s, x, ldx, cols, n, hi, lo);
     note_launch();
-    const CUtensorMap mh = plane_map(hi, T, cols), ml = plane_map(lo, T, cols);
+    // Q4_K prompts of more than 128 rows: 256-token tiles, so each weight is dequantized once per 256 tokens and each
+    // stage of dequantized weights feeds twice the MMA work
+    const int bn = (type == 12 && T > 128) ? 256 : 128;
+    const CUtensorMap mh = plane_map(hi, T, cols, bn), ml = plane_map(lo, T, cols, bn);
+    static std::mutex mu;
     static bool attr[64] = {false};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        WL_CUDA(cudaFuncSetAttribute(k_gemm<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<12>::SMEM));
-        WL_CUDA(cudaFuncSetAttribute(k_gemm<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<14>::SMEM));
-        attr[dev] = true;
+    WL_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 64 && !attr[dev]) {
+            WL_CUDA(cudaFuncSetAttribute(k_gemm<12, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<12, 128>::SMEM));
+            WL_CUDA(cudaFuncSetAttribute(k_gemm<12, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<12, 256>::SMEM));
+            WL_CUDA(cudaFuncSetAttribute(k_gemm<14, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmFmt<14, 128>::SMEM));
+            attr[dev] = true;
+        }
     }
-    const dim3 grid((rows + G_BM - 1) / G_BM, (T + G_BN - 1) / G_BN);
+    const dim3 grid((rows + G_BM - 1) / G_BM, (T + bn - 1) / bn);
     // A plain launch, and the kernel does not trigger its dependents: no other kernel overlaps a GEMM. With programmatic
     // dependent launch on both sides, consecutive GEMMs (each with its own activation-plane tensor maps) overlapped
     // and gave wrong sums now and then (1-3 % relative error in a 2-layer prefill, never with either side serialised).
-    if (type == 12)
-        k_gemm<12><<<grid, G_THREADS, GemmFmt<12>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    if (type == 12 && bn == 256)
+        k_gemm<12, 256><<<grid, G_THREADS, GemmFmt<12, 256>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+    else if (type == 12)
+        k_gemm<12, 128><<<grid, G_THREADS, GemmFmt<12, 128>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
     else
-        k_gemm<14><<<grid, G_THREADS, GemmFmt<14>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
+        k_gemm<14, 128><<<grid, G_THREADS, GemmFmt<14, 128>::SMEM, s>>>(mh, ml, tiles, row_base, rows, cols / 256, T, y, ldy, err);
     WL_CUDA(cudaGetLastError());
     note_launch();
 }
