@@ -1182,7 +1182,7 @@ int attention_splits(int T, int kv_heads)
 
 template <int HD, int G>
 static void attn_launch(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
 {
     const int S = attention_splits(T, kv_heads);
     const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
@@ -1203,12 +1203,13 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
     float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
     int* tickets = reinterpret_cast<int*>(part + (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (HD + 2));
     // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks. Wide CTAs
-    // (attn_threads) for decode steps (up to 8 rows: a wide CTA's threads carry a quarter of the dependent sums of a
-    // 128-thread one, and an SM holds twice the warps) and small grids; otherwise 128 threads, several CTAs per SM.
+    // (attn_threads) for small grids and for decode steps of up to 8 rows whose ranges hold 32 positions or more (a
+    // wide CTA's threads carry a quarter of the dependent sums of a 128-thread one, and an SM holds twice the warps;
+    // over shorter ranges several small CTAs an SM do better); otherwise 128 threads, several CTAs per SM.
     // Both give the same bits: every score and every (dim, head) sum is one thread's.
     constexpr bool can_merge = (G * HD) % 256 == 0;
     constexpr int WIDE = attn_threads(HD, G);
-    const bool wide = T <= 8 || (int64_t)S * kv_heads * T <= 2 * 148;
+    const bool wide = (T <= 8 && max_n >= 32 * S) || (int64_t)S * kv_heads * T <= 2 * 148;
     const dim3 grid(S, kv_heads, T);
     uint8_t* pb = prep ? prep->blocks : (uint8_t*)nullptr;
     if (S > 1 && can_merge) {
@@ -1235,14 +1236,14 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
 
 template <int HD>
 static void attn_launch_g(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
 {
     switch (heads / kv_heads) {
-    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
     }
 }
 
@@ -1254,7 +1255,7 @@ bool attention_supported(int heads, int kv_heads, int head_dim)
 }
 
 bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
 {
     if (T <= 0) return false;
     if (!attention_supported(heads, kv_heads, head_dim))
@@ -1263,11 +1264,11 @@ bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
     if (attention_splits(T, kv_heads) == 1) prep = nullptr;
     if (prep && (prep->cols != heads * head_dim || prep->nc != T)) WL_THROW(WL_EINVAL, "attention: prepared-activation view does not match");
     switch (head_dim) {
-    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
     }
     return prep != nullptr;
 }
