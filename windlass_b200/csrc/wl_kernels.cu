@@ -896,7 +896,7 @@ constexpr int attn_threads(int HD, int G)
 }
 
 template <int HD, int G, bool MERGE, int NT = attn_threads(HD, G)>
-__global__ void __launch_bounds__(NT, 1) k_attn_part(const float* q, int heads, int kv_heads,
+__global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_attn_part(const float* q, int heads, int kv_heads,
                                                   float scale, const RowKV* rows, int layer,
                                                   const int32_t* pos, int S,
                                                   float* out, float* part,
@@ -1182,7 +1182,7 @@ int attention_splits(int T, int kv_heads)
 
 template <int HD, int G>
 static void attn_launch(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
+                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
 {
     const int S = attention_splits(T, kv_heads);
     const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
@@ -1197,31 +1197,41 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
             WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
             WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, false, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
             WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            if (attn_threads(HD, G) > 256) {
+                WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+                WL_CUDA(cudaFuncSetAttribute(k_attn_part<HD, G, true, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+            }
             attr_set[dev] = true;
         }
     }
     float* ml = part + (size_t)ATT_PART_ROWS * S * heads * HD;
     int* tickets = reinterpret_cast<int*>(part + (size_t)ATT_PART_ROWS * attention_splits_for(kv_heads) * heads * (HD + 2));
-    // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks. Wide CTAs
-    // (attn_threads) for small grids and for decode steps of up to 8 rows whose ranges hold 32 positions or more (a
-    // wide CTA's threads carry a quarter of the dependent sums of a 128-thread one, and an SM holds twice the warps;
-    // over shorter ranges several small CTAs an SM do better); otherwise 128 threads, several CTAs per SM.
-    // Both give the same bits: every score and every (dim, head) sum is one thread's.
+    // the merge runs in the last CTA of each KV head when the group's outputs are whole superblocks
     constexpr bool can_merge = (G * HD) % 256 == 0;
     constexpr int WIDE = attn_threads(HD, G);
-    const bool wide = (T <= 8 && max_n >= 32 * S) || (int64_t)S * kv_heads * T <= 2 * 148;
+    constexpr int MID = WIDE > 256 ? 256 : WIDE;
+    // one CTA an SM when the grid fits the SMs about once or twice (a decode step of one row: the most threads per
+    // CTA); two of up to 256 threads an SM for decode steps of 2 to 8 rows whose grid spans several waves (more CTAs
+    // in flight hide each one's phases); otherwise 128 threads, several CTAs an SM. All give the same bits: every
+    // score and every (dim, head) sum is one thread's.
+    const int64_t ctas = (int64_t)S * kv_heads * T;
+    const int width = ctas <= 2 * 148 ? WIDE : T <= 8 ? MID : 128;
     const dim3 grid(S, kv_heads, T);
     uint8_t* pb = prep ? prep->blocks : (uint8_t*)nullptr;
     if (S > 1 && can_merge) {
-        if (wide) launch(k_attn_part<HD, G, true, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows, layer,
-                         pos, S, out, part, ml, tickets, pb);
+        if (width == WIDE) launch(k_attn_part<HD, G, true, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale,
+                                  rows, layer, pos, S, out, part, ml, tickets, pb);
+        else if (width == MID) launch(k_attn_part<HD, G, true, MID>, grid, dim3(MID), smem, s, q, heads, kv_heads, scale,
+                                      rows, layer, pos, S, out, part, ml, tickets, pb);
         else launch(k_attn_part<HD, G, true, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos,
                     S, out, part, ml, tickets, pb);
         launched();
         return;
     }
-    if (wide) launch(k_attn_part<HD, G, false, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows, layer,
-                     pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+    if (width == WIDE) launch(k_attn_part<HD, G, false, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows,
+                              layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+    else if (width == MID) launch(k_attn_part<HD, G, false, MID>, grid, dim3(MID), smem, s, q, heads, kv_heads, scale,
+                                  rows, layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
     else launch(k_attn_part<HD, G, false, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos, S,
                 out, part, ml, tickets, (uint8_t*)nullptr);
     launched();
@@ -1236,14 +1246,14 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
 
 template <int HD>
 static void attn_launch_g(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
+                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
 {
     switch (heads / kv_heads) {
-    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
     }
 }
 
@@ -1255,7 +1265,7 @@ bool attention_supported(int heads, int kv_heads, int head_dim)
 }
 
 bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s, int max_n)
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
 {
     if (T <= 0) return false;
     if (!attention_supported(heads, kv_heads, head_dim))
@@ -1264,11 +1274,11 @@ bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, flo
     if (attention_splits(T, kv_heads) == 1) prep = nullptr;
     if (prep && (prep->cols != heads * head_dim || prep->nc != T)) WL_THROW(WL_EINVAL, "attention: prepared-activation view does not match");
     switch (head_dim) {
-    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
-    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, max_n); break;
+    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
     }
     return prep != nullptr;
 }

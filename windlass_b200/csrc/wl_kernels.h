@@ -231,10 +231,8 @@ inline size_t attention_part_floats(int heads, int kv_heads, int head_dim)
 }
 int attention_splits(int T, int kv_heads);
 bool attention_supported(int heads, int kv_heads, int head_dim);
-// max_n (when known, else 0): the most positions a row of the step attends to, which picks the CTA width.
 bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s,
-               int max_n = 0);
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s);
 // RoPE on q (heads) and k (kv heads) of T rows, then k and v appended to the fp16 caches at pos[t] (Rope,
 // Transformer.cs:418-433, and ToHalf, :342-348), in one kernel; k is left unrotated in its buffer.
 void rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim, int rope_dims,

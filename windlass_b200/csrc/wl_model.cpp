@@ -1315,7 +1315,7 @@ void Model::layer(int l, int T, int max_n)
     if (want_prep) ap = k::xprep_view(xprep_buf_, QD, T);
     const int mark = profile_begin();
     const bool prepped = k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, att_part_, att_,
-                                      want_prep ? &ap : nullptr, stream_, step_max_n_);
+                                      want_prep ? &ap : nullptr, stream_);
     profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
     prep_x_ = nullptr;
     if (prepped) { prep_x_ = att_; prep_cols_ = QD; prep_nc_ = T; }
@@ -1414,12 +1414,10 @@ void Model::head(int T, int first)
 // Token ids, positions and KV-cache rows of one step to the device (pinned staging, async on the model's stream).
 void Model::upload_step(int T, const RowKV* rows, const int32_t* pos, const int32_t* tokens)
 {
-    step_max_n_ = 0;
     for (int t = 0; t < T; ++t) {
         h_tok_[t] = tokens[t];
         h_pos_[t] = pos[t];
         h_rows_[t] = rows[t];
-        step_max_n_ = std::max(step_max_n_, pos[t] + 1);
     }
     WL_CUDA(cudaMemcpyAsync(tok_d_, h_tok_, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));
     WL_CUDA(cudaMemcpyAsync(pos_d_, h_pos_, sizeof(int32_t) * T, cudaMemcpyHostToDevice, stream_));

@@ -318,7 +318,6 @@ private:
     // pinned host staging
     int32_t* h_tok_ = nullptr;
     int32_t* h_pos_ = nullptr;
-    int step_max_n_ = 0;                  // the most positions a row of the uploaded step attends to (a launch hint)
     RowKV* h_rows_ = nullptr;
     int32_t* h_sel_ = nullptr;
     float* h_wts_ = nullptr;
