@@ -458,6 +458,63 @@ static void launch_mv(int nc, int type, const uint8_t* w, int64_t rb, int rows, 
     }
 }
 
+// F32 matrices of few rows and a width that is a multiple of 1024 (the MoE router: experts x embedding): a CTA per
+// row, thread t holding values 4t + 1024k, each column's products added in that order, then the CTA's partial sums by
+// xor butterfly within warps and the warps in order; a column's arithmetic does not depend on the other columns.
+template <int NC>
+__global__ void __launch_bounds__(256) k_matvec_f32_row(const float* __restrict__ w, int64_t row_floats, int cols,
+                                                        const float* x, int64_t ldx, float* y, int64_t ldy)
+{
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float part[8][NC];
+    const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float* wr = w + (int64_t)row * row_floats;
+    float acc[NC];
+#pragma unroll
+    for (int t = 0; t < NC; ++t) acc[t] = 0.f;
+    for (int i = 4 * tid; i < cols; i += 1024) {
+        const float4 wv = ld4(wr + i);
+#pragma unroll
+        for (int t = 0; t < NC; ++t) {
+            const float4 xv = ld4(x + t * ldx + i);
+            acc[t] += wv.x * xv.x;
+            acc[t] += wv.y * xv.y;
+            acc[t] += wv.z * xv.z;
+            acc[t] += wv.w * xv.w;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NC; ++t) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0) part[warp][t] = v;
+    }
+    __syncthreads();
+    if (tid < NC) {
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sum += part[k][tid];
+        y[(int64_t)tid * ldy + row] = sum;
+    }
+}
+
+static void launch_f32_rows(int nc, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x,
+                            int64_t ldx, float* y, int64_t ldy, cudaStream_t s)
+{
+    const float* wf = reinterpret_cast<const float*>(w);
+    const int64_t rf = row_bytes / 4;
+    switch (nc) {
+    case 1: launch(k_matvec_f32_row<1>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 2: launch(k_matvec_f32_row<2>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 3: launch(k_matvec_f32_row<3>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 4: launch(k_matvec_f32_row<4>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 5: launch(k_matvec_f32_row<5>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 6: launch(k_matvec_f32_row<6>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    case 7: launch(k_matvec_f32_row<7>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    default: launch(k_matvec_f32_row<8>, dim3(rows), dim3(256), 0, s, wf, rf, cols, x, ldx, y, ldy); break;
+    }
+}
+
 void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, const float* x, int64_t ldx,
             int ncols, float* y, int64_t ldy, cudaStream_t s)
 {
@@ -476,6 +533,7 @@ void matvec(int type, const uint8_t* w, int64_t row_bytes, int rows, int cols, c
         else if (type == 8 && xa && w2 && cols % 32 == 0) launch_mv<MV_Q8_0>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else if (type == 23 && xa && w8 && cols % 256 == 0) launch_mv<MV_IQ4XS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else if (type == 16 && xa && w2 && cols % 256 == 0) launch_mv<MV_IQ2XXS>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
+        else if (type == 0 && xa && w16 && cols % 1024 == 0 && rows <= 1024) launch_f32_rows(nc, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else if (type == 0 && xa && w16 && cols % 32 == 0) launch_mv<MV_F32>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         else launch_mv<MV_GENERIC>(nc, type, w, row_bytes, rows, cols, xc, ldx, yc, ldy, s);
         launched();
