@@ -325,11 +325,6 @@ int32_t wl_matvec_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32
 int32_t wl_bench_matvec_tiles(int32_t type, const void* const* dev_tiles, int32_t copies, int32_t rows, int32_t cols,
                               const float* dev_x, int32_t ncols, float* dev_y, int32_t iters, double* device_ms,
                               void* stream);
-/* No counterpart in the reference: wl_matvec_tiles (Q4_K) with the superblocks of every row split into `parts` equal
- * contiguous ranges (1 <= parts <= cols / 256), as the model runs matrices with few rows: dev_y_parts holds parts
- * partial products, dev_y_parts[p*ncols*rows + t*rows + r], whose sum in order p = 0, 1, ... is W[r] . x[t]. */
-int32_t wl_matvec_tiles_split(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
-                              int32_t ncols, int32_t parts, float* dev_y_parts, void* stream);
 /* No counterpart in the reference: the tcgen05 GEMM (Q4_K only) on tile-major weights made by wl_make_tiles, for
  * T > 8 rows: dev_y[t*rows + r] = W[r] . dev_x[t]. The activations' bf16 hi/lo planes go to a scratch the library
  * keeps per device (grown on demand). Other formats return WL_EUNSUPPORTED. */

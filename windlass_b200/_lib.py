@@ -124,7 +124,6 @@ def lib():
         "wl_tiles_size": (I32, [I32, I32, I32, C.POINTER(I64)]),
         "wl_make_tiles": (I32, [I32, P, I32, I32, P, P]),
         "wl_matvec_tiles": (I32, [I32, P, I32, I32, P, I32, P, P]),
-        "wl_matvec_tiles_split": (I32, [I32, P, I32, I32, P, I32, I32, P, P]),
         "wl_bench_matvec_tiles": (I32, [I32, P, I32, I32, I32, P, I32, P, I32, C.POINTER(C.c_double), P]),
         "wl_matmul": (I32, [I32, P, I32, I32, P, I32, P, I32, P]),
         "wl_gemm_tiles": (I32, [I32, P, I32, I32, P, I32, P, P]),

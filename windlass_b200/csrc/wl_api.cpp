@@ -872,33 +872,6 @@ int32_t wl_bench_matvec_tiles(int32_t type, const void* const* dev_tiles, int32_
     });
 }
 
-int32_t wl_matvec_tiles_split(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x,
-                              int32_t ncols, int32_t parts, float* dev_y_parts, void* stream)
-{
-    return guarded([&]() -> int32_t {
-        if (type != 12 || !wl::k::tiles_supported(type, cols))
-            return wl::fail(WL_EUNSUPPORTED, "wl_matvec_tiles_split: Q4_K with cols a multiple of 256 only");
-        if (rows <= 0 || ncols <= 0) return wl::fail(WL_EINVAL, "MatMul shape mismatch.");
-        if (parts < 1 || parts > cols / 256) return wl::fail(WL_EINVAL, "wl_matvec_tiles_split: 1 <= parts <= cols / 256");
-        if (!dev_tiles || !dev_x || !dev_y_parts) return wl::fail(WL_EINVAL, "wl_matvec_tiles_split: null pointer");
-        if ((uintptr_t)dev_tiles % 16 != 0 || (uintptr_t)dev_x % 16 != 0)
-            return wl::fail(WL_EINVAL, "wl_matvec_tiles_split: dev_tiles and dev_x must be 16-byte aligned");
-        const cudaStream_t s = (cudaStream_t)stream;
-        uint8_t* scratch = (uint8_t*)export_scratch(256 + wl::k::xprep_bytes(cols, 8));
-        int* err = (int*)scratch;
-        WL_CUDA(cudaMemsetAsync(scratch + 128, 0, sizeof(int), s));   // orders the launches behind all earlier work
-        const int64_t pstride = (int64_t)ncols * rows;
-        for (int c0 = 0; c0 < ncols; c0 += 8) {
-            const int nc = ncols - c0 < 8 ? ncols - c0 : 8;
-            const wl::k::XPrep p = wl::k::xprep_view(scratch + 256, cols, nc);
-            wl::k::xprep(dev_x + (int64_t)c0 * cols, cols, cols, nc, p, s);
-            wl::k::matvec_tiles(type, (const uint8_t*)dev_tiles, 0, rows, cols, p, dev_y_parts + (int64_t)c0 * rows, rows,
-                                err, s, parts, pstride);
-        }
-        return WL_OK;
-    });
-}
-
 int32_t wl_gemm_tiles(int32_t type, const void* dev_tiles, int32_t rows, int32_t cols, const float* dev_x, int32_t T,
                       float* dev_y, void* stream)
 {

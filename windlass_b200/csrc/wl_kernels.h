@@ -149,11 +149,9 @@ void matvec_i8_tiles(int type, const uint8_t* tiles, int rows, int cols, const X
 void init_i8_tables();
 int64_t tile_bytes(int type, int rows, int cols);
 void make_tiles(int type, const uint8_t* w, int rows, int cols, int64_t row_bytes, uint8_t* tiles, cudaStream_t s);
-// P > 1 (Q4_K only, P <= cols / 256) splits the superblocks into P equal contiguous ranges and writes P partial
-// outputs, partial i at y + i * pstride; their sum in order 0..P-1 is the product.
-// With ao (Q4_K, P = 1 only) the outputs are not written to y but pushed as all-reduce ao.idx's elements.
+// With ao (Q4_K only) the outputs are not written to y but pushed as all-reduce ao.idx's elements.
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, int P = 1, int64_t pstride = 0, const ArOut* ao = nullptr);
+                  int64_t ldy, int* err, cudaStream_t s, const ArOut* ao = nullptr);
 
 // Two Q4_K matrices with the same columns and activations (q and k, gate and up) in one tensor-core matvec launch:
 // y_a[t*ldy_a + r] = A[row_base_a + r] . x[t], y_b likewise; each row's result is the one matvec_tiles gives.

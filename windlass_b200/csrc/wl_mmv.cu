@@ -374,8 +374,18 @@ __device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1,
 // one MMA per digit plane holds the columns. Both orders give every column the same fp32 operations, so a column's
 // result does not depend on how many columns share the launch.
 // PAIRS: the grouped-expert form (seg.sel set), compiled apart so that the dense matvec carries none of its code.
+// The launch bound's CTA count is what fits an SM: four (NW = 8) or eight (NW = 4) at one column, two or four from
+// three columns on; at two columns the stages leave room for only three or six (228 KB of shared memory an SM, 1 KB
+// of it reserved per CTA), and the bound says so, so that the compiler keeps the two-column loop in registers.
+constexpr int ctas_by_smem(int bytes) { return 228 * 1024 / (bytes + 1024); }
+template <int NC, int NW> constexpr int q4_min_ctas()
+{
+    return NC == 2 ? (ctas_by_smem(Q4Layout<NC, NW>::SMEM) < 32 / NW ? ctas_by_smem(Q4Layout<NC, NW>::SMEM) : 32 / NW)
+                   : (NC <= 2 ? 32 : 16) / NW;
+}
+
 template <int NC, bool TILED, bool PAIRS, int NW = 8, bool AR = false>
-__global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 32 : 16) / NW) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(32 * NW, q4_min_ctas<NC, NW>()) k_mmv_q4k(const __grid_constant__ CUtensorMap wmap,
                                                     const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb,
                                                     const uint8_t* xq, float* y_a,
                                                     int64_t ldy_a, int* err, const MvSeg seg, const ArOut ao)
@@ -817,307 +827,6 @@ __global__ void __launch_bounds__(32 * NW, 1) k_mmv_q4kp(const uint8_t* __restri
     }
 }
 
-// ---- the dual-group form (the decode matvec of the model's dense Q4_K matrices) ----
-// A CTA owns 32-row pairs of 16-row groups of the tile-major layout. Its work is a contiguous range [u_lo, u_hi) of
-// units (row pair rp, superblock sb), u = rp * nsb + sb:
-// - plain launch: one row pair per CTA and split `part` of P equal contiguous superblock ranges (P > 1 only for
-//   matrices with very few rows), partial `part` written at y + part * pstride;
-// - stream-K launch (SK): exactly gridDim.x CTAs (as many as the SMs hold at once) with equal unit ranges, so that
-//   matrices whose row pairs do not divide evenly over the SMs still keep every SM equally busy. A CTA's range then
-//   covers parts of at most two row pairs; each part's sums go to partial slot (CTA - first CTA of that row pair),
-//   and the consumer adds a row pair's 1 to 3 partials in slot order (ksplit_parts gives the count).
-// Warp w takes units u_lo + w, u_lo + w + NW, ...; each stage of its ring holds both groups' tiles of one superblock
-// and the superblock's prepared activations, so the activation fragments, the digit units, the min-term operand, the
-// barrier wait and the copies serve 32 rows. Each group's arithmetic is k_mmv_q4k's, so a row's result does not
-// depend on the other group or the other columns.
-template <int NC, int NW, int NS> struct Q4Layout2 {
-    static constexpr int X_OFF = 2 * Q4_TILE;   // 4608, a multiple of 128
-    static constexpr int STAGE = (X_OFF + NC * XP_COL + 127) / 128 * 128;
-    static constexpr int STAGES = NS;
-    static constexpr int RED = NW * 2 * Q4_ROWS * 9 * 4;   // a warp's sums of its first row pair, per warp
-    static constexpr int SMEM = NW * STAGES * STAGE + RED;
-};
-
-// The second matrix of a two-matrix dual-group launch (same columns and activations as the first; P = 1).
-struct MvSeg2 {
-    const uint8_t* wt;
-    int row_base, rows;
-    int first_ctas;             // CTAs of the first matrix; INT_MAX: one matrix
-    float* y;
-    int64_t ldy;
-};
-
-__device__ __forceinline__ int sk_cta_of(int64_t u, int64_t U, int n) { return (int)(((u + 1) * n - 1) / U); }
-
-template <int NC, int NW, int NS, bool SK>
-__global__ void __launch_bounds__(32 * NW, (NC <= 2 ? 16 : 8) / NW) k_mmv_q4k2(
-    const uint8_t* __restrict__ wt_a, int row_base_a, int rows_a, int nsb, const uint8_t* xq,
-    float* y_a, int64_t ldy_a, int P, int64_t pstride, int* err, const MvSeg2 seg)
-{
-    using LY = Q4Layout2<NC, NW, NS>;
-    constexpr bool PACK = NC <= 2;
-    constexpr int ND = PACK ? 1 : 3;            // MMAs per sub-block and group
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[NW][LY::STAGES];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const bool second = !SK && (int)blockIdx.x >= seg.first_ctas;
-    const int bx = second ? (int)blockIdx.x - seg.first_ctas : (int)blockIdx.x;
-    const uint8_t* __restrict__ wt = second ? seg.wt : wt_a;
-    const int row_base = second ? seg.row_base : row_base_a;
-    const int rows = second ? seg.rows : rows_a;
-    float* y = second ? seg.y : y_a;
-    const int64_t ldy = second ? seg.ldy : ldy_a;
-    const int n_rp = (rows + 31) / 32;
-    const int64_t U = (int64_t)n_rp * nsb;
-    int64_t u_lo, u_hi;
-    int part = 0;
-    if (SK) {
-        u_lo = (int64_t)bx * U / gridDim.x;
-        u_hi = (int64_t)(bx + 1) * U / gridDim.x;
-    } else {
-        const int Pq = second ? 1 : P;
-        const int rp = bx / Pq;
-        part = bx % Pq;
-        u_lo = (int64_t)rp * nsb + (int64_t)nsb * part / Pq;
-        u_hi = (int64_t)rp * nsb + (int64_t)nsb * (part + 1) / Pq;
-    }
-    const int rpA = (int)(u_lo / nsb), rpB = u_hi > u_lo ? (int)((u_hi - 1) / nsb) : rpA;
-    const int cnt = (int)(u_hi - u_lo);
-    const int njobs = cnt > warp ? (cnt - warp + NW - 1) / NW : 0;
-    const int tile_row0 = row_base / Q4_ROWS;
-    uint8_t* ring = smem + warp * LY::STAGES * LY::STAGE;
-    float* red0 = reinterpret_cast<float*>(smem + NW * LY::STAGES * LY::STAGE) + warp * 2 * Q4_ROWS * 9;
-
-    pdl_trigger();
-    if (lane == 0) {
-        for (int s = 0; s < LY::STAGES; ++s) mbar_init(&bars[warp][s], 1);
-        fence_mbar_init();
-        fence_proxy_async();
-    }
-    __syncwarp();
-    auto issue_w = [&](int j, int s) {      // weights: written by no kernel, so they may stream before pdl_wait()
-        uint8_t* st = ring + s * LY::STAGE;
-        const int64_t u = u_lo + warp + (int64_t)NW * j;
-        const int rp = (int)(u / nsb), sb = (int)(u - (int64_t)rp * nsb);
-        const bool two = rp * 32 + 16 < rows;
-        const int64_t t0 = (int64_t)(tile_row0 + 2 * rp) * nsb + sb;
-        mbar_expect_tx(&bars[warp][s], (two ? 2 : 1) * Q4_TILE + NC * XP_COL);
-        bulk_load(st, wt + t0 * Q4_TILE, Q4_TILE, &bars[warp][s]);
-        if (two) bulk_load(st + Q4_TILE, wt + (t0 + nsb) * Q4_TILE, Q4_TILE, &bars[warp][s]);
-    };
-    auto issue_x = [&](int j, int s) {      // prepared activations of the same superblock, on the same barrier
-        const int64_t u = u_lo + warp + (int64_t)NW * j;
-        const int sb = (int)(u % nsb);
-        uint8_t* st = ring + s * LY::STAGE;
-#pragma unroll
-        for (int n = 0; n < NC; ++n)
-            bulk_load(st + LY::X_OFF + n * XP_COL, xq + ((int64_t)n * nsb + sb) * XP_COL, XP_COL, &bars[warp][s]);
-    };
-    if (lane == 0)
-        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_w(j, j);
-    pdl_wait();
-    if (lane == 0)
-        for (int j = 0; j < LY::STAGES && j < njobs; ++j) issue_x(j, j);
-
-    const bool b_ok = PACK ? g < 3 * NC : g < NC;
-    const int b_off = LY::X_OFF + (PACK ? (g / 3) * XP_COL + (g % 3) * XP_DIGIT : g * XP_COL);
-    // per D column 2c+k2 of this lane: the digit unit's word offset and its factor, fixed over the loop
-    int u_off[2];
-    float u_fac[2][ND];
-#pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2) {
-        const int nn = 2 * c + k2;
-        const bool ok = PACK ? nn < 3 * NC : nn < NC;
-        const int col = PACK ? nn / 3 : nn;
-        u_off[k2] = LY::X_OFF + (ok ? col : 0) * XP_COL + XP_REC + 32;
-#pragma unroll
-        for (int d = 0; d < ND; ++d) {
-            const int dig = PACK ? nn % 3 : d;
-            u_fac[k2][d] = ok ? (dig == 0 ? 1024.f : dig == 1 ? 8.f : 0.0625f) : 0.f;
-        }
-    }
-    const bool m_ok0 = 2 * c < NC, m_ok1 = 2 * c + 1 < NC;
-    const int mu_off0 = LY::X_OFF + (m_ok0 ? 2 * c : 0) * XP_COL + XP_REC + 32;
-    const int mu_off1 = LY::X_OFF + (m_ok1 ? 2 * c + 1 : 0) * XP_COL + XP_REC + 32;
-    const float mu_fac0 = m_ok0 ? 1024.f : 0.f, mu_fac1 = m_ok1 ? 1024.f : 0.f;
-    const uint32_t msel = (uint32_t)((2 * c) & 3) | (4u << 4) | ((uint32_t)((2 * c + 1) & 3) << 8) | (4u << 12);
-    const __half2 k1024 = __float2half2_rn(1024.f);
-
-    float facc[2][ND][4] = {};
-    float macc[2][4] = {};
-    // the sums of both groups to a red area [2][Q4_ROWS][9]: ((plane 0 + plane 1) + plane 2) - min term per (row,
-    // column); packed layouts keep the planes and the min term apart, for the final sum's fixed order
-    auto flush = [&](float* red) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            float* rq = red + q * Q4_ROWS * 9;
-            if (PACK) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) rq[(g + 8 * (e >> 1)) * 9 + 2 * c + (e & 1)] = facc[q][0][e];
-                if (c == 0) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) rq[(g + 8 * (e >> 1)) * 9 + 6 + (e & 1)] = macc[q][e];
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = g + 8 * (e >> 1), col = 2 * c + (e & 1);
-                    if (col < NC)
-                        rq[row * 9 + col] = ((facc[q][0][e] + facc[q][ND > 1 ? 1 : 0][e]) + facc[q][ND > 2 ? 2 : 0][e]) -
-                                            macc[q][e];
-                }
-            }
-        }
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-#pragma unroll
-            for (int d = 0; d < ND; ++d)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) facc[q][d][e] = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) macc[q][e] = 0.f;
-        }
-    };
-    bool in_b = false;                          // the accumulators hold row pair rpB (else rpA)
-    for (int j = 0; j < njobs; ++j) {
-        const int s = j % LY::STAGES;
-        const int64_t u = u_lo + warp + (int64_t)NW * j;
-        const int rp = (int)(u / nsb);
-        if (SK && rp != rpA && !in_b) {         // crossing into the CTA's second row pair
-            flush(red0);
-            in_b = true;
-        }
-        const int ngrp = rp * 32 + 16 < rows ? 2 : 1;
-        const bool ok = mbar_wait_bounded(&bars[warp][s], (uint32_t)((j / LY::STAGES) & 1), err, 1);
-        const uint8_t* st = ring + s * LY::STAGE;
-        if (ok) {
-            uint4 h0[2], h1[2];
-            uint32_t s0lo[2], s0hi[2], s1lo[2], s1hi[2];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                if (q < ngrp) {
-                    h0[q] = lds128(st + q * Q4_TILE + g * 16);
-                    h1[q] = lds128(st + q * Q4_TILE + (g + 8) * 16);
-                } else {
-                    h0[q] = make_uint4(0u, 0u, 0u, 0u);
-                    h1[q] = h0[q];
-                }
-                s0lo[q] = h0[q].y & 0x3F3F3F3Fu;
-                s0hi[q] = (h0[q].w & 0x0F0F0F0Fu) | ((h0[q].y >> 2) & 0x30303030u);
-                s1lo[q] = h1[q].y & 0x3F3F3F3Fu;
-                s1hi[q] = (h1[q].w & 0x0F0F0F0Fu) | ((h1[q].y >> 2) & 0x30303030u);
-            }
-            int acc_lo[2][ND][4] = {}, acc_hi[2][ND][4] = {};
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                uint2 bf[2][ND];
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-                    for (int d = 0; d < ND; ++d)
-                        bf[hh][d] = b_ok ? lds64(st + b_off + d * XP_DIGIT + 32 * (2 * r + hh) + 8 * c) : make_uint2(0u, 0u);
-                const int kb = (2 * r) & 3;
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    if (q >= ngrp) break;
-                    const uint4 wv = lds128(st + q * Q4_TILE + Q4_HDRS + r * 512 + lane * 16);
-                    const uint32_t sw0 = r < 2 ? s0lo[q] : s0hi[q], sw1 = r < 2 ? s1lo[q] : s1hi[q];
-                    const int sl0 = (int)((sw0 >> (8 * kb)) & 0xFFu), sh0 = (int)((sw0 >> (8 * kb + 8)) & 0xFFu);
-                    const int sl1 = (int)((sw1 >> (8 * kb)) & 0xFFu), sh1 = (int)((sw1 >> (8 * kb + 8)) & 0xFFu);
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const uint32_t mask = hh ? 0xF0F0F0F0u : 0x0F0F0F0Fu;   // high nibbles stay in place: 16q
-                        const uint32_t a0 = wv.x & mask, a1 = wv.z & mask, a2 = wv.y & mask, a3 = wv.w & mask;
-                        const int sa = hh ? sh0 : sl0, sb2 = hh ? sh1 : sl1;
-#pragma unroll
-                        for (int d = 0; d < ND; ++d) {
-                            int D[4];
-                            imma16832(D, a0, a1, a2, a3, bf[hh][d].x, bf[hh][d].y);
-                            int (&acc)[4] = hh ? acc_hi[q][d] : acc_lo[q][d];
-                            acc[0] += sa * D[0];
-                            acc[1] += sa * D[1];
-                            acc[2] += sb2 * D[2];
-                            acc[3] += sb2 * D[3];
-                        }
-                    }
-                }
-            }
-            // digit planes: 16 * sum_j s_j sum(q X) = 16 acc_lo + acc_hi (exact); unit * 2^(14 - 7 digit) / 16
-            float fu[2][ND];
-#pragma unroll
-            for (int k2 = 0; k2 < 2; ++k2) {
-                const float unit = *reinterpret_cast<const float*>(st + u_off[k2]);
-#pragma unroll
-                for (int d = 0; d < ND; ++d) fu[k2][d] = unit * u_fac[k2][d];
-            }
-            // min term operands shared by the groups: B = the lane's column's hi sums (slots 0..7), lo sums (8..15)
-            const uint2 bs = g < NC ? lds64(st + LY::X_OFF + g * XP_COL + XP_REC + 8 * c) : make_uint2(0u, 0u);
-            const float mu0 = *reinterpret_cast<const float*>(st + mu_off0) * mu_fac0;
-            const float mu1 = *reinterpret_cast<const float*>(st + mu_off1) * mu_fac1;
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                if (q >= ngrp) break;
-                const float dd0 = h2f_((uint16_t)(h0[q].x & 0xFFFF)), dm0 = h2f_((uint16_t)(h0[q].x >> 16));
-                const float dd1 = h2f_((uint16_t)(h1[q].x & 0xFFFF)), dm1 = h2f_((uint16_t)(h1[q].x >> 16));
-#pragma unroll
-                for (int k2 = 0; k2 < 2; ++k2)
-#pragma unroll
-                    for (int d = 0; d < ND; ++d) {
-                        facc[q][d][k2] = fmaf((float)(acc_lo[q][d][k2] * 16 + acc_hi[q][d][k2]), dd0 * fu[k2][d],
-                                              facc[q][d][k2]);
-                        facc[q][d][k2 + 2] = fmaf((float)(acc_lo[q][d][k2 + 2] * 16 + acc_hi[q][d][k2 + 2]),
-                                                  dd1 * fu[k2][d], facc[q][d][k2 + 2]);
-                    }
-                const uint32_t m0lo = h0[q].z & 0x3F3F3F3Fu;
-                const uint32_t m0hi = ((h0[q].w >> 4) & 0x0F0F0F0Fu) | ((h0[q].z >> 2) & 0x30303030u);
-                const uint32_t m1lo = h1[q].z & 0x3F3F3F3Fu;
-                const uint32_t m1hi = ((h1[q].w >> 4) & 0x0F0F0F0Fu) | ((h1[q].z >> 2) & 0x30303030u);
-                const uint32_t mp0 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m0lo : m0hi, 0x64646464u, msel)), k1024));
-                const uint32_t mp1 = h2_bits(__hsub2(bits_h2(__byte_perm(c < 2 ? m1lo : m1hi, 0x64646464u, msel)), k1024));
-                float dn[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816(dn, mp0, mp1, mp0, mp1, bs.x, bs.y);
-                macc[q][0] = fmaf(dn[0], dm0 * mu0, macc[q][0]);
-                macc[q][1] = fmaf(dn[1], dm0 * mu1, macc[q][1]);
-                macc[q][2] = fmaf(dn[2], dm1 * mu0, macc[q][2]);
-                macc[q][3] = fmaf(dn[3], dm1 * mu1, macc[q][3]);
-            }
-        }
-        __syncwarp();
-        if (lane == 0 && j + LY::STAGES < njobs) {
-            fence_proxy_async();        // the stage's generic reads are done before the copy engine rewrites it
-            issue_w(j + LY::STAGES, s);
-            issue_x(j + LY::STAGES, s);
-        }
-    }
-    // red0: this warp's sums of rpA; the start of its ring (whose stages it has finished with): its sums of rpB
-    float* red1 = reinterpret_cast<float*>(ring);
-    if (!in_b) flush(red0);                     // (a warp with no unit of rpB leaves zeros for it)
-    flush(red1);
-    __syncthreads();
-    const int nseg = rpB != rpA ? 2 : 1;
-    for (int sg = 0; sg < nseg; ++sg) {
-        const int rp = sg ? rpB : rpA;
-        const int slot = SK ? bx - sk_cta_of((int64_t)rp * nsb, U, gridDim.x) : part;
-#pragma unroll
-        for (int pass = 0; pass < (8 + NW - 1) / NW; ++pass) {
-            const int idx = threadIdx.x + pass * 32 * NW;
-            const int rl = idx >> 3, col = idx & 7;     // rl: row 0..31 of the row pair
-            if (idx < 256 && col < NC && rp * 32 + rl < rows) {
-                float sum = 0.f;
-#pragma unroll
-                for (int wv = 0; wv < NW; ++wv) {
-                    const float* rw = (sg ? reinterpret_cast<const float*>(smem + wv * LY::STAGES * LY::STAGE)
-                                          : reinterpret_cast<const float*>(smem + NW * LY::STAGES * LY::STAGE) +
-                                                wv * 2 * Q4_ROWS * 9) + rl * 9;
-                    const float v = PACK ? ((rw[3 * col] + rw[3 * col + 1]) + rw[3 * col + 2]) - rw[6 + col] : rw[col];
-                    sum += v;
-                }
-                y[(int64_t)slot * pstride + (int64_t)col * ldy + rp * 32 + rl] = sum;
-            }
-        }
-    }
-}
-
 // Repacks rows [0, rows) of a Q4_K matrix into the tile-major layout above; rows past the end are zero. One CTA per tile.
 __global__ void k_q4k_tile(const uint8_t* src, int rows, int nsb, int64_t row_bytes,
                            uint8_t* dst)
@@ -1168,6 +877,12 @@ template <int NC> struct Q6Layout {
     static constexpr int SMEM = 8 * STAGES * STAGE;
 };
 
+// Three CTAs an SM at one column; from two columns on the stages leave room for two, and the launch bound says so.
+template <int NC> constexpr int q6_min_ctas()
+{
+    return ctas_by_smem(Q6Layout<NC>::SMEM) < 3 ? ctas_by_smem(Q6Layout<NC>::SMEM) : 3;
+}
+
 __device__ __forceinline__ void imma16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0)
 {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
@@ -1182,7 +897,7 @@ __device__ __forceinline__ uint32_t sc_pair_h2(uint32_t w, uint32_t sel, __half2
 }
 
 template <int NC>
-__global__ void __launch_bounds__(256, 3) k_mmv_q6k(const uint8_t* __restrict__ wt, int rows, int nsb,
+__global__ void __launch_bounds__(256, q6_min_ctas<NC>()) k_mmv_q6k(const uint8_t* __restrict__ wt, int rows, int nsb,
                                                     const uint8_t* xq, float* y, int64_t ldy,
                                                     int* err)
 {
@@ -1572,11 +1287,6 @@ template <int NC, bool TILED, bool PAIRS, int NW = 8, bool AR = false> struct Q4
     static void ensure() { ensure_smem_attr(k_mmv_q4k<NC, TILED, PAIRS, NW, AR>, Q4Layout<NC, NW>::SMEM, done); }
 };
 template <int NC, bool TILED, bool PAIRS, int NW, bool AR> std::atomic<bool> Q4Attr<NC, TILED, PAIRS, NW, AR>::done[64];
-template <int NC, int NW, int NS, bool SK> struct Q4Attr2 {
-    static std::atomic<bool> done[64];
-    static void ensure() { ensure_smem_attr(k_mmv_q4k2<NC, NW, NS, SK>, Q4Layout2<NC, NW, NS>::SMEM, done); }
-};
-template <int NC, int NW, int NS, bool SK> std::atomic<bool> Q4Attr2<NC, NW, NS, SK>::done[64];
 template <int NC> struct Q6Attr {
     static std::atomic<bool> done[64];
     static void ensure() { ensure_smem_attr(k_mmv_q6k<NC>, Q6Layout<NC>::SMEM, done); }
@@ -1665,39 +1375,7 @@ static void dispatch_q4k(const CUtensorMap& m, const uint8_t* tiles, int row_bas
     }
 }
 
-template <int NC, int NW, int NS, bool SK>
-static void launch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                        int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg, int sk_ctas)
-{
-    Q4Attr2<NC, NW, NS, SK>::ensure();
-    const int ctas = SK ? sk_ctas : (rows + 31) / 32 * P + (seg.wt ? (seg.rows + 31) / 32 : 0);
-    launch(k_mmv_q4k2<NC, NW, NS, SK>, dim3(ctas), dim3(32 * NW), Q4Layout2<NC, NW, NS>::SMEM, s, tiles, row_base, rows,
-           nsb, (const uint8_t*)p.blocks, y, ldy, P, pstride, err, seg);
-    note_launch();
-}
-
-template <int NW, int NS, bool SK>
-static void dispatch_q4k2_cfg(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y,
-                              int64_t ldy, int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg,
-                              int sk_ctas = 0)
-{
-    switch (p.nc) {
-    case 1: launch_q4k2<1, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 2: launch_q4k2<2, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 3: launch_q4k2<3, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 4: launch_q4k2<4, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 5: launch_q4k2<5, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 6: launch_q4k2<6, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    case 7: launch_q4k2<7, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    default: launch_q4k2<8, NW, NS, SK>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg, sk_ctas); break;
-    }
-}
-
-// The launch shape of the dual-group matvec for a matrix, from graph-timed sweeps on B200 (8192 x 8192, 9216 x 8192,
-// 8192 x 28672, 28672 x 8192 and the tensor-parallel shards): 8 warps with two stages each (two CTAs per SM) for
-// matrices of up to 4 x SMs row pairs, where the 32-row CTAs barely fill the GPU; 4 warps with two stages (four CTAs
-// per SM, twice the superblocks per warp) for taller ones, 7-10 % faster on 28672 x 8192. Deeper rings cost CTAs per
-// SM and were slower on every shape.
+// The GPU's SM count (per process, from the current device).
 static int sm_count()
 {
     static std::atomic<int> n{0};
@@ -1711,20 +1389,10 @@ static int sm_count()
     return v;
 }
 
-static void dispatch_q4k2(const uint8_t* tiles, int row_base, int rows, int nsb, const XPrep& p, float* y, int64_t ldy,
-                          int P, int64_t pstride, int* err, cudaStream_t s, const MvSeg2& seg)
-{
-    const int rp = (rows + 31) / 32 * P + (seg.wt ? (seg.rows + 31) / 32 : 0);
-    if (rp >= 4 * sm_count() && P == 1 && !seg.wt)
-        dispatch_q4k2_cfg<4, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
-    else
-        dispatch_q4k2_cfg<8, 2, false>(tiles, row_base, rows, nsb, p, y, ldy, P, pstride, err, s, seg);
-}
-
 // The model's decode matvec on tile-major Q4_K: one 16-row CTA per row tile. In a decode step every matvec follows a
 // small kernel, and CTAs this size start under programmatic dependent launch while that kernel still runs (four fit
-// beside it on an SM) and stream their first stages meanwhile; the 32-row form above, faster back to back, lost 6 %
-// of the 70B step for that reason. Eight warps per CTA for up to 8 x SMs row tiles at one or two columns; four warps
+// beside it on an SM) and stream their first stages meanwhile; a 32-row form (a warp on two tiles of the same
+// superblocks), faster back to back, lost 6 % of the 70B step for that reason and was dropped. Eight warps per CTA for up to 8 x SMs row tiles at one or two columns; four warps
 // (twice the superblocks per warp, twice the CTAs per SM) for taller matrices. The warp count fixes how a row's
 // superblocks are grouped and added, so it depends on the matrix alone, never on the column count: a decode step's
 // rows then equal single-sequence steps bit for bit. (An earlier version took four warps for every matrix from three
@@ -1860,12 +1528,11 @@ void matvec_pairs2(const uint8_t* tiles_a, const uint8_t* tiles_b, int expert_ro
 }
 
 void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int cols, const XPrep& p, float* y,
-                  int64_t ldy, int* err, cudaStream_t s, int P, int64_t pstride, const ArOut* ao)
+                  int64_t ldy, int* err, cudaStream_t s, const ArOut* ao)
 {
     if ((uintptr_t)tiles % 16 != 0 || row_base % 16 != 0) WL_THROW(WL_EINVAL, "matvec_tiles: misaligned tiles");
     if (!tiles_supported(type, cols)) WL_THROW(WL_EUNSUPPORTED, "matvec_tiles: no tile layout for this type");
-    if (P < 1 || P > cols / 256 || (type != 12 && P != 1)) WL_THROW(WL_EINVAL, "matvec_tiles: bad split count");
-    if (ao && (type != 12 || P != 1 || ao->G < 1 || ao->G > AR_MAX_RANKS || ao->rank < 0 || ao->rank >= ao->G ||
+    if (ao && (type != 12 || ao->G < 1 || ao->G > AR_MAX_RANKS || ao->rank < 0 || ao->rank >= ao->G ||
                ao->E != rows || p.nc > AR_COLS || ao->idx < 0 || ao->idx >= AR_STEP))
         WL_THROW(WL_EINVAL, "matvec_tiles: the all-reduce push does not match");
     if (i8_tiles_supported(type, cols)) {
@@ -1873,14 +1540,11 @@ void matvec_tiles(int type, const uint8_t* tiles, int row_base, int rows, int co
         matvec_i8_tiles(type, tiles + (int64_t)(row_base / 16) * tb, rows, cols, p, y, ldy, err, s);
         return;
     }
-    if (type == 12 && P == 1) {
+    if (type == 12) {
         CUtensorMap none;
         memset(&none, 0, sizeof none);
         dispatch_q4k16(none, tiles, row_base, rows, cols / 256, p, y, ldy, err, s,
                        MvSeg{nullptr, 0, 0, INT_MAX, nullptr, 0, nullptr, 0, 1, 0}, ao ? *ao : ArOut{});
-    } else if (type == 12) {
-        dispatch_q4k2(tiles, row_base, rows, cols / 256, p, y, ldy, P, pstride, err, s,
-                      MvSeg2{nullptr, 0, 0, INT_MAX, nullptr, 0});
     } else {
         matvec_q6k(tiles + (int64_t)(row_base / 16) * (cols / 256) * Q6_TILE, rows, cols, p, y, ldy, err, s);
     }

@@ -989,7 +989,7 @@ void Model::matmul(const Weight& w, const float* x, int T, float* y, int path, b
             const int mark = profile_begin();
             const bool push = ar_out_ && w.type == 12 && T <= 8;
             k::matvec_tiles(w.type, w.tiles, w.row_base, w.rows, w.cols, p, y + (int64_t)c0 * ldy, ldy, err_d_,
-                            stream_, 1, 0, push ? ar_out_ : nullptr);
+                            stream_, push ? ar_out_ : nullptr);
             if (push) ar_out_done_ = true;
             profile_end(mark, w.type, (double)w.rows * w.row_bytes + 4.0 * nc * ((double)w.cols + w.rows));
         }
