@@ -129,8 +129,9 @@ def test_qwen3moe_shape_decode_b1_and_b8(wl, oracle):
 
 def test_70b_shape_batch_rows_bit_identical_to_single_runs(wl):
     """ForwardBatch rows equal single-sequence Forward bit for bit (tests/BatchTests.cs:29-94) at the 70B layer's
-    shapes, where the decode matvec's launch shape is chosen from the matrix's row tiles: a batch of 8 sequences and
-    of 3 (the four-column and the packed two-column forms of the integer matvec against the single column)."""
+    shapes, where the decode matvec's launch shape is chosen from the matrix's row tiles: batches of 8, 3 and 2
+    sequences (the persistent paired-tile form, the three-MMA form and the packed two-column form of the integer
+    matvec against the single column)."""
     spec = llama70b_spec(layers=1)
     rng = np.random.default_rng(707)
     prompts = [rng.integers(0, spec.vocab, n).astype(np.int32) for n in (37, 5, 120, 64, 1, 77, 200, 19)]
@@ -141,7 +142,7 @@ def test_70b_shape_batch_rows_bit_identical_to_single_runs(wl):
             m.forward(p, seq=s)
             solo.forward(p, seq=r)
         toks = rng.integers(0, spec.vocab, 8).astype(np.int32)
-        for n in (8, 3):
+        for n in (8, 3, 2):
             rows = m.forward_batch(seqs[:n], toks[:n])
             for i in range(n):
                 want = solo.forward([int(toks[i])], pos0=ref[i].length, seq=ref[i])
