@@ -959,7 +959,7 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_attn_part(const float
                                                   const int32_t* pos, int S,
                                                   float* out, float* part,
                                                   float* ml, int* tickets,
-                                                  uint8_t* prep)
+                                                  uint8_t* prep, const AttnRope ro)
 {
     constexpr int KP = HD + 8;              // row pitch of the staged tiles in halves (16 bytes of padding)
     constexpr int CH = HD / 8;              // 16-byte chunks per row
@@ -985,10 +985,51 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_attn_part(const float
     const int per = (n + S - 1) / S;
     const int start = sp * per, end = min(n, start + per);
     const float* qp = q + (int64_t)t * QD + (int64_t)kvh * G * HD;
-    for (int i = tid; i < G * HD; i += NT) qs[i] = qp[i];
-    if (tid < G) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
     const uint16_t* K = rk.k + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
     const uint16_t* V = rk.v + (int64_t)layer * rk.layer_stride + (int64_t)kvh * HD;
+    // with ro.k (one-row decode): RoPE here, k_rope_append's arithmetic, at the row's new position n - 1
+    __shared__ uint16_t knew[HD], vnew[HD];
+    const bool owns_new = ro.k && start <= n - 1 && n - 1 < end;
+    if (ro.k) {
+        const int half = ro.rope_dims / 2;
+        const float* cs = ro.table + (int64_t)(n - 1) * ro.rope_dims;
+        for (int e = tid; e < G * HD; e += NT) {
+            const int hb = e - e % HD, d = e % HD;
+            float val = qp[e];
+            if (d < ro.rope_dims) {
+                const bool first = ro.neox ? d < half : (d & 1) == 0;
+                const int i = ro.neox ? (first ? d : d - half) : d >> 1;
+                const int a = ro.neox ? i : 2 * i, b = ro.neox ? i + half : 2 * i + 1;
+                const float x0 = qp[hb + a], x1 = qp[hb + b], c = cs[2 * i], sn = cs[2 * i + 1];
+                val = first ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+            }
+            qs[e] = val;
+        }
+        if (owns_new) {
+            // this KV head's k (rotated) and v at the new position, into the cache and, below, into the staged tile
+            const float* kr = ro.k + (int64_t)t * KD + (int64_t)kvh * HD;
+            const float* vr = ro.v + (int64_t)t * KD + (int64_t)kvh * HD;
+            uint16_t* Kw = rk.k + (int64_t)layer * rk.layer_stride + (int64_t)(n - 1) * KD + (int64_t)kvh * HD;
+            uint16_t* Vw = rk.v + (int64_t)layer * rk.layer_stride + (int64_t)(n - 1) * KD + (int64_t)kvh * HD;
+            for (int d = tid; d < HD; d += NT) {
+                float kv = kr[d];
+                if (d < ro.rope_dims) {
+                    const bool first = ro.neox ? d < half : (d & 1) == 0;
+                    const int i = ro.neox ? (first ? d : d - half) : d >> 1;
+                    const int a = ro.neox ? i : 2 * i, b = ro.neox ? i + half : 2 * i + 1;
+                    const float x0 = kr[a], x1 = kr[b], c = cs[2 * i], sn = cs[2 * i + 1];
+                    kv = first ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+                }
+                knew[d] = __half_as_ushort(__float2half_rn(kv));
+                vnew[d] = __half_as_ushort(__float2half_rn(vr[d]));
+                Kw[d] = knew[d];
+                Vw[d] = vnew[d];
+            }
+        }
+    } else {
+        for (int i = tid; i < G * HD; i += NT) qs[i] = qp[i];
+    }
+    if (tid < G) { mrun[tid] = -INFINITY; lrun[tid] = 0.0; }
     float o[IPT];
     int od[IPT], oh[IPT];
 #pragma unroll
@@ -1001,11 +1042,20 @@ __global__ void __launch_bounds__(NT, NT == 256 ? 2 : 1) k_attn_part(const float
     const int pl = tid % ATT_P, hs = tid / ATT_P;
     for (int tile0 = start; tile0 < end; tile0 += ATT_P) {
         const int cnt = min(ATT_P, end - tile0);
+        // (the new position's row, when this CTA wrote it, comes from knew/vnew: each thread places the values it
+        // computed, so no barrier is needed before)
+        const int rnew = owns_new && n - 1 < tile0 + cnt ? n - 1 - tile0 : -1;
         for (int i = tid; i < cnt * CH; i += NT) {
             const int r = i / CH, c = i % CH;
+            if (r == rnew) continue;
             cp_async16(ks + r * KP + c * 8, K + (int64_t)(tile0 + r) * KD + c * 8);
             cp_async16(vs + r * KP + c * 8, V + (int64_t)(tile0 + r) * KD + c * 8);
         }
+        if (rnew >= 0)
+            for (int d = tid; d < HD; d += NT) {
+                ks[rnew * KP + d] = knew[d];
+                vs[rnew * KP + d] = vnew[d];
+            }
         cp_async_wait_all();
         __syncthreads();
         // scores: the reference's four interleaved accumulators per (head, position), each on one thread
@@ -1240,7 +1290,8 @@ int attention_splits(int T, int kv_heads)
 
 template <int HD, int G>
 static void attn_launch(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+                        const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s,
+                        const AttnRope& ro)
 {
     const int S = attention_splits(T, kv_heads);
     const size_t smem = sizeof(uint16_t) * 2 * ATT_P * (HD + 8) + sizeof(float) * (size_t)G * HD;
@@ -1278,20 +1329,20 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
     uint8_t* pb = prep ? prep->blocks : (uint8_t*)nullptr;
     if (S > 1 && can_merge) {
         if (width == WIDE) launch(k_attn_part<HD, G, true, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale,
-                                  rows, layer, pos, S, out, part, ml, tickets, pb);
+                                  rows, layer, pos, S, out, part, ml, tickets, pb, ro);
         else if (width == MID) launch(k_attn_part<HD, G, true, MID>, grid, dim3(MID), smem, s, q, heads, kv_heads, scale,
-                                      rows, layer, pos, S, out, part, ml, tickets, pb);
+                                      rows, layer, pos, S, out, part, ml, tickets, pb, ro);
         else launch(k_attn_part<HD, G, true, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos,
-                    S, out, part, ml, tickets, pb);
+                    S, out, part, ml, tickets, pb, ro);
         launched();
         return;
     }
     if (width == WIDE) launch(k_attn_part<HD, G, false, WIDE>, grid, dim3(WIDE), smem, s, q, heads, kv_heads, scale, rows,
-                              layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+                              layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr, ro);
     else if (width == MID) launch(k_attn_part<HD, G, false, MID>, grid, dim3(MID), smem, s, q, heads, kv_heads, scale,
-                                  rows, layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr);
+                                  rows, layer, pos, S, out, part, ml, tickets, (uint8_t*)nullptr, ro);
     else launch(k_attn_part<HD, G, false, 128>, grid, dim3(128), smem, s, q, heads, kv_heads, scale, rows, layer, pos, S,
-                out, part, ml, tickets, (uint8_t*)nullptr);
+                out, part, ml, tickets, (uint8_t*)nullptr, ro);
     launched();
     if (S > 1) {
         auto comb = S == 16 ? k_attn_combine<16> : S == 32 ? k_attn_combine<32> : k_attn_combine<64>;
@@ -1304,14 +1355,15 @@ static void attn_launch(const float* q, int T, int heads, int kv_heads, float sc
 
 template <int HD>
 static void attn_launch_g(const float* q, int T, int heads, int kv_heads, float scale, const RowKV* rows, int layer,
-                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+                          const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s,
+                          const AttnRope& ro)
 {
     switch (heads / kv_heads) {
-    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 1: attn_launch<HD, 1>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 2: attn_launch<HD, 2>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 4: attn_launch<HD, 4>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 8: attn_launch<HD, 8>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    default: attn_launch<HD, 16>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
     }
 }
 
@@ -1323,20 +1375,24 @@ bool attention_supported(int heads, int kv_heads, int head_dim)
 }
 
 bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s)
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s,
+               const AttnRope* rope)
 {
     if (T <= 0) return false;
+    const AttnRope ro = rope ? *rope : AttnRope{};
+    if (ro.k && (T != 1 || !ro.v || !ro.table || ro.rope_dims < 2 || ro.rope_dims % 2 || ro.rope_dims > head_dim))
+        WL_THROW(WL_EINVAL, "attention: RoPE in the attention serves one row, rope_dims even and at most head_dim");
     if (!attention_supported(heads, kv_heads, head_dim))
         WL_THROW(WL_EUNSUPPORTED, "attention: unsupported head layout (1, 2, 4, 8 or 16 query heads per KV head, head_dim 64, "
                                   "80, 96, 128 or 256, heads*head_dim a multiple of 256)");
     if (attention_splits(T, kv_heads) == 1) prep = nullptr;
     if (prep && (prep->cols != heads * head_dim || prep->nc != T)) WL_THROW(WL_EINVAL, "attention: prepared-activation view does not match");
     switch (head_dim) {
-    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
-    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s); break;
+    case 64: attn_launch_g<64>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 80: attn_launch_g<80>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 96: attn_launch_g<96>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    case 128: attn_launch_g<128>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
+    default: attn_launch_g<256>(q, T, heads, kv_heads, scale, rows, layer, pos, part, out, prep, s, ro); break;
     }
     return prep != nullptr;
 }

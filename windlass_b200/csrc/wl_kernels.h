@@ -229,8 +229,19 @@ inline size_t attention_part_floats(int heads, int kv_heads, int head_dim)
 }
 int attention_splits(int T, int kv_heads);
 bool attention_supported(int heads, int kv_heads, int head_dim);
+// RoPE and the KV append of a one-row decode step done inside the attention, in place of rope_append (same
+// arithmetic, same bits): q is read unrotated and rotated as it is staged; the CTA whose position range holds the
+// row's new position pos[0] rotates k and writes k and v there, in the cache and in its staged tile. No other CTA
+// reads that position, so nothing waits for the append.
+struct AttnRope {
+    const float* k = nullptr;       // [KV heads * head_dim], unrotated
+    const float* v = nullptr;
+    const float* table = nullptr;   // the rope table (cos, sin per position and pair)
+    int rope_dims = 0, neox = 0;
+};
 bool attention(const float* q, int T, int heads, int kv_heads, int head_dim, float scale, const RowKV* rows,
-               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s);
+               int layer, const int32_t* pos, float* part, float* out, const XPrep* prep, cudaStream_t s,
+               const AttnRope* rope = nullptr);
 // RoPE on q (heads) and k (kv heads) of T rows, then k and v appended to the fp16 caches at pos[t] (Rope,
 // Transformer.cs:418-433, and ToHalf, :342-348), in one kernel; k is left unrotated in its buffer.
 void rope_append(float* q, const float* k, const float* v, int T, int heads, int kv_heads, int head_dim, int rope_dims,

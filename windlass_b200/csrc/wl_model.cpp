@@ -1304,10 +1304,15 @@ void Model::layer(int l, int T, int max_n)
             k::rmsnorm(k_, T * c_.kv_heads, HD, L.k_norm.d, c_.rms_eps, k_, stream_);
         }
     }
-    if (!roped)
+    // a one-row step leaves RoPE and the KV append to the attention kernel (same bits, one launch fewer): the row's
+    // new position is read by no CTA but the one that writes it
+    const bool rope_in_attention = !roped && T == 1 && !c_.qk_norm_full && c_.rope_dims >= 2 && c_.rope_dims % 2 == 0 &&
+                                   c_.rope_dims <= HD;
+    if (!roped && !rope_in_attention)
         k::rope_append(q_, k_, v_, T, c_.heads, c_.kv_heads, HD, c_.rope_dims, c_.rope_neox ? 1 : 0, pos_d_,
                        rope_table_, rows_d_, l, stream_);
     profile_end(rm, WL_PROFILE_ROPE, 0.0);
+    const k::AttnRope ar_rope{k_, v_, rope_table_, c_.rope_dims, c_.rope_neox ? 1 : 0};
     const float scale = c_.attention_scale != 0.f ? c_.attention_scale : 1.f / (float)std::sqrt((double)HD);
     // the o matvec's activations come out of the attention combine when it can prepare them
     const bool want_prep = L.o.tiles && T <= 8 && xprep_buf_;
@@ -1315,7 +1320,7 @@ void Model::layer(int l, int T, int max_n)
     if (want_prep) ap = k::xprep_view(xprep_buf_, QD, T);
     const int mark = profile_begin();
     const bool prepped = k::attention(q_, T, c_.heads, c_.kv_heads, HD, scale, rows_d_, l, pos_d_, att_part_, att_,
-                                      want_prep ? &ap : nullptr, stream_);
+                                      want_prep ? &ap : nullptr, stream_, rope_in_attention ? &ar_rope : nullptr);
     profile_end(mark, WL_PROFILE_ATTENTION, 0.0);
     prep_x_ = nullptr;
     if (prepped) { prep_x_ = att_; prep_cols_ = QD; prep_nc_ = T; }
