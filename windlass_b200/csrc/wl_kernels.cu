@@ -887,7 +887,10 @@ void swiglu_prep(float* g, const float* u, int T, int F, const XPrep& p, cudaStr
 // the reference's four interleaved accumulators; exponentials are fp32 expf, the running sums double. Positions
 // 0..pos[t] of row t are cut into S equal ranges by the row's own length, so a row's result does not depend on the
 // other rows; each range keeps a running max m, sum l and unnormalised output o per head across its tiles. With
-// S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order.
+// S = 1 the CTA writes the normalised output; otherwise k_attn_combine merges the ranges in order. With ro.k (a
+// one-row decode step) the kernel also does k_rope_append's work with its arithmetic: q is rotated as it is staged,
+// and the CTA whose range holds the new position rotates k, writes k and v there in the cache and places them in its
+// staged tile itself (only that CTA reads that position).
 constexpr int ATT_P = 128;          // positions per tile (a range of a decode row up to 2048 positions is one tile)
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
