@@ -131,7 +131,8 @@ def test_70b_shape_batch_rows_bit_identical_to_single_runs(wl):
     """ForwardBatch rows equal single-sequence Forward bit for bit (tests/BatchTests.cs:29-94) at the 70B layer's
     shapes, where the decode matvec's launch shape is chosen from the matrix's row tiles: batches of 8, 3 and 2
     sequences (the persistent paired-tile form, the three-MMA form and the packed two-column form of the integer
-    matvec against the single column)."""
+    matvec against the single column; the single-sequence steps also do RoPE and the KV append inside the attention
+    kernel, the batches in k_rope_append)."""
     spec = llama70b_spec(layers=1)
     rng = np.random.default_rng(707)
     prompts = [rng.integers(0, spec.vocab, n).astype(np.int32) for n in (37, 5, 120, 64, 1, 77, 200, 19)]
